@@ -1,0 +1,151 @@
+"""Seeded synthetic weights and inputs for the Pairformer block (no checkpoints here).
+
+Weights are produced directly in the ENGINE state-dict schema, the one
+``pairformer_block_from_released`` (``legacy/released.py:318-369``) emits: 56 tensors per
+AF3 block. Keys are drawn in the fixed order of :func:`block_schema` from ONE
+``torch.Generator``; a trunk draws its blocks in order from the same generator.
+
+Schemes:
+
+* ``"baseline"``: every matrix and every non-LayerNorm bias ``~N(0, 0.02)``, LayerNorm
+  gamma 1 and beta 0 (the benchmark configurations).
+* ``"randomise"``: the reference test's ``randomise`` (``tests/models/test_engine_graph.py:
+  40-51``): matrices ``0.08 N(0,1)``, norm weights ``1 + 0.1 N``, other vectors
+  ``0.05 N`` -- a non-trivial LayerNorm affine for parity work.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+Tensor = torch.Tensor
+
+
+@dataclass(frozen=True)
+class BlockShape:
+    """Widths of one AF3 Pairformer block (defaults: ``modules/dense/spec.py:18-25,161``)."""
+
+    c_z: int = 128
+    c_s: int = 384
+    hidden_mul: int = 128
+    n_head_pair: int = 4
+    d_tri: int = 32
+    n_head_single: int = 16
+    n_pair: int = 4
+    n_single: int = 4
+
+
+def block_schema(shape: BlockShape = BlockShape(), single: bool = True) -> list[tuple[str, tuple[int, ...]]]:
+    """``[(engine key, shape)]`` of one block, in the converter's output order."""
+    c, cs, h = shape.c_z, shape.c_s, shape.hidden_mul
+    ht = shape.n_head_pair * shape.d_tri
+    out: list[tuple[str, tuple[int, ...]]] = []
+    for name in ("tri_multi_outgoing", "tri_multi_incoming"):
+        out += [
+            (f"{name}.ln_pair.weight", (c,)),
+            (f"{name}.ln_pair.bias", (c,)),
+            (f"{name}.ln_out.weight", (h,)),
+            (f"{name}.ln_out.bias", (h,)),
+            (f"{name}.to_left.weight", (h, c)),
+            (f"{name}.to_right.weight", (h, c)),
+            (f"{name}.to_left_gate.weight", (h, c)),
+            (f"{name}.to_right_gate.weight", (h, c)),
+            (f"{name}.to_out.weight", (c, h)),
+            (f"{name}.to_gate.weight", (c, c)),
+        ]
+    for name in ("tri_atten_starting", "tri_atten_ending"):
+        out += [
+            (f"{name}.ln_pair.weight", (c,)),
+            (f"{name}.ln_pair.bias", (c,)),
+            (f"{name}.to_bias.weight", (shape.n_head_pair, c)),
+            (f"{name}.to_query.weight", (ht, c)),
+            (f"{name}.to_key.weight", (ht, c)),
+            (f"{name}.to_value.weight", (ht, c)),
+            (f"{name}.to_gate.weight", (ht, c)),
+            (f"{name}.to_out.weight", (c, ht)),
+        ]
+    out += [
+        ("transition_pair.ln_in.weight", (c,)),
+        ("transition_pair.ln_in.bias", (c,)),
+        ("transition_pair.expand_a.weight", (shape.n_pair * c, c)),
+        ("transition_pair.expand_b.weight", (shape.n_pair * c, c)),
+        ("transition_pair.squeeze.weight", (c, shape.n_pair * c)),
+    ]
+    if single:
+        out += [
+            ("single_attention.ln_single.weight", (cs,)),
+            ("single_attention.ln_single.bias", (cs,)),
+            ("single_attention.to_query.weight", (cs, cs)),
+            ("single_attention.to_query.bias", (cs,)),
+            ("single_attention.to_key.weight", (cs, cs)),
+            ("single_attention.to_value.weight", (cs, cs)),
+            ("single_attention.ln_pair.weight", (c,)),
+            ("single_attention.to_bias.weight", (shape.n_head_single, c)),
+            ("single_attention.to_gate.weight", (cs, cs)),
+            ("single_attention.to_out.weight", (cs, cs)),
+            ("single_transition.ln_in.weight", (cs,)),
+            ("single_transition.ln_in.bias", (cs,)),
+            ("single_transition.expand_a.weight", (shape.n_single * cs, cs)),
+            ("single_transition.expand_b.weight", (shape.n_single * cs, cs)),
+            ("single_transition.squeeze.weight", (cs, shape.n_single * cs)),
+        ]
+    return out
+
+
+def _is_norm(key: str) -> bool:
+    return ".ln_" in key
+
+
+def block_state(
+    generator: torch.Generator,
+    shape: BlockShape = BlockShape(),
+    scheme: str = "baseline",
+    single: bool = True,
+) -> dict[str, Tensor]:
+    """One block's engine-key state dict (fp32), drawn from ``generator``."""
+    if scheme not in ("baseline", "randomise"):
+        raise ValueError(f"unknown weight scheme {scheme!r}")
+    state: dict[str, Tensor] = {}
+    for key, dims in block_schema(shape, single):
+        noise = torch.randn(dims, generator=generator, dtype=torch.float32)
+        if scheme == "baseline":
+            if _is_norm(key):
+                value = torch.ones(dims) if key.endswith("weight") else torch.zeros(dims)
+            else:
+                value = 0.02 * noise
+        elif len(dims) > 1:
+            value = 0.08 * noise
+        elif _is_norm(key) and key.endswith("weight"):
+            value = 1.0 + 0.1 * noise
+        else:
+            value = 0.05 * noise
+        state[key] = value
+    return state
+
+
+def trunk_state(
+    n_blocks: int, seed: int = 0, shape: BlockShape = BlockShape(), scheme: str = "baseline"
+) -> list[dict[str, Tensor]]:
+    """``n_blocks`` block states initialised in order from one seeded generator."""
+    g = torch.Generator().manual_seed(seed)
+    return [block_state(g, shape, scheme) for _ in range(n_blocks)]
+
+
+def inputs(
+    n: int,
+    seed: int = 0,
+    c_z: int = 128,
+    c_s: int = 384,
+    masked_suffix: int = 0,
+) -> tuple[Tensor, Tensor, Tensor]:
+    """``(z [N,N,c_z], s [N,c_s], tokens [N])``: ``z`` then ``s`` drawn ``~N(0,1)`` from a
+    generator seeded ``seed``; the last ``masked_suffix`` tokens are padding (0)."""
+    g = torch.Generator().manual_seed(seed)
+    z = torch.randn(n, n, c_z, generator=g)
+    s = torch.randn(n, c_s, generator=g)
+    tokens = torch.ones(n)
+    if masked_suffix:
+        tokens[n - masked_suffix :] = 0
+    return z, s, tokens

@@ -1,0 +1,205 @@
+"""Generate the golden fixtures from the REFERENCE's own legacy Pairformer block.
+
+Run in the build container only (it imports the FoldForge source tree, which does not
+travel to GPU boxes): ``python tests/golden/make_golden.py [--reference PATH]``.
+
+For every case it
+
+1. draws the block's engine-key weights with :func:`foldforge_b200.synthetic.block_state`,
+2. maps them to the RELEASED layout (the inverse of ``legacy/released.py:135-369``),
+   loads them strictly into the reference's ``legacy.pairformer.PairformerBlock`` and
+   checks that the reference's own converter ``pairformer_block_from_released`` maps them
+   back onto exactly the drawn engine tensors (bitwise),
+3. runs the reference block (and each of its ops alone) in fp32 on seeded inputs and
+   writes the outputs to ``tests/golden/<case>.npz``.
+
+``miniworld_engine`` is not installed anywhere; the legacy block reaches it only through
+names it never calls on this path, so a stub module stands in for it at import time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import hashlib
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE.parents[1]))
+
+from foldforge_b200.synthetic import BlockShape, block_state, inputs  # noqa: E402
+
+
+def _stub_engine() -> None:
+    engine = types.ModuleType("miniworld_engine")
+    mods = types.ModuleType("miniworld_engine.modules")
+    prim = types.ModuleType("miniworld_engine.modules.primitives")
+    prim.MasterWeights = type("MasterWeights", (), {})
+    mods.LayerNorm = torch.nn.LayerNorm
+    for name in (
+        "MSAPairWeightedAveraging", "OuterProductMean", "Transition", "TriangleAttention",
+        "TriangleMultiplication", "PairformerBlock", "PairformerConfig",
+    ):
+        setattr(mods, name, type(name, (torch.nn.Module,), {}))
+    mods.primitives = prim
+    engine.modules = mods
+    sys.modules.update({
+        "miniworld_engine": engine,
+        "miniworld_engine.modules": mods,
+        "miniworld_engine.modules.primitives": prim,
+    })
+
+
+def released_from_engine(state: dict[str, torch.Tensor], g: torch.Generator) -> dict[str, torch.Tensor]:
+    """Engine keys -> the legacy block's released keys (inverse of the converter)."""
+    out: dict[str, torch.Tensor] = {}
+    for dst, src, outgoing in (
+        ("triangle_multiplication_outgoing", "tri_multi_outgoing", True),
+        ("triangle_multiplication_incoming", "tri_multi_incoming", False),
+    ):
+        e = {k[len(src) + 1 :]: v for k, v in state.items() if k.startswith(src + ".")}
+        # row 2k = branch a of hidden channel k, 2k+1 = branch b; incoming: left = b
+        a, b = ("to_left", "to_right") if outgoing else ("to_right", "to_left")
+        for released, engine in (("projection", ""), ("gate", "_gate")):
+            pa, pb = e[f"{a}{engine}.weight"], e[f"{b}{engine}.weight"]
+            out[f"{dst}.{released}.weight"] = torch.stack([pa, pb], 1).reshape(-1, pa.shape[1])
+        out[f"{dst}.left_norm_input.weight"] = e["ln_pair.weight"]
+        out[f"{dst}.left_norm_input.bias"] = e["ln_pair.bias"]
+        out[f"{dst}.center_norm.weight"] = e["ln_out.weight"]
+        out[f"{dst}.center_norm.bias"] = e["ln_out.bias"]
+        out[f"{dst}.output_projection.weight"] = e["to_out.weight"]
+        out[f"{dst}.gating_linear.weight"] = e["to_gate.weight"]
+    for dst, src in (("pair_attention1", "tri_atten_starting"), ("pair_attention2", "tri_atten_ending")):
+        for released, engine in (
+            ("act_norm.weight", "ln_pair.weight"), ("act_norm.bias", "ln_pair.bias"),
+            ("pair_bias_projection.weight", "to_bias.weight"), ("q_projection.weight", "to_query.weight"),
+            ("k_projection.weight", "to_key.weight"), ("v_projection.weight", "to_value.weight"),
+            ("gating_query.weight", "to_gate.weight"), ("output_projection.weight", "to_out.weight"),
+        ):
+            out[f"{dst}.{released}"] = state[f"{src}.{engine}"]
+    for dst, src in (("pair_transition", "transition_pair"), ("single_transition", "single_transition")):
+        if f"{src}.ln_in.weight" not in state:
+            continue
+        out[f"{dst}.input_layer_norm.weight"] = state[f"{src}.ln_in.weight"]
+        out[f"{dst}.input_layer_norm.bias"] = state[f"{src}.ln_in.bias"]
+        out[f"{dst}.transition1.weight"] = torch.cat([state[f"{src}.expand_a.weight"], state[f"{src}.expand_b.weight"]], 0)
+        out[f"{dst}.transition2.weight"] = state[f"{src}.squeeze.weight"]
+    if "single_attention.to_query.weight" in state:
+        sa = "single_attention_"
+        out[f"{sa}.adaptive_layernorm.layer_norm.weight"] = state["single_attention.ln_single.weight"]
+        out[f"{sa}.adaptive_layernorm.layer_norm.bias"] = state["single_attention.ln_single.bias"]
+        out[f"{sa}.q_projection.weight"] = state["single_attention.to_query.weight"]
+        out[f"{sa}.q_projection.bias"] = state["single_attention.to_query.bias"]
+        out[f"{sa}.k_projection.weight"] = state["single_attention.to_key.weight"]
+        out[f"{sa}.v_projection.weight"] = state["single_attention.to_value.weight"]
+        out[f"{sa}.gating_query.weight"] = state["single_attention.to_gate.weight"]
+        out[f"{sa}.adaptive_zero_init.transition2.weight"] = state["single_attention.to_out.weight"]
+        out["single_pair_logits_norm.weight"] = state["single_attention.ln_pair.weight"]
+        # discarded by the converter (softmax-invariant): a NON-zero value here checks that
+        out["single_pair_logits_norm.bias"] = 0.05 * torch.randn(state["single_attention.ln_pair.weight"].shape, generator=g)
+        out["single_pair_logits_projection.weight"] = state["single_attention.to_bias.weight"]
+    return out
+
+
+def _digest(state: dict[str, torch.Tensor]) -> str:
+    h = hashlib.sha256()
+    for k in sorted(state):
+        h.update(k.encode())
+        h.update(state[k].contiguous().numpy().tobytes())
+    return h.hexdigest()
+
+
+def run_case(name: str, *, shape: BlockShape, n: int, masked: list[int], scheme: str, wseed: int,
+             iseed: int, extra_bias: bool = False, keep_rows: list[int] | None = None) -> None:
+    from foldforge.models.checkpoints.legacy.pairformer import PairformerBlock
+    from foldforge.models.checkpoints.legacy.released import pairformer_block_from_released
+
+    g = torch.Generator().manual_seed(wseed)
+    state = block_state(g, shape, scheme)
+    legacy = PairformerBlock(
+        n_heads=shape.n_head_single, c_pair=shape.c_z, c_single=shape.c_s,
+        n_heads_pair=shape.n_head_pair, num_intermediate_factor=shape.n_pair,
+        single_intermediate_factor=shape.n_single,
+    ).eval()
+    legacy.load_state_dict(released_from_engine(state, torch.Generator().manual_seed(wseed + 1000)), strict=True)
+    back = pairformer_block_from_released(legacy.state_dict())
+    assert set(back) == set(state), sorted(set(back) ^ set(state))
+    for k, v in state.items():
+        assert torch.equal(back[k], v), k
+
+    z, s, tokens = inputs(n, iseed, shape.c_z, shape.c_s)
+    for t in masked:
+        tokens[t] = 0
+    pair_mask = tokens[:, None] * tokens[None, :]
+    bias = torch.randn(n, n, generator=torch.Generator().manual_seed(iseed + 7)) if extra_bias else None
+    with torch.no_grad():
+        ops = {
+            "tri_multi_outgoing": z + legacy.triangle_multiplication_outgoing(z, pair_mask),
+            "tri_multi_incoming": z + legacy.triangle_multiplication_incoming(z, pair_mask),
+            "tri_atten_starting": legacy.pair_attention1.residual(z, pair_mask),
+            "tri_atten_ending": legacy.pair_attention2.residual(z, pair_mask),
+            "transition_pair": z + legacy.pair_transition(z),
+            "single_transition": s + legacy.single_transition(s),
+        }
+        pair_logits = legacy.single_pair_logits_projection(legacy.single_pair_logits_norm(z)).permute(2, 0, 1)
+        if bias is not None:
+            pair_logits = pair_logits + bias[None]
+        ops["single_attention"] = s + legacy.single_attention_(s, tokens, pair_logits=pair_logits)
+        out_pair, out_single = legacy(z.clone(), pair_mask, s.clone(), tokens, extra_pair_bias=bias)
+    record: dict[str, np.ndarray] = {
+        "n": np.array(n), "tokens": tokens.numpy(),
+        "shape": np.array([shape.c_z, shape.c_s, shape.hidden_mul, shape.n_head_pair, shape.d_tri,
+                           shape.n_head_single, shape.n_pair, shape.n_single]),
+        "scheme": np.array(scheme), "wseed": np.array(wseed), "iseed": np.array(iseed),
+        "weights_sha256": np.array(_digest(state)),
+        "inputs_sha256": np.array(_digest({"z": z, "s": s})),
+        "pair_sum": np.array(out_pair.double().sum().item()),
+        "pair_sumsq": np.array(out_pair.double().square().sum().item()),
+        "single_sum": np.array(out_single.double().sum().item()),
+        "single_sumsq": np.array(out_single.double().square().sum().item()),
+        "out_single": out_single.numpy(),
+    }
+    if bias is not None:
+        record["extra_pair_bias"] = bias.numpy()
+    if keep_rows is None:
+        record["out_pair"] = out_pair.numpy()
+        for k, v in ops.items():
+            record[f"op.{k}"] = v.numpy()
+    else:
+        record["rows"] = np.array(keep_rows)
+        record["out_pair_rows"] = out_pair[keep_rows].numpy()
+    np.savez_compressed(HERE / f"{name}.npz", **record)
+    print(f"{name}: N={n} masked={masked} -> {HERE / (name + '.npz')}")
+
+
+SMALL = BlockShape(c_z=32, c_s=64, hidden_mul=32, n_head_pair=4, d_tri=8, n_head_single=4, n_pair=4, n_single=4)
+AF3 = BlockShape()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference/src")
+    args = ap.parse_args()
+    sys.path.insert(0, args.reference)
+    _stub_engine()
+    torch.set_num_threads(8)
+    # the reference test's own case: AF3 widths, 24 tokens, last 3 masked
+    run_case("af3_n24_masked3", shape=AF3, n=24, masked=[21, 22, 23], scheme="randomise", wseed=1, iseed=0)
+    # benchmark configuration 1 (N=128, all tokens real, N(0, 0.02) weights), rows kept
+    run_case("af3_n128_config1", shape=AF3, n=128, masked=[], scheme="baseline", wseed=0, iseed=0,
+             keep_rows=[0, 37, 127])
+    # small widths: ragged length, interior + suffix padding, extra pair bias
+    run_case("small_n13_ragged", shape=SMALL, n=13, masked=[3, 7, 11, 12], scheme="randomise", wseed=2, iseed=3,
+             extra_bias=True)
+    # every token masked: uniform attention rows, zero contraction
+    run_case("small_n5_allmasked", shape=SMALL, n=5, masked=[0, 1, 2, 3, 4], scheme="randomise", wseed=4, iseed=5)
+    # a single token
+    run_case("small_n1", shape=SMALL, n=1, masked=[], scheme="randomise", wseed=6, iseed=7)
+
+
+if __name__ == "__main__":
+    main()
