@@ -1,0 +1,104 @@
+"""ctypes binding of the C ABI (``include/foldforge_b200.h``) in ``_ffb.so``.
+
+The library is required: there is no fallback implementation behind these bindings. A
+missing or unloadable library raises :class:`LibraryMissing` at the first call.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+_HERE = Path(__file__).resolve().parent
+LIBRARY = Path(os.environ.get("FFB_LIBRARY", _HERE / "_ffb.so"))
+
+c_void_p = ctypes.c_void_p
+c_int = ctypes.c_int
+c_i64 = ctypes.c_int64
+c_float = ctypes.c_float
+
+#: name -> argument types, exactly as declared in include/foldforge_b200.h
+SIGNATURES: dict[str, list] = {
+    "ffb_version": [],
+    "ffb_last_error": [],
+    "ffb_device_error": [ctypes.POINTER(c_int), c_void_p],
+    "ffb_layernorm_fwd": [c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_int, c_float, c_int, c_void_p],
+    "ffb_gemm_bf16_nt": [
+        c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
+        c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p,
+    ],
+    "ffb_trimul_packed_bytes": [],
+    "ffb_trimul_workspace_bytes": [c_int, c_int],
+    "ffb_trimul_prepare": [c_void_p] * 12,
+    "ffb_trimul_fwd": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_size_t, c_int, c_int, c_int,
+                       c_int, c_void_p],
+}
+
+#: entry points that return a size_t instead of a status
+SIZE_RESULT = {"ffb_trimul_packed_bytes", "ffb_trimul_workspace_bytes"}
+
+STATUS = {0: "FFB_OK", 1: "FFB_ERR_ARG", 2: "FFB_ERR_UNSUPPORTED", 3: "FFB_ERR_CUDA", 4: "FFB_ERR_DEVICE"}
+
+
+class LibraryMissing(RuntimeError):
+    """The compiled sm_100a library could not be loaded."""
+
+
+class KernelError(RuntimeError):
+    """A C-ABI entry point returned a non-OK status."""
+
+    def __init__(self, fn: str, status: int, message: str) -> None:
+        super().__init__(f"{fn}: {STATUS.get(status, status)}: {message}")
+        self.status = status
+
+
+class UnsupportedCall(KernelError):
+    """FFB_ERR_UNSUPPORTED: the call is outside the kernels' range."""
+
+
+_lib: ctypes.CDLL | None = None
+
+
+def load() -> ctypes.CDLL:
+    """The loaded library (loaded once; raises :class:`LibraryMissing`)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIBRARY.exists():
+        raise LibraryMissing(f"{LIBRARY} is not built; run `python -m foldforge_b200.csrc.build`")
+    try:
+        lib = ctypes.CDLL(str(LIBRARY))
+    except OSError as exc:  # pragma: no cover - depends on the machine
+        raise LibraryMissing(f"cannot load {LIBRARY}: {exc}") from exc
+    for name, argtypes in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = argtypes
+        if name == "ffb_last_error":
+            fn.restype = ctypes.c_char_p
+        elif name in SIZE_RESULT:
+            fn.restype = ctypes.c_size_t
+        else:
+            fn.restype = c_int
+    _lib = lib
+    return lib
+
+
+def call(name: str, *args) -> None:
+    """Call an entry point; raise on a non-OK status."""
+    lib = load()
+    status = getattr(lib, name)(*args)
+    if status != 0:
+        msg = lib.ffb_last_error().decode(errors="replace")
+        cls = UnsupportedCall if status == 2 else KernelError
+        raise cls(name, status, msg)
+
+
+def device_error(stream: int = 0) -> int:
+    """Synchronise ``stream`` and return (and clear) the device error word (0 = none)."""
+    lib = load()
+    code = c_int(0)
+    status = lib.ffb_device_error(ctypes.byref(code), c_void_p(stream))
+    if status not in (0, 4):
+        raise KernelError("ffb_device_error", status, lib.ffb_last_error().decode(errors="replace"))
+    return code.value

@@ -1,0 +1,260 @@
+// Batched bf16 GEMM on tcgen05: D[b] = epilogue(A[b] * B[b]^T), A [M, K], B [N, K], both
+// K-major (row-major with K innermost), fp32 accumulation in TMEM.
+//
+// Persistent, warp-specialised: warp 0 issues TMA loads into a STAGES-deep ring of
+// shared-memory stages, warp 1 (one elected lane) issues tcgen05.mma and commits, warps
+// 2..5 drain the accumulator (TMEM -> registers) and run the epilogue. Two TMEM
+// accumulators of BN columns let the MMA of tile t+1 overlap the epilogue of tile t.
+//
+// Used for the triangle-multiplication contraction (one GEMM per hidden channel, batch =
+// B * hidden) and for the single-track projections.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ffb {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // one 128-byte swizzle row of bf16
+constexpr int kStages = 4;
+
+template <int BN>
+struct GemmSmem {
+  alignas(1024) uint8_t a[kStages][kBM * kBK * 2];
+  alignas(1024) uint8_t b[kStages][BN * kBK * 2];
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint32_t tmem_base;
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& b, int& tm, int& tn) {
+  const int per_batch = tiles_m * tiles_n;
+  b = tile / per_batch;
+  const int r = tile - b * per_batch;
+  tm = r / tiles_n;
+  tn = r - tm * tiles_n;
+}
+
+template <int BN>
+__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int b, int m, int n0, const uint32_t (&v)[32]) {
+  if (m >= p.M) return;
+  const int out_cols = (p.epilogue == kEpiSwiGLU) ? (p.N / 2) : p.N;
+  if (p.epilogue == kEpiSwiGLU) {
+    // the packed weight interleaves a and b in blocks of 16 rows, so accumulator columns
+    // [n0, n0 + 32) hold a[h0 : h0 + 16] then b[h0 : h0 + 16], h0 = n0 / 2
+    const int h0 = n0 / 2;
+    float out[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float a = __uint_as_float(v[i]);
+      const float bb = __uint_as_float(v[16 + i]);
+      out[i] = a / (1.0f + __expf(-a)) * bb;
+    }
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + static_cast<int64_t>(b) * p.batch_stride_d +
+                         static_cast<int64_t>(m) * p.ldd + h0;
+    if (h0 + 16 <= out_cols) {
+      uint4 w0 = make_uint4(pack_bf16(out[0], out[1]), pack_bf16(out[2], out[3]), pack_bf16(out[4], out[5]),
+                            pack_bf16(out[6], out[7]));
+      uint4 w1 = make_uint4(pack_bf16(out[8], out[9]), pack_bf16(out[10], out[11]), pack_bf16(out[12], out[13]),
+                            pack_bf16(out[14], out[15]));
+      reinterpret_cast<uint4*>(dst)[0] = w0;
+      reinterpret_cast<uint4*>(dst)[1] = w1;
+    } else {
+      for (int i = 0; i < 16 && h0 + i < out_cols; ++i) dst[i] = __float2bfloat16_rn(out[i]);
+    }
+    return;
+  }
+  float acc[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    float x = __uint_as_float(v[i]);
+    if (p.bias != nullptr && n0 + i < p.N) x += p.bias[n0 + i];
+    acc[i] = x;
+  }
+  float rowscale = 1.0f;
+  if (p.row_mask != nullptr) rowscale = p.row_mask[static_cast<int64_t>(b) * p.M + m] ? 1.0f : 0.0f;
+  const int64_t off = static_cast<int64_t>(b) * p.batch_stride_d + static_cast<int64_t>(m) * p.ldd + n0;
+  const bool full = (n0 + 32 <= p.N);
+  if (p.epilogue == kEpiResidual) {
+    // D = R + acc * rowscale, R and D share the layout and dtype
+    if (p.d_is_f32) {
+      const float* r = reinterpret_cast<const float*>(p.residual) + off;
+      float* d = reinterpret_cast<float*>(p.D) + off;
+      for (int i = 0; i < 32; ++i)
+        if (n0 + i < p.N) d[i] = r[i] + acc[i] * rowscale;
+    } else {
+      const __nv_bfloat16* r = reinterpret_cast<const __nv_bfloat16*>(p.residual) + off;
+      __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + off;
+      for (int i = 0; i < 32; ++i)
+        if (n0 + i < p.N) d[i] = __float2bfloat16_rn(__bfloat162float(r[i]) + acc[i] * rowscale);
+    }
+    return;
+  }
+  if (p.d_is_f32) {
+    float* d = reinterpret_cast<float*>(p.D) + off;
+    if (full) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(d + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (n0 + i < p.N) d[i] = acc[i];
+    }
+  } else {
+    __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + off;
+    if (full) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        uint4 w = make_uint4(pack_bf16(acc[i], acc[i + 1]), pack_bf16(acc[i + 2], acc[i + 3]),
+                             pack_bf16(acc[i + 4], acc[i + 5]), pack_bf16(acc[i + 6], acc[i + 7]));
+        *reinterpret_cast<uint4*>(d + i) = w;
+      }
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (n0 + i < p.N) d[i] = __float2bfloat16_rn(acc[i]);
+    }
+  }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_nt_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, GemmParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  GemmSmem<BN>& s = *reinterpret_cast<GemmSmem<BN>*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int tiles_m = (p.M + kBM - 1) / kBM;
+  const int tiles_n = (p.N + BN - 1) / BN;
+  const int total = p.batch * tiles_m * tiles_n;
+  const int kblocks = (p.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.acc_full[i], 1);
+      mbar_init(&s.acc_empty[i], 4);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&s.tmem_base, 2 * BN);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_map(&map_a);
+    tma_prefetch_map(&map_b);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        int b, tm, tn;
+        tile_coords(tile, tiles_m, tiles_n, b, tm, tn);
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int st = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          if (!mbar_wait(&s.empty[st], ph ^ 1, p.err, kErrTimeoutEmpty)) { ok = false; break; }
+          mbar_arrive_expect_tx(&s.full[st], (kBM + BN) * kBK * 2);
+          tma_load_3d(s.a[st], &map_a, &s.full[st], kb * kBK, tm * kBM, b);
+          tma_load_3d(s.b[st], &map_b, &s.full[st], kb * kBK, tn * BN, b);
+        }
+      }
+      // drain: every issued stage must land before the CTA may exit
+      for (int k = 0; k < kStages && k < it; ++k) {
+        const int j = it - 1 - k;
+        mbar_wait(&s.full[j % kStages], (j / kStages) & 1, p.err, kErrTimeoutLoad);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(kBM, BN);
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        if (!mbar_wait(&s.acc_empty[acc], ((local >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + acc * BN;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int st = it % kStages;
+          if (!mbar_wait(&s.full[st], (it / kStages) & 1, p.err, kErrTimeoutLoad)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t da = desc_kmajor_sw128(smem_u32(s.a[st]));
+          const uint64_t db = desc_kmajor_sw128(smem_u32(s.b[st]));
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            mma_bf16(d, da + 2 * kk, db + 2 * kk, idesc, (kb | kk) != 0);
+          mma_commit(&s.empty[st]);
+        }
+        mma_commit(&s.acc_full[acc]);
+      }
+    }
+  } else {
+    // epilogue warps 2..5: TMEM lane quarter = warp % 4
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++local) {
+      int b, tm, tn;
+      tile_coords(tile, tiles_m, tiles_n, b, tm, tn);
+      const int acc = local & 1;
+      const bool ok = mbar_wait(&s.acc_full[acc], (local >> 1) & 1, p.err, kErrTimeoutMma);
+      if (!__all_sync(0xFFFFFFFFu, ok)) break;  // warp-uniform: tcgen05.ld below is .sync.aligned
+      tc_fence_after();
+      const uint32_t base = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+      const int m = tm * kBM + row;
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(base + c, v);
+        tmem_ld_wait();
+        if (tn * BN + c < p.N) epilogue_chunk<BN>(p, b, m, tn * BN + c, v);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.acc_empty[acc]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 2 * BN);
+  }
+}
+
+}  // namespace
+
+size_t gemm_smem_bytes(int bn) {
+  return (bn == 256 ? sizeof(GemmSmem<256>) : sizeof(GemmSmem<128>)) + 1024;
+}
+
+int launch_gemm_nt(const CUtensorMap& map_a, const CUtensorMap& map_b, const GemmParams& p, int bn, int num_sms,
+                   cudaStream_t stream) {
+  const int tiles = p.batch * ((p.M + kBM - 1) / kBM) * ((p.N + bn - 1) / bn);
+  if (tiles <= 0) return 0;
+  const int grid = tiles < num_sms ? tiles : num_sms;
+  const size_t smem = gemm_smem_bytes(bn);
+  if (bn == 256) {
+    cudaFuncSetAttribute(gemm_nt_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    gemm_nt_kernel<256><<<grid, 192, smem, stream>>>(map_a, map_b, p);
+  } else {
+    cudaFuncSetAttribute(gemm_nt_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    gemm_nt_kernel<128><<<grid, 192, smem, stream>>>(map_a, map_b, p);
+  }
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace ffb

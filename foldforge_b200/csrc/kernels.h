@@ -1,0 +1,56 @@
+// Internal launch interface between the C-ABI layer (abi.cu) and the kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ffb {
+
+enum GemmEpilogue : int {
+  kEpiStore = 0,     // D = acc (+ bias[n])
+  kEpiResidual = 1,  // D = R + (acc (+ bias[n])) * row_mask[m]
+  kEpiSwiGLU = 2,    // D[:, h] = silu(a_h) * b_h from an a/b-interleaved weight
+};
+
+struct GemmParams {
+  int M, N, K, batch;
+  void* D;
+  int64_t ldd;
+  int64_t batch_stride_d;
+  int d_is_f32;
+  int epilogue;
+  const float* bias;
+  const void* residual;
+  const uint8_t* row_mask;
+  int* err;
+};
+
+size_t gemm_smem_bytes(int bn);
+int launch_gemm_nt(const CUtensorMap& map_a, const CUtensorMap& map_b, const GemmParams& p, int bn, int num_sms,
+                   cudaStream_t stream);
+
+// LayerNorm over the last axis of `rows` rows of `c` channels.
+int launch_layernorm(const void* x, void* y, const float* gamma, const float* beta, int64_t rows, int c, float eps,
+                     int is_f32, int num_sms, cudaStream_t stream);
+
+// Packs an fp32 [rows, k] weight (optionally times diag(gamma)) into the K-major SW128
+// shared-memory image at row offset `row_offset` of an image with `image_rows` rows;
+// writes wsum / bias (W beta) per row when the pointers are non-null.
+int launch_pack_weight(const float* w, int rows, int k, const float* gamma, const float* beta, uint8_t* image,
+                       int row_offset, int image_rows, float* wsum, float* bias, cudaStream_t stream);
+
+struct DeviceInfo;
+
+// ---- triangle multiplication (c_z = hidden = 128)
+struct TriMulWeights {
+  const float *ln_w, *ln_b, *ln_out_w, *ln_out_b;
+  const float *to_left, *to_right, *to_left_gate, *to_right_gate, *to_out, *to_gate;
+};
+size_t trimul_packed_bytes();
+size_t trimul_workspace_bytes(int B, int N);
+int trimul_prepare(const TriMulWeights& w, void* packed, cudaStream_t stream);
+int trimul_forward(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace, int B, int N,
+                   int outgoing, int masked_zero, const DeviceInfo& info, cudaStream_t stream);
+
+}  // namespace ffb

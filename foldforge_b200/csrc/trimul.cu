@@ -1,0 +1,545 @@
+// Triangle multiplicative update (outgoing / incoming), bf16 activations, c_z = h = 128.
+//
+//   x = LN(z);  L = sigmoid(W_lg x) * (W_l x) * m_a m_k;  R = likewise;
+//   u_ij = sum_k L_ik R_jk (outgoing) | sum_k L_ki R_kj (incoming);
+//   z' = z + W_o LN_out(u) * sigmoid(W_g x)
+// (legacy/reference/triangle.py:19-50, engine left/right per legacy/released.py:135-173).
+//
+// Three launches:
+//  1. trimul_proj: 128-pair tiles of raw z (TMA, 128B swizzle) times the resident packed
+//     projection [W_l; W_lg; W_r; W_rg] (tcgen05, fp32 in TMEM); the LayerNorm is folded
+//     into the epilogue; L and R are written CHANNEL-MAJOR [c][a][k] so that step 2 is a
+//     plain K-major GEMM per channel. The incoming direction reads COLUMN tiles of z
+//     (pairs (k, a) for fixed a), which makes its contraction the same GEMM.
+//  2. the per-channel contraction U_c = L_c R_c^T on the batched tcgen05 GEMM (gemm.cu).
+//  3. trimul_out: per 128-pair tile, the centre LayerNorm of u (channel-major in smem,
+//     transposed into a K-major operand), two tcgen05 GEMMs (gate from raw z with the
+//     folded input LayerNorm, output projection from LN_out(u)), sigmoid gate, mask and
+//     residual, written back through the z tile and a TMA store.
+//
+// Kernels 1 and 3 run G = 2 independent groups of 4 warps per CTA (one CTA per SM,
+// persistent over tiles), sharing the resident weights; each group has its own z stage and
+// 256 TMEM columns, so one group's loads and epilogue overlap the other's MMAs.
+#include "abi_util.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ffb {
+namespace {
+
+constexpr int kC = 128;       // pair channels
+constexpr int kH = 128;       // hidden channels
+constexpr int kTile = 128;    // pairs per tile
+constexpr int kGroups = 2;
+constexpr int kThreads = kGroups * 128;
+
+// ---------------------------------------------------------------- packed weight image
+// [0, 128K)            projection operand: rows 0..127 W_l', 128..255 W_lg', 256..383 W_r', 384..511 W_rg'
+// [128K, 160K)         gate operand W_g' (rows = output channels)
+// [160K, 192K)         output operand W_o' = W_o diag(gamma_out)
+// [192K, +)            fp32: wsum_proj[512] bias_proj[512] wsum_gate[128] bias_gate[128] bias_out[128]
+constexpr size_t kProjBytes = 512 * kC * 2;
+constexpr size_t kGateBytes = kC * kC * 2;
+constexpr size_t kOutBytes = kC * kH * 2;
+constexpr size_t kVecFloats = 512 + 512 + 128 + 128 + 128;
+constexpr size_t kPackedBytes = kProjBytes + kGateBytes + kOutBytes + kVecFloats * 4;
+
+struct Vecs {
+  float wsum_proj[512];
+  float bias_proj[512];
+  float wsum_gate[128];
+  float bias_gate[128];
+  float bias_out[128];
+};
+
+__device__ __forceinline__ void load_z_stats(const uint8_t* tile, int row, float& mean, float& rstd) {
+  // row `row` of a [128 x 128] bf16 tile stored as two K-major SW128 blocks
+  float s = 0.f;
+  uint4 v[16];
+#pragma unroll
+  for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      v[kb * 8 + q] = *reinterpret_cast<const uint4*>(tile + kb * 16384 + sw128_offset(row, q * 8));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) s += bf16_lo(w[j]) + bf16_hi(w[j]);
+  }
+  mean = s * (1.0f / kC);
+  float q2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float a = bf16_lo(w[j]) - mean, b = bf16_hi(w[j]) - mean;
+      q2 += a * a + b * b;
+    }
+  }
+  rstd = rsqrtf(q2 * (1.0f / kC) + 1e-5f);
+}
+
+// ====================================================================== kernel 1
+struct ProjSmem {
+  alignas(1024) uint8_t w[kProjBytes];
+  alignas(1024) uint8_t z[kGroups][kTile * kC * 2];
+  Vecs vec;
+  uint64_t wbar;
+  uint64_t full[kGroups];
+  uint64_t mma[kGroups];
+  uint32_t tmem_base;
+};
+
+struct ProjParams {
+  const uint8_t* packed;
+  const uint8_t* mask;  // [B, N]
+  __nv_bfloat16* left;  // [B*h, N, Np]
+  __nv_bfloat16* right;
+  int B, N, Np;
+  int outgoing;
+  int* err;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    trimul_proj_kernel(const __grid_constant__ CUtensorMap map_z, ProjParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  ProjSmem& s = *reinterpret_cast<ProjSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int g = threadIdx.x / 128;
+  const int gt = threadIdx.x % 128;  // thread in group == tile row == TMEM lane
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int tiles_per_row = (p.N + kTile - 1) / kTile;
+  const int total = p.B * p.N * tiles_per_row;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&s.wbar, 1);
+    for (int i = 0; i < kGroups; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.mma[i], 1);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&s.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x == 0) {
+    tma_prefetch_map(&map_z);
+    mbar_arrive_expect_tx(&s.wbar, kProjBytes);
+    for (int off = 0; off < static_cast<int>(kProjBytes); off += 32768)
+      bulk_load(s.w + off, p.packed + off, 32768, &s.wbar);
+  }
+  {
+    const float* vsrc = reinterpret_cast<const float*>(p.packed + kProjBytes + kGateBytes + kOutBytes);
+    float* vdst = s.vec.wsum_proj;
+    for (int i = threadIdx.x; i < 1024; i += kThreads) vdst[i] = vsrc[i];
+  }
+  __syncthreads();
+  bool ok = mbar_wait(&s.wbar, 0, p.err, kErrTimeoutLoad);
+  const uint32_t tmem = s.tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16) + g * 256;
+  const uint32_t tmem_mma = s.tmem_base + g * 256;
+  const uint32_t idesc = idesc_bf16_f32(128, 256);
+  uint8_t* zt = s.z[g];
+  int it = 0;
+  bool load_pending = false;
+  for (int tile = blockIdx.x * kGroups + g; tile < total; tile += gridDim.x * kGroups, ++it) {
+    const int c0 = (tile % tiles_per_row) * kTile;
+    const int rr = tile / tiles_per_row;  // b * N + r
+    const int b = rr / p.N;
+    const int r = rr - b * p.N;
+    if (gt == 0 && ok) {
+      mbar_arrive_expect_tx(&s.full[g], kTile * kC * 2);
+      for (int kb = 0; kb < 2; ++kb) {
+        if (p.outgoing)
+          tma_load_3d(zt + kb * 16384, &map_z, &s.full[g], kb * 64, c0, rr);        // z[b, r, c0 + t]
+        else
+          tma_load_3d(zt + kb * 16384, &map_z, &s.full[g], kb * 64, r, b * p.N + c0);  // z[b, c0 + t, r]
+      }
+      load_pending = true;
+    }
+    ok = ok && mbar_wait(&s.full[g], it & 1, p.err, kErrTimeoutLoad);
+    if (gt == 0 && ok) load_pending = false;
+    float mean = 0.f, rstd = 0.f;
+    if (ok) load_z_stats(zt, gt, mean, rstd);
+    const int k = c0 + gt;  // this row's position along the contraction axis
+    const bool valid = k < p.N;
+    const float pm = (valid && p.mask[b * p.N + r] && p.mask[b * p.N + k]) ? 1.0f : 0.0f;
+    for (int half = 0; half < 2; ++half) {
+      if (gt == 0 && ok) {
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(zt);
+        const uint32_t b0 = smem_u32(s.w) + half * 256 * 128;
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_bf16(tmem_mma, desc_kmajor_sw128(a0 + kb * 16384) + 2 * kk,
+                     desc_kmajor_sw128(b0 + kb * 65536) + 2 * kk, idesc, (kb | kk) != 0);
+        mma_commit(&s.mma[g]);
+      }
+      bool got = ok && mbar_wait(&s.mma[g], half, p.err, kErrTimeoutMma);
+      got = __all_sync(0xFFFFFFFFu, got);
+      tc_fence_after();
+      __nv_bfloat16* out = half == 0 ? p.left : p.right;
+      if (got) {
+        const float* wsum = s.vec.wsum_proj + half * 256;
+        const float* bias = s.vec.bias_proj + half * 256;
+#pragma unroll 1
+        for (int cc = 0; cc < kH; cc += 32) {
+          uint32_t vp[32], vg[32];
+          tmem_ld32(tmem + cc, vp);
+          tmem_ld32(tmem + 128 + cc, vg);
+          tmem_ld_wait();
+          if (valid) {
+            __nv_bfloat16* dst = out + ((static_cast<int64_t>(b) * kH + cc) * p.N + r) * p.Np + k;
+            const int64_t cstride = static_cast<int64_t>(p.N) * p.Np;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float yp = rstd * (__uint_as_float(vp[i]) - mean * wsum[cc + i]) + bias[cc + i];
+              const float yg = rstd * (__uint_as_float(vg[i]) - mean * wsum[128 + cc + i]) + bias[128 + cc + i];
+              dst[i * cstride] = __float2bfloat16_rn(yp * pm * sigmoidf_(yg));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      ok = !named_barrier_or(1 + g, 128, !ok || !got);
+    }
+    if (!ok) break;
+  }
+  if (gt == 0 && load_pending) mbar_wait(&s.full[g], it & 1, p.err, kErrTimeoutLoad);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(s.tmem_base, 512);
+  }
+}
+
+// ====================================================================== kernel 3
+struct OutSmem {
+  alignas(1024) uint8_t wg[kGateBytes];
+  alignas(1024) uint8_t wo[kOutBytes];
+  alignas(1024) uint8_t z[kGroups][kTile * kC * 2];
+  alignas(1024) uint8_t u[kGroups][kTile * kH * 2];
+  float wsum_gate[128];
+  float bias_gate[128];
+  float bias_out[128];
+  uint64_t wbar;
+  uint64_t full[kGroups];
+  uint64_t mma[kGroups];
+  uint32_t tmem_base;
+};
+
+struct OutParams {
+  const uint8_t* packed;
+  const uint8_t* mask;
+  int B, N;
+  int masked_zero;
+  int* err;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    trimul_out_kernel(const __grid_constant__ CUtensorMap map_z, const __grid_constant__ CUtensorMap map_u,
+                      const __grid_constant__ CUtensorMap map_out, OutParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  OutSmem& s = *reinterpret_cast<OutSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int g = threadIdx.x / 128;
+  const int gt = threadIdx.x % 128;
+  const int warp = threadIdx.x / 32;
+  const int tiles_per_row = (p.N + kTile - 1) / kTile;
+  const int total = p.B * p.N * tiles_per_row;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&s.wbar, 1);
+    for (int i = 0; i < kGroups; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.mma[i], 1);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&s.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x == 0) {
+    tma_prefetch_map(&map_z);
+    tma_prefetch_map(&map_u);
+    tma_prefetch_map(&map_out);
+    mbar_arrive_expect_tx(&s.wbar, kGateBytes + kOutBytes);
+    bulk_load(s.wg, p.packed + kProjBytes, kGateBytes, &s.wbar);
+    bulk_load(s.wo, p.packed + kProjBytes + kGateBytes, kOutBytes, &s.wbar);
+  }
+  {
+    const float* v = reinterpret_cast<const float*>(p.packed + kProjBytes + kGateBytes + kOutBytes) + 1024;
+    for (int i = threadIdx.x; i < 128; i += kThreads) {
+      s.wsum_gate[i] = v[i];
+      s.bias_gate[i] = v[128 + i];
+      s.bias_out[i] = v[256 + i];
+    }
+  }
+  __syncthreads();
+  bool ok = mbar_wait(&s.wbar, 0, p.err, kErrTimeoutLoad);
+  const uint32_t tmem = s.tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16) + g * 256;
+  const uint32_t tmem_mma = s.tmem_base + g * 256;
+  const uint32_t idesc = idesc_bf16_f32(128, 128);
+  uint8_t* zt = s.z[g];
+  uint8_t* ut = s.u[g];
+  int it = 0;
+  bool load_pending = false;
+  for (int tile = blockIdx.x * kGroups + g; tile < total; tile += gridDim.x * kGroups, ++it) {
+    const int c0 = (tile % tiles_per_row) * kTile;
+    const int rr = tile / tiles_per_row;
+    const int b = rr / p.N;
+    const int r = rr - b * p.N;
+    if (gt == 0 && ok) {
+      tma_store_wait_read0();  // the previous tile's output store has left the z stage
+      mbar_arrive_expect_tx(&s.full[g], kTile * kC * 2 + kTile * kH * 2);
+      tma_load_3d(zt, &map_z, &s.full[g], 0, c0, rr);
+      tma_load_3d(zt + 16384, &map_z, &s.full[g], 64, c0, rr);
+      tma_load_3d(ut, &map_u, &s.full[g], c0, r, b * kH);  // u[b, :, r, c0 + t] -> [c][t]
+      load_pending = true;
+    }
+    ok = ok && mbar_wait(&s.full[g], it & 1, p.err, kErrTimeoutLoad);
+    if (gt == 0 && ok) load_pending = false;
+    float zmean = 0.f, zrstd = 0.f;
+    uint32_t uv[64];
+    float umean = 0.f, urstd = 0.f;
+    if (ok) {
+      load_z_stats(zt, gt, zmean, zrstd);
+      const __nv_bfloat16* ucol = reinterpret_cast<const __nv_bfloat16*>(ut) + gt;
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < kH; c += 2) {
+        const __nv_bfloat16 lo = ucol[c * kTile], hi = ucol[(c + 1) * kTile];
+        const float a = __bfloat162float(lo), bb = __bfloat162float(hi);
+        sum += a + bb;
+        uv[c / 2] = pack_bf16(a, bb);
+      }
+      umean = sum * (1.0f / kH);
+      float q2 = 0.f;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float a = bf16_lo(uv[i]) - umean, bb = bf16_hi(uv[i]) - umean;
+        q2 += a * a + bb * bb;
+      }
+      urstd = rsqrtf(q2 * (1.0f / kH) + 1e-5f);
+    }
+    named_barrier(1 + g, 128);  // every column of u read before the tile is overwritten
+    if (ok) {
+      // normalised u, row gt, as a K-major SW128 operand in place of the channel-major tile
+#pragma unroll
+      for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          uint32_t w[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t x = uv[kb * 32 + q * 4 + j];
+            w[j] = pack_bf16((bf16_lo(x) - umean) * urstd, (bf16_hi(x) - umean) * urstd);
+          }
+          *reinterpret_cast<uint4*>(ut + kb * 16384 + sw128_offset(gt, q * 8)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    }
+    fence_async_smem();
+    named_barrier(1 + g, 128);
+    if (gt == 0 && ok) {
+      tc_fence_after();
+      const uint32_t za = smem_u32(zt), ua = smem_u32(ut);
+      const uint32_t wg = smem_u32(s.wg), wo = smem_u32(s.wo);
+#pragma unroll
+      for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_bf16(tmem_mma, desc_kmajor_sw128(za + kb * 16384) + 2 * kk, desc_kmajor_sw128(wg + kb * 16384) + 2 * kk,
+                   idesc, (kb | kk) != 0);
+#pragma unroll
+      for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_bf16(tmem_mma + 128, desc_kmajor_sw128(ua + kb * 16384) + 2 * kk,
+                   desc_kmajor_sw128(wo + kb * 16384) + 2 * kk, idesc, (kb | kk) != 0);
+      mma_commit(&s.mma[g]);
+    }
+    bool got = ok && mbar_wait(&s.mma[g], it & 1, p.err, kErrTimeoutMma);
+    got = __all_sync(0xFFFFFFFFu, got);
+    tc_fence_after();
+    if (got) {
+      const int j = c0 + gt;
+      const bool keep = !p.masked_zero || (j < p.N && p.mask[b * p.N + r] && p.mask[b * p.N + j]);
+#pragma unroll 1
+      for (int cc = 0; cc < kC; cc += 32) {
+        uint32_t vg[32], vo[32];
+        tmem_ld32(tmem + cc, vg);
+        tmem_ld32(tmem + 128 + cc, vo);
+        tmem_ld_wait();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int ch = cc + q * 8;
+          uint8_t* addr = zt + (ch / 64) * 16384 + sw128_offset(gt, ch % 64);
+          uint4 zv = *reinterpret_cast<const uint4*>(addr);
+          uint32_t w[4] = {zv.x, zv.y, zv.z, zv.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float o2[2];
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+              const int i = q * 8 + e * 2 + h2;
+              const int c = cc + i;
+              const float gl = zrstd * (__uint_as_float(vg[i]) - zmean * s.wsum_gate[c]) + s.bias_gate[c];
+              const float o = __uint_as_float(vo[i]) + s.bias_out[c];
+              const float zold = h2 == 0 ? bf16_lo(w[e]) : bf16_hi(w[e]);
+              o2[h2] = keep ? zold + o * sigmoidf_(gl) : zold;
+            }
+            w[e] = pack_bf16(o2[0], o2[1]);
+          }
+          *reinterpret_cast<uint4*>(addr) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+    }
+    tc_fence_before();
+    fence_async_smem();
+    ok = !named_barrier_or(1 + g, 128, !ok || !got);
+    if (gt == 0 && ok) {
+      tma_store_3d(&map_out, zt, 0, c0, rr);
+      tma_store_3d(&map_out, zt + 16384, 64, c0, rr);
+      tma_store_commit();
+    }
+    if (!ok) break;
+  }
+  if (gt == 0) {
+    tma_store_wait_all0();
+    if (load_pending) mbar_wait(&s.full[g], it & 1, p.err, kErrTimeoutLoad);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(s.tmem_base, 512);
+  }
+}
+
+}  // namespace
+
+size_t trimul_packed_bytes() { return kPackedBytes; }
+
+size_t trimul_workspace_bytes(int B, int N) {
+  const size_t np = (static_cast<size_t>(N) + 7) / 8 * 8;
+  const size_t one = static_cast<size_t>(B) * kH * N * np * 2;
+  const size_t aligned = (one + 255) / 256 * 256;
+  return 3 * aligned;
+}
+
+int trimul_prepare(const TriMulWeights& w, void* packed, cudaStream_t stream) {
+  uint8_t* img = static_cast<uint8_t*>(packed);
+  float* vec = reinterpret_cast<float*>(img + kProjBytes + kGateBytes + kOutBytes);
+  const float* mats[4] = {w.to_left, w.to_left_gate, w.to_right, w.to_right_gate};
+  int rc = 0;
+  for (int i = 0; i < 4 && rc == 0; ++i)
+    rc = launch_pack_weight(mats[i], kH, kC, w.ln_w, w.ln_b, img, i * kH, 512, vec + 0, vec + 512, stream);
+  if (rc == 0)
+    rc = launch_pack_weight(w.to_gate, kC, kC, w.ln_w, w.ln_b, img + kProjBytes, 0, kC, vec + 1024, vec + 1152,
+                            stream);
+  if (rc == 0)
+    rc = launch_pack_weight(w.to_out, kC, kH, w.ln_out_w, w.ln_out_b, img + kProjBytes + kGateBytes, 0, kC, nullptr,
+                            vec + 1280, stream);
+  return rc;
+}
+
+int trimul_forward(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace, int B, int N,
+                   int outgoing, int masked_zero, const DeviceInfo& info, cudaStream_t stream) {
+  const int np = (N + 7) / 8 * 8;
+  const size_t one = static_cast<size_t>(B) * kH * N * np * 2;
+  const size_t aligned = (one + 255) / 256 * 256;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  __nv_bfloat16* left = reinterpret_cast<__nv_bfloat16*>(ws);
+  __nv_bfloat16* right = reinterpret_cast<__nv_bfloat16*>(ws + aligned);
+  __nv_bfloat16* u = reinterpret_cast<__nv_bfloat16*>(ws + 2 * aligned);
+  const int tiles = B * N * ((N + kTile - 1) / kTile);
+  const int grid_groups = (tiles + kGroups - 1) / kGroups;
+  const int grid = grid_groups < info.num_sms ? grid_groups : info.num_sms;
+  int st;
+
+  // pair tensor maps: dims {c, N (col), B*N (row)}
+  CUtensorMap map_z, map_out;
+  {
+    const uint64_t dims[3] = {kC, static_cast<uint64_t>(N), static_cast<uint64_t>(B) * N};
+    const uint64_t strides[2] = {kC * 2, static_cast<uint64_t>(N) * kC * 2};
+    const uint32_t box_row[3] = {64, kTile, 1};
+    const uint32_t box_col[3] = {64, 1, kTile};
+    st = make_map(&map_z, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, z, dims, strides, outgoing ? box_row : box_col,
+                  CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+  }
+  ProjParams pp{static_cast<const uint8_t*>(packed), mask, left, right, B, N, np, outgoing, info.err};
+  const size_t proj_smem = sizeof(ProjSmem) + 1024;
+  cudaFuncSetAttribute(trimul_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(proj_smem));
+  trimul_proj_kernel<<<grid, kThreads, proj_smem, stream>>>(map_z, pp);
+  st = cuda_status(static_cast<int>(cudaGetLastError()), "trimul_proj launch");
+  if (st) return st;
+
+  // contraction: U[c] = L[c] R[c]^T, batch = B * h
+  CUtensorMap map_l, map_r;
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(N), static_cast<uint64_t>(N), static_cast<uint64_t>(B) * kH};
+    const uint64_t strides[2] = {static_cast<uint64_t>(np) * 2, static_cast<uint64_t>(N) * np * 2};
+    const int bn = N > 128 ? 256 : 128;
+    const uint32_t box_a[3] = {64, 128, 1};
+    const uint32_t box_b[3] = {64, static_cast<uint32_t>(bn), 1};
+    st = make_map(&map_l, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, left, dims, strides, box_a, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = make_map(&map_r, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, right, dims, strides, box_b,
+                  CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    GemmParams gp;
+    gp.M = N;
+    gp.N = N;
+    gp.K = N;
+    gp.batch = B * kH;
+    gp.D = u;
+    gp.ldd = np;
+    gp.batch_stride_d = static_cast<int64_t>(N) * np;
+    gp.d_is_f32 = 0;
+    gp.epilogue = kEpiStore;
+    gp.bias = nullptr;
+    gp.residual = nullptr;
+    gp.row_mask = nullptr;
+    gp.err = info.err;
+    st = cuda_status(launch_gemm_nt(map_l, map_r, gp, bn, info.num_sms, stream), "trimul contraction launch");
+    if (st) return st;
+  }
+
+  // output
+  CUtensorMap map_zo, map_u;
+  {
+    const uint64_t dims[3] = {kC, static_cast<uint64_t>(N), static_cast<uint64_t>(B) * N};
+    const uint64_t strides[2] = {kC * 2, static_cast<uint64_t>(N) * kC * 2};
+    const uint32_t box[3] = {64, kTile, 1};
+    st = make_map(&map_zo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, z, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = make_map(&map_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    const uint64_t udims[3] = {static_cast<uint64_t>(N), static_cast<uint64_t>(N), static_cast<uint64_t>(B) * kH};
+    const uint64_t ustrides[2] = {static_cast<uint64_t>(np) * 2, static_cast<uint64_t>(N) * np * 2};
+    const uint32_t ubox[3] = {kTile, 1, kH};
+    st = make_map(&map_u, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, u, udims, ustrides, ubox, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st) return st;
+  }
+  OutParams op{static_cast<const uint8_t*>(packed), mask, B, N, masked_zero, info.err};
+  const size_t out_smem = sizeof(OutSmem) + 1024;
+  cudaFuncSetAttribute(trimul_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(out_smem));
+  trimul_out_kernel<<<grid, kThreads, out_smem, stream>>>(map_zo, map_u, map_out, op);
+  return cuda_status(static_cast<int>(cudaGetLastError()), "trimul_out launch");
+}
+
+}  // namespace ffb

@@ -1,0 +1,127 @@
+"""Torch-facing wrappers of the C ABI: tensors in, tensors out, on the current stream.
+
+These wrappers only check tensors and pass raw pointers; all arithmetic runs in the
+sm_100a kernels of ``_ffb.so``. A tensor on the CPU, of another dtype or with an
+unsupported layout is refused with :class:`~foldforge_b200._lib.UnsupportedCall`
+before anything is launched.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from foldforge_b200 import _lib
+
+Tensor = torch.Tensor
+BF16, F32 = 0, 1
+EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU = 0, 1, 2
+_DTYPES = {torch.bfloat16: BF16, torch.float32: F32}
+
+
+def _ptr(t: Tensor | None) -> ctypes.c_void_p:
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _need_cuda(*ts: Tensor | None) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise _lib.UnsupportedCall("foldforge_b200", 2, "tensor is not on a CUDA device")
+
+
+def layer_norm(x: Tensor, weight: Tensor | None, bias: Tensor | None, eps: float = 1e-5) -> Tensor:
+    """LayerNorm over the last axis (fp32 affine), output in ``x.dtype``."""
+    _need_cuda(x, weight, bias)
+    if x.dtype not in _DTYPES:
+        raise _lib.UnsupportedCall("layer_norm", 2, f"dtype {x.dtype}")
+    x = x.contiguous()
+    y = torch.empty_like(x)
+    c = x.shape[-1]
+    w = None if weight is None else weight.detach().float().contiguous()
+    b = None if bias is None else bias.detach().float().contiguous()
+    _lib.call("ffb_layernorm_fwd", _ptr(x), _ptr(y), _ptr(w), _ptr(b), x.numel() // c, c, ctypes.c_float(eps),
+              _DTYPES[x.dtype], _stream())
+    return y
+
+
+def gemm_nt(
+    a: Tensor,
+    b: Tensor,
+    *,
+    bias: Tensor | None = None,
+    epilogue: int = EPI_STORE,
+    residual: Tensor | None = None,
+    row_mask: Tensor | None = None,
+    out_dtype: torch.dtype = torch.bfloat16,
+    out: Tensor | None = None,
+) -> Tensor:
+    """``a @ b.T`` on the tensor cores: ``a [.., m, k]``, ``b [.., n, k]`` bf16 (same batch
+    shape or ``b`` 2-D), fp32 accumulation, output ``out_dtype``."""
+    _need_cuda(a, b, bias, residual, row_mask)
+    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
+        raise _lib.UnsupportedCall("gemm_nt", 2, "operands must be bf16")
+    a = a.contiguous()
+    b = b.contiguous()
+    k = a.shape[-1]
+    n = b.shape[-2]
+    if b.dim() == 2:  # shared weight: fold every leading axis of a into the rows
+        m, batch, sb = a.numel() // k, 1, 0
+    else:
+        m = a.shape[-2]
+        batch = a.numel() // (m * k)
+        sb = n * k
+    n_out = n // 2 if epilogue == EPI_SWIGLU else n
+    if out is None:
+        out = torch.empty(*a.shape[:-1], n_out, device=a.device, dtype=out_dtype)
+    if residual is not None:
+        residual = residual.contiguous()
+    mask = None if row_mask is None else row_mask.to(torch.uint8).contiguous()
+    _lib.call(
+        "ffb_gemm_bf16_nt", _ptr(a), _ptr(b), _ptr(out), batch, m, n, k, k, k, n_out, m * k, sb, m * n_out,
+        _DTYPES[out.dtype], _ptr(None if bias is None else bias.float().contiguous()), epilogue, _ptr(residual),
+        _ptr(mask), _stream(),
+    )
+    return out
+
+
+def _f32(t: Tensor) -> Tensor:
+    return t.detach().to(torch.float32).contiguous()
+
+
+def trimul_prepare(weights: dict[str, Tensor], device: torch.device) -> Tensor:
+    """Pack a ``TriangleMultiplication``'s fp32 weights (engine keys) for the kernels."""
+    lib = _lib.load()
+    packed = torch.empty(int(lib.ffb_trimul_packed_bytes()), dtype=torch.uint8, device=device)
+    keys = ("ln_pair.weight", "ln_pair.bias", "ln_out.weight", "ln_out.bias", "to_left.weight", "to_right.weight",
+            "to_left_gate.weight", "to_right_gate.weight", "to_out.weight", "to_gate.weight")
+    ts = [_f32(weights[k]).to(device) for k in keys]
+    _need_cuda(*ts)
+    _lib.call("ffb_trimul_prepare", *[_ptr(t) for t in ts], _ptr(packed), _stream())
+    packed._keepalive = ts  # the pack kernel reads them asynchronously
+    return packed
+
+
+def _mask_u8(mask: Tensor) -> Tensor:
+    return mask.to(torch.uint8).contiguous()
+
+
+def trimul(z: Tensor, mask: Tensor, packed: Tensor, *, outgoing: bool, masked_zero: bool = True) -> Tensor:
+    """Triangle multiplicative update with residual: ``z [B, N, N, 128]`` bf16, ``mask [B, N]``."""
+    _need_cuda(z, mask, packed)
+    if z.dtype != torch.bfloat16 or z.dim() != 4 or z.shape[-1] != 128:
+        raise _lib.UnsupportedCall("trimul", 2, f"needs bf16 [B, N, N, 128], got {z.dtype} {tuple(z.shape)}")
+    z = z.contiguous()
+    b, n = z.shape[0], z.shape[1]
+    lib = _lib.load()
+    ws_bytes = int(lib.ffb_trimul_workspace_bytes(b, n))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=z.device)
+    out = torch.empty_like(z)
+    m = _mask_u8(mask)
+    _lib.call("ffb_trimul_fwd", _ptr(z), _ptr(m), _ptr(packed), _ptr(out), _ptr(ws), ctypes.c_size_t(ws_bytes), b, n,
+              int(outgoing), int(masked_zero), _stream())
+    return out

@@ -1,0 +1,101 @@
+/*
+ * foldforge_b200 C ABI: B200 (sm_100a) kernels of FoldForge's Pairformer pair stack.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream (`void*`, a
+ * cudaStream_t; NULL = the legacy default stream) and returns an ffb_status. Entry points
+ * enqueue work on the stream and return without synchronising the host, allocate nothing
+ * (scratch space is passed in by the caller), and keep no state between calls other than
+ * per-device caches (SM count, the device error word's address), so they are safe to
+ * call from several host threads and to capture in a CUDA graph.
+ *
+ * Layouts (bf16 = IEEE bfloat16, row-major, last axis contiguous):
+ *   pair  z      [B, N, N, c_z]    channels last, c_z = 128
+ *   single s     [B, N, c_s]
+ *   key mask     [B, N]            uint8, 1 = real token, 0 = padding
+ * Each op returns its input PLUS its update (the engine classes own their residual).
+ *
+ * Device-side waits are bounded: a launch that cannot make progress records a code in a
+ * per-device error word and exits; ffb_device_error() reads (and clears) it.
+ *
+ * The reference interfaces these entry points replace are the engine modules FoldForge
+ * calls through its backend guard (src/foldforge/modules/engine/policy.py:85-101); each
+ * declaration names the reference equations it computes.
+ */
+#ifndef FOLDFORGE_B200_H
+#define FOLDFORGE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  FFB_OK = 0,
+  FFB_ERR_ARG = 1,         /* a pointer, size or stride the entry point cannot take */
+  FFB_ERR_UNSUPPORTED = 2, /* a shape / dtype outside the kernels' range (the backend's refusal) */
+  FFB_ERR_CUDA = 3,        /* a CUDA runtime error while enqueueing */
+  FFB_ERR_DEVICE = 4       /* a device-side error word was set (see ffb_device_error) */
+} ffb_status;
+
+typedef enum { FFB_BF16 = 0, FFB_F32 = 1 } ffb_dtype;
+
+/* Masked-position policy of the pair/single updates.
+ * FFB_MASKED_COMPUTE: every position gets the reference equations' update, including
+ *   padded ones (what FoldForge's legacy block computes, legacy/pairformer.py:191-229).
+ * FFB_MASKED_ZERO: the update at every pair (i, j) with mask_i * mask_j == 0, and at
+ *   every padded single row, is exactly 0 (the output equals the input there). */
+typedef enum { FFB_MASKED_COMPUTE = 0, FFB_MASKED_ZERO = 1 } ffb_masked;
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int ffb_version(void);
+
+/* Human-readable text of the last non-OK status returned on this host thread. */
+const char* ffb_last_error(void);
+
+/* Synchronises `stream`, then reads and clears the current device's error word. */
+int ffb_device_error(int* code, void* stream);
+
+/* LayerNorm over the last axis: y = (x - mean) / sqrt(var + eps) * gamma + beta.
+ * x, y [rows, c] of `dtype`; gamma, beta fp32 [c] or NULL (affine skipped).
+ * Replaces the engine `LayerNorm` op (src/foldforge/modules/engine/modules.py:230-238). */
+int ffb_layernorm_fwd(const void* x, void* y, const float* gamma, const float* beta, int64_t rows, int c, float eps,
+                      int dtype, void* stream);
+
+/* Batched bf16 GEMM, D[b] = A[b] @ B[b]^T with fp32 accumulation on the tensor cores.
+ * A [batch, m, k] (row stride lda, batch stride sa), B [batch, n, k] (ldb, sb), D [batch, m, n]
+ * (ldd, sd) of d_dtype. Strides in elements; lda, ldb multiples of 8; k % 8 == 0.
+ * epilogue: 0 store (+bias[n] fp32 if non-NULL); 1 residual: D = R + (acc + bias) * row_mask[m]
+ * (R like D; row_mask uint8 [batch, m] or NULL); 2 SwiGLU over a/b rows interleaved in blocks
+ * of 16 (D has n / 2 columns).
+ * The plain projections of the single track (legacy/transformer.py:88-133). */
+int ffb_gemm_bf16_nt(const void* a, const void* b, void* d, int batch, int m, int n, int k, int64_t lda,
+                     int64_t ldb, int64_t ldd, int64_t sa, int64_t sb, int64_t sd, int d_dtype, const float* bias,
+                     int epilogue, const void* residual, const uint8_t* row_mask, void* stream);
+
+/* ---- Triangle multiplicative update (c_z = hidden = 128, bf16 activations).
+ * Replaces the engine `TriangleMultiplication` (outgoing / incoming) as FoldForge calls it
+ * (src/foldforge/modules/engine/modules.py:144-163); equations of
+ * legacy/reference/triangle.py:19-50 with the engine weight names of
+ * legacy/released.py:135-173.
+ *
+ * ffb_trimul_prepare packs the fp32 master weights (all [out, in] row-major, LayerNorm
+ * vectors [128]) into `packed` (ffb_trimul_packed_bytes() bytes, 16-byte aligned). Run it
+ * once per weight update; the forward pass only reads the packed image.
+ * ffb_trimul_fwd: z, out [B, N, N, 128] bf16 (out may not alias z), mask [B, N] uint8,
+ * workspace of ffb_trimul_workspace_bytes(B, N) bytes (256-byte aligned). */
+size_t ffb_trimul_packed_bytes(void);
+size_t ffb_trimul_workspace_bytes(int B, int N);
+int ffb_trimul_prepare(const float* ln_w, const float* ln_b, const float* ln_out_w, const float* ln_out_b,
+                       const float* to_left, const float* to_right, const float* to_left_gate,
+                       const float* to_right_gate, const float* to_out, const float* to_gate, void* packed,
+                       void* stream);
+int ffb_trimul_fwd(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace,
+                   size_t workspace_bytes, int B, int N, int outgoing, int masked, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FOLDFORGE_B200_H */

@@ -1,0 +1,75 @@
+"""Each pair-stack op on the B200 against the CPU oracle (same seeded weights and inputs).
+
+Master precision (fp32 weights, bf16 activations): the reference's bf16 tolerance is a
+relative RMS of 0.03 (tests/kernels/test_backends_cuda.py:58-59); here every op's OUTPUT
+must be within relative L2 1e-2 of the fp32 oracle and its UPDATE (output - input) within
+2e-2, both on every position (the masked ones included) in "compute" mode.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+import oracle  # noqa: E402
+from foldforge_b200 import _lib, kernels  # noqa: E402
+from foldforge_b200.synthetic import block_state  # noqa: E402
+
+OUT_TOL = 1e-2
+DELTA_TOL = 2e-2
+
+
+def sub(state, prefix):
+    return {k[len(prefix) + 1 :]: v for k, v in state.items() if k.startswith(prefix + ".")}
+
+
+@pytest.fixture(scope="module")
+def weights():
+    return block_state(torch.Generator().manual_seed(11), scheme="randomise")
+
+
+def pair_inputs(b, n, masked, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    z = torch.randn(b, n, n, 128, generator=g).bfloat16()
+    tokens = torch.ones(b, n)
+    for i in range(b):
+        if masked:
+            tokens[i, n - masked - i :] = 0
+    return z, tokens
+
+
+@pytest.fixture(autouse=True)
+def _no_device_error():
+    yield
+    assert _lib.device_error() == 0
+
+
+CASES = [(1, 24, 3), (1, 130, 10), (2, 64, 5), (1, 256, 13), (1, 1, 0)]
+
+
+@pytest.mark.parametrize("outgoing", [True, False])
+@pytest.mark.parametrize("b,n,masked", CASES)
+def test_trimul_matches_oracle(weights, outgoing, b, n, masked):
+    name = "tri_multi_outgoing" if outgoing else "tri_multi_incoming"
+    p = sub(weights, name)
+    z, tokens = pair_inputs(b, n, masked)
+    packed = kernels.trimul_prepare(p, torch.device("cuda"))
+    got = kernels.trimul(z.cuda(), tokens.cuda() > 0, packed, outgoing=outgoing, masked_zero=False).float().cpu()
+    for i in range(b):
+        want = oracle.triangle_multiplication(z[i].float(), tokens[i], p, outgoing=outgoing)
+        assert oracle.rel_l2(got[i], want) < OUT_TOL
+        assert oracle.rel_l2(got[i] - z[i].float(), want - z[i].float()) < DELTA_TOL
+
+
+@pytest.mark.parametrize("outgoing", [True, False])
+def test_trimul_masked_zero_leaves_padding_untouched(weights, outgoing):
+    p = sub(weights, "tri_multi_outgoing" if outgoing else "tri_multi_incoming")
+    z, tokens = pair_inputs(1, 150, 20, seed=3)
+    packed = kernels.trimul_prepare(p, torch.device("cuda"))
+    got = kernels.trimul(z.cuda(), tokens.cuda() > 0, packed, outgoing=outgoing, masked_zero=True).cpu()
+    pm = (tokens[0][:, None] * tokens[0][None, :]) > 0
+    assert torch.equal(got[0][~pm], z[0][~pm])
+    want = oracle.triangle_multiplication(z[0].float(), tokens[0], p, outgoing=outgoing)
+    assert oracle.rel_l2(got[0].float()[pm] - z[0].float()[pm], want[pm] - z[0].float()[pm]) < DELTA_TOL
