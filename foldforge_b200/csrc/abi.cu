@@ -223,4 +223,40 @@ int ffb_trimul_fwd(const void* z, const uint8_t* mask, const void* packed, void*
                         static_cast<cudaStream_t>(stream));
 }
 
+size_t ffb_triattn_packed_bytes(void) { return triattn_packed_bytes(); }
+
+size_t ffb_triattn_workspace_bytes(int B, int N) { return (B <= 0 || N <= 0) ? 0 : triattn_workspace_bytes(B, N); }
+
+int ffb_triattn_prepare(const float* ln_w, const float* ln_b, const float* to_bias, const float* to_query,
+                        const float* to_key, const float* to_value, const float* to_gate, const float* to_out,
+                        void* packed, void* stream) {
+  if (!ln_w || !ln_b || !to_bias || !to_query || !to_key || !to_value || !to_gate || !to_out || !packed)
+    return fail(FFB_ERR_ARG, "triattn_prepare: null pointer");
+  if ((reinterpret_cast<uintptr_t>(packed) & 15u) != 0) return fail(FFB_ERR_ARG, "triattn_prepare: packed not 16-byte aligned");
+  DeviceInfo info;
+  int st = device_info(&info);
+  if (st != FFB_OK) return st;
+  TriAttnWeights w{ln_w, ln_b, to_bias, to_query, to_key, to_value, to_gate, to_out};
+  return cuda_status(triattn_prepare(w, packed, static_cast<cudaStream_t>(stream)), "triattn_prepare");
+}
+
+int ffb_triattn_fwd(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace,
+                    size_t workspace_bytes, int B, int N, int starting, int masked, void* stream) {
+  if (B <= 0 || N <= 0) return fail(FFB_ERR_ARG, "triattn_fwd: empty problem B=%d N=%d", B, N);
+  if (!z || !mask || !packed || !out || !workspace) return fail(FFB_ERR_ARG, "triattn_fwd: null pointer");
+  if (z == out) return fail(FFB_ERR_ARG, "triattn_fwd: out must not alias z");
+  if (masked != FFB_MASKED_COMPUTE && masked != FFB_MASKED_ZERO) return fail(FFB_ERR_ARG, "triattn_fwd: masked=%d", masked);
+  if (workspace_bytes < triattn_workspace_bytes(B, N))
+    return fail(FFB_ERR_ARG, "triattn_fwd: workspace %zu < %zu bytes", workspace_bytes, triattn_workspace_bytes(B, N));
+  if (((reinterpret_cast<uintptr_t>(z) | reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(packed)) & 15u) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(FFB_ERR_ARG, "triattn_fwd: misaligned pointer");
+  if (static_cast<int64_t>(B) * N * 4 > (1 << 30) / 128) return fail(FFB_ERR_UNSUPPORTED, "triattn_fwd: B*N too large");
+  DeviceInfo info;
+  int st = device_info(&info);
+  if (st != FFB_OK) return st;
+  return triattn_forward(z, mask, packed, out, workspace, B, N, starting != 0, masked == FFB_MASKED_ZERO, info,
+                         static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -241,6 +241,18 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// K-major operand tile in the 64-byte swizzle layout: rows of 32 bf16 (64 B), 8-row groups
+// 512 B apart; +32 bytes on the start address advances K by 16 elements.
+__device__ __forceinline__ uint64_t desc_kmajor_sw64(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;
+  d |= static_cast<uint64_t>(512u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(4u) << 61;  // SWIZZLE_64B
+  return d;
+}
+
 // Instruction descriptor: bf16 x bf16 -> fp32, both operands K-major, shape M x N.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
   return (1u << 4)                                  // D format: f32

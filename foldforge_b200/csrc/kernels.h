@@ -38,7 +38,8 @@ int launch_layernorm(const void* x, void* y, const float* gamma, const float* be
 // shared-memory image at row offset `row_offset` of an image with `image_rows` rows;
 // writes wsum / bias (W beta) per row when the pointers are non-null.
 int launch_pack_weight(const float* w, int rows, int k, const float* gamma, const float* beta, uint8_t* image,
-                       int row_offset, int image_rows, float* wsum, float* bias, cudaStream_t stream);
+                       int row_offset, int image_rows, float* wsum, float* bias, cudaStream_t stream,
+                       float scale = 1.0f);
 
 struct DeviceInfo;
 
@@ -52,5 +53,15 @@ size_t trimul_workspace_bytes(int B, int N);
 int trimul_prepare(const TriMulWeights& w, void* packed, cudaStream_t stream);
 int trimul_forward(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace, int B, int N,
                    int outgoing, int masked_zero, const DeviceInfo& info, cudaStream_t stream);
+
+// ---- triangle attention (c_z = 128, 4 heads x 32)
+struct TriAttnWeights {
+  const float *ln_w, *ln_b, *to_bias, *to_query, *to_key, *to_value, *to_gate, *to_out;
+};
+size_t triattn_packed_bytes();
+size_t triattn_workspace_bytes(int B, int N);
+int triattn_prepare(const TriAttnWeights& w, void* packed, cudaStream_t stream);
+int triattn_forward(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace, int B, int N,
+                    int starting, int masked_zero, const DeviceInfo& info, cudaStream_t stream);
 
 }  // namespace ffb

@@ -20,7 +20,7 @@ namespace {
 
 __global__ void pack_weight_kernel(const float* __restrict__ w, int rows, int k, const float* __restrict__ gamma,
                                    const float* __restrict__ beta, uint8_t* __restrict__ image, int row_offset,
-                                   int image_rows, float* __restrict__ wsum, float* __restrict__ bias) {
+                                   int image_rows, float* __restrict__ wsum, float* __restrict__ bias, float scale) {
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= rows) return;
   const float* wr = w + static_cast<int64_t>(r) * k;
@@ -28,7 +28,7 @@ __global__ void pack_weight_kernel(const float* __restrict__ w, int rows, int k,
   const int dst_row = row_offset + r;
   for (int c = 0; c < k; ++c) {
     const float g = gamma ? gamma[c] : 1.0f;
-    const __nv_bfloat16 q = __float2bfloat16_rn(wr[c] * g);
+    const __nv_bfloat16 q = __float2bfloat16_rn(wr[c] * g * scale);
     s += __bfloat162float(q);
     if (beta) bsum += wr[c] * beta[c];
     const int kb = c / 64;
@@ -36,15 +36,15 @@ __global__ void pack_weight_kernel(const float* __restrict__ w, int rows, int k,
     *reinterpret_cast<__nv_bfloat16*>(block + sw128_offset(dst_row, c % 64)) = q;
   }
   if (wsum) wsum[dst_row] = s;
-  if (bias) bias[dst_row] = bsum;
+  if (bias) bias[dst_row] = bsum * scale;
 }
 
 }  // namespace
 
 int launch_pack_weight(const float* w, int rows, int k, const float* gamma, const float* beta, uint8_t* image,
-                       int row_offset, int image_rows, float* wsum, float* bias, cudaStream_t stream) {
+                       int row_offset, int image_rows, float* wsum, float* bias, cudaStream_t stream, float scale) {
   pack_weight_kernel<<<(rows + 127) / 128, 128, 0, stream>>>(w, rows, k, gamma, beta, image, row_offset, image_rows,
-                                                             wsum, bias);
+                                                             wsum, bias, scale);
   return static_cast<int>(cudaGetLastError());
 }
 

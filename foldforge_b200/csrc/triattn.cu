@@ -1,0 +1,944 @@
+// Triangle attention around the starting / ending node, bf16 activations, c_z = 128,
+// 4 heads x 32 (AF3: untransposed pair bias, no projection biases).
+//
+//   x = LN(z);  b_h[q, k] = W_b x[q, k];  per problem row r:
+//   o[r, q] = sum_k softmax_k(q[r,q] . k[r,k] / sqrt(32) + b_h[q, k], key mask m_r m_k) v[r, k]
+//   z' = z + W_o (sigmoid(W_g x) * o)
+// The starting node's problem row r is pair row i (q, k index columns); the ending node's
+// is pair column j (q, k index rows) and its output is written back transposed
+// (legacy/attention.py:108-171 with spec.py:125,437,470; masked logits are REPLACED by
+// -1e9, legacy/reference/attention.py:14-54, so a fully masked row averages uniformly).
+//
+// Three launches:
+//  1. triattn_proj: 128-pair tiles of raw z (row tiles for the starting node, column
+//     tiles for the ending node, so every write below is coalesced) x the resident packed
+//     [W_q; W_k; W_v; W_b] with the input LayerNorm folded into the epilogue. W_q carries
+//     log2(e)/sqrt(32) and W_b log2(e), so the softmax works in base 2. Writes
+//     Q, K [B, N(r), H, N(n), 32], V^T [B, N(r), H, 32, Np(n)] and the bias
+//     [B, H, N, Np] (starting: [q][k]; ending: [k][q]).
+//  2. triattn_attn: flash attention on tcgen05. A CTA owns 256 queries (two groups of
+//     128, one per softmax warpgroup) of one (row, head) and streams 64-key blocks of K,
+//     V^T and the bias through a 3-stage TMA ring shared by both groups. S = Q K^T and
+//     P V run on the tensor cores with fp32 accumulators in TMEM (double-buffered);
+//     each softmax thread owns one query row (exact online softmax, running max) and
+//     accumulates the P V partials in registers.
+//  3. triattn_out: per 128-pair tile (natural layout for both nodes), the gate GEMM on
+//     raw z (folded LayerNorm), sigmoid(gate) * o written back as a K-major operand, the
+//     output GEMM, mask and residual, TMA store.
+#include "abi_util.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ffb {
+namespace {
+
+constexpr int kC = 128;
+constexpr int kHeads = 4;
+constexpr int kD = 32;
+constexpr int kTile = 128;
+constexpr int kGroups = 2;
+constexpr int kProjRows = 400;  // Q 128 | K 128 | V 128 | bias 16 (4 used)
+constexpr float kLog2e = 1.4426950408889634f;
+
+constexpr size_t kProjBytes = static_cast<size_t>(kProjRows) * kC * 2;  // 102400
+constexpr size_t kGateBytes = kC * kC * 2;
+constexpr size_t kOutBytes = kC * kC * 2;
+constexpr size_t kVecFloats = 2 * kProjRows + 2 * 128;
+constexpr size_t kPackedBytes = kProjBytes + kGateBytes + kOutBytes + kVecFloats * 4;
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void tile_stats(const uint8_t* tile, int row, float& mean, float& rstd) {
+  float s = 0.f;
+  uint4 v[16];
+#pragma unroll
+  for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      v[kb * 8 + q] = *reinterpret_cast<const uint4*>(tile + kb * 16384 + sw128_offset(row, q * 8));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) s += bf16_lo(w[j]) + bf16_hi(w[j]);
+  }
+  mean = s * (1.0f / kC);
+  float q2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float a = bf16_lo(w[j]) - mean, b = bf16_hi(w[j]) - mean;
+      q2 += a * a + b * b;
+    }
+  }
+  rstd = rsqrtf(q2 * (1.0f / kC) + 1e-5f);
+}
+
+// ====================================================================== 1. projection
+struct ProjSmem {
+  alignas(1024) uint8_t w[kProjBytes];
+  alignas(1024) uint8_t z[kGroups][kTile * kC * 2];
+  float wsum[kProjRows];
+  float bias[kProjRows];
+  uint64_t wbar;
+  uint64_t full[kGroups];
+  uint64_t mma[kGroups];
+  uint32_t tmem_base;
+};
+
+struct ProjParams {
+  const uint8_t* packed;
+  __nv_bfloat16* q;     // [B, N, H, N, 32]
+  __nv_bfloat16* k;     // [B, N, H, N, 32]
+  __nv_bfloat16* vt;    // [B, N, H, 32, Np]
+  __nv_bfloat16* bias;  // [B, H, N, Np]
+  int B, N, Np;
+  int starting;
+  int* err;
+};
+
+__global__ void __launch_bounds__(256, 1)
+    triattn_proj_kernel(const __grid_constant__ CUtensorMap map_z, ProjParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  ProjSmem& s = *reinterpret_cast<ProjSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int g = threadIdx.x / 128;
+  const int gt = threadIdx.x % 128;
+  const int warp = threadIdx.x / 32;
+  const int tiles_per_row = (p.N + kTile - 1) / kTile;
+  const int total = p.B * p.N * tiles_per_row;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&s.wbar, 1);
+    for (int i = 0; i < kGroups; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.mma[i], 1);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&s.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x == 0) {
+    tma_prefetch_map(&map_z);
+    mbar_arrive_expect_tx(&s.wbar, kProjBytes);
+    for (int off = 0; off < static_cast<int>(kProjBytes); off += 25600)
+      bulk_load(s.w + off, p.packed + off, 25600, &s.wbar);
+  }
+  {
+    const float* v = reinterpret_cast<const float*>(p.packed + kProjBytes + kGateBytes + kOutBytes);
+    for (int i = threadIdx.x; i < kProjRows; i += 256) {
+      s.wsum[i] = v[i];
+      s.bias[i] = v[kProjRows + i];
+    }
+  }
+  __syncthreads();
+  bool ok = mbar_wait(&s.wbar, 0, p.err, kErrTimeoutLoad);
+  const uint32_t tmem = s.tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16) + g * 256;
+  const uint32_t tmem_mma = s.tmem_base + g * 256;
+  uint8_t* zt = s.z[g];
+  int it = 0;
+  bool load_pending = false;
+  for (int tile = blockIdx.x * kGroups + g; tile < total; tile += gridDim.x * kGroups, ++it) {
+    const int c0 = (tile % tiles_per_row) * kTile;
+    const int rr = tile / tiles_per_row;
+    const int b = rr / p.N;
+    const int r = rr - b * p.N;  // problem row
+    if (gt == 0 && ok) {
+      mbar_arrive_expect_tx(&s.full[g], kTile * kC * 2);
+      for (int kb = 0; kb < 2; ++kb) {
+        if (p.starting)
+          tma_load_3d(zt + kb * 16384, &map_z, &s.full[g], kb * 64, c0, rr);          // z[b, r, c0 + t]
+        else
+          tma_load_3d(zt + kb * 16384, &map_z, &s.full[g], kb * 64, r, b * p.N + c0);  // z[b, c0 + t, r]
+      }
+      load_pending = true;
+    }
+    ok = ok && mbar_wait(&s.full[g], it & 1, p.err, kErrTimeoutLoad);
+    if (gt == 0 && ok) load_pending = false;
+    float mean = 0.f, rstd = 0.f;
+    if (ok) tile_stats(zt, gt, mean, rstd);
+    const int n = c0 + gt;
+    const bool valid = n < p.N;
+    for (int half = 0; half < 2; ++half) {
+      const int ncols = half == 0 ? 256 : 144;
+      if (gt == 0 && ok) {
+        tc_fence_after();
+        const uint32_t idesc = idesc_bf16_f32(128, ncols);
+        const uint32_t a0 = smem_u32(zt);
+        const uint32_t b0 = smem_u32(s.w) + half * 256 * 128;
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_bf16(tmem_mma, desc_kmajor_sw128(a0 + kb * 16384) + 2 * kk,
+                     desc_kmajor_sw128(b0 + kb * (kProjRows * 128)) + 2 * kk, idesc, (kb | kk) != 0);
+        mma_commit(&s.mma[g]);
+      }
+      bool got = ok && mbar_wait(&s.mma[g], half, p.err, kErrTimeoutMma);
+      got = __all_sync(0xFFFFFFFFu, got);
+      tc_fence_after();
+      if (got) {
+        const int64_t row_base = (static_cast<int64_t>(b) * p.N + r) * kHeads;  // (b, r) -> head 0
+        if (half == 0) {
+          // Q (cols 0..127) and K (cols 128..255): one head = 32 columns = 64 contiguous bytes
+#pragma unroll 1
+          for (int cc = 0; cc < 256; cc += 32) {
+            uint32_t v[32];
+            tmem_ld32(tmem + cc, v);
+            tmem_ld_wait();
+            if (valid) {
+              uint32_t w[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const int c = cc + 2 * i;
+                const float a = rstd * (__uint_as_float(v[2 * i]) - mean * s.wsum[c]) + s.bias[c];
+                const float bb = rstd * (__uint_as_float(v[2 * i + 1]) - mean * s.wsum[c + 1]) + s.bias[c + 1];
+                w[i] = pack_bf16(a, bb);
+              }
+              const int head = (cc % 128) / 32;
+              __nv_bfloat16* base = (cc < 128 ? p.q : p.k) + ((row_base + head) * p.N + n) * kD;
+              uint4* dst = reinterpret_cast<uint4*>(base);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+            }
+          }
+        } else {
+          // V (cols 0..127) -> V^T[b, r, head, d, n]; bias (cols 128..131) -> [b, head, r, n]
+#pragma unroll 1
+          for (int cc = 0; cc < 128; cc += 32) {
+            uint32_t v[32];
+            tmem_ld32(tmem + cc, v);
+            tmem_ld_wait();
+            if (valid) {
+              const int head = cc / 32;
+              __nv_bfloat16* base = p.vt + (row_base + head) * kD * p.Np + n;
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const int c = 256 + cc + i;
+                base[static_cast<int64_t>(i) * p.Np] =
+                    __float2bfloat16_rn(rstd * (__uint_as_float(v[i]) - mean * s.wsum[c]) + s.bias[c]);
+              }
+            }
+          }
+          uint32_t v[16];
+          tmem_ld16(tmem + 128, v);
+          tmem_ld_wait();
+          if (valid) {
+#pragma unroll
+            for (int h = 0; h < kHeads; ++h) {
+              const int c = 384 + h;
+              p.bias[((static_cast<int64_t>(b) * kHeads + h) * p.N + r) * p.Np + n] =
+                  __float2bfloat16_rn(rstd * (__uint_as_float(v[h]) - mean * s.wsum[c]) + s.bias[c]);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      ok = !named_barrier_or(1 + g, 128, !ok || !got);
+    }
+    if (!ok) break;
+  }
+  if (gt == 0 && load_pending) mbar_wait(&s.full[g], it & 1, p.err, kErrTimeoutLoad);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(s.tmem_base, 512);
+  }
+}
+
+// ====================================================================== 2. attention
+constexpr int kKB = 64;        // keys per block
+constexpr int kKVStages = 3;
+constexpr int kAttnThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 softmax (2 groups)
+constexpr int kMaxMaskWords = 2048;  // B * ceil(N / 64) * 2 words of key-mask bits
+
+struct AttnSmem {
+  alignas(1024) uint8_t q[kGroups][kTile * kD * 2];          // 8 KB each, SW64
+  alignas(1024) uint8_t k[kKVStages][kKB * kD * 2];          // 4 KB, SW64
+  alignas(1024) uint8_t vt[kKVStages][kD * kKB * 2];         // 4 KB, SW128
+  alignas(1024) uint8_t bias[kKVStages][kGroups][kTile * kKB * 2];  // 16 KB each
+  alignas(1024) uint8_t p[kGroups][2][kTile * kKB * 2];      // 16 KB each, SW128
+  uint32_t mask_words[kMaxMaskWords];
+  uint64_t q_full, q_empty;
+  uint64_t kv_full[kKVStages], kv_empty[kKVStages];
+  uint64_t s_full[kGroups][2], s_free[kGroups][2];
+  uint64_t p_full[kGroups][2];
+  uint64_t o_full[kGroups][2], o_free[kGroups][2];
+  uint32_t tmem_base;
+};
+
+struct AttnParams {
+  const uint8_t* mask;   // [B, N]
+  __nv_bfloat16* o;      // natural pair layout [B, N, N, 128]
+  int B, N;
+  int starting;
+  int qpairs;            // ceil(ceil(N / 128) / 2)
+  int words_per_batch;   // 2 * ceil(N / 64)
+  int* err;
+};
+
+__device__ __forceinline__ void unit_coords(int unit, const AttnParams& p, int& b, int& r, int& h, int& qp) {
+  qp = unit % p.qpairs;
+  int rest = unit / p.qpairs;
+  h = rest % kHeads;
+  rest /= kHeads;
+  r = rest % p.N;
+  b = rest / p.N;
+}
+
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    triattn_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                        const __grid_constant__ CUtensorMap map_vt, const __grid_constant__ CUtensorMap map_bias,
+                        AttnParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  AttnSmem& s = *reinterpret_cast<AttnSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int units = p.B * p.N * kHeads * p.qpairs;
+  const int nkb = (p.N + kKB - 1) / kKB;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&s.q_full, 1);
+    mbar_init(&s.q_empty, 1);
+    for (int i = 0; i < kKVStages; ++i) {
+      mbar_init(&s.kv_full[i], 1);
+      mbar_init(&s.kv_empty[i], 1 + 8);  // MMA commit + 8 softmax warps (bias read)
+    }
+    for (int g = 0; g < kGroups; ++g)
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(&s.s_full[g][i], 1);
+        mbar_init(&s.s_free[g][i], 4);
+        mbar_init(&s.p_full[g][i], 4);
+        mbar_init(&s.o_full[g][i], 1);
+        mbar_init(&s.o_free[g][i], 4);
+      }
+    fence_mbar_init();
+  }
+  // key-mask bits, per batch padded to whole 64-key blocks (zero beyond N)
+  for (int w = threadIdx.x; w < p.B * p.words_per_batch; w += kAttnThreads) {
+    const int b = w / p.words_per_batch;
+    const int k0 = (w % p.words_per_batch) * 32;
+    uint32_t bits = 0;
+    for (int i = 0; i < 32; ++i) {
+      const int k = k0 + i;
+      if (k < p.N && p.mask[b * p.N + k]) bits |= 1u << i;
+    }
+    s.mask_words[w] = bits;
+  }
+  if (warp == 0) {
+    tmem_alloc(&s.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem0 = s.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_map(&map_q);
+      tma_prefetch_map(&map_k);
+      tma_prefetch_map(&map_vt);
+      tma_prefetch_map(&map_bias);
+      int kv_it = 0, u_it = 0;
+      bool ok = true;
+      for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x, ++u_it) {
+        int b, r, h, qp;
+        unit_coords(unit, p, b, r, h, qp);
+        const int qrow = (b * p.N + r) * kHeads + h;
+        if (!mbar_wait(&s.q_empty, (u_it & 1) ^ 1, p.err, kErrTimeoutEmpty)) { ok = false; break; }
+        mbar_arrive_expect_tx(&s.q_full, kGroups * kTile * kD * 2);
+        for (int g = 0; g < kGroups; ++g) tma_load_3d(s.q[g], &map_q, &s.q_full, 0, (qp * 2 + g) * kTile, qrow);
+        for (int j = 0; j < nkb; ++j, ++kv_it) {
+          const int st = kv_it % kKVStages;
+          if (!mbar_wait(&s.kv_empty[st], ((kv_it / kKVStages) & 1) ^ 1, p.err, kErrTimeoutEmpty)) { ok = false; break; }
+          mbar_arrive_expect_tx(&s.kv_full[st], kKB * kD * 2 * 2 + kGroups * kTile * kKB * 2);
+          tma_load_3d(s.k[st], &map_k, &s.kv_full[st], 0, j * kKB, qrow);
+          tma_load_3d(s.vt[st], &map_vt, &s.kv_full[st], j * kKB, 0, qrow);
+          for (int g = 0; g < kGroups; ++g) {
+            const int q0 = (qp * 2 + g) * kTile;
+            if (p.starting)
+              tma_load_3d(s.bias[st][g], &map_bias, &s.kv_full[st], j * kKB, q0, b * kHeads + h);  // [q][k]
+            else
+              tma_load_3d(s.bias[st][g], &map_bias, &s.kv_full[st], q0, j * kKB, b * kHeads + h);  // [k][q]
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc_s = idesc_bf16_f32(128, kKB);
+      const uint32_t idesc_o = idesc_bf16_f32(128, kD);
+      int kv_it = 0, u_it = 0;
+      bool ok = true;
+      auto issue_qk = [&](int it) -> bool {
+        const int st = it % kKVStages;
+        if (!mbar_wait(&s.kv_full[st], (it / kKVStages) & 1, p.err, kErrTimeoutLoad)) return false;
+        const int buf = it & 1;
+        for (int g = 0; g < kGroups; ++g) {
+          if (!mbar_wait(&s.s_free[g][buf], ((it >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty)) return false;
+          tc_fence_after();
+          const uint32_t d = tmem0 + g * 192 + buf * 64;
+          const uint64_t da = desc_kmajor_sw64(smem_u32(s.q[g]));
+          const uint64_t db = desc_kmajor_sw64(smem_u32(s.k[st]));
+          mma_bf16(d, da, db, idesc_s, 0);
+          mma_bf16(d, da + 2, db + 2, idesc_s, 1);
+          mma_commit(&s.s_full[g][buf]);
+        }
+        return true;
+      };
+      for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x, ++u_it) {
+        if (!mbar_wait(&s.q_full, u_it & 1, p.err, kErrTimeoutLoad)) break;
+        tc_fence_after();
+        const int first = kv_it;
+        if (!issue_qk(first)) break;
+        for (int j = 0; j < nkb && ok; ++j) {
+          const int it = first + j;
+          if (j + 1 < nkb) {
+            if (!issue_qk(it + 1)) { ok = false; break; }
+          } else {
+            mma_commit(&s.q_empty);  // every Q K^T of this unit issued: Q may be refilled once they finish
+          }
+          const int st = it % kKVStages;
+          const int buf = it & 1;
+          const uint32_t ph = (it >> 1) & 1;
+          for (int g = 0; g < kGroups; ++g) {
+            if (!mbar_wait(&s.p_full[g][buf], ph, p.err, kErrTimeoutMma) ||
+                !mbar_wait(&s.o_free[g][buf], ph ^ 1, p.err, kErrTimeoutEmpty)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t d = tmem0 + g * 192 + 128 + buf * 32;
+            const uint64_t da = desc_kmajor_sw128(smem_u32(s.p[g][buf]));
+            const uint64_t db = desc_kmajor_sw128(smem_u32(s.vt[st]));
+#pragma unroll
+            for (int kk = 0; kk < kKB / 16; ++kk) mma_bf16(d, da + 2 * kk, db + 2 * kk, idesc_o, kk != 0);
+            mma_commit(&s.o_full[g][buf]);
+          }
+          if (!ok) break;
+          mma_commit(&s.kv_empty[st]);
+        }
+        kv_it = first + nkb;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax warpgroups
+    const int g = (warp - 2) / 4;
+    const int t = (warp & 3) * 32 + lane;  // TMEM lane == query row in the group's tile
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const float kMasked = -1.0e9f * kLog2e;
+    const float kNegInf = -__int_as_float(0x7f800000);
+    int kv_it = 0;
+    bool ok = true;
+    for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x) {
+      int b, r, h, qp;
+      unit_coords(unit, p, b, r, h, qp);
+      const int q = (qp * 2 + g) * kTile + t;
+      const bool row_on = p.mask[b * p.N + r] != 0;
+      const uint32_t* mw = s.mask_words + b * p.words_per_batch;
+      float m = kNegInf, l = 0.f, alpha_pending = 0.f;
+      float o[kD];
+#pragma unroll
+      for (int d = 0; d < kD; ++d) o[d] = 0.f;
+      for (int j = 0; j <= nkb && ok; ++j) {
+        const int it = kv_it + j;
+        if (j < nkb) {
+          const int st = it % kKVStages;
+          const int buf = it & 1;
+          const uint32_t ph = (it >> 1) & 1;
+          bool w1 = mbar_wait(&s.s_full[g][buf], ph, p.err, kErrTimeoutMma);
+          bool w2 = mbar_wait(&s.kv_full[st], (it / kKVStages) & 1, p.err, kErrTimeoutLoad);
+          if (!__all_sync(0xFFFFFFFFu, w1 && w2)) { ok = false; break; }
+          tc_fence_after();
+          uint32_t sv[64];
+          {
+            uint32_t a[32], c[32];
+            tmem_ld32(tmem0 + lane_off + g * 192 + buf * 64, a);
+            tmem_ld32(tmem0 + lane_off + g * 192 + buf * 64 + 32, c);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              sv[i] = a[i];
+              sv[32 + i] = c[i];
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s.s_free[g][buf]);
+          // logits (base 2): s + bias, then the mask
+          float x[64];
+          const uint8_t* bt = s.bias[st][g];
+          if (p.starting) {
+#pragma unroll
+            for (int c8 = 0; c8 < 8; ++c8) {
+              const uint4 bv = *reinterpret_cast<const uint4*>(bt + sw128_offset(t, c8 * 8));
+              const uint32_t w[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                x[c8 * 8 + 2 * e] = __uint_as_float(sv[c8 * 8 + 2 * e]) + bf16_lo(w[e]);
+                x[c8 * 8 + 2 * e + 1] = __uint_as_float(sv[c8 * 8 + 2 * e + 1]) + bf16_hi(w[e]);
+              }
+            }
+          } else {
+            const __nv_bfloat16* col = reinterpret_cast<const __nv_bfloat16*>(bt) + t;
+#pragma unroll
+            for (int c = 0; c < kKB; ++c) x[c] = __uint_as_float(sv[c]) + __bfloat162float(col[c * kTile]);
+          }
+          const int k0 = j * kKB;
+          const uint64_t keep = row_on ? ((static_cast<uint64_t>(mw[2 * j + 1]) << 32) | mw[2 * j]) : 0ull;
+          const int nvalid = p.N - k0 < kKB ? p.N - k0 : kKB;
+          if (keep != ~0ull) {
+#pragma unroll
+            for (int c = 0; c < kKB; ++c) {
+              if (!((keep >> c) & 1ull)) x[c] = c < nvalid ? kMasked : kNegInf;
+            }
+          }
+          float bm = x[0];
+#pragma unroll
+          for (int c = 1; c < kKB; ++c) bm = fmaxf(bm, x[c]);
+          const float m_new = fmaxf(m, bm);
+          const float alpha = ex2(m - m_new);
+          float sum = 0.f;
+          uint32_t pw[32];
+#pragma unroll
+          for (int c = 0; c < kKB; c += 2) {
+            const float e0 = ex2(x[c] - m_new);
+            const float e1 = ex2(x[c + 1] - m_new);
+            sum += e0 + e1;
+            pw[c / 2] = pack_bf16(e0, e1);
+          }
+          l = l * alpha + sum;
+          m = m_new;
+          uint8_t* pt = s.p[g][buf];
+#pragma unroll
+          for (int c8 = 0; c8 < 8; ++c8)
+            *reinterpret_cast<uint4*>(pt + sw128_offset(t, c8 * 8)) =
+                make_uint4(pw[c8 * 4], pw[c8 * 4 + 1], pw[c8 * 4 + 2], pw[c8 * 4 + 3]);
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&s.p_full[g][buf]);
+            mbar_arrive(&s.kv_empty[st]);
+          }
+          if (j > 0) {
+            // fold in P V of the previous block
+            const int pit = it - 1;
+            const int pbuf = pit & 1;
+            bool w3 = mbar_wait(&s.o_full[g][pbuf], (pit >> 1) & 1, p.err, kErrTimeoutMma);
+            if (!__all_sync(0xFFFFFFFFu, w3)) { ok = false; break; }
+            tc_fence_after();
+            uint32_t ov[32];
+            tmem_ld32(tmem0 + lane_off + g * 192 + 128 + pbuf * 32, ov);
+            tmem_ld_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s.o_free[g][pbuf]);
+#pragma unroll
+            for (int d = 0; d < kD; ++d) o[d] = o[d] * alpha_pending + __uint_as_float(ov[d]);
+          }
+          alpha_pending = alpha;
+        } else {
+          // last block's P V, then normalise and store
+          const int pit = it - 1;
+          const int pbuf = pit & 1;
+          bool w3 = mbar_wait(&s.o_full[g][pbuf], (pit >> 1) & 1, p.err, kErrTimeoutMma);
+          if (!__all_sync(0xFFFFFFFFu, w3)) { ok = false; break; }
+          tc_fence_after();
+          uint32_t ov[32];
+          tmem_ld32(tmem0 + lane_off + g * 192 + 128 + pbuf * 32, ov);
+          tmem_ld_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s.o_free[g][pbuf]);
+          const float inv = 1.0f / l;
+#pragma unroll
+          for (int d = 0; d < kD; ++d) o[d] = (o[d] * alpha_pending + __uint_as_float(ov[d])) * inv;
+          if (q < p.N) {
+            // natural pair position: starting (i=r, j=q), ending (i=q, j=r)
+            const int64_t pi = p.starting ? r : q;
+            const int64_t pj = p.starting ? q : r;
+            uint4* dst = reinterpret_cast<uint4*>(p.o + (((static_cast<int64_t>(b) * p.N + pi) * p.N + pj) * kC + h * kD));
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              dst[i] = make_uint4(pack_bf16(o[8 * i], o[8 * i + 1]), pack_bf16(o[8 * i + 2], o[8 * i + 3]),
+                                  pack_bf16(o[8 * i + 4], o[8 * i + 5]), pack_bf16(o[8 * i + 6], o[8 * i + 7]));
+          }
+        }
+      }
+      kv_it += nkb;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem0, 512);
+  }
+}
+
+// ====================================================================== 3. output
+struct OutSmem {
+  alignas(1024) uint8_t wg[kGateBytes];
+  alignas(1024) uint8_t wo[kOutBytes];
+  alignas(1024) uint8_t z[kGroups][kTile * kC * 2];
+  alignas(1024) uint8_t o[kGroups][kTile * kC * 2];
+  float wsum_gate[128];
+  float bias_gate[128];
+  uint64_t wbar;
+  uint64_t full[kGroups];
+  uint64_t mma[kGroups];
+  uint32_t tmem_base;
+};
+
+struct OutParams {
+  const uint8_t* packed;
+  const uint8_t* mask;
+  int B, N;
+  int masked_zero;
+  int* err;
+};
+
+__global__ void __launch_bounds__(256, 1)
+    triattn_out_kernel(const __grid_constant__ CUtensorMap map_z, const __grid_constant__ CUtensorMap map_o,
+                       const __grid_constant__ CUtensorMap map_out, OutParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  OutSmem& s = *reinterpret_cast<OutSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int g = threadIdx.x / 128;
+  const int gt = threadIdx.x % 128;
+  const int warp = threadIdx.x / 32;
+  const int tiles_per_row = (p.N + kTile - 1) / kTile;
+  const int total = p.B * p.N * tiles_per_row;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&s.wbar, 1);
+    for (int i = 0; i < kGroups; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.mma[i], 1);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&s.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x == 0) {
+    tma_prefetch_map(&map_z);
+    tma_prefetch_map(&map_o);
+    tma_prefetch_map(&map_out);
+    mbar_arrive_expect_tx(&s.wbar, kGateBytes + kOutBytes);
+    bulk_load(s.wg, p.packed + kProjBytes, kGateBytes, &s.wbar);
+    bulk_load(s.wo, p.packed + kProjBytes + kGateBytes, kOutBytes, &s.wbar);
+  }
+  {
+    const float* v = reinterpret_cast<const float*>(p.packed + kProjBytes + kGateBytes + kOutBytes) + 2 * kProjRows;
+    for (int i = threadIdx.x; i < 128; i += 256) {
+      s.wsum_gate[i] = v[i];
+      s.bias_gate[i] = v[128 + i];
+    }
+  }
+  __syncthreads();
+  bool ok = mbar_wait(&s.wbar, 0, p.err, kErrTimeoutLoad);
+  const uint32_t tmem = s.tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16) + g * 256;
+  const uint32_t tmem_mma = s.tmem_base + g * 256;
+  const uint32_t idesc = idesc_bf16_f32(128, 128);
+  uint8_t* zt = s.z[g];
+  uint8_t* ot = s.o[g];
+  int it = 0;
+  bool load_pending = false;
+  for (int tile = blockIdx.x * kGroups + g; tile < total; tile += gridDim.x * kGroups, ++it) {
+    const int c0 = (tile % tiles_per_row) * kTile;
+    const int rr = tile / tiles_per_row;
+    const int b = rr / p.N;
+    const int r = rr - b * p.N;
+    if (gt == 0 && ok) {
+      tma_store_wait_read0();
+      mbar_arrive_expect_tx(&s.full[g], 2 * kTile * kC * 2);
+      for (int kb = 0; kb < 2; ++kb) {
+        tma_load_3d(zt + kb * 16384, &map_z, &s.full[g], kb * 64, c0, rr);
+        tma_load_3d(ot + kb * 16384, &map_o, &s.full[g], kb * 64, c0, rr);
+      }
+      load_pending = true;
+    }
+    ok = ok && mbar_wait(&s.full[g], it & 1, p.err, kErrTimeoutLoad);
+    if (gt == 0 && ok) load_pending = false;
+    float mean = 0.f, rstd = 0.f;
+    if (ok) tile_stats(zt, gt, mean, rstd);
+    // phase 1: gate = W_g' z
+    if (gt == 0 && ok) {
+      tc_fence_after();
+      const uint32_t za = smem_u32(zt), wg = smem_u32(s.wg);
+#pragma unroll
+      for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_bf16(tmem_mma, desc_kmajor_sw128(za + kb * 16384) + 2 * kk, desc_kmajor_sw128(wg + kb * 16384) + 2 * kk,
+                   idesc, (kb | kk) != 0);
+      mma_commit(&s.mma[g]);
+    }
+    bool got = ok && mbar_wait(&s.mma[g], 0, p.err, kErrTimeoutMma);
+    got = __all_sync(0xFFFFFFFFu, got);
+    tc_fence_after();
+    if (got) {
+      // gated o, in place, as the K-major operand of phase 2
+#pragma unroll 1
+      for (int cc = 0; cc < kC; cc += 32) {
+        uint32_t vg[32];
+        tmem_ld32(tmem + cc, vg);
+        tmem_ld_wait();
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          const int ch = cc + q8 * 8;
+          uint8_t* addr = ot + (ch / 64) * 16384 + sw128_offset(gt, ch % 64);
+          const uint4 ov = *reinterpret_cast<const uint4*>(addr);
+          const uint32_t w[4] = {ov.x, ov.y, ov.z, ov.w};
+          uint32_t out[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int i = q8 * 8 + 2 * e;
+            const float g0 = rstd * (__uint_as_float(vg[i]) - mean * s.wsum_gate[cc + i]) + s.bias_gate[cc + i];
+            const float g1 =
+                rstd * (__uint_as_float(vg[i + 1]) - mean * s.wsum_gate[cc + i + 1]) + s.bias_gate[cc + i + 1];
+            out[e] = pack_bf16(bf16_lo(w[e]) * sigmoidf_(g0), bf16_hi(w[e]) * sigmoidf_(g1));
+          }
+          *reinterpret_cast<uint4*>(addr) = make_uint4(out[0], out[1], out[2], out[3]);
+        }
+      }
+    }
+    tc_fence_before();
+    fence_async_smem();
+    named_barrier(1 + g, 128);
+    // phase 2: delta = W_o (gated o)
+    if (gt == 0 && got) {
+      tc_fence_after();
+      const uint32_t oa = smem_u32(ot), wo = smem_u32(s.wo);
+#pragma unroll
+      for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_bf16(tmem_mma + 128, desc_kmajor_sw128(oa + kb * 16384) + 2 * kk,
+                   desc_kmajor_sw128(wo + kb * 16384) + 2 * kk, idesc, (kb | kk) != 0);
+      mma_commit(&s.mma[g]);
+    }
+    bool got2 = got && mbar_wait(&s.mma[g], 1, p.err, kErrTimeoutMma);
+    got2 = __all_sync(0xFFFFFFFFu, got2);
+    tc_fence_after();
+    if (got2) {
+      const int j = c0 + gt;
+      const bool keep = !p.masked_zero || (j < p.N && p.mask[b * p.N + r] && p.mask[b * p.N + j]);
+#pragma unroll 1
+      for (int cc = 0; cc < kC; cc += 32) {
+        uint32_t vo[32];
+        tmem_ld32(tmem + 128 + cc, vo);
+        tmem_ld_wait();
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          const int ch = cc + q8 * 8;
+          uint8_t* addr = zt + (ch / 64) * 16384 + sw128_offset(gt, ch % 64);
+          const uint4 zv = *reinterpret_cast<const uint4*>(addr);
+          const uint32_t w[4] = {zv.x, zv.y, zv.z, zv.w};
+          uint32_t out[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int i = q8 * 8 + 2 * e;
+            const float d0 = keep ? __uint_as_float(vo[i]) : 0.f;
+            const float d1 = keep ? __uint_as_float(vo[i + 1]) : 0.f;
+            out[e] = pack_bf16(bf16_lo(w[e]) + d0, bf16_hi(w[e]) + d1);
+          }
+          *reinterpret_cast<uint4*>(addr) = make_uint4(out[0], out[1], out[2], out[3]);
+        }
+      }
+    }
+    tc_fence_before();
+    fence_async_smem();
+    ok = !named_barrier_or(1 + g, 128, !ok || !got || !got2);
+    if (gt == 0 && ok) {
+      tma_store_3d(&map_out, zt, 0, c0, rr);
+      tma_store_3d(&map_out, zt + 16384, 64, c0, rr);
+      tma_store_commit();
+    }
+    if (!ok) break;
+  }
+  if (gt == 0) {
+    tma_store_wait_all0();
+    if (load_pending) mbar_wait(&s.full[g], it & 1, p.err, kErrTimeoutLoad);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(s.tmem_base, 512);
+  }
+}
+
+struct Workspace {
+  __nv_bfloat16 *q, *k, *vt, *bias, *o;
+};
+
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+Workspace carve(void* ws, int B, int N) {
+  const size_t np = (static_cast<size_t>(N) + 7) / 8 * 8;
+  uint8_t* p = static_cast<uint8_t*>(ws);
+  Workspace w;
+  const size_t qk = align256(static_cast<size_t>(B) * N * kHeads * N * kD * 2);
+  const size_t vt = align256(static_cast<size_t>(B) * N * kHeads * kD * np * 2);
+  const size_t bias = align256(static_cast<size_t>(B) * kHeads * N * np * 2);
+  w.q = reinterpret_cast<__nv_bfloat16*>(p);
+  w.k = reinterpret_cast<__nv_bfloat16*>(p + qk);
+  w.vt = reinterpret_cast<__nv_bfloat16*>(p + 2 * qk);
+  w.bias = reinterpret_cast<__nv_bfloat16*>(p + 2 * qk + vt);
+  w.o = reinterpret_cast<__nv_bfloat16*>(p + 2 * qk + vt + bias);
+  return w;
+}
+
+}  // namespace
+
+size_t triattn_packed_bytes() { return kPackedBytes; }
+
+size_t triattn_workspace_bytes(int B, int N) {
+  const size_t np = (static_cast<size_t>(N) + 7) / 8 * 8;
+  const size_t qk = align256(static_cast<size_t>(B) * N * kHeads * N * kD * 2);
+  const size_t vt = align256(static_cast<size_t>(B) * N * kHeads * kD * np * 2);
+  const size_t bias = align256(static_cast<size_t>(B) * kHeads * N * np * 2);
+  const size_t o = align256(static_cast<size_t>(B) * N * N * kC * 2);
+  return 2 * qk + vt + bias + o;
+}
+
+int triattn_prepare(const TriAttnWeights& w, void* packed, cudaStream_t stream) {
+  uint8_t* img = static_cast<uint8_t*>(packed);
+  float* vec = reinterpret_cast<float*>(img + kProjBytes + kGateBytes + kOutBytes);
+  int rc = static_cast<int>(cudaMemsetAsync(packed, 0, kPackedBytes, stream));
+  const float qscale = kLog2e / sqrtf(static_cast<float>(kD));
+  if (rc == 0)
+    rc = launch_pack_weight(w.to_query, 128, kC, w.ln_w, w.ln_b, img, 0, kProjRows, vec, vec + kProjRows, stream,
+                            qscale);
+  if (rc == 0)
+    rc = launch_pack_weight(w.to_key, 128, kC, w.ln_w, w.ln_b, img, 128, kProjRows, vec, vec + kProjRows, stream);
+  if (rc == 0)
+    rc = launch_pack_weight(w.to_value, 128, kC, w.ln_w, w.ln_b, img, 256, kProjRows, vec, vec + kProjRows, stream);
+  if (rc == 0)
+    rc = launch_pack_weight(w.to_bias, kHeads, kC, w.ln_w, w.ln_b, img, 384, kProjRows, vec, vec + kProjRows, stream,
+                            kLog2e);
+  if (rc == 0)
+    rc = launch_pack_weight(w.to_gate, 128, kC, w.ln_w, w.ln_b, img + kProjBytes, 0, 128, vec + 2 * kProjRows,
+                            vec + 2 * kProjRows + 128, stream);
+  if (rc == 0)
+    rc = launch_pack_weight(w.to_out, 128, kC, nullptr, nullptr, img + kProjBytes + kGateBytes, 0, 128, nullptr,
+                            nullptr, stream);
+  return rc;
+}
+
+int triattn_forward(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace, int B, int N,
+                    int starting, int masked_zero, const DeviceInfo& info, cudaStream_t stream) {
+  const int np = (N + 7) / 8 * 8;
+  Workspace ws = carve(workspace, B, N);
+  int st;
+  const uint64_t zdims[3] = {kC, static_cast<uint64_t>(N), static_cast<uint64_t>(B) * N};
+  const uint64_t zstrides[2] = {kC * 2, static_cast<uint64_t>(N) * kC * 2};
+  // 1. projection
+  {
+    CUtensorMap map_z;
+    const uint32_t box_row[3] = {64, kTile, 1};
+    const uint32_t box_col[3] = {64, 1, kTile};
+    st = make_map(&map_z, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, z, zdims, zstrides, starting ? box_row : box_col,
+                  CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    ProjParams pp{static_cast<const uint8_t*>(packed), ws.q, ws.k, ws.vt, ws.bias, B, N, np, starting, info.err};
+    const int tiles = B * N * ((N + kTile - 1) / kTile);
+    const int groups = (tiles + kGroups - 1) / kGroups;
+    const int grid = groups < info.num_sms ? groups : info.num_sms;
+    const size_t smem = sizeof(ProjSmem) + 1024;
+    cudaFuncSetAttribute(triattn_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    triattn_proj_kernel<<<grid, 256, smem, stream>>>(map_z, pp);
+    st = cuda_status(static_cast<int>(cudaGetLastError()), "triattn_proj launch");
+    if (st) return st;
+  }
+  // 2. attention
+  {
+    CUtensorMap map_q, map_k, map_vt, map_bias;
+    const uint64_t qdims[3] = {kD, static_cast<uint64_t>(N), static_cast<uint64_t>(B) * N * kHeads};
+    const uint64_t qstrides[2] = {kD * 2, static_cast<uint64_t>(N) * kD * 2};
+    const uint32_t qbox[3] = {kD, kTile, 1};
+    const uint32_t kbox[3] = {kD, kKB, 1};
+    st = make_map(&map_q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ws.q, qdims, qstrides, qbox, CU_TENSOR_MAP_SWIZZLE_64B);
+    if (st) return st;
+    st = make_map(&map_k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ws.k, qdims, qstrides, kbox, CU_TENSOR_MAP_SWIZZLE_64B);
+    if (st) return st;
+    const uint64_t vdims[3] = {static_cast<uint64_t>(N), kD, static_cast<uint64_t>(B) * N * kHeads};
+    const uint64_t vstrides[2] = {static_cast<uint64_t>(np) * 2, static_cast<uint64_t>(kD) * np * 2};
+    const uint32_t vbox[3] = {kKB, kD, 1};
+    st = make_map(&map_vt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ws.vt, vdims, vstrides, vbox,
+                  CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    const uint64_t bdims[3] = {static_cast<uint64_t>(N), static_cast<uint64_t>(N), static_cast<uint64_t>(B) * kHeads};
+    const uint64_t bstrides[2] = {static_cast<uint64_t>(np) * 2, static_cast<uint64_t>(N) * np * 2};
+    if (starting) {
+      const uint32_t bbox[3] = {kKB, kTile, 1};  // [q rows][64 keys], 128-byte rows
+      st = make_map(&map_bias, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ws.bias, bdims, bstrides, bbox,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+    } else {
+      const uint32_t bbox[3] = {kTile, kKB, 1};  // [64 key rows][128 q]
+      st = make_map(&map_bias, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ws.bias, bdims, bstrides, bbox,
+                    CU_TENSOR_MAP_SWIZZLE_NONE);
+    }
+    if (st) return st;
+    AttnParams ap;
+    ap.mask = mask;
+    ap.o = ws.o;
+    ap.B = B;
+    ap.N = N;
+    ap.starting = starting;
+    ap.qpairs = ((N + kTile - 1) / kTile + 1) / 2;
+    ap.words_per_batch = 2 * ((N + kKB - 1) / kKB);
+    ap.err = info.err;
+    if (B * ap.words_per_batch > kMaxMaskWords) return fail(2, "triattn: B * N too large for the key-mask cache");
+    const int units = B * N * kHeads * ap.qpairs;
+    const int grid = units < info.num_sms ? units : info.num_sms;
+    const size_t smem = sizeof(AttnSmem) + 1024;
+    cudaFuncSetAttribute(triattn_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    triattn_attn_kernel<<<grid, kAttnThreads, smem, stream>>>(map_q, map_k, map_vt, map_bias, ap);
+    st = cuda_status(static_cast<int>(cudaGetLastError()), "triattn_attn launch");
+    if (st) return st;
+  }
+  // 3. output
+  {
+    CUtensorMap map_z, map_o, map_out;
+    const uint32_t box[3] = {64, kTile, 1};
+    st = make_map(&map_z, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, z, zdims, zstrides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = make_map(&map_o, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ws.o, zdims, zstrides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = make_map(&map_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out, zdims, zstrides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    OutParams op{static_cast<const uint8_t*>(packed), mask, B, N, masked_zero, info.err};
+    const int tiles = B * N * ((N + kTile - 1) / kTile);
+    const int groups = (tiles + kGroups - 1) / kGroups;
+    const int grid = groups < info.num_sms ? groups : info.num_sms;
+    const size_t smem = sizeof(OutSmem) + 1024;
+    cudaFuncSetAttribute(triattn_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    triattn_out_kernel<<<grid, 256, smem, stream>>>(map_z, map_o, map_out, op);
+    return cuda_status(static_cast<int>(cudaGetLastError()), "triattn_out launch");
+  }
+}
+
+}  // namespace ffb

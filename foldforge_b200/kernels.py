@@ -125,3 +125,33 @@ def trimul(z: Tensor, mask: Tensor, packed: Tensor, *, outgoing: bool, masked_ze
     _lib.call("ffb_trimul_fwd", _ptr(z), _ptr(m), _ptr(packed), _ptr(out), _ptr(ws), ctypes.c_size_t(ws_bytes), b, n,
               int(outgoing), int(masked_zero), _stream())
     return out
+
+
+def triattn_prepare(weights: dict[str, Tensor], device: torch.device) -> Tensor:
+    """Pack a ``TriangleAttention`` (AF3)'s fp32 weights (engine keys) for the kernels."""
+    lib = _lib.load()
+    packed = torch.empty(int(lib.ffb_triattn_packed_bytes()), dtype=torch.uint8, device=device)
+    keys = ("ln_pair.weight", "ln_pair.bias", "to_bias.weight", "to_query.weight", "to_key.weight",
+            "to_value.weight", "to_gate.weight", "to_out.weight")
+    ts = [_f32(weights[k]).to(device) for k in keys]
+    _need_cuda(*ts)
+    _lib.call("ffb_triattn_prepare", *[_ptr(t) for t in ts], _ptr(packed), _stream())
+    packed._keepalive = ts
+    return packed
+
+
+def triattn(z: Tensor, mask: Tensor, packed: Tensor, *, starting: bool, masked_zero: bool = True) -> Tensor:
+    """Triangle attention with residual: ``z [B, N, N, 128]`` bf16, ``mask [B, N]``."""
+    _need_cuda(z, mask, packed)
+    if z.dtype != torch.bfloat16 or z.dim() != 4 or z.shape[-1] != 128:
+        raise _lib.UnsupportedCall("triattn", 2, f"needs bf16 [B, N, N, 128], got {z.dtype} {tuple(z.shape)}")
+    z = z.contiguous()
+    b, n = z.shape[0], z.shape[1]
+    lib = _lib.load()
+    ws_bytes = int(lib.ffb_triattn_workspace_bytes(b, n))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=z.device)
+    out = torch.empty_like(z)
+    m = _mask_u8(mask)
+    _lib.call("ffb_triattn_fwd", _ptr(z), _ptr(m), _ptr(packed), _ptr(out), _ptr(ws), ctypes.c_size_t(ws_bytes), b, n,
+              int(starting), int(masked_zero), _stream())
+    return out

@@ -94,6 +94,21 @@ int ffb_trimul_prepare(const float* ln_w, const float* ln_b, const float* ln_out
 int ffb_trimul_fwd(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace,
                    size_t workspace_bytes, int B, int N, int outgoing, int masked, void* stream);
 
+/* ---- Triangle attention, starting / ending node (c_z = 128, 4 heads x 32, AF3: no
+ * projection biases, untransposed pair bias). Replaces the engine `TriangleAttention`
+ * (model "af3") as FoldForge calls it (src/foldforge/modules/engine/modules.py:166-181);
+ * equations of legacy/attention.py:108-171 and legacy/reference/attention.py:14-100.
+ * ffb_triattn_prepare: fp32 master weights (ln_w, ln_b [128]; to_bias [4, 128]; to_query,
+ * to_key, to_value, to_gate, to_out [128, 128]) -> `packed` (ffb_triattn_packed_bytes()).
+ * ffb_triattn_fwd: as ffb_trimul_fwd, with workspace ffb_triattn_workspace_bytes(B, N). */
+size_t ffb_triattn_packed_bytes(void);
+size_t ffb_triattn_workspace_bytes(int B, int N);
+int ffb_triattn_prepare(const float* ln_w, const float* ln_b, const float* to_bias, const float* to_query,
+                        const float* to_key, const float* to_value, const float* to_gate, const float* to_out,
+                        void* packed, void* stream);
+int ffb_triattn_fwd(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace,
+                    size_t workspace_bytes, int B, int N, int starting, int masked, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

