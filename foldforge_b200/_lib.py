@@ -38,10 +38,24 @@ SIGNATURES: dict[str, list] = {
     "ffb_triattn_prepare": [c_void_p] * 10,
     "ffb_triattn_fwd": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_size_t, c_int, c_int, c_int,
                         c_int, c_void_p],
+    "ffb_transition_packed_bytes": [],
+    "ffb_transition_prepare": [c_void_p] * 7,
+    "ffb_transition_fwd": [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p],
+    "ffb_apb_packed_bytes": [],
+    "ffb_apb_workspace_bytes": [c_int, c_int],
+    "ffb_apb_prepare": [c_void_p] * 12,
+    "ffb_apb_fwd": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_float, c_void_p, c_void_p,
+                    ctypes.c_size_t, c_int, c_int, c_int, c_void_p],
+    "ffb_single_transition_packed_bytes": [],
+    "ffb_single_transition_workspace_bytes": [c_int, c_int],
+    "ffb_single_transition_prepare": [c_void_p] * 7,
+    "ffb_single_transition_fwd": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_size_t, c_int, c_int,
+                                  c_int, c_void_p],
 }
 
 #: entry points that return a size_t instead of a status
-SIZE_RESULT = {"ffb_trimul_packed_bytes", "ffb_trimul_workspace_bytes", "ffb_triattn_packed_bytes",
+SIZE_RESULT = {"ffb_apb_packed_bytes", "ffb_apb_workspace_bytes", "ffb_single_transition_packed_bytes",
+               "ffb_single_transition_workspace_bytes", "ffb_transition_packed_bytes", "ffb_trimul_packed_bytes", "ffb_trimul_workspace_bytes", "ffb_triattn_packed_bytes",
                "ffb_triattn_workspace_bytes"}
 
 STATUS = {0: "FFB_OK", 1: "FFB_ERR_ARG", 2: "FFB_ERR_UNSUPPORTED", 3: "FFB_ERR_CUDA", 4: "FFB_ERR_DEVICE"}

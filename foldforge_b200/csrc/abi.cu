@@ -259,4 +259,114 @@ int ffb_triattn_fwd(const void* z, const uint8_t* mask, const void* packed, void
                          static_cast<cudaStream_t>(stream));
 }
 
+size_t ffb_transition_packed_bytes(void) { return transition_packed_bytes(); }
+
+int ffb_transition_prepare(const float* ln_w, const float* ln_b, const float* expand_a, const float* expand_b,
+                           const float* squeeze, void* packed, void* stream) {
+  if (!ln_w || !ln_b || !expand_a || !expand_b || !squeeze || !packed)
+    return fail(FFB_ERR_ARG, "transition_prepare: null pointer");
+  if ((reinterpret_cast<uintptr_t>(packed) & 15u) != 0) return fail(FFB_ERR_ARG, "transition_prepare: packed not 16-byte aligned");
+  DeviceInfo info;
+  int st = device_info(&info);
+  if (st != FFB_OK) return st;
+  TransitionWeights w{ln_w, ln_b, expand_a, expand_b, squeeze};
+  return cuda_status(transition_prepare(w, packed, static_cast<cudaStream_t>(stream)), "transition_prepare");
+}
+
+int ffb_transition_fwd(const void* z, const uint8_t* mask, const void* packed, void* out, int B, int N, int masked,
+                       void* stream) {
+  if (B <= 0 || N <= 0) return fail(FFB_ERR_ARG, "transition_fwd: empty problem B=%d N=%d", B, N);
+  if (!z || !packed || !out) return fail(FFB_ERR_ARG, "transition_fwd: null pointer");
+  if (masked == FFB_MASKED_ZERO && !mask) return fail(FFB_ERR_ARG, "transition_fwd: masked zero needs the mask");
+  if (masked != FFB_MASKED_COMPUTE && masked != FFB_MASKED_ZERO) return fail(FFB_ERR_ARG, "transition_fwd: masked=%d", masked);
+  if (z == out) return fail(FFB_ERR_ARG, "transition_fwd: out must not alias z");
+  if ((reinterpret_cast<uintptr_t>(z) | reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(packed)) & 15u)
+    return fail(FFB_ERR_ARG, "transition_fwd: misaligned pointer");
+  if (static_cast<int64_t>(B) * N * N >= (int64_t(1) << 31) - 256) return fail(FFB_ERR_UNSUPPORTED, "transition_fwd: too many rows");
+  DeviceInfo info;
+  int st = device_info(&info);
+  if (st != FFB_OK) return st;
+  return transition_forward(z, mask, packed, out, B, N, masked == FFB_MASKED_ZERO, info,
+                            static_cast<cudaStream_t>(stream));
+}
+
+size_t ffb_apb_packed_bytes(void) { return apb_packed_bytes(); }
+
+size_t ffb_apb_workspace_bytes(int B, int N) { return (B <= 0 || N <= 0) ? 0 : apb_workspace_bytes(B, N); }
+
+int ffb_apb_prepare(const float* ln_single_w, const float* ln_single_b, const float* to_query,
+                    const float* query_bias, const float* to_key, const float* to_value, const float* to_gate,
+                    const float* to_out, const float* ln_pair_w, const float* to_bias, void* packed, void* stream) {
+  if (!ln_single_w || !ln_single_b || !to_query || !query_bias || !to_key || !to_value || !to_gate || !to_out ||
+      !ln_pair_w || !to_bias || !packed)
+    return fail(FFB_ERR_ARG, "apb_prepare: null pointer");
+  if ((reinterpret_cast<uintptr_t>(packed) & 255u) != 0) return fail(FFB_ERR_ARG, "apb_prepare: packed not 256-byte aligned");
+  DeviceInfo info;
+  int st = device_info(&info);
+  if (st != FFB_OK) return st;
+  ApbWeights w{ln_single_w, ln_single_b, to_query, query_bias, to_key, to_value, to_gate, to_out, ln_pair_w, to_bias};
+  return cuda_status(apb_prepare(w, packed, static_cast<cudaStream_t>(stream)), "apb_prepare");
+}
+
+int ffb_apb_fwd(const void* s, const void* z, const uint8_t* mask, const void* packed, const void* extra_pair_bias,
+                int extra_dtype, float gate_bias, void* out, void* workspace, size_t workspace_bytes, int B, int N,
+                int masked, void* stream) {
+  if (B <= 0 || N <= 0) return fail(FFB_ERR_ARG, "apb_fwd: empty problem B=%d N=%d", B, N);
+  if (!s || !z || !mask || !packed || !out || !workspace) return fail(FFB_ERR_ARG, "apb_fwd: null pointer");
+  if (s == out) return fail(FFB_ERR_ARG, "apb_fwd: out must not alias s");
+  if (masked != FFB_MASKED_COMPUTE && masked != FFB_MASKED_ZERO) return fail(FFB_ERR_ARG, "apb_fwd: masked=%d", masked);
+  if (extra_pair_bias && extra_dtype != FFB_BF16 && extra_dtype != FFB_F32) return fail(FFB_ERR_ARG, "apb_fwd: extra dtype");
+  if (workspace_bytes < apb_workspace_bytes(B, N))
+    return fail(FFB_ERR_ARG, "apb_fwd: workspace %zu < %zu bytes", workspace_bytes, apb_workspace_bytes(B, N));
+  if (((reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(z) | reinterpret_cast<uintptr_t>(out)) & 15u) ||
+      ((reinterpret_cast<uintptr_t>(packed) | reinterpret_cast<uintptr_t>(workspace)) & 255u))
+    return fail(FFB_ERR_ARG, "apb_fwd: misaligned pointer");
+  if (static_cast<int64_t>(B) * N * N >= (int64_t(1) << 31) - 256) return fail(FFB_ERR_UNSUPPORTED, "apb_fwd: too many pairs");
+  DeviceInfo info;
+  int st = device_info(&info);
+  if (st != FFB_OK) return st;
+  return apb_forward(s, z, mask, packed, extra_pair_bias, extra_dtype == FFB_F32, gate_bias, out, workspace, B, N,
+                     masked == FFB_MASKED_ZERO, info, static_cast<cudaStream_t>(stream));
+}
+
+size_t ffb_single_transition_packed_bytes(void) { return single_transition_packed_bytes(); }
+
+size_t ffb_single_transition_workspace_bytes(int B, int N) {
+  return (B <= 0 || N <= 0) ? 0 : single_transition_workspace_bytes(B, N);
+}
+
+int ffb_single_transition_prepare(const float* ln_w, const float* ln_b, const float* expand_a,
+                                  const float* expand_b, const float* squeeze, void* packed, void* stream) {
+  if (!ln_w || !ln_b || !expand_a || !expand_b || !squeeze || !packed)
+    return fail(FFB_ERR_ARG, "single_transition_prepare: null pointer");
+  if ((reinterpret_cast<uintptr_t>(packed) & 255u) != 0)
+    return fail(FFB_ERR_ARG, "single_transition_prepare: packed not 256-byte aligned");
+  DeviceInfo info;
+  int st = device_info(&info);
+  if (st != FFB_OK) return st;
+  TransitionWeights w{ln_w, ln_b, expand_a, expand_b, squeeze};
+  return cuda_status(single_transition_prepare(w, packed, static_cast<cudaStream_t>(stream)),
+                     "single_transition_prepare");
+}
+
+int ffb_single_transition_fwd(const void* s, const uint8_t* mask, const void* packed, void* out, void* workspace,
+                              size_t workspace_bytes, int B, int N, int masked, void* stream) {
+  if (B <= 0 || N <= 0) return fail(FFB_ERR_ARG, "single_transition_fwd: empty problem B=%d N=%d", B, N);
+  if (!s || !packed || !out || !workspace) return fail(FFB_ERR_ARG, "single_transition_fwd: null pointer");
+  if (masked == FFB_MASKED_ZERO && !mask) return fail(FFB_ERR_ARG, "single_transition_fwd: masked zero needs the mask");
+  if (masked != FFB_MASKED_COMPUTE && masked != FFB_MASKED_ZERO)
+    return fail(FFB_ERR_ARG, "single_transition_fwd: masked=%d", masked);
+  if (s == out) return fail(FFB_ERR_ARG, "single_transition_fwd: out must not alias s");
+  if (workspace_bytes < single_transition_workspace_bytes(B, N))
+    return fail(FFB_ERR_ARG, "single_transition_fwd: workspace too small");
+  if (((reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(out)) & 15u) ||
+      ((reinterpret_cast<uintptr_t>(packed) | reinterpret_cast<uintptr_t>(workspace)) & 255u))
+    return fail(FFB_ERR_ARG, "single_transition_fwd: misaligned pointer");
+  DeviceInfo info;
+  int st = device_info(&info);
+  if (st != FFB_OK) return st;
+  return single_transition_forward(s, mask, packed, out, workspace, B, N, masked == FFB_MASKED_ZERO, info,
+                                   static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

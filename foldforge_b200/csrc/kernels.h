@@ -64,4 +64,30 @@ int triattn_prepare(const TriAttnWeights& w, void* packed, cudaStream_t stream);
 int triattn_forward(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace, int B, int N,
                     int starting, int masked_zero, const DeviceInfo& info, cudaStream_t stream);
 
+// ---- pair transition (c_z = 128, n = 4)
+struct TransitionWeights {
+  const float *ln_w, *ln_b, *expand_a, *expand_b, *squeeze;
+};
+size_t transition_packed_bytes();
+int transition_prepare(const TransitionWeights& w, void* packed, cudaStream_t stream);
+int transition_forward(const void* z, const uint8_t* mask, const void* packed, void* out, int B, int N,
+                       int masked_zero, const DeviceInfo& info, cudaStream_t stream);
+
+// ---- single track (c_s = 384, 16 heads x 24, c_z = 128)
+struct ApbWeights {
+  const float *ln_single_w, *ln_single_b, *to_query, *query_bias, *to_key, *to_value, *to_gate, *to_out;
+  const float *ln_pair_w, *to_bias;
+};
+size_t apb_packed_bytes();
+size_t apb_workspace_bytes(int B, int N);
+int apb_prepare(const ApbWeights& w, void* packed, cudaStream_t stream);
+int apb_forward(const void* s, const void* z, const uint8_t* mask, const void* packed, const void* extra,
+                int extra_f32, float gate_bias, void* out, void* workspace, int B, int N, int masked_zero,
+                const DeviceInfo& info, cudaStream_t stream);
+size_t single_transition_packed_bytes();
+size_t single_transition_workspace_bytes(int B, int N);
+int single_transition_prepare(const TransitionWeights& w, void* packed, cudaStream_t stream);
+int single_transition_forward(const void* s, const uint8_t* mask, const void* packed, void* out, void* workspace,
+                              int B, int N, int masked_zero, const DeviceInfo& info, cudaStream_t stream);
+
 }  // namespace ffb

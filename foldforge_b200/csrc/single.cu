@@ -1,0 +1,288 @@
+// Single track of the Pairformer block: attention with pair bias and the single
+// transition (c_s = 384, 16 heads x 24, factor 4). Both are small next to the pair ops
+// (about 1% of a block's flops at N = 512) and are composed from the library's tcgen05
+// GEMM and LayerNorm launchers plus one attention kernel:
+//
+// attention with pair bias (legacy/pairformer.py:204-226, legacy/transformer.py:88-133):
+//   pb[b, i, j, h] = W_pb (gamma_pair * LNhat(z[b, i, j]))     LayerNorm + GEMM (N = 16)
+//   y = LN(s);  [q | k | v | g] = y W^T + [b_q | 0 | 0 | 0]     GEMM (N = 1536)
+//   o = softmax_j(q_i . k_j / sqrt(24) + pb[i, j, h] (+ extra[h, i, j]), key mask) v_j
+//   s' = s + W_o (sigmoid(g + gate_bias) * o)                    GEMM with residual epilogue
+// single transition: s' = s + W_sq (silu(W_a LN(s)) * W_b LN(s))  (SwiGLU GEMM epilogue)
+#include "abi_util.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ffb {
+namespace {
+
+constexpr int kCs = 384;
+constexpr int kHs = 16;
+constexpr int kDs = 24;
+constexpr int kCz = 128;
+
+// ---------------------------------------------------------------- weight conversion
+// dst[r, :] = bf16(src[perm(r), :]); perm interleaves a / b halves in blocks of 16 rows
+// when `interleave` is set (the SwiGLU epilogue layout), identity otherwise.
+__global__ void to_bf16_rows_kernel(const float* __restrict__ a, const float* __restrict__ b, int rows_each, int cols,
+                                    int interleave, __nv_bfloat16* __restrict__ dst) {
+  const int64_t total = static_cast<int64_t>(interleave ? 2 * rows_each : rows_each) * cols;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i / cols);
+    const int c = static_cast<int>(i % cols);
+    float v;
+    if (interleave) {
+      const int blk = r / 32, within = r % 32;
+      const int src_row = blk * 16 + (within % 16);
+      v = (within < 16 ? a : b)[static_cast<int64_t>(src_row) * cols + c];
+    } else {
+      v = a[static_cast<int64_t>(r) * cols + c];
+    }
+    dst[i] = __float2bfloat16_rn(v);
+  }
+}
+
+int to_bf16(const float* a, const float* b, int rows_each, int cols, int interleave, void* dst, cudaStream_t st) {
+  to_bf16_rows_kernel<<<256, 256, 0, st>>>(a, b, rows_each, cols, interleave, static_cast<__nv_bfloat16*>(dst));
+  return static_cast<int>(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------- attention kernel
+// One warp per (batch, head, query). Lanes stride over the keys keeping a private online
+// softmax (max, sum, 24 partial outputs), merged across the warp at the end. Masked keys
+// get the reference's REPLACED logit -1e9 (so a row with every key masked averages
+// uniformly); keys past N do not exist.
+__global__ void __launch_bounds__(256) single_attention_kernel(const __nv_bfloat16* __restrict__ qkvg,
+                                                                const float* __restrict__ pair_bias,
+                                                                const void* __restrict__ extra, int extra_f32,
+                                                                const uint8_t* __restrict__ mask, float gate_bias,
+                                                                __nv_bfloat16* __restrict__ out, int B, int N) {
+  const int lane = threadIdx.x & 31;
+  const int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+  if (w >= static_cast<int64_t>(B) * kHs * N) return;
+  const int i = static_cast<int>(w % N);
+  const int h = static_cast<int>((w / N) % kHs);
+  const int b = static_cast<int>(w / (static_cast<int64_t>(N) * kHs));
+  const __nv_bfloat16* row_i = qkvg + (static_cast<int64_t>(b) * N + i) * (4 * kCs);
+  float q[kDs];
+  const float scale = rsqrtf(static_cast<float>(kDs));
+#pragma unroll
+  for (int d = 0; d < kDs; ++d) q[d] = __bfloat162float(row_i[h * kDs + d]) * scale;
+  float m = -__int_as_float(0x7f800000), l = 0.f;
+  float o[kDs];
+#pragma unroll
+  for (int d = 0; d < kDs; ++d) o[d] = 0.f;
+  const float* pb_row = pair_bias + ((static_cast<int64_t>(b) * N + i) * N) * kHs + h;
+  for (int j = lane; j < N; j += 32) {
+    const __nv_bfloat16* row_j = qkvg + (static_cast<int64_t>(b) * N + j) * (4 * kCs);
+    float x = 0.f;
+#pragma unroll
+    for (int d = 0; d < kDs; ++d) x += q[d] * __bfloat162float(row_j[kCs + h * kDs + d]);
+    x += pb_row[static_cast<int64_t>(j) * kHs];
+    if (extra != nullptr) {
+      const int64_t e = ((static_cast<int64_t>(b) * kHs + h) * N + i) * N + j;
+      x += extra_f32 ? static_cast<const float*>(extra)[e]
+                     : __bfloat162float(static_cast<const __nv_bfloat16*>(extra)[e]);
+    }
+    if (!mask[static_cast<int64_t>(b) * N + j]) x = -1.0e9f;
+    const float m_new = fmaxf(m, x);
+    const float alpha = __expf(m - m_new);
+    const float p = __expf(x - m_new);
+    l = l * alpha + p;
+#pragma unroll
+    for (int d = 0; d < kDs; ++d) o[d] = o[d] * alpha + p * __bfloat162float(row_j[2 * kCs + h * kDs + d]);
+    m = m_new;
+  }
+  // merge the 32 lane-private softmax states
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float m2 = __shfl_xor_sync(0xFFFFFFFFu, m, off);
+    const float l2 = __shfl_xor_sync(0xFFFFFFFFu, l, off);
+    const float mn = fmaxf(m, m2);
+    const float a1 = (l > 0.f) ? __expf(m - mn) : 0.f;
+    const float a2 = (l2 > 0.f) ? __expf(m2 - mn) : 0.f;
+#pragma unroll
+    for (int d = 0; d < kDs; ++d) {
+      const float o2 = __shfl_xor_sync(0xFFFFFFFFu, o[d], off);
+      o[d] = o[d] * a1 + o2 * a2;
+    }
+    l = l * a1 + l2 * a2;
+    m = mn;
+  }
+  if (lane < kDs) {
+    float v = 0.f;
+#pragma unroll
+    for (int d = 0; d < kDs; ++d)
+      if (d == lane) v = o[d];
+    v /= l;
+    const float g = __bfloat162float(row_i[3 * kCs + h * kDs + lane]) + gate_bias;
+    out[(static_cast<int64_t>(b) * N + i) * kCs + h * kDs + lane] = __float2bfloat16_rn(v * sigmoidf_(g));
+  }
+}
+
+// ---------------------------------------------------------------- helpers
+int gemm(const void* a, const void* w, void* d, int m, int n, int k, int d_f32, const float* bias, int epilogue,
+         const void* residual, const uint8_t* row_mask, const DeviceInfo& info, cudaStream_t stream) {
+  const int bn = n >= 256 ? 256 : 128;
+  CUtensorMap ma, mb;
+  const uint64_t adims[3] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m), 1};
+  const uint64_t astr[2] = {static_cast<uint64_t>(k) * 2, static_cast<uint64_t>(k) * m * 2};
+  const uint32_t abox[3] = {64, 128, 1};
+  int st = make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a, adims, astr, abox, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st) return st;
+  const uint64_t bdims[3] = {static_cast<uint64_t>(k), static_cast<uint64_t>(n), 1};
+  const uint64_t bstr[2] = {static_cast<uint64_t>(k) * 2, static_cast<uint64_t>(k) * n * 2};
+  const uint32_t bbox[3] = {64, static_cast<uint32_t>(bn), 1};
+  st = make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w, bdims, bstr, bbox, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st) return st;
+  GemmParams p;
+  p.M = m;
+  p.N = n;
+  p.K = k;
+  p.batch = 1;
+  p.D = d;
+  p.ldd = epilogue == kEpiSwiGLU ? n / 2 : n;
+  p.batch_stride_d = 0;
+  p.d_is_f32 = d_f32;
+  p.epilogue = epilogue;
+  p.bias = bias;
+  p.residual = residual;
+  p.row_mask = row_mask;
+  p.err = info.err;
+  return cuda_status(launch_gemm_nt(ma, mb, p, bn, info.num_sms, stream), "single-track gemm");
+}
+
+size_t a256(size_t x) { return (x + 255) / 256 * 256; }
+
+// packed attention-with-pair-bias image
+struct ApbLayout {
+  size_t w_qkvg, b_qkvg, w_o, w_pb, ln_s_w, ln_s_b, ln_p_w, total;
+};
+ApbLayout apb_layout() {
+  ApbLayout L;
+  size_t o = 0;
+  L.w_qkvg = o;  o = a256(o + static_cast<size_t>(4 * kCs) * kCs * 2);
+  L.b_qkvg = o;  o = a256(o + 4 * kCs * 4);
+  L.w_o = o;     o = a256(o + static_cast<size_t>(kCs) * kCs * 2);
+  L.w_pb = o;    o = a256(o + kHs * kCz * 2);
+  L.ln_s_w = o;  o = a256(o + kCs * 4);
+  L.ln_s_b = o;  o = a256(o + kCs * 4);
+  L.ln_p_w = o;  o = a256(o + kCz * 4);
+  L.total = o;
+  return L;
+}
+
+struct StLayout {
+  size_t w_ab, w_sq, ln_w, ln_b, total;
+};
+StLayout st_layout() {
+  StLayout L;
+  size_t o = 0;
+  L.w_ab = o;  o = a256(o + static_cast<size_t>(8 * kCs) * kCs * 2);
+  L.w_sq = o;  o = a256(o + static_cast<size_t>(kCs) * 4 * kCs * 2);
+  L.ln_w = o;  o = a256(o + kCs * 4);
+  L.ln_b = o;  o = a256(o + kCs * 4);
+  L.total = o;
+  return L;
+}
+
+}  // namespace
+
+size_t apb_packed_bytes() { return apb_layout().total; }
+
+size_t apb_workspace_bytes(int B, int N) {
+  const size_t P = static_cast<size_t>(B) * N * N, T = static_cast<size_t>(B) * N;
+  return a256(P * kCz * 2) + a256(P * kHs * 4) + a256(T * kCs * 2) + a256(T * 4 * kCs * 2) + a256(T * kCs * 2);
+}
+
+int apb_prepare(const ApbWeights& w, void* packed, cudaStream_t stream) {
+  const ApbLayout L = apb_layout();
+  uint8_t* img = static_cast<uint8_t*>(packed);
+  int rc = static_cast<int>(cudaMemsetAsync(packed, 0, L.total, stream));
+  const float* mats[4] = {w.to_query, w.to_key, w.to_value, w.to_gate};
+  for (int i = 0; i < 4 && rc == 0; ++i)
+    rc = to_bf16(mats[i], nullptr, kCs, kCs, 0, img + L.w_qkvg + static_cast<size_t>(i) * kCs * kCs * 2, stream);
+  if (rc == 0) rc = static_cast<int>(cudaMemcpyAsync(img + L.b_qkvg, w.query_bias, kCs * 4, cudaMemcpyDeviceToDevice, stream));
+  if (rc == 0) rc = to_bf16(w.to_out, nullptr, kCs, kCs, 0, img + L.w_o, stream);
+  if (rc == 0) rc = to_bf16(w.to_bias, nullptr, kHs, kCz, 0, img + L.w_pb, stream);
+  if (rc == 0) rc = static_cast<int>(cudaMemcpyAsync(img + L.ln_s_w, w.ln_single_w, kCs * 4, cudaMemcpyDeviceToDevice, stream));
+  if (rc == 0) rc = static_cast<int>(cudaMemcpyAsync(img + L.ln_s_b, w.ln_single_b, kCs * 4, cudaMemcpyDeviceToDevice, stream));
+  if (rc == 0) rc = static_cast<int>(cudaMemcpyAsync(img + L.ln_p_w, w.ln_pair_w, kCz * 4, cudaMemcpyDeviceToDevice, stream));
+  return rc;
+}
+
+int apb_forward(const void* s, const void* z, const uint8_t* mask, const void* packed, const void* extra,
+                int extra_f32, float gate_bias, void* out, void* workspace, int B, int N, int masked_zero,
+                const DeviceInfo& info, cudaStream_t stream) {
+  const ApbLayout L = apb_layout();
+  const uint8_t* img = static_cast<const uint8_t*>(packed);
+  const size_t P = static_cast<size_t>(B) * N * N, T = static_cast<size_t>(B) * N;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  void* zn = ws;
+  float* pb = reinterpret_cast<float*>(ws + a256(P * kCz * 2));
+  void* y = ws + a256(P * kCz * 2) + a256(P * kHs * 4);
+  void* qkvg = static_cast<uint8_t*>(y) + a256(T * kCs * 2);
+  void* gated = static_cast<uint8_t*>(qkvg) + a256(T * 4 * kCs * 2);
+  int st = cuda_status(launch_layernorm(z, zn, reinterpret_cast<const float*>(img + L.ln_p_w), nullptr,
+                                        static_cast<int64_t>(P), kCz, 1e-5f, 0, info.num_sms, stream),
+                       "apb pair layernorm");
+  if (st) return st;
+  st = gemm(zn, img + L.w_pb, pb, static_cast<int>(P), kHs, kCz, 1, nullptr, kEpiStore, nullptr, nullptr, info, stream);
+  if (st) return st;
+  st = cuda_status(launch_layernorm(s, y, reinterpret_cast<const float*>(img + L.ln_s_w),
+                                    reinterpret_cast<const float*>(img + L.ln_s_b), static_cast<int64_t>(T), kCs,
+                                    1e-5f, 0, info.num_sms, stream),
+                   "apb single layernorm");
+  if (st) return st;
+  st = gemm(y, img + L.w_qkvg, qkvg, static_cast<int>(T), 4 * kCs, kCs, 0,
+            reinterpret_cast<const float*>(img + L.b_qkvg), kEpiStore, nullptr, nullptr, info, stream);
+  if (st) return st;
+  const int64_t warps = static_cast<int64_t>(B) * kHs * N;
+  single_attention_kernel<<<static_cast<int>((warps + 7) / 8), 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(qkvg), pb, extra, extra_f32, mask, gate_bias,
+      static_cast<__nv_bfloat16*>(gated), B, N);
+  st = cuda_status(static_cast<int>(cudaGetLastError()), "single attention launch");
+  if (st) return st;
+  return gemm(gated, img + L.w_o, out, static_cast<int>(T), kCs, kCs, 0, nullptr, kEpiResidual, s,
+              masked_zero ? mask : nullptr, info, stream);
+}
+
+size_t single_transition_packed_bytes() { return st_layout().total; }
+
+size_t single_transition_workspace_bytes(int B, int N) {
+  const size_t T = static_cast<size_t>(B) * N;
+  return a256(T * kCs * 2) + a256(T * 4 * kCs * 2);
+}
+
+int single_transition_prepare(const TransitionWeights& w, void* packed, cudaStream_t stream) {
+  const StLayout L = st_layout();
+  uint8_t* img = static_cast<uint8_t*>(packed);
+  int rc = to_bf16(w.expand_a, w.expand_b, 4 * kCs, kCs, 1, img + L.w_ab, stream);
+  if (rc == 0) rc = to_bf16(w.squeeze, nullptr, kCs, 4 * kCs, 0, img + L.w_sq, stream);
+  if (rc == 0) rc = static_cast<int>(cudaMemcpyAsync(img + L.ln_w, w.ln_w, kCs * 4, cudaMemcpyDeviceToDevice, stream));
+  if (rc == 0) rc = static_cast<int>(cudaMemcpyAsync(img + L.ln_b, w.ln_b, kCs * 4, cudaMemcpyDeviceToDevice, stream));
+  return rc;
+}
+
+int single_transition_forward(const void* s, const uint8_t* mask, const void* packed, void* out, void* workspace,
+                              int B, int N, int masked_zero, const DeviceInfo& info, cudaStream_t stream) {
+  const StLayout L = st_layout();
+  const uint8_t* img = static_cast<const uint8_t*>(packed);
+  const size_t T = static_cast<size_t>(B) * N;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  void* y = ws;
+  void* hid = ws + a256(T * kCs * 2);
+  int st = cuda_status(launch_layernorm(s, y, reinterpret_cast<const float*>(img + L.ln_w),
+                                        reinterpret_cast<const float*>(img + L.ln_b), static_cast<int64_t>(T), kCs,
+                                        1e-5f, 0, info.num_sms, stream),
+                       "single transition layernorm");
+  if (st) return st;
+  st = gemm(y, img + L.w_ab, hid, static_cast<int>(T), 8 * kCs, kCs, 0, nullptr, kEpiSwiGLU, nullptr, nullptr, info,
+            stream);
+  if (st) return st;
+  return gemm(hid, img + L.w_sq, out, static_cast<int>(T), kCs, 4 * kCs, 0, nullptr, kEpiResidual, s,
+              masked_zero ? mask : nullptr, info, stream);
+}
+
+}  // namespace ffb

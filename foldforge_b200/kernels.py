@@ -155,3 +155,95 @@ def triattn(z: Tensor, mask: Tensor, packed: Tensor, *, starting: bool, masked_z
     _lib.call("ffb_triattn_fwd", _ptr(z), _ptr(m), _ptr(packed), _ptr(out), _ptr(ws), ctypes.c_size_t(ws_bytes), b, n,
               int(starting), int(masked_zero), _stream())
     return out
+
+
+def transition_prepare(weights: dict[str, Tensor], device: torch.device) -> Tensor:
+    """Pack a pair ``Transition(128, 4)``'s fp32 weights (engine keys) for the fused kernel."""
+    lib = _lib.load()
+    packed = torch.empty(int(lib.ffb_transition_packed_bytes()), dtype=torch.uint8, device=device)
+    keys = ("ln_in.weight", "ln_in.bias", "expand_a.weight", "expand_b.weight", "squeeze.weight")
+    ts = [_f32(weights[k]).to(device) for k in keys]
+    _need_cuda(*ts)
+    _lib.call("ffb_transition_prepare", *[_ptr(t) for t in ts], _ptr(packed), _stream())
+    packed._keepalive = ts
+    return packed
+
+
+def transition(z: Tensor, mask: Tensor | None, packed: Tensor, *, masked_zero: bool = True) -> Tensor:
+    """Fused pair transition with residual: ``z [B, N, N, 128]`` bf16."""
+    _need_cuda(z, mask, packed)
+    if z.dtype != torch.bfloat16 or z.dim() != 4 or z.shape[-1] != 128:
+        raise _lib.UnsupportedCall("transition", 2, f"needs bf16 [B, N, N, 128], got {z.dtype} {tuple(z.shape)}")
+    z = z.contiguous()
+    out = torch.empty_like(z)
+    m = None if mask is None else _mask_u8(mask)
+    _lib.call("ffb_transition_fwd", _ptr(z), _ptr(m), _ptr(packed), _ptr(out), z.shape[0], z.shape[1],
+              int(masked_zero and m is not None), _stream())
+    return out
+
+
+def apb_prepare(weights: dict[str, Tensor], device: torch.device) -> Tensor:
+    """Pack an ``AttentionPairBias``'s fp32 weights (engine keys) for the kernels."""
+    lib = _lib.load()
+    packed = torch.empty(int(lib.ffb_apb_packed_bytes()), dtype=torch.uint8, device=device)
+    keys = ("ln_single.weight", "ln_single.bias", "to_query.weight", "to_query.bias", "to_key.weight",
+            "to_value.weight", "to_gate.weight", "to_out.weight", "ln_pair.weight", "to_bias.weight")
+    ts = [_f32(weights[k]).to(device) for k in keys]
+    _need_cuda(*ts)
+    _lib.call("ffb_apb_prepare", *[_ptr(t) for t in ts], _ptr(packed), _stream())
+    packed._keepalive = ts
+    return packed
+
+
+def attention_pair_bias(s: Tensor, z: Tensor, mask: Tensor, packed: Tensor, *, extra_pair_bias: Tensor | None = None,
+                        gate_bias: float = 0.0, masked_zero: bool = True) -> Tensor:
+    """Single attention with pair bias and residual: ``s [B, N, 384]``, ``z [B, N, N, 128]`` bf16."""
+    _need_cuda(s, z, mask, packed, extra_pair_bias)
+    if s.dtype != torch.bfloat16 or z.dtype != torch.bfloat16 or s.shape[-1] != 384 or z.shape[-1] != 128:
+        raise _lib.UnsupportedCall("attention_pair_bias", 2, "needs bf16 s [B, N, 384] and z [B, N, N, 128]")
+    s, z = s.contiguous(), z.contiguous()
+    b, n = s.shape[0], s.shape[1]
+    lib = _lib.load()
+    ws_bytes = int(lib.ffb_apb_workspace_bytes(b, n))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=s.device)
+    out = torch.empty_like(s)
+    extra = None
+    extra_dtype = BF16
+    if extra_pair_bias is not None:
+        extra = extra_pair_bias.expand(b, 16, n, n).contiguous()
+        if extra.dtype not in (torch.bfloat16, torch.float32):
+            extra = extra.float()
+        extra_dtype = _DTYPES[extra.dtype]
+    _lib.call("ffb_apb_fwd", _ptr(s), _ptr(z), _ptr(_mask_u8(mask)), _ptr(packed), _ptr(extra), extra_dtype,
+              ctypes.c_float(gate_bias), _ptr(out), _ptr(ws), ctypes.c_size_t(ws_bytes), b, n, int(masked_zero),
+              _stream())
+    return out
+
+
+def single_transition_prepare(weights: dict[str, Tensor], device: torch.device) -> Tensor:
+    """Pack a single ``Transition(384, 4)``'s fp32 weights for the GEMM path."""
+    lib = _lib.load()
+    packed = torch.empty(int(lib.ffb_single_transition_packed_bytes()), dtype=torch.uint8, device=device)
+    keys = ("ln_in.weight", "ln_in.bias", "expand_a.weight", "expand_b.weight", "squeeze.weight")
+    ts = [_f32(weights[k]).to(device) for k in keys]
+    _need_cuda(*ts)
+    _lib.call("ffb_single_transition_prepare", *[_ptr(t) for t in ts], _ptr(packed), _stream())
+    packed._keepalive = ts
+    return packed
+
+
+def single_transition(s: Tensor, mask: Tensor | None, packed: Tensor, *, masked_zero: bool = True) -> Tensor:
+    """Single transition with residual: ``s [B, N, 384]`` bf16."""
+    _need_cuda(s, mask, packed)
+    if s.dtype != torch.bfloat16 or s.shape[-1] != 384:
+        raise _lib.UnsupportedCall("single_transition", 2, "needs bf16 [B, N, 384]")
+    s = s.contiguous()
+    b, n = s.shape[0], s.shape[1]
+    lib = _lib.load()
+    ws_bytes = int(lib.ffb_single_transition_workspace_bytes(b, n))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=s.device)
+    out = torch.empty_like(s)
+    m = None if mask is None else _mask_u8(mask)
+    _lib.call("ffb_single_transition_fwd", _ptr(s), _ptr(m), _ptr(packed), _ptr(out), _ptr(ws),
+              ctypes.c_size_t(ws_bytes), b, n, int(masked_zero and m is not None), _stream())
+    return out

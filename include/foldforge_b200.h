@@ -109,6 +109,47 @@ int ffb_triattn_prepare(const float* ln_w, const float* ln_b, const float* to_bi
 int ffb_triattn_fwd(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace,
                     size_t workspace_bytes, int B, int N, int starting, int masked, void* stream);
 
+/* ---- Pair transition (c_z = 128, factor 4), fused LayerNorm -> expand -> SwiGLU ->
+ * squeeze -> residual. Replaces the engine `Transition(128, 4)` as FoldForge calls it
+ * (src/foldforge/modules/engine/modules.py:133-141); equations of legacy/primitives.py:20-37
+ * and legacy/reference/transition.py:28-59 (expand_a / expand_b = legacy/released.py:211-224).
+ * ffb_transition_prepare: ln_w, ln_b [128], expand_a, expand_b [512, 128], squeeze [128, 512]
+ * fp32 -> `packed` (ffb_transition_packed_bytes()). ffb_transition_fwd needs no workspace.
+ * `mask` may be NULL when masked == FFB_MASKED_COMPUTE. */
+size_t ffb_transition_packed_bytes(void);
+int ffb_transition_prepare(const float* ln_w, const float* ln_b, const float* expand_a, const float* expand_b,
+                           const float* squeeze, void* packed, void* stream);
+int ffb_transition_fwd(const void* z, const uint8_t* mask, const void* packed, void* out, int B, int N, int masked,
+                       void* stream);
+
+/* ---- Single-track attention with pair bias (c_s = 384, 16 heads x 24, c_z = 128).
+ * Replaces the engine `AttentionPairBias` of the Pairformer block; equations of
+ * legacy/pairformer.py:204-226 and legacy/transformer.py:88-133 with the engine weight
+ * names of legacy/released.py:281-315 (the pair LayerNorm has no offset).
+ * ffb_apb_prepare: ln_single_w/_b [384], to_query [384, 384], query_bias [384], to_key,
+ * to_value, to_gate, to_out [384, 384], ln_pair_w [128], to_bias [16, 128] (fp32).
+ * ffb_apb_fwd: s, out [B, N, 384] bf16; z [B, N, N, 128] bf16 (the pair AFTER the pair
+ * track); extra_pair_bias [B, 16, N, N] (extra_dtype FFB_BF16 / FFB_F32) or NULL;
+ * gate_bias is added to the gate logits (0 for AF3). */
+size_t ffb_apb_packed_bytes(void);
+size_t ffb_apb_workspace_bytes(int B, int N);
+int ffb_apb_prepare(const float* ln_single_w, const float* ln_single_b, const float* to_query,
+                    const float* query_bias, const float* to_key, const float* to_value, const float* to_gate,
+                    const float* to_out, const float* ln_pair_w, const float* to_bias, void* packed, void* stream);
+int ffb_apb_fwd(const void* s, const void* z, const uint8_t* mask, const void* packed, const void* extra_pair_bias,
+                int extra_dtype, float gate_bias, void* out, void* workspace, size_t workspace_bytes, int B, int N,
+                int masked, void* stream);
+
+/* ---- Single transition (c_s = 384, factor 4). Same equations as the pair transition.
+ * ffb_single_transition_prepare: ln_w, ln_b [384], expand_a, expand_b [1536, 384],
+ * squeeze [384, 1536] fp32. ffb_single_transition_fwd: s, out [B, N, 384] bf16. */
+size_t ffb_single_transition_packed_bytes(void);
+size_t ffb_single_transition_workspace_bytes(int B, int N);
+int ffb_single_transition_prepare(const float* ln_w, const float* ln_b, const float* expand_a,
+                                  const float* expand_b, const float* squeeze, void* packed, void* stream);
+int ffb_single_transition_fwd(const void* s, const uint8_t* mask, const void* packed, void* out, void* workspace,
+                              size_t workspace_bytes, int B, int N, int masked, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

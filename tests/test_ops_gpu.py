@@ -101,3 +101,57 @@ def test_triattn_fully_masked_rows_average_uniformly(weights, starting):
     assert oracle.rel_l2(got[0] - z[0].float(), want - z[0].float()) < DELTA_TOL
     zero = kernels.triattn(z.cuda(), tokens.cuda() > 0, packed, starting=starting, masked_zero=True).cpu()
     assert torch.equal(zero, z)
+
+
+@pytest.mark.parametrize("b,n,masked", CASES + [(1, 200, 0)])
+def test_pair_transition_matches_oracle(weights, b, n, masked):
+    p = sub(weights, "transition_pair")
+    z, tokens = pair_inputs(b, n, masked, seed=8)
+    packed = kernels.transition_prepare(p, torch.device("cuda"))
+    got = kernels.transition(z.cuda(), tokens.cuda() > 0, packed, masked_zero=False).float().cpu()
+    for i in range(b):
+        want = oracle.transition(z[i].float(), p)
+        assert oracle.rel_l2(got[i], want) < OUT_TOL
+        assert oracle.rel_l2(got[i] - z[i].float(), want - z[i].float()) < DELTA_TOL
+    zero = kernels.transition(z.cuda(), tokens.cuda() > 0, packed, masked_zero=True).cpu()
+    for i in range(b):
+        pm = (tokens[i][:, None] * tokens[i][None, :]) > 0
+        assert torch.equal(zero[i][~pm], z[i][~pm])
+
+
+def single_inputs(b, n, masked, seed=9):
+    g = torch.Generator().manual_seed(seed)
+    s = torch.randn(b, n, 384, generator=g).bfloat16()
+    z, tokens = pair_inputs(b, n, masked, seed=seed + 1)
+    return s, z, tokens
+
+
+@pytest.mark.parametrize("extra", [False, True])
+@pytest.mark.parametrize("b,n,masked", CASES + [(1, 300, 17)])
+def test_attention_pair_bias_matches_oracle(weights, extra, b, n, masked):
+    p = sub(weights, "single_attention")
+    s, z, tokens = single_inputs(b, n, masked)
+    bias = torch.randn(n, n, generator=torch.Generator().manual_seed(4)) if extra else None
+    packed = kernels.apb_prepare(p, torch.device("cuda"))
+    ext = None if bias is None else bias.cuda()[None, None]
+    got = kernels.attention_pair_bias(s.cuda(), z.cuda(), tokens.cuda() > 0, packed, extra_pair_bias=ext,
+                                      masked_zero=False).float().cpu()
+    for i in range(b):
+        want = oracle.attention_pair_bias(s[i].float(), z[i].float(), tokens[i], p, extra_pair_bias=bias)
+        assert oracle.rel_l2(got[i], want) < OUT_TOL
+        assert oracle.rel_l2(got[i] - s[i].float(), want - s[i].float()) < DELTA_TOL
+
+
+@pytest.mark.parametrize("b,n,masked", CASES)
+def test_single_transition_matches_oracle(weights, b, n, masked):
+    p = sub(weights, "single_transition")
+    s, _, tokens = single_inputs(b, n, masked, seed=12)
+    packed = kernels.single_transition_prepare(p, torch.device("cuda"))
+    got = kernels.single_transition(s.cuda(), tokens.cuda() > 0, packed, masked_zero=False).float().cpu()
+    for i in range(b):
+        want = oracle.transition(s[i].float(), p)
+        assert oracle.rel_l2(got[i], want) < OUT_TOL
+        assert oracle.rel_l2(got[i] - s[i].float(), want - s[i].float()) < DELTA_TOL
+    zero = kernels.single_transition(s.cuda(), tokens.cuda() > 0, packed, masked_zero=True).cpu()
+    for i in range(b):
+        assert torch.equal(zero[i][tokens[i] == 0], s[i][tokens[i] == 0])
