@@ -1,0 +1,581 @@
+"""The engine op classes of the Pairformer pair stack, with a ``pytorch`` and a ``b200`` backend.
+
+These re-provide the engine-module contract FoldForge's graph consumes (the classes of
+``miniworld_engine.modules`` that ``src/foldforge/modules/engine/{modules,pairformer}.py``
+build): the same class names, constructor arguments, child names and state-dict keys
+(the schema ``legacy/released.py:318-369`` writes), ``backends`` / ``backend`` /
+``set_backend`` / ``unsupported`` / ``_forward_<backend>``, the ``dead`` flag and the
+``MasterWeights`` mixin. Every op returns its input PLUS its update (the residual is owned).
+
+* ``pytorch``: the reference equations (``legacy/reference/*.py``) on batched tensors, in
+  fp32 internally, output in the input dtype.
+* ``b200``: the sm_100a kernels through the C ABI (:mod:`foldforge_b200.kernels`); it
+  never falls back by itself -- a call outside its range is refused by ``unsupported()``
+  and the caller's guard decides (``engine.unsupported``).
+
+Masked positions: ``masked_update = "zero"`` (default) leaves every pair (i, j) with
+``mask_i * mask_j == 0`` and every padded single row exactly unchanged; ``"compute"``
+applies the reference equations there too.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+Tensor = torch.Tensor
+MASKED_UPDATES = ("zero", "compute")
+
+
+class BackendUnsupported(RuntimeError):
+    """A call outside the selected backend's range, made directly (without the guard)."""
+
+
+class MasterWeights:
+    """fp32 master parameters: under ``set_master_weights()`` a bulk cast keeps them fp32
+    (the kernels cast to bf16 themselves); LayerNorm affines are fp32 under any cast."""
+
+    master_weights: bool = False
+
+    def set_master_weights(self) -> None:
+        for m in self.modules():  # type: ignore[attr-defined]
+            if isinstance(m, MasterWeights):
+                m.master_weights = True
+
+    def _apply(self, fn, recurse=True):  # noqa: ANN001 - torch.nn.Module._apply signature
+        out = super()._apply(fn, recurse)  # type: ignore[misc]
+        if self.master_weights:
+            for p in self.parameters():  # type: ignore[attr-defined]
+                if p.is_floating_point() and p.dtype != torch.float32:
+                    p.data = p.data.float()
+        return out
+
+
+class LayerNorm(nn.LayerNorm):
+    """The engine ``LayerNorm``: fp32 affine under any cast; backends ``pytorch`` / ``b200``."""
+
+    backends = ("pytorch", "b200")
+    dead = False
+
+    def __init__(self, d, eps: float = 1e-5, bias: bool = True, elementwise_affine: bool = True) -> None:
+        super().__init__(d, eps=eps, elementwise_affine=elementwise_affine, bias=bias)
+        self.backend = "pytorch"
+
+    def _apply(self, fn, recurse=True):  # noqa: ANN001
+        out = super()._apply(fn, recurse)
+        for p in self.parameters(recurse=False):
+            if p.dtype != torch.float32:
+                p.data = p.data.float()
+        return out
+
+    def set_backend(self, name: str) -> None:
+        _check_backend(self, name)
+        self.backend = name
+
+    def unsupported(self, x: Tensor) -> str | None:
+        if self.backend == "pytorch":
+            return None
+        reason = _cuda_reason(x)
+        if reason:
+            return reason
+        if x.dtype not in (torch.bfloat16, torch.float32):
+            return f"dtype {x.dtype} (bf16 or fp32 only)"
+        if len(self.normalized_shape) != 1:
+            return "normalisation over more than one axis"
+        return None
+
+    def forward(self, x: Tensor) -> Tensor:
+        return _dispatch(self, x)
+
+    def _forward_pytorch(self, x: Tensor) -> Tensor:
+        w = None if self.weight is None else self.weight.float()
+        b = None if self.bias is None else self.bias.float()
+        return F.layer_norm(x.float(), self.normalized_shape, w, b, self.eps).to(x.dtype)
+
+    def _forward_b200(self, x: Tensor) -> Tensor:
+        from foldforge_b200 import kernels
+
+        return kernels.layer_norm(x, self.weight, self.bias, self.eps)
+
+
+# --------------------------------------------------------------------------- helpers
+def _check_backend(module: nn.Module, name: str) -> None:
+    if name not in type(module).backends:
+        message = f"{type(module).__name__} has no {name!r} backend (available: {', '.join(type(module).backends)})"
+        raise BackendUnsupported(message)
+
+
+def _cuda_reason(*ts: Tensor | None) -> str | None:
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            return "tensor is not on a CUDA device"
+        if torch.cuda.get_device_capability(t.device) != (10, 0):
+            return "the b200 kernels need an sm_100 device"
+        if t.requires_grad and torch.is_grad_enabled():
+            return "autograd is not supported by the b200 kernels (inference only)"
+    return None
+
+
+def _library_reason() -> str | None:
+    from foldforge_b200 import _lib
+
+    try:
+        _lib.load()
+    except _lib.LibraryMissing as exc:
+        return str(exc)
+    return None
+
+
+def _dispatch(module: nn.Module, *args, **kwargs):
+    backend = module.backend
+    if backend != "pytorch":
+        reason = module.unsupported(*args, **kwargs)
+        if reason is not None:
+            raise BackendUnsupported(f"{type(module).__name__} backend {backend!r}: {reason}")
+    if module.dead:
+        return args[0]
+    return getattr(module, f"_forward_{backend}")(*args, **kwargs)
+
+
+def _pair_mask(key_mask: Tensor | None, x: Tensor) -> Tensor:
+    if key_mask is None:
+        return torch.ones(x.shape[:-1], device=x.device, dtype=torch.float32)
+    m = key_mask.float()
+    return m[:, :, None] * m[:, None, :]
+
+
+def _linear(x: Tensor, layer: nn.Linear) -> Tensor:
+    return F.linear(x, layer.weight.float(), None if layer.bias is None else layer.bias.float())
+
+
+def _ln(x: Tensor, norm: nn.LayerNorm) -> Tensor:
+    w = None if norm.weight is None else norm.weight.float()
+    b = None if norm.bias is None else norm.bias.float()
+    return F.layer_norm(x, norm.normalized_shape, w, b, norm.eps)
+
+
+class _PairOp(MasterWeights, nn.Module):
+    """Shared plumbing of the pair ops: backend selection, refusals, the packed-weight cache."""
+
+    backends = ("pytorch", "b200")
+    dead = False
+    #: channels the b200 kernels are built for
+    b200_channels = 128
+
+    def __init__(self) -> None:
+        super().__init__()
+        self.backend = "pytorch"
+        self.masked_update = "zero"
+        self._packed: tuple[tuple, Tensor] | None = None
+
+    def set_backend(self, name: str) -> None:
+        _check_backend(self, name)
+        self.backend = name
+
+    def _pair_reason(self, x: Tensor, key_mask: Tensor | None) -> str | None:
+        reason = _cuda_reason(x, key_mask) or _library_reason()
+        if reason:
+            return reason
+        if x.dtype != torch.bfloat16:
+            return f"activations are {x.dtype}; the b200 pair kernels take bf16 (master precision)"
+        if x.dim() != 4 or x.shape[1] != x.shape[2]:
+            return f"pair tensor shape {tuple(x.shape)} is not [B, N, N, c]"
+        if x.shape[-1] != self.b200_channels:
+            return f"c_z = {x.shape[-1]} (the b200 kernels are built for {self.b200_channels})"
+        if key_mask is not None and tuple(key_mask.shape) != tuple(x.shape[:2]):
+            return f"key mask {tuple(key_mask.shape)} does not match pair {tuple(x.shape)}"
+        return None
+
+    def _cached_pack(self, pack) -> Tensor:
+        key = tuple((p.data_ptr(), p._version, p.device) for p in self.parameters())
+        if self._packed is None or self._packed[0] != key:
+            with torch.no_grad():
+                self._packed = (key, pack())
+        return self._packed[1]
+
+    def _key_mask(self, x: Tensor, key_mask: Tensor | None) -> Tensor:
+        if key_mask is None:
+            return torch.ones(x.shape[:2], dtype=torch.bool, device=x.device)
+        return key_mask
+
+    def _masked_zero(self) -> bool:
+        if self.masked_update not in MASKED_UPDATES:
+            raise ValueError(f"masked_update must be one of {MASKED_UPDATES}, got {self.masked_update!r}")
+        return self.masked_update == "zero"
+
+    def _zero_masked(self, x: Tensor, delta: Tensor, key_mask: Tensor | None) -> Tensor:
+        if self._masked_zero() and key_mask is not None:
+            delta = delta * _pair_mask(key_mask, x)[..., None]
+        return (x.float() + delta).to(x.dtype)
+
+
+# --------------------------------------------------------------------------- triangle multiplication
+class TriangleMultiplication(_PairOp):
+    """Triangle multiplicative update, outgoing or incoming, residual included.
+
+    Reference equations: ``legacy/reference/triangle.py:19-50`` (``triangle_update``),
+    engine left/right per ``legacy/released.py:135-173``.
+    """
+
+    def __init__(self, d_pair: int, d_hidden: int | None = None, outgoing: bool = True, p_drop: float = 0.0,
+                 model: str | None = None) -> None:
+        super().__init__()
+        if model not in (None, "af3"):
+            raise ValueError(f"TriangleMultiplication(model={model!r}): only the AF3 form is built here")
+        hidden = d_hidden or d_pair
+        self.d_pair, self.d_hidden, self.outgoing, self.p_drop = d_pair, hidden, outgoing, p_drop
+        self.ln_pair = LayerNorm(d_pair)
+        self.ln_out = LayerNorm(hidden)
+        self.to_left = nn.Linear(d_pair, hidden, bias=False)
+        self.to_right = nn.Linear(d_pair, hidden, bias=False)
+        self.to_left_gate = nn.Linear(d_pair, hidden, bias=False)
+        self.to_right_gate = nn.Linear(d_pair, hidden, bias=False)
+        self.to_out = nn.Linear(hidden, d_pair, bias=False)
+        self.to_gate = nn.Linear(d_pair, d_pair, bias=False)
+
+    def unsupported(self, x: Tensor, key_mask: Tensor | None = None) -> str | None:
+        if self.backend == "pytorch":
+            return None
+        if self.d_hidden != 128:
+            return f"hidden width {self.d_hidden} (the b200 kernels are built for 128)"
+        return self._pair_reason(x, key_mask)
+
+    def forward(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
+        return _dispatch(self, x, key_mask)
+
+    def _forward_pytorch(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
+        z = x.float()
+        v = _ln(z, self.ln_pair)
+        m = _pair_mask(key_mask, z)[..., None]
+        left = _linear(v, self.to_left) * m * torch.sigmoid(_linear(v, self.to_left_gate))
+        right = _linear(v, self.to_right) * m * torch.sigmoid(_linear(v, self.to_right_gate))
+        eq = "bikc,bjkc->bijc" if self.outgoing else "bkic,bkjc->bijc"
+        u = torch.einsum(eq, left, right)
+        delta = _linear(_ln(u, self.ln_out), self.to_out) * torch.sigmoid(_linear(v, self.to_gate))
+        return self._zero_masked(x, delta, key_mask)
+
+    def _forward_b200(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
+        from foldforge_b200 import kernels
+
+        weights = {k: v for k, v in self.state_dict().items()}
+        packed = self._cached_pack(lambda: kernels.trimul_prepare(weights, x.device))
+        return kernels.trimul(x, self._key_mask(x, key_mask), packed, outgoing=self.outgoing,
+                              masked_zero=self._masked_zero())
+
+
+# --------------------------------------------------------------------------- triangle attention
+TRIANGLE_ATTENTION_MODELS: dict[str, str] = {"af3": "TriangleAttentionAF3"}
+
+
+class TriangleAttention(_PairOp):
+    """Triangle attention around the starting (rows) or ending (columns) node.
+
+    ``TriangleAttention(..., model=key)`` builds the class of ``key``; only AF3's
+    (``TriangleAttentionAF3``: untransposed pair bias, no projection biases) is built here.
+    Reference equations: ``legacy/attention.py:108-171``, ``legacy/reference/attention.py:14-100``.
+    """
+
+    def __new__(cls, *args, model: str = "af3", **kwargs):  # noqa: D102 - dispatch on the model key
+        if cls is TriangleAttention:
+            name = TRIANGLE_ATTENTION_MODELS.get(model)
+            if name is None:
+                raise ValueError(f"TriangleAttention(model={model!r}): known {sorted(TRIANGLE_ATTENTION_MODELS)}")
+            cls = globals()[name]
+        return super().__new__(cls)
+
+    def __init__(self, d_pair: int, n_head: int, d_hidden: int | None = None, starting: bool = True,
+                 p_drop: float = 0.0, model: str = "af3") -> None:
+        super().__init__()
+        hidden = d_hidden * n_head if d_hidden else d_pair
+        self.d_pair, self.n_head, self.starting, self.p_drop, self.model = d_pair, n_head, starting, p_drop, model
+        self.d_head = hidden // n_head
+        self.ln_pair = LayerNorm(d_pair)
+        self.to_bias = nn.Linear(d_pair, n_head, bias=False)
+        self.to_query = nn.Linear(d_pair, hidden, bias=False)
+        self.to_key = nn.Linear(d_pair, hidden, bias=False)
+        self.to_value = nn.Linear(d_pair, hidden, bias=False)
+        self.to_gate = nn.Linear(d_pair, hidden, bias=False)
+        self.to_out = nn.Linear(hidden, d_pair, bias=False)
+
+    def unsupported(self, x: Tensor, key_mask: Tensor | None = None) -> str | None:
+        if self.backend == "pytorch":
+            return None
+        if (self.n_head, self.d_head) != (4, 32):
+            return f"{self.n_head} heads x {self.d_head} (the b200 kernels are built for 4 x 32)"
+        return self._pair_reason(x, key_mask)
+
+    def forward(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
+        return _dispatch(self, x, key_mask)
+
+    def _forward_pytorch(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
+        z = x.float()
+        b, n = z.shape[0], z.shape[1]
+        v = _ln(z, self.ln_pair)
+        bias = _linear(v, self.to_bias).permute(0, 3, 1, 2)  # [B, H, q, k]
+        if not self.starting:
+            v = v.transpose(1, 2)
+
+        def heads(t: Tensor) -> Tensor:  # [B, rows, n, H*d] -> [B, rows, H, n, d]
+            return t.reshape(b, n, n, self.n_head, self.d_head).permute(0, 1, 3, 2, 4)
+
+        q = heads(_linear(v, self.to_query)) * self.d_head**-0.5
+        k = heads(_linear(v, self.to_key))
+        val = heads(_linear(v, self.to_value))
+        logits = q @ k.transpose(-1, -2) + bias[:, None]
+        keep = (_pair_mask(key_mask, z) > 0)[:, :, None, None, :]
+        logits = logits.masked_fill(~keep, -1e9)
+        o = (logits.softmax(-1) @ val).permute(0, 1, 3, 2, 4).reshape(b, n, n, -1)
+        delta = _linear(torch.sigmoid(_linear(v, self.to_gate)) * o, self.to_out)
+        if not self.starting:
+            delta = delta.transpose(1, 2)
+        return self._zero_masked(x, delta, key_mask)
+
+    def _forward_b200(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
+        from foldforge_b200 import kernels
+
+        weights = dict(self.state_dict())
+        packed = self._cached_pack(lambda: kernels.triattn_prepare(weights, x.device))
+        return kernels.triattn(x, self._key_mask(x, key_mask), packed, starting=self.starting,
+                               masked_zero=self._masked_zero())
+
+
+class TriangleAttentionAF3(TriangleAttention):
+    """AF3's triangle attention (``model="af3"``)."""
+
+
+# --------------------------------------------------------------------------- transition
+class Transition(_PairOp):
+    """``x + W_sq(silu(W_a LN(x)) * W_b LN(x))`` (``legacy/primitives.py:20-37``,
+    ``legacy/reference/transition.py:28-59``); pair (c = 128) and single (c = 384) widths
+    have b200 kernels."""
+
+    def __init__(self, d_hidden: int, n: int = 4) -> None:
+        super().__init__()
+        self.d, self.n = d_hidden, n
+        self.ln_in = LayerNorm(d_hidden)
+        self.expand_a = nn.Linear(d_hidden, n * d_hidden, bias=False)
+        self.expand_b = nn.Linear(d_hidden, n * d_hidden, bias=False)
+        self.squeeze = nn.Linear(n * d_hidden, d_hidden, bias=False)
+
+    def unsupported(self, x: Tensor, key_mask: Tensor | None = None) -> str | None:
+        if self.backend == "pytorch":
+            return None
+        if self.n != 4 or self.d not in (128, 384):
+            return f"Transition({self.d}, {self.n}) (b200 kernels: (128, 4) pair, (384, 4) single)"
+        reason = _cuda_reason(x, key_mask) or _library_reason()
+        if reason:
+            return reason
+        if x.dtype != torch.bfloat16:
+            return f"activations are {x.dtype}; the b200 kernels take bf16 (master precision)"
+        if self.d == 128 and (x.dim() != 4 or x.shape[1] != x.shape[2]):
+            return f"pair transition input {tuple(x.shape)} is not [B, N, N, 128]"
+        if self.d == 384 and x.dim() != 3:
+            return f"single transition input {tuple(x.shape)} is not [B, N, 384]"
+        return None
+
+    def forward(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
+        return _dispatch(self, x, key_mask)
+
+    def _forward_pytorch(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
+        v = _ln(x.float(), self.ln_in)
+        delta = _linear(F.silu(_linear(v, self.expand_a)) * _linear(v, self.expand_b), self.squeeze)
+        if self._masked_zero() and key_mask is not None:
+            m = _pair_mask(key_mask, x) if x.dim() == 4 else key_mask.float()
+            delta = delta * m[..., None]
+        return (x.float() + delta).to(x.dtype)
+
+    def _forward_b200(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
+        from foldforge_b200 import kernels
+
+        weights = dict(self.state_dict())
+        if self.d == 128:
+            packed = self._cached_pack(lambda: kernels.transition_prepare(weights, x.device))
+            return kernels.transition(x, key_mask, packed, masked_zero=self._masked_zero())
+        packed = self._cached_pack(lambda: kernels.single_transition_prepare(weights, x.device))
+        return kernels.single_transition(x, key_mask, packed, masked_zero=self._masked_zero())
+
+
+# --------------------------------------------------------------------------- single attention
+class AttentionPairBias(_PairOp):
+    """Single-track attention with pair bias, residual included
+    (``legacy/pairformer.py:204-226``, ``legacy/transformer.py:88-133``)."""
+
+    def __init__(self, d_single: int, d_pair: int, n_head: int = 16, gate_bias: float = 0.0) -> None:
+        super().__init__()
+        self.d_single, self.d_pair, self.n_head, self.gate_bias = d_single, d_pair, n_head, gate_bias
+        self.ln_single = LayerNorm(d_single)
+        self.to_query = nn.Linear(d_single, d_single, bias=True)
+        self.to_key = nn.Linear(d_single, d_single, bias=False)
+        self.to_value = nn.Linear(d_single, d_single, bias=False)
+        self.ln_pair = LayerNorm(d_pair, bias=False)
+        self.to_bias = nn.Linear(d_pair, n_head, bias=False)
+        self.to_gate = nn.Linear(d_single, d_single, bias=False)
+        self.to_out = nn.Linear(d_single, d_single, bias=False)
+
+    def unsupported(self, s: Tensor, z: Tensor, key_mask: Tensor | None = None,
+                    extra_pair_bias: Tensor | None = None) -> str | None:
+        if self.backend == "pytorch":
+            return None
+        if (self.d_single, self.d_pair, self.n_head) != (384, 128, 16):
+            return f"widths ({self.d_single}, {self.d_pair}, {self.n_head} heads) (b200: 384, 128, 16)"
+        reason = _cuda_reason(s, z, key_mask, extra_pair_bias) or _library_reason()
+        if reason:
+            return reason
+        if s.dtype != torch.bfloat16 or z.dtype != torch.bfloat16:
+            return "activations must be bf16 (master precision)"
+        if s.dim() != 3 or z.dim() != 4 or z.shape[:2] != s.shape[:2] or z.shape[1] != z.shape[2]:
+            return f"shapes s {tuple(s.shape)}, z {tuple(z.shape)}"
+        return None
+
+    def forward(self, s: Tensor, z: Tensor, key_mask: Tensor | None = None,
+                extra_pair_bias: Tensor | None = None) -> Tensor:
+        return _dispatch(self, s, z, key_mask, extra_pair_bias)
+
+    def _forward_pytorch(self, s: Tensor, z: Tensor, key_mask: Tensor | None = None,
+                         extra_pair_bias: Tensor | None = None) -> Tensor:
+        b, n, cs = s.shape
+        d = cs // self.n_head
+        bias = _linear(_ln(z.float(), self.ln_pair), self.to_bias).permute(0, 3, 1, 2)
+        if extra_pair_bias is not None:
+            bias = bias + extra_pair_bias.float()
+        y = _ln(s.float(), self.ln_single)
+
+        def heads(t: Tensor) -> Tensor:
+            return t.reshape(b, n, self.n_head, d).permute(0, 2, 1, 3)
+
+        q, k, v = heads(_linear(y, self.to_query)), heads(_linear(y, self.to_key)), heads(_linear(y, self.to_value))
+        logits = (q * d**-0.5) @ k.transpose(-1, -2) + bias
+        if key_mask is not None:
+            logits = logits.masked_fill(~key_mask.bool()[:, None, None, :], -1e9)
+        o = (logits.softmax(-1) @ v).permute(0, 2, 1, 3).reshape(b, n, cs)
+        gate = _linear(y, self.to_gate) + self.gate_bias
+        delta = _linear(torch.sigmoid(gate) * o, self.to_out)
+        if self._masked_zero() and key_mask is not None:
+            delta = delta * key_mask.float()[..., None]
+        return (s.float() + delta).to(s.dtype)
+
+    def _forward_b200(self, s: Tensor, z: Tensor, key_mask: Tensor | None = None,
+                      extra_pair_bias: Tensor | None = None) -> Tensor:
+        from foldforge_b200 import kernels
+
+        sd = dict(self.state_dict())
+        if "to_query.bias" not in sd or sd["to_query.bias"] is None:
+            sd["to_query.bias"] = torch.zeros(self.d_single, device=s.device)
+        packed = self._cached_pack(lambda: kernels.apb_prepare(sd, s.device))
+        mask = self._key_mask(s, key_mask)
+        return kernels.attention_pair_bias(s, z, mask, packed, extra_pair_bias=extra_pair_bias,
+                                           gate_bias=self.gate_bias, masked_zero=self._masked_zero())
+
+
+# --------------------------------------------------------------------------- the block
+@dataclass(frozen=True)
+class PairformerConfig:
+    """The engine block's configuration (``modules/engine/pairformer.py:38-53``)."""
+
+    d_pair: int = 128
+    d_hidden_tri_multi: int = 128
+    d_hidden_tri_attention: int = 32
+    n_head_tri_attention: int = 4
+    p_drop: float = 0.0
+    use_triangle_attention: bool = True
+    model: str = "af3"
+    d_single: int = 384
+    n_head_single: int = 16
+    single_gate_bias: float = 0.0
+    pair_transition_n: int = 4
+    single_transition_n: int = 4
+    parallel: bool = False
+    masked_update: str = "zero"
+
+
+class PairformerBlock(MasterWeights, nn.Module):
+    """One AF3 Pairformer block (``legacy/pairformer.py:191-229``, sequential schedule):
+    ``z += TMo; z += TMi; z += TAs; z += TAe; z += Tr(z); s += APB(s, z); s += Tr(s)``.
+
+    Called as ``block(pair [B, N, N, c], key_mask [B, N] bool, single [B, N, c_s] = None,
+    extra_pair_bias [B, H_s, N, N] = None)``; returns ``pair`` or ``(pair, single)``.
+    """
+
+    backends = ("pytorch", "b200")
+    dead = False
+
+    def __init__(self, config: PairformerConfig) -> None:
+        super().__init__()
+        if config.parallel:
+            raise ValueError("the parallel (Chai-1 / RoseTTAFold3) schedule is not built here")
+        if config.masked_update not in MASKED_UPDATES:
+            raise ValueError(f"masked_update must be one of {MASKED_UPDATES}")
+        self.config = config
+        self.backend = "pytorch"
+        c = config.d_pair
+        self.tri_multi_outgoing = TriangleMultiplication(c, config.d_hidden_tri_multi, outgoing=True)
+        self.tri_multi_incoming = TriangleMultiplication(c, config.d_hidden_tri_multi, outgoing=False)
+        if config.use_triangle_attention:
+            self.tri_atten_starting = TriangleAttention(c, config.n_head_tri_attention,
+                                                        d_hidden=config.d_hidden_tri_attention, starting=True,
+                                                        model=config.model)
+            self.tri_atten_ending = TriangleAttention(c, config.n_head_tri_attention,
+                                                      d_hidden=config.d_hidden_tri_attention, starting=False,
+                                                      model=config.model)
+        self.transition_pair = Transition(c, config.pair_transition_n)
+        if config.d_single > 0:
+            self.single_attention = AttentionPairBias(config.d_single, c, config.n_head_single,
+                                                      config.single_gate_bias)
+            self.single_transition = Transition(config.d_single, config.single_transition_n)
+        for m in self.modules():
+            if isinstance(m, _PairOp):
+                m.masked_update = config.masked_update
+
+    def set_backend(self, name: str) -> None:
+        """Put every child op on ``name`` (the composite itself stays a plain module)."""
+        _check_backend(self, name)
+        for m in self.modules():
+            if isinstance(m, _PairOp):
+                m.set_backend(name)
+
+    def forward(self, pair: Tensor, key_mask: Tensor | None = None, single: Tensor | None = None,
+                extra_pair_bias: Tensor | None = None):
+        pair = self.tri_multi_outgoing(pair, key_mask)
+        pair = self.tri_multi_incoming(pair, key_mask)
+        if self.config.use_triangle_attention:
+            pair = self.tri_atten_starting(pair, key_mask)
+            pair = self.tri_atten_ending(pair, key_mask)
+        pair = self.transition_pair(pair, key_mask)
+        if single is None or self.config.d_single <= 0:
+            return pair
+        single = self.single_attention(single, pair, key_mask, extra_pair_bias)
+        single = self.single_transition(single, key_mask)
+        return pair, single
+
+
+class Pairformer(MasterWeights, nn.Module):
+    """A stack of :class:`PairformerBlock` (the trunk), run in order."""
+
+    backends = ("pytorch", "b200")
+    dead = False
+
+    def __init__(self, config: PairformerConfig, n_blocks: int) -> None:
+        super().__init__()
+        self.config = config
+        self.backend = "pytorch"
+        self.blocks = nn.ModuleList(PairformerBlock(config) for _ in range(n_blocks))
+
+    def set_backend(self, name: str) -> None:
+        _check_backend(self, name)
+        for block in self.blocks:
+            block.set_backend(name)
+
+    def forward(self, pair: Tensor, key_mask: Tensor | None = None, single: Tensor | None = None,
+                extra_pair_bias: Tensor | None = None):
+        for block in self.blocks:
+            out = block(pair, key_mask, single, extra_pair_bias)
+            if single is None:
+                pair = out
+            else:
+                pair, single = out
+        return pair if single is None else (pair, single)
