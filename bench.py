@@ -1,0 +1,353 @@
+#!/usr/bin/env python
+"""Benchmark: ms per 48-block Pairformer trunk pass at N = 512, master precision, on B200.
+
+Workload (benchmark configuration 2): 48 AF3 Pairformer blocks (c_z 128, c_s 384), N = 512
+tokens, the last 26 padded, z and s ~ N(0, 1), weights ~ N(0, 0.02) with LayerNorm gamma 1 /
+beta 0, blocks drawn in order from one seed-0 generator; fp32 master weights, bf16
+activations. One step = one trunk pass over one input.
+
+* ``value``: device time of the trunk (CUDA events on the launching stream, graph-replayed,
+  inputs resident in HBM, L2 flushed before every step), max over ranks.
+* ``e2e``: the same pass through the public API from pinned HOST buffers: host->device copy
+  of z and s, the trunk, device->host copy of the updated pair and single, all timed.
+* ``roofline``: the dominant kernel (triangle attention core) timed alone on the same data.
+* ``cpu_baseline``: the CPU oracle (a restatement of the reference's block) on this host's
+  cores, one block at N = 512, times 48.
+
+``--gpus N`` (torchrun, one rank per GPU): every rank runs its own trunk on its own input
+(replicas: the N = 512 trunk fits one GPU); ``value`` is ms per trunk pass of the whole job
+(max rank time / N), ``scaling`` weak.
+
+``--impl reference``: the reference's algorithm (CPU oracle) on this host, same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "ms per 48-block Pairformer trunk at N=512 bf16; N=2048 at 1/2/4/8 B200"
+N_TOKENS = 512
+N_BLOCKS = 48
+MASKED = 26
+#: DRAM traffic of one triangle-attention core launch at N = 512, from the ncu capture
+#: summarised in profiles/triattn_attn_n512.md (dram__bytes_read.sum + dram__bytes_write.sum).
+ATTN_TRAFFIC_BYTES: float | None = None
+
+
+def parse() -> argparse.Namespace:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--n", type=int, default=N_TOKENS)
+    ap.add_argument("--blocks", type=int, default=N_BLOCKS)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        return {"hbm": d["hbm_gbs"], "bf16": d["bf16_tflops"], "bf16_sustained": d["bf16_tflops_sustained"],
+                "source": "measured"}
+    return {"hbm": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+def block_flops(n: int) -> float:
+    return 1536.0 * n**3 + 1_121_792.0 * n**2 + 5.0e6 * n
+
+
+# ------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """``nvidia-smi`` samples every 200 ms while active (SM clock, reasons)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.lines: list[str] = []
+        self.proc = None
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        threading.Thread(target=self._read, daemon=True).start()
+
+    def _read(self) -> None:
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------ distributed
+def dist_setup(gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+        return rank, world, local, dist
+    if gpus != 1:
+        print(f"--gpus {gpus} needs torchrun (one process per GPU)", file=sys.stderr)
+    return 0, 1, local, None
+
+
+def max_over_ranks(value: float, dist) -> float:
+    if dist is None:
+        return value
+    t = torch.tensor([value], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------------------ CPU baseline
+def cpu_block_ms(n: int, warm: bool = False) -> tuple[float, int]:
+    """One block of the oracle (fp32, all host cores) at ``n`` tokens; returns (ms, threads)."""
+    import oracle
+    from foldforge_b200.synthetic import block_state, inputs
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    state = block_state(torch.Generator().manual_seed(0), scheme="baseline")
+    z, s, tokens = inputs(n, 0, masked_suffix=round(MASKED * n / N_TOKENS))
+    if warm:
+        oracle.pairformer_block(z[:64, :64].contiguous(), s[:64], tokens[:64], state)
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        oracle.pairformer_block(z, s, tokens, state)
+    return (time.perf_counter() - t0) * 1e3, threads
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    times = []
+    threads = os.cpu_count() or 1
+    for i in range(min(args.warmup, 1) + args.steps):
+        ms, threads = cpu_block_ms(args.n, warm=(i == 0))
+        if i >= min(args.warmup, 1):
+            times.append(ms)
+    value = statistics.median(times) * args.blocks
+    sample = f"one block of {args.blocks} at N={args.n} per step (fp32 CPU oracle), median of {len(times)}, x{args.blocks}"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "ms", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(value, 3), "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.blocks}-block Pairformer trunk, N={args.n}, last {MASKED} tokens masked",
+                   "model": "AF3 Pairformer block (c_z 128, c_s 384)", "global_batch": 1, "seq_len": args.n,
+                   "parallelism": "cpu"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "ms", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------ the b200 arm
+def run_b200(args, rank: int, world: int, local: int, dist) -> None:
+    import foldforge_b200
+    from foldforge_b200 import _lib, kernels
+    from foldforge_b200.engine.capture import GraphedCall
+    from foldforge_b200.synthetic import inputs, trunk_state
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    n, nb = args.n, args.blocks
+    states = trunk_state(nb, seed=0, scheme="baseline")
+    trunk = foldforge_b200.load(states, backend="b200", unsupported="error", dtype=torch.bfloat16, device=dev)
+    z, s, tokens = inputs(n, seed=rank, masked_suffix=round(MASKED * n / N_TOKENS))
+    mask = (tokens > 0)[None].to(dev)
+
+    def step(zz: torch.Tensor, ss: torch.Tensor):
+        return trunk(zz, mask, ss)
+
+    z_dev = z.bfloat16()[None].to(dev)
+    s_dev = s.bfloat16()[None].to(dev)
+    _lib.launch_count = 0
+    graphed = GraphedCall(step, [z_dev, s_dev], warmup=1)
+    # launches recorded during the warm-up call and the capture: two passes
+    launches = _lib.launch_count // 2
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    for _ in range(max(args.warmup, 3)):
+        flush.fill_(1.0)
+        graphed.replay()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    for start, end in events:
+        flush.fill_(1.0)  # 256 MB write: L2 (126 MB) holds nothing of the previous step
+        start.record()
+        graphed.replay()
+        end.record()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    clocks = sampler.stop()
+    times = [a.elapsed_time(b) for a, b in events]
+    local_ms = sum(times) / len(times)
+    trunk_ms = max_over_ranks(local_ms, dist)
+    value = trunk_ms / world
+    err = _lib.device_error()
+    if err:
+        raise RuntimeError(f"device error word {err} after the timed region")
+
+    # ---------------------------------------------------------------- dominant kernel alone
+    block0 = trunk.blocks[0]
+    zz = graphed.static_inputs[0]
+    ta = block0.tri_atten_starting
+    packed = ta._packed[1]
+    ws = torch.empty(int(_lib.load().ffb_triattn_workspace_bytes(1, n)), dtype=torch.uint8, device=dev)
+    out = torch.empty_like(zz)
+    kernels.triattn(zz, mask, packed, starting=True, stages=1, workspace=ws, out=out)
+    reps = 20
+    for _ in range(3):
+        kernels.triattn(zz, mask, packed, starting=True, stages=2, workspace=ws, out=out)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(reps):
+        kernels.triattn(zz, mask, packed, starting=True, stages=2, workspace=ws, out=out)
+    b.record()
+    torch.cuda.synchronize()
+    attn_ms = a.elapsed_time(b) / reps
+    attn_flops = 4.0 * n**3 * 128  # Q K^T + P V, multiply-add = 2
+    pk = peaks()
+    achieved = attn_flops / (attn_ms * 1e-3) / 1e12
+
+    # ---------------------------------------------------------------- end to end from host buffers
+    e2e = None
+    if not args.no_e2e:
+        z_host = z.bfloat16()[None].pin_memory()
+        s_host = s.bfloat16()[None].pin_memory()
+        pair_host = torch.empty_like(z_host).pin_memory()
+        single_host = torch.empty_like(s_host).pin_memory()
+        stream = torch.cuda.current_stream()
+        e_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                    for _ in range(args.steps)]
+        for start, end in e_events:
+            flush.fill_(1.0)
+            start.record(stream)
+            pair_out, single_out = graphed(z_host, s_host)  # host -> static device inputs, then replay
+            pair_host.copy_(pair_out, non_blocking=True)
+            single_host.copy_(single_out, non_blocking=True)
+            end.record(stream)
+        torch.cuda.synchronize()
+        e_ms = max_over_ranks(sum(x.elapsed_time(y) for x, y in e_events) / len(e_events), dist)
+        e2e = {"value": round(e_ms / world, 3), "unit": "ms",
+               "h2d_bytes_per_step": z_host.numel() * 2 + s_host.numel() * 2,
+               "d2h_bytes_per_step": pair_host.numel() * 2 + single_host.numel() * 2}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        ms, threads = cpu_block_ms(n, warm=True)
+        cpu = {"value": round(ms * nb, 1), "unit": "ms", "cores": threads, "kind": "port",
+               "sample": f"one block at N={n} (fp32 CPU oracle, all host threads), x{nb} blocks"}
+
+    if rank == 0:
+        trunk_flops = block_flops(n) * nb
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "ms", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(trunk_ms, 3), "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {
+                "workload": f"{nb}-block Pairformer trunk, N={n}, last {round(MASKED * n / N_TOKENS)} tokens masked, "
+                            "master precision (fp32 weights, bf16 activations), CUDA-graph replay",
+                "model": "AF3 Pairformer block (c_z 128, c_s 384, 4x32 / 16x24 heads)",
+                "global_batch": world, "seq_len": n, "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                "l2": "flushed by a 256 MB write before every timed step",
+                "trunk_tflops": round(trunk_flops / (trunk_ms * 1e-3) / 1e12, 1),
+                "ms_per_block": round(trunk_ms / nb, 4),
+            },
+            "roofline": {
+                "kernel": "triattn_attn_kernel (starting node, N=512)",
+                "bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16"], "unit": "TFLOP/s",
+                "frac": round(achieved / pk["bf16"], 4), "traffic": ATTN_TRAFFIC_BYTES,
+                "launch_ms": round(attn_ms, 4), "peak_source": f"{pk['source']} (burst: kernel timed alone)",
+                "algorithmic": f"4 * N^3 * 128 = {attn_flops:.3e} flop per launch",
+            },
+            "clocks": clocks,
+            "gpu_launches": launches * args.steps,
+        }
+        if e2e is not None:
+            line["e2e"] = e2e
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    args = parse()
+    rank, world, local, dist = dist_setup(args.gpus)
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_b200(args, rank, world, local, dist)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

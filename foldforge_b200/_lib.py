@@ -33,6 +33,10 @@ SIGNATURES: dict[str, list] = {
     "ffb_trimul_prepare": [c_void_p] * 12,
     "ffb_trimul_fwd": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_size_t, c_int, c_int, c_int,
                        c_int, c_void_p],
+    "ffb_trimul_fwd_stages": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_size_t, c_int, c_int,
+                              c_int, c_int, c_int, c_void_p],
+    "ffb_triattn_fwd_stages": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_size_t, c_int, c_int,
+                               c_int, c_int, c_int, c_void_p],
     "ffb_triattn_packed_bytes": [],
     "ffb_triattn_workspace_bytes": [c_int, c_int],
     "ffb_triattn_prepare": [c_void_p] * 10,
@@ -104,10 +108,29 @@ def load() -> ctypes.CDLL:
     return lib
 
 
+#: kernels each forward entry point launches (the bench's count of this library's launches)
+LAUNCHES = {
+    "ffb_layernorm_fwd": 1, "ffb_gemm_bf16_nt": 1, "ffb_trimul_fwd": 3, "ffb_triattn_fwd": 3,
+    "ffb_transition_fwd": 1, "ffb_apb_fwd": 6, "ffb_single_transition_fwd": 3,
+}
+launch_count = 0
+
+
+def _stage_launches(args) -> int:
+    stages = args[10]
+    return bin(int(stages)).count("1")
+
+
 def call(name: str, *args) -> None:
     """Call an entry point; raise on a non-OK status."""
+    global launch_count
     lib = load()
     status = getattr(lib, name)(*args)
+    if status == 0:
+        if name in ("ffb_trimul_fwd_stages", "ffb_triattn_fwd_stages"):
+            launch_count += _stage_launches(args)
+        else:
+            launch_count += LAUNCHES.get(name, 0)
     if status != 0:
         msg = lib.ffb_last_error().decode(errors="replace")
         cls = UnsupportedCall if status == 2 else KernelError

@@ -206,6 +206,12 @@ int ffb_trimul_prepare(const float* ln_w, const float* ln_b, const float* ln_out
 
 int ffb_trimul_fwd(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace,
                    size_t workspace_bytes, int B, int N, int outgoing, int masked, void* stream) {
+  return ffb_trimul_fwd_stages(z, mask, packed, out, workspace, workspace_bytes, B, N, outgoing, masked, 7, stream);
+}
+
+int ffb_trimul_fwd_stages(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace,
+                          size_t workspace_bytes, int B, int N, int outgoing, int masked, int stages, void* stream) {
+  if (stages <= 0 || stages > 7) return fail(FFB_ERR_ARG, "trimul_fwd: stages=%d", stages);
   if (B <= 0 || N <= 0) return fail(FFB_ERR_ARG, "trimul_fwd: empty problem B=%d N=%d", B, N);
   if (!z || !mask || !packed || !out || !workspace) return fail(FFB_ERR_ARG, "trimul_fwd: null pointer");
   if (z == out) return fail(FFB_ERR_ARG, "trimul_fwd: out must not alias z");
@@ -219,7 +225,7 @@ int ffb_trimul_fwd(const void* z, const uint8_t* mask, const void* packed, void*
   DeviceInfo info;
   int st = device_info(&info);
   if (st != FFB_OK) return st;
-  return trimul_forward(z, mask, packed, out, workspace, B, N, outgoing != 0, masked == FFB_MASKED_ZERO, info,
+  return trimul_forward(z, mask, packed, out, workspace, B, N, outgoing != 0, masked == FFB_MASKED_ZERO, stages, info,
                         static_cast<cudaStream_t>(stream));
 }
 
@@ -242,6 +248,12 @@ int ffb_triattn_prepare(const float* ln_w, const float* ln_b, const float* to_bi
 
 int ffb_triattn_fwd(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace,
                     size_t workspace_bytes, int B, int N, int starting, int masked, void* stream) {
+  return ffb_triattn_fwd_stages(z, mask, packed, out, workspace, workspace_bytes, B, N, starting, masked, 7, stream);
+}
+
+int ffb_triattn_fwd_stages(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace,
+                           size_t workspace_bytes, int B, int N, int starting, int masked, int stages, void* stream) {
+  if (stages <= 0 || stages > 7) return fail(FFB_ERR_ARG, "triattn_fwd: stages=%d", stages);
   if (B <= 0 || N <= 0) return fail(FFB_ERR_ARG, "triattn_fwd: empty problem B=%d N=%d", B, N);
   if (!z || !mask || !packed || !out || !workspace) return fail(FFB_ERR_ARG, "triattn_fwd: null pointer");
   if (z == out) return fail(FFB_ERR_ARG, "triattn_fwd: out must not alias z");
@@ -255,8 +267,8 @@ int ffb_triattn_fwd(const void* z, const uint8_t* mask, const void* packed, void
   DeviceInfo info;
   int st = device_info(&info);
   if (st != FFB_OK) return st;
-  return triattn_forward(z, mask, packed, out, workspace, B, N, starting != 0, masked == FFB_MASKED_ZERO, info,
-                         static_cast<cudaStream_t>(stream));
+  return triattn_forward(z, mask, packed, out, workspace, B, N, starting != 0, masked == FFB_MASKED_ZERO, stages,
+                         info, static_cast<cudaStream_t>(stream));
 }
 
 size_t ffb_transition_packed_bytes(void) { return transition_packed_bytes(); }

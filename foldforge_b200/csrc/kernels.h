@@ -52,7 +52,7 @@ size_t trimul_packed_bytes();
 size_t trimul_workspace_bytes(int B, int N);
 int trimul_prepare(const TriMulWeights& w, void* packed, cudaStream_t stream);
 int trimul_forward(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace, int B, int N,
-                   int outgoing, int masked_zero, const DeviceInfo& info, cudaStream_t stream);
+                   int outgoing, int masked_zero, int stages, const DeviceInfo& info, cudaStream_t stream);
 
 // ---- triangle attention (c_z = 128, 4 heads x 32)
 struct TriAttnWeights {
@@ -62,7 +62,7 @@ size_t triattn_packed_bytes();
 size_t triattn_workspace_bytes(int B, int N);
 int triattn_prepare(const TriAttnWeights& w, void* packed, cudaStream_t stream);
 int triattn_forward(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace, int B, int N,
-                    int starting, int masked_zero, const DeviceInfo& info, cudaStream_t stream);
+                    int starting, int masked_zero, int stages, const DeviceInfo& info, cudaStream_t stream);
 
 // ---- pair transition (c_z = 128, n = 4)
 struct TransitionWeights {

@@ -49,75 +49,89 @@ int to_bf16(const float* a, const float* b, int rows_each, int cols, int interle
 }
 
 // ---------------------------------------------------------------- attention kernel
-// One warp per (batch, head, query). Lanes stride over the keys keeping a private online
-// softmax (max, sum, 24 partial outputs), merged across the warp at the end. Masked keys
-// get the reference's REPLACED logit -1e9 (so a row with every key masked averages
-// uniformly); keys past N do not exist.
-__global__ void __launch_bounds__(256) single_attention_kernel(const __nv_bfloat16* __restrict__ qkvg,
-                                                                const float* __restrict__ pair_bias,
-                                                                const void* __restrict__ extra, int extra_f32,
-                                                                const uint8_t* __restrict__ mask, float gate_bias,
-                                                                __nv_bfloat16* __restrict__ out, int B, int N) {
-  const int lane = threadIdx.x & 31;
-  const int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
-  if (w >= static_cast<int64_t>(B) * kHs * N) return;
-  const int i = static_cast<int>(w % N);
-  const int h = static_cast<int>((w / N) % kHs);
-  const int b = static_cast<int>(w / (static_cast<int64_t>(N) * kHs));
-  const __nv_bfloat16* row_i = qkvg + (static_cast<int64_t>(b) * N + i) * (4 * kCs);
-  float q[kDs];
+// One thread per query, a CTA per (batch, head, 64 queries). The head's keys and values are
+// staged through shared memory in chunks of kKeyChunk (fp32, read as broadcasts), so every
+// key row is fetched once per CTA instead of once per query. Each thread runs an exact
+// online softmax over its row (the running max is raised only when a logit exceeds it).
+// Masked keys get the reference's REPLACED logit -1e9, so a row whose keys are all
+// masked averages uniformly; keys past N do not exist.
+constexpr int kQueriesPerCta = 64;
+constexpr int kKeyChunk = 128;
+
+__global__ void __launch_bounds__(kQueriesPerCta) single_attention_kernel(
+    const __nv_bfloat16* __restrict__ qkvg, const float* __restrict__ pair_bias, const void* __restrict__ extra,
+    int extra_f32, const uint8_t* __restrict__ mask, float gate_bias, __nv_bfloat16* __restrict__ out, int B, int N) {
+  __shared__ float4 ks[kKeyChunk][kDs / 4];
+  __shared__ float4 vs[kKeyChunk][kDs / 4];
+  __shared__ float keep[kKeyChunk];
+  const int qblocks = (N + kQueriesPerCta - 1) / kQueriesPerCta;
+  const int h = blockIdx.x % kHs;
+  const int qb = (blockIdx.x / kHs) % qblocks;
+  const int b = blockIdx.x / (kHs * qblocks);
+  const int i = qb * kQueriesPerCta + threadIdx.x;
+  const bool active = i < N;
+  const int row = active ? i : N - 1;
+  const __nv_bfloat16* row_i = qkvg + (static_cast<int64_t>(b) * N + row) * (4 * kCs);
   const float scale = rsqrtf(static_cast<float>(kDs));
+  float q[kDs];
 #pragma unroll
   for (int d = 0; d < kDs; ++d) q[d] = __bfloat162float(row_i[h * kDs + d]) * scale;
-  float m = -__int_as_float(0x7f800000), l = 0.f;
+  float m = -1.0e30f, l = 0.f;
   float o[kDs];
 #pragma unroll
   for (int d = 0; d < kDs; ++d) o[d] = 0.f;
-  const float* pb_row = pair_bias + ((static_cast<int64_t>(b) * N + i) * N) * kHs + h;
-  for (int j = lane; j < N; j += 32) {
-    const __nv_bfloat16* row_j = qkvg + (static_cast<int64_t>(b) * N + j) * (4 * kCs);
-    float x = 0.f;
-#pragma unroll
-    for (int d = 0; d < kDs; ++d) x += q[d] * __bfloat162float(row_j[kCs + h * kDs + d]);
-    x += pb_row[static_cast<int64_t>(j) * kHs];
-    if (extra != nullptr) {
-      const int64_t e = ((static_cast<int64_t>(b) * kHs + h) * N + i) * N + j;
-      x += extra_f32 ? static_cast<const float*>(extra)[e]
-                     : __bfloat162float(static_cast<const __nv_bfloat16*>(extra)[e]);
+  const float* pb_row = pair_bias + ((static_cast<int64_t>(b) * N + row) * N) * kHs + h;
+  for (int j0 = 0; j0 < N; j0 += kKeyChunk) {
+    const int nk = N - j0 < kKeyChunk ? N - j0 : kKeyChunk;
+    __syncthreads();
+    for (int e = threadIdx.x; e < nk * kDs; e += kQueriesPerCta) {
+      const int j = e / kDs, d = e % kDs;
+      const __nv_bfloat16* rj = qkvg + (static_cast<int64_t>(b) * N + j0 + j) * (4 * kCs) + h * kDs + d;
+      reinterpret_cast<float*>(ks[j])[d] = __bfloat162float(rj[kCs]);
+      reinterpret_cast<float*>(vs[j])[d] = __bfloat162float(rj[2 * kCs]);
     }
-    if (!mask[static_cast<int64_t>(b) * N + j]) x = -1.0e9f;
-    const float m_new = fmaxf(m, x);
-    const float alpha = __expf(m - m_new);
-    const float p = __expf(x - m_new);
-    l = l * alpha + p;
+    for (int j = threadIdx.x; j < nk; j += kQueriesPerCta) keep[j] = mask[static_cast<int64_t>(b) * N + j0 + j] ? 1.f : 0.f;
+    __syncthreads();
+    for (int j = 0; j < nk; ++j) {
+      float x = 0.f;
 #pragma unroll
-    for (int d = 0; d < kDs; ++d) o[d] = o[d] * alpha + p * __bfloat162float(row_j[2 * kCs + h * kDs + d]);
-    m = m_new;
-  }
-  // merge the 32 lane-private softmax states
+      for (int d4 = 0; d4 < kDs / 4; ++d4) {
+        const float4 k4 = ks[j][d4];
+        x += q[4 * d4] * k4.x + q[4 * d4 + 1] * k4.y + q[4 * d4 + 2] * k4.z + q[4 * d4 + 3] * k4.w;
+      }
+      x += pb_row[static_cast<int64_t>(j0 + j) * kHs];
+      if (extra != nullptr) {
+        const int64_t e = ((static_cast<int64_t>(b) * kHs + h) * N + row) * N + j0 + j;
+        x += extra_f32 ? static_cast<const float*>(extra)[e]
+                       : __bfloat162float(static_cast<const __nv_bfloat16*>(extra)[e]);
+      }
+      if (keep[j] == 0.f) x = -1.0e9f;
+      if (x > m) {
+        const float alpha = __expf(m - x);
+        l *= alpha;
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) {
-    const float m2 = __shfl_xor_sync(0xFFFFFFFFu, m, off);
-    const float l2 = __shfl_xor_sync(0xFFFFFFFFu, l, off);
-    const float mn = fmaxf(m, m2);
-    const float a1 = (l > 0.f) ? __expf(m - mn) : 0.f;
-    const float a2 = (l2 > 0.f) ? __expf(m2 - mn) : 0.f;
+        for (int d = 0; d < kDs; ++d) o[d] *= alpha;
+        m = x;
+      }
+      const float p = __expf(x - m);
+      l += p;
 #pragma unroll
-    for (int d = 0; d < kDs; ++d) {
-      const float o2 = __shfl_xor_sync(0xFFFFFFFFu, o[d], off);
-      o[d] = o[d] * a1 + o2 * a2;
+      for (int d4 = 0; d4 < kDs / 4; ++d4) {
+        const float4 v4 = vs[j][d4];
+        o[4 * d4] += p * v4.x;
+        o[4 * d4 + 1] += p * v4.y;
+        o[4 * d4 + 2] += p * v4.z;
+        o[4 * d4 + 3] += p * v4.w;
+      }
     }
-    l = l * a1 + l2 * a2;
-    m = mn;
   }
-  if (lane < kDs) {
-    float v = 0.f;
+  if (!active) return;
+  const float inv = 1.0f / l;
+  __nv_bfloat16* dst = out + (static_cast<int64_t>(b) * N + i) * kCs + h * kDs;
 #pragma unroll
-    for (int d = 0; d < kDs; ++d)
-      if (d == lane) v = o[d];
-    v /= l;
-    const float g = __bfloat162float(row_i[3 * kCs + h * kDs + lane]) + gate_bias;
-    out[(static_cast<int64_t>(b) * N + i) * kCs + h * kDs + lane] = __float2bfloat16_rn(v * sigmoidf_(g));
+  for (int d = 0; d < kDs; ++d) {
+    const float g = __bfloat162float(row_i[3 * kCs + h * kDs + d]) + gate_bias;
+    dst[d] = __float2bfloat16_rn(o[d] * inv * sigmoidf_(g));
   }
 }
 
@@ -238,8 +252,8 @@ int apb_forward(const void* s, const void* z, const uint8_t* mask, const void* p
   st = gemm(y, img + L.w_qkvg, qkvg, static_cast<int>(T), 4 * kCs, kCs, 0,
             reinterpret_cast<const float*>(img + L.b_qkvg), kEpiStore, nullptr, nullptr, info, stream);
   if (st) return st;
-  const int64_t warps = static_cast<int64_t>(B) * kHs * N;
-  single_attention_kernel<<<static_cast<int>((warps + 7) / 8), 256, 0, stream>>>(
+  const int ctas = B * kHs * ((N + kQueriesPerCta - 1) / kQueriesPerCta);
+  single_attention_kernel<<<ctas, kQueriesPerCta, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(qkvg), pb, extra, extra_f32, mask, gate_bias,
       static_cast<__nv_bfloat16*>(gated), B, N);
   st = cuda_status(static_cast<int>(cudaGetLastError()), "single attention launch");

@@ -849,14 +849,14 @@ int triattn_prepare(const TriAttnWeights& w, void* packed, cudaStream_t stream) 
 }
 
 int triattn_forward(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace, int B, int N,
-                    int starting, int masked_zero, const DeviceInfo& info, cudaStream_t stream) {
+                    int starting, int masked_zero, int stages, const DeviceInfo& info, cudaStream_t stream) {
   const int np = (N + 7) / 8 * 8;
   Workspace ws = carve(workspace, B, N);
   int st;
   const uint64_t zdims[3] = {kC, static_cast<uint64_t>(N), static_cast<uint64_t>(B) * N};
   const uint64_t zstrides[2] = {kC * 2, static_cast<uint64_t>(N) * kC * 2};
   // 1. projection
-  {
+  if (stages & 1) {
     CUtensorMap map_z;
     const uint32_t box_row[3] = {64, kTile, 1};
     const uint32_t box_col[3] = {64, 1, kTile};
@@ -874,7 +874,7 @@ int triattn_forward(const void* z, const uint8_t* mask, const void* packed, void
     if (st) return st;
   }
   // 2. attention
-  {
+  if (stages & 2) {
     CUtensorMap map_q, map_k, map_vt, map_bias;
     const uint64_t qdims[3] = {kD, static_cast<uint64_t>(N), static_cast<uint64_t>(B) * N * kHeads};
     const uint64_t qstrides[2] = {kD * 2, static_cast<uint64_t>(N) * kD * 2};
@@ -921,7 +921,7 @@ int triattn_forward(const void* z, const uint8_t* mask, const void* packed, void
     if (st) return st;
   }
   // 3. output
-  {
+  if (stages & 4) {
     CUtensorMap map_z, map_o, map_out;
     const uint32_t box[3] = {64, kTile, 1};
     st = make_map(&map_z, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, z, zdims, zstrides, box, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -939,6 +939,7 @@ int triattn_forward(const void* z, const uint8_t* mask, const void* packed, void
     triattn_out_kernel<<<grid, 256, smem, stream>>>(map_z, map_o, map_out, op);
     return cuda_status(static_cast<int>(cudaGetLastError()), "triattn_out launch");
   }
+  return 0;
 }
 
 }  // namespace ffb

@@ -82,13 +82,31 @@ __device__ __forceinline__ void load_z_stats(const uint8_t* tile, int row, float
 }
 
 // ====================================================================== kernel 1
+// Warp-specialised, persistent, 64-pair tiles. The projection is computed TRANSPOSED,
+// D[channel][pair] = W'[channel][:] . z[pair][:], so a TMEM lane is an output channel and
+// its columns are consecutive pairs: each epilogue thread owns one channel of L (or R) and
+// writes 32 consecutive pairs of the channel-major layout as four 16-byte stores.
+//   warp 0      TMA: z tiles into a 4-stage ring
+//   warp 1      MMA: 4 x (M 128 channels, N 64 pairs, K 128) per tile -> 256 TMEM columns,
+//               double-buffered (512 columns)
+//   warps 2-3   LayerNorm statistics and pair mask of the tile's 64 pairs -> shared memory
+//   warps 4-11  epilogue: warps 4-7 produce L, warps 8-11 produce R
+constexpr int kPTile = 64;
+constexpr int kPStages = 4;
+constexpr int kPThreads = 384;
+
 struct ProjSmem {
   alignas(1024) uint8_t w[kProjBytes];
-  alignas(1024) uint8_t z[kGroups][kTile * kC * 2];
-  Vecs vec;
+  alignas(1024) uint8_t z[kPStages][kPTile * kC * 2];
+  float wsum[512];
+  float bias[512];
+  float mean[2][kPTile];
+  float rstd[2][kPTile];
+  float pm[2][kPTile];
   uint64_t wbar;
-  uint64_t full[kGroups];
-  uint64_t mma[kGroups];
+  uint64_t z_full[kPStages], z_empty[kPStages];
+  uint64_t acc_full[2], acc_free[2];
+  uint64_t st_full[2], st_free[2];
   uint32_t tmem_base;
 };
 
@@ -102,24 +120,35 @@ struct ProjParams {
   int* err;
 };
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kPThreads, 1)
     trimul_proj_kernel(const __grid_constant__ CUtensorMap map_z, ProjParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   ProjSmem& s = *reinterpret_cast<ProjSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int g = threadIdx.x / 128;
-  const int gt = threadIdx.x % 128;  // thread in group == tile row == TMEM lane
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int tiles_per_row = (p.N + kTile - 1) / kTile;
+  const int tiles_per_row = (p.N + kPTile - 1) / kPTile;
   const int total = p.B * p.N * tiles_per_row;
 
   if (threadIdx.x == 0) {
     mbar_init(&s.wbar, 1);
-    for (int i = 0; i < kGroups; ++i) {
-      mbar_init(&s.full[i], 1);
-      mbar_init(&s.mma[i], 1);
+    for (int i = 0; i < kPStages; ++i) {
+      mbar_init(&s.z_full[i], 1);
+      mbar_init(&s.z_empty[i], 1 + 2);  // MMA commit + the two statistics warps
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.acc_full[i], 1);
+      mbar_init(&s.acc_free[i], 8);
+      mbar_init(&s.st_full[i], 2);
+      mbar_init(&s.st_free[i], 8);
     }
     fence_mbar_init();
+  }
+  {
+    const float* v = reinterpret_cast<const float*>(p.packed + kProjBytes + kGateBytes + kOutBytes);
+    for (int i = threadIdx.x; i < 512; i += kPThreads) {
+      s.wsum[i] = v[i];
+      s.bias[i] = v[512 + i];
+    }
   }
   if (warp == 0) {
     tmem_alloc(&s.tmem_base, 512);
@@ -128,97 +157,169 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (threadIdx.x == 0) {
-    tma_prefetch_map(&map_z);
-    mbar_arrive_expect_tx(&s.wbar, kProjBytes);
-    for (int off = 0; off < static_cast<int>(kProjBytes); off += 32768)
-      bulk_load(s.w + off, p.packed + off, 32768, &s.wbar);
-  }
-  {
-    const float* vsrc = reinterpret_cast<const float*>(p.packed + kProjBytes + kGateBytes + kOutBytes);
-    float* vdst = s.vec.wsum_proj;
-    for (int i = threadIdx.x; i < 1024; i += kThreads) vdst[i] = vsrc[i];
-  }
-  __syncthreads();
-  bool ok = mbar_wait(&s.wbar, 0, p.err, kErrTimeoutLoad);
-  const uint32_t tmem = s.tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16) + g * 256;
-  const uint32_t tmem_mma = s.tmem_base + g * 256;
-  const uint32_t idesc = idesc_bf16_f32(128, 256);
-  uint8_t* zt = s.z[g];
-  int it = 0;
-  bool load_pending = false;
-  for (int tile = blockIdx.x * kGroups + g; tile < total; tile += gridDim.x * kGroups, ++it) {
-    const int c0 = (tile % tiles_per_row) * kTile;
-    const int rr = tile / tiles_per_row;  // b * N + r
-    const int b = rr / p.N;
-    const int r = rr - b * p.N;
-    if (gt == 0 && ok) {
-      mbar_arrive_expect_tx(&s.full[g], kTile * kC * 2);
-      for (int kb = 0; kb < 2; ++kb) {
-        if (p.outgoing)
-          tma_load_3d(zt + kb * 16384, &map_z, &s.full[g], kb * 64, c0, rr);        // z[b, r, c0 + t]
-        else
-          tma_load_3d(zt + kb * 16384, &map_z, &s.full[g], kb * 64, r, b * p.N + c0);  // z[b, c0 + t, r]
+  const uint32_t tmem0 = s.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_map(&map_z);
+      mbar_arrive_expect_tx(&s.wbar, kProjBytes);
+      for (int off = 0; off < static_cast<int>(kProjBytes); off += 32768)
+        bulk_load(s.w + off, p.packed + off, 32768, &s.wbar);
+      int it = 0;
+      for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
+        const int st = it % kPStages;
+        if (!mbar_wait(&s.z_empty[st], ((it / kPStages) & 1) ^ 1, p.err, kErrTimeoutEmpty)) break;
+        const int c0 = (tile % tiles_per_row) * kPTile;
+        const int rr = tile / tiles_per_row;
+        const int b = rr / p.N, r = rr - b * p.N;
+        mbar_arrive_expect_tx(&s.z_full[st], kPTile * kC * 2);
+        for (int kb = 0; kb < 2; ++kb) {
+          uint8_t* dst = s.z[st] + kb * (kPTile * 128);
+          if (p.outgoing)
+            tma_load_3d(dst, &map_z, &s.z_full[st], kb * 64, c0, rr);          // z[b, r, c0 + t]
+          else
+            tma_load_3d(dst, &map_z, &s.z_full[st], kb * 64, r, b * p.N + c0);  // z[b, c0 + t, r]
+        }
       }
-      load_pending = true;
+      mbar_wait(&s.wbar, 0, p.err, kErrTimeoutLoad);
     }
-    ok = ok && mbar_wait(&s.full[g], it & 1, p.err, kErrTimeoutLoad);
-    if (gt == 0 && ok) load_pending = false;
-    float mean = 0.f, rstd = 0.f;
-    if (ok) load_z_stats(zt, gt, mean, rstd);
-    const int k = c0 + gt;  // this row's position along the contraction axis
-    const bool valid = k < p.N;
-    const float pm = (valid && p.mask[b * p.N + r] && p.mask[b * p.N + k]) ? 1.0f : 0.0f;
-    for (int half = 0; half < 2; ++half) {
-      if (gt == 0 && ok) {
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(128, kPTile);
+      bool ok = mbar_wait(&s.wbar, 0, p.err, kErrTimeoutLoad);
+      int it = 0;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
+        const int st = it % kPStages, buf = it & 1;
+        if (!mbar_wait(&s.z_full[st], (it / kPStages) & 1, p.err, kErrTimeoutLoad)) break;
+        if (!mbar_wait(&s.acc_free[buf], ((it >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty)) break;
         tc_fence_after();
-        const uint32_t a0 = smem_u32(zt);
-        const uint32_t b0 = smem_u32(s.w) + half * 256 * 128;
+        const uint32_t wa = smem_u32(s.w), za = smem_u32(s.z[st]);
 #pragma unroll
-        for (int kb = 0; kb < 2; ++kb)
+        for (int m = 0; m < 4; ++m)
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_bf16(tmem_mma, desc_kmajor_sw128(a0 + kb * 16384) + 2 * kk,
-                     desc_kmajor_sw128(b0 + kb * 65536) + 2 * kk, idesc, (kb | kk) != 0);
-        mma_commit(&s.mma[g]);
+          for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_bf16(tmem0 + buf * 256 + m * kPTile, desc_kmajor_sw128(wa + kb * 65536 + m * 16384) + 2 * kk,
+                       desc_kmajor_sw128(za + kb * (kPTile * 128)) + 2 * kk, idesc, (kb | kk) != 0);
+        mma_commit(&s.acc_full[buf]);
+        mma_commit(&s.z_empty[st]);
       }
-      bool got = ok && mbar_wait(&s.mma[g], half, p.err, kErrTimeoutMma);
-      got = __all_sync(0xFFFFFFFFu, got);
-      tc_fence_after();
-      __nv_bfloat16* out = half == 0 ? p.left : p.right;
-      if (got) {
-        const float* wsum = s.vec.wsum_proj + half * 256;
-        const float* bias = s.vec.bias_proj + half * 256;
-#pragma unroll 1
-        for (int cc = 0; cc < kH; cc += 32) {
-          uint32_t vp[32], vg[32];
-          tmem_ld32(tmem + cc, vp);
-          tmem_ld32(tmem + 128 + cc, vg);
-          tmem_ld_wait();
-          if (valid) {
-            __nv_bfloat16* dst = out + ((static_cast<int64_t>(b) * kH + cc) * p.N + r) * p.Np + k;
-            const int64_t cstride = static_cast<int64_t>(p.N) * p.Np;
+    }
+  } else if (warp < 4) {
+    // statistics: thread t = pair t of the tile
+    const int t = (warp - 2) * 32 + lane;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
+      const int st = it % kPStages, buf = it & 1;
+      bool w1 = mbar_wait(&s.z_full[st], (it / kPStages) & 1, p.err, kErrTimeoutLoad);
+      bool w2 = mbar_wait(&s.st_free[buf], ((it >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty);
+      if (!__all_sync(0xFFFFFFFFu, w1 && w2)) break;
+      const uint8_t* zt = s.z[st];
+      float sum = 0.f;
+      uint4 v[16];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const float yp = rstd * (__uint_as_float(vp[i]) - mean * wsum[cc + i]) + bias[cc + i];
-              const float yg = rstd * (__uint_as_float(vg[i]) - mean * wsum[128 + cc + i]) + bias[128 + cc + i];
-              dst[i * cstride] = __float2bfloat16_rn(yp * pm * sigmoidf_(yg));
-            }
+      for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          v[kb * 8 + q] = *reinterpret_cast<const uint4*>(zt + kb * (kPTile * 128) + sw128_offset(t, q * 8));
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sum += bf16_lo(w[j]) + bf16_hi(w[j]);
+      }
+      const float mean = sum * (1.0f / kC);
+      float q2 = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float a = bf16_lo(w[j]) - mean, bb = bf16_hi(w[j]) - mean;
+          q2 += a * a + bb * bb;
+        }
+      }
+      const int c0 = (tile % tiles_per_row) * kPTile;
+      const int rr = tile / tiles_per_row;
+      const int b = rr / p.N, r = rr - b * p.N;
+      const int k = c0 + t;
+      s.mean[buf][t] = mean;
+      s.rstd[buf][t] = rsqrtf(q2 * (1.0f / kC) + 1e-5f);
+      s.pm[buf][t] = (k < p.N && p.mask[b * p.N + r] && p.mask[b * p.N + k]) ? 1.0f : 0.0f;
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&s.st_full[buf]);
+        mbar_arrive(&s.z_empty[st]);
+      }
+    }
+  } else {
+    // epilogue: warp 4..7 -> L, 8..11 -> R; lane = output channel
+    const int part = (warp - 4) / 4;
+    const int c = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const int rp = part * 256 + c, rg = part * 256 + 128 + c;
+    const float wsp = s.wsum[rp], bsp = s.bias[rp], wsg = s.wsum[rg], bsg = s.bias[rg];
+    __nv_bfloat16* out = part == 0 ? p.left : p.right;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
+      const int buf = it & 1;
+      bool w1 = mbar_wait(&s.acc_full[buf], (it >> 1) & 1, p.err, kErrTimeoutMma);
+      bool w2 = mbar_wait(&s.st_full[buf], (it >> 1) & 1, p.err, kErrTimeoutLoad);
+      if (!__all_sync(0xFFFFFFFFu, w1 && w2)) break;
+      tc_fence_after();
+      const int c0 = (tile % tiles_per_row) * kPTile;
+      const int rr = tile / tiles_per_row;
+      const int b = rr / p.N, r = rr - b * p.N;
+      __nv_bfloat16* row = out + ((static_cast<int64_t>(b) * kH + c) * p.N + r) * p.Np + c0;
+#pragma unroll 1
+      for (int ch = 0; ch < kPTile; ch += 32) {
+        uint32_t vp[32], vg[32];
+        tmem_ld32(tmem0 + lane_off + buf * 256 + (2 * part) * kPTile + ch, vp);
+        tmem_ld32(tmem0 + lane_off + buf * 256 + (2 * part + 1) * kPTile + ch, vg);
+        tmem_ld_wait();
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float o2[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int j = ch + 2 * i + e;
+            const float mu = s.mean[buf][j], rs = s.rstd[buf][j];
+            const float yp = rs * (__uint_as_float(vp[2 * i + e]) - mu * wsp) + bsp;
+            const float yg = rs * (__uint_as_float(vg[2 * i + e]) - mu * wsg) + bsg;
+            o2[e] = yp * sigmoid_fast(yg) * s.pm[buf][j];
+          }
+          packed[i] = pack_bf16(o2[0], o2[1]);
+        }
+        const int k0 = c0 + ch;
+        if (k0 + 32 <= p.N) {
+          uint4* dst = reinterpret_cast<uint4*>(row + ch);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+        } else {
+          for (int i = 0; i < 32 && k0 + i < p.N; ++i) {
+            const uint32_t w = packed[i / 2];
+            const uint16_t h = static_cast<uint16_t>((i & 1) ? (w >> 16) : (w & 0xFFFFu));
+            reinterpret_cast<uint16_t*>(row + ch)[i] = h;
           }
         }
       }
       tc_fence_before();
-      ok = !named_barrier_or(1 + g, 128, !ok || !got);
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&s.acc_free[buf]);
+        mbar_arrive(&s.st_free[buf]);
+      }
     }
-    if (!ok) break;
   }
-  if (gt == 0 && load_pending) mbar_wait(&s.full[g], it & 1, p.err, kErrTimeoutLoad);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(s.tmem_base, 512);
+    tmem_dealloc(tmem0, 512);
   }
 }
 
@@ -457,7 +558,7 @@ int trimul_prepare(const TriMulWeights& w, void* packed, cudaStream_t stream) {
 }
 
 int trimul_forward(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace, int B, int N,
-                   int outgoing, int masked_zero, const DeviceInfo& info, cudaStream_t stream) {
+                   int outgoing, int masked_zero, int stages, const DeviceInfo& info, cudaStream_t stream) {
   const int np = (N + 7) / 8 * 8;
   const size_t one = static_cast<size_t>(B) * kH * N * np * 2;
   const size_t aligned = (one + 255) / 256 * 256;
@@ -468,6 +569,8 @@ int trimul_forward(const void* z, const uint8_t* mask, const void* packed, void*
   const int tiles = B * N * ((N + kTile - 1) / kTile);
   const int grid_groups = (tiles + kGroups - 1) / kGroups;
   const int grid = grid_groups < info.num_sms ? grid_groups : info.num_sms;
+  const int ptiles = B * N * ((N + kPTile - 1) / kPTile);
+  const int pgrid = ptiles < info.num_sms ? ptiles : info.num_sms;
   int st;
 
   // pair tensor maps: dims {c, N (col), B*N (row)}
@@ -475,18 +578,20 @@ int trimul_forward(const void* z, const uint8_t* mask, const void* packed, void*
   {
     const uint64_t dims[3] = {kC, static_cast<uint64_t>(N), static_cast<uint64_t>(B) * N};
     const uint64_t strides[2] = {kC * 2, static_cast<uint64_t>(N) * kC * 2};
-    const uint32_t box_row[3] = {64, kTile, 1};
-    const uint32_t box_col[3] = {64, 1, kTile};
+    const uint32_t box_row[3] = {64, kPTile, 1};
+    const uint32_t box_col[3] = {64, 1, kPTile};
     st = make_map(&map_z, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, z, dims, strides, outgoing ? box_row : box_col,
                   CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
   }
-  ProjParams pp{static_cast<const uint8_t*>(packed), mask, left, right, B, N, np, outgoing, info.err};
-  const size_t proj_smem = sizeof(ProjSmem) + 1024;
-  cudaFuncSetAttribute(trimul_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(proj_smem));
-  trimul_proj_kernel<<<grid, kThreads, proj_smem, stream>>>(map_z, pp);
-  st = cuda_status(static_cast<int>(cudaGetLastError()), "trimul_proj launch");
-  if (st) return st;
+  if (stages & 1) {
+    ProjParams pp{static_cast<const uint8_t*>(packed), mask, left, right, B, N, np, outgoing, info.err};
+    const size_t proj_smem = sizeof(ProjSmem) + 1024;
+    cudaFuncSetAttribute(trimul_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(proj_smem));
+    trimul_proj_kernel<<<pgrid, kPThreads, proj_smem, stream>>>(map_z, pp);
+    st = cuda_status(static_cast<int>(cudaGetLastError()), "trimul_proj launch");
+    if (st) return st;
+  }
 
   // contraction: U[c] = L[c] R[c]^T, batch = B * h
   CUtensorMap map_l, map_r;
@@ -515,8 +620,10 @@ int trimul_forward(const void* z, const uint8_t* mask, const void* packed, void*
     gp.residual = nullptr;
     gp.row_mask = nullptr;
     gp.err = info.err;
-    st = cuda_status(launch_gemm_nt(map_l, map_r, gp, bn, info.num_sms, stream), "trimul contraction launch");
-    if (st) return st;
+    if (stages & 2) {
+      st = cuda_status(launch_gemm_nt(map_l, map_r, gp, bn, info.num_sms, stream), "trimul contraction launch");
+      if (st) return st;
+    }
   }
 
   // output
@@ -535,6 +642,7 @@ int trimul_forward(const void* z, const uint8_t* mask, const void* packed, void*
     st = make_map(&map_u, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, u, udims, ustrides, ubox, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st) return st;
   }
+  if (!(stages & 4)) return 0;
   OutParams op{static_cast<const uint8_t*>(packed), mask, B, N, masked_zero, info.err};
   const size_t out_smem = sizeof(OutSmem) + 1024;
   cudaFuncSetAttribute(trimul_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(out_smem));

@@ -107,11 +107,15 @@ def trimul_prepare(weights: dict[str, Tensor], device: torch.device) -> Tensor:
 
 
 def _mask_u8(mask: Tensor) -> Tensor:
+    if mask.dtype == torch.bool and mask.is_contiguous():
+        return mask.view(torch.uint8)  # same bytes, no cast kernel
     return mask.to(torch.uint8).contiguous()
 
 
-def trimul(z: Tensor, mask: Tensor, packed: Tensor, *, outgoing: bool, masked_zero: bool = True) -> Tensor:
-    """Triangle multiplicative update with residual: ``z [B, N, N, 128]`` bf16, ``mask [B, N]``."""
+def trimul(z: Tensor, mask: Tensor, packed: Tensor, *, outgoing: bool, masked_zero: bool = True,
+           stages: int = 7, workspace: Tensor | None = None, out: Tensor | None = None) -> Tensor:
+    """Triangle multiplicative update with residual: ``z [B, N, N, 128]`` bf16, ``mask [B, N]``.
+    ``stages`` / ``workspace`` / ``out`` select and reuse buffers for a subset of its launches."""
     _need_cuda(z, mask, packed)
     if z.dtype != torch.bfloat16 or z.dim() != 4 or z.shape[-1] != 128:
         raise _lib.UnsupportedCall("trimul", 2, f"needs bf16 [B, N, N, 128], got {z.dtype} {tuple(z.shape)}")
@@ -119,11 +123,11 @@ def trimul(z: Tensor, mask: Tensor, packed: Tensor, *, outgoing: bool, masked_ze
     b, n = z.shape[0], z.shape[1]
     lib = _lib.load()
     ws_bytes = int(lib.ffb_trimul_workspace_bytes(b, n))
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=z.device)
-    out = torch.empty_like(z)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=z.device) if workspace is None else workspace
+    out = torch.empty_like(z) if out is None else out
     m = _mask_u8(mask)
-    _lib.call("ffb_trimul_fwd", _ptr(z), _ptr(m), _ptr(packed), _ptr(out), _ptr(ws), ctypes.c_size_t(ws_bytes), b, n,
-              int(outgoing), int(masked_zero), _stream())
+    _lib.call("ffb_trimul_fwd_stages", _ptr(z), _ptr(m), _ptr(packed), _ptr(out), _ptr(ws), ctypes.c_size_t(ws.numel()),
+              b, n, int(outgoing), int(masked_zero), stages, _stream())
     return out
 
 
@@ -140,7 +144,8 @@ def triattn_prepare(weights: dict[str, Tensor], device: torch.device) -> Tensor:
     return packed
 
 
-def triattn(z: Tensor, mask: Tensor, packed: Tensor, *, starting: bool, masked_zero: bool = True) -> Tensor:
+def triattn(z: Tensor, mask: Tensor, packed: Tensor, *, starting: bool, masked_zero: bool = True,
+            stages: int = 7, workspace: Tensor | None = None, out: Tensor | None = None) -> Tensor:
     """Triangle attention with residual: ``z [B, N, N, 128]`` bf16, ``mask [B, N]``."""
     _need_cuda(z, mask, packed)
     if z.dtype != torch.bfloat16 or z.dim() != 4 or z.shape[-1] != 128:
@@ -149,11 +154,11 @@ def triattn(z: Tensor, mask: Tensor, packed: Tensor, *, starting: bool, masked_z
     b, n = z.shape[0], z.shape[1]
     lib = _lib.load()
     ws_bytes = int(lib.ffb_triattn_workspace_bytes(b, n))
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=z.device)
-    out = torch.empty_like(z)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=z.device) if workspace is None else workspace
+    out = torch.empty_like(z) if out is None else out
     m = _mask_u8(mask)
-    _lib.call("ffb_triattn_fwd", _ptr(z), _ptr(m), _ptr(packed), _ptr(out), _ptr(ws), ctypes.c_size_t(ws_bytes), b, n,
-              int(starting), int(masked_zero), _stream())
+    _lib.call("ffb_triattn_fwd_stages", _ptr(z), _ptr(m), _ptr(packed), _ptr(out), _ptr(ws),
+              ctypes.c_size_t(ws.numel()), b, n, int(starting), int(masked_zero), stages, _stream())
     return out
 
 

@@ -93,6 +93,11 @@ int ffb_trimul_prepare(const float* ln_w, const float* ln_b, const float* ln_out
                        void* stream);
 int ffb_trimul_fwd(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace,
                    size_t workspace_bytes, int B, int N, int outgoing, int masked, void* stream);
+/* The same with a subset of its three launches: `stages` bit 0 = projection (z -> L, R in
+ * the workspace), bit 1 = contraction (L, R -> U), bit 2 = output (U, z -> out); 7 = all.
+ * For profiling one launch, and for callers that move the workspace between stages. */
+int ffb_trimul_fwd_stages(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace,
+                          size_t workspace_bytes, int B, int N, int outgoing, int masked, int stages, void* stream);
 
 /* ---- Triangle attention, starting / ending node (c_z = 128, 4 heads x 32, AF3: no
  * projection biases, untransposed pair bias). Replaces the engine `TriangleAttention`
@@ -108,6 +113,10 @@ int ffb_triattn_prepare(const float* ln_w, const float* ln_b, const float* to_bi
                         void* packed, void* stream);
 int ffb_triattn_fwd(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace,
                     size_t workspace_bytes, int B, int N, int starting, int masked, void* stream);
+/* `stages` bit 0 = projection (z -> Q, K, V^T, bias), bit 1 = attention (-> o), bit 2 =
+ * gated output projection (o, z -> out); 7 = all. */
+int ffb_triattn_fwd_stages(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace,
+                           size_t workspace_bytes, int B, int N, int starting, int masked, int stages, void* stream);
 
 /* ---- Pair transition (c_z = 128, factor 4), fused LayerNorm -> expand -> SwiGLU ->
  * squeeze -> residual. Replaces the engine `Transition(128, 4)` as FoldForge calls it
