@@ -53,6 +53,7 @@ SIGNATURES: dict[str, list] = {
     "ffb_single_transition_packed_bytes": [],
     "ffb_single_transition_workspace_bytes": [c_int, c_int],
     "ffb_single_transition_prepare": [c_void_p] * 7,
+    "ffb_single_transition_fwd_noalloc": [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p],
     "ffb_single_transition_fwd": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_size_t, c_int, c_int,
                                   c_int, c_void_p],
 }

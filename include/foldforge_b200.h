@@ -159,6 +159,19 @@ int ffb_single_transition_prepare(const float* ln_w, const float* ln_b, const fl
 int ffb_single_transition_fwd(const void* s, const uint8_t* mask, const void* packed, void* out, void* workspace,
                               size_t workspace_bytes, int B, int N, int masked, void* stream);
 
+/* The single transition for callers that cannot allocate device memory when they run it
+ * (a host whose device memory belongs to its own pool or arena, a pipeline that allocates
+ * only at start-up). No counterpart in the reference: it exists for those callers only.
+ * Same arguments and result as ffb_single_transition_fwd minus the workspace, which is a
+ * fixed 3,932,160-byte array inside the library that every GPU loading the library keeps
+ * until the process exits. B * N must be at most 1024 tokens (larger calls return
+ * FFB_ERR_UNSUPPORTED). The array's device address is looked up on a device's first call,
+ * with that device current: make the first call before any stream capture. All calls share
+ * the array, so calls whose GPU work overlaps race and must be serialised by the caller.
+ * Allocates nothing. */
+int ffb_single_transition_fwd_noalloc(const void* s, const uint8_t* mask, const void* packed, void* out, int B, int N,
+                                      int masked, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
