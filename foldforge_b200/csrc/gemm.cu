@@ -55,7 +55,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int b, int m
     }
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + static_cast<int64_t>(b) * p.batch_stride_d +
                          static_cast<int64_t>(m) * p.ldd + h0;
-    if (h0 + 16 <= out_cols) {
+    if (h0 + 16 <= out_cols && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
       uint4 w0 = make_uint4(pack_bf16(out[0], out[1]), pack_bf16(out[2], out[3]), pack_bf16(out[4], out[5]),
                             pack_bf16(out[6], out[7]));
       uint4 w1 = make_uint4(pack_bf16(out[8], out[9]), pack_bf16(out[10], out[11]), pack_bf16(out[12], out[13]),
@@ -95,7 +95,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int b, int m
   }
   if (p.d_is_f32) {
     float* d = reinterpret_cast<float*>(p.D) + off;
-    if (full) {
+    if (full && (reinterpret_cast<uintptr_t>(d) & 15u) == 0) {
 #pragma unroll
       for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(d + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
     } else {
@@ -104,7 +104,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int b, int m
     }
   } else {
     __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + off;
-    if (full) {
+    if (full && (reinterpret_cast<uintptr_t>(d) & 15u) == 0) {
 #pragma unroll
       for (int i = 0; i < 32; i += 8) {
         uint4 w = make_uint4(pack_bf16(acc[i], acc[i + 1]), pack_bf16(acc[i + 2], acc[i + 3]),

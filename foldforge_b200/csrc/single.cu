@@ -4,7 +4,7 @@
 // GEMM and LayerNorm launchers plus one attention kernel:
 //
 // attention with pair bias (legacy/pairformer.py:204-226, legacy/transformer.py:88-133):
-//   pb[b, i, j, h] = W_pb (gamma_pair * LNhat(z[b, i, j]))     LayerNorm + GEMM (N = 16)
+//   pb[h, b, i, j] = W_pb (gamma_pair * LNhat(z[b, i, j]))     LayerNorm + GEMM (16 rows)
 //   y = LN(s);  [q | k | v | g] = y W^T + [b_q | 0 | 0 | 0]     GEMM (N = 1536)
 //   o = softmax_j(q_i . k_j / sqrt(24) + pb[i, j, h] (+ extra[h, i, j]), key mask) v_j
 //   s' = s + W_o (sigmoid(g + gate_bias) * o)                    GEMM with residual epilogue
@@ -49,28 +49,33 @@ int to_bf16(const float* a, const float* b, int rows_each, int cols, int interle
 }
 
 // ---------------------------------------------------------------- attention kernel
-// One thread per query, a CTA per (batch, head, 64 queries). The head's keys and values are
-// staged through shared memory in chunks of kKeyChunk (fp32, read as broadcasts), so every
-// key row is fetched once per CTA instead of once per query. Each thread runs an exact
-// online softmax over its row (the running max is raised only when a logit exceeds it).
-// Masked keys get the reference's REPLACED logit -1e9, so a row whose keys are all
-// masked averages uniformly; keys past N do not exist.
-constexpr int kQueriesPerCta = 64;
-constexpr int kKeyChunk = 128;
+// A CTA per (batch, head, 32 queries), 4 warps. Lane = query; warp w takes keys w*16 ..
+// w*16+15 of every 64-key chunk, which is staged once per CTA in shared memory: keys and
+// values (fp32) and the pair-bias tile [32 q][64 k] (head-major bias, coalesced rows, padded
+// rows so that lanes reading one key hit distinct banks). Each warp keeps a private exact
+// online softmax per query; the four partial states are merged at the end. Masked keys get
+// the reference's REPLACED logit -1e9, so a row whose keys are all masked averages
+// uniformly; keys past N do not exist.
+constexpr int kQ = 32;        // queries per CTA
+constexpr int kKC = 64;       // keys per staged chunk
+constexpr int kWarps = 4;
+constexpr int kKPW = kKC / kWarps;
 
-__global__ void __launch_bounds__(kQueriesPerCta) single_attention_kernel(
-    const __nv_bfloat16* __restrict__ qkvg, const float* __restrict__ pair_bias, const void* __restrict__ extra,
+__global__ void __launch_bounds__(kQ * kWarps) single_attention_kernel(
+    const __nv_bfloat16* __restrict__ qkvg, const float* __restrict__ pair_bias_hm, const void* __restrict__ extra,
     int extra_f32, const uint8_t* __restrict__ mask, float gate_bias, __nv_bfloat16* __restrict__ out, int B, int N) {
-  __shared__ float4 ks[kKeyChunk][kDs / 4];
-  __shared__ float4 vs[kKeyChunk][kDs / 4];
-  __shared__ float keep[kKeyChunk];
-  const int qblocks = (N + kQueriesPerCta - 1) / kQueriesPerCta;
+  __shared__ float ks[kKC][kDs];
+  __shared__ float vs[kKC][kDs];
+  __shared__ float bias[kQ][kKC + 1];
+  __shared__ float keep[kKC];
+  __shared__ float part[kWarps][kQ][kDs + 2];
+  const int qblocks = (N + kQ - 1) / kQ;
   const int h = blockIdx.x % kHs;
   const int qb = (blockIdx.x / kHs) % qblocks;
   const int b = blockIdx.x / (kHs * qblocks);
-  const int i = qb * kQueriesPerCta + threadIdx.x;
-  const bool active = i < N;
-  const int row = active ? i : N - 1;
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  const int i = qb * kQ + lane;
+  const int row = i < N ? i : N - 1;
   const __nv_bfloat16* row_i = qkvg + (static_cast<int64_t>(b) * N + row) * (4 * kCs);
   const float scale = rsqrtf(static_cast<float>(kDs));
   float q[kDs];
@@ -80,32 +85,54 @@ __global__ void __launch_bounds__(kQueriesPerCta) single_attention_kernel(
   float o[kDs];
 #pragma unroll
   for (int d = 0; d < kDs; ++d) o[d] = 0.f;
-  const float* pb_row = pair_bias + ((static_cast<int64_t>(b) * N + row) * N) * kHs + h;
-  for (int j0 = 0; j0 < N; j0 += kKeyChunk) {
-    const int nk = N - j0 < kKeyChunk ? N - j0 : kKeyChunk;
+  // head-major bias: [h][b][i][j]
+  const float* pb = pair_bias_hm + (static_cast<int64_t>(h) * B + b) * static_cast<int64_t>(N) * N;
+  for (int j0 = 0; j0 < N; j0 += kKC) {
+    const int nk = N - j0 < kKC ? N - j0 : kKC;
     __syncthreads();
-    for (int e = threadIdx.x; e < nk * kDs; e += kQueriesPerCta) {
+    for (int e = threadIdx.x; e < kKC * kDs; e += kQ * kWarps) {
       const int j = e / kDs, d = e % kDs;
-      const __nv_bfloat16* rj = qkvg + (static_cast<int64_t>(b) * N + j0 + j) * (4 * kCs) + h * kDs + d;
-      reinterpret_cast<float*>(ks[j])[d] = __bfloat162float(rj[kCs]);
-      reinterpret_cast<float*>(vs[j])[d] = __bfloat162float(rj[2 * kCs]);
+      float kv = 0.f, vv = 0.f;
+      if (j < nk) {
+        const __nv_bfloat16* rj = qkvg + (static_cast<int64_t>(b) * N + j0 + j) * (4 * kCs) + h * kDs + d;
+        kv = __bfloat162float(rj[kCs]);
+        vv = __bfloat162float(rj[2 * kCs]);
+      }
+      ks[j][d] = kv;
+      vs[j][d] = vv;
     }
-    for (int j = threadIdx.x; j < nk; j += kQueriesPerCta) keep[j] = mask[static_cast<int64_t>(b) * N + j0 + j] ? 1.f : 0.f;
+    for (int e = threadIdx.x; e < kQ * kKC; e += kQ * kWarps) {
+      const int qq = e / kKC, j = e % kKC;
+      const int ii = qb * kQ + qq;
+      float v = 0.f;
+      if (ii < N && j < nk) {
+        v = pb[static_cast<int64_t>(ii) * N + j0 + j];
+        if (extra != nullptr) {
+          const int64_t x = ((static_cast<int64_t>(b) * kHs + h) * N + ii) * N + j0 + j;
+          v += extra_f32 ? static_cast<const float*>(extra)[x]
+                         : __bfloat162float(static_cast<const __nv_bfloat16*>(extra)[x]);
+        }
+      }
+      bias[qq][j] = v;
+    }
+    for (int j = threadIdx.x; j < kKC; j += kQ * kWarps)
+      keep[j] = (j < nk) ? (mask[static_cast<int64_t>(b) * N + j0 + j] ? 1.f : 0.f) : -1.f;
     __syncthreads();
-    for (int j = 0; j < nk; ++j) {
-      float x = 0.f;
+#pragma unroll 2
+    for (int jj = 0; jj < kKPW; ++jj) {
+      const int j = warp * kKPW + jj;
+      const float kp = keep[j];
+      if (kp < 0.f) continue;  // past N (uniform across the warp)
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll
-      for (int d4 = 0; d4 < kDs / 4; ++d4) {
-        const float4 k4 = ks[j][d4];
-        x += q[4 * d4] * k4.x + q[4 * d4 + 1] * k4.y + q[4 * d4 + 2] * k4.z + q[4 * d4 + 3] * k4.w;
+      for (int d = 0; d < kDs; d += 4) {
+        a0 += q[d] * ks[j][d];
+        a1 += q[d + 1] * ks[j][d + 1];
+        a2 += q[d + 2] * ks[j][d + 2];
+        a3 += q[d + 3] * ks[j][d + 3];
       }
-      x += pb_row[static_cast<int64_t>(j0 + j) * kHs];
-      if (extra != nullptr) {
-        const int64_t e = ((static_cast<int64_t>(b) * kHs + h) * N + row) * N + j0 + j;
-        x += extra_f32 ? static_cast<const float*>(extra)[e]
-                       : __bfloat162float(static_cast<const __nv_bfloat16*>(extra)[e]);
-      }
-      if (keep[j] == 0.f) x = -1.0e9f;
+      float x = (a0 + a1) + (a2 + a3) + bias[lane][j];
+      if (kp == 0.f) x = -1.0e9f;
       if (x > m) {
         const float alpha = __expf(m - x);
         l *= alpha;
@@ -116,22 +143,36 @@ __global__ void __launch_bounds__(kQueriesPerCta) single_attention_kernel(
       const float p = __expf(x - m);
       l += p;
 #pragma unroll
-      for (int d4 = 0; d4 < kDs / 4; ++d4) {
-        const float4 v4 = vs[j][d4];
-        o[4 * d4] += p * v4.x;
-        o[4 * d4 + 1] += p * v4.y;
-        o[4 * d4 + 2] += p * v4.z;
-        o[4 * d4 + 3] += p * v4.w;
-      }
+      for (int d = 0; d < kDs; ++d) o[d] += p * vs[j][d];
     }
   }
-  if (!active) return;
-  const float inv = 1.0f / l;
+  // merge the four warps' partial softmax states per query
+#pragma unroll
+  for (int d = 0; d < kDs; ++d) part[warp][lane][d] = o[d];
+  part[warp][lane][kDs] = m;
+  part[warp][lane][kDs + 1] = l;
+  __syncthreads();
+  if (warp != 0 || i >= N) return;
+  float mm = -1.0e30f;
+  for (int w = 0; w < kWarps; ++w)
+    if (part[w][lane][kDs + 1] > 0.f) mm = fmaxf(mm, part[w][lane][kDs]);
+  float ll = 0.f, acc[kDs];
+#pragma unroll
+  for (int d = 0; d < kDs; ++d) acc[d] = 0.f;
+  for (int w = 0; w < kWarps; ++w) {
+    const float lw = part[w][lane][kDs + 1];
+    if (lw <= 0.f) continue;
+    const float f = __expf(part[w][lane][kDs] - mm);
+    ll += lw * f;
+#pragma unroll
+    for (int d = 0; d < kDs; ++d) acc[d] += part[w][lane][d] * f;
+  }
+  const float inv = 1.0f / ll;
   __nv_bfloat16* dst = out + (static_cast<int64_t>(b) * N + i) * kCs + h * kDs;
 #pragma unroll
   for (int d = 0; d < kDs; ++d) {
     const float g = __bfloat162float(row_i[3 * kCs + h * kDs + d]) + gate_bias;
-    dst[d] = __float2bfloat16_rn(o[d] * inv * sigmoidf_(g));
+    dst[d] = __float2bfloat16_rn(acc[d] * inv * sigmoidf_(g));
   }
 }
 
@@ -242,7 +283,9 @@ int apb_forward(const void* s, const void* z, const uint8_t* mask, const void* p
                                         static_cast<int64_t>(P), kCz, 1e-5f, 0, info.num_sms, stream),
                        "apb pair layernorm");
   if (st) return st;
-  st = gemm(zn, img + L.w_pb, pb, static_cast<int>(P), kHs, kCz, 1, nullptr, kEpiStore, nullptr, nullptr, info, stream);
+  // head-major pair bias pb[h][p] = W_pb[h] . zn[p]: the weight is the A operand (16 rows;
+  // the tile's other rows are zero-filled by TMA), the pairs are the N dimension
+  st = gemm(img + L.w_pb, zn, pb, kHs, static_cast<int>(P), kCz, 1, nullptr, kEpiStore, nullptr, nullptr, info, stream);
   if (st) return st;
   st = cuda_status(launch_layernorm(s, y, reinterpret_cast<const float*>(img + L.ln_s_w),
                                     reinterpret_cast<const float*>(img + L.ln_s_b), static_cast<int64_t>(T), kCs,
@@ -252,8 +295,8 @@ int apb_forward(const void* s, const void* z, const uint8_t* mask, const void* p
   st = gemm(y, img + L.w_qkvg, qkvg, static_cast<int>(T), 4 * kCs, kCs, 0,
             reinterpret_cast<const float*>(img + L.b_qkvg), kEpiStore, nullptr, nullptr, info, stream);
   if (st) return st;
-  const int ctas = B * kHs * ((N + kQueriesPerCta - 1) / kQueriesPerCta);
-  single_attention_kernel<<<ctas, kQueriesPerCta, 0, stream>>>(
+  const int ctas = B * kHs * ((N + kQ - 1) / kQ);
+  single_attention_kernel<<<ctas, kQ * kWarps, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(qkvg), pb, extra, extra_f32, mask, gate_bias,
       static_cast<__nv_bfloat16*>(gated), B, N);
   st = cuda_status(static_cast<int>(cudaGetLastError()), "single attention launch");
