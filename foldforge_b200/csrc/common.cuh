@@ -14,6 +14,7 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -260,6 +261,26 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw64(uint32_t smem_addr) {
   return d;
 }
 
+// MN-major operand in the 128-byte swizzle layout: each 128-byte row holds 64 consecutive
+// M (or N) elements of one K index, 8-row K groups `sbo` bytes apart (1024 for a dense
+// tile), and the next 64-element M/N block `lbo` bytes further. Advancing K by 16 is
+// +16 rows (2 K groups) on the start address.
+__device__ __forceinline__ uint64_t desc_mnmajor_sw128(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: bf16 A (K-major) x bf16 B (MN-major) -> fp32, shape M x N.
+__host__ __device__ constexpr uint32_t idesc_bf16_f32_bmn(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16)  // B is MN-major
+         | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
 // Instruction descriptor: bf16 x bf16 -> fp32, both operands K-major, shape M x N.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
   return (1u << 4)                                  // D format: f32
@@ -267,6 +288,13 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
          | (1u << 10)                               // B format: bf16
          | (static_cast<uint32_t>(n >> 3) << 17)    // N / 8
          | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
+}
+
+// Instruction descriptor: f16 x f16 -> fp32, both operands K-major, shape M x N.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
+  return (1u << 4)                                  // D format: f32
+         | (static_cast<uint32_t>(n >> 3) << 17)    // A, B format: f16 (0)
+         | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
 // Byte offset of element (row, col) (col in bf16 units, < 64) inside a K-major SW128 atom
@@ -297,6 +325,51 @@ __device__ __forceinline__ float tanh_fast(float x) {
 
 // sigmoid(x) = 0.5 tanh(x / 2) + 0.5: one MUFU op and two FMAs.
 __device__ __forceinline__ float sigmoid_fast(float x) { return fmaf(0.5f, tanh_fast(0.5f * x), 0.5f); }
+
+// ---- paired fp32 arithmetic (sm_100 f32x2) and f16x2 helpers
+__device__ __forceinline__ uint64_t f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f32x2_split(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// {lo, hi} fp32 -> f16x2 (lo in the low half)
+__device__ __forceinline__ uint32_t f16x2_from(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ uint32_t ex2_f16x2(uint32_t x) {
+  uint32_t r;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(x));
+  return r;
+}
+__device__ __forceinline__ uint32_t add_f16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ float f16x2_sum(uint32_t v) {
+  __half2 h = *reinterpret_cast<__half2*>(&v);
+  return __low2float(h) + __high2float(h);
+}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -38,10 +38,11 @@ constexpr int kThreads = kGroups * 128;
 // [128K, 160K)         gate operand W_g' (rows = output channels)
 // [160K, 192K)         output operand W_o' = W_o diag(gamma_out)
 // [192K, +)            fp32: wsum_proj[512] bias_proj[512] wsum_gate[128] bias_gate[128] bias_out[128]
+//                      wsum_out[128]
 constexpr size_t kProjBytes = 512 * kC * 2;
 constexpr size_t kGateBytes = kC * kC * 2;
 constexpr size_t kOutBytes = kC * kH * 2;
-constexpr size_t kVecFloats = 512 + 512 + 128 + 128 + 128;
+constexpr size_t kVecFloats = 512 + 512 + 128 + 128 + 128 + 128;
 constexpr size_t kPackedBytes = kProjBytes + kGateBytes + kOutBytes + kVecFloats * 4;
 
 struct Vecs {
@@ -324,17 +325,33 @@ __global__ void __launch_bounds__(kPThreads, 1)
 }
 
 // ====================================================================== kernel 3
+// Warp-specialised, persistent, 128-pair tiles, computed TRANSPOSED (TMEM lane = output
+// channel, column = pair):
+//   gate[c][p] = W_g'[c] . z[p]          B = the z tile (K-major, as TMA lands it)
+//   out[c][p]  = W_o'[c] . u[:, p]       B = the channel-major u tile used as an MN-major
+//                                        operand (no transposition in shared memory)
+// with both LayerNorms folded into the epilogue through per-pair statistics:
+//   delta[c][p] = (ru_p (out - mu_p wsum_o[c]) + b_o[c]) * sigmoid(rz_p (gate - mz_p wsum_g[c]) + b_g[c])
+// The epilogue adds delta into the z tile in place (lanes = consecutive channels of one pair
+// row) and one thread stores the tile with TMA.
+//   warp 0      TMA: z and u tiles into a 2-stage ring
+//   warp 1      MMA: gate and out products -> 256 TMEM columns, double-buffered
+//   warps 2-3   per-pair statistics of z (rows) and u (columns) and the keep mask
+//   warps 4-11  epilogue: lane = channel, warps 4-7 pairs 0-63, warps 8-11 pairs 64-127
+constexpr int kOTile = 128;
+constexpr int kOStages = 2;
+constexpr int kOThreads = 384;
+
 struct OutSmem {
   alignas(1024) uint8_t wg[kGateBytes];
   alignas(1024) uint8_t wo[kOutBytes];
-  alignas(1024) uint8_t z[kGroups][kTile * kC * 2];
-  alignas(1024) uint8_t u[kGroups][kTile * kH * 2];
-  float wsum_gate[128];
-  float bias_gate[128];
-  float bias_out[128];
+  alignas(1024) uint8_t z[kOStages][kOTile * kC * 2];  // [p][c]: 2 K-blocks of [128 p x 128 B]
+  alignas(1024) uint8_t u[kOStages][kH * kOTile * 2];  // [c][p]: 2 p-blocks of [128 c x 128 B]
+  float wsum_gate[128], bias_gate[128], wsum_out[128], bias_out[128];
+  float zm[2][kOTile], zr[2][kOTile], um[2][kOTile], ur[2][kOTile], keep[2][kOTile];
   uint64_t wbar;
-  uint64_t full[kGroups];
-  uint64_t mma[kGroups];
+  uint64_t full[kOStages], empty[kOStages];
+  uint64_t acc_full[2], acc_free[2], st_full[2], st_free[2];
   uint32_t tmem_base;
 };
 
@@ -346,24 +363,45 @@ struct OutParams {
   int* err;
 };
 
-__global__ void __launch_bounds__(kThreads, 1)
+// u[c][p] in the MN-major SW128 tile
+__device__ __forceinline__ float u_at(const uint8_t* ut, int c, int p) {
+  const int blk = p >> 6, pp = p & 63;
+  const uint32_t off = static_cast<uint32_t>(blk) * (kH * 128) + c * 128 + ((((pp >> 3) ^ (c & 7)) << 4)) + (pp & 7) * 2;
+  return __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(ut + off));
+}
+
+__global__ void __launch_bounds__(kOThreads, 1)
     trimul_out_kernel(const __grid_constant__ CUtensorMap map_z, const __grid_constant__ CUtensorMap map_u,
                       const __grid_constant__ CUtensorMap map_out, OutParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   OutSmem& s = *reinterpret_cast<OutSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int g = threadIdx.x / 128;
-  const int gt = threadIdx.x % 128;
   const int warp = threadIdx.x / 32;
-  const int tiles_per_row = (p.N + kTile - 1) / kTile;
+  const int lane = threadIdx.x % 32;
+  const int tiles_per_row = (p.N + kOTile - 1) / kOTile;
   const int total = p.B * p.N * tiles_per_row;
 
   if (threadIdx.x == 0) {
     mbar_init(&s.wbar, 1);
-    for (int i = 0; i < kGroups; ++i) {
+    for (int i = 0; i < kOStages; ++i) {
       mbar_init(&s.full[i], 1);
-      mbar_init(&s.mma[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.acc_full[i], 1);
+      mbar_init(&s.acc_free[i], 8);
+      mbar_init(&s.st_full[i], 2);
+      mbar_init(&s.st_free[i], 8);
     }
     fence_mbar_init();
+  }
+  {
+    const float* v = reinterpret_cast<const float*>(p.packed + kProjBytes + kGateBytes + kOutBytes);
+    for (int i = threadIdx.x; i < 128; i += kOThreads) {
+      s.wsum_gate[i] = v[1024 + i];
+      s.bias_gate[i] = v[1152 + i];
+      s.bias_out[i] = v[1280 + i];
+      s.wsum_out[i] = v[1408 + i];
+    }
   }
   if (warp == 0) {
     tmem_alloc(&s.tmem_base, 512);
@@ -372,161 +410,187 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (threadIdx.x == 0) {
-    tma_prefetch_map(&map_z);
-    tma_prefetch_map(&map_u);
-    tma_prefetch_map(&map_out);
-    mbar_arrive_expect_tx(&s.wbar, kGateBytes + kOutBytes);
-    bulk_load(s.wg, p.packed + kProjBytes, kGateBytes, &s.wbar);
-    bulk_load(s.wo, p.packed + kProjBytes + kGateBytes, kOutBytes, &s.wbar);
-  }
-  {
-    const float* v = reinterpret_cast<const float*>(p.packed + kProjBytes + kGateBytes + kOutBytes) + 1024;
-    for (int i = threadIdx.x; i < 128; i += kThreads) {
-      s.wsum_gate[i] = v[i];
-      s.bias_gate[i] = v[128 + i];
-      s.bias_out[i] = v[256 + i];
-    }
-  }
-  __syncthreads();
-  bool ok = mbar_wait(&s.wbar, 0, p.err, kErrTimeoutLoad);
-  const uint32_t tmem = s.tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16) + g * 256;
-  const uint32_t tmem_mma = s.tmem_base + g * 256;
-  const uint32_t idesc = idesc_bf16_f32(128, 128);
-  uint8_t* zt = s.z[g];
-  uint8_t* ut = s.u[g];
-  int it = 0;
-  bool load_pending = false;
-  for (int tile = blockIdx.x * kGroups + g; tile < total; tile += gridDim.x * kGroups, ++it) {
-    const int c0 = (tile % tiles_per_row) * kTile;
-    const int rr = tile / tiles_per_row;
-    const int b = rr / p.N;
-    const int r = rr - b * p.N;
-    if (gt == 0 && ok) {
-      tma_store_wait_read0();  // the previous tile's output store has left the z stage
-      mbar_arrive_expect_tx(&s.full[g], kTile * kC * 2 + kTile * kH * 2);
-      tma_load_3d(zt, &map_z, &s.full[g], 0, c0, rr);
-      tma_load_3d(zt + 16384, &map_z, &s.full[g], 64, c0, rr);
-      tma_load_3d(ut, &map_u, &s.full[g], c0, r, b * kH);  // u[b, :, r, c0 + t] -> [c][t]
-      load_pending = true;
-    }
-    ok = ok && mbar_wait(&s.full[g], it & 1, p.err, kErrTimeoutLoad);
-    if (gt == 0 && ok) load_pending = false;
-    float zmean = 0.f, zrstd = 0.f;
-    uint32_t uv[64];
-    float umean = 0.f, urstd = 0.f;
-    if (ok) {
-      load_z_stats(zt, gt, zmean, zrstd);
-      const __nv_bfloat16* ucol = reinterpret_cast<const __nv_bfloat16*>(ut) + gt;
-      float sum = 0.f;
-#pragma unroll
-      for (int c = 0; c < kH; c += 2) {
-        const __nv_bfloat16 lo = ucol[c * kTile], hi = ucol[(c + 1) * kTile];
-        const float a = __bfloat162float(lo), bb = __bfloat162float(hi);
-        sum += a + bb;
-        uv[c / 2] = pack_bf16(a, bb);
+  const uint32_t tmem0 = s.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_map(&map_z);
+      tma_prefetch_map(&map_u);
+      tma_prefetch_map(&map_out);
+      mbar_arrive_expect_tx(&s.wbar, kGateBytes + kOutBytes);
+      bulk_load(s.wg, p.packed + kProjBytes, kGateBytes, &s.wbar);
+      bulk_load(s.wo, p.packed + kProjBytes + kGateBytes, kOutBytes, &s.wbar);
+      int it = 0;
+      for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
+        const int st = it % kOStages;
+        if (!mbar_wait(&s.empty[st], ((it / kOStages) & 1) ^ 1, p.err, kErrTimeoutEmpty)) break;
+        const int c0 = (tile % tiles_per_row) * kOTile;
+        const int rr = tile / tiles_per_row;
+        const int b = rr / p.N, r = rr - b * p.N;
+        mbar_arrive_expect_tx(&s.full[st], 2 * kOTile * kC * 2);
+        for (int kb = 0; kb < 2; ++kb) {
+          tma_load_3d(s.z[st] + kb * (kOTile * 128), &map_z, &s.full[st], kb * 64, c0, rr);
+          tma_load_3d(s.u[st] + kb * (kH * 128), &map_u, &s.full[st], c0 + kb * 64, r, b * kH);
+        }
       }
-      umean = sum * (1.0f / kH);
-      float q2 = 0.f;
-#pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float a = bf16_lo(uv[i]) - umean, bb = bf16_hi(uv[i]) - umean;
-        q2 += a * a + bb * bb;
-      }
-      urstd = rsqrtf(q2 * (1.0f / kH) + 1e-5f);
+      mbar_wait(&s.wbar, 0, p.err, kErrTimeoutLoad);
     }
-    named_barrier(1 + g, 128);  // every column of u read before the tile is overwritten
-    if (ok) {
-      // normalised u, row gt, as a K-major SW128 operand in place of the channel-major tile
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc_g = idesc_bf16_f32(128, kOTile);
+      const uint32_t idesc_o = idesc_bf16_f32_bmn(128, kOTile);
+      bool ok = mbar_wait(&s.wbar, 0, p.err, kErrTimeoutLoad);
+      int it = 0;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
+        const int st = it % kOStages, buf = it & 1;
+        if (!mbar_wait(&s.full[st], (it / kOStages) & 1, p.err, kErrTimeoutLoad)) break;
+        if (!mbar_wait(&s.acc_free[buf], ((it >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty)) break;
+        tc_fence_after();
+        const uint32_t wg = smem_u32(s.wg), wo = smem_u32(s.wo), za = smem_u32(s.z[st]), ua = smem_u32(s.u[st]);
+        const uint32_t dg = tmem0 + buf * 256, dout = tmem0 + buf * 256 + kOTile;
 #pragma unroll
-      for (int kb = 0; kb < 2; ++kb)
+        for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          uint32_t w[4];
+          for (int kk = 0; kk < 4; ++kk)
+            mma_bf16(dg, desc_kmajor_sw128(wg + kb * 16384) + 2 * kk, desc_kmajor_sw128(za + kb * (kOTile * 128)) + 2 * kk,
+                     idesc_g, (kb | kk) != 0);
+#pragma unroll
+        for (int ks = 0; ks < kH / 16; ++ks)
+          mma_bf16(dout, desc_kmajor_sw128(wo + (ks / 4) * 16384) + 2 * (ks % 4),
+                   desc_mnmajor_sw128(ua + ks * 2048, kH * 128, 1024), idesc_o, ks != 0);
+        mma_commit(&s.acc_full[buf]);
+      }
+    }
+  } else if (warp < 4) {
+    // statistics: thread t handles pairs t and t + 64 of the tile
+    const int t = (warp - 2) * 32 + lane;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
+      const int st = it % kOStages, buf = it & 1;
+      const bool w1 = mbar_wait(&s.full[st], (it / kOStages) & 1, p.err, kErrTimeoutLoad);
+      const bool w2 = mbar_wait(&s.st_free[buf], ((it >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty);
+      if (!__all_sync(0xFFFFFFFFu, w1 && w2)) break;
+      const int c0 = (tile % tiles_per_row) * kOTile;
+      const int rr = tile / tiles_per_row;
+      const int b = rr / p.N, r = rr - b * p.N;
+      const uint8_t* zt = s.z[st];
+      const uint8_t* ut = s.u[st];
+#pragma unroll 1
+      for (int k = 0; k < 2; ++k) {
+        const int pp = t + 64 * k;
+        // z row statistics
+        float sum = 0.f;
+        uint4 v[16];
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            v[kb * 8 + q] = *reinterpret_cast<const uint4*>(zt + kb * (kOTile * 128) + sw128_offset(pp, q * 8));
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) sum += bf16_lo(w[j]) + bf16_hi(w[j]);
+        }
+        const float zmean = sum * (1.0f / kC);
+        float q2 = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const uint32_t x = uv[kb * 32 + q * 4 + j];
-            w[j] = pack_bf16((bf16_lo(x) - umean) * urstd, (bf16_hi(x) - umean) * urstd);
+            const float a = bf16_lo(w[j]) - zmean, bb = bf16_hi(w[j]) - zmean;
+            q2 += a * a + bb * bb;
           }
-          *reinterpret_cast<uint4*>(ut + kb * 16384 + sw128_offset(gt, q * 8)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
+        // u column statistics (two-pass over the 128 channels)
+        float us = 0.f;
+#pragma unroll 8
+        for (int c = 0; c < kH; ++c) us += u_at(ut, c, pp);
+        const float umean = us * (1.0f / kH);
+        float uq = 0.f;
+#pragma unroll 8
+        for (int c = 0; c < kH; ++c) {
+          const float d = u_at(ut, c, pp) - umean;
+          uq += d * d;
+        }
+        const int j = c0 + pp;
+        s.zm[buf][pp] = zmean;
+        s.zr[buf][pp] = rsqrtf(q2 * (1.0f / kC) + 1e-5f);
+        s.um[buf][pp] = umean;
+        s.ur[buf][pp] = rsqrtf(uq * (1.0f / kH) + 1e-5f);
+        s.keep[buf][pp] = (!p.masked_zero || (j < p.N && p.mask[b * p.N + r] && p.mask[b * p.N + j])) ? 1.f : 0.f;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.st_full[buf]);
     }
-    fence_async_smem();
-    named_barrier(1 + g, 128);
-    if (gt == 0 && ok) {
+  } else {
+    // epilogue: lane = output channel c; half = which 64 pairs
+    const int half = (warp - 4) / 4;
+    const int c = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const float wsg = s.wsum_gate[c], bg = s.bias_gate[c], wso = s.wsum_out[c], bo = s.bias_out[c];
+    const int kb = c / 64;
+    int it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
+      const int st = it % kOStages, buf = it & 1;
+      if (ok) {
+        const bool w1 = mbar_wait(&s.acc_full[buf], (it >> 1) & 1, p.err, kErrTimeoutMma);
+        const bool w2 = mbar_wait(&s.st_full[buf], (it >> 1) & 1, p.err, kErrTimeoutLoad);
+        ok = __all_sync(0xFFFFFFFFu, w1 && w2);
+      }
       tc_fence_after();
-      const uint32_t za = smem_u32(zt), ua = smem_u32(ut);
-      const uint32_t wg = smem_u32(s.wg), wo = smem_u32(s.wo);
-#pragma unroll
-      for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_bf16(tmem_mma, desc_kmajor_sw128(za + kb * 16384) + 2 * kk, desc_kmajor_sw128(wg + kb * 16384) + 2 * kk,
-                   idesc, (kb | kk) != 0);
-#pragma unroll
-      for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_bf16(tmem_mma + 128, desc_kmajor_sw128(ua + kb * 16384) + 2 * kk,
-                   desc_kmajor_sw128(wo + kb * 16384) + 2 * kk, idesc, (kb | kk) != 0);
-      mma_commit(&s.mma[g]);
-    }
-    bool got = ok && mbar_wait(&s.mma[g], it & 1, p.err, kErrTimeoutMma);
-    got = __all_sync(0xFFFFFFFFu, got);
-    tc_fence_after();
-    if (got) {
-      const int j = c0 + gt;
-      const bool keep = !p.masked_zero || (j < p.N && p.mask[b * p.N + r] && p.mask[b * p.N + j]);
+      uint8_t* zt = s.z[st];
+      if (ok) {
 #pragma unroll 1
-      for (int cc = 0; cc < kC; cc += 32) {
-        uint32_t vg[32], vo[32];
-        tmem_ld32(tmem + cc, vg);
-        tmem_ld32(tmem + 128 + cc, vo);
-        tmem_ld_wait();
+        for (int ch = 0; ch < 64; ch += 32) {
+          const int p0 = half * 64 + ch;
+          uint32_t vg[32], vo[32];
+          tmem_ld32(tmem0 + lane_off + buf * 256 + p0, vg);
+          tmem_ld32(tmem0 + lane_off + buf * 256 + kOTile + p0, vo);
+          tmem_ld_wait();
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int ch = cc + q * 8;
-          uint8_t* addr = zt + (ch / 64) * 16384 + sw128_offset(gt, ch % 64);
-          uint4 zv = *reinterpret_cast<const uint4*>(addr);
-          uint32_t w[4] = {zv.x, zv.y, zv.z, zv.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float o2[2];
-#pragma unroll
-            for (int h2 = 0; h2 < 2; ++h2) {
-              const int i = q * 8 + e * 2 + h2;
-              const int c = cc + i;
-              const float gl = zrstd * (__uint_as_float(vg[i]) - zmean * s.wsum_gate[c]) + s.bias_gate[c];
-              const float o = __uint_as_float(vo[i]) + s.bias_out[c];
-              const float zold = h2 == 0 ? bf16_lo(w[e]) : bf16_hi(w[e]);
-              o2[h2] = keep ? zold + o * sigmoidf_(gl) : zold;
-            }
-            w[e] = pack_bf16(o2[0], o2[1]);
+          for (int i = 0; i < 32; ++i) {
+            const int pp = p0 + i;
+            const float g = s.zr[buf][pp] * (__uint_as_float(vg[i]) - s.zm[buf][pp] * wsg) + bg;
+            const float o = s.ur[buf][pp] * (__uint_as_float(vo[i]) - s.um[buf][pp] * wso) + bo;
+            __nv_bfloat16* addr = reinterpret_cast<__nv_bfloat16*>(zt + kb * (kOTile * 128) + sw128_offset(pp, c % 64));
+            const float zo = __bfloat162float(*addr);
+            *addr = __float2bfloat16_rn(zo + o * sigmoid_fast(g) * s.keep[buf][pp]);
           }
-          *reinterpret_cast<uint4*>(addr) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
+      tc_fence_before();
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&s.acc_free[buf]);
+        mbar_arrive(&s.st_free[buf]);
+      }
+      // all eight epilogue warps have written the tile: one thread stores it
+      ok = !named_barrier_or(1, 256, !ok);
+      if (warp == 4 && lane == 0) {
+        if (ok) {
+          const int c0 = (tile % tiles_per_row) * kOTile;
+          const int rr = tile / tiles_per_row;
+          tma_store_3d(&map_out, zt, 0, c0, rr);
+          tma_store_3d(&map_out, zt + kOTile * 128, 64, c0, rr);
+          tma_store_commit();
+          tma_store_wait_read0();
+        }
+        mbar_arrive(&s.empty[st]);
+      }
+      if (!ok) break;
     }
-    tc_fence_before();
-    fence_async_smem();
-    ok = !named_barrier_or(1 + g, 128, !ok || !got);
-    if (gt == 0 && ok) {
-      tma_store_3d(&map_out, zt, 0, c0, rr);
-      tma_store_3d(&map_out, zt + 16384, 64, c0, rr);
-      tma_store_commit();
-    }
-    if (!ok) break;
-  }
-  if (gt == 0) {
-    tma_store_wait_all0();
-    if (load_pending) mbar_wait(&s.full[g], it & 1, p.err, kErrTimeoutLoad);
+    if (warp == 4 && lane == 0) tma_store_wait_all0();
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(s.tmem_base, 512);
+    tmem_dealloc(tmem0, 512);
   }
 }
 
@@ -552,8 +616,8 @@ int trimul_prepare(const TriMulWeights& w, void* packed, cudaStream_t stream) {
     rc = launch_pack_weight(w.to_gate, kC, kC, w.ln_w, w.ln_b, img + kProjBytes, 0, kC, vec + 1024, vec + 1152,
                             stream);
   if (rc == 0)
-    rc = launch_pack_weight(w.to_out, kC, kH, w.ln_out_w, w.ln_out_b, img + kProjBytes + kGateBytes, 0, kC, nullptr,
-                            vec + 1280, stream);
+    rc = launch_pack_weight(w.to_out, kC, kH, w.ln_out_w, w.ln_out_b, img + kProjBytes + kGateBytes, 0, kC,
+                            vec + 1408, vec + 1280, stream);
   return rc;
 }
 
@@ -638,15 +702,17 @@ int trimul_forward(const void* z, const uint8_t* mask, const void* packed, void*
     if (st) return st;
     const uint64_t udims[3] = {static_cast<uint64_t>(N), static_cast<uint64_t>(N), static_cast<uint64_t>(B) * kH};
     const uint64_t ustrides[2] = {static_cast<uint64_t>(np) * 2, static_cast<uint64_t>(N) * np * 2};
-    const uint32_t ubox[3] = {kTile, 1, kH};
-    st = make_map(&map_u, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, u, udims, ustrides, ubox, CU_TENSOR_MAP_SWIZZLE_NONE);
+    const uint32_t ubox[3] = {64, 1, kH};  // [128 channels][64 pairs], 128-byte swizzled rows
+    st = make_map(&map_u, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, u, udims, ustrides, ubox, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
   }
   if (!(stages & 4)) return 0;
   OutParams op{static_cast<const uint8_t*>(packed), mask, B, N, masked_zero, info.err};
   const size_t out_smem = sizeof(OutSmem) + 1024;
+  const int otiles = B * N * ((N + kOTile - 1) / kOTile);
+  const int ogrid = otiles < info.num_sms ? otiles : info.num_sms;
   cudaFuncSetAttribute(trimul_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(out_smem));
-  trimul_out_kernel<<<grid, kThreads, out_smem, stream>>>(map_zo, map_u, map_out, op);
+  trimul_out_kernel<<<ogrid, kOThreads, out_smem, stream>>>(map_zo, map_u, map_out, op);
   return cuda_status(static_cast<int>(cudaGetLastError()), "trimul_out launch");
 }
 
