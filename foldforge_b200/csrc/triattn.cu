@@ -80,6 +80,37 @@ __device__ __forceinline__ void tile_stats(const uint8_t* tile, int row, float& 
   rstd = rsqrtf(q2 * (1.0f / kC) + 1e-5f);
 }
 
+// LayerNorm statistics of row `row` of a K-major SW128 tile of 128 channels stored as two
+// 64-channel blocks `block_bytes` apart.
+__device__ __forceinline__ void tile_stats_rows(const uint8_t* tile, int block_bytes, int row, float& mean,
+                                                float& rstd) {
+  float s = 0.f;
+  uint4 v[16];
+#pragma unroll
+  for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      v[kb * 8 + q] = *reinterpret_cast<const uint4*>(tile + kb * block_bytes + sw128_offset(row, q * 8));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) s += bf16_lo(w[j]) + bf16_hi(w[j]);
+  }
+  mean = s * (1.0f / kC);
+  float q2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float a = bf16_lo(w[j]) - mean, b = bf16_hi(w[j]) - mean;
+      q2 += a * a + b * b;
+    }
+  }
+  rstd = rsqrtf(q2 * (1.0f / kC) + 1e-5f);
+}
+
 // ====================================================================== 1. projection
 struct ProjSmem {
   alignas(1024) uint8_t w[kProjBytes];
@@ -593,16 +624,32 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 }
 
 // ====================================================================== 3. output
+// Warp-specialised, persistent, 64-pair tiles (natural pair layout for both nodes), computed
+// TRANSPOSED (TMEM lane = channel, column = pair):
+//   gate[c][p] = W_g'[c] . z[p]                        (folded input LayerNorm)
+//   G[c][p]    = sigmoid(gate[c][p]) * o[p][c]         written by the epilogue warps as an
+//                                                      MN-major operand ([c] rows of pairs)
+//   delta[c][p] = W_o[c] . G[:, p];   z'[p][c] = z[p][c] + delta[c][p]  (in place, TMA store)
+//   warp 0      TMA: z and o tiles, 2-stage ring
+//   warp 1      MMA: gate product (tile t + 1) ahead of the output product (tile t)
+//   warps 2-3   per-pair LayerNorm statistics of z and the keep mask
+//   warps 4-11  lane = channel; warps 4-7 pairs 0-31, warps 8-11 pairs 32-63
+constexpr int kOTile = 64;
+constexpr int kOStages = 2;
+constexpr int kOThreads = 384;
+
 struct OutSmem {
   alignas(1024) uint8_t wg[kGateBytes];
   alignas(1024) uint8_t wo[kOutBytes];
-  alignas(1024) uint8_t z[kGroups][kTile * kC * 2];
-  alignas(1024) uint8_t o[kGroups][kTile * kC * 2];
-  float wsum_gate[128];
-  float bias_gate[128];
+  alignas(1024) uint8_t z[kOStages][kOTile * kC * 2];  // [p][c]: 2 K-blocks of [64 p x 128 B]
+  alignas(1024) uint8_t o[kOStages][kOTile * kC * 2];  // [p][c], same layout
+  alignas(1024) uint8_t gt[kC * kOTile * 2];           // G: [c][p], 128 rows x 128 B (MN-major)
+  float wsum_gate[128], bias_gate[128];
+  float zm[2][kOTile], zr[2][kOTile], keep[2][kOTile];
   uint64_t wbar;
-  uint64_t full[kGroups];
-  uint64_t mma[kGroups];
+  uint64_t full[kOStages], empty[kOStages];
+  uint64_t g_full[2], d_full[2], acc_free[2], st_full[2], st_free[2];
+  uint64_t gt_ready;
   uint32_t tmem_base;
 };
 
@@ -614,179 +661,219 @@ struct OutParams {
   int* err;
 };
 
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(kOThreads, 1)
     triattn_out_kernel(const __grid_constant__ CUtensorMap map_z, const __grid_constant__ CUtensorMap map_o,
                        const __grid_constant__ CUtensorMap map_out, OutParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   OutSmem& s = *reinterpret_cast<OutSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int g = threadIdx.x / 128;
-  const int gt = threadIdx.x % 128;
   const int warp = threadIdx.x / 32;
-  const int tiles_per_row = (p.N + kTile - 1) / kTile;
+  const int lane = threadIdx.x % 32;
+  const int tiles_per_row = (p.N + kOTile - 1) / kOTile;
   const int total = p.B * p.N * tiles_per_row;
 
   if (threadIdx.x == 0) {
     mbar_init(&s.wbar, 1);
-    for (int i = 0; i < kGroups; ++i) {
+    for (int i = 0; i < kOStages; ++i) {
       mbar_init(&s.full[i], 1);
-      mbar_init(&s.mma[i], 1);
+      mbar_init(&s.empty[i], 1);
     }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.g_full[i], 1);
+      mbar_init(&s.d_full[i], 1);
+      mbar_init(&s.acc_free[i], 8);
+      mbar_init(&s.st_full[i], 2);
+      mbar_init(&s.st_free[i], 8);
+    }
+    mbar_init(&s.gt_ready, 8);
     fence_mbar_init();
   }
+  {
+    const float* v = reinterpret_cast<const float*>(p.packed + kProjBytes + kGateBytes + kOutBytes) + 2 * kProjRows;
+    for (int i = threadIdx.x; i < 128; i += kOThreads) {
+      s.wsum_gate[i] = v[i];
+      s.bias_gate[i] = v[128 + i];
+    }
+  }
   if (warp == 0) {
-    tmem_alloc(&s.tmem_base, 512);
+    tmem_alloc(&s.tmem_base, 256);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (threadIdx.x == 0) {
-    tma_prefetch_map(&map_z);
-    tma_prefetch_map(&map_o);
-    tma_prefetch_map(&map_out);
-    mbar_arrive_expect_tx(&s.wbar, kGateBytes + kOutBytes);
-    bulk_load(s.wg, p.packed + kProjBytes, kGateBytes, &s.wbar);
-    bulk_load(s.wo, p.packed + kProjBytes + kGateBytes, kOutBytes, &s.wbar);
-  }
-  {
-    const float* v = reinterpret_cast<const float*>(p.packed + kProjBytes + kGateBytes + kOutBytes) + 2 * kProjRows;
-    for (int i = threadIdx.x; i < 128; i += 256) {
-      s.wsum_gate[i] = v[i];
-      s.bias_gate[i] = v[128 + i];
-    }
-  }
-  __syncthreads();
-  bool ok = mbar_wait(&s.wbar, 0, p.err, kErrTimeoutLoad);
-  const uint32_t tmem = s.tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16) + g * 256;
-  const uint32_t tmem_mma = s.tmem_base + g * 256;
-  const uint32_t idesc = idesc_bf16_f32(128, 128);
-  uint8_t* zt = s.z[g];
-  uint8_t* ot = s.o[g];
-  int it = 0;
-  bool load_pending = false;
-  for (int tile = blockIdx.x * kGroups + g; tile < total; tile += gridDim.x * kGroups, ++it) {
-    const int c0 = (tile % tiles_per_row) * kTile;
-    const int rr = tile / tiles_per_row;
-    const int b = rr / p.N;
-    const int r = rr - b * p.N;
-    if (gt == 0 && ok) {
-      tma_store_wait_read0();
-      mbar_arrive_expect_tx(&s.full[g], 2 * kTile * kC * 2);
-      for (int kb = 0; kb < 2; ++kb) {
-        tma_load_3d(zt + kb * 16384, &map_z, &s.full[g], kb * 64, c0, rr);
-        tma_load_3d(ot + kb * 16384, &map_o, &s.full[g], kb * 64, c0, rr);
+  const uint32_t tmem0 = s.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_map(&map_z);
+      tma_prefetch_map(&map_o);
+      tma_prefetch_map(&map_out);
+      mbar_arrive_expect_tx(&s.wbar, kGateBytes + kOutBytes);
+      bulk_load(s.wg, p.packed + kProjBytes, kGateBytes, &s.wbar);
+      bulk_load(s.wo, p.packed + kProjBytes + kGateBytes, kOutBytes, &s.wbar);
+      int it = 0;
+      for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
+        const int st = it % kOStages;
+        if (!mbar_wait(&s.empty[st], ((it / kOStages) & 1) ^ 1, p.err, kErrTimeoutEmpty)) break;
+        const int c0 = (tile % tiles_per_row) * kOTile;
+        const int rr = tile / tiles_per_row;
+        mbar_arrive_expect_tx(&s.full[st], 2 * kOTile * kC * 2);
+        for (int kb = 0; kb < 2; ++kb) {
+          tma_load_3d(s.z[st] + kb * (kOTile * 128), &map_z, &s.full[st], kb * 64, c0, rr);
+          tma_load_3d(s.o[st] + kb * (kOTile * 128), &map_o, &s.full[st], kb * 64, c0, rr);
+        }
       }
-      load_pending = true;
+      mbar_wait(&s.wbar, 0, p.err, kErrTimeoutLoad);
     }
-    ok = ok && mbar_wait(&s.full[g], it & 1, p.err, kErrTimeoutLoad);
-    if (gt == 0 && ok) load_pending = false;
-    float mean = 0.f, rstd = 0.f;
-    if (ok) tile_stats(zt, gt, mean, rstd);
-    // phase 1: gate = W_g' z
-    if (gt == 0 && ok) {
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc_g = idesc_bf16_f32(128, kOTile);
+      const uint32_t idesc_o = idesc_bf16_f32_bmn(128, kOTile);
+      bool ok = mbar_wait(&s.wbar, 0, p.err, kErrTimeoutLoad);
+      const uint32_t wg = smem_u32(s.wg), wo = smem_u32(s.wo), ga = smem_u32(s.gt);
+      auto gate_mma = [&](int it) -> bool {
+        const int st = it % kOStages, buf = it & 1;
+        if (!mbar_wait(&s.full[st], (it / kOStages) & 1, p.err, kErrTimeoutLoad)) return false;
+        if (!mbar_wait(&s.acc_free[buf], ((it >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty)) return false;
+        tc_fence_after();
+        const uint32_t za = smem_u32(s.z[st]);
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_bf16(tmem0 + buf * 128, desc_kmajor_sw128(wg + kb * 16384) + 2 * kk,
+                     desc_kmajor_sw128(za + kb * (kOTile * 128)) + 2 * kk, idesc_g, (kb | kk) != 0);
+        mma_commit(&s.g_full[buf]);
+        return true;
+      };
+      int it = 0;
+      const int mine = (blockIdx.x < total) ? (total - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+      if (ok && mine > 0) ok = gate_mma(0);
+      for (it = 0; it < mine && ok; ++it) {
+        if (it + 1 < mine && !gate_mma(it + 1)) break;
+        const int buf = it & 1;
+        if (!mbar_wait(&s.gt_ready, it & 1, p.err, kErrTimeoutMma)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < kC / 16; ++ks)
+          mma_bf16(tmem0 + buf * 128 + kOTile, desc_kmajor_sw128(wo + (ks / 4) * 16384) + 2 * (ks % 4),
+                   desc_mnmajor_sw128(ga + ks * 2048, 16384, 1024), idesc_o, ks != 0);
+        mma_commit(&s.d_full[buf]);
+      }
+    }
+  } else if (warp < 4) {
+    // statistics: thread t = pair t of the tile
+    const int t = (warp - 2) * 32 + lane;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
+      const int st = it % kOStages, buf = it & 1;
+      const bool w1 = mbar_wait(&s.full[st], (it / kOStages) & 1, p.err, kErrTimeoutLoad);
+      const bool w2 = mbar_wait(&s.st_free[buf], ((it >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty);
+      if (!__all_sync(0xFFFFFFFFu, w1 && w2)) break;
+      float mean, rstd;
+      tile_stats_rows(s.z[st], kOTile * 128, t, mean, rstd);
+      const int c0 = (tile % tiles_per_row) * kOTile;
+      const int rr = tile / tiles_per_row;
+      const int b = rr / p.N, r = rr - b * p.N;
+      const int j = c0 + t;
+      s.zm[buf][t] = mean;
+      s.zr[buf][t] = rstd;
+      s.keep[buf][t] = (!p.masked_zero || (j < p.N && p.mask[b * p.N + r] && p.mask[b * p.N + j])) ? 1.f : 0.f;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.st_full[buf]);
+    }
+  } else {
+    const int half = (warp - 4) / 4;
+    const int c = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const float wsg = s.wsum_gate[c], bg = s.bias_gate[c];
+    const int kb = c / 64, cc = c % 64;
+    const int p0 = half * 32;
+    int it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
+      const int st = it % kOStages, buf = it & 1;
+      if (ok) {
+        const bool w1 = mbar_wait(&s.g_full[buf], (it >> 1) & 1, p.err, kErrTimeoutMma);
+        const bool w2 = mbar_wait(&s.st_full[buf], (it >> 1) & 1, p.err, kErrTimeoutLoad);
+        ok = __all_sync(0xFFFFFFFFu, w1 && w2);
+      }
       tc_fence_after();
-      const uint32_t za = smem_u32(zt), wg = smem_u32(s.wg);
-#pragma unroll
-      for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_bf16(tmem_mma, desc_kmajor_sw128(za + kb * 16384) + 2 * kk, desc_kmajor_sw128(wg + kb * 16384) + 2 * kk,
-                   idesc, (kb | kk) != 0);
-      mma_commit(&s.mma[g]);
-    }
-    bool got = ok && mbar_wait(&s.mma[g], 0, p.err, kErrTimeoutMma);
-    got = __all_sync(0xFFFFFFFFu, got);
-    tc_fence_after();
-    if (got) {
-      // gated o, in place, as the K-major operand of phase 2
-#pragma unroll 1
-      for (int cc = 0; cc < kC; cc += 32) {
+      const uint8_t* ot = s.o[st];
+      if (ok) {
+        // G[c][p] = sigmoid(gate) * o[p][c] for this warp's 32 pairs -> 4 x 16-byte chunks of row c
         uint32_t vg[32];
-        tmem_ld32(tmem + cc, vg);
+        tmem_ld32(tmem0 + lane_off + buf * 128 + p0, vg);
         tmem_ld_wait();
+        uint32_t gw[16];
 #pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) {
-          const int ch = cc + q8 * 8;
-          uint8_t* addr = ot + (ch / 64) * 16384 + sw128_offset(gt, ch % 64);
-          const uint4 ov = *reinterpret_cast<const uint4*>(addr);
-          const uint32_t w[4] = {ov.x, ov.y, ov.z, ov.w};
-          uint32_t out[4];
+        for (int i = 0; i < 32; i += 2) {
+          float gv[2];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int i = q8 * 8 + 2 * e;
-            const float g0 = rstd * (__uint_as_float(vg[i]) - mean * s.wsum_gate[cc + i]) + s.bias_gate[cc + i];
-            const float g1 =
-                rstd * (__uint_as_float(vg[i + 1]) - mean * s.wsum_gate[cc + i + 1]) + s.bias_gate[cc + i + 1];
-            out[e] = pack_bf16(bf16_lo(w[e]) * sigmoidf_(g0), bf16_hi(w[e]) * sigmoidf_(g1));
+          for (int e = 0; e < 2; ++e) {
+            const int pp = p0 + i + e;
+            const float g = s.zr[buf][pp] * (__uint_as_float(vg[i + e]) - s.zm[buf][pp] * wsg) + bg;
+            const float ov = __bfloat162float(
+                *reinterpret_cast<const __nv_bfloat16*>(ot + kb * (kOTile * 128) + sw128_offset(pp, cc)));
+            gv[e] = ov * sigmoid_fast(g);
           }
-          *reinterpret_cast<uint4*>(addr) = make_uint4(out[0], out[1], out[2], out[3]);
+          gw[i / 2] = pack_bf16(gv[0], gv[1]);
         }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<uint4*>(s.gt + sw128_offset(c, p0 + q * 8)) =
+              make_uint4(gw[4 * q], gw[4 * q + 1], gw[4 * q + 2], gw[4 * q + 3]);
       }
-    }
-    tc_fence_before();
-    fence_async_smem();
-    named_barrier(1 + g, 128);
-    // phase 2: delta = W_o (gated o)
-    if (gt == 0 && got) {
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.gt_ready);
+      if (ok) {
+        const bool w3 = mbar_wait(&s.d_full[buf], (it >> 1) & 1, p.err, kErrTimeoutMma);
+        ok = __all_sync(0xFFFFFFFFu, w3);
+      }
       tc_fence_after();
-      const uint32_t oa = smem_u32(ot), wo = smem_u32(s.wo);
-#pragma unroll
-      for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_bf16(tmem_mma + 128, desc_kmajor_sw128(oa + kb * 16384) + 2 * kk,
-                   desc_kmajor_sw128(wo + kb * 16384) + 2 * kk, idesc, (kb | kk) != 0);
-      mma_commit(&s.mma[g]);
-    }
-    bool got2 = got && mbar_wait(&s.mma[g], 1, p.err, kErrTimeoutMma);
-    got2 = __all_sync(0xFFFFFFFFu, got2);
-    tc_fence_after();
-    if (got2) {
-      const int j = c0 + gt;
-      const bool keep = !p.masked_zero || (j < p.N && p.mask[b * p.N + r] && p.mask[b * p.N + j]);
-#pragma unroll 1
-      for (int cc = 0; cc < kC; cc += 32) {
-        uint32_t vo[32];
-        tmem_ld32(tmem + 128 + cc, vo);
+      uint8_t* zt = s.z[st];
+      if (ok) {
+        uint32_t vd[32];
+        tmem_ld32(tmem0 + lane_off + buf * 128 + kOTile + p0, vd);
         tmem_ld_wait();
 #pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) {
-          const int ch = cc + q8 * 8;
-          uint8_t* addr = zt + (ch / 64) * 16384 + sw128_offset(gt, ch % 64);
-          const uint4 zv = *reinterpret_cast<const uint4*>(addr);
-          const uint32_t w[4] = {zv.x, zv.y, zv.z, zv.w};
-          uint32_t out[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int i = q8 * 8 + 2 * e;
-            const float d0 = keep ? __uint_as_float(vo[i]) : 0.f;
-            const float d1 = keep ? __uint_as_float(vo[i + 1]) : 0.f;
-            out[e] = pack_bf16(bf16_lo(w[e]) + d0, bf16_hi(w[e]) + d1);
-          }
-          *reinterpret_cast<uint4*>(addr) = make_uint4(out[0], out[1], out[2], out[3]);
+        for (int i = 0; i < 32; ++i) {
+          const int pp = p0 + i;
+          __nv_bfloat16* addr = reinterpret_cast<__nv_bfloat16*>(zt + kb * (kOTile * 128) + sw128_offset(pp, cc));
+          *addr = __float2bfloat16_rn(__bfloat162float(*addr) + __uint_as_float(vd[i]) * s.keep[buf][pp]);
         }
       }
+      tc_fence_before();
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&s.acc_free[buf]);
+        mbar_arrive(&s.st_free[buf]);
+      }
+      ok = !named_barrier_or(1, 256, !ok);
+      if (warp == 4 && lane == 0) {
+        if (ok) {
+          const int c0 = (tile % tiles_per_row) * kOTile;
+          const int rr = tile / tiles_per_row;
+          tma_store_3d(&map_out, zt, 0, c0, rr);
+          tma_store_3d(&map_out, zt + kOTile * 128, 64, c0, rr);
+          tma_store_commit();
+          tma_store_wait_read0();
+        }
+        mbar_arrive(&s.empty[st]);
+      }
+      if (!ok) break;
     }
-    tc_fence_before();
-    fence_async_smem();
-    ok = !named_barrier_or(1 + g, 128, !ok || !got || !got2);
-    if (gt == 0 && ok) {
-      tma_store_3d(&map_out, zt, 0, c0, rr);
-      tma_store_3d(&map_out, zt + 16384, 64, c0, rr);
-      tma_store_commit();
-    }
-    if (!ok) break;
-  }
-  if (gt == 0) {
-    tma_store_wait_all0();
-    if (load_pending) mbar_wait(&s.full[g], it & 1, p.err, kErrTimeoutLoad);
+    if (warp == 4 && lane == 0) tma_store_wait_all0();
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(s.tmem_base, 512);
+    tmem_dealloc(tmem0, 256);
   }
 }
 
@@ -923,7 +1010,7 @@ int triattn_forward(const void* z, const uint8_t* mask, const void* packed, void
   // 3. output
   if (stages & 4) {
     CUtensorMap map_z, map_o, map_out;
-    const uint32_t box[3] = {64, kTile, 1};
+    const uint32_t box[3] = {64, kOTile, 1};
     st = make_map(&map_z, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, z, zdims, zstrides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
     st = make_map(&map_o, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ws.o, zdims, zstrides, box, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -931,12 +1018,11 @@ int triattn_forward(const void* z, const uint8_t* mask, const void* packed, void
     st = make_map(&map_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out, zdims, zstrides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
     OutParams op{static_cast<const uint8_t*>(packed), mask, B, N, masked_zero, info.err};
-    const int tiles = B * N * ((N + kTile - 1) / kTile);
-    const int groups = (tiles + kGroups - 1) / kGroups;
-    const int grid = groups < info.num_sms ? groups : info.num_sms;
+    const int tiles = B * N * ((N + kOTile - 1) / kOTile);
+    const int grid = tiles < info.num_sms ? tiles : info.num_sms;
     const size_t smem = sizeof(OutSmem) + 1024;
     cudaFuncSetAttribute(triattn_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    triattn_out_kernel<<<grid, 256, smem, stream>>>(map_z, map_o, map_out, op);
+    triattn_out_kernel<<<grid, kOThreads, smem, stream>>>(map_z, map_o, map_out, op);
     return cuda_status(static_cast<int>(cudaGetLastError()), "triattn_out launch");
   }
   return 0;
