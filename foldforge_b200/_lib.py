@@ -112,7 +112,7 @@ def load() -> ctypes.CDLL:
 #: kernels each forward entry point launches (the bench's count of this library's launches)
 LAUNCHES = {
     "ffb_layernorm_fwd": 1, "ffb_gemm_bf16_nt": 1, "ffb_trimul_fwd": 3, "ffb_triattn_fwd": 3,
-    "ffb_transition_fwd": 1, "ffb_apb_fwd": 6, "ffb_single_transition_fwd": 3,
+    "ffb_transition_fwd": 1, "ffb_apb_fwd": 5, "ffb_single_transition_fwd": 3,
 }
 launch_count = 0
 

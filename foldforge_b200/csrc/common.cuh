@@ -308,6 +308,38 @@ __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t col) {
 __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 
+// LayerNorm statistics (mean, 1/sqrt(var + 1e-5)) of row `row` of a K-major SW128 tile of
+// 128 bf16 channels stored as two 64-channel blocks `block_bytes` apart (two-pass variance
+// over the row held in registers).
+__device__ __forceinline__ void ln_stats_c128(const uint8_t* tile, int block_bytes, int row, float& mean,
+                                              float& rstd) {
+  float s = 0.f;
+  uint4 v[16];
+#pragma unroll
+  for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      v[kb * 8 + q] = *reinterpret_cast<const uint4*>(tile + kb * block_bytes + sw128_offset(row, q * 8));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) s += bf16_lo(w[j]) + bf16_hi(w[j]);
+  }
+  mean = s * (1.0f / 128.0f);
+  float q2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float a = bf16_lo(w[j]) - mean, b = bf16_hi(w[j]) - mean;
+      q2 += a * a + b * b;
+    }
+  }
+  rstd = rsqrtf(q2 * (1.0f / 128.0f) + 1e-5f);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);

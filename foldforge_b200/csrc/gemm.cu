@@ -63,33 +63,84 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int b, int m
       reinterpret_cast<uint4*>(dst)[0] = w0;
       reinterpret_cast<uint4*>(dst)[1] = w1;
     } else {
-      for (int i = 0; i < 16 && h0 + i < out_cols; ++i) dst[i] = __float2bfloat16_rn(out[i]);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (h0 + i < out_cols) dst[i] = __float2bfloat16_rn(out[i]);
     }
     return;
   }
+  const bool full = (n0 + 32 <= p.N);
   float acc[32];
+  if (p.bias != nullptr && full && (reinterpret_cast<uintptr_t>(p.bias + n0) & 15u) == 0) {
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    float x = __uint_as_float(v[i]);
-    if (p.bias != nullptr && n0 + i < p.N) x += p.bias[n0 + i];
-    acc[i] = x;
+    for (int i = 0; i < 32; i += 4) {
+      const float4 bb = *reinterpret_cast<const float4*>(p.bias + n0 + i);
+      acc[i] = __uint_as_float(v[i]) + bb.x;
+      acc[i + 1] = __uint_as_float(v[i + 1]) + bb.y;
+      acc[i + 2] = __uint_as_float(v[i + 2]) + bb.z;
+      acc[i + 3] = __uint_as_float(v[i + 3]) + bb.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      float x = __uint_as_float(v[i]);
+      if (p.bias != nullptr && n0 + i < p.N) x += p.bias[n0 + i];
+      acc[i] = x;
+    }
   }
   float rowscale = 1.0f;
   if (p.row_mask != nullptr) rowscale = p.row_mask[static_cast<int64_t>(b) * p.M + m] ? 1.0f : 0.0f;
   const int64_t off = static_cast<int64_t>(b) * p.batch_stride_d + static_cast<int64_t>(m) * p.ldd + n0;
-  const bool full = (n0 + 32 <= p.N);
   if (p.epilogue == kEpiResidual) {
-    // D = R + acc * rowscale, R and D share the layout and dtype
+    // D = R + acc * rowscale, R and D share the layout and dtype. All of the chunk's residual
+    // values are read before the first store (R may alias D), 16 bytes at a time when the
+    // chunk is whole and aligned.
     if (p.d_is_f32) {
       const float* r = reinterpret_cast<const float*>(p.residual) + off;
       float* d = reinterpret_cast<float*>(p.D) + off;
-      for (int i = 0; i < 32; ++i)
-        if (n0 + i < p.N) d[i] = r[i] + acc[i] * rowscale;
+      if (full && ((reinterpret_cast<uintptr_t>(r) | reinterpret_cast<uintptr_t>(d)) & 15u) == 0) {
+        float4 rv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) rv[i] = reinterpret_cast<const float4*>(r)[i];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          reinterpret_cast<float4*>(d)[i] =
+              make_float4(fmaf(acc[4 * i], rowscale, rv[i].x), fmaf(acc[4 * i + 1], rowscale, rv[i].y),
+                          fmaf(acc[4 * i + 2], rowscale, rv[i].z), fmaf(acc[4 * i + 3], rowscale, rv[i].w));
+      } else {
+        float rv[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) rv[i] = (n0 + i < p.N) ? r[i] : 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (n0 + i < p.N) d[i] = fmaf(acc[i], rowscale, rv[i]);
+      }
     } else {
       const __nv_bfloat16* r = reinterpret_cast<const __nv_bfloat16*>(p.residual) + off;
       __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + off;
-      for (int i = 0; i < 32; ++i)
-        if (n0 + i < p.N) d[i] = __float2bfloat16_rn(__bfloat162float(r[i]) + acc[i] * rowscale);
+      if (full && ((reinterpret_cast<uintptr_t>(r) | reinterpret_cast<uintptr_t>(d)) & 15u) == 0) {
+        uint4 rv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) rv[i] = reinterpret_cast<const uint4*>(r)[i];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t w[4] = {rv[i].x, rv[i].y, rv[i].z, rv[i].w};
+          uint32_t o[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int e = 8 * i + 2 * k;
+            o[k] = pack_bf16(fmaf(acc[e], rowscale, bf16_lo(w[k])), fmaf(acc[e + 1], rowscale, bf16_hi(w[k])));
+          }
+          reinterpret_cast<uint4*>(d)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      } else {
+        float rv[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) rv[i] = (n0 + i < p.N) ? __bfloat162float(r[i]) : 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (n0 + i < p.N) d[i] = __float2bfloat16_rn(fmaf(acc[i], rowscale, rv[i]));
+      }
     }
     return;
   }

@@ -1,14 +1,16 @@
 // Single track of the Pairformer block: attention with pair bias and the single
 // transition (c_s = 384, 16 heads x 24, factor 4). Both are small next to the pair ops
 // (about 1% of a block's flops at N = 512) and are composed from the library's tcgen05
-// GEMM and LayerNorm launchers plus one attention kernel:
+// GEMM and LayerNorm launchers plus two kernels of their own:
 //
 // attention with pair bias (legacy/pairformer.py:204-226, legacy/transformer.py:88-133):
-//   pb[h, b, i, j] = W_pb (gamma_pair * LNhat(z[b, i, j]))     LayerNorm + GEMM (16 rows)
+//   pb[h, b, i, j] = W_pb (gamma_pair * LNhat(z[b, i, j]))     pair_bias_kernel (tcgen05,
+//                                                              LayerNorm folded, reads z once)
 //   y = LN(s);  [q | k | v | g] = y W^T + [b_q | 0 | 0 | 0]     GEMM (N = 1536)
 //   o = softmax_j(q_i . k_j / sqrt(24) + pb[i, j, h] (+ extra[h, i, j]), key mask) v_j
 //   s' = s + W_o (sigmoid(g + gate_bias) * o)                    GEMM with residual epilogue
 // single transition: s' = s + W_sq (silu(W_a LN(s)) * W_b LN(s))  (SwiGLU GEMM epilogue)
+#include "../../include/foldforge_b200.h"
 #include "abi_util.h"
 #include "common.cuh"
 #include "kernels.h"
@@ -48,27 +50,256 @@ int to_bf16(const float* a, const float* b, int rows_each, int cols, int interle
   return static_cast<int>(cudaGetLastError());
 }
 
+// ---------------------------------------------------------------- pair bias
+// pb[h][p] = W_pb[h] . (gamma * LNhat(z[p])) for every pair p of the B * N * N rows of z,
+// head-major ([h][b][i][j]). The LayerNorm is folded: W' = bf16(W_pb diag gamma) and
+// wsum[h] = sum_c W'[h][c], so pb = rstd * (W' z - mean * wsum) on RAW z (the LayerNorm
+// offset beta adds one constant per head to every logit of a row, which the softmax
+// cancels). Persistent, warp-specialised, 128-pair tiles:
+//   warp 0      TMA: z tiles (two 64-channel SW128 blocks) through a 4-stage ring
+//   warp 1      MMA: acc[p][h] = z[p] . W'[h] (M = 128 pairs, N = 16 heads, K = 128),
+//               double-buffered in TMEM
+//   warps 2-5   lane = pair: LayerNorm statistics from the staged tile, then the epilogue;
+//               a warp's 32 pairs of one head are one coalesced 128-byte store
+constexpr int kPbTile = 128;
+constexpr int kPbStages = 4;
+constexpr int kPbThreads = 192;
+constexpr uint32_t kPbWBytes = 2 * kHs * 128;  // W' image: two 64-channel blocks of 16 rows
+
+struct PbSmem {
+  alignas(1024) uint8_t z[kPbStages][2][kPbTile * 128];
+  alignas(1024) uint8_t w[kPbWBytes];
+  float wsum[kHs];
+  uint64_t full[kPbStages];
+  uint64_t empty[kPbStages];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t wbar;
+  uint32_t tmem_base;
+};
+
+__global__ void __launch_bounds__(kPbThreads, 1)
+    pair_bias_kernel(const __grid_constant__ CUtensorMap map_z, const uint8_t* __restrict__ w_img,
+                     const float* __restrict__ wsum, float* __restrict__ pb, int64_t P, int* err) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  PbSmem& s = *reinterpret_cast<PbSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                         ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int64_t tiles = (P + kPbTile - 1) / kPbTile;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kPbStages; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1 + 4);  // the MMA commit and the four statistics warps
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.acc_full[i], 1);
+      mbar_init(&s.acc_empty[i], 4);
+    }
+    mbar_init(&s.wbar, 1);
+    fence_mbar_init();
+  }
+  if (threadIdx.x < kHs) s.wsum[threadIdx.x] = wsum[threadIdx.x];
+  if (warp == 1) {
+    tmem_alloc(&s.tmem_base, 32);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) tma_prefetch_map(&map_z);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&s.wbar, kPbWBytes);
+      bulk_load(s.w, w_img, kPbWBytes, &s.wbar);
+      int it = 0;
+      for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
+        const int st = it % kPbStages;
+        if (!mbar_wait(&s.empty[st], ((it / kPbStages) & 1) ^ 1, err, kErrTimeoutEmpty)) break;
+        mbar_arrive_expect_tx(&s.full[st], 2 * kPbTile * 128);
+        const int y = static_cast<int>(t * kPbTile);
+        tma_load_2d(s.z[st][0], &map_z, &s.full[st], 0, y);
+        tma_load_2d(s.z[st][1], &map_z, &s.full[st], 64, y);
+      }
+      // every issued copy lands before the CTA may exit
+      mbar_wait(&s.wbar, 0, err, kErrTimeoutLoad);
+      for (int k = 0; k < kPbStages && k < it; ++k) {
+        const int j = it - 1 - k;
+        mbar_wait(&s.full[j % kPbStages], (j / kPbStages) & 1, err, kErrTimeoutLoad);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && mbar_wait(&s.wbar, 0, err, kErrTimeoutLoad)) {
+      const uint32_t idesc = idesc_bf16_f32(kPbTile, kHs);
+      int it = 0;
+      for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
+        const int st = it % kPbStages, acc = it & 1;
+        if (!mbar_wait(&s.acc_empty[acc], ((it >> 1) & 1) ^ 1, err, kErrTimeoutEmpty)) break;
+        if (!mbar_wait(&s.full[st], (it / kPbStages) & 1, err, kErrTimeoutLoad)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + acc * kHs;
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb) {
+          const uint64_t da = desc_kmajor_sw128(smem_u32(s.z[st][kb]));
+          const uint64_t db = desc_kmajor_sw128(smem_u32(s.w + kb * kHs * 128));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) mma_bf16(d, da + 2 * kk, db + 2 * kk, idesc, (kb | kk) != 0);
+        }
+        mma_commit(&s.empty[st]);
+        mma_commit(&s.acc_full[acc]);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may read
+    const int row = quarter * 32 + lane;
+    int it = 0;
+    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
+      const int st = it % kPbStages, acc = it & 1;
+      bool ok = mbar_wait(&s.full[st], (it / kPbStages) & 1, err, kErrTimeoutLoad);
+      if (!__all_sync(0xFFFFFFFFu, ok)) break;
+      float mean, rstd;
+      ln_stats_c128(s.z[st][0], kPbTile * 128, row, mean, rstd);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.empty[st]);
+      ok = mbar_wait(&s.acc_full[acc], (it >> 1) & 1, err, kErrTimeoutMma);
+      if (!__all_sync(0xFFFFFFFFu, ok)) break;
+      tc_fence_after();
+      uint32_t v[16];
+      tmem_ld16(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kHs, v);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.acc_empty[acc]);
+      const int64_t p = t * kPbTile + row;
+      if (p < P) {
+#pragma unroll
+        for (int h = 0; h < kHs; ++h) pb[h * P + p] = rstd * (__uint_as_float(v[h]) - mean * s.wsum[h]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 32);
+  }
+}
+
 // ---------------------------------------------------------------- attention kernel
-// A CTA per (batch, head, 32 queries), 4 warps. Lane = query; warp w takes keys w*16 ..
-// w*16+15 of every 64-key chunk, which is staged once per CTA in shared memory: keys and
-// values (fp32) and the pair-bias tile [32 q][64 k] (head-major bias, coalesced rows, padded
-// rows so that lanes reading one key hit distinct banks). Each warp keeps a private exact
-// online softmax per query; the four partial states are merged at the end. Masked keys get
-// the reference's REPLACED logit -1e9, so a row whose keys are all masked averages
-// uniformly; keys past N do not exist.
+// A CTA per (batch, head, 32 queries), 8 warps. Lane = query; warp w takes keys w*8 ..
+// w*8+7 of every 64-key chunk. Chunks are staged in shared memory (keys and values as fp32,
+// the pair-bias tile [32 q][64 k] from the head-major bias with padded rows so lanes
+// reading one key hit distinct banks) through two buffers: the global loads of chunk c + 1
+// are issued before the warps work on chunk c and land in the other buffer afterwards, one
+// barrier per chunk. Each warp keeps an exact online softmax per query, updated once per 8
+// keys; the eight partial states are merged at the end. Masked keys get the reference's
+// REPLACED logit -1e9, so a row whose keys are all masked averages uniformly; keys past N
+// do not exist.
 constexpr int kQ = 32;        // queries per CTA
 constexpr int kKC = 64;       // keys per staged chunk
-constexpr int kWarps = 4;
+constexpr int kWarps = 8;
 constexpr int kKPW = kKC / kWarps;
+constexpr int kAttnThreads = kQ * kWarps;
+constexpr int kBiasPitch = kKC + 1;
+constexpr int kBufFloats = 2 * kKC * kDs + kQ * kBiasPitch + kKC;  // keys, values, bias, keep
+constexpr int kPartPitch = kDs + 2;
+static_assert(kWarps * kQ * kPartPitch <= 2 * kBufFloats, "merge scratch must fit the chunk buffers");
+static_assert(kKC * 6 <= 2 * kAttnThreads && kQ * kKC / 4 == 2 * kAttnThreads, "staging assignment");
 
-__global__ void __launch_bounds__(kQ * kWarps) single_attention_kernel(
+struct ChunkRegs {
+  uint4 kv[2];     // key / value vectors (8 bf16 each)
+  float4 bias[2];  // four bias values each
+  float keep;
+};
+
+__device__ __forceinline__ void attn_load_chunk(ChunkRegs& r, const __nv_bfloat16* __restrict__ qkvg,
+                                                const float* __restrict__ pb, const void* __restrict__ extra,
+                                                int extra_f32, const uint8_t* __restrict__ mask, int b, int h,
+                                                int qb, int N, int j0) {
+  const int t = threadIdx.x;
+  const int nk = N - j0 < kKC ? N - j0 : kKC;
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int e = t + u * kAttnThreads;
+    r.kv[u] = make_uint4(0u, 0u, 0u, 0u);
+    if (e < kKC * 6) {
+      const int j = e / 6, part = e % 6;  // part 0-2: key vectors, 3-5: value vectors
+      if (j < nk)
+        r.kv[u] = *reinterpret_cast<const uint4*>(qkvg + (static_cast<int64_t>(b) * N + j0 + j) * (4 * kCs) +
+                                                  (part < 3 ? kCs : 2 * kCs) + h * kDs + (part % 3) * 8);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int e = t + u * kAttnThreads;
+    const int qq = e / (kKC / 4), j = (e % (kKC / 4)) * 4;
+    const int ii = qb * kQ + qq;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (ii < N) {
+      const float* src = pb + static_cast<int64_t>(ii) * N + j0 + j;
+      if (j + 4 <= nk && (reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+        const float4 f = *reinterpret_cast<const float4*>(src);
+        v[0] = f.x;
+        v[1] = f.y;
+        v[2] = f.z;
+        v[3] = f.w;
+      } else {
+        for (int i = 0; i < 4; ++i)
+          if (j + i < nk) v[i] = src[i];
+      }
+      if (extra != nullptr) {
+        for (int i = 0; i < 4 && j + i < nk; ++i) {
+          const int64_t x = ((static_cast<int64_t>(b) * kHs + h) * N + ii) * N + j0 + j + i;
+          v[i] += extra_f32 ? static_cast<const float*>(extra)[x]
+                            : __bfloat162float(static_cast<const __nv_bfloat16*>(extra)[x]);
+        }
+      }
+    }
+    r.bias[u] = make_float4(v[0], v[1], v[2], v[3]);
+  }
+  r.keep = 0.f;
+  if (t < kKC) r.keep = (t < nk) ? (mask[static_cast<int64_t>(b) * N + j0 + t] ? 1.f : 0.f) : -1.f;
+}
+
+__device__ __forceinline__ void attn_store_chunk(const ChunkRegs& r, float* buf) {
+  float* ks = buf;
+  float* vs = buf + kKC * kDs;
+  float* bias = vs + kKC * kDs;
+  float* keep = bias + kQ * kBiasPitch;
+  const int t = threadIdx.x;
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int e = t + u * kAttnThreads;
+    if (e < kKC * 6) {
+      const int j = e / 6, part = e % 6;
+      float* dst = (part < 3 ? ks : vs) + j * kDs + (part % 3) * 8;
+      const uint32_t w[4] = {r.kv[u].x, r.kv[u].y, r.kv[u].z, r.kv[u].w};
+      float4 lo, hi;
+      lo.x = bf16_lo(w[0]); lo.y = bf16_hi(w[0]); lo.z = bf16_lo(w[1]); lo.w = bf16_hi(w[1]);
+      hi.x = bf16_lo(w[2]); hi.y = bf16_hi(w[2]); hi.z = bf16_lo(w[3]); hi.w = bf16_hi(w[3]);
+      reinterpret_cast<float4*>(dst)[0] = lo;
+      reinterpret_cast<float4*>(dst)[1] = hi;
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int e = t + u * kAttnThreads;
+    const int qq = e / (kKC / 4), j = (e % (kKC / 4)) * 4;
+    float* dst = bias + qq * kBiasPitch + j;
+    dst[0] = r.bias[u].x;
+    dst[1] = r.bias[u].y;
+    dst[2] = r.bias[u].z;
+    dst[3] = r.bias[u].w;
+  }
+  if (t < kKC) keep[t] = r.keep;
+}
+
+__global__ void __launch_bounds__(kAttnThreads, 2) single_attention_kernel(
     const __nv_bfloat16* __restrict__ qkvg, const float* __restrict__ pair_bias_hm, const void* __restrict__ extra,
     int extra_f32, const uint8_t* __restrict__ mask, float gate_bias, __nv_bfloat16* __restrict__ out, int B, int N) {
-  __shared__ float ks[kKC][kDs];
-  __shared__ float vs[kKC][kDs];
-  __shared__ float bias[kQ][kKC + 1];
-  __shared__ float keep[kKC];
-  __shared__ float part[kWarps][kQ][kDs + 2];
+  __shared__ __align__(16) float smem[2 * kBufFloats];
   const int qblocks = (N + kQ - 1) / kQ;
   const int h = blockIdx.x % kHs;
   const int qb = (blockIdx.x / kHs) % qblocks;
@@ -80,99 +311,123 @@ __global__ void __launch_bounds__(kQ * kWarps) single_attention_kernel(
   const float scale = rsqrtf(static_cast<float>(kDs));
   float q[kDs];
 #pragma unroll
-  for (int d = 0; d < kDs; ++d) q[d] = __bfloat162float(row_i[h * kDs + d]) * scale;
+  for (int u = 0; u < 3; ++u) {
+    const uint4 v = *reinterpret_cast<const uint4*>(row_i + h * kDs + u * 8);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      q[u * 8 + 2 * k] = bf16_lo(w[k]) * scale;
+      q[u * 8 + 2 * k + 1] = bf16_hi(w[k]) * scale;
+    }
+  }
   float m = -1.0e30f, l = 0.f;
   float o[kDs];
 #pragma unroll
   for (int d = 0; d < kDs; ++d) o[d] = 0.f;
   // head-major bias: [h][b][i][j]
   const float* pb = pair_bias_hm + (static_cast<int64_t>(h) * B + b) * static_cast<int64_t>(N) * N;
-  for (int j0 = 0; j0 < N; j0 += kKC) {
-    const int nk = N - j0 < kKC ? N - j0 : kKC;
-    __syncthreads();
-    for (int e = threadIdx.x; e < kKC * kDs; e += kQ * kWarps) {
-      const int j = e / kDs, d = e % kDs;
-      float kv = 0.f, vv = 0.f;
-      if (j < nk) {
-        const __nv_bfloat16* rj = qkvg + (static_cast<int64_t>(b) * N + j0 + j) * (4 * kCs) + h * kDs + d;
-        kv = __bfloat162float(rj[kCs]);
-        vv = __bfloat162float(rj[2 * kCs]);
-      }
-      ks[j][d] = kv;
-      vs[j][d] = vv;
-    }
-    for (int e = threadIdx.x; e < kQ * kKC; e += kQ * kWarps) {
-      const int qq = e / kKC, j = e % kKC;
-      const int ii = qb * kQ + qq;
-      float v = 0.f;
-      if (ii < N && j < nk) {
-        v = pb[static_cast<int64_t>(ii) * N + j0 + j];
-        if (extra != nullptr) {
-          const int64_t x = ((static_cast<int64_t>(b) * kHs + h) * N + ii) * N + j0 + j;
-          v += extra_f32 ? static_cast<const float*>(extra)[x]
-                         : __bfloat162float(static_cast<const __nv_bfloat16*>(extra)[x]);
-        }
-      }
-      bias[qq][j] = v;
-    }
-    for (int j = threadIdx.x; j < kKC; j += kQ * kWarps)
-      keep[j] = (j < nk) ? (mask[static_cast<int64_t>(b) * N + j0 + j] ? 1.f : 0.f) : -1.f;
-    __syncthreads();
-#pragma unroll 2
+  const int chunks = (N + kKC - 1) / kKC;
+  {
+    ChunkRegs r;
+    attn_load_chunk(r, qkvg, pb, extra, extra_f32, mask, b, h, qb, N, 0);
+    attn_store_chunk(r, smem);
+  }
+  __syncthreads();
+  for (int c = 0; c < chunks; ++c) {
+    const bool next = c + 1 < chunks;
+    ChunkRegs r;
+    if (next) attn_load_chunk(r, qkvg, pb, extra, extra_f32, mask, b, h, qb, N, (c + 1) * kKC);
+    const float* buf = smem + (c & 1) * kBufFloats;
+    const float* ks = buf;
+    const float* vs = buf + kKC * kDs;
+    const float* bias = vs + kKC * kDs;
+    const float* keep = bias + kQ * kBiasPitch;
+    float x[kKPW];
+    float mx = -INFINITY;
+#pragma unroll
     for (int jj = 0; jj < kKPW; ++jj) {
       const int j = warp * kKPW + jj;
-      const float kp = keep[j];
-      if (kp < 0.f) continue;  // past N (uniform across the warp)
+      const float4* kr = reinterpret_cast<const float4*>(ks + j * kDs);
       float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll
-      for (int d = 0; d < kDs; d += 4) {
-        a0 += q[d] * ks[j][d];
-        a1 += q[d + 1] * ks[j][d + 1];
-        a2 += q[d + 2] * ks[j][d + 2];
-        a3 += q[d + 3] * ks[j][d + 3];
+      for (int u = 0; u < kDs / 4; ++u) {
+        const float4 kk = kr[u];
+        a0 = fmaf(q[4 * u], kk.x, a0);
+        a1 = fmaf(q[4 * u + 1], kk.y, a1);
+        a2 = fmaf(q[4 * u + 2], kk.z, a2);
+        a3 = fmaf(q[4 * u + 3], kk.w, a3);
       }
-      float x = (a0 + a1) + (a2 + a3) + bias[lane][j];
-      if (kp == 0.f) x = -1.0e9f;
-      if (x > m) {
-        const float alpha = __expf(m - x);
-        l *= alpha;
-#pragma unroll
-        for (int d = 0; d < kDs; ++d) o[d] *= alpha;
-        m = x;
-      }
-      const float p = __expf(x - m);
-      l += p;
-#pragma unroll
-      for (int d = 0; d < kDs; ++d) o[d] += p * vs[j][d];
+      const float kp = keep[j];
+      float xv = (a0 + a1) + (a2 + a3) + bias[lane * kBiasPitch + j];
+      if (kp == 0.f) xv = -1.0e9f;
+      if (kp < 0.f) xv = -INFINITY;  // past N
+      x[jj] = xv;
+      mx = fmaxf(mx, xv);
     }
-  }
-  // merge the four warps' partial softmax states per query
+    const float m_new = fmaxf(m, mx);
+    const float alpha = __expf(m - m_new);
+    l *= alpha;
 #pragma unroll
-  for (int d = 0; d < kDs; ++d) part[warp][lane][d] = o[d];
-  part[warp][lane][kDs] = m;
-  part[warp][lane][kDs + 1] = l;
+    for (int d = 0; d < kDs; ++d) o[d] *= alpha;
+#pragma unroll
+    for (int jj = 0; jj < kKPW; ++jj) {
+      const int j = warp * kKPW + jj;
+      const float p = __expf(x[jj] - m_new);
+      l += p;
+      const float4* vr = reinterpret_cast<const float4*>(vs + j * kDs);
+#pragma unroll
+      for (int u = 0; u < kDs / 4; ++u) {
+        const float4 vv = vr[u];
+        o[4 * u] = fmaf(p, vv.x, o[4 * u]);
+        o[4 * u + 1] = fmaf(p, vv.y, o[4 * u + 1]);
+        o[4 * u + 2] = fmaf(p, vv.z, o[4 * u + 2]);
+        o[4 * u + 3] = fmaf(p, vv.w, o[4 * u + 3]);
+      }
+    }
+    m = m_new;
+    if (next) attn_store_chunk(r, smem + ((c + 1) & 1) * kBufFloats);
+    __syncthreads();
+  }
+  // merge the warps' partial softmax states per query (scratch aliases the chunk buffers;
+  // the loop's last barrier ended every read of them)
+  float* part = smem;
+#pragma unroll
+  for (int d = 0; d < kDs; ++d) part[(warp * kQ + lane) * kPartPitch + d] = o[d];
+  part[(warp * kQ + lane) * kPartPitch + kDs] = m;
+  part[(warp * kQ + lane) * kPartPitch + kDs + 1] = l;
   __syncthreads();
   if (warp != 0 || i >= N) return;
   float mm = -1.0e30f;
-  for (int w = 0; w < kWarps; ++w)
-    if (part[w][lane][kDs + 1] > 0.f) mm = fmaxf(mm, part[w][lane][kDs]);
+  for (int w = 0; w < kWarps; ++w) {
+    const float* pw = part + (w * kQ + lane) * kPartPitch;
+    if (pw[kDs + 1] > 0.f) mm = fmaxf(mm, pw[kDs]);
+  }
   float ll = 0.f, acc[kDs];
 #pragma unroll
   for (int d = 0; d < kDs; ++d) acc[d] = 0.f;
   for (int w = 0; w < kWarps; ++w) {
-    const float lw = part[w][lane][kDs + 1];
+    const float* pw = part + (w * kQ + lane) * kPartPitch;
+    const float lw = pw[kDs + 1];
     if (lw <= 0.f) continue;
-    const float f = __expf(part[w][lane][kDs] - mm);
+    const float f = __expf(pw[kDs] - mm);
     ll += lw * f;
 #pragma unroll
-    for (int d = 0; d < kDs; ++d) acc[d] += part[w][lane][d] * f;
+    for (int d = 0; d < kDs; ++d) acc[d] = fmaf(pw[d], f, acc[d]);
   }
   const float inv = 1.0f / ll;
   __nv_bfloat16* dst = out + (static_cast<int64_t>(b) * N + i) * kCs + h * kDs;
 #pragma unroll
-  for (int d = 0; d < kDs; ++d) {
-    const float g = __bfloat162float(row_i[3 * kCs + h * kDs + d]) + gate_bias;
-    dst[d] = __float2bfloat16_rn(acc[d] * inv * sigmoidf_(g));
+  for (int u = 0; u < 3; ++u) {
+    const uint4 gv = *reinterpret_cast<const uint4*>(row_i + 3 * kCs + h * kDs + u * 8);
+    const uint32_t w[4] = {gv.x, gv.y, gv.z, gv.w};
+    uint32_t ov[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int d = u * 8 + 2 * k;
+      ov[k] = pack_bf16(acc[d] * inv * sigmoidf_(bf16_lo(w[k]) + gate_bias),
+                        acc[d + 1] * inv * sigmoidf_(bf16_hi(w[k]) + gate_bias));
+    }
+    reinterpret_cast<uint4*>(dst)[u] = make_uint4(ov[0], ov[1], ov[2], ov[3]);
   }
 }
 
@@ -212,7 +467,7 @@ size_t a256(size_t x) { return (x + 255) / 256 * 256; }
 
 // packed attention-with-pair-bias image
 struct ApbLayout {
-  size_t w_qkvg, b_qkvg, w_o, w_pb, ln_s_w, ln_s_b, ln_p_w, total;
+  size_t w_qkvg, b_qkvg, w_o, w_pb, pb_wsum, ln_s_w, ln_s_b, total;
 };
 ApbLayout apb_layout() {
   ApbLayout L;
@@ -220,10 +475,10 @@ ApbLayout apb_layout() {
   L.w_qkvg = o;  o = a256(o + static_cast<size_t>(4 * kCs) * kCs * 2);
   L.b_qkvg = o;  o = a256(o + 4 * kCs * 4);
   L.w_o = o;     o = a256(o + static_cast<size_t>(kCs) * kCs * 2);
-  L.w_pb = o;    o = a256(o + kHs * kCz * 2);
+  L.w_pb = o;    o = a256(o + kPbWBytes);  // W_pb diag(gamma_pair), SW128 image
+  L.pb_wsum = o; o = a256(o + kHs * 4);
   L.ln_s_w = o;  o = a256(o + kCs * 4);
   L.ln_s_b = o;  o = a256(o + kCs * 4);
-  L.ln_p_w = o;  o = a256(o + kCz * 4);
   L.total = o;
   return L;
 }
@@ -248,7 +503,7 @@ size_t apb_packed_bytes() { return apb_layout().total; }
 
 size_t apb_workspace_bytes(int B, int N) {
   const size_t P = static_cast<size_t>(B) * N * N, T = static_cast<size_t>(B) * N;
-  return a256(P * kCz * 2) + a256(P * kHs * 4) + a256(T * kCs * 2) + a256(T * 4 * kCs * 2) + a256(T * kCs * 2);
+  return a256(P * kHs * 4) + a256(T * kCs * 2) + a256(T * 4 * kCs * 2) + a256(T * kCs * 2);
 }
 
 int apb_prepare(const ApbWeights& w, void* packed, cudaStream_t stream) {
@@ -260,10 +515,11 @@ int apb_prepare(const ApbWeights& w, void* packed, cudaStream_t stream) {
     rc = to_bf16(mats[i], nullptr, kCs, kCs, 0, img + L.w_qkvg + static_cast<size_t>(i) * kCs * kCs * 2, stream);
   if (rc == 0) rc = static_cast<int>(cudaMemcpyAsync(img + L.b_qkvg, w.query_bias, kCs * 4, cudaMemcpyDeviceToDevice, stream));
   if (rc == 0) rc = to_bf16(w.to_out, nullptr, kCs, kCs, 0, img + L.w_o, stream);
-  if (rc == 0) rc = to_bf16(w.to_bias, nullptr, kHs, kCz, 0, img + L.w_pb, stream);
+  if (rc == 0)
+    rc = launch_pack_weight(w.to_bias, kHs, kCz, w.ln_pair_w, nullptr, img + L.w_pb, 0, kHs,
+                            reinterpret_cast<float*>(img + L.pb_wsum), nullptr, stream);
   if (rc == 0) rc = static_cast<int>(cudaMemcpyAsync(img + L.ln_s_w, w.ln_single_w, kCs * 4, cudaMemcpyDeviceToDevice, stream));
   if (rc == 0) rc = static_cast<int>(cudaMemcpyAsync(img + L.ln_s_b, w.ln_single_b, kCs * 4, cudaMemcpyDeviceToDevice, stream));
-  if (rc == 0) rc = static_cast<int>(cudaMemcpyAsync(img + L.ln_p_w, w.ln_pair_w, kCz * 4, cudaMemcpyDeviceToDevice, stream));
   return rc;
 }
 
@@ -274,19 +530,29 @@ int apb_forward(const void* s, const void* z, const uint8_t* mask, const void* p
   const uint8_t* img = static_cast<const uint8_t*>(packed);
   const size_t P = static_cast<size_t>(B) * N * N, T = static_cast<size_t>(B) * N;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  void* zn = ws;
-  float* pb = reinterpret_cast<float*>(ws + a256(P * kCz * 2));
-  void* y = ws + a256(P * kCz * 2) + a256(P * kHs * 4);
+  float* pb = reinterpret_cast<float*>(ws);
+  void* y = ws + a256(P * kHs * 4);
   void* qkvg = static_cast<uint8_t*>(y) + a256(T * kCs * 2);
   void* gated = static_cast<uint8_t*>(qkvg) + a256(T * 4 * kCs * 2);
-  int st = cuda_status(launch_layernorm(z, zn, reinterpret_cast<const float*>(img + L.ln_p_w), nullptr,
-                                        static_cast<int64_t>(P), kCz, 1e-5f, 0, info.num_sms, stream),
-                       "apb pair layernorm");
+  // head-major pair bias from raw z (LayerNorm folded into the epilogue)
+  if (P >= (static_cast<size_t>(1) << 31))
+    return fail(FFB_ERR_UNSUPPORTED, "attention_pair_bias: %zu pairs exceed the 2^31 TMA row range", P);
+  CUtensorMap mz;
+  const uint64_t zdims[2] = {static_cast<uint64_t>(kCz), static_cast<uint64_t>(P)};
+  const uint64_t zstr[1] = {static_cast<uint64_t>(kCz) * 2};
+  const uint32_t zbox[2] = {64, kPbTile};
+  int st = make_map(&mz, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, z, zdims, zstr, zbox, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
-  // head-major pair bias pb[h][p] = W_pb[h] . zn[p]: the weight is the A operand (16 rows;
-  // the tile's other rows are zero-filled by TMA), the pairs are the N dimension
-  st = gemm(img + L.w_pb, zn, pb, kHs, static_cast<int>(P), kCz, 1, nullptr, kEpiStore, nullptr, nullptr, info, stream);
-  if (st) return st;
+  {
+    const int64_t tiles = static_cast<int64_t>((P + kPbTile - 1) / kPbTile);
+    const int grid = static_cast<int>(tiles < info.num_sms ? tiles : info.num_sms);
+    const size_t smem = sizeof(PbSmem) + 1024;
+    cudaFuncSetAttribute(pair_bias_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    pair_bias_kernel<<<grid, kPbThreads, smem, stream>>>(mz, img + L.w_pb, reinterpret_cast<const float*>(img + L.pb_wsum),
+                                                         pb, static_cast<int64_t>(P), info.err);
+    st = cuda_status(static_cast<int>(cudaGetLastError()), "pair bias launch");
+    if (st) return st;
+  }
   st = cuda_status(launch_layernorm(s, y, reinterpret_cast<const float*>(img + L.ln_s_w),
                                     reinterpret_cast<const float*>(img + L.ln_s_b), static_cast<int64_t>(T), kCs,
                                     1e-5f, 0, info.num_sms, stream),
@@ -296,7 +562,7 @@ int apb_forward(const void* s, const void* z, const uint8_t* mask, const void* p
             reinterpret_cast<const float*>(img + L.b_qkvg), kEpiStore, nullptr, nullptr, info, stream);
   if (st) return st;
   const int ctas = B * kHs * ((N + kQ - 1) / kQ);
-  single_attention_kernel<<<ctas, kQ * kWarps, 0, stream>>>(
+  single_attention_kernel<<<ctas, kAttnThreads, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(qkvg), pb, extra, extra_f32, mask, gate_bias,
       static_cast<__nv_bfloat16*>(gated), B, N);
   st = cuda_status(static_cast<int>(cudaGetLastError()), "single attention launch");

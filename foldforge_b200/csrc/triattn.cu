@@ -52,63 +52,9 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// LayerNorm statistics of row `row` of a 128-row tile stored as two SW128 channel blocks.
 __device__ __forceinline__ void tile_stats(const uint8_t* tile, int row, float& mean, float& rstd) {
-  float s = 0.f;
-  uint4 v[16];
-#pragma unroll
-  for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-    for (int q = 0; q < 8; ++q)
-      v[kb * 8 + q] = *reinterpret_cast<const uint4*>(tile + kb * 16384 + sw128_offset(row, q * 8));
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) s += bf16_lo(w[j]) + bf16_hi(w[j]);
-  }
-  mean = s * (1.0f / kC);
-  float q2 = 0.f;
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float a = bf16_lo(w[j]) - mean, b = bf16_hi(w[j]) - mean;
-      q2 += a * a + b * b;
-    }
-  }
-  rstd = rsqrtf(q2 * (1.0f / kC) + 1e-5f);
-}
-
-// LayerNorm statistics of row `row` of a K-major SW128 tile of 128 channels stored as two
-// 64-channel blocks `block_bytes` apart.
-__device__ __forceinline__ void tile_stats_rows(const uint8_t* tile, int block_bytes, int row, float& mean,
-                                                float& rstd) {
-  float s = 0.f;
-  uint4 v[16];
-#pragma unroll
-  for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-    for (int q = 0; q < 8; ++q)
-      v[kb * 8 + q] = *reinterpret_cast<const uint4*>(tile + kb * block_bytes + sw128_offset(row, q * 8));
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) s += bf16_lo(w[j]) + bf16_hi(w[j]);
-  }
-  mean = s * (1.0f / kC);
-  float q2 = 0.f;
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float a = bf16_lo(w[j]) - mean, b = bf16_hi(w[j]) - mean;
-      q2 += a * a + b * b;
-    }
-  }
-  rstd = rsqrtf(q2 * (1.0f / kC) + 1e-5f);
+  ln_stats_c128(tile, 16384, row, mean, rstd);
 }
 
 // ====================================================================== 1. projection
@@ -771,7 +717,7 @@ __global__ void __launch_bounds__(kOThreads, 1)
       const bool w2 = mbar_wait(&s.st_free[buf], ((it >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty);
       if (!__all_sync(0xFFFFFFFFu, w1 && w2)) break;
       float mean, rstd;
-      tile_stats_rows(s.z[st], kOTile * 128, t, mean, rstd);
+      ln_stats_c128(s.z[st], kOTile * 128, t, mean, rstd);
       const int c0 = (tile % tiles_per_row) * kOTile;
       const int rr = tile / tiles_per_row;
       const int b = rr / p.N, r = rr - b * p.N;
