@@ -77,20 +77,39 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete is suspended by
+// the hardware until the phase completes or `ns` nanoseconds pass, instead of polling.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase with the given parity to complete. Returns false (and records
-// `code`) after FFB_WAIT_CYCLES, or at once when another thread already recorded one.
+// `code`) after FFB_WAIT_CYCLES, or when another thread has already recorded an error
+// (checked about every million cycles, so the wait loop issues almost nothing and reads
+// no global memory while it waits).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const long long start = clock64();
+  long long checked = start;
   while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(a, parity)) return true;
-    if (error_raised(err)) return false;
-    if (clock64() - start > FFB_WAIT_CYCLES) {
-      set_error(err, code);
-      return false;
+    if (mbar_try_wait_suspend(a, parity, 20000u)) return true;
+    const long long now = clock64();
+    if (now - checked > (1ll << 20)) {
+      checked = now;
+      if (error_raised(err)) return false;
+      if (now - start > FFB_WAIT_CYCLES) {
+        set_error(err, code);
+        return false;
+      }
     }
   }
 }
@@ -212,6 +231,10 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 
 // 32 lanes x 32 bits, 16 consecutive columns: thread t of the warp receives lane
 // (warp % 4) * 32 + t, columns [col, col + 16).
+__device__ __forceinline__ void tmem_ld1(uint32_t taddr, uint32_t& r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr) : "memory");
+}
+
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
@@ -401,6 +424,34 @@ __device__ __forceinline__ uint32_t add_f16x2(uint32_t a, uint32_t b) {
 __device__ __forceinline__ float f16x2_sum(uint32_t v) {
   __half2 h = *reinterpret_cast<__half2*>(&v);
   return __low2float(h) + __high2float(h);
+}
+
+// 2^d for a pair of fp32 values on the FMA and integer pipes (no MUFU): d is clamped to
+// [-126, 0], split as n + f with n = round(d) (the 1.5 * 2^23 rounding constant) and
+// f in [-0.5, 0.5]; 2^f is a cubic fitted to relative error (max 7.8e-5 on the interval)
+// and 2^n enters as an integer add to the exponent field. Inputs below -126 (masked
+// logits, -inf) give at most 2^-126.
+__device__ __forceinline__ void exp2_poly_x2(uint64_t d, float& e0, float& e1) {
+  float d0, d1;
+  f32x2_split(d, d0, d1);
+  const uint64_t dc = f32x2(fmaxf(d0, -126.0f), fmaxf(d1, -126.0f));
+  const uint64_t t = add_f32x2(dc, f32x2(12582912.0f, 12582912.0f));
+  const uint64_t n = add_f32x2(t, f32x2(-12582912.0f, -12582912.0f));
+  const uint64_t fr = fma_f32x2(n, f32x2(-1.0f, -1.0f), dc);
+  uint64_t p = fma_f32x2(f32x2(0.05508876592f, 0.05508876592f), fr, f32x2(0.24260465801f, 0.24260465801f));
+  p = fma_f32x2(p, fr, f32x2(0.69327628613f, 0.69327628613f));
+  p = fma_f32x2(p, fr, f32x2(0.99992889166f, 0.99992889166f));
+  float p0, p1, t0, t1;
+  f32x2_split(p, p0, p1);
+  f32x2_split(t, t0, t1);
+  e0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  e1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+}
+
+// Two non-negative finite fp32 values -> bf16x2 (lo in the low half), rounded half up,
+// with integer adds and a byte permute (no conversion instruction).
+__device__ __forceinline__ uint32_t pack_bf16_nonneg(float lo, float hi) {
+  return __byte_perm(__float_as_uint(lo) + 0x8000u, __float_as_uint(hi) + 0x8000u, 0x7632);
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

@@ -11,11 +11,12 @@
 //
 // Three launches:
 //  1. triattn_proj: 128-pair tiles of raw z (row tiles for the starting node, column
-//     tiles for the ending node, so every write below is coalesced) x the resident packed
-//     [W_q; W_k; W_v; W_b] with the input LayerNorm folded into the epilogue. W_q carries
-//     log2(e)/sqrt(32) and W_b log2(e), so the softmax works in base 2. Writes
+//     tiles for the ending node, so the Q / K / V^T writes are coalesced) x the resident
+//     packed [W_q; W_k; W_v; W_b] with the input LayerNorm folded into the epilogue. W_q
+//     carries log2(e)/sqrt(32) and W_b log2(e), so the softmax works in base 2. Writes
 //     Q, K [B, N(r), H, N(n), 32], V^T [B, N(r), H, 32, Np(n)] and the bias
-//     [B, H, N, Np] (starting: [q][k]; ending: [k][q]).
+//     [B, H, N, Np] in the natural pair layout, which both nodes read as [query][key] rows
+//     (the ending node's column tiles write it with a stride).
 //  2. triattn_attn: flash attention on tcgen05. A CTA owns 256 queries (two groups of
 //     128, one per softmax warpgroup) of one (row, head) and streams 64-key blocks of K,
 //     V^T and the bias through a 3-stage TMA ring shared by both groups. S = Q K^T and
@@ -214,7 +215,10 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
             for (int h = 0; h < kHeads; ++h) {
               const int c = 384 + h;
-              p.bias[((static_cast<int64_t>(b) * kHeads + h) * p.N + r) * p.Np + n] =
+              // natural pair layout [b, h, i, j] for both nodes (starting: i = r, j = n;
+              // ending: i = n, j = r), so the attention reads rows of queries x keys
+              const int64_t bi = p.starting ? r : n, bj = p.starting ? n : r;
+              p.bias[((static_cast<int64_t>(b) * kHeads + h) * p.N + bi) * p.Np + bj] =
                   __float2bfloat16_rn(rstd * (__uint_as_float(v[h]) - mean * s.wsum[c]) + s.bias[c]);
             }
           }
@@ -240,6 +244,7 @@ constexpr int kKB = 64;        // keys per block
 constexpr int kKVStages = 3;
 constexpr int kAttnThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 softmax (2 groups)
 constexpr int kMaxMaskWords = 2048;  // B * ceil(N / 64) * 2 words of key-mask bits
+constexpr int kPolyEvery = 4;        // one key pair in four takes the FMA-pipe exponential
 
 struct AttnSmem {
   alignas(1024) uint8_t q[kGroups][kTile * kD * 2];          // 8 KB each, SW64
@@ -347,10 +352,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           tma_load_3d(s.vt[st], &map_vt, &s.kv_full[st], j * kKB, 0, qrow);
           for (int g = 0; g < kGroups; ++g) {
             const int q0 = (qp * 2 + g) * kTile;
-            if (p.starting)
-              tma_load_3d(s.bias[st][g], &map_bias, &s.kv_full[st], j * kKB, q0, b * kHeads + h);  // [q][k]
-            else
-              tma_load_3d(s.bias[st][g], &map_bias, &s.kv_full[st], q0, j * kKB, b * kHeads + h);  // [k][q]
+            tma_load_3d(s.bias[st][g], &map_bias, &s.kv_full[st], j * kKB, q0, b * kHeads + h);  // [q][k]
           }
         }
       }
@@ -460,21 +462,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           // logits (base 2): s + bias, then the mask
           float x[64];
           const uint8_t* bt = s.bias[st][g];
-          if (p.starting) {
 #pragma unroll
-            for (int c8 = 0; c8 < 8; ++c8) {
-              const uint4 bv = *reinterpret_cast<const uint4*>(bt + sw128_offset(t, c8 * 8));
-              const uint32_t w[4] = {bv.x, bv.y, bv.z, bv.w};
+          for (int c8 = 0; c8 < 8; ++c8) {
+            const uint4 bv = *reinterpret_cast<const uint4*>(bt + sw128_offset(t, c8 * 8));
+            const uint32_t w[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                x[c8 * 8 + 2 * e] = __uint_as_float(sv[c8 * 8 + 2 * e]) + bf16_lo(w[e]);
-                x[c8 * 8 + 2 * e + 1] = __uint_as_float(sv[c8 * 8 + 2 * e + 1]) + bf16_hi(w[e]);
-              }
+            for (int e = 0; e < 4; ++e) {
+              const int c = c8 * 8 + 2 * e;
+              f32x2_split(add_f32x2(f32x2(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])),
+                                    f32x2(bf16_lo(w[e]), bf16_hi(w[e]))),
+                          x[c], x[c + 1]);
             }
-          } else {
-            const __nv_bfloat16* col = reinterpret_cast<const __nv_bfloat16*>(bt) + t;
-#pragma unroll
-            for (int c = 0; c < kKB; ++c) x[c] = __uint_as_float(sv[c]) + __bfloat162float(col[c * kTile]);
           }
           const int k0 = j * kKB;
           const uint64_t keep = row_on ? ((static_cast<uint64_t>(mw[2 * j + 1]) << 32) | mw[2 * j]) : 0ull;
@@ -485,19 +483,46 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               if (!((keep >> c) & 1ull)) x[c] = c < nvalid ? kMasked : kNegInf;
             }
           }
-          float bm = x[0];
+          // block maximum: a three-input max tree (depth 4)
+          float t1[22];
 #pragma unroll
-          for (int c = 1; c < kKB; ++c) bm = fmaxf(bm, x[c]);
+          for (int i = 0; i < 21; ++i) t1[i] = max3f(x[3 * i], x[3 * i + 1], x[3 * i + 2]);
+          t1[21] = x[63];
+          float t2[8];
+#pragma unroll
+          for (int i = 0; i < 7; ++i) t2[i] = max3f(t1[3 * i], t1[3 * i + 1], t1[3 * i + 2]);
+          t2[7] = t1[21];
+          const float bm = max3f(max3f(t2[0], t2[1], t2[2]), max3f(t2[3], t2[4], t2[5]), fmaxf(t2[6], t2[7]));
           const float m_new = fmaxf(m, bm);
           const float alpha = ex2(m - m_new);
-          float sum = 0.f;
+          // P = 2^(x - m): one key pair in kPolyEvery on the FMA pipe (cubic), the rest on
+          // MUFU; packed to bf16 with integer rounding
+          const uint64_t neg_m = f32x2(-m_new, -m_new);
+          uint64_t acc[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[i] = f32x2(0.f, 0.f);
           uint32_t pw[32];
 #pragma unroll
           for (int c = 0; c < kKB; c += 2) {
-            const float e0 = ex2(x[c] - m_new);
-            const float e1 = ex2(x[c + 1] - m_new);
-            sum += e0 + e1;
-            pw[c / 2] = pack_bf16(e0, e1);
+            const uint64_t d = add_f32x2(f32x2(x[c], x[c + 1]), neg_m);
+            float e0, e1;
+            if ((c / 2) % kPolyEvery == kPolyEvery - 1) {
+              exp2_poly_x2(d, e0, e1);
+            } else {
+              float d0, d1;
+              f32x2_split(d, d0, d1);
+              e0 = ex2(d0);
+              e1 = ex2(d1);
+            }
+            acc[(c / 2) & 3] = add_f32x2(acc[(c / 2) & 3], f32x2(e0, e1));
+            pw[c / 2] = pack_bf16_nonneg(e0, e1);
+          }
+          float sum = 0.f;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            float a0, a1;
+            f32x2_split(acc[i], a0, a1);
+            sum += a0 + a1;
           }
           l = l * alpha + sum;
           m = m_new;
@@ -925,15 +950,9 @@ int triattn_forward(const void* z, const uint8_t* mask, const void* packed, void
     if (st) return st;
     const uint64_t bdims[3] = {static_cast<uint64_t>(N), static_cast<uint64_t>(N), static_cast<uint64_t>(B) * kHeads};
     const uint64_t bstrides[2] = {static_cast<uint64_t>(np) * 2, static_cast<uint64_t>(N) * np * 2};
-    if (starting) {
-      const uint32_t bbox[3] = {kKB, kTile, 1};  // [q rows][64 keys], 128-byte rows
-      st = make_map(&map_bias, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ws.bias, bdims, bstrides, bbox,
-                    CU_TENSOR_MAP_SWIZZLE_128B);
-    } else {
-      const uint32_t bbox[3] = {kTile, kKB, 1};  // [64 key rows][128 q]
-      st = make_map(&map_bias, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ws.bias, bdims, bstrides, bbox,
-                    CU_TENSOR_MAP_SWIZZLE_NONE);
-    }
+    const uint32_t bbox[3] = {kKB, kTile, 1};  // [q rows][64 keys], 128-byte rows
+    st = make_map(&map_bias, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ws.bias, bdims, bstrides, bbox,
+                  CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
     AttnParams ap;
     ap.mask = mask;
