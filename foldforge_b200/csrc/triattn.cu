@@ -240,26 +240,47 @@ __global__ void __launch_bounds__(256, 1)
 }
 
 // ====================================================================== 2. attention
+// Per CTA, a flat sequence of (unit, 64-key block) steps; a unit is 256 queries (two groups
+// of 128) of one (batch, row, head).
+//   warp 0      TMA: Q per unit (double-buffered), K, V^T and the two groups' bias tiles
+//               per block through a 3-stage ring
+//   warp 1      MMA: S = Q K^T of step i + 1 (into the group's S/P buffer i % 2) ahead of
+//               O += P V of step i, with P read from TMEM (A operand) and O accumulated in
+//               TMEM across the unit's blocks (O buffer = unit % 2)
+//   warps 2-9   softmax, thread = query row (TMEM lane): logits = S + bias (+ key mask),
+//               P = 2^(x - m) written back over S as bf16. The running maximum m is raised
+//               lazily: only when a block's maximum exceeds m + kRescale does the warp
+//               rescale O (and the row sum) in TMEM, after the previous P V has landed, so
+//               P <= 2^kRescale. V^T carries a row of ones (B operand row 32), so O column 32
+//               is the row sum of P as the tensor core multiplied it. A unit's output is
+//               read, normalised and stored while the next unit's first block runs.
 constexpr int kKB = 64;        // keys per block
 constexpr int kKVStages = 3;
 constexpr int kAttnThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 softmax (2 groups)
 constexpr int kMaxMaskWords = 2048;  // B * ceil(N / 64) * 2 words of key-mask bits
 constexpr int kPolyEvery = 4;        // one key pair in four takes the FMA-pipe exponential
+constexpr int kVtRows = 48;          // V^T (32 rows), a row of ones, 15 zero rows
+constexpr int kOCols = 48;           // O (32 columns), the row sum, 15 unused
+constexpr int kGroupCols = 256;      // per group: S/P buffers at +0 / +64, O buffers at +128 / +192
+constexpr float kRescale = 8.0f;     // lazy-rescale threshold in log2 units
 
 struct AttnSmem {
-  alignas(1024) uint8_t q[kGroups][kTile * kD * 2];          // 8 KB each, SW64
+  alignas(1024) uint8_t q[2][kGroups][kTile * kD * 2];       // 8 KB each, SW64, by unit parity
   alignas(1024) uint8_t k[kKVStages][kKB * kD * 2];          // 4 KB, SW64
-  alignas(1024) uint8_t vt[kKVStages][kD * kKB * 2];         // 4 KB, SW128
-  alignas(1024) uint8_t bias[kKVStages][kGroups][kTile * kKB * 2];  // 16 KB each
-  alignas(1024) uint8_t p[kGroups][2][kTile * kKB * 2];      // 16 KB each, SW128
+  alignas(1024) uint8_t vt[kKVStages][kVtRows * kKB * 2];    // 6 KB, SW128
+  alignas(1024) uint8_t bias[kKVStages][kGroups][kTile * kKB * 2];  // 16 KB each, SW128
   uint32_t mask_words[kMaxMaskWords];
-  uint64_t q_full, q_empty;
+  uint64_t q_full[2], q_empty[2];
   uint64_t kv_full[kKVStages], kv_empty[kKVStages];
-  uint64_t s_full[kGroups][2], s_free[kGroups][2];
+  uint64_t s_full[kGroups][2];
   uint64_t p_full[kGroups][2];
+  uint64_t pv_done[kGroups];
   uint64_t o_full[kGroups][2], o_free[kGroups][2];
+  uint64_t mma_done;
   uint32_t tmem_base;
 };
+
+static_assert(sizeof(AttnSmem) + 1024 <= 232448, "attention shared memory exceeds the per-CTA limit");
 
 struct AttnParams {
   const uint8_t* mask;   // [B, N]
@@ -290,22 +311,28 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int lane = threadIdx.x % 32;
   const int units = p.B * p.N * kHeads * p.qpairs;
   const int nkb = (p.N + kKB - 1) / kKB;
+  const int my_units = blockIdx.x < units ? (units - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1 : 0;
+  const int steps = my_units * nkb;
 
   if (threadIdx.x == 0) {
-    mbar_init(&s.q_full, 1);
-    mbar_init(&s.q_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.q_full[i], 1);
+      mbar_init(&s.q_empty[i], 1);
+    }
     for (int i = 0; i < kKVStages; ++i) {
       mbar_init(&s.kv_full[i], 1);
       mbar_init(&s.kv_empty[i], 1 + 8);  // MMA commit + 8 softmax warps (bias read)
     }
-    for (int g = 0; g < kGroups; ++g)
+    for (int g = 0; g < kGroups; ++g) {
+      mbar_init(&s.pv_done[g], 1);
       for (int i = 0; i < 2; ++i) {
         mbar_init(&s.s_full[g][i], 1);
-        mbar_init(&s.s_free[g][i], 4);
         mbar_init(&s.p_full[g][i], 4);
         mbar_init(&s.o_full[g][i], 1);
         mbar_init(&s.o_free[g][i], 4);
       }
+    }
+    mbar_init(&s.mma_done, 1);
     fence_mbar_init();
   }
   // key-mask bits, per batch padded to whole 64-key blocks (zero beyond N)
@@ -319,6 +346,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     s.mask_words[w] = bits;
   }
+  // constant rows 32..47 of every V^T stage: bf16 ones, then zeros (TMA writes rows 0..31)
+  for (int w = threadIdx.x; w < kKVStages * (kVtRows - kD) * 32; w += kAttnThreads) {
+    const int st = w / ((kVtRows - kD) * 32);
+    const int row = kD + (w / 32) % (kVtRows - kD);
+    reinterpret_cast<uint32_t*>(s.vt[st] + row * 128)[w % 32] = row == kD ? 0x3F803F80u : 0u;
+  }
+  fence_async_smem();
   if (warp == 0) {
     tmem_alloc(&s.tmem_base, 512);
     tmem_relinquish();
@@ -335,255 +369,242 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tma_prefetch_map(&map_k);
       tma_prefetch_map(&map_vt);
       tma_prefetch_map(&map_bias);
-      int kv_it = 0, u_it = 0;
+      int kv_it = 0, ul = 0;
       bool ok = true;
-      for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x, ++u_it) {
+      for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x, ++ul) {
         int b, r, h, qp;
         unit_coords(unit, p, b, r, h, qp);
         const int qrow = (b * p.N + r) * kHeads + h;
-        if (!mbar_wait(&s.q_empty, (u_it & 1) ^ 1, p.err, kErrTimeoutEmpty)) { ok = false; break; }
-        mbar_arrive_expect_tx(&s.q_full, kGroups * kTile * kD * 2);
-        for (int g = 0; g < kGroups; ++g) tma_load_3d(s.q[g], &map_q, &s.q_full, 0, (qp * 2 + g) * kTile, qrow);
+        const int qb = ul & 1;
+        if (!mbar_wait(&s.q_empty[qb], ((ul >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty)) break;
+        mbar_arrive_expect_tx(&s.q_full[qb], kGroups * kTile * kD * 2);
+        for (int g = 0; g < kGroups; ++g) tma_load_3d(s.q[qb][g], &map_q, &s.q_full[qb], 0, (qp * 2 + g) * kTile, qrow);
         for (int j = 0; j < nkb; ++j, ++kv_it) {
           const int st = kv_it % kKVStages;
           if (!mbar_wait(&s.kv_empty[st], ((kv_it / kKVStages) & 1) ^ 1, p.err, kErrTimeoutEmpty)) { ok = false; break; }
           mbar_arrive_expect_tx(&s.kv_full[st], kKB * kD * 2 * 2 + kGroups * kTile * kKB * 2);
           tma_load_3d(s.k[st], &map_k, &s.kv_full[st], 0, j * kKB, qrow);
           tma_load_3d(s.vt[st], &map_vt, &s.kv_full[st], j * kKB, 0, qrow);
-          for (int g = 0; g < kGroups; ++g) {
-            const int q0 = (qp * 2 + g) * kTile;
-            tma_load_3d(s.bias[st][g], &map_bias, &s.kv_full[st], j * kKB, q0, b * kHeads + h);  // [q][k]
-          }
+          for (int g = 0; g < kGroups; ++g)
+            tma_load_3d(s.bias[st][g], &map_bias, &s.kv_full[st], j * kKB, (qp * 2 + g) * kTile, b * kHeads + h);
         }
+        if (!ok) {
+          ++ul;
+          break;
+        }
+      }
+      // every issued copy lands before the CTA may exit
+      for (int k = 0; k < kKVStages && k < kv_it; ++k) {
+        const int i = kv_it - 1 - k;
+        mbar_wait(&s.kv_full[i % kKVStages], (i / kKVStages) & 1, p.err, kErrTimeoutLoad);
+      }
+      for (int k = 0; k < 2 && k < ul; ++k) {
+        const int i = ul - 1 - k;
+        mbar_wait(&s.q_full[i & 1], (i >> 1) & 1, p.err, kErrTimeoutLoad);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc_s = idesc_bf16_f32(128, kKB);
-      const uint32_t idesc_o = idesc_bf16_f32(128, kD);
-      int kv_it = 0, u_it = 0;
-      bool ok = true;
-      auto issue_qk = [&](int it) -> bool {
-        const int st = it % kKVStages;
-        if (!mbar_wait(&s.kv_full[st], (it / kKVStages) & 1, p.err, kErrTimeoutLoad)) return false;
-        const int buf = it & 1;
+      const uint32_t idesc_o = idesc_bf16_f32(128, kOCols);
+      auto issue_s = [&](int i) -> bool {
+        const int ul = i / nkb, j = i % nkb;
+        const int st = i % kKVStages, buf = i & 1, qb = ul & 1;
+        if (j == 0 && !mbar_wait(&s.q_full[qb], (ul >> 1) & 1, p.err, kErrTimeoutLoad)) return false;
+        if (!mbar_wait(&s.kv_full[st], (i / kKVStages) & 1, p.err, kErrTimeoutLoad)) return false;
+        tc_fence_after();
         for (int g = 0; g < kGroups; ++g) {
-          if (!mbar_wait(&s.s_free[g][buf], ((it >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty)) return false;
-          tc_fence_after();
-          const uint32_t d = tmem0 + g * 192 + buf * 64;
-          const uint64_t da = desc_kmajor_sw64(smem_u32(s.q[g]));
+          const uint32_t d = tmem0 + g * kGroupCols + buf * 64;
+          const uint64_t da = desc_kmajor_sw64(smem_u32(s.q[qb][g]));
           const uint64_t db = desc_kmajor_sw64(smem_u32(s.k[st]));
           mma_bf16(d, da, db, idesc_s, 0);
           mma_bf16(d, da + 2, db + 2, idesc_s, 1);
           mma_commit(&s.s_full[g][buf]);
         }
+        if (j == nkb - 1) mma_commit(&s.q_empty[qb]);  // the unit's Q may be refilled once these finish
         return true;
       };
-      for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x, ++u_it) {
-        if (!mbar_wait(&s.q_full, u_it & 1, p.err, kErrTimeoutLoad)) break;
-        tc_fence_after();
-        const int first = kv_it;
-        if (!issue_qk(first)) break;
-        for (int j = 0; j < nkb && ok; ++j) {
-          const int it = first + j;
-          if (j + 1 < nkb) {
-            if (!issue_qk(it + 1)) { ok = false; break; }
-          } else {
-            mma_commit(&s.q_empty);  // every Q K^T of this unit issued: Q may be refilled once they finish
-          }
-          const int st = it % kKVStages;
-          const int buf = it & 1;
-          const uint32_t ph = (it >> 1) & 1;
-          for (int g = 0; g < kGroups; ++g) {
-            if (!mbar_wait(&s.p_full[g][buf], ph, p.err, kErrTimeoutMma) ||
-                !mbar_wait(&s.o_free[g][buf], ph ^ 1, p.err, kErrTimeoutEmpty)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t d = tmem0 + g * 192 + 128 + buf * 32;
-            const uint64_t da = desc_kmajor_sw128(smem_u32(s.p[g][buf]));
-            const uint64_t db = desc_kmajor_sw128(smem_u32(s.vt[st]));
+      bool ok = steps > 0 && issue_s(0);
+      for (int i = 0; i < steps && ok; ++i) {
+        // S of the next step first: it overwrites the buffer whose P was consumed by the
+        // P V issued one step ago (same thread, so the tensor pipe keeps the order)
+        if (i + 1 < steps && !issue_s(i + 1)) break;
+        const int ul = i / nkb, j = i % nkb;
+        const int st = i % kKVStages, buf = i & 1, ob = ul & 1;
+        for (int g = 0; g < kGroups; ++g) {
+          if (!mbar_wait(&s.p_full[g][buf], (i >> 1) & 1, p.err, kErrTimeoutMma)) { ok = false; break; }
+          if (j == 0 && !mbar_wait(&s.o_free[g][ob], ((ul >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t d = tmem0 + g * kGroupCols + 128 + ob * 64;
+          const uint32_t a = tmem0 + g * kGroupCols + buf * 64;
+          const uint64_t db = desc_kmajor_sw128(smem_u32(s.vt[st]));
 #pragma unroll
-            for (int kk = 0; kk < kKB / 16; ++kk) mma_bf16(d, da + 2 * kk, db + 2 * kk, idesc_o, kk != 0);
-            mma_commit(&s.o_full[g][buf]);
-          }
-          if (!ok) break;
-          mma_commit(&s.kv_empty[st]);
+          for (int kk = 0; kk < kKB / 16; ++kk)
+            mma_bf16_tmem_a(d, a + kk * 8, db + 2 * kk, idesc_o, (j | kk) != 0);
+          mma_commit(&s.pv_done[g]);
+          if (j == nkb - 1) mma_commit(&s.o_full[g][ob]);
         }
-        kv_it = first + nkb;
+        if (!ok) break;
+        mma_commit(&s.kv_empty[st]);
       }
+      // every issued MMA completes before TMEM is released
+      mma_commit(&s.mma_done);
+      mbar_wait(&s.mma_done, 0, p.err, kErrTimeoutMma);
     }
   } else {
     // ------------------------------------------------------------ softmax warpgroups
     const int g = (warp - 2) / 4;
     const int t = (warp & 3) * 32 + lane;  // TMEM lane == query row in the group's tile
-    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t gbase = tmem0 + (static_cast<uint32_t>((warp & 3) * 32) << 16) + g * kGroupCols;
     const float kMasked = -1.0e9f * kLog2e;
     const float kNegInf = -__int_as_float(0x7f800000);
-    int kv_it = 0;
     bool ok = true;
-    for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x) {
+    int i = 0;                                   // step index
+    int prev_q = 0, prev_b = 0, prev_r = 0, prev_h = 0;  // the unit awaiting its output
+    // read, normalise and store the output of unit `pu` (O buffer pu % 2)
+    auto finalize = [&](int pu) -> bool {
+      const int pob = pu & 1;
+      const bool w = mbar_wait(&s.o_full[g][pob], (pu >> 1) & 1, p.err, kErrTimeoutMma);
+      if (!__all_sync(0xFFFFFFFFu, w)) return false;
+      tc_fence_after();
+      uint32_t ov[32], os;
+      tmem_ld32(gbase + 128 + pob * 64, ov);
+      tmem_ld1(gbase + 128 + pob * 64 + kD, os);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.o_free[g][pob]);
+      if (prev_q < p.N) {
+        const float inv = 1.0f / __uint_as_float(os);
+        // natural pair position: starting (i=r, j=q), ending (i=q, j=r)
+        const int64_t pi = p.starting ? prev_r : prev_q;
+        const int64_t pj = p.starting ? prev_q : prev_r;
+        uint4* dst = reinterpret_cast<uint4*>(
+            p.o + (((static_cast<int64_t>(prev_b) * p.N + pi) * p.N + pj) * kC + prev_h * kD));
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float* f = reinterpret_cast<const float*>(ov) + 8 * k;
+          dst[k] = make_uint4(pack_bf16(f[0] * inv, f[1] * inv), pack_bf16(f[2] * inv, f[3] * inv),
+                              pack_bf16(f[4] * inv, f[5] * inv), pack_bf16(f[6] * inv, f[7] * inv));
+        }
+      }
+      return true;
+    };
+    int ul = 0;
+    for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x, ++ul) {
       int b, r, h, qp;
       unit_coords(unit, p, b, r, h, qp);
       const int q = (qp * 2 + g) * kTile + t;
       const bool row_on = p.mask[b * p.N + r] != 0;
       const uint32_t* mw = s.mask_words + b * p.words_per_batch;
-      float m = kNegInf, l = 0.f, alpha_pending = 0.f;
-      float o[kD];
+      const int ob = ul & 1;
+      float m = 0.f;
+      for (int j = 0; j < nkb; ++j, ++i) {
+        const int st = i % kKVStages;
+        const int buf = i & 1;
+        const bool w1 = mbar_wait(&s.s_full[g][buf], (i >> 1) & 1, p.err, kErrTimeoutMma);
+        const bool w2 = mbar_wait(&s.kv_full[st], (i / kKVStages) & 1, p.err, kErrTimeoutLoad);
+        if (!__all_sync(0xFFFFFFFFu, w1 && w2)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t sv[64];
+        tmem_ld32(gbase + buf * 64, *reinterpret_cast<uint32_t(*)[32]>(sv));
+        tmem_ld32(gbase + buf * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+        tmem_ld_wait();
+        // logits (base 2): s + bias, then the mask
+        float x[64];
+        const uint8_t* bt = s.bias[st][g];
 #pragma unroll
-      for (int d = 0; d < kD; ++d) o[d] = 0.f;
-      for (int j = 0; j <= nkb && ok; ++j) {
-        const int it = kv_it + j;
-        if (j < nkb) {
-          const int st = it % kKVStages;
-          const int buf = it & 1;
-          const uint32_t ph = (it >> 1) & 1;
-          bool w1 = mbar_wait(&s.s_full[g][buf], ph, p.err, kErrTimeoutMma);
-          bool w2 = mbar_wait(&s.kv_full[st], (it / kKVStages) & 1, p.err, kErrTimeoutLoad);
-          if (!__all_sync(0xFFFFFFFFu, w1 && w2)) { ok = false; break; }
-          tc_fence_after();
-          uint32_t sv[64];
-          {
-            uint32_t a[32], c[32];
-            tmem_ld32(tmem0 + lane_off + g * 192 + buf * 64, a);
-            tmem_ld32(tmem0 + lane_off + g * 192 + buf * 64 + 32, c);
-            tmem_ld_wait();
+        for (int c8 = 0; c8 < 8; ++c8) {
+          const uint4 bv = *reinterpret_cast<const uint4*>(bt + sw128_offset(t, c8 * 8));
+          const uint32_t w[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              sv[i] = a[i];
-              sv[32 + i] = c[i];
-            }
-          }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&s.s_free[g][buf]);
-          // logits (base 2): s + bias, then the mask
-          float x[64];
-          const uint8_t* bt = s.bias[st][g];
-#pragma unroll
-          for (int c8 = 0; c8 < 8; ++c8) {
-            const uint4 bv = *reinterpret_cast<const uint4*>(bt + sw128_offset(t, c8 * 8));
-            const uint32_t w[4] = {bv.x, bv.y, bv.z, bv.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int c = c8 * 8 + 2 * e;
-              f32x2_split(add_f32x2(f32x2(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])),
-                                    f32x2(bf16_lo(w[e]), bf16_hi(w[e]))),
-                          x[c], x[c + 1]);
-            }
-          }
-          const int k0 = j * kKB;
-          const uint64_t keep = row_on ? ((static_cast<uint64_t>(mw[2 * j + 1]) << 32) | mw[2 * j]) : 0ull;
-          const int nvalid = p.N - k0 < kKB ? p.N - k0 : kKB;
-          if (keep != ~0ull) {
-#pragma unroll
-            for (int c = 0; c < kKB; ++c) {
-              if (!((keep >> c) & 1ull)) x[c] = c < nvalid ? kMasked : kNegInf;
-            }
-          }
-          // block maximum: a three-input max tree (depth 4)
-          float t1[22];
-#pragma unroll
-          for (int i = 0; i < 21; ++i) t1[i] = max3f(x[3 * i], x[3 * i + 1], x[3 * i + 2]);
-          t1[21] = x[63];
-          float t2[8];
-#pragma unroll
-          for (int i = 0; i < 7; ++i) t2[i] = max3f(t1[3 * i], t1[3 * i + 1], t1[3 * i + 2]);
-          t2[7] = t1[21];
-          const float bm = max3f(max3f(t2[0], t2[1], t2[2]), max3f(t2[3], t2[4], t2[5]), fmaxf(t2[6], t2[7]));
-          const float m_new = fmaxf(m, bm);
-          const float alpha = ex2(m - m_new);
-          // P = 2^(x - m): one key pair in kPolyEvery on the FMA pipe (cubic), the rest on
-          // MUFU; packed to bf16 with integer rounding
-          const uint64_t neg_m = f32x2(-m_new, -m_new);
-          uint64_t acc[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) acc[i] = f32x2(0.f, 0.f);
-          uint32_t pw[32];
-#pragma unroll
-          for (int c = 0; c < kKB; c += 2) {
-            const uint64_t d = add_f32x2(f32x2(x[c], x[c + 1]), neg_m);
-            float e0, e1;
-            if ((c / 2) % kPolyEvery == kPolyEvery - 1) {
-              exp2_poly_x2(d, e0, e1);
-            } else {
-              float d0, d1;
-              f32x2_split(d, d0, d1);
-              e0 = ex2(d0);
-              e1 = ex2(d1);
-            }
-            acc[(c / 2) & 3] = add_f32x2(acc[(c / 2) & 3], f32x2(e0, e1));
-            pw[c / 2] = pack_bf16_nonneg(e0, e1);
-          }
-          float sum = 0.f;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            float a0, a1;
-            f32x2_split(acc[i], a0, a1);
-            sum += a0 + a1;
-          }
-          l = l * alpha + sum;
-          m = m_new;
-          uint8_t* pt = s.p[g][buf];
-#pragma unroll
-          for (int c8 = 0; c8 < 8; ++c8)
-            *reinterpret_cast<uint4*>(pt + sw128_offset(t, c8 * 8)) =
-                make_uint4(pw[c8 * 4], pw[c8 * 4 + 1], pw[c8 * 4 + 2], pw[c8 * 4 + 3]);
-          fence_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(&s.p_full[g][buf]);
-            mbar_arrive(&s.kv_empty[st]);
-          }
-          if (j > 0) {
-            // fold in P V of the previous block
-            const int pit = it - 1;
-            const int pbuf = pit & 1;
-            bool w3 = mbar_wait(&s.o_full[g][pbuf], (pit >> 1) & 1, p.err, kErrTimeoutMma);
-            if (!__all_sync(0xFFFFFFFFu, w3)) { ok = false; break; }
-            tc_fence_after();
-            uint32_t ov[32];
-            tmem_ld32(tmem0 + lane_off + g * 192 + 128 + pbuf * 32, ov);
-            tmem_ld_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s.o_free[g][pbuf]);
-#pragma unroll
-            for (int d = 0; d < kD; ++d) o[d] = o[d] * alpha_pending + __uint_as_float(ov[d]);
-          }
-          alpha_pending = alpha;
-        } else {
-          // last block's P V, then normalise and store
-          const int pit = it - 1;
-          const int pbuf = pit & 1;
-          bool w3 = mbar_wait(&s.o_full[g][pbuf], (pit >> 1) & 1, p.err, kErrTimeoutMma);
-          if (!__all_sync(0xFFFFFFFFu, w3)) { ok = false; break; }
-          tc_fence_after();
-          uint32_t ov[32];
-          tmem_ld32(tmem0 + lane_off + g * 192 + 128 + pbuf * 32, ov);
-          tmem_ld_wait();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&s.o_free[g][pbuf]);
-          const float inv = 1.0f / l;
-#pragma unroll
-          for (int d = 0; d < kD; ++d) o[d] = (o[d] * alpha_pending + __uint_as_float(ov[d])) * inv;
-          if (q < p.N) {
-            // natural pair position: starting (i=r, j=q), ending (i=q, j=r)
-            const int64_t pi = p.starting ? r : q;
-            const int64_t pj = p.starting ? q : r;
-            uint4* dst = reinterpret_cast<uint4*>(p.o + (((static_cast<int64_t>(b) * p.N + pi) * p.N + pj) * kC + h * kD));
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              dst[i] = make_uint4(pack_bf16(o[8 * i], o[8 * i + 1]), pack_bf16(o[8 * i + 2], o[8 * i + 3]),
-                                  pack_bf16(o[8 * i + 4], o[8 * i + 5]), pack_bf16(o[8 * i + 6], o[8 * i + 7]));
+          for (int e = 0; e < 4; ++e) {
+            const int c = c8 * 8 + 2 * e;
+            f32x2_split(add_f32x2(f32x2(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])),
+                                  f32x2(bf16_lo(w[e]), bf16_hi(w[e]))),
+                        x[c], x[c + 1]);
           }
         }
+        const int k0 = j * kKB;
+        const uint64_t keep = row_on ? ((static_cast<uint64_t>(mw[2 * j + 1]) << 32) | mw[2 * j]) : 0ull;
+        const int nvalid = p.N - k0 < kKB ? p.N - k0 : kKB;
+        if (keep != ~0ull) {
+#pragma unroll
+          for (int c = 0; c < kKB; ++c) {
+            if (!((keep >> c) & 1ull)) x[c] = c < nvalid ? kMasked : kNegInf;
+          }
+        }
+        // block maximum: a three-input max tree (depth 4)
+        float t1[22];
+#pragma unroll
+        for (int k = 0; k < 21; ++k) t1[k] = max3f(x[3 * k], x[3 * k + 1], x[3 * k + 2]);
+        t1[21] = x[63];
+        float t2[8];
+#pragma unroll
+        for (int k = 0; k < 7; ++k) t2[k] = max3f(t1[3 * k], t1[3 * k + 1], t1[3 * k + 2]);
+        t2[7] = t1[21];
+        const float bm = max3f(max3f(t2[0], t2[1], t2[2]), max3f(t2[3], t2[4], t2[5]), fmaxf(t2[6], t2[7]));
+        if (j == 0) {
+          m = bm;  // the unit's first block: nothing accumulated yet
+        } else {
+          const bool need = bm > m + kRescale;
+          if (__any_sync(0xFFFFFFFFu, need)) {
+            // raise m: O and the row sum (in TMEM) scale by 2^(m - m_new) once the previous
+            // P V has landed
+            const float m_new = need ? bm : m;
+            const float alpha = ex2(m - m_new);
+            const bool w3 = mbar_wait(&s.pv_done[g], (i - 1) & 1, p.err, kErrTimeoutMma);
+            if (!__all_sync(0xFFFFFFFFu, w3)) { ok = false; break; }
+            tc_fence_after();
+            uint32_t ov[32], os;
+            tmem_ld32(gbase + 128 + ob * 64, ov);
+            tmem_ld1(gbase + 128 + ob * 64 + kD, os);
+            tmem_ld_wait();
+#pragma unroll
+            for (int d = 0; d < kD; ++d) ov[d] = __float_as_uint(__uint_as_float(ov[d]) * alpha);
+            os = __float_as_uint(__uint_as_float(os) * alpha);
+            tmem_st32(gbase + 128 + ob * 64, ov);
+            tmem_st1(gbase + 128 + ob * 64 + kD, os);
+            tmem_st_wait();
+            m = m_new;
+          }
+        }
+        // P = 2^(x - m) <= 2^kRescale: one key pair in kPolyEvery on the FMA pipe (cubic),
+        // the rest on MUFU; bf16 by integer rounding, written over S in TMEM
+        const uint64_t neg_m = f32x2(-m, -m);
+        uint32_t pw[32];
+#pragma unroll
+        for (int c = 0; c < kKB; c += 2) {
+          const uint64_t d = add_f32x2(f32x2(x[c], x[c + 1]), neg_m);
+          float e0, e1;
+          if ((c / 2) % kPolyEvery == kPolyEvery - 1) {
+            exp2_poly_x2(d, e0, e1);
+          } else {
+            float d0, d1;
+            f32x2_split(d, d0, d1);
+            e0 = ex2(d0);
+            e1 = ex2(d1);
+          }
+          pw[c / 2] = pack_bf16_nonneg(e0, e1);
+        }
+        tmem_st32(gbase + buf * 64, pw);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&s.p_full[g][buf]);
+          mbar_arrive(&s.kv_empty[st]);
+        }
+        // the previous unit's output, while this unit's first P V runs
+        if (j == 0 && ul > 0 && !finalize(ul - 1)) { ok = false; break; }
       }
-      kv_it += nkb;
+      prev_q = q;
+      prev_b = b;
+      prev_r = r;
+      prev_h = h;
     }
+    if (ok && ul > 0) finalize(ul - 1);
   }
   tc_fence_before();
   __syncthreads();
