@@ -477,12 +477,6 @@ __device__ __forceinline__ void exp2_poly_x2(uint64_t d, float& e0, float& e1) {
   e1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
 }
 
-// Two non-negative finite fp32 values -> bf16x2 (lo in the low half), rounded half up,
-// with integer adds and a byte permute (no conversion instruction).
-__device__ __forceinline__ uint32_t pack_bf16_nonneg(float lo, float hi) {
-  return __byte_perm(__float_as_uint(lo) + 0x8000u, __float_as_uint(hi) + 0x8000u, 0x7632);
-}
-
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);

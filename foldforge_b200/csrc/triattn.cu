@@ -255,7 +255,7 @@ __global__ void __launch_bounds__(256, 1)
 //               is the row sum of P as the tensor core multiplied it. A unit's output is
 //               read, normalised and stored while the next unit's first block runs.
 constexpr int kKB = 64;        // keys per block
-constexpr int kKVStages = 3;
+constexpr int kKVStages = 4;
 constexpr int kAttnThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 softmax (2 groups)
 constexpr int kMaxMaskWords = 2048;  // B * ceil(N / 64) * 2 words of key-mask bits
 constexpr int kPolyEvery = 4;        // one key pair in four takes the FMA-pipe exponential
@@ -571,7 +571,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         }
         // P = 2^(x - m) <= 2^kRescale: one key pair in kPolyEvery on the FMA pipe (cubic),
-        // the rest on MUFU; bf16 by integer rounding, written over S in TMEM
+        // the rest on MUFU; packed to bf16 and written over S in TMEM
         const uint64_t neg_m = f32x2(-m, -m);
         uint32_t pw[32];
 #pragma unroll
@@ -586,7 +586,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             e0 = ex2(d0);
             e1 = ex2(d1);
           }
-          pw[c / 2] = pack_bf16_nonneg(e0, e1);
+          pw[c / 2] = pack_bf16(e0, e1);
         }
         tmem_st32(gbase + buf * 64, pw);
         tmem_st_wait();
