@@ -356,6 +356,14 @@ __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t col) {
   return row * 128u + chunk * 16u + (col & 7u) * 2u;
 }
 
+// Byte offset of element (row, col) (col in bf16 units, < 32) inside a K-major SW64 tile
+// whose rows are 64 bytes (tile base 512-byte aligned): the 16-byte chunk index is XOR-ed
+// with (row / 2) % 4, the 64-byte swizzle pattern of TMA and the UMMA descriptor.
+__device__ __forceinline__ uint32_t sw64_offset(uint32_t row, uint32_t col) {
+  const uint32_t chunk = ((col >> 3) ^ (row >> 1)) & 3u;
+  return row * 64u + chunk * 16u + (col & 7u) * 2u;
+}
+
 // ------------------------------------------------------------------ math helpers
 __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
@@ -422,6 +430,11 @@ __device__ __forceinline__ void f32x2_split(uint64_t v, float& lo, float& hi) {
 __device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
 __device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {

@@ -2,16 +2,27 @@
 // (legacy/primitives.py:20-37, legacy/reference/transition.py:28-59; swiglu
 // modules/dense/diffusion_transformer.py:36-44).
 //
-// One CTA owns 256 pair rows (two halves of 128, one TMEM lane block each) and walks the
-// 512 hidden units in 8 chunks of 64:
-//   MMA1  acc1[h] = z[h] x [W_a'; W_b'](chunk)^T    (M 128, N 128 = 64 a | 64 b, K 128)
-//   SwiGLU on acc1 with the folded input LayerNorm -> H[h] (bf16, K-major, smem)
-//   MMA2  acc2[h] += H[h] x W_sq(chunk)^T           (M 128, N 128, K 64)
-// then z + acc2 (pair mask applied in "zero" mode) goes back through the z tile and a TMA
-// store. The hidden activation never leaves the SM. Weight chunks stream through a
-// 2-deep TMA ring; the two halves alternate so one half's SwiGLU overlaps the other's MMAs.
+// One CTA owns 128 pair rows at a time (one TMEM lane block) and walks the 512 hidden
+// units in 8 chunks of 64:
+//   MMA1  A1[j % 2] = Z x [W_a'; W_b'](j)^T       (M 128, N 128 = 64 a | 64 b, K 128)
+//   SwiGLU on A1 (+ bias W beta) -> H[j % 2] (bf16)
+//   MMA2  ACC2 += H[j % 2] x W_sq(j)^T             (M 128, N 128, K 64)
+// Both products take their A operand from TMEM (Z: the tile's rows normalised by the
+// statistics warps, (z - mean) * rstd in bf16; H: written by the SwiGLU warps), so the
+// first product already is W_a' LN(z) up to the bias W beta (gamma is folded into W' and
+// 1/2 into the a rows, so the SwiGLU is  h = a/2 + b_a/2,  silu(a) b = (h + h tanh h) b).
+// Shared memory only feeds the weight operands. The first product runs two chunks ahead of the
+// second. z tiles (double-buffered) and weight chunks (3-stage ring) arrive by TMA / bulk
+// copy; the residual (pair mask applied in "zero" mode) is written over the staged z tile
+// and leaves through a TMA store. The next tile's statistics are taken before this tile's
+// residual, so its first products overlap the residual.
 //
-// Warps 0..7: epilogue (half = warp / 4); warp 8: TMA; warp 9: MMA issue.
+// TMEM columns: Z 0..63 (bf16 pairs) | A1[0] 64..191 | A1[1] 192..319 | H[0] 320..351 |
+// H[1] 352..383 | ACC2 384..511.
+// Warps 0..7: SwiGLU and residual, two warps per TMEM lane quarter (warp / 4 = which half of
+// a chunk's hidden units, and of the output channels); warps 0..3 also normalise the tile's
+// rows into Z; warp 8: TMA; warp 9: MMA issue.
+#include "../../include/foldforge_b200.h"
 #include "abi_util.h"
 #include "common.cuh"
 #include "kernels.h"
@@ -23,26 +34,30 @@ constexpr int kC = 128;
 constexpr int kHidden = 512;
 constexpr int kChunk = 64;
 constexpr int kChunks = kHidden / kChunk;
-constexpr int kRows = 256;
+constexpr int kRows = 128;
 constexpr int kThreads = 320;
-constexpr size_t kW1Chunk = 128 * kC * 2;      // 32 KB: [64 a | 64 b] x 128
-constexpr size_t kW2Chunk = kC * kChunk * 2;   // 16 KB: 128 out x 64
+constexpr int kWStages = 3;
+constexpr size_t kW1Chunk = 128 * kC * 2;      // 32 KB: [64 a | 64 b] x 128, two SW128 K-blocks
+constexpr size_t kW2Chunk = kC * kChunk * 2;   // 16 KB: 128 out x 64 hidden, SW128
 constexpr size_t kW1Bytes = kW1Chunk * kChunks;
 constexpr size_t kW2Bytes = kW2Chunk * kChunks;
 constexpr size_t kPackedBytes = kW1Bytes + kW2Bytes + 2 * 2 * kHidden * 4;
+constexpr uint32_t kColZ = 0, kColA1 = 64, kColH = 320, kColAcc2 = 384;
 
 struct Smem {
-  alignas(1024) uint8_t z[2][kC * 128 * 2];       // per half: 2 K-blocks of [128 x 128 B]
-  alignas(1024) uint8_t w1[2][kW1Chunk];
-  alignas(1024) uint8_t w2[2][kW2Chunk];
-  alignas(1024) uint8_t hbuf[2][128 * kChunk * 2];  // per half: [128 x 64] bf16
-  float wsum[2 * kHidden];
+  alignas(1024) uint8_t z[2][kRows * kC * 2];   // per tile parity: 2 K-blocks of [128 x 128 B]
+  alignas(1024) uint8_t w1[kWStages][kW1Chunk];
+  alignas(1024) uint8_t w2[kWStages][kW2Chunk];
   float bias[2 * kHidden];
-  uint64_t z_full, z_empty;
-  uint64_t w_full[2], w_empty[2];
-  uint64_t acc1_full[2], h_full[2], acc2_full[2], acc2_free[2];
+  uint64_t z_full[2], z_empty[2];
+  uint64_t w_full[kWStages], w_empty[kWStages];
+  uint64_t zt_full, zt_free;
+  uint64_t a1_full[2], h_full[2];
+  uint64_t acc2_full, acc2_free;
   uint32_t tmem_base;
 };
+
+static_assert(sizeof(Smem) + 1024 <= 232448, "transition shared memory exceeds the per-CTA limit");
 
 struct Params {
   const uint8_t* packed;
@@ -53,10 +68,13 @@ struct Params {
   int* err;
 };
 
-__device__ __forceinline__ float silu_(float a) {
-  float t;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * a));
-  return 0.5f * a * (1.0f + t);
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -67,26 +85,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const int tiles = static_cast<int>((p.rows + kRows - 1) / kRows);
+  const int my_tiles = static_cast<int>(blockIdx.x) < tiles ? (tiles - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1 : 0;
 
   if (threadIdx.x == 0) {
-    mbar_init(&s.z_full, 1);
-    mbar_init(&s.z_empty, 2);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.z_full[i], 1);
+      mbar_init(&s.z_empty[i], 1);
+      mbar_init(&s.a1_full[i], 1);
+      mbar_init(&s.h_full[i], 8);
+    }
+    for (int i = 0; i < kWStages; ++i) {
       mbar_init(&s.w_full[i], 1);
       mbar_init(&s.w_empty[i], 1);
-      mbar_init(&s.acc1_full[i], 1);
-      mbar_init(&s.h_full[i], 4);
-      mbar_init(&s.acc2_full[i], 1);
-      mbar_init(&s.acc2_free[i], 4);
     }
+    mbar_init(&s.zt_full, 4);
+    mbar_init(&s.zt_free, 1);
+    mbar_init(&s.acc2_full, 1);
+    mbar_init(&s.acc2_free, 8);
     fence_mbar_init();
   }
   {
     const float* v = reinterpret_cast<const float*>(p.packed + kW1Bytes + kW2Bytes);
-    for (int i = threadIdx.x; i < 2 * kHidden; i += kThreads) {
-      s.wsum[i] = v[i];
-      s.bias[i] = v[2 * kHidden + i];
-    }
+    for (int i = threadIdx.x; i < 2 * kHidden; i += kThreads) s.bias[i] = v[2 * kHidden + i];
   }
   if (warp == 0) {
     tmem_alloc(&s.tmem_base, 512);
@@ -102,208 +122,235 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       tma_prefetch_map(&map_z);
       tma_prefetch_map(&map_out);
-      int t_it = 0;
+      int zl = 0, wc = 0;  // z tiles and weight chunks issued
       bool ok = true;
-      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++t_it) {
-        const int row0 = tile * kRows;
-        if (!mbar_wait(&s.z_empty, (t_it & 1) ^ 1, p.err, kErrTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(&s.z_full, 2 * kC * 128 * 2);
-        for (int h = 0; h < 2; ++h)
-          for (int kb = 0; kb < 2; ++kb) tma_load_2d(s.z[h] + kb * 16384, &map_z, &s.z_full, kb * 64, row0 + h * 128);
-        for (int j = 0; j < kChunks; ++j) {
-          const int w_it = t_it * kChunks + j;
-          const int buf = w_it & 1;
-          if (!mbar_wait(&s.w_empty[buf], ((w_it >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty)) { ok = false; break; }
-          mbar_arrive_expect_tx(&s.w_full[buf], kW1Chunk + kW2Chunk);
-          bulk_load(s.w1[buf], p.packed + j * kW1Chunk, kW1Chunk, &s.w_full[buf]);
-          bulk_load(s.w2[buf], p.packed + kW1Bytes + j * kW2Chunk, kW2Chunk, &s.w_full[buf]);
+      auto load_z = [&](int ti) -> bool {  // tile ti of this CTA into buffer ti % 2
+        const int zb = ti & 1;
+        if (!mbar_wait(&s.z_empty[zb], ((ti >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty)) return false;
+        const int row0 = (static_cast<int>(blockIdx.x) + ti * static_cast<int>(gridDim.x)) * kRows;
+        mbar_arrive_expect_tx(&s.z_full[zb], kRows * kC * 2);
+        for (int kb = 0; kb < 2; ++kb) tma_load_2d(s.z[zb] + kb * 16384, &map_z, &s.z_full[zb], kb * 64, row0);
+        ++zl;
+        return true;
+      };
+      if (my_tiles > 0) ok = load_z(0);
+      for (int ti = 0; ti < my_tiles && ok; ++ti) {
+        for (int j = 0; j < kChunks; ++j, ++wc) {
+          const int st = wc % kWStages;
+          if (!mbar_wait(&s.w_empty[st], ((wc / kWStages) & 1) ^ 1, p.err, kErrTimeoutEmpty)) { ok = false; break; }
+          mbar_arrive_expect_tx(&s.w_full[st], kW1Chunk + kW2Chunk);
+          bulk_load(s.w1[st], p.packed + j * kW1Chunk, kW1Chunk, &s.w_full[st]);
+          bulk_load(s.w2[st], p.packed + kW1Bytes + j * kW2Chunk, kW2Chunk, &s.w_full[st]);
+          // the next tile's z follows the third chunk of this one
+          if (j == 2 && ti + 1 < my_tiles && !load_z(ti + 1)) { ok = false; break; }
         }
+      }
+      // every issued copy lands before the CTA may exit
+      for (int k = 0; k < 2 && k < zl; ++k) {
+        const int i = zl - 1 - k;
+        mbar_wait(&s.z_full[i & 1], (i >> 1) & 1, p.err, kErrTimeoutLoad);
+      }
+      for (int k = 0; k < kWStages && k < wc; ++k) {
+        const int i = wc - 1 - k;
+        mbar_wait(&s.w_full[i % kWStages], (i / kWStages) & 1, p.err, kErrTimeoutLoad);
       }
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc1 = idesc_bf16_f32(128, 128);
-      const uint32_t idesc2 = idesc_bf16_f32(128, 128);
-      int t_it = 0;
+      const uint32_t idesc = idesc_bf16_f32(128, 128);
       bool ok = true;
-      auto mma1 = [&](int h, int buf) {
-        const uint32_t a0 = smem_u32(s.z[h]);
-        const uint32_t b0 = smem_u32(s.w1[buf]);
+      // first product of chunk j (global weight counter wc) into A1[j % 2]; A = Z from TMEM
+      auto mma1 = [&](int j, int wc) {
+        const uint32_t b0 = smem_u32(s.w1[wc % kWStages]);
+        const uint32_t d = tmem0 + kColA1 + (j & 1) * 128;
 #pragma unroll
         for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_bf16(tmem0 + h * 128, desc_kmajor_sw128(a0 + kb * 16384) + 2 * kk,
-                     desc_kmajor_sw128(b0 + kb * 16384) + 2 * kk, idesc1, (kb | kk) != 0);
-        mma_commit(&s.acc1_full[h]);
+            mma_bf16_tmem_a(d, tmem0 + kColZ + (kb * 4 + kk) * 8, desc_kmajor_sw128(b0 + kb * 16384) + 2 * kk, idesc,
+                            (kb | kk) != 0);
+        mma_commit(&s.a1_full[j & 1]);
       };
-      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++t_it) {
-        if (!mbar_wait(&s.z_full, t_it & 1, p.err, kErrTimeoutLoad)) break;
-        const int w0 = t_it * kChunks;
-        if (!mbar_wait(&s.w_full[w0 & 1], (w0 >> 1) & 1, p.err, kErrTimeoutLoad)) break;
-        tc_fence_after();
-        mma1(0, w0 & 1);
-        mma1(1, w0 & 1);
-        for (int j = 0; j < kChunks && ok; ++j) {
-          const int w_it = w0 + j;
-          const int buf = w_it & 1;
-          for (int h = 0; h < 2; ++h) {
-            if (!mbar_wait(&s.h_full[h], j & 1, p.err, kErrTimeoutMma)) { ok = false; break; }
-            if (j == 0 && !mbar_wait(&s.acc2_free[h], (t_it & 1) ^ 1, p.err, kErrTimeoutEmpty)) { ok = false; break; }
-            tc_fence_after();
-            const uint32_t a0 = smem_u32(s.hbuf[h]);
-            const uint32_t b0 = smem_u32(s.w2[buf]);
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              mma_bf16(tmem0 + 256 + h * 128, desc_kmajor_sw128(a0) + 2 * kk, desc_kmajor_sw128(b0) + 2 * kk, idesc2,
-                       (j | kk) != 0);
-            if (j + 1 < kChunks) {
-              const int nb = (w_it + 1) & 1;
-              if (h == 0 && !mbar_wait(&s.w_full[nb], ((w_it + 1) >> 1) & 1, p.err, kErrTimeoutLoad)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              mma1(h, nb);
-            }
+      for (int ti = 0; ti < my_tiles && ok; ++ti) {
+        const int w0 = ti * kChunks;
+        if (!mbar_wait(&s.zt_full, ti & 1, p.err, kErrTimeoutLoad)) break;
+        // prologue: chunks 0 and 1 (A1[0] / A1[1] were last read by chunks 6 / 7 of the
+        // previous tile, whose H this thread already waited for)
+        for (int j = 0; j < 2 && ok; ++j) {
+          if (!mbar_wait(&s.w_full[(w0 + j) % kWStages], ((w0 + j) / kWStages) & 1, p.err, kErrTimeoutLoad)) {
+            ok = false;
+            break;
           }
-          if (!ok) break;
-          mma_commit(&s.w_empty[buf]);
+          tc_fence_after();
+          mma1(j, w0 + j);
+        }
+        for (int j = 0; j < kChunks && ok; ++j) {
+          const int wc = w0 + j;
+          const int u = ti * (kChunks / 2) + j / 2;  // use count of A1 / H buffer j % 2
+          if (j + 2 < kChunks &&
+              !mbar_wait(&s.w_full[(wc + 2) % kWStages], ((wc + 2) / kWStages) & 1, p.err, kErrTimeoutLoad)) {
+            ok = false;
+            break;
+          }
+          if (!mbar_wait(&s.h_full[j & 1], u & 1, p.err, kErrTimeoutMma)) { ok = false; break; }
+          if (j == 0 && !mbar_wait(&s.acc2_free, (ti & 1) ^ 1, p.err, kErrTimeoutEmpty)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t b0 = smem_u32(s.w2[wc % kWStages]);
+#pragma unroll
+          for (int kk = 0; kk < kChunk / 16; ++kk)
+            mma_bf16_tmem_a(tmem0 + kColAcc2, tmem0 + kColH + (j & 1) * 32 + kk * 8, desc_kmajor_sw128(b0) + 2 * kk,
+                            idesc, (j | kk) != 0);
+          if (j + 2 < kChunks) mma1(j + 2, wc + 2);
+          mma_commit(&s.w_empty[wc % kWStages]);
+          if (j == kChunks - 3) mma_commit(&s.zt_free);  // the tile's last first product is issued
         }
         if (!ok) break;
-        mma_commit(&s.acc2_full[0]);
-        mma_commit(&s.acc2_full[1]);
+        mma_commit(&s.acc2_full);
       }
     }
   } else {
-    // ------------------------------------------------------------ epilogue warps
-    const int h = warp / 4;
+    // ------------------------------------------------------------ SwiGLU / residual warps
+    const int part = warp / 4;  // hidden units [32 part, 32 part + 32) of each chunk; output channels [64 part, +64)
     const int t = (warp & 3) * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    uint8_t* zt = s.z[h];
-    uint8_t* hb = s.hbuf[h];
-    int t_it = 0;
+    const uint32_t tl = tmem0 + lane_off;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t_it) {
-      const int64_t row = static_cast<int64_t>(tile) * kRows + h * 128 + t;
-      bool w = mbar_wait(&s.z_full, t_it & 1, p.err, kErrTimeoutLoad);
-      ok = __all_sync(0xFFFFFFFFu, w) && ok;
-      float mean = 0.f, rstd = 0.f;
-      if (ok) {
-        float sum = 0.f;
-#pragma unroll
-        for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const uint4 v = *reinterpret_cast<const uint4*>(zt + kb * 16384 + sw128_offset(t, q * 8));
-            const uint32_t u[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) sum += bf16_lo(u[e]) + bf16_hi(u[e]);
-          }
-        mean = sum * (1.0f / kC);
-        float q2 = 0.f;
-#pragma unroll
-        for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const uint4 v = *reinterpret_cast<const uint4*>(zt + kb * 16384 + sw128_offset(t, q * 8));
-            const uint32_t u[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float a = bf16_lo(u[e]) - mean, b = bf16_hi(u[e]) - mean;
-              q2 += a * a + b * b;
-            }
-          }
-        rstd = rsqrtf(q2 * (1.0f / kC) + 1e-5f);
+    // row t of tile ti, LayerNorm-normalised (no affine: gamma and beta are in the weights),
+    // into Z (warps 0..3)
+    auto stage_z = [&](int ti) {
+      const int zb = ti & 1;
+      bool w = mbar_wait(&s.z_full[zb], (ti >> 1) & 1, p.err, kErrTimeoutLoad);
+      if (ti > 0) w = w && mbar_wait(&s.zt_free, (ti - 1) & 1, p.err, kErrTimeoutMma);
+      if (!__all_sync(0xFFFFFFFFu, w)) {
+        ok = false;
+        return;
       }
-      for (int j = 0; j < kChunks; ++j) {
-        bool w1 = ok && mbar_wait(&s.acc1_full[h], j & 1, p.err, kErrTimeoutMma);
-        ok = __all_sync(0xFFFFFFFFu, w1);
-        tc_fence_after();
-        if (ok) {
-          const float* ws = s.wsum + j * 128;
-          const float* bs = s.bias + j * 128;
-#pragma unroll 1
-          for (int half32 = 0; half32 < 2; ++half32) {
-            uint32_t va[32], vb[32];
-            tmem_ld32(tmem0 + lane_off + h * 128 + half32 * 32, va);
-            tmem_ld32(tmem0 + lane_off + h * 128 + 64 + half32 * 32, vb);
-            tmem_ld_wait();
-            uint32_t packed[16];
+      tc_fence_after();
+      const uint8_t* zt = s.z[zb];
+      uint32_t zw[64];
+      float sum = 0.f;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              float hv[2];
+      for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
-              for (int e = 0; e < 2; ++e) {
-                const int c = half32 * 32 + 2 * i + e;
-                const float a = rstd * (__uint_as_float(va[2 * i + e]) - mean * ws[c]) + bs[c];
-                const float b = rstd * (__uint_as_float(vb[2 * i + e]) - mean * ws[64 + c]) + bs[64 + c];
-                hv[e] = silu_(a) * b;
-              }
-              packed[i] = pack_bf16(hv[0], hv[1]);
-            }
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-              *reinterpret_cast<uint4*>(hb + sw128_offset(t, half32 * 32 + q * 8)) =
-                  make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-          }
+        for (int q = 0; q < 8; ++q) {
+          const uint4 v = *reinterpret_cast<const uint4*>(zt + kb * 16384 + sw128_offset(t, q * 8));
+          const int w0 = (kb * 8 + q) * 4;
+          zw[w0] = v.x;
+          zw[w0 + 1] = v.y;
+          zw[w0 + 2] = v.z;
+          zw[w0 + 3] = v.w;
         }
-        fence_async_smem();
+#pragma unroll
+      for (int i = 0; i < 64; ++i) sum += bf16_lo(zw[i]) + bf16_hi(zw[i]);
+      const float mean = sum * (1.0f / kC);
+      float q2 = 0.f;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float a = bf16_lo(zw[i]) - mean, b = bf16_hi(zw[i]) - mean;
+        q2 += a * a + b * b;
+      }
+      const float rstd = rsqrtf(q2 * (1.0f / kC) + 1e-5f);
+      const float nm = -mean * rstd;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) zw[i] = pack_bf16(fmaf(bf16_lo(zw[i]), rstd, nm), fmaf(bf16_hi(zw[i]), rstd, nm));
+      tmem_st32(tl + kColZ, *reinterpret_cast<uint32_t(*)[32]>(zw));
+      tmem_st32(tl + kColZ + 32, *reinterpret_cast<uint32_t(*)[32]>(zw + 32));
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.zt_full);
+    };
+    if (part == 0 && my_tiles > 0) stage_z(0);
+    for (int ti = 0; ti < my_tiles; ++ti) {
+      const int zb = ti & 1;
+      const int64_t row = (static_cast<int64_t>(blockIdx.x) + static_cast<int64_t>(ti) * gridDim.x) * kRows + t;
+      for (int j = 0; j < kChunks && ok; ++j) {
+        const int u = ti * (kChunks / 2) + j / 2;
+        if (!__all_sync(0xFFFFFFFFu, mbar_wait(&s.a1_full[j & 1], u & 1, p.err, kErrTimeoutMma))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t va[32], vb[32];
+        tmem_ld32(tl + kColA1 + (j & 1) * 128 + part * 32, va);
+        tmem_ld32(tl + kColA1 + (j & 1) * 128 + 64 + part * 32, vb);
+        tmem_ld_wait();
+        const float* bs = s.bias + j * 128 + part * 32;
+        uint32_t hw[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int c = 2 * i;
+          // h = a / 2 (the a rows carry the 1/2), b; silu(a) b = (h + h tanh h) b
+          const uint64_t hh = add_f32x2(f32x2(__uint_as_float(va[c]), __uint_as_float(va[c + 1])), f32x2(bs[c], bs[c + 1]));
+          const uint64_t b = add_f32x2(f32x2(__uint_as_float(vb[c]), __uint_as_float(vb[c + 1])), f32x2(bs[64 + c], bs[65 + c]));
+          float h0, h1;
+          f32x2_split(hh, h0, h1);
+          const uint64_t sa = fma_f32x2(hh, f32x2(tanh_fast(h0), tanh_fast(h1)), hh);
+          float o0, o1;
+          f32x2_split(mul_f32x2(sa, b), o0, o1);
+          hw[i] = pack_bf16(o0, o1);
+        }
+        tmem_st16(tl + kColH + (j & 1) * 32 + part * 16, hw);
+        tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&s.h_full[h]);
+        if (lane == 0) mbar_arrive(&s.h_full[j & 1]);
       }
-      bool w2 = ok && mbar_wait(&s.acc2_full[h], t_it & 1, p.err, kErrTimeoutMma);
-      ok = __all_sync(0xFFFFFFFFu, w2);
-      tc_fence_after();
+      // the next tile's statistics and Z, so its first products overlap this residual
+      if (part == 0 && ok && ti + 1 < my_tiles) stage_z(ti + 1);
+      // residual: z (staged tile) + ACC2 written over the tile, then one TMA store
+      if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.acc2_full, ti & 1, p.err, kErrTimeoutMma));
       if (ok) {
+        tc_fence_after();
         bool keep = true;
         if (p.masked_zero && row < p.rows) {
-          const int64_t j = row % p.N;
+          const int64_t jj = row % p.N;
           const int64_t bi = row / p.N;  // b * N + i
           const int64_t b = bi / p.N;
-          keep = p.mask[bi] && p.mask[b * p.N + j];
+          keep = p.mask[bi] && p.mask[b * p.N + jj];
         }
+        uint8_t* zt = s.z[zb];
 #pragma unroll 1
-        for (int cc = 0; cc < kC; cc += 32) {
+        for (int cc = 0; cc < 64; cc += 32) {
           uint32_t vo[32];
-          tmem_ld32(tmem0 + lane_off + 256 + h * 128 + cc, vo);
+          tmem_ld32(tl + kColAcc2 + part * 64 + cc, vo);
           tmem_ld_wait();
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            const int ch = cc + q * 8;
+            const int ch = part * 64 + cc + q * 8;
             uint8_t* addr = zt + (ch / 64) * 16384 + sw128_offset(t, ch % 64);
             const uint4 zv = *reinterpret_cast<const uint4*>(addr);
-            const uint32_t u[4] = {zv.x, zv.y, zv.z, zv.w};
+            const uint32_t zw[4] = {zv.x, zv.y, zv.z, zv.w};
             uint32_t o[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const float d0 = keep ? __uint_as_float(vo[q * 8 + 2 * e]) : 0.f;
               const float d1 = keep ? __uint_as_float(vo[q * 8 + 2 * e + 1]) : 0.f;
-              o[e] = pack_bf16(bf16_lo(u[e]) + d0, bf16_hi(u[e]) + d1);
+              o[e] = pack_bf16(bf16_lo(zw[e]) + d0, bf16_hi(zw[e]) + d1);
             }
             *reinterpret_cast<uint4*>(addr) = make_uint4(o[0], o[1], o[2], o[3]);
           }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.acc2_free);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s.acc2_free[h]);
       fence_async_smem();
-      ok = !named_barrier_or(1 + h, 128, !ok);  // half-uniform from here on
-      if (t == 0) {
+      ok = !named_barrier_or(1, 256, !ok);  // uniform over the eight warps from here on
+      if (threadIdx.x == 0) {
         if (ok) {
-          const int r0 = static_cast<int>(static_cast<int64_t>(tile) * kRows + h * 128);
-          tma_store_2d(&map_out, zt, 0, r0);
-          tma_store_2d(&map_out, zt + 16384, 64, r0);
+          const int r0 = static_cast<int>(row - t);
+          tma_store_2d(&map_out, s.z[zb], 0, r0);
+          tma_store_2d(&map_out, s.z[zb] + 16384, 64, r0);
           tma_store_commit();
           tma_store_wait_read0();
         }
-        mbar_arrive(&s.z_empty);
+        mbar_arrive(&s.z_empty[zb]);
       }
       if (!ok) break;
     }
+    if (threadIdx.x == 0) tma_store_wait_all0();
   }
   tc_fence_before();
   __syncthreads();
@@ -323,12 +370,15 @@ int transition_prepare(const TransitionWeights& w, void* packed, cudaStream_t st
   float* vec = reinterpret_cast<float*>(img + kW1Bytes + kW2Bytes);
   int rc = 0;
   for (int j = 0; j < kChunks && rc == 0; ++j) {
+    // first-product rows: 1/2 W_a rows [64 j, 64 j + 64) then W_b rows, gamma folded; the
+    // bias entries (W beta) j * 128 + [0, 128) follow the same row order
     rc = launch_pack_weight(w.expand_a + static_cast<int64_t>(j) * kChunk * kC, kChunk, kC, w.ln_w, w.ln_b,
-                            img + j * kW1Chunk, 0, 128, vec + j * 128, vec + 2 * kHidden + j * 128, stream);
+                            img + j * kW1Chunk, 0, 128, vec + j * 128, vec + 2 * kHidden + j * 128, stream, 0.5f);
     if (rc == 0)
       rc = launch_pack_weight(w.expand_b + static_cast<int64_t>(j) * kChunk * kC, kChunk, kC, w.ln_w, w.ln_b,
                               img + j * kW1Chunk, 64, 128, vec + j * 128, vec + 2 * kHidden + j * 128, stream);
   }
+  // W_sq [128 x 512]: chunk j = 64-column block j of the K-major SW128 image (16 KB each)
   if (rc == 0)
     rc = launch_pack_weight(w.squeeze, kC, kHidden, nullptr, nullptr, img + kW1Bytes, 0, kC, nullptr, nullptr, stream);
   return rc;
@@ -337,10 +387,13 @@ int transition_prepare(const TransitionWeights& w, void* packed, cudaStream_t st
 int transition_forward(const void* z, const uint8_t* mask, const void* packed, void* out, int B, int N,
                        int masked_zero, const DeviceInfo& info, cudaStream_t stream) {
   const int64_t rows = static_cast<int64_t>(B) * N * N;
+  if (rows >= (static_cast<int64_t>(1) << 31))
+    return fail(FFB_ERR_UNSUPPORTED, "transition: %lld pair rows exceed the 2^31 TMA row range",
+                static_cast<long long>(rows));
   CUtensorMap map_z, map_out;
   const uint64_t dims[2] = {kC, static_cast<uint64_t>(rows)};
   const uint64_t strides[1] = {kC * 2};
-  const uint32_t box[2] = {64, 128};
+  const uint32_t box[2] = {64, kRows};
   int st = make_map(&map_z, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, z, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
   st = make_map(&map_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
