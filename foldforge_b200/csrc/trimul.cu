@@ -12,10 +12,11 @@
 //     plain K-major GEMM per channel. The incoming direction reads COLUMN tiles of z
 //     (pairs (k, a) for fixed a), which makes its contraction the same GEMM.
 //  2. the per-channel contraction U_c = L_c R_c^T on the batched tcgen05 GEMM (gemm.cu).
-//  3. trimul_out: per 128-pair tile, the centre LayerNorm of u (channel-major in smem,
-//     transposed into a K-major operand), two tcgen05 GEMMs (gate from raw z with the
-//     folded input LayerNorm, output projection from LN_out(u)), sigmoid gate, mask and
-//     residual, written back through the z tile and a TMA store.
+//  3. trimul_ustats (per-pair mean / rstd of u over its 128 channels, one coalesced pass)
+//     and trimul_out: per 128-pair tile, two tcgen05 GEMMs (gate from raw z, output
+//     projection from raw u) with both LayerNorms folded into the epilogue through the
+//     per-pair statistics (z's from step 1, u's from trimul_ustats), sigmoid gate, mask
+//     and residual, written back through the z tile and a TMA store.
 //
 // Kernels 1 and 3 run G = 2 independent groups of 4 warps per CTA (one CTA per SM,
 // persistent over tiles), sharing the resident weights; each group has its own z stage and
@@ -116,6 +117,7 @@ struct ProjParams {
   const uint8_t* mask;  // [B, N]
   __nv_bfloat16* left;  // [B*h, N, Np]
   __nv_bfloat16* right;
+  float2* zstats;       // [B, N, N] (mean, rstd) of the input LayerNorm, natural pair order
   int B, N, Np;
   int outgoing;
   int* err;
@@ -245,8 +247,14 @@ __global__ void __launch_bounds__(kPThreads, 1)
       const int rr = tile / tiles_per_row;
       const int b = rr / p.N, r = rr - b * p.N;
       const int k = c0 + t;
+      const float rstd = rsqrtf(q2 * (1.0f / kC) + 1e-5f);
       s.mean[buf][t] = mean;
-      s.rstd[buf][t] = rsqrtf(q2 * (1.0f / kC) + 1e-5f);
+      s.rstd[buf][t] = rstd;
+      if (k < p.N) {
+        // natural pair (i, j): outgoing row tile (r, k), incoming column tile (k, r)
+        const int64_t pi = p.outgoing ? r : k, pj = p.outgoing ? k : r;
+        p.zstats[(static_cast<int64_t>(b) * p.N + pi) * p.N + pj] = make_float2(mean, rstd);
+      }
       s.pm[buf][t] = (k < p.N && p.mask[b * p.N + r] && p.mask[b * p.N + k]) ? 1.0f : 0.0f;
       __syncwarp();
       if (lane == 0) {
@@ -358,16 +366,61 @@ struct OutSmem {
 struct OutParams {
   const uint8_t* packed;
   const uint8_t* mask;
+  const float2* zstats;  // [B, N, N] (mean, rstd) of z (input LayerNorm)
+  const float2* ustats;  // [B, N, N] (mean, rstd) of u (centre LayerNorm)
   int B, N;
   int masked_zero;
   int* err;
 };
 
-// u[c][p] in the MN-major SW128 tile
-__device__ __forceinline__ float u_at(const uint8_t* ut, int c, int p) {
-  const int blk = p >> 6, pp = p & 63;
-  const uint32_t off = static_cast<uint32_t>(blk) * (kH * 128) + c * 128 + ((((pp >> 3) ^ (c & 7)) << 4)) + (pp & 7) * 2;
-  return __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(ut + off));
+// Per-pair mean and 1/sqrt(var + 1e-5) of u over its 128 channels (u channel-major
+// [B*h, N, Np]). A thread owns 8 consecutive pairs of one row and walks the channels with
+// 16-byte loads (coalesced across the warp); the variance is accumulated about the first
+// channel's value (shifted data, no cancellation for rows whose mean is large).
+__global__ void __launch_bounds__(256) trimul_ustats_kernel(const __nv_bfloat16* __restrict__ u,
+                                                             float2* __restrict__ ustats, int B, int N, int Np) {
+  const int groups = (N + 7) / 8;
+  const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (gid >= static_cast<int64_t>(B) * N * groups) return;
+  const int g = static_cast<int>(gid % groups);
+  const int64_t bi = gid / groups;  // b * N + i
+  const int b = static_cast<int>(bi / N), i = static_cast<int>(bi % N);
+  const int64_t plane = static_cast<int64_t>(N) * Np;
+  const __nv_bfloat16* src = u + (static_cast<int64_t>(b) * kH * N + i) * Np + g * 8;
+  float shift[8], s1[8], s2[8];
+  {
+    const uint4 v = *reinterpret_cast<const uint4*>(src);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      shift[2 * e] = bf16_lo(w[e]);
+      shift[2 * e + 1] = bf16_hi(w[e]);
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s1[e] = s2[e] = 0.f;
+  }
+#pragma unroll 8
+  for (int c = 1; c < kH; ++c) {
+    const uint4 v = *reinterpret_cast<const uint4*>(src + c * plane);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float d0 = bf16_lo(w[e]) - shift[2 * e], d1 = bf16_hi(w[e]) - shift[2 * e + 1];
+      s1[2 * e] += d0;
+      s2[2 * e] = fmaf(d0, d0, s2[2 * e]);
+      s1[2 * e + 1] += d1;
+      s2[2 * e + 1] = fmaf(d1, d1, s2[2 * e + 1]);
+    }
+  }
+  float2* dst = ustats + bi * N + g * 8;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    if (g * 8 + e < N) {
+      const float m = s1[e] * (1.0f / kH);
+      const float var = fmaxf(s2[e] * (1.0f / kH) - m * m, 0.f);
+      dst[e] = make_float2(shift[e] + m, rsqrtf(var + 1e-5f));
+    }
+  }
 }
 
 __global__ void __launch_bounds__(kOThreads, 1)
@@ -462,63 +515,30 @@ __global__ void __launch_bounds__(kOThreads, 1)
       }
     }
   } else if (warp < 4) {
-    // statistics: thread t handles pairs t and t + 64 of the tile
+    // per-pair statistics (precomputed) and keep mask: thread t handles pairs t and t + 64
     const int t = (warp - 2) * 32 + lane;
     int it = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
-      const int st = it % kOStages, buf = it & 1;
-      const bool w1 = mbar_wait(&s.full[st], (it / kOStages) & 1, p.err, kErrTimeoutLoad);
+      const int buf = it & 1;
       const bool w2 = mbar_wait(&s.st_free[buf], ((it >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty);
-      if (!__all_sync(0xFFFFFFFFu, w1 && w2)) break;
+      if (!__all_sync(0xFFFFFFFFu, w2)) break;
       const int c0 = (tile % tiles_per_row) * kOTile;
       const int rr = tile / tiles_per_row;
       const int b = rr / p.N, r = rr - b * p.N;
-      const uint8_t* zt = s.z[st];
-      const uint8_t* ut = s.u[st];
-#pragma unroll 1
+#pragma unroll
       for (int k = 0; k < 2; ++k) {
         const int pp = t + 64 * k;
-        // z row statistics
-        float sum = 0.f;
-        uint4 v[16];
-#pragma unroll
-        for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-          for (int q = 0; q < 8; ++q)
-            v[kb * 8 + q] = *reinterpret_cast<const uint4*>(zt + kb * (kOTile * 128) + sw128_offset(pp, q * 8));
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) sum += bf16_lo(w[j]) + bf16_hi(w[j]);
-        }
-        const float zmean = sum * (1.0f / kC);
-        float q2 = 0.f;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float a = bf16_lo(w[j]) - zmean, bb = bf16_hi(w[j]) - zmean;
-            q2 += a * a + bb * bb;
-          }
-        }
-        // u column statistics (two-pass over the 128 channels)
-        float us = 0.f;
-#pragma unroll 8
-        for (int c = 0; c < kH; ++c) us += u_at(ut, c, pp);
-        const float umean = us * (1.0f / kH);
-        float uq = 0.f;
-#pragma unroll 8
-        for (int c = 0; c < kH; ++c) {
-          const float d = u_at(ut, c, pp) - umean;
-          uq += d * d;
-        }
         const int j = c0 + pp;
-        s.zm[buf][pp] = zmean;
-        s.zr[buf][pp] = rsqrtf(q2 * (1.0f / kC) + 1e-5f);
-        s.um[buf][pp] = umean;
-        s.ur[buf][pp] = rsqrtf(uq * (1.0f / kH) + 1e-5f);
+        float2 zs = make_float2(0.f, 0.f), us = make_float2(0.f, 0.f);
+        if (j < p.N) {
+          const int64_t pair = (static_cast<int64_t>(b) * p.N + r) * p.N + j;
+          zs = p.zstats[pair];
+          us = p.ustats[pair];
+        }
+        s.zm[buf][pp] = zs.x;
+        s.zr[buf][pp] = zs.y;
+        s.um[buf][pp] = us.x;
+        s.ur[buf][pp] = us.y;
         s.keep[buf][pp] = (!p.masked_zero || (j < p.N && p.mask[b * p.N + r] && p.mask[b * p.N + j])) ? 1.f : 0.f;
       }
       __syncwarp();
@@ -602,7 +622,8 @@ size_t trimul_workspace_bytes(int B, int N) {
   const size_t np = (static_cast<size_t>(N) + 7) / 8 * 8;
   const size_t one = static_cast<size_t>(B) * kH * N * np * 2;
   const size_t aligned = (one + 255) / 256 * 256;
-  return 3 * aligned;
+  const size_t stats = (static_cast<size_t>(B) * N * N * 8 + 255) / 256 * 256;
+  return 3 * aligned + 2 * stats;  // L, R, U, z statistics, u statistics
 }
 
 int trimul_prepare(const TriMulWeights& w, void* packed, cudaStream_t stream) {
@@ -630,6 +651,9 @@ int trimul_forward(const void* z, const uint8_t* mask, const void* packed, void*
   __nv_bfloat16* left = reinterpret_cast<__nv_bfloat16*>(ws);
   __nv_bfloat16* right = reinterpret_cast<__nv_bfloat16*>(ws + aligned);
   __nv_bfloat16* u = reinterpret_cast<__nv_bfloat16*>(ws + 2 * aligned);
+  const size_t stats_bytes = (static_cast<size_t>(B) * N * N * 8 + 255) / 256 * 256;
+  float2* zstats = reinterpret_cast<float2*>(ws + 3 * aligned);
+  float2* ustats = reinterpret_cast<float2*>(ws + 3 * aligned + stats_bytes);
   const int tiles = B * N * ((N + kTile - 1) / kTile);
   const int grid_groups = (tiles + kGroups - 1) / kGroups;
   const int grid = grid_groups < info.num_sms ? grid_groups : info.num_sms;
@@ -649,7 +673,7 @@ int trimul_forward(const void* z, const uint8_t* mask, const void* packed, void*
     if (st) return st;
   }
   if (stages & 1) {
-    ProjParams pp{static_cast<const uint8_t*>(packed), mask, left, right, B, N, np, outgoing, info.err};
+    ProjParams pp{static_cast<const uint8_t*>(packed), mask, left, right, zstats, B, N, np, outgoing, info.err};
     const size_t proj_smem = sizeof(ProjSmem) + 1024;
     cudaFuncSetAttribute(trimul_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(proj_smem));
     trimul_proj_kernel<<<pgrid, kPThreads, proj_smem, stream>>>(map_z, pp);
@@ -707,7 +731,13 @@ int trimul_forward(const void* z, const uint8_t* mask, const void* packed, void*
     if (st) return st;
   }
   if (!(stages & 4)) return 0;
-  OutParams op{static_cast<const uint8_t*>(packed), mask, B, N, masked_zero, info.err};
+  {
+    const int64_t threads = static_cast<int64_t>(B) * N * ((N + 7) / 8);
+    trimul_ustats_kernel<<<static_cast<int>((threads + 255) / 256), 256, 0, stream>>>(u, ustats, B, N, np);
+    st = cuda_status(static_cast<int>(cudaGetLastError()), "trimul_ustats launch");
+    if (st) return st;
+  }
+  OutParams op{static_cast<const uint8_t*>(packed), mask, zstats, ustats, B, N, masked_zero, info.err};
   const size_t out_smem = sizeof(OutSmem) + 1024;
   const int otiles = B * N * ((N + kOTile - 1) / kOTile);
   const int ogrid = otiles < info.num_sms ? otiles : info.num_sms;
