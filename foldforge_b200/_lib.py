@@ -56,12 +56,25 @@ SIGNATURES: dict[str, list] = {
     "ffb_single_transition_fwd_noalloc": [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p],
     "ffb_single_transition_fwd": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_size_t, c_int, c_int,
                                   c_int, c_void_p],
+    # row-sharded pieces (B = 1)
+    "ffb_trimul_shard_proj": [c_void_p] * 6 + [c_int, c_int, c_int, c_void_p],
+    "ffb_trimul_shard_contract": [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p],
+    "ffb_trimul_shard_out": [c_void_p] * 7 + [c_int, c_int, c_int, c_int, c_void_p],
+    "ffb_triattn_shard_proj": [c_void_p] * 6 + [c_int, c_int, c_void_p],
+    "ffb_triattn_shard_attn": [c_void_p] * 6 + [c_int, c_int, c_int, c_void_p],
+    "ffb_triattn_shard_out": [c_void_p] * 5 + [c_int, c_int, c_int, c_int, c_void_p],
+    "ffb_transition_shard_fwd": [c_void_p] * 4 + [c_int, c_int, c_int, c_int, c_void_p],
+    "ffb_apb_shard_pair_bias": [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p],
+    "ffb_apb_single_workspace_bytes": [c_int],
+    "ffb_apb_shard_single": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_float, c_void_p, c_void_p,
+                             ctypes.c_size_t, c_int, c_int, c_void_p],
 }
 
 #: entry points that return a size_t instead of a status
 SIZE_RESULT = {"ffb_apb_packed_bytes", "ffb_apb_workspace_bytes", "ffb_single_transition_packed_bytes",
-               "ffb_single_transition_workspace_bytes", "ffb_transition_packed_bytes", "ffb_trimul_packed_bytes", "ffb_trimul_workspace_bytes", "ffb_triattn_packed_bytes",
-               "ffb_triattn_workspace_bytes"}
+               "ffb_single_transition_workspace_bytes", "ffb_transition_packed_bytes", "ffb_trimul_packed_bytes",
+               "ffb_trimul_workspace_bytes", "ffb_triattn_packed_bytes", "ffb_triattn_workspace_bytes",
+               "ffb_apb_single_workspace_bytes"}
 
 STATUS = {0: "FFB_OK", 1: "FFB_ERR_ARG", 2: "FFB_ERR_UNSUPPORTED", 3: "FFB_ERR_CUDA", 4: "FFB_ERR_DEVICE"}
 
@@ -113,6 +126,10 @@ def load() -> ctypes.CDLL:
 LAUNCHES = {
     "ffb_layernorm_fwd": 1, "ffb_gemm_bf16_nt": 1, "ffb_trimul_fwd": 4, "ffb_triattn_fwd": 3,
     "ffb_transition_fwd": 1, "ffb_apb_fwd": 5, "ffb_single_transition_fwd": 3,
+    "ffb_trimul_shard_proj": 1, "ffb_trimul_shard_contract": 1, "ffb_trimul_shard_out": 2,
+    "ffb_triattn_shard_proj": 1, "ffb_triattn_shard_attn": 1, "ffb_triattn_shard_out": 1,
+    "ffb_transition_shard_fwd": 1, "ffb_apb_shard_pair_bias": 1, "ffb_apb_shard_single": 4,
+    "ffb_single_transition_fwd_noalloc": 3,
 }
 launch_count = 0
 

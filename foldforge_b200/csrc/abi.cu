@@ -382,3 +382,153 @@ int ffb_single_transition_fwd(const void* s, const uint8_t* mask, const void* pa
 }
 
 }  // extern "C"
+
+// ---- row-sharded pieces (axial parallelism; B = 1; the rank holds pair rows
+// [row0, row0 + R) of an N x N pair, or of its transpose for the column-wise ops)
+namespace {
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+int shard_args(const char* what, int R, int N, int row0) {
+  if (R <= 0 || N <= 0 || row0 < 0 || row0 + R > N)
+    return fail(FFB_ERR_ARG, "%s: rows [%d, %d) of N=%d", what, row0, row0 + R, N);
+  if (static_cast<int64_t>(R) * N >= (int64_t(1) << 31) - 256) return fail(FFB_ERR_UNSUPPORTED, "%s: too many pairs", what);
+  return FFB_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int ffb_trimul_shard_proj(const void* z, const uint8_t* mask, const void* packed, void* left, void* right,
+                          void* zstats, int R, int N, int row0, void* stream) {
+  int st = shard_args("trimul_shard_proj", R, N, row0);
+  if (st) return st;
+  if (!z || !mask || !packed || !left || !right || !zstats) return fail(FFB_ERR_ARG, "trimul_shard_proj: null pointer");
+  if (!aligned16(z) || !aligned16(packed) || !aligned16(left) || !aligned16(right) || !aligned16(zstats))
+    return fail(FFB_ERR_ARG, "trimul_shard_proj: misaligned pointer");
+  DeviceInfo info;
+  st = device_info(&info);
+  if (st != FFB_OK) return st;
+  return trimul_shard_proj(z, mask, packed, left, right, zstats, R, N, row0, info, static_cast<cudaStream_t>(stream));
+}
+
+int ffb_trimul_shard_contract(const void* left, const void* right_all, void* u, int R, int N, void* stream) {
+  int st = shard_args("trimul_shard_contract", R, N, 0);
+  if (st) return st;
+  if (!left || !right_all || !u) return fail(FFB_ERR_ARG, "trimul_shard_contract: null pointer");
+  if (!aligned16(left) || !aligned16(right_all) || !aligned16(u))
+    return fail(FFB_ERR_ARG, "trimul_shard_contract: misaligned pointer");
+  DeviceInfo info;
+  st = device_info(&info);
+  if (st != FFB_OK) return st;
+  return trimul_shard_contract(left, right_all, u, R, N, info, static_cast<cudaStream_t>(stream));
+}
+
+int ffb_trimul_shard_out(const void* z, const uint8_t* mask, const void* packed, const void* u, const void* zstats,
+                         void* ustats, void* out, int R, int N, int row0, int masked, void* stream) {
+  int st = shard_args("trimul_shard_out", R, N, row0);
+  if (st) return st;
+  if (!z || !mask || !packed || !u || !zstats || !ustats || !out) return fail(FFB_ERR_ARG, "trimul_shard_out: null pointer");
+  if (z == out) return fail(FFB_ERR_ARG, "trimul_shard_out: out must not alias z");
+  if (masked != FFB_MASKED_COMPUTE && masked != FFB_MASKED_ZERO) return fail(FFB_ERR_ARG, "trimul_shard_out: masked=%d", masked);
+  if (!aligned16(z) || !aligned16(packed) || !aligned16(u) || !aligned16(zstats) || !aligned16(ustats) || !aligned16(out))
+    return fail(FFB_ERR_ARG, "trimul_shard_out: misaligned pointer");
+  DeviceInfo info;
+  st = device_info(&info);
+  if (st != FFB_OK) return st;
+  return trimul_shard_out(z, mask, packed, u, zstats, ustats, out, R, N, row0, masked == FFB_MASKED_ZERO, info,
+                          static_cast<cudaStream_t>(stream));
+}
+
+int ffb_triattn_shard_proj(const void* z, const void* packed, void* q, void* k, void* vt, void* bias_rows, int R, int N,
+                           void* stream) {
+  int st = shard_args("triattn_shard_proj", R, N, 0);
+  if (st) return st;
+  if (!z || !packed || !q || !k || !vt || !bias_rows) return fail(FFB_ERR_ARG, "triattn_shard_proj: null pointer");
+  if (!aligned16(z) || !aligned16(packed) || !aligned16(q) || !aligned16(k) || !aligned16(vt) || !aligned16(bias_rows))
+    return fail(FFB_ERR_ARG, "triattn_shard_proj: misaligned pointer");
+  DeviceInfo info;
+  st = device_info(&info);
+  if (st != FFB_OK) return st;
+  return triattn_shard_proj(z, packed, q, k, vt, bias_rows, R, N, info, static_cast<cudaStream_t>(stream));
+}
+
+int ffb_triattn_shard_attn(const void* q, const void* k, const void* vt, const void* bias_all, const uint8_t* mask,
+                           void* o, int R, int N, int row0, void* stream) {
+  int st = shard_args("triattn_shard_attn", R, N, row0);
+  if (st) return st;
+  if (!q || !k || !vt || !bias_all || !mask || !o) return fail(FFB_ERR_ARG, "triattn_shard_attn: null pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(vt) || !aligned16(bias_all) || !aligned16(o))
+    return fail(FFB_ERR_ARG, "triattn_shard_attn: misaligned pointer");
+  DeviceInfo info;
+  st = device_info(&info);
+  if (st != FFB_OK) return st;
+  return triattn_shard_attn(q, k, vt, bias_all, mask, o, R, N, row0, info, static_cast<cudaStream_t>(stream));
+}
+
+int ffb_triattn_shard_out(const void* z, const uint8_t* mask, const void* packed, const void* o, void* out, int R, int N,
+                          int row0, int masked, void* stream) {
+  int st = shard_args("triattn_shard_out", R, N, row0);
+  if (st) return st;
+  if (!z || !mask || !packed || !o || !out) return fail(FFB_ERR_ARG, "triattn_shard_out: null pointer");
+  if (z == out) return fail(FFB_ERR_ARG, "triattn_shard_out: out must not alias z");
+  if (masked != FFB_MASKED_COMPUTE && masked != FFB_MASKED_ZERO) return fail(FFB_ERR_ARG, "triattn_shard_out: masked=%d", masked);
+  if (!aligned16(z) || !aligned16(packed) || !aligned16(o) || !aligned16(out))
+    return fail(FFB_ERR_ARG, "triattn_shard_out: misaligned pointer");
+  DeviceInfo info;
+  st = device_info(&info);
+  if (st != FFB_OK) return st;
+  return triattn_shard_out(z, mask, packed, o, out, R, N, row0, masked == FFB_MASKED_ZERO, info,
+                           static_cast<cudaStream_t>(stream));
+}
+
+int ffb_transition_shard_fwd(const void* z, const uint8_t* mask, const void* packed, void* out, int R, int N, int row0,
+                             int masked, void* stream) {
+  int st = shard_args("transition_shard_fwd", R, N, row0);
+  if (st) return st;
+  if (!z || !packed || !out) return fail(FFB_ERR_ARG, "transition_shard_fwd: null pointer");
+  if (masked == FFB_MASKED_ZERO && !mask) return fail(FFB_ERR_ARG, "transition_shard_fwd: masked zero needs the mask");
+  if (masked != FFB_MASKED_COMPUTE && masked != FFB_MASKED_ZERO) return fail(FFB_ERR_ARG, "transition_shard_fwd: masked=%d", masked);
+  if (z == out) return fail(FFB_ERR_ARG, "transition_shard_fwd: out must not alias z");
+  if (!aligned16(z) || !aligned16(out) || !aligned16(packed)) return fail(FFB_ERR_ARG, "transition_shard_fwd: misaligned pointer");
+  DeviceInfo info;
+  st = device_info(&info);
+  if (st != FFB_OK) return st;
+  return transition_shard_forward(z, mask, packed, out, R, N, row0, masked == FFB_MASKED_ZERO, info,
+                                  static_cast<cudaStream_t>(stream));
+}
+
+int ffb_apb_shard_pair_bias(const void* z, const void* packed, void* pb_rows, int R, int N, void* stream) {
+  int st = shard_args("apb_shard_pair_bias", R, N, 0);
+  if (st) return st;
+  if (!z || !packed || !pb_rows) return fail(FFB_ERR_ARG, "apb_shard_pair_bias: null pointer");
+  if (!aligned16(z) || (reinterpret_cast<uintptr_t>(packed) & 255u) || !aligned16(pb_rows))
+    return fail(FFB_ERR_ARG, "apb_shard_pair_bias: misaligned pointer");
+  DeviceInfo info;
+  st = device_info(&info);
+  if (st != FFB_OK) return st;
+  return apb_shard_pair_bias(z, packed, pb_rows, R, N, info, static_cast<cudaStream_t>(stream));
+}
+
+size_t ffb_apb_single_workspace_bytes(int N) { return N <= 0 ? 0 : apb_single_workspace_bytes(N); }
+
+int ffb_apb_shard_single(const void* s, const uint8_t* mask, const void* packed, const void* pb_all,
+                         const void* extra_pair_bias, int extra_dtype, float gate_bias, void* out, void* workspace,
+                         size_t workspace_bytes, int N, int masked, void* stream) {
+  if (N <= 0) return fail(FFB_ERR_ARG, "apb_shard_single: N=%d", N);
+  if (!s || !mask || !packed || !pb_all || !out || !workspace) return fail(FFB_ERR_ARG, "apb_shard_single: null pointer");
+  if (s == out) return fail(FFB_ERR_ARG, "apb_shard_single: out must not alias s");
+  if (masked != FFB_MASKED_COMPUTE && masked != FFB_MASKED_ZERO) return fail(FFB_ERR_ARG, "apb_shard_single: masked=%d", masked);
+  if (extra_pair_bias && extra_dtype != FFB_BF16 && extra_dtype != FFB_F32)
+    return fail(FFB_ERR_ARG, "apb_shard_single: extra dtype");
+  if (workspace_bytes < apb_single_workspace_bytes(N))
+    return fail(FFB_ERR_ARG, "apb_shard_single: workspace %zu < %zu bytes", workspace_bytes, apb_single_workspace_bytes(N));
+  if (!aligned16(s) || !aligned16(out) || !aligned16(pb_all) ||
+      ((reinterpret_cast<uintptr_t>(packed) | reinterpret_cast<uintptr_t>(workspace)) & 255u))
+    return fail(FFB_ERR_ARG, "apb_shard_single: misaligned pointer");
+  DeviceInfo info;
+  int st = device_info(&info);
+  if (st != FFB_OK) return st;
+  return apb_shard_single(s, mask, packed, pb_all, extra_pair_bias, extra_dtype == FFB_F32, gate_bias, out, workspace,
+                          N, masked == FFB_MASKED_ZERO, info, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

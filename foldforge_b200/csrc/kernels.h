@@ -53,6 +53,13 @@ size_t trimul_workspace_bytes(int B, int N);
 int trimul_prepare(const TriMulWeights& w, void* packed, cudaStream_t stream);
 int trimul_forward(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace, int B, int N,
                    int outgoing, int masked_zero, int stages, const DeviceInfo& info, cudaStream_t stream);
+int trimul_shard_proj(const void* z, const uint8_t* mask, const void* packed, void* left, void* right, void* zstats,
+                      int R, int N, int row0, const DeviceInfo& info, cudaStream_t stream);
+int trimul_shard_contract(const void* left, const void* right_all, void* u, int R, int N, const DeviceInfo& info,
+                          cudaStream_t stream);
+int trimul_shard_out(const void* z, const uint8_t* mask, const void* packed, const void* u, const void* zstats,
+                     void* ustats, void* out, int R, int N, int row0, int masked_zero, const DeviceInfo& info,
+                     cudaStream_t stream);
 
 // ---- triangle attention (c_z = 128, 4 heads x 32)
 struct TriAttnWeights {
@@ -63,6 +70,12 @@ size_t triattn_workspace_bytes(int B, int N);
 int triattn_prepare(const TriAttnWeights& w, void* packed, cudaStream_t stream);
 int triattn_forward(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace, int B, int N,
                     int starting, int masked_zero, int stages, const DeviceInfo& info, cudaStream_t stream);
+int triattn_shard_proj(const void* z, const void* packed, void* q, void* k, void* vt, void* bias_rows, int R, int N,
+                       const DeviceInfo& info, cudaStream_t stream);
+int triattn_shard_attn(const void* q, const void* k, const void* vt, const void* bias_all, const uint8_t* mask, void* o,
+                       int R, int N, int row0, const DeviceInfo& info, cudaStream_t stream);
+int triattn_shard_out(const void* z, const uint8_t* mask, const void* packed, const void* o, void* out, int R, int N,
+                      int row0, int masked_zero, const DeviceInfo& info, cudaStream_t stream);
 
 // ---- pair transition (c_z = 128, n = 4)
 struct TransitionWeights {
@@ -84,6 +97,14 @@ int apb_prepare(const ApbWeights& w, void* packed, cudaStream_t stream);
 int apb_forward(const void* s, const void* z, const uint8_t* mask, const void* packed, const void* extra,
                 int extra_f32, float gate_bias, void* out, void* workspace, int B, int N, int masked_zero,
                 const DeviceInfo& info, cudaStream_t stream);
+int apb_shard_pair_bias(const void* z, const void* packed, void* pb_rows, int R, int N, const DeviceInfo& info,
+                        cudaStream_t stream);
+size_t apb_single_workspace_bytes(int N);
+int apb_shard_single(const void* s, const uint8_t* mask, const void* packed, const void* pb_all, const void* extra,
+                     int extra_f32, float gate_bias, void* out, void* workspace, int N, int masked_zero,
+                     const DeviceInfo& info, cudaStream_t stream);
+int transition_shard_forward(const void* z, const uint8_t* mask, const void* packed, void* out, int R, int N, int row0,
+                             int masked_zero, const DeviceInfo& info, cudaStream_t stream);
 size_t single_transition_packed_bytes();
 size_t single_transition_workspace_bytes(int B, int N);
 int single_transition_prepare(const TransitionWeights& w, void* packed, cudaStream_t stream);

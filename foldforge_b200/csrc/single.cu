@@ -80,7 +80,8 @@ struct PbSmem {
 
 __global__ void __launch_bounds__(kPbThreads, 1)
     pair_bias_kernel(const __grid_constant__ CUtensorMap map_z, const uint8_t* __restrict__ w_img,
-                     const float* __restrict__ wsum, float* __restrict__ pb, int64_t P, int* err) {
+                     const float* __restrict__ wsum, float* __restrict__ pb, int64_t P, int N, int64_t pb_h,
+                     int64_t pb_r, int* err) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   PbSmem& s = *reinterpret_cast<PbSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                          ~static_cast<uintptr_t>(1023));
@@ -174,7 +175,12 @@ __global__ void __launch_bounds__(kPbThreads, 1)
       const int64_t p = t * kPbTile + row;
       if (p < P) {
 #pragma unroll
-        for (int h = 0; h < kHs; ++h) pb[h * P + p] = rstd * (__uint_as_float(v[h]) - mean * s.wsum[h]);
+        {
+          // pair p = row * N + col of the rows held: pb[h * pb_h + row * pb_r + col]
+          float* dst = pb + (p / N) * pb_r + (p % N);
+#pragma unroll
+          for (int h = 0; h < kHs; ++h) dst[h * pb_h] = rstd * (__uint_as_float(v[h]) - mean * s.wsum[h]);
+        }
       }
     }
   }
@@ -215,7 +221,7 @@ struct ChunkRegs {
 };
 
 __device__ __forceinline__ void attn_load_chunk(ChunkRegs& r, const __nv_bfloat16* __restrict__ qkvg,
-                                                const float* __restrict__ pb, const void* __restrict__ extra,
+                                                const float* __restrict__ pb, int64_t pb_r, const void* __restrict__ extra,
                                                 int extra_f32, const uint8_t* __restrict__ mask, int b, int h,
                                                 int qb, int N, int j0) {
   const int t = threadIdx.x;
@@ -238,7 +244,7 @@ __device__ __forceinline__ void attn_load_chunk(ChunkRegs& r, const __nv_bfloat1
     const int ii = qb * kQ + qq;
     float v[4] = {0.f, 0.f, 0.f, 0.f};
     if (ii < N) {
-      const float* src = pb + static_cast<int64_t>(ii) * N + j0 + j;
+      const float* src = pb + static_cast<int64_t>(ii) * pb_r + j0 + j;
       if (j + 4 <= nk && (reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
         const float4 f = *reinterpret_cast<const float4*>(src);
         v[0] = f.x;
@@ -297,7 +303,8 @@ __device__ __forceinline__ void attn_store_chunk(const ChunkRegs& r, float* buf)
 }
 
 __global__ void __launch_bounds__(kAttnThreads, 2) single_attention_kernel(
-    const __nv_bfloat16* __restrict__ qkvg, const float* __restrict__ pair_bias_hm, const void* __restrict__ extra,
+    const __nv_bfloat16* __restrict__ qkvg, const float* __restrict__ pair_bias, int64_t pb_h, int64_t pb_r,
+    const void* __restrict__ extra,
     int extra_f32, const uint8_t* __restrict__ mask, float gate_bias, __nv_bfloat16* __restrict__ out, int B, int N) {
   __shared__ __align__(16) float smem[2 * kBufFloats];
   const int qblocks = (N + kQ - 1) / kQ;
@@ -324,19 +331,19 @@ __global__ void __launch_bounds__(kAttnThreads, 2) single_attention_kernel(
   float o[kDs];
 #pragma unroll
   for (int d = 0; d < kDs; ++d) o[d] = 0.f;
-  // head-major bias: [h][b][i][j]
-  const float* pb = pair_bias_hm + (static_cast<int64_t>(h) * B + b) * static_cast<int64_t>(N) * N;
+  // bias row i of head h: pair_bias + h * pb_h + (b * N + i) * pb_r
+  const float* pb = pair_bias + h * pb_h + static_cast<int64_t>(b) * N * pb_r;
   const int chunks = (N + kKC - 1) / kKC;
   {
     ChunkRegs r;
-    attn_load_chunk(r, qkvg, pb, extra, extra_f32, mask, b, h, qb, N, 0);
+    attn_load_chunk(r, qkvg, pb, pb_r, extra, extra_f32, mask, b, h, qb, N, 0);
     attn_store_chunk(r, smem);
   }
   __syncthreads();
   for (int c = 0; c < chunks; ++c) {
     const bool next = c + 1 < chunks;
     ChunkRegs r;
-    if (next) attn_load_chunk(r, qkvg, pb, extra, extra_f32, mask, b, h, qb, N, (c + 1) * kKC);
+    if (next) attn_load_chunk(r, qkvg, pb, pb_r, extra, extra_f32, mask, b, h, qb, N, (c + 1) * kKC);
     const float* buf = smem + (c & 1) * kBufFloats;
     const float* ks = buf;
     const float* vs = buf + kKC * kDs;
@@ -523,18 +530,13 @@ int apb_prepare(const ApbWeights& w, void* packed, cudaStream_t stream) {
   return rc;
 }
 
-int apb_forward(const void* s, const void* z, const uint8_t* mask, const void* packed, const void* extra,
-                int extra_f32, float gate_bias, void* out, void* workspace, int B, int N, int masked_zero,
-                const DeviceInfo& info, cudaStream_t stream) {
+namespace {
+
+// pb[h * pb_h + row * pb_r + col] for the `rows` pair rows of N pairs of z
+int launch_pair_bias(const void* z, const uint8_t* img, float* pb, int64_t rows, int N, int64_t pb_h, int64_t pb_r,
+                     const DeviceInfo& info, cudaStream_t stream) {
   const ApbLayout L = apb_layout();
-  const uint8_t* img = static_cast<const uint8_t*>(packed);
-  const size_t P = static_cast<size_t>(B) * N * N, T = static_cast<size_t>(B) * N;
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
-  float* pb = reinterpret_cast<float*>(ws);
-  void* y = ws + a256(P * kHs * 4);
-  void* qkvg = static_cast<uint8_t*>(y) + a256(T * kCs * 2);
-  void* gated = static_cast<uint8_t*>(qkvg) + a256(T * 4 * kCs * 2);
-  // head-major pair bias from raw z (LayerNorm folded into the epilogue)
+  const size_t P = static_cast<size_t>(rows) * N;
   if (P >= (static_cast<size_t>(1) << 31))
     return fail(FFB_ERR_UNSUPPORTED, "attention_pair_bias: %zu pairs exceed the 2^31 TMA row range", P);
   CUtensorMap mz;
@@ -543,32 +545,78 @@ int apb_forward(const void* s, const void* z, const uint8_t* mask, const void* p
   const uint32_t zbox[2] = {64, kPbTile};
   int st = make_map(&mz, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, z, zdims, zstr, zbox, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
-  {
-    const int64_t tiles = static_cast<int64_t>((P + kPbTile - 1) / kPbTile);
-    const int grid = static_cast<int>(tiles < info.num_sms ? tiles : info.num_sms);
-    const size_t smem = sizeof(PbSmem) + 1024;
-    cudaFuncSetAttribute(pair_bias_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    pair_bias_kernel<<<grid, kPbThreads, smem, stream>>>(mz, img + L.w_pb, reinterpret_cast<const float*>(img + L.pb_wsum),
-                                                         pb, static_cast<int64_t>(P), info.err);
-    st = cuda_status(static_cast<int>(cudaGetLastError()), "pair bias launch");
-    if (st) return st;
-  }
-  st = cuda_status(launch_layernorm(s, y, reinterpret_cast<const float*>(img + L.ln_s_w),
-                                    reinterpret_cast<const float*>(img + L.ln_s_b), static_cast<int64_t>(T), kCs,
-                                    1e-5f, 0, info.num_sms, stream),
-                   "apb single layernorm");
+  const int64_t tiles = static_cast<int64_t>((P + kPbTile - 1) / kPbTile);
+  const int grid = static_cast<int>(tiles < info.num_sms ? tiles : info.num_sms);
+  const size_t smem = sizeof(PbSmem) + 1024;
+  cudaFuncSetAttribute(pair_bias_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  pair_bias_kernel<<<grid, kPbThreads, smem, stream>>>(mz, img + L.w_pb, reinterpret_cast<const float*>(img + L.pb_wsum),
+                                                       pb, static_cast<int64_t>(P), N, pb_h, pb_r, info.err);
+  return cuda_status(static_cast<int>(cudaGetLastError()), "pair bias launch");
+}
+
+// the single track of attention with pair bias, given the pair bias (strides pb_h, pb_r)
+int launch_single_attention(const void* s, const uint8_t* mask, const uint8_t* img, const float* pb, int64_t pb_h,
+                            int64_t pb_r, const void* extra, int extra_f32, float gate_bias, void* out, uint8_t* ws,
+                            int B, int N, int masked_zero, const DeviceInfo& info, cudaStream_t stream) {
+  const ApbLayout L = apb_layout();
+  const size_t T = static_cast<size_t>(B) * N;
+  void* y = ws;
+  void* qkvg = static_cast<uint8_t*>(y) + a256(T * kCs * 2);
+  void* gated = static_cast<uint8_t*>(qkvg) + a256(T * 4 * kCs * 2);
+  int st = cuda_status(launch_layernorm(s, y, reinterpret_cast<const float*>(img + L.ln_s_w),
+                                        reinterpret_cast<const float*>(img + L.ln_s_b), static_cast<int64_t>(T), kCs,
+                                        1e-5f, 0, info.num_sms, stream),
+                       "apb single layernorm");
   if (st) return st;
   st = gemm(y, img + L.w_qkvg, qkvg, static_cast<int>(T), 4 * kCs, kCs, 0,
             reinterpret_cast<const float*>(img + L.b_qkvg), kEpiStore, nullptr, nullptr, info, stream);
   if (st) return st;
   const int ctas = B * kHs * ((N + kQ - 1) / kQ);
   single_attention_kernel<<<ctas, kAttnThreads, 0, stream>>>(
-      static_cast<const __nv_bfloat16*>(qkvg), pb, extra, extra_f32, mask, gate_bias,
+      static_cast<const __nv_bfloat16*>(qkvg), pb, pb_h, pb_r, extra, extra_f32, mask, gate_bias,
       static_cast<__nv_bfloat16*>(gated), B, N);
   st = cuda_status(static_cast<int>(cudaGetLastError()), "single attention launch");
   if (st) return st;
   return gemm(gated, img + L.w_o, out, static_cast<int>(T), kCs, kCs, 0, nullptr, kEpiResidual, s,
               masked_zero ? mask : nullptr, info, stream);
+}
+
+}  // namespace
+
+int apb_forward(const void* s, const void* z, const uint8_t* mask, const void* packed, const void* extra,
+                int extra_f32, float gate_bias, void* out, void* workspace, int B, int N, int masked_zero,
+                const DeviceInfo& info, cudaStream_t stream) {
+  const uint8_t* img = static_cast<const uint8_t*>(packed);
+  const size_t P = static_cast<size_t>(B) * N * N;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* pb = reinterpret_cast<float*>(ws);
+  // head-major pair bias [16][B][N][N] from raw z (LayerNorm folded into the epilogue)
+  int st = launch_pair_bias(z, img, pb, static_cast<int64_t>(B) * N, N, static_cast<int64_t>(P), N, info, stream);
+  if (st) return st;
+  return launch_single_attention(s, mask, img, pb, static_cast<int64_t>(P), N, extra, extra_f32, gate_bias, out,
+                                 ws + a256(P * kHs * 4), B, N, masked_zero, info, stream);
+}
+
+// ---- row-sharded pieces (B = 1). The rank's pair-bias rows [R][16][N] (fp32) concatenate
+// under an all-gather into the [N][16][N] bias the single track reads; the single track is
+// replicated on every rank (workspace: apb_single_workspace_bytes).
+int apb_shard_pair_bias(const void* z, const void* packed, void* pb_rows, int R, int N, const DeviceInfo& info,
+                        cudaStream_t stream) {
+  return launch_pair_bias(z, static_cast<const uint8_t*>(packed), static_cast<float*>(pb_rows), R, N, N,
+                          static_cast<int64_t>(kHs) * N, info, stream);
+}
+
+size_t apb_single_workspace_bytes(int N) {
+  const size_t T = static_cast<size_t>(N);
+  return a256(T * kCs * 2) + a256(T * 4 * kCs * 2) + a256(T * kCs * 2);
+}
+
+int apb_shard_single(const void* s, const uint8_t* mask, const void* packed, const void* pb_all, const void* extra,
+                     int extra_f32, float gate_bias, void* out, void* workspace, int N, int masked_zero,
+                     const DeviceInfo& info, cudaStream_t stream) {
+  return launch_single_attention(s, mask, static_cast<const uint8_t*>(packed), static_cast<const float*>(pb_all), N,
+                                 static_cast<int64_t>(kHs) * N, extra, extra_f32, gate_bias, out,
+                                 static_cast<uint8_t*>(workspace), 1, N, masked_zero, info, stream);
 }
 
 size_t single_transition_packed_bytes() { return st_layout().total; }

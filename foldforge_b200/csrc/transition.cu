@@ -62,8 +62,9 @@ static_assert(sizeof(Smem) + 1024 <= 232448, "transition shared memory exceeds t
 struct Params {
   const uint8_t* packed;
   const uint8_t* mask;
-  int64_t rows;  // B * N * N
+  int64_t rows;  // B * R * N pair rows
   int N;
+  int R, row0;   // problem rows held (N unless row-sharded) and the first one's global index
   int masked_zero;
   int* err;
 };
@@ -306,9 +307,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool keep = true;
         if (p.masked_zero && row < p.rows) {
           const int64_t jj = row % p.N;
-          const int64_t bi = row / p.N;  // b * N + i
-          const int64_t b = bi / p.N;
-          keep = p.mask[bi] && p.mask[b * p.N + jj];
+          const int64_t bi = row / p.N;  // b * R + i
+          const int64_t b = bi / p.R, i = bi - b * p.R;
+          keep = p.mask[b * p.N + p.row0 + i] && p.mask[b * p.N + jj];
         }
         uint8_t* zt = s.z[zb];
 #pragma unroll 1
@@ -384,9 +385,11 @@ int transition_prepare(const TransitionWeights& w, void* packed, cudaStream_t st
   return rc;
 }
 
-int transition_forward(const void* z, const uint8_t* mask, const void* packed, void* out, int B, int N,
-                       int masked_zero, const DeviceInfo& info, cudaStream_t stream) {
-  const int64_t rows = static_cast<int64_t>(B) * N * N;
+namespace {
+
+int launch_transition(const void* z, const uint8_t* mask, const void* packed, void* out, int B, int R, int N, int row0,
+                      int masked_zero, const DeviceInfo& info, cudaStream_t stream) {
+  const int64_t rows = static_cast<int64_t>(B) * R * N;
   if (rows >= (static_cast<int64_t>(1) << 31))
     return fail(FFB_ERR_UNSUPPORTED, "transition: %lld pair rows exceed the 2^31 TMA row range",
                 static_cast<long long>(rows));
@@ -398,13 +401,26 @@ int transition_forward(const void* z, const uint8_t* mask, const void* packed, v
   if (st) return st;
   st = make_map(&map_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
-  Params pp{static_cast<const uint8_t*>(packed), mask, rows, N, masked_zero, info.err};
+  Params pp{static_cast<const uint8_t*>(packed), mask, rows, N, R, row0, masked_zero, info.err};
   const int tiles = static_cast<int>((rows + kRows - 1) / kRows);
   const int grid = tiles < info.num_sms ? tiles : info.num_sms;
   const size_t smem = sizeof(Smem) + 1024;
   cudaFuncSetAttribute(transition_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   transition_kernel<<<grid, kThreads, smem, stream>>>(map_z, map_out, pp);
   return cuda_status(static_cast<int>(cudaGetLastError()), "transition launch");
+}
+
+}  // namespace
+
+int transition_forward(const void* z, const uint8_t* mask, const void* packed, void* out, int B, int N,
+                       int masked_zero, const DeviceInfo& info, cudaStream_t stream) {
+  return launch_transition(z, mask, packed, out, B, N, N, 0, masked_zero, info, stream);
+}
+
+// row-sharded (B = 1): the rank holds pair rows [row0, row0 + R)
+int transition_shard_forward(const void* z, const uint8_t* mask, const void* packed, void* out, int R, int N, int row0,
+                             int masked_zero, const DeviceInfo& info, cudaStream_t stream) {
+  return launch_transition(z, mask, packed, out, 1, R, N, row0, masked_zero, info, stream);
 }
 
 }  // namespace ffb

@@ -75,8 +75,10 @@ struct ProjParams {
   __nv_bfloat16* q;     // [B, N, H, N, 32]
   __nv_bfloat16* k;     // [B, N, H, N, 32]
   __nv_bfloat16* vt;    // [B, N, H, 32, Np]
-  __nv_bfloat16* bias;  // [B, H, N, Np]
+  __nv_bfloat16* bias;  // natural pair layout, element strides below
   int B, N, Np;
+  int R, row0;          // problem rows held (N unless row-sharded) and the first one's global index
+  int64_t bias_b, bias_h, bias_r;  // bias strides of batch, head and pair row (pair column: 1)
   int starting;
   int* err;
 };
@@ -89,7 +91,7 @@ __global__ void __launch_bounds__(256, 1)
   const int gt = threadIdx.x % 128;
   const int warp = threadIdx.x / 32;
   const int tiles_per_row = (p.N + kTile - 1) / kTile;
-  const int total = p.B * p.N * tiles_per_row;
+  const int total = p.B * p.R * tiles_per_row;
 
   if (threadIdx.x == 0) {
     mbar_init(&s.wbar, 1);
@@ -129,8 +131,8 @@ __global__ void __launch_bounds__(256, 1)
   for (int tile = blockIdx.x * kGroups + g; tile < total; tile += gridDim.x * kGroups, ++it) {
     const int c0 = (tile % tiles_per_row) * kTile;
     const int rr = tile / tiles_per_row;
-    const int b = rr / p.N;
-    const int r = rr - b * p.N;  // problem row
+    const int b = rr / p.R;
+    const int r = rr - b * p.R;  // problem row (of the rows held)
     if (gt == 0 && ok) {
       mbar_arrive_expect_tx(&s.full[g], kTile * kC * 2);
       for (int kb = 0; kb < 2; ++kb) {
@@ -166,7 +168,7 @@ __global__ void __launch_bounds__(256, 1)
       got = __all_sync(0xFFFFFFFFu, got);
       tc_fence_after();
       if (got) {
-        const int64_t row_base = (static_cast<int64_t>(b) * p.N + r) * kHeads;  // (b, r) -> head 0
+        const int64_t row_base = (static_cast<int64_t>(b) * p.R + r) * kHeads;  // (b, r) -> head 0
         if (half == 0) {
           // Q (cols 0..127) and K (cols 128..255): one head = 32 columns = 64 contiguous bytes
 #pragma unroll 1
@@ -218,7 +220,7 @@ __global__ void __launch_bounds__(256, 1)
               // natural pair layout [b, h, i, j] for both nodes (starting: i = r, j = n;
               // ending: i = n, j = r), so the attention reads rows of queries x keys
               const int64_t bi = p.starting ? r : n, bj = p.starting ? n : r;
-              p.bias[((static_cast<int64_t>(b) * kHeads + h) * p.N + bi) * p.Np + bj] =
+              p.bias[b * p.bias_b + h * p.bias_h + bi * p.bias_r + bj] =
                   __float2bfloat16_rn(rstd * (__uint_as_float(v[h]) - mean * s.wsum[c]) + s.bias[c]);
             }
           }
@@ -284,8 +286,9 @@ static_assert(sizeof(AttnSmem) + 1024 <= 232448, "attention shared memory exceed
 
 struct AttnParams {
   const uint8_t* mask;   // [B, N]
-  __nv_bfloat16* o;      // natural pair layout [B, N, N, 128]
+  __nv_bfloat16* o;      // natural pair layout [B, R, N, 128]
   int B, N;
+  int R, row0;           // problem rows held and the first one's global index
   int starting;
   int qpairs;            // ceil(ceil(N / 128) / 2)
   int words_per_batch;   // 2 * ceil(N / 64)
@@ -297,8 +300,8 @@ __device__ __forceinline__ void unit_coords(int unit, const AttnParams& p, int& 
   int rest = unit / p.qpairs;
   h = rest % kHeads;
   rest /= kHeads;
-  r = rest % p.N;
-  b = rest / p.N;
+  r = rest % p.R;
+  b = rest / p.R;
 }
 
 __global__ void __launch_bounds__(kAttnThreads, 1)
@@ -309,7 +312,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   AttnSmem& s = *reinterpret_cast<AttnSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int units = p.B * p.N * kHeads * p.qpairs;
+  const int units = p.B * p.R * kHeads * p.qpairs;
   const int nkb = (p.N + kKB - 1) / kKB;
   const int my_units = blockIdx.x < units ? (units - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1 : 0;
   const int steps = my_units * nkb;
@@ -374,7 +377,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x, ++ul) {
         int b, r, h, qp;
         unit_coords(unit, p, b, r, h, qp);
-        const int qrow = (b * p.N + r) * kHeads + h;
+        const int qrow = (b * p.R + r) * kHeads + h;
         const int qb = ul & 1;
         if (!mbar_wait(&s.q_empty[qb], ((ul >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty)) break;
         mbar_arrive_expect_tx(&s.q_full[qb], kGroups * kTile * kD * 2);
@@ -481,7 +484,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const int64_t pi = p.starting ? prev_r : prev_q;
         const int64_t pj = p.starting ? prev_q : prev_r;
         uint4* dst = reinterpret_cast<uint4*>(
-            p.o + (((static_cast<int64_t>(prev_b) * p.N + pi) * p.N + pj) * kC + prev_h * kD));
+            p.o + (((static_cast<int64_t>(prev_b) * p.R + pi) * p.N + pj) * kC + prev_h * kD));
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const float* f = reinterpret_cast<const float*>(ov) + 8 * k;
@@ -496,7 +499,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       int b, r, h, qp;
       unit_coords(unit, p, b, r, h, qp);
       const int q = (qp * 2 + g) * kTile + t;
-      const bool row_on = p.mask[b * p.N + r] != 0;
+      const bool row_on = p.mask[b * p.N + p.row0 + r] != 0;
       const uint32_t* mw = s.mask_words + b * p.words_per_batch;
       const int ob = ul & 1;
       float m = 0.f;
@@ -649,6 +652,7 @@ struct OutParams {
   const uint8_t* packed;
   const uint8_t* mask;
   int B, N;
+  int R, row0;  // pair rows held and the first one's global index
   int masked_zero;
   int* err;
 };
@@ -661,7 +665,7 @@ __global__ void __launch_bounds__(kOThreads, 1)
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const int tiles_per_row = (p.N + kOTile - 1) / kOTile;
-  const int total = p.B * p.N * tiles_per_row;
+  const int total = p.B * p.R * tiles_per_row;
 
   if (threadIdx.x == 0) {
     mbar_init(&s.wbar, 1);
@@ -766,11 +770,12 @@ __global__ void __launch_bounds__(kOThreads, 1)
       ln_stats_c128(s.z[st], kOTile * 128, t, mean, rstd);
       const int c0 = (tile % tiles_per_row) * kOTile;
       const int rr = tile / tiles_per_row;
-      const int b = rr / p.N, r = rr - b * p.N;
+      const int b = rr / p.R, r = rr - b * p.R;
       const int j = c0 + t;
       s.zm[buf][t] = mean;
       s.zr[buf][t] = rstd;
-      s.keep[buf][t] = (!p.masked_zero || (j < p.N && p.mask[b * p.N + r] && p.mask[b * p.N + j])) ? 1.f : 0.f;
+      s.keep[buf][t] =
+          (!p.masked_zero || (j < p.N && p.mask[b * p.N + p.row0 + r] && p.mask[b * p.N + j])) ? 1.f : 0.f;
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.st_full[buf]);
     }
@@ -927,91 +932,143 @@ int triattn_prepare(const TriAttnWeights& w, void* packed, cudaStream_t stream) 
   return rc;
 }
 
+namespace {
+
+// z-shaped map ([B * R] rows of N pairs x 128 channels) with a box of `rows` pairs along a
+// row (row tiles) or along a column (column tiles, R == N)
+int pair_map(CUtensorMap* m, const void* base, int B, int R, int N, int rows, bool column_tiles) {
+  const uint64_t dims[3] = {kC, static_cast<uint64_t>(N), static_cast<uint64_t>(B) * R};
+  const uint64_t strides[2] = {kC * 2, static_cast<uint64_t>(N) * kC * 2};
+  const uint32_t box_row[3] = {64, static_cast<uint32_t>(rows), 1};
+  const uint32_t box_col[3] = {64, 1, static_cast<uint32_t>(rows)};
+  return make_map(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, column_tiles ? box_col : box_row,
+                  CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int launch_proj(const void* z, const void* packed, __nv_bfloat16* q, __nv_bfloat16* k, __nv_bfloat16* vt,
+                __nv_bfloat16* bias, int64_t bias_b, int64_t bias_h, int64_t bias_r, int B, int R, int N,
+                int starting, const DeviceInfo& info, cudaStream_t stream) {
+  const int np = (N + 7) / 8 * 8;
+  CUtensorMap map_z;
+  int st = pair_map(&map_z, z, B, R, N, kTile, !starting);
+  if (st) return st;
+  ProjParams pp{static_cast<const uint8_t*>(packed), q, k, vt, bias, B, N, np, R, 0, bias_b, bias_h, bias_r,
+                starting, info.err};
+  const int tiles = B * R * ((N + kTile - 1) / kTile);
+  const int groups = (tiles + kGroups - 1) / kGroups;
+  const int grid = groups < info.num_sms ? groups : info.num_sms;
+  const size_t smem = sizeof(ProjSmem) + 1024;
+  cudaFuncSetAttribute(triattn_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  triattn_proj_kernel<<<grid, 256, smem, stream>>>(map_z, pp);
+  return cuda_status(static_cast<int>(cudaGetLastError()), "triattn_proj launch");
+}
+
+// bias: rows = queries, element strides of query row `bq` and of (batch * H + head) `bbh`
+int launch_attn(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* vt, const __nv_bfloat16* bias,
+                int64_t bq, int64_t bbh, const uint8_t* mask, __nv_bfloat16* o, int B, int R, int N, int row0,
+                int starting, const DeviceInfo& info, cudaStream_t stream) {
+  const int np = (N + 7) / 8 * 8;
+  CUtensorMap map_q, map_k, map_vt, map_bias;
+  const uint64_t qdims[3] = {kD, static_cast<uint64_t>(N), static_cast<uint64_t>(B) * R * kHeads};
+  const uint64_t qstrides[2] = {kD * 2, static_cast<uint64_t>(N) * kD * 2};
+  const uint32_t qbox[3] = {kD, kTile, 1};
+  const uint32_t kbox[3] = {kD, kKB, 1};
+  int st = make_map(&map_q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, q, qdims, qstrides, qbox, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (st) return st;
+  st = make_map(&map_k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, k, qdims, qstrides, kbox, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (st) return st;
+  const uint64_t vdims[3] = {static_cast<uint64_t>(N), kD, static_cast<uint64_t>(B) * R * kHeads};
+  const uint64_t vstrides[2] = {static_cast<uint64_t>(np) * 2, static_cast<uint64_t>(kD) * np * 2};
+  const uint32_t vbox[3] = {kKB, kD, 1};
+  st = make_map(&map_vt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, vt, vdims, vstrides, vbox, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st) return st;
+  const uint64_t bdims[3] = {static_cast<uint64_t>(N), static_cast<uint64_t>(N), static_cast<uint64_t>(B) * kHeads};
+  const uint64_t bstrides[2] = {static_cast<uint64_t>(bq) * 2, static_cast<uint64_t>(bbh) * 2};
+  const uint32_t bbox[3] = {kKB, kTile, 1};  // [q rows][64 keys], 128-byte rows
+  st = make_map(&map_bias, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, bias, bdims, bstrides, bbox, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st) return st;
+  AttnParams ap;
+  ap.mask = mask;
+  ap.o = o;
+  ap.B = B;
+  ap.N = N;
+  ap.R = R;
+  ap.row0 = row0;
+  ap.starting = starting;
+  ap.qpairs = ((N + kTile - 1) / kTile + 1) / 2;
+  ap.words_per_batch = 2 * ((N + kKB - 1) / kKB);
+  ap.err = info.err;
+  if (B * ap.words_per_batch > kMaxMaskWords) return fail(2, "triattn: B * N too large for the key-mask cache");
+  const int units = B * R * kHeads * ap.qpairs;
+  const int grid = units < info.num_sms ? units : info.num_sms;
+  const size_t smem = sizeof(AttnSmem) + 1024;
+  cudaFuncSetAttribute(triattn_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  triattn_attn_kernel<<<grid, kAttnThreads, smem, stream>>>(map_q, map_k, map_vt, map_bias, ap);
+  return cuda_status(static_cast<int>(cudaGetLastError()), "triattn_attn launch");
+}
+
+int launch_out(const void* z, const uint8_t* mask, const void* packed, const void* o, void* out, int B, int R, int N,
+               int row0, int masked_zero, const DeviceInfo& info, cudaStream_t stream) {
+  CUtensorMap map_z, map_o, map_out;
+  int st = pair_map(&map_z, z, B, R, N, kOTile, false);
+  if (st) return st;
+  st = pair_map(&map_o, o, B, R, N, kOTile, false);
+  if (st) return st;
+  st = pair_map(&map_out, out, B, R, N, kOTile, false);
+  if (st) return st;
+  OutParams op{static_cast<const uint8_t*>(packed), mask, B, N, R, row0, masked_zero, info.err};
+  const int tiles = B * R * ((N + kOTile - 1) / kOTile);
+  const int grid = tiles < info.num_sms ? tiles : info.num_sms;
+  const size_t smem = sizeof(OutSmem) + 1024;
+  cudaFuncSetAttribute(triattn_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  triattn_out_kernel<<<grid, kOThreads, smem, stream>>>(map_z, map_o, map_out, op);
+  return cuda_status(static_cast<int>(cudaGetLastError()), "triattn_out launch");
+}
+
+}  // namespace
+
 int triattn_forward(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace, int B, int N,
                     int starting, int masked_zero, int stages, const DeviceInfo& info, cudaStream_t stream) {
-  const int np = (N + 7) / 8 * 8;
+  const int64_t np = (N + 7) / 8 * 8;
   Workspace ws = carve(workspace, B, N);
-  int st;
-  const uint64_t zdims[3] = {kC, static_cast<uint64_t>(N), static_cast<uint64_t>(B) * N};
-  const uint64_t zstrides[2] = {kC * 2, static_cast<uint64_t>(N) * kC * 2};
-  // 1. projection
+  // bias [B, H, N, Np] in the natural pair layout
+  const int64_t bias_r = np, bias_h = static_cast<int64_t>(N) * np, bias_b = kHeads * bias_h;
+  int st = 0;
   if (stages & 1) {
-    CUtensorMap map_z;
-    const uint32_t box_row[3] = {64, kTile, 1};
-    const uint32_t box_col[3] = {64, 1, kTile};
-    st = make_map(&map_z, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, z, zdims, zstrides, starting ? box_row : box_col,
-                  CU_TENSOR_MAP_SWIZZLE_128B);
-    if (st) return st;
-    ProjParams pp{static_cast<const uint8_t*>(packed), ws.q, ws.k, ws.vt, ws.bias, B, N, np, starting, info.err};
-    const int tiles = B * N * ((N + kTile - 1) / kTile);
-    const int groups = (tiles + kGroups - 1) / kGroups;
-    const int grid = groups < info.num_sms ? groups : info.num_sms;
-    const size_t smem = sizeof(ProjSmem) + 1024;
-    cudaFuncSetAttribute(triattn_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    triattn_proj_kernel<<<grid, 256, smem, stream>>>(map_z, pp);
-    st = cuda_status(static_cast<int>(cudaGetLastError()), "triattn_proj launch");
+    st = launch_proj(z, packed, ws.q, ws.k, ws.vt, ws.bias, bias_b, bias_h, bias_r, B, N, N, starting, info, stream);
     if (st) return st;
   }
-  // 2. attention
   if (stages & 2) {
-    CUtensorMap map_q, map_k, map_vt, map_bias;
-    const uint64_t qdims[3] = {kD, static_cast<uint64_t>(N), static_cast<uint64_t>(B) * N * kHeads};
-    const uint64_t qstrides[2] = {kD * 2, static_cast<uint64_t>(N) * kD * 2};
-    const uint32_t qbox[3] = {kD, kTile, 1};
-    const uint32_t kbox[3] = {kD, kKB, 1};
-    st = make_map(&map_q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ws.q, qdims, qstrides, qbox, CU_TENSOR_MAP_SWIZZLE_64B);
-    if (st) return st;
-    st = make_map(&map_k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ws.k, qdims, qstrides, kbox, CU_TENSOR_MAP_SWIZZLE_64B);
-    if (st) return st;
-    const uint64_t vdims[3] = {static_cast<uint64_t>(N), kD, static_cast<uint64_t>(B) * N * kHeads};
-    const uint64_t vstrides[2] = {static_cast<uint64_t>(np) * 2, static_cast<uint64_t>(kD) * np * 2};
-    const uint32_t vbox[3] = {kKB, kD, 1};
-    st = make_map(&map_vt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ws.vt, vdims, vstrides, vbox,
-                  CU_TENSOR_MAP_SWIZZLE_128B);
-    if (st) return st;
-    const uint64_t bdims[3] = {static_cast<uint64_t>(N), static_cast<uint64_t>(N), static_cast<uint64_t>(B) * kHeads};
-    const uint64_t bstrides[2] = {static_cast<uint64_t>(np) * 2, static_cast<uint64_t>(N) * np * 2};
-    const uint32_t bbox[3] = {kKB, kTile, 1};  // [q rows][64 keys], 128-byte rows
-    st = make_map(&map_bias, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ws.bias, bdims, bstrides, bbox,
-                  CU_TENSOR_MAP_SWIZZLE_128B);
-    if (st) return st;
-    AttnParams ap;
-    ap.mask = mask;
-    ap.o = ws.o;
-    ap.B = B;
-    ap.N = N;
-    ap.starting = starting;
-    ap.qpairs = ((N + kTile - 1) / kTile + 1) / 2;
-    ap.words_per_batch = 2 * ((N + kKB - 1) / kKB);
-    ap.err = info.err;
-    if (B * ap.words_per_batch > kMaxMaskWords) return fail(2, "triattn: B * N too large for the key-mask cache");
-    const int units = B * N * kHeads * ap.qpairs;
-    const int grid = units < info.num_sms ? units : info.num_sms;
-    const size_t smem = sizeof(AttnSmem) + 1024;
-    cudaFuncSetAttribute(triattn_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    triattn_attn_kernel<<<grid, kAttnThreads, smem, stream>>>(map_q, map_k, map_vt, map_bias, ap);
-    st = cuda_status(static_cast<int>(cudaGetLastError()), "triattn_attn launch");
+    st = launch_attn(ws.q, ws.k, ws.vt, ws.bias, bias_r, bias_h, mask, ws.o, B, N, N, 0, starting, info, stream);
     if (st) return st;
   }
-  // 3. output
-  if (stages & 4) {
-    CUtensorMap map_z, map_o, map_out;
-    const uint32_t box[3] = {64, kOTile, 1};
-    st = make_map(&map_z, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, z, zdims, zstrides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (st) return st;
-    st = make_map(&map_o, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ws.o, zdims, zstrides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (st) return st;
-    st = make_map(&map_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out, zdims, zstrides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (st) return st;
-    OutParams op{static_cast<const uint8_t*>(packed), mask, B, N, masked_zero, info.err};
-    const int tiles = B * N * ((N + kOTile - 1) / kOTile);
-    const int grid = tiles < info.num_sms ? tiles : info.num_sms;
-    const size_t smem = sizeof(OutSmem) + 1024;
-    cudaFuncSetAttribute(triattn_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    triattn_out_kernel<<<grid, kOThreads, smem, stream>>>(map_z, map_o, map_out, op);
-    return cuda_status(static_cast<int>(cudaGetLastError()), "triattn_out launch");
-  }
-  return 0;
+  if (stages & 4) st = launch_out(z, mask, packed, ws.o, out, B, N, N, 0, masked_zero, info, stream);
+  return st;
+}
+
+// ---- row-sharded entry points (B = 1): the rank holds rows [row0, row0 + R) of the pair
+// (for the ending node: of the transposed pair). Q, K [R, H, N, 32], V^T [R, H, 32, Np],
+// o [R, N, 128]; the rank's bias rows [R][H][Np] concatenate under an all-gather into the
+// [N][H][Np] bias (rows = queries) the attention reads.
+int triattn_shard_proj(const void* z, const void* packed, void* q, void* k, void* vt, void* bias_rows, int R, int N,
+                       const DeviceInfo& info, cudaStream_t stream) {
+  const int64_t np = (N + 7) / 8 * 8;
+  return launch_proj(z, packed, static_cast<__nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(k),
+                     static_cast<__nv_bfloat16*>(vt), static_cast<__nv_bfloat16*>(bias_rows), R * kHeads * np, np,
+                     kHeads * np, 1, R, N, 1, info, stream);
+}
+
+int triattn_shard_attn(const void* q, const void* k, const void* vt, const void* bias_all, const uint8_t* mask, void* o,
+                       int R, int N, int row0, const DeviceInfo& info, cudaStream_t stream) {
+  const int64_t np = (N + 7) / 8 * 8;
+  return launch_attn(static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
+                     static_cast<const __nv_bfloat16*>(vt), static_cast<const __nv_bfloat16*>(bias_all), kHeads * np,
+                     np, mask, static_cast<__nv_bfloat16*>(o), 1, R, N, row0, 1, info, stream);
+}
+
+int triattn_shard_out(const void* z, const uint8_t* mask, const void* packed, const void* o, void* out, int R, int N,
+                      int row0, int masked_zero, const DeviceInfo& info, cudaStream_t stream) {
+  return launch_out(z, mask, packed, o, out, 1, R, N, row0, masked_zero, info, stream);
 }
 
 }  // namespace ffb

@@ -117,8 +117,10 @@ struct ProjParams {
   const uint8_t* mask;  // [B, N]
   __nv_bfloat16* left;  // [B*h, N, Np]
   __nv_bfloat16* right;
-  float2* zstats;       // [B, N, N] (mean, rstd) of the input LayerNorm, natural pair order
+  float2* zstats;       // [B, R, N] (mean, rstd) of the input LayerNorm, natural pair order
   int B, N, Np;
+  int R, row0;          // problem rows held (N unless row-sharded) and the first one's global index
+  int64_t ls_b, ls_c, ls_r;  // L / R element strides of batch, channel and row
   int outgoing;
   int* err;
 };
@@ -130,7 +132,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const int tiles_per_row = (p.N + kPTile - 1) / kPTile;
-  const int total = p.B * p.N * tiles_per_row;
+  const int total = p.B * p.R * tiles_per_row;
 
   if (threadIdx.x == 0) {
     mbar_init(&s.wbar, 1);
@@ -174,7 +176,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         if (!mbar_wait(&s.z_empty[st], ((it / kPStages) & 1) ^ 1, p.err, kErrTimeoutEmpty)) break;
         const int c0 = (tile % tiles_per_row) * kPTile;
         const int rr = tile / tiles_per_row;
-        const int b = rr / p.N, r = rr - b * p.N;
+        const int b = rr / p.R, r = rr - b * p.R;
         mbar_arrive_expect_tx(&s.z_full[st], kPTile * kC * 2);
         for (int kb = 0; kb < 2; ++kb) {
           uint8_t* dst = s.z[st] + kb * (kPTile * 128);
@@ -245,17 +247,18 @@ __global__ void __launch_bounds__(kPThreads, 1)
       }
       const int c0 = (tile % tiles_per_row) * kPTile;
       const int rr = tile / tiles_per_row;
-      const int b = rr / p.N, r = rr - b * p.N;
+      const int b = rr / p.R, r = rr - b * p.R;
       const int k = c0 + t;
       const float rstd = rsqrtf(q2 * (1.0f / kC) + 1e-5f);
       s.mean[buf][t] = mean;
       s.rstd[buf][t] = rstd;
       if (k < p.N) {
-        // natural pair (i, j): outgoing row tile (r, k), incoming column tile (k, r)
+        // natural pair (i, j) of the rows held: outgoing row tile (r, k), incoming column
+        // tile (k, r) (the incoming direction always holds all N rows)
         const int64_t pi = p.outgoing ? r : k, pj = p.outgoing ? k : r;
-        p.zstats[(static_cast<int64_t>(b) * p.N + pi) * p.N + pj] = make_float2(mean, rstd);
+        p.zstats[(static_cast<int64_t>(b) * p.R + pi) * p.N + pj] = make_float2(mean, rstd);
       }
-      s.pm[buf][t] = (k < p.N && p.mask[b * p.N + r] && p.mask[b * p.N + k]) ? 1.0f : 0.0f;
+      s.pm[buf][t] = (k < p.N && p.mask[b * p.N + p.row0 + r] && p.mask[b * p.N + k]) ? 1.0f : 0.0f;
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&s.st_full[buf]);
@@ -279,8 +282,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
       tc_fence_after();
       const int c0 = (tile % tiles_per_row) * kPTile;
       const int rr = tile / tiles_per_row;
-      const int b = rr / p.N, r = rr - b * p.N;
-      __nv_bfloat16* row = out + ((static_cast<int64_t>(b) * kH + c) * p.N + r) * p.Np + c0;
+      const int b = rr / p.R, r = rr - b * p.R;
+      __nv_bfloat16* row = out + b * p.ls_b + c * p.ls_c + r * p.ls_r + c0;
 #pragma unroll 1
       for (int ch = 0; ch < kPTile; ch += 32) {
         uint32_t vp[32], vg[32];
@@ -366,27 +369,29 @@ struct OutSmem {
 struct OutParams {
   const uint8_t* packed;
   const uint8_t* mask;
-  const float2* zstats;  // [B, N, N] (mean, rstd) of z (input LayerNorm)
-  const float2* ustats;  // [B, N, N] (mean, rstd) of u (centre LayerNorm)
+  const float2* zstats;  // [B, R, N] (mean, rstd) of z (input LayerNorm)
+  const float2* ustats;  // [B, R, N] (mean, rstd) of u (centre LayerNorm)
   int B, N;
+  int R, row0;           // rows held and the first one's global index
   int masked_zero;
   int* err;
 };
 
 // Per-pair mean and 1/sqrt(var + 1e-5) of u over its 128 channels (u channel-major
-// [B*h, N, Np]). A thread owns 8 consecutive pairs of one row and walks the channels with
+// [B*h, R, Np], R rows held). A thread owns 8 consecutive pairs of one row and walks the channels with
 // 16-byte loads (coalesced across the warp); the variance is accumulated about the first
 // channel's value (shifted data, no cancellation for rows whose mean is large).
 __global__ void __launch_bounds__(256) trimul_ustats_kernel(const __nv_bfloat16* __restrict__ u,
-                                                             float2* __restrict__ ustats, int B, int N, int Np) {
+                                                             float2* __restrict__ ustats, int B, int R, int N,
+                                                             int Np) {
   const int groups = (N + 7) / 8;
   const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (gid >= static_cast<int64_t>(B) * N * groups) return;
+  if (gid >= static_cast<int64_t>(B) * R * groups) return;
   const int g = static_cast<int>(gid % groups);
-  const int64_t bi = gid / groups;  // b * N + i
-  const int b = static_cast<int>(bi / N), i = static_cast<int>(bi % N);
-  const int64_t plane = static_cast<int64_t>(N) * Np;
-  const __nv_bfloat16* src = u + (static_cast<int64_t>(b) * kH * N + i) * Np + g * 8;
+  const int64_t bi = gid / groups;  // b * R + i
+  const int b = static_cast<int>(bi / R), i = static_cast<int>(bi % R);
+  const int64_t plane = static_cast<int64_t>(R) * Np;
+  const __nv_bfloat16* src = u + (static_cast<int64_t>(b) * kH * R + i) * Np + g * 8;
   float shift[8], s1[8], s2[8];
   {
     const uint4 v = *reinterpret_cast<const uint4*>(src);
@@ -431,7 +436,7 @@ __global__ void __launch_bounds__(kOThreads, 1)
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const int tiles_per_row = (p.N + kOTile - 1) / kOTile;
-  const int total = p.B * p.N * tiles_per_row;
+  const int total = p.B * p.R * tiles_per_row;
 
   if (threadIdx.x == 0) {
     mbar_init(&s.wbar, 1);
@@ -479,7 +484,7 @@ __global__ void __launch_bounds__(kOThreads, 1)
         if (!mbar_wait(&s.empty[st], ((it / kOStages) & 1) ^ 1, p.err, kErrTimeoutEmpty)) break;
         const int c0 = (tile % tiles_per_row) * kOTile;
         const int rr = tile / tiles_per_row;
-        const int b = rr / p.N, r = rr - b * p.N;
+        const int b = rr / p.R, r = rr - b * p.R;
         mbar_arrive_expect_tx(&s.full[st], 2 * kOTile * kC * 2);
         for (int kb = 0; kb < 2; ++kb) {
           tma_load_3d(s.z[st] + kb * (kOTile * 128), &map_z, &s.full[st], kb * 64, c0, rr);
@@ -524,14 +529,14 @@ __global__ void __launch_bounds__(kOThreads, 1)
       if (!__all_sync(0xFFFFFFFFu, w2)) break;
       const int c0 = (tile % tiles_per_row) * kOTile;
       const int rr = tile / tiles_per_row;
-      const int b = rr / p.N, r = rr - b * p.N;
+      const int b = rr / p.R, r = rr - b * p.R;
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
         const int pp = t + 64 * k;
         const int j = c0 + pp;
         float2 zs = make_float2(0.f, 0.f), us = make_float2(0.f, 0.f);
         if (j < p.N) {
-          const int64_t pair = (static_cast<int64_t>(b) * p.N + r) * p.N + j;
+          const int64_t pair = (static_cast<int64_t>(b) * p.R + r) * p.N + j;
           zs = p.zstats[pair];
           us = p.ustats[pair];
         }
@@ -539,7 +544,8 @@ __global__ void __launch_bounds__(kOThreads, 1)
         s.zr[buf][pp] = zs.y;
         s.um[buf][pp] = us.x;
         s.ur[buf][pp] = us.y;
-        s.keep[buf][pp] = (!p.masked_zero || (j < p.N && p.mask[b * p.N + r] && p.mask[b * p.N + j])) ? 1.f : 0.f;
+        s.keep[buf][pp] =
+            (!p.masked_zero || (j < p.N && p.mask[b * p.N + p.row0 + r] && p.mask[b * p.N + j])) ? 1.f : 0.f;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.st_full[buf]);
@@ -642,108 +648,151 @@ int trimul_prepare(const TriMulWeights& w, void* packed, cudaStream_t stream) {
   return rc;
 }
 
+namespace {
+
+// z tensor map over the rows held ([B * R] rows of N pairs x 128 channels), box of `rows`
+// pairs of one row (row tiles) or, for the incoming direction, one pair of `rows` rows
+// (column tiles, R == N).
+int z_map(CUtensorMap* m, const void* z, int B, int R, int N, int rows, bool column_tiles) {
+  const uint64_t dims[3] = {kC, static_cast<uint64_t>(N), static_cast<uint64_t>(B) * R};
+  const uint64_t strides[2] = {kC * 2, static_cast<uint64_t>(N) * kC * 2};
+  const uint32_t box_row[3] = {64, static_cast<uint32_t>(rows), 1};
+  const uint32_t box_col[3] = {64, 1, static_cast<uint32_t>(rows)};
+  return make_map(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, z, dims, strides, column_tiles ? box_col : box_row,
+                  CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int launch_proj(const void* z, const uint8_t* mask, const void* packed, void* left, void* right, float2* zstats,
+                int B, int R, int N, int row0, int64_t ls_b, int64_t ls_c, int64_t ls_r, int outgoing,
+                const DeviceInfo& info, cudaStream_t stream) {
+  const int np = (N + 7) / 8 * 8;
+  CUtensorMap map_z;
+  int st = z_map(&map_z, z, B, R, N, kPTile, !outgoing);
+  if (st) return st;
+  ProjParams pp{static_cast<const uint8_t*>(packed), mask, static_cast<__nv_bfloat16*>(left),
+                static_cast<__nv_bfloat16*>(right), zstats, B, N, np, R, row0, ls_b, ls_c, ls_r, outgoing, info.err};
+  const int ptiles = B * R * ((N + kPTile - 1) / kPTile);
+  const int pgrid = ptiles < info.num_sms ? ptiles : info.num_sms;
+  const size_t proj_smem = sizeof(ProjSmem) + 1024;
+  cudaFuncSetAttribute(trimul_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(proj_smem));
+  trimul_proj_kernel<<<pgrid, kPThreads, proj_smem, stream>>>(map_z, pp);
+  return cuda_status(static_cast<int>(cudaGetLastError()), "trimul_proj launch");
+}
+
+// U[c] (R x N) = L[c] (R x N(k)) R[c]^T for the 128 channels of one batch entry per call
+// group; element strides of L / R: channel `lc`, row `lr`; batch `lb` (batch count B).
+int launch_contract(const void* left, const void* right, void* u, int B, int R, int N, int64_t l_c, int64_t l_r,
+                    int64_t r_c, int64_t r_r, const DeviceInfo& info, cudaStream_t stream) {
+  const int np = (N + 7) / 8 * 8;
+  CUtensorMap map_l, map_r;
+  const int bn = N > 128 ? 256 : 128;
+  const uint64_t ldims[3] = {static_cast<uint64_t>(N), static_cast<uint64_t>(R), static_cast<uint64_t>(B) * kH};
+  const uint64_t lstrides[2] = {static_cast<uint64_t>(l_r) * 2, static_cast<uint64_t>(l_c) * 2};
+  const uint64_t rdims[3] = {static_cast<uint64_t>(N), static_cast<uint64_t>(N), static_cast<uint64_t>(B) * kH};
+  const uint64_t rstrides[2] = {static_cast<uint64_t>(r_r) * 2, static_cast<uint64_t>(r_c) * 2};
+  const uint32_t box_a[3] = {64, 128, 1};
+  const uint32_t box_b[3] = {64, static_cast<uint32_t>(bn), 1};
+  int st = make_map(&map_l, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, left, ldims, lstrides, box_a, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st) return st;
+  st = make_map(&map_r, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, right, rdims, rstrides, box_b, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st) return st;
+  GemmParams gp;
+  gp.M = R;
+  gp.N = N;
+  gp.K = N;
+  gp.batch = B * kH;
+  gp.D = u;
+  gp.ldd = np;
+  gp.batch_stride_d = static_cast<int64_t>(R) * np;
+  gp.d_is_f32 = 0;
+  gp.epilogue = kEpiStore;
+  gp.bias = nullptr;
+  gp.residual = nullptr;
+  gp.row_mask = nullptr;
+  gp.err = info.err;
+  return cuda_status(launch_gemm_nt(map_l, map_r, gp, bn, info.num_sms, stream), "trimul contraction launch");
+}
+
+int launch_out(const void* z, const uint8_t* mask, const void* packed, const void* u, const float2* zstats,
+               float2* ustats, void* out, int B, int R, int N, int row0, int masked_zero, const DeviceInfo& info,
+               cudaStream_t stream) {
+  const int np = (N + 7) / 8 * 8;
+  {
+    const int64_t threads = static_cast<int64_t>(B) * R * ((N + 7) / 8);
+    trimul_ustats_kernel<<<static_cast<int>((threads + 255) / 256), 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(u), ustats, B, R, N, np);
+    int st = cuda_status(static_cast<int>(cudaGetLastError()), "trimul_ustats launch");
+    if (st) return st;
+  }
+  CUtensorMap map_zo, map_out, map_u;
+  int st = z_map(&map_zo, z, B, R, N, kOTile, false);
+  if (st) return st;
+  st = z_map(&map_out, out, B, R, N, kOTile, false);
+  if (st) return st;
+  const uint64_t udims[3] = {static_cast<uint64_t>(N), static_cast<uint64_t>(R), static_cast<uint64_t>(B) * kH};
+  const uint64_t ustrides[2] = {static_cast<uint64_t>(np) * 2, static_cast<uint64_t>(R) * np * 2};
+  const uint32_t ubox[3] = {64, 1, kH};  // [128 channels][64 pairs], 128-byte swizzled rows
+  st = make_map(&map_u, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, u, udims, ustrides, ubox, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st) return st;
+  OutParams op{static_cast<const uint8_t*>(packed), mask, zstats, ustats, B, N, R, row0, masked_zero, info.err};
+  const size_t out_smem = sizeof(OutSmem) + 1024;
+  const int otiles = B * R * ((N + kOTile - 1) / kOTile);
+  const int ogrid = otiles < info.num_sms ? otiles : info.num_sms;
+  cudaFuncSetAttribute(trimul_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(out_smem));
+  trimul_out_kernel<<<ogrid, kOThreads, out_smem, stream>>>(map_zo, map_u, map_out, op);
+  return cuda_status(static_cast<int>(cudaGetLastError()), "trimul_out launch");
+}
+
+}  // namespace
+
 int trimul_forward(const void* z, const uint8_t* mask, const void* packed, void* out, void* workspace, int B, int N,
                    int outgoing, int masked_zero, int stages, const DeviceInfo& info, cudaStream_t stream) {
   const int np = (N + 7) / 8 * 8;
   const size_t one = static_cast<size_t>(B) * kH * N * np * 2;
   const size_t aligned = (one + 255) / 256 * 256;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  __nv_bfloat16* left = reinterpret_cast<__nv_bfloat16*>(ws);
-  __nv_bfloat16* right = reinterpret_cast<__nv_bfloat16*>(ws + aligned);
-  __nv_bfloat16* u = reinterpret_cast<__nv_bfloat16*>(ws + 2 * aligned);
+  void* left = ws;
+  void* right = ws + aligned;
+  void* u = ws + 2 * aligned;
   const size_t stats_bytes = (static_cast<size_t>(B) * N * N * 8 + 255) / 256 * 256;
   float2* zstats = reinterpret_cast<float2*>(ws + 3 * aligned);
   float2* ustats = reinterpret_cast<float2*>(ws + 3 * aligned + stats_bytes);
-  const int tiles = B * N * ((N + kTile - 1) / kTile);
-  const int grid_groups = (tiles + kGroups - 1) / kGroups;
-  const int grid = grid_groups < info.num_sms ? grid_groups : info.num_sms;
-  const int ptiles = B * N * ((N + kPTile - 1) / kPTile);
-  const int pgrid = ptiles < info.num_sms ? ptiles : info.num_sms;
-  int st;
-
-  // pair tensor maps: dims {c, N (col), B*N (row)}
-  CUtensorMap map_z, map_out;
-  {
-    const uint64_t dims[3] = {kC, static_cast<uint64_t>(N), static_cast<uint64_t>(B) * N};
-    const uint64_t strides[2] = {kC * 2, static_cast<uint64_t>(N) * kC * 2};
-    const uint32_t box_row[3] = {64, kPTile, 1};
-    const uint32_t box_col[3] = {64, 1, kPTile};
-    st = make_map(&map_z, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, z, dims, strides, outgoing ? box_row : box_col,
-                  CU_TENSOR_MAP_SWIZZLE_128B);
-    if (st) return st;
-  }
+  // channel-major L, R, U: [B * 128][N][Np]
+  const int64_t s_c = static_cast<int64_t>(N) * np, s_b = kH * s_c;
+  int st = 0;
   if (stages & 1) {
-    ProjParams pp{static_cast<const uint8_t*>(packed), mask, left, right, zstats, B, N, np, outgoing, info.err};
-    const size_t proj_smem = sizeof(ProjSmem) + 1024;
-    cudaFuncSetAttribute(trimul_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(proj_smem));
-    trimul_proj_kernel<<<pgrid, kPThreads, proj_smem, stream>>>(map_z, pp);
-    st = cuda_status(static_cast<int>(cudaGetLastError()), "trimul_proj launch");
+    st = launch_proj(z, mask, packed, left, right, zstats, B, N, N, 0, s_b, s_c, np, outgoing, info, stream);
     if (st) return st;
   }
+  if (stages & 2) {
+    st = launch_contract(left, right, u, B, N, N, s_c, np, s_c, np, info, stream);
+    if (st) return st;
+  }
+  if (stages & 4) st = launch_out(z, mask, packed, u, zstats, ustats, out, B, N, N, 0, masked_zero, info, stream);
+  return st;
+}
 
-  // contraction: U[c] = L[c] R[c]^T, batch = B * h
-  CUtensorMap map_l, map_r;
-  {
-    const uint64_t dims[3] = {static_cast<uint64_t>(N), static_cast<uint64_t>(N), static_cast<uint64_t>(B) * kH};
-    const uint64_t strides[2] = {static_cast<uint64_t>(np) * 2, static_cast<uint64_t>(N) * np * 2};
-    const int bn = N > 128 ? 256 : 128;
-    const uint32_t box_a[3] = {64, 128, 1};
-    const uint32_t box_b[3] = {64, static_cast<uint32_t>(bn), 1};
-    st = make_map(&map_l, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, left, dims, strides, box_a, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (st) return st;
-    st = make_map(&map_r, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, right, dims, strides, box_b,
-                  CU_TENSOR_MAP_SWIZZLE_128B);
-    if (st) return st;
-    GemmParams gp;
-    gp.M = N;
-    gp.N = N;
-    gp.K = N;
-    gp.batch = B * kH;
-    gp.D = u;
-    gp.ldd = np;
-    gp.batch_stride_d = static_cast<int64_t>(N) * np;
-    gp.d_is_f32 = 0;
-    gp.epilogue = kEpiStore;
-    gp.bias = nullptr;
-    gp.residual = nullptr;
-    gp.row_mask = nullptr;
-    gp.err = info.err;
-    if (stages & 2) {
-      st = cuda_status(launch_gemm_nt(map_l, map_r, gp, bn, info.num_sms, stream), "trimul contraction launch");
-      if (st) return st;
-    }
-  }
+// ---- row-sharded entry points (B = 1): the rank holds rows [row0, row0 + R) of the pair.
+// L, R (and the gathered right operand): [rows][128][Np] so that an all-gather over rows
+// concatenates whole tensors; U: [128][R][Np]; statistics [R][N].
+int trimul_shard_proj(const void* z, const uint8_t* mask, const void* packed, void* left, void* right, void* zstats,
+                      int R, int N, int row0, const DeviceInfo& info, cudaStream_t stream) {
+  const int64_t np = (N + 7) / 8 * 8;
+  return launch_proj(z, mask, packed, left, right, static_cast<float2*>(zstats), 1, R, N, row0, R * kH * np, np,
+                     kH * np, 1, info, stream);
+}
 
-  // output
-  CUtensorMap map_zo, map_u;
-  {
-    const uint64_t dims[3] = {kC, static_cast<uint64_t>(N), static_cast<uint64_t>(B) * N};
-    const uint64_t strides[2] = {kC * 2, static_cast<uint64_t>(N) * kC * 2};
-    const uint32_t box[3] = {64, kTile, 1};
-    st = make_map(&map_zo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, z, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (st) return st;
-    st = make_map(&map_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (st) return st;
-    const uint64_t udims[3] = {static_cast<uint64_t>(N), static_cast<uint64_t>(N), static_cast<uint64_t>(B) * kH};
-    const uint64_t ustrides[2] = {static_cast<uint64_t>(np) * 2, static_cast<uint64_t>(N) * np * 2};
-    const uint32_t ubox[3] = {64, 1, kH};  // [128 channels][64 pairs], 128-byte swizzled rows
-    st = make_map(&map_u, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, u, udims, ustrides, ubox, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (st) return st;
-  }
-  if (!(stages & 4)) return 0;
-  {
-    const int64_t threads = static_cast<int64_t>(B) * N * ((N + 7) / 8);
-    trimul_ustats_kernel<<<static_cast<int>((threads + 255) / 256), 256, 0, stream>>>(u, ustats, B, N, np);
-    st = cuda_status(static_cast<int>(cudaGetLastError()), "trimul_ustats launch");
-    if (st) return st;
-  }
-  OutParams op{static_cast<const uint8_t*>(packed), mask, zstats, ustats, B, N, masked_zero, info.err};
-  const size_t out_smem = sizeof(OutSmem) + 1024;
-  const int otiles = B * N * ((N + kOTile - 1) / kOTile);
-  const int ogrid = otiles < info.num_sms ? otiles : info.num_sms;
-  cudaFuncSetAttribute(trimul_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(out_smem));
-  trimul_out_kernel<<<ogrid, kOThreads, out_smem, stream>>>(map_zo, map_u, map_out, op);
-  return cuda_status(static_cast<int>(cudaGetLastError()), "trimul_out launch");
+int trimul_shard_contract(const void* left, const void* right_all, void* u, int R, int N, const DeviceInfo& info,
+                          cudaStream_t stream) {
+  const int64_t np = (N + 7) / 8 * 8;
+  return launch_contract(left, right_all, u, 1, R, N, np, kH * np, np, kH * np, info, stream);
+}
+
+int trimul_shard_out(const void* z, const uint8_t* mask, const void* packed, const void* u, const void* zstats,
+                     void* ustats, void* out, int R, int N, int row0, int masked_zero, const DeviceInfo& info,
+                     cudaStream_t stream) {
+  return launch_out(z, mask, packed, u, static_cast<const float2*>(zstats), static_cast<float2*>(ustats), out, 1, R,
+                    N, row0, masked_zero, info, stream);
 }
 
 }  // namespace ffb

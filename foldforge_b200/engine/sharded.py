@@ -1,0 +1,343 @@
+"""Row-sharded (axial-parallel) Pairformer block over the GPUs of one box.
+
+FoldForge runs the Pairformer on one device; this module adds the pair-axis sharding of the
+AF3 trunk across the ranks of one process group (no reference counterpart). Rank r holds the
+pair rows ``[r N / P, (r + 1) N / P)`` of ``z [N, N, 128]`` (batch 1); the single track is
+replicated. Row-wise ops run on the local rows; the column-wise ops run as their row-wise
+counterparts on the transposed pair, reached by an all-to-all:
+
+* TriMul incoming on z = TriMul outgoing on z^T with the left / right projections (and
+  their gates) swapped;
+* TriAttn ending on z = TriAttn starting on z^T with the UNtransposed pair bias (AF3,
+  ``transposed_column_pair_bias=False``), i.e. the transpose of the bias projected from z^T.
+
+Per block: ``TMo (rows) -> A2A -> TMi (z^T rows) -> A2A -> TAs (rows) -> A2A -> TAe (z^T
+rows) -> transition (z^T rows) -> A2A -> single track``: four all-to-alls, plus all-gathers
+of the TriMul right operand (``[rows][128][Np]`` bf16), the triangle-attention bias rows and
+the single-attention pair-bias rows. The b200 ops call the row-sharded C-ABI pieces
+(``ffb_*_shard_*``); the torch ops restate the same equations in fp32 for CPU checks of the
+schedule (legacy/reference/triangle.py:19-50, legacy/attention.py:108-171,
+legacy/reference/transition.py:28-59, legacy/transformer.py:88-133).
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+from foldforge_b200 import _lib
+
+Tensor = torch.Tensor
+_LOG2E = 1.4426950408889634
+
+
+# --------------------------------------------------------------------------- communication
+class ShardComm:
+    """The two collectives of the schedule over one process group.
+
+    NCCL groups exchange device tensors directly; other backends (gloo) exchange host copies.
+    ``world == 1`` (no group) makes both collectives local copies."""
+
+    def __init__(self, group: dist.ProcessGroup | None = None):
+        self.group = group
+        if dist.is_available() and dist.is_initialized():
+            self.rank = dist.get_rank(group)
+            self.world = dist.get_world_size(group)
+            self.nccl = dist.get_backend(group) == "nccl"
+        else:
+            self.rank, self.world, self.nccl = 0, 1, False
+
+    def rows(self, n: int) -> tuple[int, int]:
+        """(R, row0) of this rank for a pair of n rows (n must divide evenly)."""
+        if n % self.world:
+            raise ValueError(f"N={n} is not divisible by the {self.world} ranks of the group")
+        r = n // self.world
+        return r, self.rank * r
+
+    def gather_rows(self, x: Tensor) -> Tensor:
+        """Concatenate every rank's ``x`` along dim 0 (rank order)."""
+        if self.world == 1:
+            return x
+        if self.nccl or not x.is_cuda:
+            out = torch.empty((self.world * x.shape[0],) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+            dist.all_gather_into_tensor(out, x.contiguous(), group=self.group)
+            return out
+        host = x.detach().cpu().contiguous()
+        out = torch.empty((self.world * host.shape[0],) + tuple(host.shape[1:]), dtype=host.dtype)
+        dist.all_gather_into_tensor(out, host, group=self.group)
+        return out.to(x.device)
+
+    def transpose(self, x: Tensor) -> Tensor:
+        """Rows [row0, row0 + R) of z -> the same rows of z^T (x: [R, N, c], N = world * R)."""
+        if self.world == 1:
+            return x.transpose(0, 1).contiguous()
+        r, n, c = x.shape
+        p = self.world
+        # send[q] = x[:, q R : (q + 1) R] (the block of z^T rows that rank q holds)
+        send = x.view(r, p, r, c).permute(1, 0, 2, 3).contiguous()
+        if self.nccl or not x.is_cuda:
+            recv = torch.empty_like(send)
+            dist.all_to_all_single(recv, send, group=self.group)
+        else:
+            host = send.cpu()
+            recv_h = torch.empty_like(host)
+            dist.all_to_all_single(recv_h, host, group=self.group)
+            recv = recv_h.to(x.device)
+        # recv[q][i][a] = z[q R + i][row0 + a]  ->  y[a][q R + i]
+        return recv.permute(2, 0, 1, 3).reshape(r, n, c).contiguous()
+
+
+def swapped_trimul_weights(weights: dict[str, Tensor]) -> dict[str, Tensor]:
+    """TriMul weights with the left / right projections and gates exchanged: incoming on z
+    equals outgoing on z^T with these."""
+    sw = dict(weights)
+    for a, b in (("to_left.weight", "to_right.weight"), ("to_left_gate.weight", "to_right_gate.weight")):
+        sw[a], sw[b] = weights[b], weights[a]
+    return sw
+
+
+# --------------------------------------------------------------------------- b200 shard ops
+def _ptr(t: Tensor | None) -> ctypes.c_void_p:
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+class B200ShardOps:
+    """The row-sharded pieces on the sm_100a kernels (bf16 activations, master weights)."""
+
+    def __init__(self, comm: ShardComm, masked_zero: bool = True):
+        self.comm = comm
+        self.masked = int(masked_zero)
+
+    def trimul(self, z: Tensor, mask: Tensor, packed: Tensor) -> Tensor:
+        r, n, _ = z.shape
+        _, row0 = self.comm.rows(n)
+        np_ = (n + 7) // 8 * 8
+        dev = z.device
+        left = torch.empty((r, 128, np_), dtype=torch.bfloat16, device=dev)
+        right = torch.empty_like(left)
+        zstats = torch.empty((r, n, 2), dtype=torch.float32, device=dev)
+        _lib.call("ffb_trimul_shard_proj", _ptr(z), _ptr(mask), _ptr(packed), _ptr(left), _ptr(right), _ptr(zstats),
+                  r, n, row0, _stream())
+        right_all = self.comm.gather_rows(right)
+        u = torch.empty((128, r, np_), dtype=torch.bfloat16, device=dev)
+        _lib.call("ffb_trimul_shard_contract", _ptr(left), _ptr(right_all), _ptr(u), r, n, _stream())
+        ustats = torch.empty_like(zstats)
+        out = torch.empty_like(z)
+        _lib.call("ffb_trimul_shard_out", _ptr(z), _ptr(mask), _ptr(packed), _ptr(u), _ptr(zstats), _ptr(ustats),
+                  _ptr(out), r, n, row0, self.masked, _stream())
+        return out
+
+    def triattn(self, z: Tensor, mask: Tensor, packed: Tensor, *, transposed_bias: bool) -> Tensor:
+        r, n, _ = z.shape
+        _, row0 = self.comm.rows(n)
+        np_ = (n + 7) // 8 * 8
+        dev = z.device
+        q = torch.empty((r, 4, n, 32), dtype=torch.bfloat16, device=dev)
+        k = torch.empty_like(q)
+        vt = torch.empty((r, 4, 32, np_), dtype=torch.bfloat16, device=dev)
+        bias_rows = torch.empty((r, 4, np_), dtype=torch.bfloat16, device=dev)
+        _lib.call("ffb_triattn_shard_proj", _ptr(z), _ptr(packed), _ptr(q), _ptr(k), _ptr(vt), _ptr(bias_rows), r, n,
+                  _stream())
+        bias_all = self.comm.gather_rows(bias_rows)  # [N (rows of the pair held), 4, Np]
+        if transposed_bias:
+            # bias[q][h][k] = G[k][h][q]: the ending node's bias comes from the untransposed pair
+            t = torch.zeros_like(bias_all)
+            t[:, :, :n] = bias_all[:, :, :n].permute(2, 1, 0)
+            bias_all = t
+        o = torch.empty((r, n, 128), dtype=torch.bfloat16, device=dev)
+        _lib.call("ffb_triattn_shard_attn", _ptr(q), _ptr(k), _ptr(vt), _ptr(bias_all), _ptr(mask), _ptr(o), r, n,
+                  row0, _stream())
+        out = torch.empty_like(z)
+        _lib.call("ffb_triattn_shard_out", _ptr(z), _ptr(mask), _ptr(packed), _ptr(o), _ptr(out), r, n, row0,
+                  self.masked, _stream())
+        return out
+
+    def transition(self, z: Tensor, mask: Tensor, packed: Tensor) -> Tensor:
+        r, n, _ = z.shape
+        _, row0 = self.comm.rows(n)
+        out = torch.empty_like(z)
+        _lib.call("ffb_transition_shard_fwd", _ptr(z), _ptr(mask), _ptr(packed), _ptr(out), r, n, row0, self.masked,
+                  _stream())
+        return out
+
+    def single(self, s: Tensor, z: Tensor, mask: Tensor, apb_packed: Tensor, gate_bias: float,
+               st_packed: Tensor) -> Tensor:
+        from foldforge_b200 import kernels
+
+        r, n, _ = z.shape
+        pb_rows = torch.empty((r, 16, n), dtype=torch.float32, device=z.device)
+        _lib.call("ffb_apb_shard_pair_bias", _ptr(z), _ptr(apb_packed), _ptr(pb_rows), r, n, _stream())
+        pb_all = self.comm.gather_rows(pb_rows)  # [N, 16, N]
+        lib = _lib.load()
+        ws = torch.empty(int(lib.ffb_apb_single_workspace_bytes(n)), dtype=torch.uint8, device=z.device)
+        s2 = torch.empty_like(s)
+        _lib.call("ffb_apb_shard_single", _ptr(s), _ptr(mask), _ptr(apb_packed), _ptr(pb_all), _ptr(None), 0,
+                  ctypes.c_float(gate_bias), _ptr(s2), _ptr(ws), ctypes.c_size_t(ws.numel()), n, self.masked,
+                  _stream())
+        return kernels.single_transition(s2[None], mask[None], st_packed, masked_zero=bool(self.masked))[0]
+
+
+# --------------------------------------------------------------------------- torch shard ops
+def _ln(x: Tensor, w: Tensor | None, b: Tensor | None) -> Tensor:
+    return F.layer_norm(x, x.shape[-1:], w, b, 1e-5)
+
+
+def _lin(x: Tensor, w: Tensor) -> Tensor:
+    return x @ w.t()
+
+
+class TorchShardOps:
+    """The same row-sharded pieces in fp32 torch (CPU or GPU): a check of the schedule."""
+
+    def __init__(self, comm: ShardComm, masked_zero: bool = True):
+        self.comm = comm
+        self.masked_zero = masked_zero
+
+    def _pair_mask(self, mask: Tensor, n: int) -> Tensor:
+        r, row0 = self.comm.rows(n)
+        m = mask.float()
+        return m[row0:row0 + r, None] * m[None, :]  # [R, N]
+
+    def trimul(self, z: Tensor, mask: Tensor, w: dict[str, Tensor]) -> Tensor:
+        r, n, _ = z.shape
+        pm = self._pair_mask(mask, n)[..., None]
+        x = _ln(z, w["ln_pair.weight"], w["ln_pair.bias"])
+        left = _lin(x, w["to_left.weight"]) * torch.sigmoid(_lin(x, w["to_left_gate.weight"])) * pm
+        right = _lin(x, w["to_right.weight"]) * torch.sigmoid(_lin(x, w["to_right_gate.weight"])) * pm
+        right_all = self.comm.gather_rows(right)  # [N, N, h]
+        u = torch.einsum("ikc,jkc->ijc", left, right_all)
+        delta = _lin(_ln(u, w["ln_out.weight"], w["ln_out.bias"]), w["to_out.weight"]) * torch.sigmoid(
+            _lin(x, w["to_gate.weight"]))
+        if self.masked_zero:
+            delta = delta * pm
+        return z + delta
+
+    def triattn(self, z: Tensor, mask: Tensor, w: dict[str, Tensor], *, transposed_bias: bool) -> Tensor:
+        r, n, c = z.shape
+        h = w["to_bias.weight"].shape[0]
+        d = w["to_query.weight"].shape[0] // h
+        x = _ln(z, w["ln_pair.weight"], w["ln_pair.bias"])
+        bias_all = self.comm.gather_rows(_lin(x, w["to_bias.weight"]))  # [N(q), N(k), H] of the pair held
+        if transposed_bias:
+            bias_all = bias_all.transpose(0, 1)
+        bias = bias_all.permute(2, 0, 1)  # [H, q, k]
+
+        def heads(t: Tensor) -> Tensor:  # [R, N, H*d] -> [R, H, N, d]
+            return t.reshape(r, n, h, d).permute(0, 2, 1, 3)
+
+        q = heads(_lin(x, w["to_query.weight"])) / d ** 0.5
+        k = heads(_lin(x, w["to_key.weight"]))
+        v = heads(_lin(x, w["to_value.weight"]))
+        logits = q @ k.transpose(-1, -2) + bias[None]
+        keep = self._pair_mask(mask, n)[:, None, None, :] > 0  # key mask of row i: m_i m_k
+        logits = torch.where(keep, logits, torch.full_like(logits, -1e9))
+        o = (logits.softmax(-1) @ v).permute(0, 2, 1, 3).reshape(r, n, h * d)
+        delta = _lin(torch.sigmoid(_lin(x, w["to_gate.weight"])) * o, w["to_out.weight"])
+        if self.masked_zero:
+            delta = delta * self._pair_mask(mask, n)[..., None]
+        return z + delta
+
+    def transition(self, z: Tensor, mask: Tensor, w: dict[str, Tensor]) -> Tensor:
+        x = _ln(z, w["ln_in.weight"], w["ln_in.bias"])
+        delta = _lin(F.silu(_lin(x, w["expand_a.weight"])) * _lin(x, w["expand_b.weight"]), w["squeeze.weight"])
+        if self.masked_zero:
+            delta = delta * self._pair_mask(mask, z.shape[1])[..., None]
+        return z + delta
+
+    def single(self, s: Tensor, z: Tensor, mask: Tensor, wa: dict[str, Tensor], gate_bias: float,
+               wt: dict[str, Tensor]) -> Tensor:
+        n = z.shape[1]
+        hs = wa["to_bias.weight"].shape[0]
+        pb = self.comm.gather_rows(_lin(_ln(z, wa["ln_pair.weight"], None), wa["to_bias.weight"]))  # [N, N, 16]
+        y = _ln(s, wa["ln_single.weight"], wa["ln_single.bias"])
+        cs = y.shape[-1]
+        ds = cs // hs
+        q = _lin(y, wa["to_query.weight"]) + wa["to_query.bias"]
+        k, v = _lin(y, wa["to_key.weight"]), _lin(y, wa["to_value.weight"])
+        q, k, v = (t.reshape(n, hs, ds).transpose(0, 1) for t in (q, k, v))
+        logits = q @ k.transpose(-1, -2) / ds ** 0.5 + pb.permute(2, 0, 1)
+        logits = torch.where(mask[None, None, :] > 0, logits, torch.full_like(logits, -1e9))
+        o = (logits.softmax(-1) @ v).transpose(0, 1).reshape(n, cs)
+        delta = _lin(torch.sigmoid(_lin(y, wa["to_gate.weight"]) + gate_bias) * o, wa["to_out.weight"])
+        if self.masked_zero:
+            delta = delta * mask.float()[:, None]
+        s = s + delta
+        x = _ln(s, wt["ln_in.weight"], wt["ln_in.bias"])
+        d2 = _lin(F.silu(_lin(x, wt["expand_a.weight"])) * _lin(x, wt["expand_b.weight"]), wt["squeeze.weight"])
+        if self.masked_zero:
+            d2 = d2 * mask.float()[:, None]
+        return s + d2
+
+
+# --------------------------------------------------------------------------- the block
+def _sub(state: dict[str, Tensor], prefix: str) -> dict[str, Tensor]:
+    return {k[len(prefix) + 1:]: v for k, v in state.items() if k.startswith(prefix + ".")}
+
+
+class ShardedPairformerBlock:
+    """One AF3 Pairformer block over the row shards of a process group.
+
+    ``block`` is an engine :class:`~foldforge_b200.engine.modules.PairformerBlock` (its
+    weights are used, not its forward); ``ops`` is ``"b200"`` (the kernels; bf16 pair rows on
+    the rank's GPU) or ``"torch"`` (fp32 restatement)."""
+
+    def __init__(self, block, comm: ShardComm | None = None, *, ops: str = "b200", masked_zero: bool = True):
+        self.comm = comm or ShardComm()
+        self.ops_name = ops
+        state = {k: v.detach() for k, v in block.state_dict().items()}
+        self.gate_bias = float(getattr(block.single_attention, "gate_bias", 0.0))
+        self.w = {name: _sub(state, name) for name in (
+            "tri_multi_outgoing", "tri_multi_incoming", "tri_atten_starting", "tri_atten_ending",
+            "transition_pair", "single_attention", "single_transition")}
+        if "to_query.bias" not in self.w["single_attention"]:
+            self.w["single_attention"]["to_query.bias"] = torch.zeros(
+                self.w["single_attention"]["to_query.weight"].shape[0])
+        # TriMul incoming runs as outgoing on z^T with left / right swapped
+        self.w["tri_multi_incoming_t"] = swapped_trimul_weights(self.w["tri_multi_incoming"])
+        if ops == "b200":
+            self.ops = B200ShardOps(self.comm, masked_zero)
+            self.packs: dict[str, Tensor] = {}
+        elif ops == "torch":
+            self.ops = TorchShardOps(self.comm, masked_zero)
+        else:
+            raise ValueError(f"unknown shard ops {ops!r}")
+
+    def _pack(self, name: str, device: torch.device) -> Tensor:
+        from foldforge_b200 import kernels
+
+        if name not in self.packs:
+            prep = {"tri_multi_outgoing": kernels.trimul_prepare, "tri_multi_incoming_t": kernels.trimul_prepare,
+                    "tri_atten_starting": kernels.triattn_prepare, "tri_atten_ending": kernels.triattn_prepare,
+                    "transition_pair": kernels.transition_prepare, "single_attention": kernels.apb_prepare,
+                    "single_transition": kernels.single_transition_prepare}[name]
+            self.packs[name] = prep(self.w[name], device)
+        return self.packs[name]
+
+    def _arg(self, name: str, device: torch.device):
+        return self._pack(name, device) if self.ops_name == "b200" else self.w[name]
+
+    def __call__(self, z: Tensor, mask: Tensor, s: Tensor) -> tuple[Tensor, Tensor]:
+        """z: this rank's pair rows ``[R, N, 128]``; mask ``[N]`` (bool / uint8, all tokens);
+        s ``[N, 384]`` (replicated). Returns the updated rows and single."""
+        comm, ops, dev = self.comm, self.ops, z.device
+        if self.ops_name == "b200":
+            mask = mask.to(torch.uint8).contiguous()
+        a = lambda name: self._arg(name, dev)  # noqa: E731
+        z = ops.trimul(z, mask, a("tri_multi_outgoing"))
+        y = comm.transpose(z)
+        y = ops.trimul(y, mask, a("tri_multi_incoming_t"))
+        z = comm.transpose(y)
+        z = ops.triattn(z, mask, a("tri_atten_starting"), transposed_bias=False)
+        y = comm.transpose(z)
+        y = ops.triattn(y, mask, a("tri_atten_ending"), transposed_bias=True)
+        y = ops.transition(y, mask, a("transition_pair"))
+        z = comm.transpose(y)
+        s = ops.single(s, z, mask, a("single_attention"), self.gate_bias, a("single_transition"))
+        return z, s

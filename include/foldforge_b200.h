@@ -172,6 +172,36 @@ int ffb_single_transition_fwd(const void* s, const uint8_t* mask, const void* pa
 int ffb_single_transition_fwd_noalloc(const void* s, const uint8_t* mask, const void* packed, void* out, int B, int N,
                                       int masked, void* stream);
 
+/* ---- Row-sharded pieces (axial parallelism over the GPUs of one box; B = 1). A rank holds
+ * pair rows [row0, row0 + R) of the N x N pair z [R, N, 128] (bf16), or of its transpose
+ * for the column-wise ops (TriMul incoming = outgoing on z^T with the left / right weights
+ * swapped; TriAttn ending = starting on z^T with the untransposed bias). The host moves data
+ * between the pieces with NCCL (all-gather over rows, all-to-all transposes); no new
+ * reference interface corresponds to these: FoldForge has no multi-GPU Pairformer.
+ * Layouts: TriMul L, R, and the gathered right operand [rows][128][Np] bf16 (Np = N rounded
+ * up to 8), U [128][R][Np] bf16, statistics [R][N] float2; TriAttn Q, K [R][4][N][32],
+ * V^T [R][4][32][Np], bias rows [R][4][Np] (gathered: [N][4][Np], rows = queries), o [R][N][128];
+ * single-track pair-bias rows [R][16][N] fp32 (gathered: [N][16][N]). Weights are the
+ * ffb_*_prepare images. Status codes as elsewhere. */
+int ffb_trimul_shard_proj(const void* z, const uint8_t* mask, const void* packed, void* left, void* right,
+                          void* zstats, int R, int N, int row0, void* stream);
+int ffb_trimul_shard_contract(const void* left, const void* right_all, void* u, int R, int N, void* stream);
+int ffb_trimul_shard_out(const void* z, const uint8_t* mask, const void* packed, const void* u, const void* zstats,
+                         void* ustats, void* out, int R, int N, int row0, int masked, void* stream);
+int ffb_triattn_shard_proj(const void* z, const void* packed, void* q, void* k, void* vt, void* bias_rows, int R, int N,
+                           void* stream);
+int ffb_triattn_shard_attn(const void* q, const void* k, const void* vt, const void* bias_all, const uint8_t* mask,
+                           void* o, int R, int N, int row0, void* stream);
+int ffb_triattn_shard_out(const void* z, const uint8_t* mask, const void* packed, const void* o, void* out, int R, int N,
+                          int row0, int masked, void* stream);
+int ffb_transition_shard_fwd(const void* z, const uint8_t* mask, const void* packed, void* out, int R, int N, int row0,
+                             int masked, void* stream);
+int ffb_apb_shard_pair_bias(const void* z, const void* packed, void* pb_rows, int R, int N, void* stream);
+size_t ffb_apb_single_workspace_bytes(int N);
+int ffb_apb_shard_single(const void* s, const uint8_t* mask, const void* packed, const void* pb_all,
+                         const void* extra_pair_bias, int extra_dtype, float gate_bias, void* out, void* workspace,
+                         size_t workspace_bytes, int N, int masked, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
