@@ -14,9 +14,15 @@ activations. One step = one trunk pass over one input.
 * ``cpu_baseline``: the CPU oracle (a restatement of the reference's block) on this host's
   cores, one block at N = 512, times 48.
 
-``--gpus N`` (torchrun, one rank per GPU): every rank runs its own trunk on its own input
-(replicas: the N = 512 trunk fits one GPU); ``value`` is ms per trunk pass of the whole job
-(max rank time / N), ``scaling`` weak.
+``--gpus N`` (torchrun, one rank per GPU, N > 1): the pair is ROW-SHARDED across the ranks
+(axial parallelism, ``foldforge_b200/engine/sharded.py``: NCCL all-to-all transposes between
+the row-wise and column-wise triangle ops, all-gathers of the TriMul right operand and the
+attention biases; the single track replicated). ``value`` is ms per 48-block trunk pass of
+the whole job (max over ranks) at N = 512 P^(1/3) rounded to a multiple of 8 P tokens (640,
+800, 1024 on 2, 4, 8 GPUs): per-GPU work held at the N = 512 trunk's, ``scaling`` weak, so
+value(1) / value(P) is the weak-scaling efficiency. ``ladder`` reports the benchmark's
+N = 2048 length-ladder trunk (configuration 3, 5% padded suffix) on the same GPUs (strong
+scaling; the N = 1 line carries the single-GPU figure).
 
 ``--impl reference``: the reference's algorithm (CPU oracle) on this host, same metric.
 """
@@ -57,7 +63,17 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--blocks", type=int, default=N_BLOCKS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-ladder", action="store_true", help="skip the N=2048 length-ladder measurement")
     return ap.parse_args()
+
+
+def weak_n(gpus: int) -> int:
+    """Tokens of the weak-scaling trunk on ``gpus`` ranks: 512 P^(1/3), a multiple of 8 P."""
+    unit = 8 * gpus
+    return max(unit, round(N_TOKENS * gpus ** (1.0 / 3.0) / unit) * unit)
+
+
+LADDER_N = 2048
 
 
 def peaks() -> dict:
@@ -333,6 +349,195 @@ def run_b200(args, rank: int, world: int, local: int, dist) -> None:
             line["e2e"] = e2e
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if world == 1 and not args.no_ladder:
+            del graphed, trunk
+            torch.cuda.empty_cache()
+            line["ladder"] = ladder_single_gpu(dev)
+        print(json.dumps(line), flush=True)
+
+
+def ladder_single_gpu(dev: torch.device) -> dict:
+    """The N = 2048 length-ladder trunk on one GPU (CUDA-graph replay): 1 warm-up, 2 timed."""
+    import math
+
+    import foldforge_b200
+    from foldforge_b200.engine.capture import GraphedCall
+    from foldforge_b200.synthetic import inputs, trunk_state
+
+    n = LADDER_N
+    masked = math.ceil(0.05 * n)
+    trunk = foldforge_b200.load(trunk_state(N_BLOCKS, seed=0, scheme="baseline"), backend="b200",
+                                unsupported="error", dtype=torch.bfloat16, device=dev)
+    z, s, tokens = inputs(n, seed=0, masked_suffix=masked)
+    mask = (tokens > 0)[None].to(dev)
+    graphed = GraphedCall(lambda zz, ss: trunk(zz, mask, ss), [z.bfloat16()[None].to(dev), s.bfloat16()[None].to(dev)],
+                          warmup=1)
+    del z
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    graphed.replay()
+    ts = []
+    for _ in range(2):
+        flush.fill_(1.0)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        graphed.replay()
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    del graphed, trunk
+    torch.cuda.empty_cache()
+    ms = sum(ts) / len(ts)
+    return {"n": n, "n_gpus": 1, "ms_per_trunk": round(ms, 1), "ms_per_block": round(ms / N_BLOCKS, 3),
+            "masked_suffix": masked, "steps": 2, "warmup": 1, "parallelism": "single GPU (CUDA-graph replay)"}
+
+
+def run_sharded(args, rank: int, world: int, local: int, dist) -> None:
+    """Row-sharded trunk over the ranks: weak-scaling ``value`` and the N = 2048 ladder."""
+    import math
+
+    import foldforge_b200
+    from foldforge_b200 import _lib, kernels
+    from foldforge_b200.engine.sharded import ShardComm, ShardedPairformerBlock
+    from foldforge_b200.synthetic import inputs, trunk_state
+
+    dev = torch.device("cuda", local)
+    nb = args.blocks
+    trunk = foldforge_b200.load(trunk_state(nb, seed=0, scheme="baseline"), backend="b200", unsupported="error",
+                                dtype=torch.bfloat16, device=dev)
+    comm = ShardComm()
+    blocks = [ShardedPairformerBlock(b, comm, ops="b200", masked_zero=True) for b in trunk.blocks]
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def run_trunk(z_rows, mask, s):
+        for blk in blocks:
+            z_rows, s = blk(z_rows, mask, s)
+        return z_rows, s
+
+    def data(n: int, masked: int):
+        z, s, tokens = inputs(n, seed=0, masked_suffix=masked)
+        r, row0 = comm.rows(n)
+        rows = z[row0:row0 + r].bfloat16().contiguous()
+        return rows, s.bfloat16(), (tokens > 0).to(dev)
+
+    def measure(n: int, masked: int, steps: int, warmup: int, clocks: bool = False):
+        rows_h, s_h, mask = data(n, masked)
+        rows, s = rows_h.to(dev), s_h.to(dev)
+        for _ in range(warmup):
+            run_trunk(rows, mask, s)
+        torch.cuda.synchronize()
+        dist.barrier()
+        sampler = ClockSampler(local) if clocks else None
+        if sampler:
+            sampler.start()
+            time.sleep(0.3)
+        _lib.launch_count = 0
+        ts = []
+        for _ in range(steps):
+            flush.fill_(1.0)
+            torch.cuda.synchronize()
+            dist.barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            run_trunk(rows, mask, s)
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        launches = _lib.launch_count
+        dist.barrier()
+        clk = sampler.stop() if sampler else None
+        ms = max_over_ranks(sum(ts) / len(ts), dist)
+        return ms, clk, launches, (rows_h, s_h, mask)
+
+    n_w = weak_n(world)
+    masked_w = round(MASKED * n_w / N_TOKENS)
+    value_ms, clocks, launches, (rows_h, s_h, mask) = measure(n_w, masked_w, args.steps, max(args.warmup, 3), True)
+    err = _lib.device_error()
+    if err:
+        raise RuntimeError(f"device error word {err} after the timed region")
+
+    e2e = None
+    if not args.no_e2e:
+        rows_pin, s_pin = rows_h.pin_memory(), s_h.pin_memory()
+        out_pin, s_out_pin = torch.empty_like(rows_pin).pin_memory(), torch.empty_like(s_pin).pin_memory()
+        ts = []
+        for _ in range(max(1, min(args.steps, 3))):
+            flush.fill_(1.0)
+            torch.cuda.synchronize()
+            dist.barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            zo, so = run_trunk(rows_pin.to(dev, non_blocking=True), mask, s_pin.to(dev, non_blocking=True))
+            out_pin.copy_(zo, non_blocking=True)
+            s_out_pin.copy_(so, non_blocking=True)
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        e2e = {"value": round(max_over_ranks(sum(ts) / len(ts), dist), 3), "unit": "ms",
+               "h2d_bytes_per_step": rows_pin.numel() * 2 + s_pin.numel() * 2,
+               "d2h_bytes_per_step": out_pin.numel() * 2 + s_out_pin.numel() * 2,
+               "per": "rank (its pair rows and the replicated single), max over ranks"}
+
+    ladder = None
+    if not args.no_ladder:
+        lad_ms, _, _, _ = measure(LADDER_N, math.ceil(0.05 * LADDER_N), 2, 1)
+        ladder = {"n": LADDER_N, "n_gpus": world, "ms_per_trunk": round(lad_ms, 1),
+                  "ms_per_block": round(lad_ms / nb, 3), "masked_suffix": math.ceil(0.05 * LADDER_N), "steps": 2,
+                  "warmup": 1, "parallelism": f"axial row-sharding x{world} (eager)"}
+
+    # dominant kernel alone (triangle-attention core at N = 512 on this GPU)
+    n = N_TOKENS
+    zz, _, tok = inputs(n, seed=0, masked_suffix=MASKED)
+    zz = zz.bfloat16()[None].to(dev)
+    m512 = (tok > 0)[None].to(dev)
+    packed = kernels.triattn_prepare({k[len("tri_atten_starting") + 1:]: v for k, v in trunk.blocks[0].state_dict().items()
+                                      if k.startswith("tri_atten_starting.")}, dev)
+    ws = torch.empty(int(_lib.load().ffb_triattn_workspace_bytes(1, n)), dtype=torch.uint8, device=dev)
+    out = torch.empty_like(zz)
+    kernels.triattn(zz, m512, packed, starting=True, stages=1, workspace=ws, out=out)
+    for _ in range(3):
+        kernels.triattn(zz, m512, packed, starting=True, stages=2, workspace=ws, out=out)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(20):
+        kernels.triattn(zz, m512, packed, starting=True, stages=2, workspace=ws, out=out)
+    b.record()
+    torch.cuda.synchronize()
+    attn_ms = a.elapsed_time(b) / 20
+    attn_flops = 4.0 * n**3 * 128
+    pk = peaks()
+    achieved = attn_flops / (attn_ms * 1e-3) / 1e12
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value_ms, 3), "unit": "ms", "n_gpus": world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": round(value_ms, 3), "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {
+                "workload": f"{nb}-block Pairformer trunk, N={n_w} row-sharded over {world} GPUs (per-GPU work "
+                            f"{n_w ** 3 / world / N_TOKENS ** 3:.2f} x the N=512 trunk), last {masked_w} tokens "
+                            "masked, master precision, eager launches",
+                "model": "AF3 Pairformer block (c_z 128, c_s 384, 4x32 / 16x24 heads)",
+                "global_batch": 1, "seq_len": n_w, "parallelism": f"axial row-sharding x{world} (NCCL all-to-all / "
+                                                                  "all-gather)",
+                "l2": "flushed by a 256 MB write before every timed step",
+                "trunk_tflops": round(block_flops(n_w) * nb / (value_ms * 1e-3) / 1e12, 1),
+                "ms_per_block": round(value_ms / nb, 4),
+            },
+            "roofline": {
+                "kernel": "triattn_attn_kernel (starting node, N=512, one GPU)",
+                "bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16"], "unit": "TFLOP/s",
+                "frac": round(achieved / pk["bf16"], 4), "traffic": ATTN_TRAFFIC_BYTES,
+                "launch_ms": round(attn_ms, 4), "peak_source": f"{pk['source']} (burst: kernel timed alone)",
+                "algorithmic": f"4 * N^3 * 128 = {attn_flops:.3e} flop per launch",
+            },
+            "clocks": clocks,
+            "gpu_launches": launches,
+        }
+        if e2e is not None:
+            line["e2e"] = e2e
+        if ladder is not None:
+            line["ladder"] = ladder
         print(json.dumps(line), flush=True)
 
 
@@ -342,6 +547,8 @@ def main() -> None:
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
+        elif world > 1:
+            run_sharded(args, rank, world, local, dist)
         else:
             run_b200(args, rank, world, local, dist)
     finally:
