@@ -48,9 +48,9 @@ METRIC = "ms per 48-block Pairformer trunk at N=512 bf16; N=2048 at 1/2/4/8 B200
 N_TOKENS = 512
 N_BLOCKS = 48
 MASKED = 26
-#: DRAM traffic of one triangle-attention core launch at N = 512, from the ncu capture
-#: summarised in profiles/triattn_attn_n512.md (dram__bytes_read.sum + dram__bytes_write.sum).
-ATTN_TRAFFIC_BYTES: float | None = None
+#: DRAM traffic of one triangle-attention core launch at N = 512 (dram__bytes_read.sum +
+#: dram__bytes_write.sum of one ncu capture of ``--kernels-once --n 512``: 203.5 + 47.5 MB).
+ATTN_TRAFFIC_BYTES: float | None = 251.0e6
 
 
 def parse() -> argparse.Namespace:
@@ -64,6 +64,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-ladder", action="store_true", help="skip the N=2048 length-ladder measurement")
+    ap.add_argument("--kernels-once", action="store_true",
+                    help="launch every pair-stack kernel once at --n (a driver for ncu captures; no timing)")
     return ap.parse_args()
 
 
@@ -541,8 +543,43 @@ def run_sharded(args, rank: int, world: int, local: int, dist) -> None:
         print(json.dumps(line), flush=True)
 
 
+def kernels_once(n: int) -> None:
+    """Each kernel of one block once on the bench's inputs: TriMul outgoing stages 1, 2, 4,
+    TriAttn starting stages 1, 2, 4, pair transition, attention with pair bias, single
+    transition."""
+    from foldforge_b200 import _lib, kernels
+    from foldforge_b200.synthetic import block_state, inputs
+
+    st = block_state(torch.Generator().manual_seed(0))
+    sub = lambda pre: {k[len(pre) + 1:]: v for k, v in st.items() if k.startswith(pre + ".")}  # noqa: E731
+    dev = torch.device("cuda")
+    z, s, tok = inputs(n, 0, masked_suffix=round(MASKED * n / N_TOKENS))
+    z, s, mask = z.bfloat16()[None].to(dev), s.bfloat16()[None].to(dev), (tok > 0)[None].to(dev)
+    lib = _lib.load()
+    out = torch.empty_like(z)
+    pk = kernels.trimul_prepare(sub("tri_multi_outgoing"), dev)
+    ws = torch.empty(int(lib.ffb_trimul_workspace_bytes(1, n)), dtype=torch.uint8, device=dev)
+    for stg in (1, 2, 4):
+        kernels.trimul(z, mask, pk, outgoing=True, stages=stg, workspace=ws, out=out)
+    pk = kernels.triattn_prepare(sub("tri_atten_starting"), dev)
+    ws = torch.empty(int(lib.ffb_triattn_workspace_bytes(1, n)), dtype=torch.uint8, device=dev)
+    for stg in (1, 2, 4):
+        kernels.triattn(z, mask, pk, starting=True, stages=stg, workspace=ws, out=out)
+    kernels.transition(z, mask, kernels.transition_prepare(sub("transition_pair"), dev))
+    kernels.attention_pair_bias(s, z, mask, kernels.apb_prepare(sub("single_attention"), dev))
+    kernels.single_transition(s, mask, kernels.single_transition_prepare(sub("single_transition"), dev))
+    torch.cuda.synchronize()
+    err = _lib.device_error()
+    print(f"kernels-once N={n}: device error word {err}")
+    if err:
+        raise SystemExit(1)
+
+
 def main() -> None:
     args = parse()
+    if args.kernels_once:
+        kernels_once(args.n)
+        return
     rank, world, local, dist = dist_setup(args.gpus)
     try:
         if args.impl == "reference":
