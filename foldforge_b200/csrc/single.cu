@@ -441,7 +441,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2) single_attention_kernel(
 // ---------------------------------------------------------------- helpers
 int gemm(const void* a, const void* w, void* d, int m, int n, int k, int d_f32, const float* bias, int epilogue,
          const void* residual, const uint8_t* row_mask, const DeviceInfo& info, cudaStream_t stream) {
-  const int bn = n >= 256 ? 256 : 128;
+  // 128-wide tiles unless 256-wide ones already give every SM a tile: the single track's
+  // GEMMs are small (M = B * N tokens), so more CTAs beat wider tiles
+  const int tiles256 = ((m + 127) / 128) * ((n + 255) / 256);
+  const int bn = (n >= 256 && tiles256 >= info.num_sms) ? 256 : 128;
   CUtensorMap ma, mb;
   const uint64_t adims[3] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m), 1};
   const uint64_t astr[2] = {static_cast<uint64_t>(k) * 2, static_cast<uint64_t>(k) * m * 2};

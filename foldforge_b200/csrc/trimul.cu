@@ -378,17 +378,20 @@ struct OutParams {
 };
 
 // Per-pair mean and 1/sqrt(var + 1e-5) of u over its 128 channels (u channel-major
-// [B*h, R, Np], R rows held). A thread owns 8 consecutive pairs of one row and walks the channels with
-// 16-byte loads (coalesced across the warp); the variance is accumulated about the first
-// channel's value (shifted data, no cancellation for rows whose mean is large).
+// [B*h, R, Np], R rows held). Two adjacent lanes own 8 consecutive pairs of one row and walk
+// 64 channels each with 16-byte loads (coalesced across the warp, 16 loads in flight per
+// pair group); the variance is accumulated about channel 0's value (shifted data, no
+// cancellation for pairs whose mean is large) and the two halves are combined by a shuffle.
 __global__ void __launch_bounds__(256) trimul_ustats_kernel(const __nv_bfloat16* __restrict__ u,
                                                              float2* __restrict__ ustats, int B, int R, int N,
                                                              int Np) {
   const int groups = (N + 7) / 8;
-  const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (gid >= static_cast<int64_t>(B) * R * groups) return;
-  const int g = static_cast<int>(gid % groups);
-  const int64_t bi = gid / groups;  // b * R + i
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t gid = tid >> 1;
+  const int half = static_cast<int>(tid & 1);
+  const bool live = gid < static_cast<int64_t>(B) * R * groups;
+  const int g = live ? static_cast<int>(gid % groups) : 0;
+  const int64_t bi = live ? gid / groups : 0;  // b * R + i
   const int b = static_cast<int>(bi / R), i = static_cast<int>(bi % R);
   const int64_t plane = static_cast<int64_t>(R) * Np;
   const __nv_bfloat16* src = u + (static_cast<int64_t>(b) * kH * R + i) * Np + g * 8;
@@ -404,8 +407,9 @@ __global__ void __launch_bounds__(256) trimul_ustats_kernel(const __nv_bfloat16*
 #pragma unroll
     for (int e = 0; e < 8; ++e) s1[e] = s2[e] = 0.f;
   }
-#pragma unroll 8
-  for (int c = 1; c < kH; ++c) {
+  const int c0 = half * (kH / 2);
+#pragma unroll 16
+  for (int c = c0; c < c0 + kH / 2; ++c) {
     const uint4 v = *reinterpret_cast<const uint4*>(src + c * plane);
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -417,6 +421,12 @@ __global__ void __launch_bounds__(256) trimul_ustats_kernel(const __nv_bfloat16*
       s2[2 * e + 1] = fmaf(d1, d1, s2[2 * e + 1]);
     }
   }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    s1[e] += __shfl_xor_sync(0xFFFFFFFFu, s1[e], 1);
+    s2[e] += __shfl_xor_sync(0xFFFFFFFFu, s2[e], 1);
+  }
+  if (!live || half) return;
   float2* dst = ustats + bi * N + g * 8;
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
@@ -718,7 +728,7 @@ int launch_out(const void* z, const uint8_t* mask, const void* packed, const voi
                cudaStream_t stream) {
   const int np = (N + 7) / 8 * 8;
   {
-    const int64_t threads = static_cast<int64_t>(B) * R * ((N + 7) / 8);
+    const int64_t threads = 2 * static_cast<int64_t>(B) * R * ((N + 7) / 8);
     trimul_ustats_kernel<<<static_cast<int>((threads + 255) / 256), 256, 0, stream>>>(
         static_cast<const __nv_bfloat16*>(u), ustats, B, R, N, np);
     int st = cuda_status(static_cast<int>(cudaGetLastError()), "trimul_ustats launch");
