@@ -11,9 +11,10 @@
 //
 // Three launches:
 //  1. triattn_proj: 128-pair tiles of raw z (row tiles for the starting node, column
-//     tiles for the ending node, so the Q / K / V^T writes are coalesced) x the resident
-//     packed [W_q; W_k; W_v; W_b] with the input LayerNorm folded into the epilogue. W_q
-//     carries log2(e)/sqrt(32) and W_b log2(e), so the softmax works in base 2. Writes
+//     tiles for the ending node, so the Q / K / V^T writes are contiguous) x the resident
+//     packed [W_q; W_k; W_v; W_b] with the input LayerNorm folded into the epilogue; V is
+//     computed transposed (W_v z^T) and leaves through TMA stores. W_q carries
+//     log2(e)/sqrt(32) and W_b log2(e), so the softmax works in base 2. Writes
 //     Q, K [B, N(r), H, N(n), 32], V^T [B, N(r), H, 32, Np(n)] and the bias
 //     [B, H, N, Np] in the natural pair layout, which both nodes read as [query][key] rows
 //     (the ending node's column tiles write it with a stride).
@@ -59,22 +60,43 @@ __device__ __forceinline__ void tile_stats(const uint8_t* tile, int row, float& 
 }
 
 // ====================================================================== 1. projection
+// Warp-specialised, persistent, 128-pair tiles. Per tile three products on the resident
+// weights, all reading the same z tile from shared memory:
+//   X[pair][256]   = z . [W_q; W_k]^T     (TMEM lane = pair)     Q, K
+//   X[pair][16]    = z . W_b^T            (lane = pair)          pair bias (4 heads used)
+//   Y[channel][128] = W_v . z^T           (lane = V channel)     V^T, computed transposed
+// so every thread's output run is contiguous: a pair's 32 channels of Q / K per head, a
+// channel's 128 pairs of V^T (staged 128-byte-swizzled, written by TMA stores).
+//   warp 0      TMA: the weights once, z tiles into a 2-stage ring
+//   warp 1      MMA: X (QK + bias, 272 columns) and Y (V^T, 128 columns), one buffer each
+//   warps 2-5   thread = pair: LayerNorm statistics (-> shared memory for warps 6-9), then
+//               Q, K and bias from X with the LayerNorm folded in
+//   warps 6-9   thread = V channel: V^T from Y with the pair statistics folded in
+constexpr int kProjThreads = 320;
+constexpr int kProjStages = 2;
+constexpr uint32_t kColX = 0;    // QK 0..255, bias 256..271
+constexpr uint32_t kColY = 384;  // V^T 384..511
+
 struct ProjSmem {
   alignas(1024) uint8_t w[kProjBytes];
-  alignas(1024) uint8_t z[kGroups][kTile * kC * 2];
+  alignas(1024) uint8_t z[kProjStages][kTile * kC * 2];
+  alignas(1024) uint8_t vt[2][kC * 64 * 2];  // V^T staging: [128 channels][pairs 0..63 | 64..127], SW128
   float wsum[kProjRows];
   float bias[kProjRows];
+  float2 stats[2][kTile];  // (mean, rstd) per pair, by tile parity
   uint64_t wbar;
-  uint64_t full[kGroups];
-  uint64_t mma[kGroups];
+  uint64_t z_full[kProjStages], z_empty[kProjStages];
+  uint64_t x_full, x_free, y_full, y_free;
+  uint64_t st_full[2], st_free[2];
   uint32_t tmem_base;
 };
+
+static_assert(sizeof(ProjSmem) + 1024 <= 232448, "projection shared memory exceeds the per-CTA limit");
 
 struct ProjParams {
   const uint8_t* packed;
   __nv_bfloat16* q;     // [B, N, H, N, 32]
   __nv_bfloat16* k;     // [B, N, H, N, 32]
-  __nv_bfloat16* vt;    // [B, N, H, 32, Np]
   __nv_bfloat16* bias;  // natural pair layout, element strides below
   int B, N, Np;
   int R, row0;          // problem rows held (N unless row-sharded) and the first one's global index
@@ -83,23 +105,38 @@ struct ProjParams {
   int* err;
 };
 
-__global__ void __launch_bounds__(256, 1)
-    triattn_proj_kernel(const __grid_constant__ CUtensorMap map_z, ProjParams p) {
+__global__ void __launch_bounds__(kProjThreads, 1)
+    triattn_proj_kernel(const __grid_constant__ CUtensorMap map_z, const __grid_constant__ CUtensorMap map_vt,
+                        ProjParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   ProjSmem& s = *reinterpret_cast<ProjSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int g = threadIdx.x / 128;
-  const int gt = threadIdx.x % 128;
   const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
   const int tiles_per_row = (p.N + kTile - 1) / kTile;
   const int total = p.B * p.R * tiles_per_row;
 
   if (threadIdx.x == 0) {
     mbar_init(&s.wbar, 1);
-    for (int i = 0; i < kGroups; ++i) {
-      mbar_init(&s.full[i], 1);
-      mbar_init(&s.mma[i], 1);
+    for (int i = 0; i < kProjStages; ++i) {
+      mbar_init(&s.z_full[i], 1);
+      mbar_init(&s.z_empty[i], 1 + 4);  // MMA commit + the four statistics warps
+    }
+    mbar_init(&s.x_full, 1);
+    mbar_init(&s.x_free, 4);
+    mbar_init(&s.y_full, 1);
+    mbar_init(&s.y_free, 4);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.st_full[i], 4);
+      mbar_init(&s.st_free[i], 4);
     }
     fence_mbar_init();
+  }
+  {
+    const float* v = reinterpret_cast<const float*>(p.packed + kProjBytes + kGateBytes + kOutBytes);
+    for (int i = threadIdx.x; i < kProjRows; i += kProjThreads) {
+      s.wsum[i] = v[i];
+      s.bias[i] = v[kProjRows + i];
+    }
   }
   if (warp == 0) {
     tmem_alloc(&s.tmem_base, 512);
@@ -108,136 +145,199 @@ __global__ void __launch_bounds__(256, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (threadIdx.x == 0) {
-    tma_prefetch_map(&map_z);
-    mbar_arrive_expect_tx(&s.wbar, kProjBytes);
-    for (int off = 0; off < static_cast<int>(kProjBytes); off += 25600)
-      bulk_load(s.w + off, p.packed + off, 25600, &s.wbar);
-  }
-  {
-    const float* v = reinterpret_cast<const float*>(p.packed + kProjBytes + kGateBytes + kOutBytes);
-    for (int i = threadIdx.x; i < kProjRows; i += 256) {
-      s.wsum[i] = v[i];
-      s.bias[i] = v[kProjRows + i];
-    }
-  }
-  __syncthreads();
-  bool ok = mbar_wait(&s.wbar, 0, p.err, kErrTimeoutLoad);
-  const uint32_t tmem = s.tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16) + g * 256;
-  const uint32_t tmem_mma = s.tmem_base + g * 256;
-  uint8_t* zt = s.z[g];
-  int it = 0;
-  bool load_pending = false;
-  for (int tile = blockIdx.x * kGroups + g; tile < total; tile += gridDim.x * kGroups, ++it) {
-    const int c0 = (tile % tiles_per_row) * kTile;
-    const int rr = tile / tiles_per_row;
-    const int b = rr / p.R;
-    const int r = rr - b * p.R;  // problem row (of the rows held)
-    if (gt == 0 && ok) {
-      mbar_arrive_expect_tx(&s.full[g], kTile * kC * 2);
-      for (int kb = 0; kb < 2; ++kb) {
-        if (p.starting)
-          tma_load_3d(zt + kb * 16384, &map_z, &s.full[g], kb * 64, c0, rr);          // z[b, r, c0 + t]
-        else
-          tma_load_3d(zt + kb * 16384, &map_z, &s.full[g], kb * 64, r, b * p.N + c0);  // z[b, c0 + t, r]
+  const uint32_t tmem0 = s.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_map(&map_z);
+      tma_prefetch_map(&map_vt);
+      mbar_arrive_expect_tx(&s.wbar, kProjBytes);
+      for (int off = 0; off < static_cast<int>(kProjBytes); off += 25600)
+        bulk_load(s.w + off, p.packed + off, 25600, &s.wbar);
+      int it = 0;
+      for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
+        const int st = it % kProjStages;
+        if (!mbar_wait(&s.z_empty[st], ((it / kProjStages) & 1) ^ 1, p.err, kErrTimeoutEmpty)) break;
+        const int c0 = (tile % tiles_per_row) * kTile;
+        const int rr = tile / tiles_per_row;
+        const int b = rr / p.R, r = rr - b * p.R;
+        mbar_arrive_expect_tx(&s.z_full[st], kTile * kC * 2);
+        for (int kb = 0; kb < 2; ++kb) {
+          uint8_t* dst = s.z[st] + kb * (kTile * 128);
+          if (p.starting)
+            tma_load_3d(dst, &map_z, &s.z_full[st], kb * 64, c0, rr);          // z[b, r, c0 + t]
+          else
+            tma_load_3d(dst, &map_z, &s.z_full[st], kb * 64, r, b * p.N + c0);  // z[b, c0 + t, r]
+        }
       }
-      load_pending = true;
+      // every issued load has landed before the CTA can exit
+      mbar_wait(&s.wbar, 0, p.err, kErrTimeoutLoad);
+      if (it > 0) mbar_wait(&s.z_full[(it - 1) % kProjStages], ((it - 1) / kProjStages) & 1, p.err, kErrTimeoutLoad);
     }
-    ok = ok && mbar_wait(&s.full[g], it & 1, p.err, kErrTimeoutLoad);
-    if (gt == 0 && ok) load_pending = false;
-    float mean = 0.f, rstd = 0.f;
-    if (ok) tile_stats(zt, gt, mean, rstd);
-    const int n = c0 + gt;
-    const bool valid = n < p.N;
-    for (int half = 0; half < 2; ++half) {
-      const int ncols = half == 0 ? 256 : 144;
-      if (gt == 0 && ok) {
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc_qk = idesc_bf16_f32(128, 256);
+      const uint32_t idesc_b = idesc_bf16_f32(128, 16);
+      const uint32_t idesc_v = idesc_bf16_f32(128, kTile);
+      const uint32_t wa = smem_u32(s.w);
+      constexpr uint32_t kWBlock = kProjRows * 128;  // one 64-channel K block of the weights
+      bool ok = mbar_wait(&s.wbar, 0, p.err, kErrTimeoutLoad);
+      int it = 0;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
+        const int st = it % kProjStages;
+        const uint32_t za = smem_u32(s.z[st]);
+        if (!mbar_wait(&s.z_full[st], (it / kProjStages) & 1, p.err, kErrTimeoutLoad)) break;
+        if (!mbar_wait(&s.x_free, (it & 1) ^ 1, p.err, kErrTimeoutEmpty)) break;
         tc_fence_after();
-        const uint32_t idesc = idesc_bf16_f32(128, ncols);
-        const uint32_t a0 = smem_u32(zt);
-        const uint32_t b0 = smem_u32(s.w) + half * 256 * 128;
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t dz = desc_kmajor_sw128(za + kb * (kTile * 128)) + 2 * kk;
+            mma_bf16(tmem0 + kColX, dz, desc_kmajor_sw128(wa + kb * kWBlock) + 2 * kk, idesc_qk, (kb | kk) != 0);
+            mma_bf16(tmem0 + kColX + 256, dz, desc_kmajor_sw128(wa + kb * kWBlock + 384 * 128) + 2 * kk, idesc_b,
+                     (kb | kk) != 0);
+          }
+        mma_commit(&s.x_full);
+        if (!mbar_wait(&s.y_free, (it & 1) ^ 1, p.err, kErrTimeoutEmpty)) break;
+        tc_fence_after();
 #pragma unroll
         for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_bf16(tmem_mma, desc_kmajor_sw128(a0 + kb * 16384) + 2 * kk,
-                     desc_kmajor_sw128(b0 + kb * (kProjRows * 128)) + 2 * kk, idesc, (kb | kk) != 0);
-        mma_commit(&s.mma[g]);
+            mma_bf16(tmem0 + kColY, desc_kmajor_sw128(wa + kb * kWBlock + 256 * 128) + 2 * kk,
+                     desc_kmajor_sw128(za + kb * (kTile * 128)) + 2 * kk, idesc_v, (kb | kk) != 0);
+        mma_commit(&s.y_full);
+        mma_commit(&s.z_empty[st]);
       }
-      bool got = ok && mbar_wait(&s.mma[g], half, p.err, kErrTimeoutMma);
-      got = __all_sync(0xFFFFFFFFu, got);
+    }
+  } else if (warp < 6) {
+    // thread = pair t of the tile (TMEM lanes of warp w are 32 (w % 4) ...)
+    const int t = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
+      const int st = it % kProjStages, sb = it & 1;
+      bool w1 = mbar_wait(&s.z_full[st], (it / kProjStages) & 1, p.err, kErrTimeoutLoad);
+      bool w2 = mbar_wait(&s.st_free[sb], ((it >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty);
+      if (!__all_sync(0xFFFFFFFFu, w1 && w2)) break;
+      float mean, rstd;
+      tile_stats(s.z[st], t, mean, rstd);
+      s.stats[sb][t] = make_float2(mean, rstd);
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&s.st_full[sb]);
+        mbar_arrive(&s.z_empty[st]);
+      }
+      const int c0 = (tile % tiles_per_row) * kTile;
+      const int rr = tile / tiles_per_row;
+      const int b = rr / p.R, r = rr - b * p.R;
+      const int n = c0 + t;
+      const bool valid = n < p.N;
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&s.x_full, it & 1, p.err, kErrTimeoutMma))) break;
       tc_fence_after();
-      if (got) {
-        const int64_t row_base = (static_cast<int64_t>(b) * p.R + r) * kHeads;  // (b, r) -> head 0
-        if (half == 0) {
-          // Q (cols 0..127) and K (cols 128..255): one head = 32 columns = 64 contiguous bytes
+      const int64_t row_base = (static_cast<int64_t>(b) * p.R + r) * kHeads;  // (b, r) -> head 0
+      // Q (columns 0..127) and K (128..255): one head = 32 columns = 64 contiguous bytes
 #pragma unroll 1
-          for (int cc = 0; cc < 256; cc += 32) {
-            uint32_t v[32];
-            tmem_ld32(tmem + cc, v);
-            tmem_ld_wait();
-            if (valid) {
-              uint32_t w[16];
+      for (int cc = 0; cc < 256; cc += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem0 + lane_off + kColX + cc, v);
+        tmem_ld_wait();
+        if (valid) {
+          uint32_t w[16];
 #pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                const int c = cc + 2 * i;
-                const float a = rstd * (__uint_as_float(v[2 * i]) - mean * s.wsum[c]) + s.bias[c];
-                const float bb = rstd * (__uint_as_float(v[2 * i + 1]) - mean * s.wsum[c + 1]) + s.bias[c + 1];
-                w[i] = pack_bf16(a, bb);
-              }
-              const int head = (cc % 128) / 32;
-              __nv_bfloat16* base = (cc < 128 ? p.q : p.k) + ((row_base + head) * p.N + n) * kD;
-              uint4* dst = reinterpret_cast<uint4*>(base);
-#pragma unroll
-              for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
-            }
+          for (int i = 0; i < 16; ++i) {
+            const int c = cc + 2 * i;
+            const float a = rstd * (__uint_as_float(v[2 * i]) - mean * s.wsum[c]) + s.bias[c];
+            const float bb = rstd * (__uint_as_float(v[2 * i + 1]) - mean * s.wsum[c + 1]) + s.bias[c + 1];
+            w[i] = pack_bf16(a, bb);
           }
-        } else {
-          // V (cols 0..127) -> V^T[b, r, head, d, n]; bias (cols 128..131) -> [b, head, r, n]
-#pragma unroll 1
-          for (int cc = 0; cc < 128; cc += 32) {
-            uint32_t v[32];
-            tmem_ld32(tmem + cc, v);
-            tmem_ld_wait();
-            if (valid) {
-              const int head = cc / 32;
-              __nv_bfloat16* base = p.vt + (row_base + head) * kD * p.Np + n;
+          const int head = (cc % 128) / 32;
+          uint4* dst = reinterpret_cast<uint4*>((cc < 128 ? p.q : p.k) + ((row_base + head) * p.N + n) * kD);
 #pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                const int c = 256 + cc + i;
-                base[static_cast<int64_t>(i) * p.Np] =
-                    __float2bfloat16_rn(rstd * (__uint_as_float(v[i]) - mean * s.wsum[c]) + s.bias[c]);
-              }
-            }
-          }
-          uint32_t v[16];
-          tmem_ld16(tmem + 128, v);
-          tmem_ld_wait();
-          if (valid) {
+          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        }
+      }
+      {
+        uint32_t v[16];
+        tmem_ld16(tmem0 + lane_off + kColX + 256, v);
+        tmem_ld_wait();
+        if (valid) {
 #pragma unroll
-            for (int h = 0; h < kHeads; ++h) {
-              const int c = 384 + h;
-              // natural pair layout [b, h, i, j] for both nodes (starting: i = r, j = n;
-              // ending: i = n, j = r), so the attention reads rows of queries x keys
-              const int64_t bi = p.starting ? r : n, bj = p.starting ? n : r;
-              p.bias[b * p.bias_b + h * p.bias_h + bi * p.bias_r + bj] =
-                  __float2bfloat16_rn(rstd * (__uint_as_float(v[h]) - mean * s.wsum[c]) + s.bias[c]);
-            }
+          for (int h = 0; h < kHeads; ++h) {
+            const int c = 384 + h;
+            // natural pair layout [b, h, i, j] for both nodes (starting: i = r, j = n;
+            // ending: i = n, j = r), so the attention reads rows of queries x keys
+            const int64_t bi = p.starting ? r : n, bj = p.starting ? n : r;
+            p.bias[b * p.bias_b + h * p.bias_h + bi * p.bias_r + bj] =
+                __float2bfloat16_rn(rstd * (__uint_as_float(v[h]) - mean * s.wsum[c]) + s.bias[c]);
           }
         }
       }
       tc_fence_before();
-      ok = !named_barrier_or(1 + g, 128, !ok || !got);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.x_free);
     }
-    if (!ok) break;
+  } else {
+    // thread = V channel c (head c / 32, d = c % 32); TMEM columns = the tile's pairs
+    const int c = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const float wsv = s.wsum[256 + c], bsv = s.bias[256 + c];
+    const bool issuer = warp == 6 && lane == 0;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
+      const int sb = it & 1;
+      bool w1 = mbar_wait(&s.y_full, it & 1, p.err, kErrTimeoutMma);
+      bool w2 = mbar_wait(&s.st_full[sb], (it >> 1) & 1, p.err, kErrTimeoutLoad);
+      // the previous tile's stores have finished reading the staging tiles; the four warps
+      // leave together on a failed wait
+      if (issuer) tma_store_wait_read0();
+      if (named_barrier_or(1, 128, !(w1 && w2))) break;
+      tc_fence_after();
+      const int c0 = (tile % tiles_per_row) * kTile;
+      const int rr = tile / tiles_per_row;
+#pragma unroll 1
+      for (int ch = 0; ch < kTile; ch += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem0 + lane_off + kColY + ch, v);
+        tmem_ld_wait();
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 s0 = s.stats[sb][ch + 2 * i], s1 = s.stats[sb][ch + 2 * i + 1];
+          const float a = s0.y * (__uint_as_float(v[2 * i]) - s0.x * wsv) + bsv;
+          const float bb = s1.y * (__uint_as_float(v[2 * i + 1]) - s1.x * wsv) + bsv;
+          packed[i] = pack_bf16(a, bb);
+        }
+        uint8_t* stage = s.vt[ch / 64];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<uint4*>(stage + sw128_offset(c, (ch % 64) + 8 * q)) =
+              make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&s.y_free);
+        mbar_arrive(&s.st_free[sb]);
+      }
+      fence_async_smem();
+      named_barrier(1, 128);
+      if (issuer) {
+        // V^T rows (b, r, head, d) = rr * 128 + c; pairs past N are clipped by the map
+        tma_store_2d(&map_vt, s.vt[0], c0, rr * kC);
+        if (c0 + 64 < p.N) tma_store_2d(&map_vt, s.vt[1], c0 + 64, rr * kC);
+        tma_store_commit();
+      }
+    }
+    if (issuer) tma_store_wait_all0();
   }
-  if (gt == 0 && load_pending) mbar_wait(&s.full[g], it & 1, p.err, kErrTimeoutLoad);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(s.tmem_base, 512);
+    tmem_dealloc(tmem0, 512);
   }
 }
 
@@ -949,17 +1049,24 @@ int launch_proj(const void* z, const void* packed, __nv_bfloat16* q, __nv_bfloat
                 __nv_bfloat16* bias, int64_t bias_b, int64_t bias_h, int64_t bias_r, int B, int R, int N,
                 int starting, const DeviceInfo& info, cudaStream_t stream) {
   const int np = (N + 7) / 8 * 8;
-  CUtensorMap map_z;
+  CUtensorMap map_z, map_vt;
   int st = pair_map(&map_z, z, B, R, N, kTile, !starting);
   if (st) return st;
-  ProjParams pp{static_cast<const uint8_t*>(packed), q, k, vt, bias, B, N, np, R, 0, bias_b, bias_h, bias_r,
+  {
+    // V^T as rows (b, r, head, d) of N pairs (row stride Np), stored in [128 x 64] boxes
+    const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(B) * R * kC};
+    const uint64_t strides[1] = {static_cast<uint64_t>(np) * 2};
+    const uint32_t box[2] = {64, kC};
+    st = make_map(&map_vt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, vt, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+  }
+  ProjParams pp{static_cast<const uint8_t*>(packed), q, k, bias, B, N, np, R, 0, bias_b, bias_h, bias_r,
                 starting, info.err};
   const int tiles = B * R * ((N + kTile - 1) / kTile);
-  const int groups = (tiles + kGroups - 1) / kGroups;
-  const int grid = groups < info.num_sms ? groups : info.num_sms;
+  const int grid = tiles < info.num_sms ? tiles : info.num_sms;
   const size_t smem = sizeof(ProjSmem) + 1024;
   cudaFuncSetAttribute(triattn_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  triattn_proj_kernel<<<grid, 256, smem, stream>>>(map_z, pp);
+  triattn_proj_kernel<<<grid, kProjThreads, smem, stream>>>(map_z, map_vt, pp);
   return cuda_status(static_cast<int>(cudaGetLastError()), "triattn_proj launch");
 }
 

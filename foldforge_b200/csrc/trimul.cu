@@ -86,20 +86,22 @@ __device__ __forceinline__ void load_z_stats(const uint8_t* tile, int row, float
 // ====================================================================== kernel 1
 // Warp-specialised, persistent, 64-pair tiles. The projection is computed TRANSPOSED,
 // D[channel][pair] = W'[channel][:] . z[pair][:], so a TMEM lane is an output channel and
-// its columns are consecutive pairs: each epilogue thread owns one channel of L (or R) and
-// writes 32 consecutive pairs of the channel-major layout as four 16-byte stores.
-//   warp 0      TMA: z tiles into a 4-stage ring
+// its columns are consecutive pairs: each epilogue thread owns one channel of L (or R),
+// writes its 64 pairs into a 128-byte-swizzled [channel][pair] staging tile, and one thread
+// per part stores the tile with a TMA store (pairs past N are clipped by the tensor map).
+//   warp 0      TMA: z tiles into a 3-stage ring
 //   warp 1      MMA: 4 x (M 128 channels, N 64 pairs, K 128) per tile -> 256 TMEM columns,
 //               double-buffered (512 columns)
 //   warps 2-3   LayerNorm statistics and pair mask of the tile's 64 pairs -> shared memory
 //   warps 4-11  epilogue: warps 4-7 produce L, warps 8-11 produce R
 constexpr int kPTile = 64;
-constexpr int kPStages = 4;
+constexpr int kPStages = 3;
 constexpr int kPThreads = 384;
 
 struct ProjSmem {
   alignas(1024) uint8_t w[kProjBytes];
   alignas(1024) uint8_t z[kPStages][kPTile * kC * 2];
+  alignas(1024) uint8_t out[2][kH * kPTile * 2];  // L / R staging: [128 channels][64 pairs], SW128
   float wsum[512];
   float bias[512];
   float mean[2][kPTile];
@@ -125,8 +127,11 @@ struct ProjParams {
   int* err;
 };
 
+static_assert(sizeof(ProjSmem) + 1024 <= 232448, "projection shared memory exceeds the per-CTA limit");
+
 __global__ void __launch_bounds__(kPThreads, 1)
-    trimul_proj_kernel(const __grid_constant__ CUtensorMap map_z, ProjParams p) {
+    trimul_proj_kernel(const __grid_constant__ CUtensorMap map_z, const __grid_constant__ CUtensorMap map_l,
+                       const __grid_constant__ CUtensorMap map_r, ProjParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   ProjSmem& s = *reinterpret_cast<ProjSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x / 32;
@@ -167,6 +172,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       tma_prefetch_map(&map_z);
+      tma_prefetch_map(&map_l);
+      tma_prefetch_map(&map_r);
       mbar_arrive_expect_tx(&s.wbar, kProjBytes);
       for (int off = 0; off < static_cast<int>(kProjBytes); off += 32768)
         bulk_load(s.w + off, p.packed + off, 32768, &s.wbar);
@@ -272,18 +279,22 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const int rp = part * 256 + c, rg = part * 256 + 128 + c;
     const float wsp = s.wsum[rp], bsp = s.bias[rp], wsg = s.wsum[rg], bsg = s.bias[rg];
-    __nv_bfloat16* out = part == 0 ? p.left : p.right;
+    const CUtensorMap* map_out = part == 0 ? &map_l : &map_r;
+    const bool issuer = (warp & 3) == 0 && lane == 0;
+    uint8_t* stage = s.out[part];
     int it = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
       const int buf = it & 1;
       bool w1 = mbar_wait(&s.acc_full[buf], (it >> 1) & 1, p.err, kErrTimeoutMma);
       bool w2 = mbar_wait(&s.st_full[buf], (it >> 1) & 1, p.err, kErrTimeoutLoad);
-      if (!__all_sync(0xFFFFFFFFu, w1 && w2)) break;
+      // the previous tile's store has finished reading the staging tile before it is
+      // rewritten; the part's four warps leave together on a failed wait
+      if (issuer) tma_store_wait_read0();
+      if (named_barrier_or(1 + part, 128, !(w1 && w2))) break;
       tc_fence_after();
       const int c0 = (tile % tiles_per_row) * kPTile;
       const int rr = tile / tiles_per_row;
       const int b = rr / p.R, r = rr - b * p.R;
-      __nv_bfloat16* row = out + b * p.ls_b + c * p.ls_c + r * p.ls_r + c0;
 #pragma unroll 1
       for (int ch = 0; ch < kPTile; ch += 32) {
         uint32_t vp[32], vg[32];
@@ -304,19 +315,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
           }
           packed[i] = pack_bf16(o2[0], o2[1]);
         }
-        const int k0 = c0 + ch;
-        if (k0 + 32 <= p.N) {
-          uint4* dst = reinterpret_cast<uint4*>(row + ch);
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-        } else {
-          for (int i = 0; i < 32 && k0 + i < p.N; ++i) {
-            const uint32_t w = packed[i / 2];
-            const uint16_t h = static_cast<uint16_t>((i & 1) ? (w >> 16) : (w & 0xFFFFu));
-            reinterpret_cast<uint16_t*>(row + ch)[i] = h;
-          }
-        }
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<uint4*>(stage + sw128_offset(c, ch + 8 * q)) =
+              make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
       }
       tc_fence_before();
       __syncwarp();
@@ -324,7 +326,14 @@ __global__ void __launch_bounds__(kPThreads, 1)
         mbar_arrive(&s.acc_free[buf]);
         mbar_arrive(&s.st_free[buf]);
       }
+      fence_async_smem();
+      named_barrier(1 + part, 128);
+      if (issuer) {
+        tma_store_4d(map_out, stage, c0, 0, r, b);  // [pairs c0..c0+63][channels][row r][batch b]
+        tma_store_commit();
+      }
     }
+    if (issuer) tma_store_wait_all0();
   }
   tc_fence_before();
   __syncthreads();
@@ -676,16 +685,27 @@ int launch_proj(const void* z, const uint8_t* mask, const void* packed, void* le
                 int B, int R, int N, int row0, int64_t ls_b, int64_t ls_c, int64_t ls_r, int outgoing,
                 const DeviceInfo& info, cudaStream_t stream) {
   const int np = (N + 7) / 8 * 8;
-  CUtensorMap map_z;
+  CUtensorMap map_z, map_l, map_r;
   int st = z_map(&map_z, z, B, R, N, kPTile, !outgoing);
   if (st) return st;
+  {
+    // L / R as [pair k (N, clipped)][channel][row][batch] with the caller's strides
+    const uint64_t dims[4] = {static_cast<uint64_t>(N), kH, static_cast<uint64_t>(R), static_cast<uint64_t>(B)};
+    const uint64_t strides[3] = {static_cast<uint64_t>(ls_c) * 2, static_cast<uint64_t>(ls_r) * 2,
+                                 static_cast<uint64_t>(ls_b) * 2};
+    const uint32_t box[4] = {kPTile, kH, 1, 1};
+    st = make_map(&map_l, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, left, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = make_map(&map_r, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, right, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+  }
   ProjParams pp{static_cast<const uint8_t*>(packed), mask, static_cast<__nv_bfloat16*>(left),
                 static_cast<__nv_bfloat16*>(right), zstats, B, N, np, R, row0, ls_b, ls_c, ls_r, outgoing, info.err};
   const int ptiles = B * R * ((N + kPTile - 1) / kPTile);
   const int pgrid = ptiles < info.num_sms ? ptiles : info.num_sms;
   const size_t proj_smem = sizeof(ProjSmem) + 1024;
   cudaFuncSetAttribute(trimul_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(proj_smem));
-  trimul_proj_kernel<<<pgrid, kPThreads, proj_smem, stream>>>(map_z, pp);
+  trimul_proj_kernel<<<pgrid, kPThreads, proj_smem, stream>>>(map_z, map_l, map_r, pp);
   return cuda_status(static_cast<int>(cudaGetLastError()), "trimul_proj launch");
 }
 
