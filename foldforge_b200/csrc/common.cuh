@@ -340,6 +340,12 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32_bmn(int m, int n) {
          | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
+// Instruction descriptor: bf16 A (MN-major) x bf16 B (K-major) -> fp32, shape M x N.
+__host__ __device__ constexpr uint32_t idesc_bf16_f32_amn(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15)  // A is MN-major
+         | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
 // Instruction descriptor: bf16 x bf16 -> fp32, both operands K-major, shape M x N.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
   return (1u << 4)                                  // D format: f32

@@ -719,34 +719,38 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 }
 
 // ====================================================================== 3. output
-// Warp-specialised, persistent, 64-pair tiles (natural pair layout for both nodes), computed
-// TRANSPOSED (TMEM lane = channel, column = pair):
-//   gate[c][p] = W_g'[c] . z[p]                        (folded input LayerNorm)
-//   G[c][p]    = sigmoid(gate[c][p]) * o[p][c]         written by the epilogue warps as an
-//                                                      MN-major operand ([c] rows of pairs)
-//   delta[c][p] = W_o[c] . G[:, p];   z'[p][c] = z[p][c] + delta[c][p]  (in place, TMA store)
+// Warp-specialised, persistent, 128-pair tiles (natural pair layout for both nodes); TMEM
+// lane = pair, column = channel:
+//   gate[p][c]  = z[p] . W_g'[c]                       (folded input LayerNorm)
+//   G[p][c]     = sigmoid(gate[p][c]) * o[p][c]        written over the o tile in place: it
+//                                                      is the K-major A operand of
+//   delta[p][c] = G[p] . W_o[c];   z'[p][c] = z[p][c] + delta[p][c]  (in place, TMA store)
+// A thread owns one pair: its o and z rows are read and written as 16-byte swizzled
+// vectors, its LayerNorm coefficients stay in registers, and the paired fp32 pipe handles
+// two channels per instruction.
 //   warp 0      TMA: z and o tiles, 2-stage ring
 //   warp 1      MMA: gate product (tile t + 1) ahead of the output product (tile t)
 //   warps 2-3   per-pair LayerNorm statistics of z and the keep mask
-//   warps 4-11  lane = channel; warps 4-7 pairs 0-31, warps 8-11 pairs 32-63
-constexpr int kOTile = 64;
+//   warps 4-11  lane = pair; warps 4-7 channels 0-63, warps 8-11 channels 64-127
+constexpr int kOTile = 128;
 constexpr int kOStages = 2;
 constexpr int kOThreads = 384;
 
 struct OutSmem {
-  alignas(1024) uint8_t wg[kGateBytes];
+  alignas(1024) uint8_t wg[kGateBytes];                // [c][k]: 2 K-blocks of [128 c x 128 B]
   alignas(1024) uint8_t wo[kOutBytes];
-  alignas(1024) uint8_t z[kOStages][kOTile * kC * 2];  // [p][c]: 2 K-blocks of [64 p x 128 B]
-  alignas(1024) uint8_t o[kOStages][kOTile * kC * 2];  // [p][c], same layout
-  alignas(1024) uint8_t gt[kC * kOTile * 2];           // G: [c][p], 128 rows x 128 B (MN-major)
-  float wsum_gate[128], bias_gate[128];
-  float zm[2][kOTile], zr[2][kOTile], keep[2][kOTile];
+  alignas(1024) uint8_t z[kOStages][kOTile * kC * 2];  // [p][c]: 2 K-blocks of [128 p x 128 B]
+  alignas(1024) uint8_t o[kOStages][kOTile * kC * 2];  // [p][c], same layout; G replaces o
+  float4 cg[kC / 2];       // channel pair (2i, 2i+1): wsum_gate x2, bias_gate / 2 x2
+  float2 pc[2][kOTile];    // per pair: rstd / 2, -rstd mean / 2
+  float keep[2][kOTile];
   uint64_t wbar;
   uint64_t full[kOStages], empty[kOStages];
-  uint64_t g_full[2], d_full[2], acc_free[2], st_full[2], st_free[2];
-  uint64_t gt_ready;
+  uint64_t g_full[2], gt_ready[2], d_full[2], acc_free[2], st_full[2], st_free[2];
   uint32_t tmem_base;
 };
+
+static_assert(sizeof(OutSmem) + 1024 <= 232448, "output shared memory exceeds the per-CTA limit");
 
 struct OutParams {
   const uint8_t* packed;
@@ -771,27 +775,25 @@ __global__ void __launch_bounds__(kOThreads, 1)
     mbar_init(&s.wbar, 1);
     for (int i = 0; i < kOStages; ++i) {
       mbar_init(&s.full[i], 1);
-      mbar_init(&s.empty[i], 1);
+      mbar_init(&s.empty[i], 2);  // the output MMA's commit (o / G read) + the store's read of z
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.g_full[i], 1);
+      mbar_init(&s.gt_ready[i], 8);
       mbar_init(&s.d_full[i], 1);
       mbar_init(&s.acc_free[i], 8);
       mbar_init(&s.st_full[i], 2);
       mbar_init(&s.st_free[i], 8);
     }
-    mbar_init(&s.gt_ready, 8);
     fence_mbar_init();
   }
   {
     const float* v = reinterpret_cast<const float*>(p.packed + kProjBytes + kGateBytes + kOutBytes) + 2 * kProjRows;
-    for (int i = threadIdx.x; i < 128; i += kOThreads) {
-      s.wsum_gate[i] = v[i];
-      s.bias_gate[i] = v[128 + i];
-    }
+    for (int i = threadIdx.x; i < kC / 2; i += kOThreads)
+      s.cg[i] = make_float4(v[2 * i], v[2 * i + 1], 0.5f * v[128 + 2 * i], 0.5f * v[128 + 2 * i + 1]);
   }
   if (warp == 0) {
-    tmem_alloc(&s.tmem_base, 256);
+    tmem_alloc(&s.tmem_base, 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -819,14 +821,15 @@ __global__ void __launch_bounds__(kOThreads, 1)
           tma_load_3d(s.o[st] + kb * (kOTile * 128), &map_o, &s.full[st], kb * 64, c0, rr);
         }
       }
+      // every issued load has landed before the CTA can exit
       mbar_wait(&s.wbar, 0, p.err, kErrTimeoutLoad);
+      if (it > 0) mbar_wait(&s.full[(it - 1) % kOStages], ((it - 1) / kOStages) & 1, p.err, kErrTimeoutLoad);
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc_g = idesc_bf16_f32(128, kOTile);
-      const uint32_t idesc_o = idesc_bf16_f32_bmn(128, kOTile);
+      const uint32_t idesc = idesc_bf16_f32(kOTile, kC);
       bool ok = mbar_wait(&s.wbar, 0, p.err, kErrTimeoutLoad);
-      const uint32_t wg = smem_u32(s.wg), wo = smem_u32(s.wo), ga = smem_u32(s.gt);
+      const uint32_t wg = smem_u32(s.wg), wo = smem_u32(s.wo);
       auto gate_mma = [&](int it) -> bool {
         const int st = it % kOStages, buf = it & 1;
         if (!mbar_wait(&s.full[st], (it / kOStages) & 1, p.err, kErrTimeoutLoad)) return false;
@@ -837,28 +840,31 @@ __global__ void __launch_bounds__(kOThreads, 1)
         for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_bf16(tmem0 + buf * 128, desc_kmajor_sw128(wg + kb * 16384) + 2 * kk,
-                     desc_kmajor_sw128(za + kb * (kOTile * 128)) + 2 * kk, idesc_g, (kb | kk) != 0);
+            mma_bf16(tmem0 + buf * 256, desc_kmajor_sw128(za + kb * (kOTile * 128)) + 2 * kk,
+                     desc_kmajor_sw128(wg + kb * 16384) + 2 * kk, idesc, (kb | kk) != 0);
         mma_commit(&s.g_full[buf]);
         return true;
       };
-      int it = 0;
       const int mine = (blockIdx.x < total) ? (total - 1 - blockIdx.x) / gridDim.x + 1 : 0;
       if (ok && mine > 0) ok = gate_mma(0);
-      for (it = 0; it < mine && ok; ++it) {
+      for (int it = 0; it < mine && ok; ++it) {
         if (it + 1 < mine && !gate_mma(it + 1)) break;
-        const int buf = it & 1;
-        if (!mbar_wait(&s.gt_ready, it & 1, p.err, kErrTimeoutMma)) break;
+        const int st = it % kOStages, buf = it & 1;
+        if (!mbar_wait(&s.gt_ready[buf], (it >> 1) & 1, p.err, kErrTimeoutMma)) break;
         tc_fence_after();
+        const uint32_t ga = smem_u32(s.o[st]);
 #pragma unroll
-        for (int ks = 0; ks < kC / 16; ++ks)
-          mma_bf16(tmem0 + buf * 128 + kOTile, desc_kmajor_sw128(wo + (ks / 4) * 16384) + 2 * (ks % 4),
-                   desc_mnmajor_sw128(ga + ks * 2048, 16384, 1024), idesc_o, ks != 0);
+        for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_bf16(tmem0 + buf * 256 + kC, desc_kmajor_sw128(ga + kb * (kOTile * 128)) + 2 * kk,
+                     desc_kmajor_sw128(wo + kb * 16384) + 2 * kk, idesc, (kb | kk) != 0);
         mma_commit(&s.d_full[buf]);
+        mma_commit(&s.empty[st]);
       }
     }
   } else if (warp < 4) {
-    // statistics: thread t = pair t of the tile
+    // statistics: thread t handles pairs t and t + 64 of the tile
     const int t = (warp - 2) * 32 + lane;
     int it = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
@@ -866,26 +872,27 @@ __global__ void __launch_bounds__(kOThreads, 1)
       const bool w1 = mbar_wait(&s.full[st], (it / kOStages) & 1, p.err, kErrTimeoutLoad);
       const bool w2 = mbar_wait(&s.st_free[buf], ((it >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty);
       if (!__all_sync(0xFFFFFFFFu, w1 && w2)) break;
-      float mean, rstd;
-      ln_stats_c128(s.z[st], kOTile * 128, t, mean, rstd);
       const int c0 = (tile % tiles_per_row) * kOTile;
       const int rr = tile / tiles_per_row;
       const int b = rr / p.R, r = rr - b * p.R;
-      const int j = c0 + t;
-      s.zm[buf][t] = mean;
-      s.zr[buf][t] = rstd;
-      s.keep[buf][t] =
-          (!p.masked_zero || (j < p.N && p.mask[b * p.N + p.row0 + r] && p.mask[b * p.N + j])) ? 1.f : 0.f;
+#pragma unroll 1
+      for (int k = 0; k < 2; ++k) {
+        const int pp = t + 64 * k;
+        float mean, rstd;
+        ln_stats_c128(s.z[st], kOTile * 128, pp, mean, rstd);
+        const int j = c0 + pp;
+        s.pc[buf][pp] = make_float2(0.5f * rstd, -0.5f * rstd * mean);
+        s.keep[buf][pp] =
+            (j < p.N && (!p.masked_zero || (p.mask[b * p.N + p.row0 + r] && p.mask[b * p.N + j]))) ? 1.f : 0.f;
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.st_full[buf]);
     }
   } else {
+    // lane = pair pp; half = which 64 channels
     const int half = (warp - 4) / 4;
-    const int c = (warp & 3) * 32 + lane;
+    const int pp = (warp & 3) * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const float wsg = s.wsum_gate[c], bg = s.bias_gate[c];
-    const int kb = c / 64, cc = c % 64;
-    const int p0 = half * 32;
     int it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
@@ -896,50 +903,74 @@ __global__ void __launch_bounds__(kOThreads, 1)
         ok = __all_sync(0xFFFFFFFFu, w1 && w2);
       }
       tc_fence_after();
-      const uint8_t* ot = s.o[st];
+      uint8_t* orow = s.o[st] + half * (kOTile * 128);
+      uint8_t* zrow = s.z[st] + half * (kOTile * 128);
+      const bool keep = s.keep[buf][pp] != 0.f;
       if (ok) {
-        // G[c][p] = sigmoid(gate) * o[p][c] for this warp's 32 pairs -> 4 x 16-byte chunks of row c
-        uint32_t vg[32];
-        tmem_ld32(tmem0 + lane_off + buf * 128 + p0, vg);
-        tmem_ld_wait();
-        uint32_t gw[16];
+        // G = o * sigmoid(g) = (o / 2) tanh(g / 2) + o / 2, g / 2 = (rstd/2) gate - (rstd mean/2) wsum + b/2
+        const float2 pc = s.pc[buf][pp];
+        const uint64_t ga = f32x2(pc.x, pc.x), gb = f32x2(pc.y, pc.y), h2 = f32x2(0.5f, 0.5f);
+#pragma unroll 1
+        for (int ch = 0; ch < 64; ch += 32) {
+          uint32_t vg[32];
+          tmem_ld32(tmem0 + lane_off + buf * 256 + half * 64 + ch, vg);
+          tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float gv[2];
+          for (int q = 0; q < 4; ++q) {
+            uint4* op = reinterpret_cast<uint4*>(orow + sw128_offset(pp, ch + 8 * q));
+            const uint4 ov = *op;
+            const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w};
+            uint32_t res[4];
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int pp = p0 + i + e;
-            const float g = s.zr[buf][pp] * (__uint_as_float(vg[i + e]) - s.zm[buf][pp] * wsg) + bg;
-            const float ov = __bfloat162float(
-                *reinterpret_cast<const __nv_bfloat16*>(ot + kb * (kOTile * 128) + sw128_offset(pp, cc)));
-            gv[e] = ov * sigmoid_fast(g);
+            for (int e = 0; e < 4; ++e) {
+              const int i = 8 * q + 2 * e;
+              const float4 cg = s.cg[(half * 64 + ch + i) / 2];
+              const uint64_t g = fma_f32x2(ga, f32x2(__uint_as_float(vg[i]), __uint_as_float(vg[i + 1])),
+                                           fma_f32x2(gb, f32x2(cg.x, cg.y), f32x2(cg.z, cg.w)));
+              float g0, g1;
+              f32x2_split(g, g0, g1);
+              const uint64_t o2 = mul_f32x2(f32x2(bf16_lo(ow[e]), bf16_hi(ow[e])), h2);
+              const uint64_t gv = fma_f32x2(o2, f32x2(tanh_fast(g0), tanh_fast(g1)), o2);
+              float r0, r1;
+              f32x2_split(gv, r0, r1);
+              res[e] = pack_bf16(r0, r1);
+            }
+            *op = make_uint4(res[0], res[1], res[2], res[3]);
           }
-          gw[i / 2] = pack_bf16(gv[0], gv[1]);
         }
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          *reinterpret_cast<uint4*>(s.gt + sw128_offset(c, p0 + q * 8)) =
-              make_uint4(gw[4 * q], gw[4 * q + 1], gw[4 * q + 2], gw[4 * q + 3]);
       }
       fence_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s.gt_ready);
+      if (lane == 0) mbar_arrive(&s.gt_ready[buf]);
       if (ok) {
         const bool w3 = mbar_wait(&s.d_full[buf], (it >> 1) & 1, p.err, kErrTimeoutMma);
         ok = __all_sync(0xFFFFFFFFu, w3);
       }
       tc_fence_after();
-      uint8_t* zt = s.z[st];
       if (ok) {
-        uint32_t vd[32];
-        tmem_ld32(tmem0 + lane_off + buf * 128 + kOTile + p0, vd);
-        tmem_ld_wait();
+#pragma unroll 1
+        for (int ch = 0; ch < 64; ch += 32) {
+          uint32_t vd[32];
+          tmem_ld32(tmem0 + lane_off + buf * 256 + kC + half * 64 + ch, vd);
+          tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int pp = p0 + i;
-          __nv_bfloat16* addr = reinterpret_cast<__nv_bfloat16*>(zt + kb * (kOTile * 128) + sw128_offset(pp, cc));
-          *addr = __float2bfloat16_rn(__bfloat162float(*addr) + __uint_as_float(vd[i]) * s.keep[buf][pp]);
+          for (int q = 0; q < 4; ++q) {
+            uint4* zp = reinterpret_cast<uint4*>(zrow + sw128_offset(pp, ch + 8 * q));
+            const uint4 zv = *zp;
+            const uint32_t zw[4] = {zv.x, zv.y, zv.z, zv.w};
+            uint32_t res[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int i = 8 * q + 2 * e;
+              const uint64_t zz = add_f32x2(f32x2(bf16_lo(zw[e]), bf16_hi(zw[e])),
+                                            f32x2(__uint_as_float(vd[i]), __uint_as_float(vd[i + 1])));
+              float r0, r1;
+              f32x2_split(zz, r0, r1);
+              res[e] = pack_bf16(r0, r1);
+            }
+            if (keep) *zp = make_uint4(res[0], res[1], res[2], res[3]);
+          }
         }
       }
       tc_fence_before();
@@ -954,8 +985,8 @@ __global__ void __launch_bounds__(kOThreads, 1)
         if (ok) {
           const int c0 = (tile % tiles_per_row) * kOTile;
           const int rr = tile / tiles_per_row;
-          tma_store_3d(&map_out, zt, 0, c0, rr);
-          tma_store_3d(&map_out, zt + kOTile * 128, 64, c0, rr);
+          tma_store_3d(&map_out, s.z[st], 0, c0, rr);
+          tma_store_3d(&map_out, s.z[st] + kOTile * 128, 64, c0, rr);
           tma_store_commit();
           tma_store_wait_read0();
         }
@@ -970,7 +1001,7 @@ __global__ void __launch_bounds__(kOThreads, 1)
   if (warp == 0) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem0, 256);
+    tmem_dealloc(tmem0, 512);
   }
 }
 

@@ -6,7 +6,7 @@
 // (legacy/reference/triangle.py:19-50, engine left/right per legacy/released.py:135-173).
 //
 // Three launches:
-//  1. trimul_proj: 128-pair tiles of raw z (TMA, 128B swizzle) times the resident packed
+//  1. trimul_proj: 64-pair tiles of raw z (TMA, 128B swizzle) times the resident packed
 //     projection [W_l; W_lg; W_r; W_rg] (tcgen05, fp32 in TMEM); the LayerNorm is folded
 //     into the epilogue; L and R are written CHANNEL-MAJOR [c][a][k] so that step 2 is a
 //     plain K-major GEMM per channel. The incoming direction reads COLUMN tiles of z
@@ -18,9 +18,9 @@
 //     per-pair statistics (z's from step 1, u's from trimul_ustats), sigmoid gate, mask
 //     and residual, written back through the z tile and a TMA store.
 //
-// Kernels 1 and 3 run G = 2 independent groups of 4 warps per CTA (one CTA per SM,
-// persistent over tiles), sharing the resident weights; each group has its own z stage and
-// 256 TMEM columns, so one group's loads and epilogue overlap the other's MMAs.
+// Kernels 1 and 3 are persistent (one CTA per SM) and warp-specialised: a TMA warp, an MMA
+// warp, statistics warps and eight epilogue warps, with the resident weights, a ring of
+// input tiles and double-buffered TMEM accumulators.
 #include "abi_util.h"
 #include "common.cuh"
 #include "kernels.h"
@@ -30,9 +30,6 @@ namespace {
 
 constexpr int kC = 128;       // pair channels
 constexpr int kH = 128;       // hidden channels
-constexpr int kTile = 128;    // pairs per tile
-constexpr int kGroups = 2;
-constexpr int kThreads = kGroups * 128;
 
 // ---------------------------------------------------------------- packed weight image
 // [0, 128K)            projection operand: rows 0..127 W_l', 128..255 W_lg', 256..383 W_r', 384..511 W_rg'
@@ -53,35 +50,6 @@ struct Vecs {
   float bias_gate[128];
   float bias_out[128];
 };
-
-__device__ __forceinline__ void load_z_stats(const uint8_t* tile, int row, float& mean, float& rstd) {
-  // row `row` of a [128 x 128] bf16 tile stored as two K-major SW128 blocks
-  float s = 0.f;
-  uint4 v[16];
-#pragma unroll
-  for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-    for (int q = 0; q < 8; ++q)
-      v[kb * 8 + q] = *reinterpret_cast<const uint4*>(tile + kb * 16384 + sw128_offset(row, q * 8));
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) s += bf16_lo(w[j]) + bf16_hi(w[j]);
-  }
-  mean = s * (1.0f / kC);
-  float q2 = 0.f;
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float a = bf16_lo(w[j]) - mean, b = bf16_hi(w[j]) - mean;
-      q2 += a * a + b * b;
-    }
-  }
-  rstd = rsqrtf(q2 * (1.0f / kC) + 1e-5f);
-}
 
 // ====================================================================== kernel 1
 // Warp-specialised, persistent, 64-pair tiles. The projection is computed TRANSPOSED,
@@ -345,35 +313,39 @@ __global__ void __launch_bounds__(kPThreads, 1)
 }
 
 // ====================================================================== kernel 3
-// Warp-specialised, persistent, 128-pair tiles, computed TRANSPOSED (TMEM lane = output
-// channel, column = pair):
-//   gate[c][p] = W_g'[c] . z[p]          B = the z tile (K-major, as TMA lands it)
-//   out[c][p]  = W_o'[c] . u[:, p]       B = the channel-major u tile used as an MN-major
+// Warp-specialised, persistent, 128-pair tiles; TMEM lane = pair, column = channel:
+//   gate[p][c] = z[p] . W_g'[c]          A = the z tile (K-major, as TMA lands it)
+//   out[p][c]  = u[:, p] . W_o'[c]       A = the channel-major u tile read as an MN-major
 //                                        operand (no transposition in shared memory)
 // with both LayerNorms folded into the epilogue through per-pair statistics:
-//   delta[c][p] = (ru_p (out - mu_p wsum_o[c]) + b_o[c]) * sigmoid(rz_p (gate - mz_p wsum_g[c]) + b_g[c])
-// The epilogue adds delta into the z tile in place (lanes = consecutive channels of one pair
-// row) and one thread stores the tile with TMA.
+//   delta[p][c] = (ru_p (out - mu_p wsum_o[c]) + b_o[c]) * sigmoid(rz_p (gate - mz_p wsum_g[c]) + b_g[c])
+// A thread owns one pair and adds delta into that pair's row of the z tile in place
+// (16-byte swizzled vectors); the per-pair coefficients stay in registers and the paired
+// fp32 pipe computes two channels per instruction. One thread stores the tile with TMA.
 //   warp 0      TMA: z and u tiles into a 2-stage ring
 //   warp 1      MMA: gate and out products -> 256 TMEM columns, double-buffered
-//   warps 2-3   per-pair statistics of z (rows) and u (columns) and the keep mask
-//   warps 4-11  epilogue: lane = channel, warps 4-7 pairs 0-63, warps 8-11 pairs 64-127
+//   warps 2-3   per-pair coefficients (precomputed statistics) and the keep mask
+//   warps 4-11  epilogue: lane = pair, warps 4-7 channels 0-63, warps 8-11 channels 64-127
 constexpr int kOTile = 128;
 constexpr int kOStages = 2;
 constexpr int kOThreads = 384;
 
 struct OutSmem {
-  alignas(1024) uint8_t wg[kGateBytes];
+  alignas(1024) uint8_t wg[kGateBytes];                // [c][k]: 2 K-blocks of [128 c x 128 B]
   alignas(1024) uint8_t wo[kOutBytes];
   alignas(1024) uint8_t z[kOStages][kOTile * kC * 2];  // [p][c]: 2 K-blocks of [128 p x 128 B]
   alignas(1024) uint8_t u[kOStages][kH * kOTile * 2];  // [c][p]: 2 p-blocks of [128 c x 128 B]
-  float wsum_gate[128], bias_gate[128], wsum_out[128], bias_out[128];
-  float zm[2][kOTile], zr[2][kOTile], um[2][kOTile], ur[2][kOTile], keep[2][kOTile];
+  float4 cg[kC / 2];  // channel pair (2i, 2i+1): wsum_gate x2, bias_gate / 2 x2
+  float4 co[kC / 2];  // channel pair: wsum_out x2, bias_out / 2 x2
+  float4 pc[2][kOTile];  // per pair: rz / 2, -rz mz / 2, ru / 2, -ru mu / 2
+  float keep[2][kOTile];
   uint64_t wbar;
   uint64_t full[kOStages], empty[kOStages];
   uint64_t acc_full[2], acc_free[2], st_full[2], st_free[2];
   uint32_t tmem_base;
 };
+
+static_assert(sizeof(OutSmem) + 1024 <= 232448, "output shared memory exceeds the per-CTA limit");
 
 struct OutParams {
   const uint8_t* packed;
@@ -461,7 +433,7 @@ __global__ void __launch_bounds__(kOThreads, 1)
     mbar_init(&s.wbar, 1);
     for (int i = 0; i < kOStages; ++i) {
       mbar_init(&s.full[i], 1);
-      mbar_init(&s.empty[i], 1);
+      mbar_init(&s.empty[i], 2);  // the MMA commit (u, z read) + the store's read of z
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.acc_full[i], 1);
@@ -473,11 +445,9 @@ __global__ void __launch_bounds__(kOThreads, 1)
   }
   {
     const float* v = reinterpret_cast<const float*>(p.packed + kProjBytes + kGateBytes + kOutBytes);
-    for (int i = threadIdx.x; i < 128; i += kOThreads) {
-      s.wsum_gate[i] = v[1024 + i];
-      s.bias_gate[i] = v[1152 + i];
-      s.bias_out[i] = v[1280 + i];
-      s.wsum_out[i] = v[1408 + i];
+    for (int i = threadIdx.x; i < kC / 2; i += kOThreads) {
+      s.cg[i] = make_float4(v[1024 + 2 * i], v[1024 + 2 * i + 1], 0.5f * v[1152 + 2 * i], 0.5f * v[1152 + 2 * i + 1]);
+      s.co[i] = make_float4(v[1408 + 2 * i], v[1408 + 2 * i + 1], 0.5f * v[1280 + 2 * i], 0.5f * v[1280 + 2 * i + 1]);
     }
   }
   if (warp == 0) {
@@ -510,12 +480,14 @@ __global__ void __launch_bounds__(kOThreads, 1)
           tma_load_3d(s.u[st] + kb * (kH * 128), &map_u, &s.full[st], c0 + kb * 64, r, b * kH);
         }
       }
+      // every issued load has landed before the CTA can exit
       mbar_wait(&s.wbar, 0, p.err, kErrTimeoutLoad);
+      if (it > 0) mbar_wait(&s.full[(it - 1) % kOStages], ((it - 1) / kOStages) & 1, p.err, kErrTimeoutLoad);
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc_g = idesc_bf16_f32(128, kOTile);
-      const uint32_t idesc_o = idesc_bf16_f32_bmn(128, kOTile);
+      const uint32_t idesc_g = idesc_bf16_f32(kOTile, kC);
+      const uint32_t idesc_o = idesc_bf16_f32_amn(kOTile, kC);
       bool ok = mbar_wait(&s.wbar, 0, p.err, kErrTimeoutLoad);
       int it = 0;
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
@@ -524,22 +496,24 @@ __global__ void __launch_bounds__(kOThreads, 1)
         if (!mbar_wait(&s.acc_free[buf], ((it >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty)) break;
         tc_fence_after();
         const uint32_t wg = smem_u32(s.wg), wo = smem_u32(s.wo), za = smem_u32(s.z[st]), ua = smem_u32(s.u[st]);
-        const uint32_t dg = tmem0 + buf * 256, dout = tmem0 + buf * 256 + kOTile;
+        const uint32_t dg = tmem0 + buf * 256, dout = tmem0 + buf * 256 + kC;
 #pragma unroll
         for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_bf16(dg, desc_kmajor_sw128(wg + kb * 16384) + 2 * kk, desc_kmajor_sw128(za + kb * (kOTile * 128)) + 2 * kk,
+            mma_bf16(dg, desc_kmajor_sw128(za + kb * (kOTile * 128)) + 2 * kk, desc_kmajor_sw128(wg + kb * 16384) + 2 * kk,
                      idesc_g, (kb | kk) != 0);
 #pragma unroll
         for (int ks = 0; ks < kH / 16; ++ks)
-          mma_bf16(dout, desc_kmajor_sw128(wo + (ks / 4) * 16384) + 2 * (ks % 4),
-                   desc_mnmajor_sw128(ua + ks * 2048, kH * 128, 1024), idesc_o, ks != 0);
+          mma_bf16(dout, desc_mnmajor_sw128(ua + ks * 2048, kH * 128, 1024),
+                   desc_kmajor_sw128(wo + (ks / 4) * 16384) + 2 * (ks % 4), idesc_o, ks != 0);
         mma_commit(&s.acc_full[buf]);
+        mma_commit(&s.empty[st]);
       }
     }
   } else if (warp < 4) {
-    // per-pair statistics (precomputed) and keep mask: thread t handles pairs t and t + 64
+    // per-pair coefficients (precomputed statistics) and keep mask: thread t handles pairs
+    // t and t + 64
     const int t = (warp - 2) * 32 + lane;
     int it = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
@@ -559,23 +533,20 @@ __global__ void __launch_bounds__(kOThreads, 1)
           zs = p.zstats[pair];
           us = p.ustats[pair];
         }
-        s.zm[buf][pp] = zs.x;
-        s.zr[buf][pp] = zs.y;
-        s.um[buf][pp] = us.x;
-        s.ur[buf][pp] = us.y;
+        s.pc[buf][pp] = make_float4(0.5f * zs.y, -0.5f * zs.y * zs.x, 0.5f * us.y, -0.5f * us.y * us.x);
         s.keep[buf][pp] =
-            (!p.masked_zero || (j < p.N && p.mask[b * p.N + p.row0 + r] && p.mask[b * p.N + j])) ? 1.f : 0.f;
+            (j < p.N && (!p.masked_zero || (p.mask[b * p.N + p.row0 + r] && p.mask[b * p.N + j]))) ? 1.f : 0.f;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.st_full[buf]);
     }
   } else {
-    // epilogue: lane = output channel c; half = which 64 pairs
+    // epilogue: lane = pair pp of the tile; half = which 64 channels. Per channel pair:
+    //   g/2 = (rz/2) gate + (-rz mz/2) wsum_g + b_g/2,   o/2 likewise with ru, mu, W_o's vectors,
+    //   z' = z + o * sigmoid(g) = z + (o/2) tanh(g/2) + o/2
     const int half = (warp - 4) / 4;
-    const int c = (warp & 3) * 32 + lane;
+    const int pp = (warp & 3) * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const float wsg = s.wsum_gate[c], bg = s.bias_gate[c], wso = s.wsum_out[c], bo = s.bias_out[c];
-    const int kb = c / 64;
     int it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
@@ -586,23 +557,41 @@ __global__ void __launch_bounds__(kOThreads, 1)
         ok = __all_sync(0xFFFFFFFFu, w1 && w2);
       }
       tc_fence_after();
-      uint8_t* zt = s.z[st];
+      uint8_t* zrow = s.z[st] + half * (kOTile * 128);
       if (ok) {
+        const float4 pc = s.pc[buf][pp];
+        const bool keep = s.keep[buf][pp] != 0.f;
+        const uint64_t ga = f32x2(pc.x, pc.x), gb = f32x2(pc.y, pc.y), oa = f32x2(pc.z, pc.z), ob = f32x2(pc.w, pc.w);
 #pragma unroll 1
         for (int ch = 0; ch < 64; ch += 32) {
-          const int p0 = half * 64 + ch;
+          const int cb = half * 64 + ch;
           uint32_t vg[32], vo[32];
-          tmem_ld32(tmem0 + lane_off + buf * 256 + p0, vg);
-          tmem_ld32(tmem0 + lane_off + buf * 256 + kOTile + p0, vo);
+          tmem_ld32(tmem0 + lane_off + buf * 256 + cb, vg);
+          tmem_ld32(tmem0 + lane_off + buf * 256 + kC + cb, vo);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int pp = p0 + i;
-            const float g = s.zr[buf][pp] * (__uint_as_float(vg[i]) - s.zm[buf][pp] * wsg) + bg;
-            const float o = s.ur[buf][pp] * (__uint_as_float(vo[i]) - s.um[buf][pp] * wso) + bo;
-            __nv_bfloat16* addr = reinterpret_cast<__nv_bfloat16*>(zt + kb * (kOTile * 128) + sw128_offset(pp, c % 64));
-            const float zo = __bfloat162float(*addr);
-            *addr = __float2bfloat16_rn(zo + o * sigmoid_fast(g) * s.keep[buf][pp]);
+          for (int q = 0; q < 4; ++q) {
+            uint4* zp = reinterpret_cast<uint4*>(zrow + sw128_offset(pp, ch + 8 * q));
+            const uint4 zv = *zp;
+            const uint32_t zw[4] = {zv.x, zv.y, zv.z, zv.w};
+            uint32_t res[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int i = 8 * q + 2 * e;  // channel pair (cb + i, cb + i + 1)
+              const float4 cg = s.cg[(cb + i) / 2], co = s.co[(cb + i) / 2];
+              const uint64_t g = fma_f32x2(ga, f32x2(__uint_as_float(vg[i]), __uint_as_float(vg[i + 1])),
+                                           fma_f32x2(gb, f32x2(cg.x, cg.y), f32x2(cg.z, cg.w)));
+              const uint64_t o = fma_f32x2(oa, f32x2(__uint_as_float(vo[i]), __uint_as_float(vo[i + 1])),
+                                           fma_f32x2(ob, f32x2(co.x, co.y), f32x2(co.z, co.w)));
+              float g0, g1;
+              f32x2_split(g, g0, g1);
+              const uint64_t d = fma_f32x2(o, f32x2(tanh_fast(g0), tanh_fast(g1)), o);
+              const uint64_t zz = add_f32x2(d, f32x2(bf16_lo(zw[e]), bf16_hi(zw[e])));
+              float r0, r1;
+              f32x2_split(zz, r0, r1);
+              res[e] = pack_bf16(r0, r1);
+            }
+            if (keep) *zp = make_uint4(res[0], res[1], res[2], res[3]);
           }
         }
       }
@@ -619,8 +608,8 @@ __global__ void __launch_bounds__(kOThreads, 1)
         if (ok) {
           const int c0 = (tile % tiles_per_row) * kOTile;
           const int rr = tile / tiles_per_row;
-          tma_store_3d(&map_out, zt, 0, c0, rr);
-          tma_store_3d(&map_out, zt + kOTile * 128, 64, c0, rr);
+          tma_store_3d(&map_out, s.z[st], 0, c0, rr);
+          tma_store_3d(&map_out, s.z[st] + kOTile * 128, 64, c0, rr);
           tma_store_commit();
           tma_store_wait_read0();
         }
