@@ -174,13 +174,10 @@ __global__ void __launch_bounds__(kPbThreads, 1)
       if (lane == 0) mbar_arrive(&s.acc_empty[acc]);
       const int64_t p = t * kPbTile + row;
       if (p < P) {
+        // pair p = row * N + col of the rows held: pb[h * pb_h + row * pb_r + col]
+        float* dst = pb + (p / N) * pb_r + (p % N);
 #pragma unroll
-        {
-          // pair p = row * N + col of the rows held: pb[h * pb_h + row * pb_r + col]
-          float* dst = pb + (p / N) * pb_r + (p % N);
-#pragma unroll
-          for (int h = 0; h < kHs; ++h) dst[h * pb_h] = rstd * (__uint_as_float(v[h]) - mean * s.wsum[h]);
-        }
+        for (int h = 0; h < kHs; ++h) dst[h * pb_h] = rstd * (__uint_as_float(v[h]) - mean * s.wsum[h]);
       }
     }
   }

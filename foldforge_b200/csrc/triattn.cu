@@ -345,10 +345,12 @@ __global__ void __launch_bounds__(kProjThreads, 1)
 // Per CTA, a flat sequence of (unit, 64-key block) steps; a unit is 256 queries (two groups
 // of 128) of one (batch, row, head).
 //   warp 0      TMA: Q per unit (double-buffered), K, V^T and the two groups' bias tiles
-//               per block through a 3-stage ring
-//   warp 1      MMA: S = Q K^T of step i + 1 (into the group's S/P buffer i % 2) ahead of
-//               O += P V of step i, with P read from TMEM (A operand) and O accumulated in
-//               TMEM across the unit's blocks (O buffer = unit % 2)
+//               per block through a 4-stage ring
+//   warp 1      MMA: S = Q K^T of step i + 2 (into the group's S/P buffer (i + 2) % 3) ahead
+//               of O += P V of step i, with P read from TMEM (A operand) and O accumulated
+//               in TMEM across the unit's blocks (one O buffer per group: the next unit's
+//               first P V waits until the previous output has been read). Three S/P
+//               buffers let the tensor pipe run two steps ahead of the softmax.
 //   warps 2-9   softmax, thread = query row (TMEM lane): logits = S + bias (+ key mask),
 //               P = 2^(x - m) written back over S as bf16. The running maximum m is raised
 //               lazily: only when a block's maximum exceeds m + kRescale does the warp
@@ -363,7 +365,9 @@ constexpr int kMaxMaskWords = 2048;  // B * ceil(N / 64) * 2 words of key-mask b
 constexpr int kPolyEvery = 4;        // one key pair in four takes the FMA-pipe exponential
 constexpr int kVtRows = 48;          // V^T (32 rows), a row of ones, 15 zero rows
 constexpr int kOCols = 48;           // O (32 columns), the row sum, 15 unused
-constexpr int kGroupCols = 256;      // per group: S/P buffers at +0 / +64, O buffers at +128 / +192
+constexpr int kSBufs = 3;            // S/P buffers per group
+constexpr int kGroupCols = 256;      // per group: S/P buffers at +0 / +64 / +128, O at +192
+constexpr uint32_t kOCol = 192;
 constexpr float kRescale = 8.0f;     // lazy-rescale threshold in log2 units
 
 struct AttnSmem {
@@ -374,10 +378,10 @@ struct AttnSmem {
   uint32_t mask_words[kMaxMaskWords];
   uint64_t q_full[2], q_empty[2];
   uint64_t kv_full[kKVStages], kv_empty[kKVStages];
-  uint64_t s_full[kGroups][2];
-  uint64_t p_full[kGroups][2];
-  uint64_t pv_done[kGroups];
-  uint64_t o_full[kGroups][2], o_free[kGroups][2];
+  uint64_t s_full[kSBufs];            // both groups' S of a step
+  uint64_t p_full[kGroups][kSBufs];
+  uint64_t pv_done;                   // both groups' P V of a step
+  uint64_t o_full[kGroups], o_free[kGroups];
   uint64_t mma_done;
   uint32_t tmem_base;
 };
@@ -427,15 +431,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&s.kv_empty[i], 1 + 8);  // MMA commit + 8 softmax warps (bias read)
     }
     for (int g = 0; g < kGroups; ++g) {
-      mbar_init(&s.pv_done[g], 1);
-      for (int i = 0; i < 2; ++i) {
-        mbar_init(&s.s_full[g][i], 1);
+      mbar_init(&s.o_full[g], 1);
+      mbar_init(&s.o_free[g], 4);
+      for (int i = 0; i < kSBufs; ++i) {
         mbar_init(&s.p_full[g][i], 4);
-        mbar_init(&s.o_full[g][i], 1);
-        mbar_init(&s.o_free[g][i], 4);
+        if (g == 0) mbar_init(&s.s_full[i], 1);
       }
     }
     mbar_init(&s.mma_done, 1);
+    mbar_init(&s.pv_done, 1);
     fence_mbar_init();
   }
   // key-mask bits, per batch padded to whole 64-key blocks (zero beyond N)
@@ -513,7 +517,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const uint32_t idesc_o = idesc_bf16_f32(128, kOCols);
       auto issue_s = [&](int i) -> bool {
         const int ul = i / nkb, j = i % nkb;
-        const int st = i % kKVStages, buf = i & 1, qb = ul & 1;
+        const int st = i % kKVStages, buf = i % kSBufs, qb = ul & 1;
         if (j == 0 && !mbar_wait(&s.q_full[qb], (ul >> 1) & 1, p.err, kErrTimeoutLoad)) return false;
         if (!mbar_wait(&s.kv_full[st], (i / kKVStages) & 1, p.err, kErrTimeoutLoad)) return false;
         tc_fence_after();
@@ -523,32 +527,34 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           const uint64_t db = desc_kmajor_sw64(smem_u32(s.k[st]));
           mma_bf16(d, da, db, idesc_s, 0);
           mma_bf16(d, da + 2, db + 2, idesc_s, 1);
-          mma_commit(&s.s_full[g][buf]);
         }
+        mma_commit(&s.s_full[buf]);  // both groups' S
         if (j == nkb - 1) mma_commit(&s.q_empty[qb]);  // the unit's Q may be refilled once these finish
         return true;
       };
-      bool ok = steps > 0 && issue_s(0);
+      bool ok = true;
+      for (int i = 0; i < 2 && i < steps && ok; ++i) ok = issue_s(i);
       for (int i = 0; i < steps && ok; ++i) {
-        // S of the next step first: it overwrites the buffer whose P was consumed by the
-        // P V issued one step ago (same thread, so the tensor pipe keeps the order)
-        if (i + 1 < steps && !issue_s(i + 1)) break;
+        // S two steps ahead: its buffer's last P was read by the P V issued one step ago
+        // (same thread, so the tensor pipe keeps the order)
+        if (i + 2 < steps && !issue_s(i + 2)) break;
         const int ul = i / nkb, j = i % nkb;
-        const int st = i % kKVStages, buf = i & 1, ob = ul & 1;
+        const int st = i % kKVStages, buf = i % kSBufs;
         for (int g = 0; g < kGroups; ++g) {
-          if (!mbar_wait(&s.p_full[g][buf], (i >> 1) & 1, p.err, kErrTimeoutMma)) { ok = false; break; }
-          if (j == 0 && !mbar_wait(&s.o_free[g][ob], ((ul >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty)) { ok = false; break; }
+          if (!mbar_wait(&s.p_full[g][buf], (i / kSBufs) & 1, p.err, kErrTimeoutMma)) { ok = false; break; }
+          // the single O buffer: the previous unit's output has been read
+          if (j == 0 && !mbar_wait(&s.o_free[g], (ul & 1) ^ 1, p.err, kErrTimeoutEmpty)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t d = tmem0 + g * kGroupCols + 128 + ob * 64;
+          const uint32_t d = tmem0 + g * kGroupCols + kOCol;
           const uint32_t a = tmem0 + g * kGroupCols + buf * 64;
           const uint64_t db = desc_kmajor_sw128(smem_u32(s.vt[st]));
 #pragma unroll
           for (int kk = 0; kk < kKB / 16; ++kk)
             mma_bf16_tmem_a(d, a + kk * 8, db + 2 * kk, idesc_o, (j | kk) != 0);
-          mma_commit(&s.pv_done[g]);
-          if (j == nkb - 1) mma_commit(&s.o_full[g][ob]);
+          if (j == nkb - 1) mma_commit(&s.o_full[g]);
         }
         if (!ok) break;
+        mma_commit(&s.pv_done);  // both groups' P V
         mma_commit(&s.kv_empty[st]);
       }
       // every issued MMA completes before TMEM is released
@@ -567,17 +573,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     int prev_q = 0, prev_b = 0, prev_r = 0, prev_h = 0;  // the unit awaiting its output
     // read, normalise and store the output of unit `pu` (O buffer pu % 2)
     auto finalize = [&](int pu) -> bool {
-      const int pob = pu & 1;
-      const bool w = mbar_wait(&s.o_full[g][pob], (pu >> 1) & 1, p.err, kErrTimeoutMma);
+      const bool w = mbar_wait(&s.o_full[g], pu & 1, p.err, kErrTimeoutMma);
       if (!__all_sync(0xFFFFFFFFu, w)) return false;
       tc_fence_after();
       uint32_t ov[32], os;
-      tmem_ld32(gbase + 128 + pob * 64, ov);
-      tmem_ld1(gbase + 128 + pob * 64 + kD, os);
+      tmem_ld32(gbase + kOCol, ov);
+      tmem_ld1(gbase + kOCol + kD, os);
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s.o_free[g][pob]);
+      if (lane == 0) mbar_arrive(&s.o_free[g]);
       if (prev_q < p.N) {
         const float inv = 1.0f / __uint_as_float(os);
         // natural pair position: starting (i=r, j=q), ending (i=q, j=r)
@@ -601,12 +606,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const int q = (qp * 2 + g) * kTile + t;
       const bool row_on = p.mask[b * p.N + p.row0 + r] != 0;
       const uint32_t* mw = s.mask_words + b * p.words_per_batch;
-      const int ob = ul & 1;
       float m = 0.f;
       for (int j = 0; j < nkb; ++j, ++i) {
         const int st = i % kKVStages;
-        const int buf = i & 1;
-        const bool w1 = mbar_wait(&s.s_full[g][buf], (i >> 1) & 1, p.err, kErrTimeoutMma);
+        const int buf = i % kSBufs;
+        const bool w1 = mbar_wait(&s.s_full[buf], (i / kSBufs) & 1, p.err, kErrTimeoutMma);
         const bool w2 = mbar_wait(&s.kv_full[st], (i / kKVStages) & 1, p.err, kErrTimeoutLoad);
         if (!__all_sync(0xFFFFFFFFu, w1 && w2)) { ok = false; break; }
         tc_fence_after();
@@ -657,18 +661,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             // P V has landed
             const float m_new = need ? bm : m;
             const float alpha = ex2(m - m_new);
-            const bool w3 = mbar_wait(&s.pv_done[g], (i - 1) & 1, p.err, kErrTimeoutMma);
+            const bool w3 = mbar_wait(&s.pv_done, (i - 1) & 1, p.err, kErrTimeoutMma);
             if (!__all_sync(0xFFFFFFFFu, w3)) { ok = false; break; }
             tc_fence_after();
             uint32_t ov[32], os;
-            tmem_ld32(gbase + 128 + ob * 64, ov);
-            tmem_ld1(gbase + 128 + ob * 64 + kD, os);
+            tmem_ld32(gbase + kOCol, ov);
+            tmem_ld1(gbase + kOCol + kD, os);
             tmem_ld_wait();
 #pragma unroll
             for (int d = 0; d < kD; ++d) ov[d] = __float_as_uint(__uint_as_float(ov[d]) * alpha);
             os = __float_as_uint(__uint_as_float(os) * alpha);
-            tmem_st32(gbase + 128 + ob * 64, ov);
-            tmem_st1(gbase + 128 + ob * 64 + kD, os);
+            tmem_st32(gbase + kOCol, ov);
+            tmem_st1(gbase + kOCol + kD, os);
             tmem_st_wait();
             m = m_new;
           }
