@@ -12,8 +12,9 @@
 // first product already is W_a' LN(z) up to the bias W beta (gamma is folded into W' and
 // 1/2 into the a rows, so the SwiGLU is  h = a/2 + b_a/2,  silu(a) b = (h + h tanh h) b).
 // Shared memory only feeds the weight operands. The first product runs two chunks ahead of the
-// second. z tiles (double-buffered) and weight chunks (3-stage ring) arrive by TMA / bulk
-// copy; the residual (pair mask applied in "zero" mode) is written over the staged z tile
+// second. z tiles (double-buffered) and weight chunks arrive by TMA / bulk copy, the
+// chunks' first- and second-product parts through separate 3-stage rings, each stage
+// released by the product that reads it (so loads run up to three chunks ahead); the residual (pair mask applied in "zero" mode) is written over the staged z tile
 // and leaves through a TMA store. The next tile's statistics are taken before this tile's
 // residual, so its first products overlap the residual.
 //
@@ -50,7 +51,8 @@ struct Smem {
   alignas(1024) uint8_t w2[kWStages][kW2Chunk];
   float bias[2 * kHidden];
   uint64_t z_full[2], z_empty[2];
-  uint64_t w_full[kWStages], w_empty[kWStages];
+  uint64_t w1_full[kWStages], w1_empty[kWStages];  // first-product weight chunks
+  uint64_t w2_full[kWStages], w2_empty[kWStages];  // second-product weight chunks
   uint64_t zt_full, zt_free;
   uint64_t a1_full[2], h_full[2];
   uint64_t acc2_full, acc2_free;
@@ -96,8 +98,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.h_full[i], 8);
     }
     for (int i = 0; i < kWStages; ++i) {
-      mbar_init(&s.w_full[i], 1);
-      mbar_init(&s.w_empty[i], 1);
+      mbar_init(&s.w1_full[i], 1);
+      mbar_init(&s.w1_empty[i], 1);
+      mbar_init(&s.w2_full[i], 1);
+      mbar_init(&s.w2_empty[i], 1);
     }
     mbar_init(&s.zt_full, 4);
     mbar_init(&s.zt_free, 1);
@@ -123,7 +127,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       tma_prefetch_map(&map_z);
       tma_prefetch_map(&map_out);
-      int zl = 0, wc = 0;  // z tiles and weight chunks issued
+      int zl = 0, n1 = 0, n2 = 0;  // z tiles, first- and second-product weight chunks issued
       bool ok = true;
       auto load_z = [&](int ti) -> bool {  // tile ti of this CTA into buffer ti % 2
         const int zb = ti & 1;
@@ -134,26 +138,47 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++zl;
         return true;
       };
+      // global chunk wc = tile * kChunks + j; each ring stage is released by the product that
+      // reads it, so the loads run up to kWStages chunks ahead of their product
+      auto load_w1 = [&](int wc) -> bool {
+        const int st = wc % kWStages;
+        if (!mbar_wait(&s.w1_empty[st], ((wc / kWStages) & 1) ^ 1, p.err, kErrTimeoutEmpty)) return false;
+        mbar_arrive_expect_tx(&s.w1_full[st], kW1Chunk);
+        bulk_load(s.w1[st], p.packed + (wc % kChunks) * kW1Chunk, kW1Chunk, &s.w1_full[st]);
+        ++n1;
+        return true;
+      };
+      auto load_w2 = [&](int wc) -> bool {
+        const int st = wc % kWStages;
+        if (!mbar_wait(&s.w2_empty[st], ((wc / kWStages) & 1) ^ 1, p.err, kErrTimeoutEmpty)) return false;
+        mbar_arrive_expect_tx(&s.w2_full[st], kW2Chunk);
+        bulk_load(s.w2[st], p.packed + kW1Bytes + (wc % kChunks) * kW2Chunk, kW2Chunk, &s.w2_full[st]);
+        ++n2;
+        return true;
+      };
+      // the order the MMA thread consumes them: first products run two chunks ahead
+      const int total = my_tiles * kChunks;
       if (my_tiles > 0) ok = load_z(0);
-      for (int ti = 0; ti < my_tiles && ok; ++ti) {
-        for (int j = 0; j < kChunks; ++j, ++wc) {
-          const int st = wc % kWStages;
-          if (!mbar_wait(&s.w_empty[st], ((wc / kWStages) & 1) ^ 1, p.err, kErrTimeoutEmpty)) { ok = false; break; }
-          mbar_arrive_expect_tx(&s.w_full[st], kW1Chunk + kW2Chunk);
-          bulk_load(s.w1[st], p.packed + j * kW1Chunk, kW1Chunk, &s.w_full[st]);
-          bulk_load(s.w2[st], p.packed + kW1Bytes + j * kW2Chunk, kW2Chunk, &s.w_full[st]);
-          // the next tile's z follows the third chunk of this one
-          if (j == 2 && ti + 1 < my_tiles && !load_z(ti + 1)) { ok = false; break; }
-        }
+      for (int wc = 0; wc < 2 && wc < total && ok; ++wc) ok = load_w1(wc);
+      for (int wc = 0; wc < total && ok; ++wc) {
+        if (!load_w2(wc)) break;
+        if (wc + 2 < total && !load_w1(wc + 2)) break;
+        // the next tile's z follows the third chunk of this one
+        const int ti = wc / kChunks;
+        if (wc % kChunks == 2 && ti + 1 < my_tiles && !load_z(ti + 1)) break;
       }
       // every issued copy lands before the CTA may exit
       for (int k = 0; k < 2 && k < zl; ++k) {
         const int i = zl - 1 - k;
         mbar_wait(&s.z_full[i & 1], (i >> 1) & 1, p.err, kErrTimeoutLoad);
       }
-      for (int k = 0; k < kWStages && k < wc; ++k) {
-        const int i = wc - 1 - k;
-        mbar_wait(&s.w_full[i % kWStages], (i / kWStages) & 1, p.err, kErrTimeoutLoad);
+      for (int k = 0; k < kWStages && k < n1; ++k) {
+        const int i = n1 - 1 - k;
+        mbar_wait(&s.w1_full[i % kWStages], (i / kWStages) & 1, p.err, kErrTimeoutLoad);
+      }
+      for (int k = 0; k < kWStages && k < n2; ++k) {
+        const int i = n2 - 1 - k;
+        mbar_wait(&s.w2_full[i % kWStages], (i / kWStages) & 1, p.err, kErrTimeoutLoad);
       }
     }
   } else if (warp == 9) {
@@ -162,8 +187,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t idesc = idesc_bf16_f32(128, 128);
       bool ok = true;
       // first product of chunk j (global weight counter wc) into A1[j % 2]; A = Z from TMEM
-      auto mma1 = [&](int j, int wc) {
-        const uint32_t b0 = smem_u32(s.w1[wc % kWStages]);
+      auto mma1 = [&](int j, int wc) -> bool {
+        const int st = wc % kWStages;
+        if (!mbar_wait(&s.w1_full[st], (wc / kWStages) & 1, p.err, kErrTimeoutLoad)) return false;
+        tc_fence_after();
+        const uint32_t b0 = smem_u32(s.w1[st]);
         const uint32_t d = tmem0 + kColA1 + (j & 1) * 128;
 #pragma unroll
         for (int kb = 0; kb < 2; ++kb)
@@ -172,38 +200,30 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_bf16_tmem_a(d, tmem0 + kColZ + (kb * 4 + kk) * 8, desc_kmajor_sw128(b0 + kb * 16384) + 2 * kk, idesc,
                             (kb | kk) != 0);
         mma_commit(&s.a1_full[j & 1]);
+        mma_commit(&s.w1_empty[st]);
+        return true;
       };
       for (int ti = 0; ti < my_tiles && ok; ++ti) {
         const int w0 = ti * kChunks;
         if (!mbar_wait(&s.zt_full, ti & 1, p.err, kErrTimeoutLoad)) break;
         // prologue: chunks 0 and 1 (A1[0] / A1[1] were last read by chunks 6 / 7 of the
         // previous tile, whose H this thread already waited for)
-        for (int j = 0; j < 2 && ok; ++j) {
-          if (!mbar_wait(&s.w_full[(w0 + j) % kWStages], ((w0 + j) / kWStages) & 1, p.err, kErrTimeoutLoad)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          mma1(j, w0 + j);
-        }
+        for (int j = 0; j < 2 && ok; ++j) ok = mma1(j, w0 + j);
         for (int j = 0; j < kChunks && ok; ++j) {
           const int wc = w0 + j;
+          const int st = wc % kWStages;
           const int u = ti * (kChunks / 2) + j / 2;  // use count of A1 / H buffer j % 2
-          if (j + 2 < kChunks &&
-              !mbar_wait(&s.w_full[(wc + 2) % kWStages], ((wc + 2) / kWStages) & 1, p.err, kErrTimeoutLoad)) {
-            ok = false;
-            break;
-          }
           if (!mbar_wait(&s.h_full[j & 1], u & 1, p.err, kErrTimeoutMma)) { ok = false; break; }
           if (j == 0 && !mbar_wait(&s.acc2_free, (ti & 1) ^ 1, p.err, kErrTimeoutEmpty)) { ok = false; break; }
+          if (!mbar_wait(&s.w2_full[st], (wc / kWStages) & 1, p.err, kErrTimeoutLoad)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t b0 = smem_u32(s.w2[wc % kWStages]);
+          const uint32_t b0 = smem_u32(s.w2[st]);
 #pragma unroll
           for (int kk = 0; kk < kChunk / 16; ++kk)
             mma_bf16_tmem_a(tmem0 + kColAcc2, tmem0 + kColH + (j & 1) * 32 + kk * 8, desc_kmajor_sw128(b0) + 2 * kk,
                             idesc, (j | kk) != 0);
-          if (j + 2 < kChunks) mma1(j + 2, wc + 2);
-          mma_commit(&s.w_empty[wc % kWStages]);
+          mma_commit(&s.w2_empty[st]);
+          if (j + 2 < kChunks && !mma1(j + 2, wc + 2)) { ok = false; break; }
           if (j == kChunks - 3) mma_commit(&s.zt_free);  // the tile's last first product is issued
         }
         if (!ok) break;
