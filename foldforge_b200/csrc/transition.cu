@@ -20,9 +20,10 @@
 //
 // TMEM columns: Z 0..63 (bf16 pairs) | A1[0] 64..191 | A1[1] 192..319 | H[0] 320..351 |
 // H[1] 352..383 | ACC2 384..511.
-// Warps 0..7: SwiGLU and residual, two warps per TMEM lane quarter (warp / 4 = which half of
-// a chunk's hidden units, and of the output channels); warps 0..3 also normalise the tile's
-// rows into Z; warp 8: TMA; warp 9: MMA issue.
+// Warps 0..15: Z staging, SwiGLU and residual, four warps per TMEM lane quarter (warp / 4 =
+// which 16 of a chunk's hidden units, which 32 of the channels of Z and of the output; the
+// row's LayerNorm sums, taken about its channel 0, are combined over the four through shared
+// memory); warp 16: TMA; warp 17: MMA issue.
 #include "../../include/foldforge_b200.h"
 #include "abi_util.h"
 #include "common.cuh"
@@ -36,7 +37,7 @@ constexpr int kHidden = 512;
 constexpr int kChunk = 64;
 constexpr int kChunks = kHidden / kChunk;
 constexpr int kRows = 128;
-constexpr int kThreads = 320;
+constexpr int kThreads = 576;  // 16 SwiGLU / residual warps, TMA warp 16, MMA warp 17
 constexpr int kWStages = 3;
 constexpr size_t kW1Chunk = 128 * kC * 2;      // 32 KB: [64 a | 64 b] x 128, two SW128 K-blocks
 constexpr size_t kW2Chunk = kC * kChunk * 2;   // 16 KB: 128 out x 64 hidden, SW128
@@ -53,6 +54,8 @@ struct Smem {
   uint64_t z_full[2], z_empty[2];
   uint64_t w1_full[kWStages], w1_empty[kWStages];  // first-product weight chunks
   uint64_t w2_full[kWStages], w2_empty[kWStages];  // second-product weight chunks
+  float2 zx[2][4][kRows];   // LayerNorm partial sums of a row's four channel quarters, by tile parity
+  uint64_t zx_bar[2][4];    // a lane quarter's four partial sums written, by tile parity
   uint64_t zt_full, zt_free;
   uint64_t a1_full[2], h_full[2];
   uint64_t acc2_full, acc2_free;
@@ -70,6 +73,12 @@ struct Params {
   int masked_zero;
   int* err;
 };
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
 
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
@@ -95,7 +104,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.z_full[i], 1);
       mbar_init(&s.z_empty[i], 1);
       mbar_init(&s.a1_full[i], 1);
-      mbar_init(&s.h_full[i], 8);
+      mbar_init(&s.h_full[i], 16);
     }
     for (int i = 0; i < kWStages; ++i) {
       mbar_init(&s.w1_full[i], 1);
@@ -103,10 +112,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.w2_full[i], 1);
       mbar_init(&s.w2_empty[i], 1);
     }
-    mbar_init(&s.zt_full, 4);
+    mbar_init(&s.zt_full, 16);
+    for (int i = 0; i < 8; ++i) mbar_init(&s.zx_bar[i / 4][i % 4], 4);
     mbar_init(&s.zt_free, 1);
     mbar_init(&s.acc2_full, 1);
-    mbar_init(&s.acc2_free, 8);
+    mbar_init(&s.acc2_free, 16);
     fence_mbar_init();
   }
   {
@@ -122,7 +132,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem0 = s.tmem_base;
 
-  if (warp == 8) {
+  if (warp == 16) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       tma_prefetch_map(&map_z);
@@ -181,7 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(&s.w2_full[i % kWStages], (i / kWStages) & 1, p.err, kErrTimeoutLoad);
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == 17) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16_f32(128, 128);
@@ -232,57 +242,74 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ SwiGLU / residual warps
-    const int part = warp / 4;  // hidden units [32 part, 32 part + 32) of each chunk; output channels [64 part, +64)
+    // warp w: lane quarter w % 4 (TMEM lanes = the tile's rows); part w / 4 takes 16 of a
+    // chunk's 64 hidden units and 32 of the 128 channels of Z and of the output
+    const int part = warp / 4;
     const int t = (warp & 3) * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tl = tmem0 + lane_off;
+    const int kb = part / 2, cb = (part % 2) * 32;  // this part's channels: z-tile K-block kb, columns cb..cb+31
     bool ok = true;
     // row t of tile ti, LayerNorm-normalised (no affine: gamma and beta are in the weights),
-    // into Z (warps 0..3)
+    // into Z; the row's sums, taken about its channel 0, are combined over the four parts
+    // through shared memory
     auto stage_z = [&](int ti) {
       const int zb = ti & 1;
       bool w = mbar_wait(&s.z_full[zb], (ti >> 1) & 1, p.err, kErrTimeoutLoad);
       if (ti > 0) w = w && mbar_wait(&s.zt_free, (ti - 1) & 1, p.err, kErrTimeoutMma);
-      if (!__all_sync(0xFFFFFFFFu, w)) {
+      const bool good = __all_sync(0xFFFFFFFFu, w);
+      const uint8_t* zt = s.z[zb] + kb * 16384;
+      uint32_t zw[16];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 v = *reinterpret_cast<const uint4*>(zt + sw128_offset(t, cb + q * 8));
+        zw[4 * q] = v.x;
+        zw[4 * q + 1] = v.y;
+        zw[4 * q + 2] = v.z;
+        zw[4 * q + 3] = v.w;
+      }
+      const float shift = bf16_lo(*reinterpret_cast<const uint32_t*>(s.z[zb] + sw128_offset(t, 0)));
+      const uint64_t sh = f32x2(-shift, -shift);
+      uint64_t a1 = f32x2(0.f, 0.f), a2 = f32x2(0.f, 0.f);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint64_t d = add_f32x2(f32x2(bf16_lo(zw[i]), bf16_hi(zw[i])), sh);
+        a1 = add_f32x2(a1, d);
+        a2 = fma_f32x2(d, d, a2);
+      }
+      float s1a, s1b, s2a, s2b;
+      f32x2_split(a1, s1a, s1b);
+      f32x2_split(a2, s2a, s2b);
+      s.zx[zb][part][t] = make_float2(s1a + s1b, s2a + s2b);
+      // the quarter's four warps (bounded wait: a warp that left on an error cannot hold the others)
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.zx_bar[zb][warp & 3]);
+      const bool wx =
+          __all_sync(0xFFFFFFFFu, mbar_wait(&s.zx_bar[zb][warp & 3], (ti >> 1) & 1, p.err, kErrTimeoutEmpty));
+      float t1 = 0.f, t2 = 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 v = s.zx[zb][k][t];
+        t1 += v.x;
+        t2 += v.y;
+      }
+      const float m1 = t1 * (1.0f / kC);
+      const float var = fmaxf(t2 * (1.0f / kC) - m1 * m1, 0.f);
+      const float rstd = rsqrtf(var + 1e-5f);
+      const float nm = -(shift + m1) * rstd;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) zw[i] = pack_bf16(fmaf(bf16_lo(zw[i]), rstd, nm), fmaf(bf16_hi(zw[i]), rstd, nm));
+      if (!good || !wx) {
         ok = false;
         return;
       }
-      tc_fence_after();
-      const uint8_t* zt = s.z[zb];
-      uint32_t zw[64];
-      float sum = 0.f;
-#pragma unroll
-      for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const uint4 v = *reinterpret_cast<const uint4*>(zt + kb * 16384 + sw128_offset(t, q * 8));
-          const int w0 = (kb * 8 + q) * 4;
-          zw[w0] = v.x;
-          zw[w0 + 1] = v.y;
-          zw[w0 + 2] = v.z;
-          zw[w0 + 3] = v.w;
-        }
-#pragma unroll
-      for (int i = 0; i < 64; ++i) sum += bf16_lo(zw[i]) + bf16_hi(zw[i]);
-      const float mean = sum * (1.0f / kC);
-      float q2 = 0.f;
-#pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float a = bf16_lo(zw[i]) - mean, b = bf16_hi(zw[i]) - mean;
-        q2 += a * a + b * b;
-      }
-      const float rstd = rsqrtf(q2 * (1.0f / kC) + 1e-5f);
-      const float nm = -mean * rstd;
-#pragma unroll
-      for (int i = 0; i < 64; ++i) zw[i] = pack_bf16(fmaf(bf16_lo(zw[i]), rstd, nm), fmaf(bf16_hi(zw[i]), rstd, nm));
-      tmem_st32(tl + kColZ, *reinterpret_cast<uint32_t(*)[32]>(zw));
-      tmem_st32(tl + kColZ + 32, *reinterpret_cast<uint32_t(*)[32]>(zw + 32));
+      tmem_st16(tl + kColZ + part * 16, zw);
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.zt_full);
     };
-    if (part == 0 && my_tiles > 0) stage_z(0);
+    if (my_tiles > 0) stage_z(0);
     for (int ti = 0; ti < my_tiles; ++ti) {
       const int zb = ti & 1;
       const int64_t row = (static_cast<int64_t>(blockIdx.x) + static_cast<int64_t>(ti) * gridDim.x) * kRows + t;
@@ -293,33 +320,39 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        uint32_t va[32], vb[32];
-        tmem_ld32(tl + kColA1 + (j & 1) * 128 + part * 32, va);
-        tmem_ld32(tl + kColA1 + (j & 1) * 128 + 64 + part * 32, vb);
+        uint32_t va[16], vb[16];
+        tmem_ld16(tl + kColA1 + (j & 1) * 128 + part * 16, va);
+        tmem_ld16(tl + kColA1 + (j & 1) * 128 + 64 + part * 16, vb);
         tmem_ld_wait();
-        const float* bs = s.bias + j * 128 + part * 32;
-        uint32_t hw[16];
+        const float4* bs4 = reinterpret_cast<const float4*>(s.bias + j * 128 + part * 16);
+        uint32_t hw[8];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int c = 2 * i;
-          // h = a / 2 (the a rows carry the 1/2), b; silu(a) b = (h + h tanh h) b
-          const uint64_t hh = add_f32x2(f32x2(__uint_as_float(va[c]), __uint_as_float(va[c + 1])), f32x2(bs[c], bs[c + 1]));
-          const uint64_t b = add_f32x2(f32x2(__uint_as_float(vb[c]), __uint_as_float(vb[c + 1])), f32x2(bs[64 + c], bs[65 + c]));
-          float h0, h1;
-          f32x2_split(hh, h0, h1);
-          const uint64_t sa = fma_f32x2(hh, f32x2(tanh_fast(h0), tanh_fast(h1)), hh);
-          float o0, o1;
-          f32x2_split(mul_f32x2(sa, b), o0, o1);
-          hw[i] = pack_bf16(o0, o1);
+        for (int q = 0; q < 4; ++q) {
+          const float4 ba = bs4[q], bb = bs4[16 + q];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int c = 4 * q + 2 * e;
+            // h = a / 2 (the a rows carry the 1/2), b; silu(a) b = (h + h tanh h) b
+            const uint64_t hh = add_f32x2(f32x2(__uint_as_float(va[c]), __uint_as_float(va[c + 1])),
+                                          e == 0 ? f32x2(ba.x, ba.y) : f32x2(ba.z, ba.w));
+            const uint64_t b = add_f32x2(f32x2(__uint_as_float(vb[c]), __uint_as_float(vb[c + 1])),
+                                         e == 0 ? f32x2(bb.x, bb.y) : f32x2(bb.z, bb.w));
+            float h0, h1;
+            f32x2_split(hh, h0, h1);
+            const uint64_t sa = fma_f32x2(hh, f32x2(tanh_fast(h0), tanh_fast(h1)), hh);
+            float o0, o1;
+            f32x2_split(mul_f32x2(sa, b), o0, o1);
+            hw[c / 2] = pack_bf16(o0, o1);
+          }
         }
-        tmem_st16(tl + kColH + (j & 1) * 32 + part * 16, hw);
+        tmem_st8(tl + kColH + (j & 1) * 32 + part * 8, hw);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s.h_full[j & 1]);
       }
       // the next tile's statistics and Z, so its first products overlap this residual
-      if (part == 0 && ok && ti + 1 < my_tiles) stage_z(ti + 1);
+      if (ok && ti + 1 < my_tiles) stage_z(ti + 1);
       // residual: z (staged tile) + ACC2 written over the tile, then one TMA store
       if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.acc2_full, ti & 1, p.err, kErrTimeoutMma));
       if (ok) {
@@ -331,34 +364,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int64_t b = bi / p.R, i = bi - b * p.R;
           keep = p.mask[b * p.N + p.row0 + i] && p.mask[b * p.N + jj];
         }
-        uint8_t* zt = s.z[zb];
-#pragma unroll 1
-        for (int cc = 0; cc < 64; cc += 32) {
-          uint32_t vo[32];
-          tmem_ld32(tl + kColAcc2 + part * 64 + cc, vo);
-          tmem_ld_wait();
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int ch = part * 64 + cc + q * 8;
-            uint8_t* addr = zt + (ch / 64) * 16384 + sw128_offset(t, ch % 64);
-            const uint4 zv = *reinterpret_cast<const uint4*>(addr);
-            const uint32_t zw[4] = {zv.x, zv.y, zv.z, zv.w};
-            uint32_t o[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float d0 = keep ? __uint_as_float(vo[q * 8 + 2 * e]) : 0.f;
-              const float d1 = keep ? __uint_as_float(vo[q * 8 + 2 * e + 1]) : 0.f;
-              o[e] = pack_bf16(bf16_lo(zw[e]) + d0, bf16_hi(zw[e]) + d1);
-            }
-            *reinterpret_cast<uint4*>(addr) = make_uint4(o[0], o[1], o[2], o[3]);
-          }
-        }
+        uint8_t* zt = s.z[zb] + kb * 16384;
+        uint32_t vo[32];
+        tmem_ld32(tl + kColAcc2 + part * 32, vo);
+        tmem_ld_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s.acc2_free);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint8_t* addr = zt + sw128_offset(t, cb + q * 8);
+          const uint4 zv = *reinterpret_cast<const uint4*>(addr);
+          const uint32_t zw[4] = {zv.x, zv.y, zv.z, zv.w};
+          uint32_t o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float d0 = keep ? __uint_as_float(vo[q * 8 + 2 * e]) : 0.f;
+            const float d1 = keep ? __uint_as_float(vo[q * 8 + 2 * e + 1]) : 0.f;
+            o[e] = pack_bf16(bf16_lo(zw[e]) + d0, bf16_hi(zw[e]) + d1);
+          }
+          *reinterpret_cast<uint4*>(addr) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
       }
       fence_async_smem();
-      ok = !named_barrier_or(1, 256, !ok);  // uniform over the eight warps from here on
+      ok = !named_barrier_or(1, 512, !ok);  // uniform over the sixteen warps from here on
       if (threadIdx.x == 0) {
         if (ok) {
           const int r0 = static_cast<int>(row - t);
