@@ -68,6 +68,15 @@ SIGNATURES: dict[str, list] = {
     "ffb_apb_single_workspace_bytes": [c_int],
     "ffb_apb_shard_single": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_float, c_void_p, c_void_p,
                              ctypes.c_size_t, c_int, c_int, c_void_p],
+    # row-shard exchanges over NVLink peer memory (CUDA IPC buffers)
+    "ffb_p2p_handle_bytes": [],
+    "ffb_p2p_alloc": [ctypes.c_size_t, ctypes.POINTER(c_void_p), c_void_p],
+    "ffb_p2p_open": [c_void_p, ctypes.POINTER(c_void_p)],
+    "ffb_p2p_close": [c_void_p],
+    "ffb_p2p_free": [c_void_p],
+    "ffb_shard_transpose_p2p": [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p],
+    "ffb_shard_gather_p2p": [c_void_p, ctypes.c_size_t, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p],
+    "ffb_shard_wait_p2p": [c_void_p, c_void_p, c_int, c_void_p],
 }
 
 #: entry points that return a size_t instead of a status
@@ -130,6 +139,7 @@ LAUNCHES = {
     "ffb_triattn_shard_proj": 1, "ffb_triattn_shard_attn": 1, "ffb_triattn_shard_out": 1,
     "ffb_transition_shard_fwd": 1, "ffb_apb_shard_pair_bias": 1, "ffb_apb_shard_single": 4,
     "ffb_single_transition_fwd_noalloc": 3,
+    "ffb_shard_transpose_p2p": 1, "ffb_shard_gather_p2p": 1, "ffb_shard_wait_p2p": 1,
 }
 launch_count = 0
 

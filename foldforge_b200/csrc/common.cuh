@@ -33,6 +33,7 @@ enum DeviceError : int {
   kErrTimeoutEmpty = 103,  // a consumer never released a stage
   kErrTimeoutStore = 104,
   kErrBadLaunch = 105,     // launch geometry the kernel was not written for
+  kErrTimeoutPeer = 106,   // another rank never signalled an exchange
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -1,0 +1,214 @@
+// Row-shard exchanges over NVLink peer memory: the pair transpose (the all-to-all between the
+// row-wise and the column-wise ops) and the all-gather over rows, written by one kernel
+// straight into the peers' buffers in their final layout, plus a bounded wait for the peers'
+// writes. No counterpart in the reference (FoldForge has no multi-GPU Pairformer).
+//
+// Buffers are plain cudaMalloc allocations shared through CUDA IPC handles (no multicast
+// object is created or bound); each rank maps its peers' buffers with
+// cudaIpcOpenMemHandle and passes the peer base addresses to the kernels as a device array.
+//
+// Signalling: every exchange kernel ends with its last CTA (an arrival counter in the
+// rank's `sync` words) fencing at system scope and storing a new epoch, with release
+// semantics, into slot [rank] of every peer's flag array (its own included). The epoch is
+// counted on the device (sync[1]), so a CUDA graph replaying the exchange signals new
+// epochs. ffb_shard_wait_p2p then waits, with acquire loads and a bounded spin, until
+// every slot of this rank's flags has reached the epoch: the peers' writes into this
+// rank's buffers are then visible. A wait that runs out records kErrTimeoutPeer in the
+// device error word and returns; it never traps.
+//
+// The kernels assume one rank per GPU (they wait on other ranks' kernels, which need not
+// run concurrently on a shared GPU): the host uses this path only then.
+#include "../../include/foldforge_b200.h"
+#include "abi_util.h"
+#include "common.cuh"
+
+namespace ffb {
+namespace {
+
+constexpr int kMaxRanks = 8;
+constexpr int kXThreads = 256;
+constexpr long long kPeerWaitCycles = 4000000000ll;  // ~2 s
+
+// The last CTA of the grid publishes a new epoch to every peer's flag slot [rank].
+__device__ __forceinline__ void signal_peers(const uint64_t* flag_ptrs, uint32_t* sync, int rank, int P) {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");  // this thread's peer stores before the arrival
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t done;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(done) : "l"(sync) : "memory");
+    if (done + 1 == gridDim.x) {
+      sync[0] = 0;  // arrival counter ready for the next launch
+      const uint32_t e = sync[1] + 1;
+      sync[1] = e;
+      asm volatile("fence.acq_rel.sys;" ::: "memory");
+      for (int q = 0; q < P; ++q) {
+        uint32_t* slot = reinterpret_cast<uint32_t*>(flag_ptrs[q]) + rank;
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(slot), "r"(e) : "memory");
+      }
+    }
+  }
+}
+
+// x: this rank's pair rows [R][N][128] bf16 (global rows row0 + i). Pair (i, c), c = q R + a,
+// goes to rank q's receive buffer at [a][row0 + i]: the rows of z^T that rank q holds.
+__global__ void __launch_bounds__(kXThreads) pair_transpose_scatter_kernel(const uint4* __restrict__ x,
+                                                                           const uint64_t* __restrict__ dst,
+                                                                           const uint64_t* __restrict__ flag_ptrs,
+                                                                           uint32_t* sync, int R, int N, int row0,
+                                                                           int rank, int P) {
+  __shared__ uint64_t sdst[kMaxRanks];
+  if (threadIdx.x < P) sdst[threadIdx.x] = dst[threadIdx.x];
+  __syncthreads();
+  const int64_t pairs = static_cast<int64_t>(R) * N;
+  const int part = threadIdx.x & 15;  // 16-byte chunk of the 256-byte pair
+  const int64_t stride = (static_cast<int64_t>(gridDim.x) * kXThreads) >> 4;
+  int64_t p0 = (static_cast<int64_t>(blockIdx.x) * kXThreads + threadIdx.x) >> 4;
+  constexpr int kUnroll = 4;
+  for (; p0 < pairs; p0 += kUnroll * stride) {
+    uint4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t pp = p0 + u * stride;
+      if (pp < pairs) v[u] = x[pp * 16 + part];
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t pp = p0 + u * stride;
+      if (pp < pairs) {
+        const int i = static_cast<int>(pp / N), c = static_cast<int>(pp - static_cast<int64_t>(i) * N);
+        const int q = c / R, a = c - q * R;
+        uint4* d = reinterpret_cast<uint4*>(sdst[q]);
+        d[(static_cast<int64_t>(a) * N + row0 + i) * 16 + part] = v[u];
+      }
+    }
+  }
+  signal_peers(flag_ptrs, sync, rank, P);
+}
+
+// src: this rank's chunk of `bytes` (a multiple of 16); copied to offset rank * bytes of every
+// rank's gather buffer (dst[q]), so the buffers end up as the rank-ordered concatenation.
+__global__ void __launch_bounds__(kXThreads) row_gather_kernel(const uint4* __restrict__ src,
+                                                               const uint64_t* __restrict__ dst,
+                                                               const uint64_t* __restrict__ flag_ptrs, uint32_t* sync,
+                                                               int64_t words, int rank, int P) {
+  __shared__ uint64_t sdst[kMaxRanks];
+  if (threadIdx.x < P) sdst[threadIdx.x] = dst[threadIdx.x];
+  __syncthreads();
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kXThreads;
+  for (int64_t w = static_cast<int64_t>(blockIdx.x) * kXThreads + threadIdx.x; w < words; w += stride) {
+    const uint4 v = src[w];
+    for (int q = 0; q < P; ++q) reinterpret_cast<uint4*>(sdst[q])[static_cast<int64_t>(rank) * words + w] = v;
+  }
+  signal_peers(flag_ptrs, sync, rank, P);
+}
+
+// One thread per rank q: wait until flags[q] has reached this rank's current epoch.
+__global__ void shard_wait_kernel(const uint32_t* flags, const uint32_t* sync, int P, int* err) {
+  const int q = threadIdx.x;
+  if (q >= P) return;
+  const uint32_t e = sync[1];
+  const long long start = clock64();
+  while (true) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + q) : "memory");
+    if (static_cast<int32_t>(v - e) >= 0) break;
+    if (clock64() - start > kPeerWaitCycles || error_raised(err)) {
+      set_error(err, kErrTimeoutPeer);
+      break;
+    }
+    __nanosleep(200);
+  }
+}
+
+int exchange_grid(const DeviceInfo& info) { return info.num_sms * 4; }
+
+}  // namespace
+}  // namespace ffb
+
+using namespace ffb;
+
+extern "C" {
+
+int ffb_p2p_alloc(size_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes == 0) return fail(FFB_ERR_ARG, "p2p_alloc: null pointer or zero size");
+  void* p = nullptr;
+  int st = cuda_status(static_cast<int>(cudaMalloc(&p, bytes)), "p2p_alloc: cudaMalloc");
+  if (st) return st;
+  st = cuda_status(static_cast<int>(cudaMemset(p, 0, bytes)), "p2p_alloc: cudaMemset");
+  if (st) {
+    cudaFree(p);
+    return st;
+  }
+  cudaIpcMemHandle_t h;
+  st = cuda_status(static_cast<int>(cudaIpcGetMemHandle(&h, p)), "p2p_alloc: cudaIpcGetMemHandle");
+  if (st) {
+    cudaFree(p);
+    return st;
+  }
+  memcpy(handle, &h, sizeof(h));
+  *ptr = p;
+  return FFB_OK;
+}
+
+int ffb_p2p_handle_bytes(void) { return static_cast<int>(sizeof(cudaIpcMemHandle_t)); }
+
+int ffb_p2p_open(const void* handle, void** ptr) {
+  if (!ptr || !handle) return fail(FFB_ERR_ARG, "p2p_open: null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return cuda_status(static_cast<int>(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess)),
+                     "p2p_open: cudaIpcOpenMemHandle");
+}
+
+int ffb_p2p_close(void* ptr) {
+  if (!ptr) return FFB_OK;
+  return cuda_status(static_cast<int>(cudaIpcCloseMemHandle(ptr)), "p2p_close: cudaIpcCloseMemHandle");
+}
+
+int ffb_p2p_free(void* ptr) {
+  if (!ptr) return FFB_OK;
+  return cuda_status(static_cast<int>(cudaFree(ptr)), "p2p_free: cudaFree");
+}
+
+int ffb_shard_transpose_p2p(const void* x, const void* dst_ptrs, const void* flag_ptrs, void* sync, int R, int N,
+                            int row0, int rank, int P, void* stream) {
+  if (!x || !dst_ptrs || !flag_ptrs || !sync) return fail(FFB_ERR_ARG, "shard_transpose_p2p: null pointer");
+  if (P < 1 || P > kMaxRanks || rank < 0 || rank >= P || R <= 0 || N != R * P || row0 != rank * R)
+    return fail(FFB_ERR_ARG, "shard_transpose_p2p: R=%d N=%d row0=%d rank=%d P=%d", R, N, row0, rank, P);
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) != 0) return fail(FFB_ERR_ARG, "shard_transpose_p2p: misaligned x");
+  DeviceInfo info;
+  int st = device_info(&info);
+  if (st != FFB_OK) return st;
+  pair_transpose_scatter_kernel<<<exchange_grid(info), kXThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(x), static_cast<const uint64_t*>(dst_ptrs), static_cast<const uint64_t*>(flag_ptrs),
+      static_cast<uint32_t*>(sync), R, N, row0, rank, P);
+  return cuda_status(static_cast<int>(cudaGetLastError()), "shard_transpose_p2p launch");
+}
+
+int ffb_shard_gather_p2p(const void* src, size_t bytes, const void* dst_ptrs, const void* flag_ptrs, void* sync,
+                         int rank, int P, void* stream) {
+  if (!src || !dst_ptrs || !flag_ptrs || !sync) return fail(FFB_ERR_ARG, "shard_gather_p2p: null pointer");
+  if (P < 1 || P > kMaxRanks || rank < 0 || rank >= P || bytes == 0 || bytes % 16 != 0)
+    return fail(FFB_ERR_ARG, "shard_gather_p2p: bytes=%zu rank=%d P=%d", bytes, rank, P);
+  if ((reinterpret_cast<uintptr_t>(src) & 15u) != 0) return fail(FFB_ERR_ARG, "shard_gather_p2p: misaligned src");
+  DeviceInfo info;
+  int st = device_info(&info);
+  if (st != FFB_OK) return st;
+  row_gather_kernel<<<exchange_grid(info), kXThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(src), static_cast<const uint64_t*>(dst_ptrs), static_cast<const uint64_t*>(flag_ptrs),
+      static_cast<uint32_t*>(sync), static_cast<int64_t>(bytes / 16), rank, P);
+  return cuda_status(static_cast<int>(cudaGetLastError()), "shard_gather_p2p launch");
+}
+
+int ffb_shard_wait_p2p(const void* flags, const void* sync, int P, void* stream) {
+  if (!flags || !sync) return fail(FFB_ERR_ARG, "shard_wait_p2p: null pointer");
+  if (P < 1 || P > kMaxRanks) return fail(FFB_ERR_ARG, "shard_wait_p2p: P=%d", P);
+  DeviceInfo info;
+  int st = device_info(&info);
+  if (st != FFB_OK) return st;
+  shard_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const uint32_t*>(flags),
+                                                                       static_cast<const uint32_t*>(sync), P, info.err);
+  return cuda_status(static_cast<int>(cudaGetLastError()), "shard_wait_p2p launch");
+}
+
+}  // extern "C"

@@ -35,13 +35,117 @@ _LOG2E = 1.4426950408889634
 
 
 # --------------------------------------------------------------------------- communication
+class _CudaArray:
+    """A raw device allocation exposed to ``torch.as_tensor`` (CUDA array interface, no copy)."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3}
+
+
+class _PeerBuffer:
+    """A device buffer of ``nbytes`` on every rank, each rank's mapped in all the others
+    (CUDA IPC through the C ABI; handles exchanged over the group). ``local`` is this rank's
+    buffer as a uint8 tensor; ``ptrs(offset)`` a device array of the P ranks' addresses."""
+
+    def __init__(self, comm: "ShardComm", nbytes: int, device: torch.device):
+        lib = _lib.load()
+        hb = int(lib.ffb_p2p_handle_bytes())
+        self.comm, self.nbytes, self.device = comm, nbytes, device
+        self.base = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * hb)()
+        _lib.call("ffb_p2p_alloc", ctypes.c_size_t(nbytes), ctypes.byref(self.base), handle)
+        mine = torch.tensor(list(handle), dtype=torch.uint8, device=device)
+        everyone = torch.empty(comm.world * hb, dtype=torch.uint8, device=device)
+        dist.all_gather_into_tensor(everyone, mine, group=comm.group)
+        everyone = everyone.view(comm.world, hb).cpu()
+        self.addrs, self.opened = [], []
+        for q in range(comm.world):
+            if q == comm.rank:
+                self.addrs.append(self.base.value)
+                continue
+            h = (ctypes.c_uint8 * hb)(*everyone[q].tolist())
+            peer = ctypes.c_void_p()
+            _lib.call("ffb_p2p_open", h, ctypes.byref(peer))
+            self.addrs.append(peer.value)
+            self.opened.append(peer)
+        self.local = torch.as_tensor(_CudaArray(self.base.value, nbytes), device=device)
+
+    def ptrs(self, offset: int = 0) -> Tensor:
+        return torch.tensor([a + offset for a in self.addrs], dtype=torch.int64, device=self.device)
+
+    def close(self) -> None:
+        for peer in self.opened:
+            _lib.call("ffb_p2p_close", peer)
+        self.opened = []
+
+
+class _PeerExchange:
+    """The NVLink peer-memory path of :class:`ShardComm` (one rank per GPU): transposes
+    written by one kernel straight into the owning ranks' buffers (two buffers, alternated)
+    and row gathers written into every rank's buffer, each followed by a bounded wait for
+    the peers' writes (``ffb_shard_transpose_p2p`` / ``ffb_shard_gather_p2p`` /
+    ``ffb_shard_wait_p2p``). Buffers are created on first use per shape, collectively (every
+    rank runs the same schedule). A returned tensor aliases an exchange buffer: it is valid
+    until the second-next exchange of its kind."""
+
+    def __init__(self, comm: "ShardComm", device: torch.device):
+        self.comm, self.device = comm, device
+        p = comm.world
+        self.flags = _PeerBuffer(comm, 256, device)   # P uint32 slots per rank
+        self.flag_ptrs = self.flags.ptrs()
+        self.sync = torch.zeros(2, dtype=torch.int32, device=device)  # arrival counter, epoch
+        self.t_bufs: dict[tuple, tuple] = {}
+        self.g_bufs: dict[tuple, tuple] = {}
+        self.parity = 0
+        assert p <= 8
+
+    def _wait(self) -> None:
+        _lib.call("ffb_shard_wait_p2p", _ptr(self.flags.local), _ptr(self.sync), self.comm.world, _stream())
+
+    def transpose(self, x: Tensor) -> Tensor:
+        r, n, c = x.shape
+        key = (r, n, c, x.dtype)
+        if key not in self.t_bufs:
+            one = r * n * c * x.element_size()
+            buf = _PeerBuffer(self.comm, 2 * one, self.device)
+            self.t_bufs[key] = (buf, buf.ptrs(0), buf.ptrs(one), one)
+        buf, p0, p1, one = self.t_bufs[key]
+        b = self.parity
+        self.parity ^= 1
+        x = x.contiguous()
+        _lib.call("ffb_shard_transpose_p2p", _ptr(x), _ptr(p1 if b else p0), _ptr(self.flag_ptrs), _ptr(self.sync),
+                  r, n, self.comm.rank * r, self.comm.rank, self.comm.world, _stream())
+        self._wait()
+        return buf.local[b * one:(b + 1) * one].view(x.dtype).view(r, n, c)
+
+    def gather_rows(self, x: Tensor) -> Tensor:
+        x = x.contiguous()
+        key = (tuple(x.shape), x.dtype)
+        one = x.numel() * x.element_size()
+        if key not in self.g_bufs:
+            buf = _PeerBuffer(self.comm, self.comm.world * one, self.device)
+            self.g_bufs[key] = (buf, buf.ptrs(0))
+        buf, ptrs = self.g_bufs[key]
+        _lib.call("ffb_shard_gather_p2p", _ptr(x), ctypes.c_size_t(one), _ptr(ptrs), _ptr(self.flag_ptrs),
+                  _ptr(self.sync), self.comm.rank, self.comm.world, _stream())
+        self._wait()
+        return buf.local.view(x.dtype).view((self.comm.world * x.shape[0],) + tuple(x.shape[1:]))
+
+    def close(self) -> None:
+        for buf, *_ in list(self.t_bufs.values()) + list(self.g_bufs.values()):
+            buf.close()
+        self.flags.close()
+
+
 class ShardComm:
     """The two collectives of the schedule over one process group.
 
-    NCCL groups exchange device tensors directly; other backends (gloo) exchange host copies.
-    ``world == 1`` (no group) makes both collectives local copies."""
+    With NCCL and one rank per GPU (``peer="auto"``) the exchanges run over NVLink peer
+    memory (:class:`_PeerExchange`: one kernel writes each transpose / gather straight into
+    the peers' buffers); otherwise NCCL collectives on device tensors, or host copies for
+    other backends (gloo). ``world == 1`` (no group) makes both collectives local."""
 
-    def __init__(self, group: dist.ProcessGroup | None = None):
+    def __init__(self, group: dist.ProcessGroup | None = None, *, peer: str = "auto"):
         self.group = group
         if dist.is_available() and dist.is_initialized():
             self.rank = dist.get_rank(group)
@@ -49,6 +153,25 @@ class ShardComm:
             self.nccl = dist.get_backend(group) == "nccl"
         else:
             self.rank, self.world, self.nccl = 0, 1, False
+        self.peer_mode = peer
+        self._peer: _PeerExchange | None = None
+
+    def _peer_path(self, x: Tensor) -> _PeerExchange | None:
+        if self.peer_mode == "off" or self.world == 1 or not self.nccl or not x.is_cuda:
+            return None
+        if self._peer is None:
+            if torch.cuda.device_count() < self.world or self.world > 8:
+                return None  # ranks sharing a GPU: their kernels must not wait on one another
+            self._peer = _PeerExchange(self, x.device)
+        return self._peer
+
+    def close(self) -> None:
+        """Unmap the peers' exchange buffers (call on every rank, before the group is destroyed)."""
+        if self._peer is not None:
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)
+            self._peer.close()
+            self._peer = None
 
     def rows(self, n: int) -> tuple[int, int]:
         """(R, row0) of this rank for a pair of n rows (n must divide evenly)."""
@@ -61,6 +184,9 @@ class ShardComm:
         """Concatenate every rank's ``x`` along dim 0 (rank order)."""
         if self.world == 1:
             return x
+        peer = self._peer_path(x)
+        if peer is not None:
+            return peer.gather_rows(x)
         if self.nccl or not x.is_cuda:
             out = torch.empty((self.world * x.shape[0],) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
             dist.all_gather_into_tensor(out, x.contiguous(), group=self.group)
@@ -76,6 +202,9 @@ class ShardComm:
             return x.transpose(0, 1).contiguous()
         r, n, c = x.shape
         p = self.world
+        peer = self._peer_path(x)
+        if peer is not None and x.dtype == torch.bfloat16 and c == 128:
+            return peer.transpose(x)
         # send[q] = x[:, q R : (q + 1) R] (the block of z^T rows that rank q holds)
         send = x.view(r, p, r, c).permute(1, 0, 2, 3).contiguous()
         if self.nccl or not x.is_cuda:

@@ -202,6 +202,33 @@ int ffb_apb_shard_single(const void* s, const uint8_t* mask, const void* packed,
                          const void* extra_pair_bias, int extra_dtype, float gate_bias, void* out, void* workspace,
                          size_t workspace_bytes, int N, int masked, void* stream);
 
+/* ---- Row-shard exchanges over NVLink peer memory (one rank per GPU of one box). Buffers
+ * are plain device allocations shared through CUDA IPC handles (no multicast object):
+ * ffb_p2p_alloc allocates and zeroes `bytes` on the current device and writes the IPC handle
+ * (ffb_p2p_handle_bytes() bytes) to `handle`; a peer maps it with ffb_p2p_open and unmaps it
+ * with ffb_p2p_close; the owner frees it with ffb_p2p_free once every peer has closed it.
+ * ffb_shard_transpose_p2p: x = this rank's pair rows [R][N][128] bf16 (N = P R, row0 = rank R);
+ * pair (i, q R + a) is written to rank q's buffer dst_ptrs[q] at [a][row0 + i] (the rows of
+ * z^T rank q holds). ffb_shard_gather_p2p: `bytes` (a multiple of 16) from src are written to
+ * every rank's buffer dst_ptrs[q] at offset rank * bytes. Both end by publishing a new epoch
+ * (counted in this rank's `sync` words, two uint32 zeroed at allocation) into slot [rank] of
+ * every rank's flag array (flag_ptrs[q]: P uint32); ffb_shard_wait_p2p makes the stream wait
+ * until every slot of this rank's `flags` has reached this rank's epoch (a bounded wait: a
+ * peer that never signals sets the device error word, code 106, instead of hanging).
+ * dst_ptrs and flag_ptrs are device arrays of P uint64 addresses (peers' mapped addresses,
+ * this rank's own). Every rank issues the same sequence of exchanges; consecutive exchanges
+ * must write different buffers. P <= 8. */
+int ffb_p2p_handle_bytes(void);
+int ffb_p2p_alloc(size_t bytes, void** ptr, void* handle);
+int ffb_p2p_open(const void* handle, void** ptr);
+int ffb_p2p_close(void* ptr);
+int ffb_p2p_free(void* ptr);
+int ffb_shard_transpose_p2p(const void* x, const void* dst_ptrs, const void* flag_ptrs, void* sync, int R, int N,
+                            int row0, int rank, int P, void* stream);
+int ffb_shard_gather_p2p(const void* src, size_t bytes, const void* dst_ptrs, const void* flag_ptrs, void* sync,
+                         int rank, int P, void* stream);
+int ffb_shard_wait_p2p(const void* flags, const void* sync, int P, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -48,11 +48,11 @@ def _rank(rank: int, world: int, port: int, n: int, masked: int, zero: bool) -> 
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl" if nccl else "gloo", rank=rank, world_size=world,
                             device_id=dev if nccl else None)
+    comm = ShardComm()
     try:
         state = block_state(torch.Generator().manual_seed(31), scheme="randomise")
         z, s, tokens = inputs(n, 4, masked_suffix=masked)
         zb, sb = z.bfloat16(), s.bfloat16()
-        comm = ShardComm()
         r, row0 = comm.rows(n)
         block = _block(state, "zero" if zero else "compute")
         sharded = ShardedPairformerBlock(block, comm, ops="b200", masked_zero=zero)
@@ -82,6 +82,7 @@ def _rank(rank: int, world: int, port: int, n: int, masked: int, zero: bool) -> 
             assert oracle.rel_l2(z_all, ref_z.float().cpu()) < 1e-2
             assert oracle.rel_l2(s_out, ref_s.float().cpu()) < 1e-2
     finally:
+        comm.close()
         dist.barrier()
         dist.destroy_process_group()
 
@@ -89,3 +90,35 @@ def _rank(rank: int, world: int, port: int, n: int, masked: int, zero: bool) -> 
 @pytest.mark.parametrize("n,masked,zero", [(64, 5, False), (256, 13, True)])
 def test_two_rank_sharded_block(n, masked, zero):
     mp.spawn(_rank, args=(2, _free_port(), n, masked, zero), nprocs=2, join=True)
+
+
+def _exchange_rank(rank: int, world: int, port: int) -> None:
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    peer = ShardComm()
+    try:
+        ref = ShardComm(peer="off")
+        n = 40 * world
+        r, row0 = peer.rows(n)
+        g = torch.Generator().manual_seed(100 + rank)
+        for rep in range(3):  # alternating transpose buffers, interleaved gathers
+            x = torch.randn(r, n, 128, generator=g).bfloat16().to(dev)
+            small = torch.randn(r, 4, 48, generator=g).bfloat16().to(dev)
+            y, y_ref = peer.transpose(x).clone(), ref.transpose(x)
+            assert torch.equal(y, y_ref)
+            assert torch.equal(peer.gather_rows(small).clone(), ref.gather_rows(small))
+            assert torch.equal(peer.transpose(y).clone(), x)
+        assert peer._peer is not None  # the peer-memory path ran
+        assert _lib.device_error() == 0
+    finally:
+        peer.close()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="the peer-memory exchange needs one GPU per rank")
+def test_peer_memory_exchanges_match_nccl():
+    mp.spawn(_exchange_rank, args=(2, _free_port()), nprocs=2, join=True)
