@@ -15,9 +15,10 @@ activations. One step = one trunk pass over one input.
   cores, one block at N = 512, times 48.
 
 ``--gpus N`` (torchrun, one rank per GPU, N > 1): the pair is ROW-SHARDED across the ranks
-(axial parallelism, ``foldforge_b200/engine/sharded.py``: NCCL all-to-all transposes between
-the row-wise and column-wise triangle ops, all-gathers of the TriMul right operand and the
-attention biases; the single track replicated). ``value`` is ms per 48-block trunk pass of
+(axial parallelism, ``foldforge_b200/engine/sharded.py``: pair transposes between the row-wise
+and column-wise triangle ops and row gathers of the TriMul right operand and the attention
+biases, each written by one kernel straight into the peers' buffers over NVLink (CUDA IPC
+peer memory, bounded waits); the single track replicated). ``value`` is ms per 48-block trunk pass of
 the whole job (max over ranks) at N = 512 P^(1/3) rounded to a multiple of 8 P tokens (640,
 800, 1024 on 2, 4, 8 GPUs): per-GPU work held at the N = 512 trunk's, ``scaling`` weak, so
 value(1) / value(P) is the weak-scaling efficiency. ``ladder`` reports the benchmark's
@@ -520,8 +521,8 @@ def run_sharded(args, rank: int, world: int, local: int, dist) -> None:
                             f"{n_w ** 3 / world / N_TOKENS ** 3:.2f} x the N=512 trunk), last {masked_w} tokens "
                             "masked, master precision, eager launches",
                 "model": "AF3 Pairformer block (c_z 128, c_s 384, 4x32 / 16x24 heads)",
-                "global_batch": 1, "seq_len": n_w, "parallelism": f"axial row-sharding x{world} (NCCL all-to-all / "
-                                                                  "all-gather)",
+                "global_batch": 1, "seq_len": n_w, "parallelism": f"axial row-sharding x{world} (NVLink peer-memory "
+                                                                  "transposes / row gathers)",
                 "l2": "flushed by a 256 MB write before every timed step",
                 "trunk_tflops": round(block_flops(n_w) * nb / (value_ms * 1e-3) / 1e12, 1),
                 "ms_per_block": round(value_ms / nb, 4),
@@ -541,6 +542,7 @@ def run_sharded(args, rank: int, world: int, local: int, dist) -> None:
         if ladder is not None:
             line["ladder"] = ladder
         print(json.dumps(line), flush=True)
+    comm.close()  # every rank: unmap the peers' exchange buffers before the group goes
 
 
 def kernels_once(n: int) -> None:

@@ -77,6 +77,8 @@ SIGNATURES: dict[str, list] = {
     "ffb_shard_transpose_p2p": [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p],
     "ffb_shard_gather_p2p": [c_void_p, ctypes.c_size_t, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p],
     "ffb_shard_wait_p2p": [c_void_p, c_void_p, c_int, c_void_p],
+    "ffb_shard_rows_p2p": [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p],
+    "ffb_trimul_channel_contract": [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p],
 }
 
 #: entry points that return a size_t instead of a status
@@ -139,7 +141,8 @@ LAUNCHES = {
     "ffb_triattn_shard_proj": 1, "ffb_triattn_shard_attn": 1, "ffb_triattn_shard_out": 1,
     "ffb_transition_shard_fwd": 1, "ffb_apb_shard_pair_bias": 1, "ffb_apb_shard_single": 4,
     "ffb_single_transition_fwd_noalloc": 3,
-    "ffb_shard_transpose_p2p": 1, "ffb_shard_gather_p2p": 1, "ffb_shard_wait_p2p": 1,
+    "ffb_shard_transpose_p2p": 1, "ffb_shard_gather_p2p": 1, "ffb_shard_wait_p2p": 1, "ffb_shard_rows_p2p": 1,
+    "ffb_trimul_channel_contract": 1,
 }
 launch_count = 0
 

@@ -422,6 +422,18 @@ int ffb_trimul_shard_contract(const void* left, const void* right_all, void* u, 
   return trimul_shard_contract(left, right_all, u, R, N, info, static_cast<cudaStream_t>(stream));
 }
 
+int ffb_trimul_channel_contract(const void* left, const void* right, void* u, int C, int N, void* stream) {
+  if (C <= 0 || C > 128 || N <= 0 || static_cast<int64_t>(C) * N >= (int64_t(1) << 31) - 256)
+    return fail(FFB_ERR_ARG, "trimul_channel_contract: C=%d N=%d", C, N);
+  if (!left || !right || !u) return fail(FFB_ERR_ARG, "trimul_channel_contract: null pointer");
+  if (!aligned16(left) || !aligned16(right) || !aligned16(u))
+    return fail(FFB_ERR_ARG, "trimul_channel_contract: misaligned pointer");
+  DeviceInfo info;
+  int st = device_info(&info);
+  if (st != FFB_OK) return st;
+  return trimul_channel_contract(left, right, u, C, N, info, static_cast<cudaStream_t>(stream));
+}
+
 int ffb_trimul_shard_out(const void* z, const uint8_t* mask, const void* packed, const void* u, const void* zstats,
                          void* ustats, void* out, int R, int N, int row0, int masked, void* stream) {
   int st = shard_args("trimul_shard_out", R, N, row0);

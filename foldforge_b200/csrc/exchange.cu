@@ -102,6 +102,42 @@ __global__ void __launch_bounds__(kXThreads) row_gather_kernel(const uint4* __re
   signal_peers(flag_ptrs, sync, rank, P);
 }
 
+// Row scatters of the channel-sharded TriMul contraction (rows of Np bf16, `row_words`
+// 16-byte words each; cpp = 128 / P channels per rank):
+//   mode 0 (L / R to the channel owners): src [R][128][Np] (this rank's rows i); row (i, c)
+//          goes to rank q = c / cpp at [c % cpp][row0 + i] of its [cpp][N][Np] buffer;
+//   mode 1 (U back to the row owners): src [cpp][N][Np] (this rank's channels c'); row
+//          (c', g) goes to rank q = g / R at [rank cpp + c'][g % R] of its [128][R][Np] buffer.
+__global__ void __launch_bounds__(kXThreads) row_scatter_kernel(const uint4* __restrict__ src,
+                                                                const uint64_t* __restrict__ dst,
+                                                                const uint64_t* __restrict__ flag_ptrs, uint32_t* sync,
+                                                                int mode, int R, int N, int cpp, int row_words,
+                                                                int rank, int P) {
+  __shared__ uint64_t sdst[kMaxRanks];
+  if (threadIdx.x < P) sdst[threadIdx.x] = dst[threadIdx.x];
+  __syncthreads();
+  const int64_t rows = mode == 0 ? static_cast<int64_t>(R) * 128 : static_cast<int64_t>(cpp) * N;
+  const int64_t words = rows * row_words;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kXThreads;
+  for (int64_t w = static_cast<int64_t>(blockIdx.x) * kXThreads + threadIdx.x; w < words; w += stride) {
+    const int64_t r = w / row_words;
+    const int k = static_cast<int>(w - r * row_words);
+    int q;
+    int64_t drow;
+    if (mode == 0) {
+      const int i = static_cast<int>(r / 128), c = static_cast<int>(r % 128);
+      q = c / cpp;
+      drow = static_cast<int64_t>(c - q * cpp) * N + static_cast<int64_t>(rank) * R + i;
+    } else {
+      const int cl = static_cast<int>(r / N), g = static_cast<int>(r % N);
+      q = g / R;
+      drow = static_cast<int64_t>(rank * cpp + cl) * R + (g - q * R);
+    }
+    reinterpret_cast<uint4*>(sdst[q])[drow * row_words + k] = src[w];
+  }
+  signal_peers(flag_ptrs, sync, rank, P);
+}
+
 // One thread per rank q: wait until flags[q] has reached this rank's current epoch.
 __global__ void shard_wait_kernel(const uint32_t* flags, const uint32_t* sync, int P, int* err) {
   const int q = threadIdx.x;
@@ -198,6 +234,22 @@ int ffb_shard_gather_p2p(const void* src, size_t bytes, const void* dst_ptrs, co
       static_cast<const uint4*>(src), static_cast<const uint64_t*>(dst_ptrs), static_cast<const uint64_t*>(flag_ptrs),
       static_cast<uint32_t*>(sync), static_cast<int64_t>(bytes / 16), rank, P);
   return cuda_status(static_cast<int>(cudaGetLastError()), "shard_gather_p2p launch");
+}
+
+int ffb_shard_rows_p2p(const void* src, int mode, int R, int N, const void* dst_ptrs, const void* flag_ptrs,
+                       void* sync, int rank, int P, void* stream) {
+  if (!src || !dst_ptrs || !flag_ptrs || !sync) return fail(FFB_ERR_ARG, "shard_rows_p2p: null pointer");
+  if (P < 1 || P > kMaxRanks || 128 % P != 0 || rank < 0 || rank >= P || R <= 0 || N != R * P || (mode != 0 && mode != 1))
+    return fail(FFB_ERR_ARG, "shard_rows_p2p: mode=%d R=%d N=%d rank=%d P=%d", mode, R, N, rank, P);
+  if ((reinterpret_cast<uintptr_t>(src) & 15u) != 0) return fail(FFB_ERR_ARG, "shard_rows_p2p: misaligned src");
+  DeviceInfo info;
+  int st = device_info(&info);
+  if (st != FFB_OK) return st;
+  const int np = (N + 7) / 8 * 8;
+  row_scatter_kernel<<<exchange_grid(info), kXThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(src), static_cast<const uint64_t*>(dst_ptrs), static_cast<const uint64_t*>(flag_ptrs),
+      static_cast<uint32_t*>(sync), mode, R, N, 128 / P, np / 8, rank, P);
+  return cuda_status(static_cast<int>(cudaGetLastError()), "shard_rows_p2p launch");
 }
 
 int ffb_shard_wait_p2p(const void* flags, const void* sync, int P, void* stream) {

@@ -55,6 +55,8 @@ int trimul_forward(const void* z, const uint8_t* mask, const void* packed, void*
                    int outgoing, int masked_zero, int stages, const DeviceInfo& info, cudaStream_t stream);
 int trimul_shard_proj(const void* z, const uint8_t* mask, const void* packed, void* left, void* right, void* zstats,
                       int R, int N, int row0, const DeviceInfo& info, cudaStream_t stream);
+int trimul_channel_contract(const void* left, const void* right, void* u, int C, int N, const DeviceInfo& info,
+                            cudaStream_t stream);
 int trimul_shard_contract(const void* left, const void* right_all, void* u, int R, int N, const DeviceInfo& info,
                           cudaStream_t stream);
 int trimul_shard_out(const void* z, const uint8_t* mask, const void* packed, const void* u, const void* zstats,

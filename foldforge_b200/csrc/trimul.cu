@@ -698,16 +698,17 @@ int launch_proj(const void* z, const uint8_t* mask, const void* packed, void* le
   return cuda_status(static_cast<int>(cudaGetLastError()), "trimul_proj launch");
 }
 
-// U[c] (R x N) = L[c] (R x N(k)) R[c]^T for the 128 channels of one batch entry per call
-// group; element strides of L / R: channel `lc`, row `lr`; batch `lb` (batch count B).
-int launch_contract(const void* left, const void* right, void* u, int B, int R, int N, int64_t l_c, int64_t l_r,
-                    int64_t r_c, int64_t r_r, const DeviceInfo& info, cudaStream_t stream) {
+// U[c] (R x N) = L[c] (R x N(k)) R[c]^T for `channels` channels of each of B batch entries;
+// element strides of L / R: channel `l_c` / `r_c`, row `l_r` / `r_r` (batch entries follow
+// their channels); U is [B * channels][R][Np].
+int launch_contract(const void* left, const void* right, void* u, int B, int channels, int R, int N, int64_t l_c,
+                    int64_t l_r, int64_t r_c, int64_t r_r, const DeviceInfo& info, cudaStream_t stream) {
   const int np = (N + 7) / 8 * 8;
   CUtensorMap map_l, map_r;
   const int bn = N > 128 ? 256 : 128;
-  const uint64_t ldims[3] = {static_cast<uint64_t>(N), static_cast<uint64_t>(R), static_cast<uint64_t>(B) * kH};
+  const uint64_t ldims[3] = {static_cast<uint64_t>(N), static_cast<uint64_t>(R), static_cast<uint64_t>(B) * channels};
   const uint64_t lstrides[2] = {static_cast<uint64_t>(l_r) * 2, static_cast<uint64_t>(l_c) * 2};
-  const uint64_t rdims[3] = {static_cast<uint64_t>(N), static_cast<uint64_t>(N), static_cast<uint64_t>(B) * kH};
+  const uint64_t rdims[3] = {static_cast<uint64_t>(N), static_cast<uint64_t>(N), static_cast<uint64_t>(B) * channels};
   const uint64_t rstrides[2] = {static_cast<uint64_t>(r_r) * 2, static_cast<uint64_t>(r_c) * 2};
   const uint32_t box_a[3] = {64, 128, 1};
   const uint32_t box_b[3] = {64, static_cast<uint32_t>(bn), 1};
@@ -719,7 +720,7 @@ int launch_contract(const void* left, const void* right, void* u, int B, int R, 
   gp.M = R;
   gp.N = N;
   gp.K = N;
-  gp.batch = B * kH;
+  gp.batch = B * channels;
   gp.D = u;
   gp.ldd = np;
   gp.batch_stride_d = static_cast<int64_t>(R) * np;
@@ -784,7 +785,7 @@ int trimul_forward(const void* z, const uint8_t* mask, const void* packed, void*
     if (st) return st;
   }
   if (stages & 2) {
-    st = launch_contract(left, right, u, B, N, N, s_c, np, s_c, np, info, stream);
+    st = launch_contract(left, right, u, B, kH, N, N, s_c, np, s_c, np, info, stream);
     if (st) return st;
   }
   if (stages & 4) st = launch_out(z, mask, packed, u, zstats, ustats, out, B, N, N, 0, masked_zero, info, stream);
@@ -804,7 +805,16 @@ int trimul_shard_proj(const void* z, const uint8_t* mask, const void* packed, vo
 int trimul_shard_contract(const void* left, const void* right_all, void* u, int R, int N, const DeviceInfo& info,
                           cudaStream_t stream) {
   const int64_t np = (N + 7) / 8 * 8;
-  return launch_contract(left, right_all, u, 1, R, N, np, kH * np, np, kH * np, info, stream);
+  return launch_contract(left, right_all, u, 1, kH, R, N, np, kH * np, np, kH * np, info, stream);
+}
+
+// Channel-sharded contraction: L, R [C][N][Np] (C of the 128 channels, all N rows) ->
+// U [C][N][Np].
+int trimul_channel_contract(const void* left, const void* right, void* u, int C, int N, const DeviceInfo& info,
+                            cudaStream_t stream) {
+  const int64_t np = (N + 7) / 8 * 8;
+  return launch_contract(left, right, u, 1, C, N, N, static_cast<int64_t>(N) * np, np, static_cast<int64_t>(N) * np, np,
+                         info, stream);
 }
 
 int trimul_shard_out(const void* z, const uint8_t* mask, const void* packed, const void* u, const void* zstats,

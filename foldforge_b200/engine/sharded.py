@@ -96,6 +96,7 @@ class _PeerExchange:
         self.sync = torch.zeros(2, dtype=torch.int32, device=device)  # arrival counter, epoch
         self.t_bufs: dict[tuple, tuple] = {}
         self.g_bufs: dict[tuple, tuple] = {}
+        self.r_bufs: dict[tuple, tuple] = {}
         self.parity = 0
         assert p <= 8
 
@@ -131,8 +132,27 @@ class _PeerExchange:
         self._wait()
         return buf.local.view(x.dtype).view((self.comm.world * x.shape[0],) + tuple(x.shape[1:]))
 
+    def channel_rows(self, x: Tensor, mode: int, n: int, tag: str) -> Tensor:
+        """The channel-sharded TriMul's scatters: mode 0 sends L or R rows ``[R][128][Np]`` to
+        the channel owners (returns this rank's ``[C][N][Np]``, C = 128 / P); mode 1 sends U
+        ``[C][N][Np]`` back to the row owners (returns this rank's ``[128][R][Np]``). ``tag``
+        names the buffer (L, R and U each have their own)."""
+        p = self.comm.world
+        r, np_ = n // p, (n + 7) // 8 * 8
+        shape = (128 // p, n, np_) if mode == 0 else (128, r, np_)
+        key = (tag, shape)
+        if key not in self.r_bufs:
+            buf = _PeerBuffer(self.comm, shape[0] * shape[1] * shape[2] * 2, self.device)
+            self.r_bufs[key] = (buf, buf.ptrs(0))
+        buf, ptrs = self.r_bufs[key]
+        x = x.contiguous()
+        _lib.call("ffb_shard_rows_p2p", _ptr(x), mode, r, n, _ptr(ptrs), _ptr(self.flag_ptrs), _ptr(self.sync),
+                  self.comm.rank, p, _stream())
+        self._wait()
+        return buf.local.view(torch.bfloat16).view(shape)
+
     def close(self) -> None:
-        for buf, *_ in list(self.t_bufs.values()) + list(self.g_bufs.values()):
+        for buf, *_ in list(self.t_bufs.values()) + list(self.g_bufs.values()) + list(self.r_bufs.values()):
             buf.close()
         self.flags.close()
 
@@ -145,7 +165,7 @@ class ShardComm:
     the peers' buffers); otherwise NCCL collectives on device tensors, or host copies for
     other backends (gloo). ``world == 1`` (no group) makes both collectives local."""
 
-    def __init__(self, group: dist.ProcessGroup | None = None, *, peer: str = "auto"):
+    def __init__(self, group: dist.ProcessGroup | None = None, *, peer: str = "auto", trimul: str = "auto"):
         self.group = group
         if dist.is_available() and dist.is_initialized():
             self.rank = dist.get_rank(group)
@@ -154,6 +174,7 @@ class ShardComm:
         else:
             self.rank, self.world, self.nccl = 0, 1, False
         self.peer_mode = peer
+        self.trimul_mode = trimul
         self._peer: _PeerExchange | None = None
 
     def _peer_path(self, x: Tensor) -> _PeerExchange | None:
@@ -164,6 +185,16 @@ class ShardComm:
                 return None  # ranks sharing a GPU: their kernels must not wait on one another
             self._peer = _PeerExchange(self, x.device)
         return self._peer
+
+    def trimul_by_channels(self, x: Tensor) -> bool:
+        """Whether the TriMul contraction is sharded by channel: each rank receives L and R for
+        its 128 / P channels over all rows and sends U back to the row owners, 3 (P - 1) / P of
+        the pair per rank instead of the P - 1 rank chunks a gather of the right operand
+        receives; the default for P >= 4 on the peer-memory path (``trimul="channels"`` /
+        ``"rows"`` force either)."""
+        if self.trimul_mode == "rows" or 128 % max(self.world, 1) or self._peer_path(x) is None:
+            return False
+        return self.trimul_mode == "channels" or self.world >= 4
 
     def close(self) -> None:
         """Unmap the peers' exchange buffers (call on every rank, before the group is destroyed)."""
@@ -254,9 +285,18 @@ class B200ShardOps:
         zstats = torch.empty((r, n, 2), dtype=torch.float32, device=dev)
         _lib.call("ffb_trimul_shard_proj", _ptr(z), _ptr(mask), _ptr(packed), _ptr(left), _ptr(right), _ptr(zstats),
                   r, n, row0, _stream())
-        right_all = self.comm.gather_rows(right)
-        u = torch.empty((128, r, np_), dtype=torch.bfloat16, device=dev)
-        _lib.call("ffb_trimul_shard_contract", _ptr(left), _ptr(right_all), _ptr(u), r, n, _stream())
+        if self.comm.trimul_by_channels(z):
+            peer = self.comm._peer
+            cpp = 128 // self.comm.world
+            lc = peer.channel_rows(left, 0, n, "L")
+            rc = peer.channel_rows(right, 0, n, "R")
+            uc = torch.empty((cpp, n, np_), dtype=torch.bfloat16, device=dev)
+            _lib.call("ffb_trimul_channel_contract", _ptr(lc), _ptr(rc), _ptr(uc), cpp, n, _stream())
+            u = peer.channel_rows(uc, 1, n, "U")
+        else:
+            right_all = self.comm.gather_rows(right)
+            u = torch.empty((128, r, np_), dtype=torch.bfloat16, device=dev)
+            _lib.call("ffb_trimul_shard_contract", _ptr(left), _ptr(right_all), _ptr(u), r, n, _stream())
         ustats = torch.empty_like(zstats)
         out = torch.empty_like(z)
         _lib.call("ffb_trimul_shard_out", _ptr(z), _ptr(mask), _ptr(packed), _ptr(u), _ptr(zstats), _ptr(ustats),

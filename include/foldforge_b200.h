@@ -229,6 +229,16 @@ int ffb_shard_gather_p2p(const void* src, size_t bytes, const void* dst_ptrs, co
                          int rank, int P, void* stream);
 int ffb_shard_wait_p2p(const void* flags, const void* sync, int P, void* stream);
 
+/* Channel-sharded TriMul contraction (P >= 4 ranks move less data this way than by gathering
+ * the right operand): rank q owns channels [q C, (q + 1) C), C = 128 / P.
+ * ffb_shard_rows_p2p mode 0: L or R rows [R][128][Np] of this rank -> every rank's
+ * [C][N][Np] buffer (its channels, all rows); mode 1: U [C][N][Np] of this rank's channels ->
+ * every rank's [128][R][Np] buffer (its rows, all channels). Signalling as above.
+ * ffb_trimul_channel_contract: U[c] = L[c] R[c]^T for C channels, L, R, U [C][N][Np] bf16. */
+int ffb_shard_rows_p2p(const void* src, int mode, int R, int N, const void* dst_ptrs, const void* flag_ptrs, void* sync,
+                       int rank, int P, void* stream);
+int ffb_trimul_channel_contract(const void* left, const void* right, void* u, int C, int N, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -39,7 +39,7 @@ def _block(state, masked_update):
     return block.eval()
 
 
-def _rank(rank: int, world: int, port: int, n: int, masked: int, zero: bool) -> None:
+def _rank(rank: int, world: int, port: int, n: int, masked: int, zero: bool, trimul: str) -> None:
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     ngpu = torch.cuda.device_count()
@@ -48,7 +48,7 @@ def _rank(rank: int, world: int, port: int, n: int, masked: int, zero: bool) -> 
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl" if nccl else "gloo", rank=rank, world_size=world,
                             device_id=dev if nccl else None)
-    comm = ShardComm()
+    comm = ShardComm(trimul=trimul)
     try:
         state = block_state(torch.Generator().manual_seed(31), scheme="randomise")
         z, s, tokens = inputs(n, 4, masked_suffix=masked)
@@ -87,9 +87,12 @@ def _rank(rank: int, world: int, port: int, n: int, masked: int, zero: bool) -> 
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("n,masked,zero", [(64, 5, False), (256, 13, True)])
-def test_two_rank_sharded_block(n, masked, zero):
-    mp.spawn(_rank, args=(2, _free_port(), n, masked, zero), nprocs=2, join=True)
+@pytest.mark.parametrize("n,masked,zero,trimul", [(64, 5, False, "auto"), (256, 13, True, "auto"),
+                                                  (192, 9, True, "channels")])
+def test_two_rank_sharded_block(n, masked, zero, trimul):
+    """``trimul="channels"`` forces the channel-sharded TriMul contraction (the default from
+    four ranks on) onto the two ranks, when they have a GPU each."""
+    mp.spawn(_rank, args=(2, _free_port(), n, masked, zero, trimul), nprocs=2, join=True)
 
 
 def _exchange_rank(rank: int, world: int, port: int) -> None:
