@@ -135,9 +135,9 @@ def load() -> ctypes.CDLL:
 
 #: kernels each forward entry point launches (the bench's count of this library's launches)
 LAUNCHES = {
-    "ffb_layernorm_fwd": 1, "ffb_gemm_bf16_nt": 1, "ffb_trimul_fwd": 4, "ffb_triattn_fwd": 3,
+    "ffb_layernorm_fwd": 1, "ffb_gemm_bf16_nt": 1, "ffb_trimul_fwd": 3, "ffb_triattn_fwd": 3,
     "ffb_transition_fwd": 1, "ffb_apb_fwd": 5, "ffb_single_transition_fwd": 3,
-    "ffb_trimul_shard_proj": 1, "ffb_trimul_shard_contract": 1, "ffb_trimul_shard_out": 2,
+    "ffb_trimul_shard_proj": 1, "ffb_trimul_shard_contract": 1, "ffb_trimul_shard_out": 1,
     "ffb_triattn_shard_proj": 1, "ffb_triattn_shard_attn": 1, "ffb_triattn_shard_out": 1,
     "ffb_transition_shard_fwd": 1, "ffb_apb_shard_pair_bias": 1, "ffb_apb_shard_single": 4,
     "ffb_single_transition_fwd_noalloc": 3,
@@ -148,11 +148,7 @@ launch_count = 0
 
 
 def _stage_launches(name: str, args) -> int:
-    stages = int(args[10])
-    n = bin(stages).count("1")
-    if name == "ffb_trimul_fwd_stages" and stages & 4:
-        n += 1  # the output stage also launches the u-statistics pass
-    return n
+    return bin(int(args[10])).count("1")
 
 
 def call(name: str, *args) -> None:

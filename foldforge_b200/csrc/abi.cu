@@ -438,10 +438,10 @@ int ffb_trimul_shard_out(const void* z, const uint8_t* mask, const void* packed,
                          void* ustats, void* out, int R, int N, int row0, int masked, void* stream) {
   int st = shard_args("trimul_shard_out", R, N, row0);
   if (st) return st;
-  if (!z || !mask || !packed || !u || !zstats || !ustats || !out) return fail(FFB_ERR_ARG, "trimul_shard_out: null pointer");
+  if (!z || !mask || !packed || !u || !zstats || !out) return fail(FFB_ERR_ARG, "trimul_shard_out: null pointer");
   if (z == out) return fail(FFB_ERR_ARG, "trimul_shard_out: out must not alias z");
   if (masked != FFB_MASKED_COMPUTE && masked != FFB_MASKED_ZERO) return fail(FFB_ERR_ARG, "trimul_shard_out: masked=%d", masked);
-  if (!aligned16(z) || !aligned16(packed) || !aligned16(u) || !aligned16(zstats) || !aligned16(ustats) || !aligned16(out))
+  if (!aligned16(z) || !aligned16(packed) || !aligned16(u) || !aligned16(zstats) || !aligned16(out))
     return fail(FFB_ERR_ARG, "trimul_shard_out: misaligned pointer");
   DeviceInfo info;
   st = device_info(&info);

@@ -83,7 +83,8 @@ struct ProjSmem {
   alignas(1024) uint8_t vt[2][kC * 64 * 2];  // V^T staging: [128 channels][pairs 0..63 | 64..127], SW128
   float wsum[kProjRows];
   float bias[kProjRows];
-  float2 stats[2][kTile];  // (mean, rstd) per pair, by tile parity
+  float4 stats[2][kTile / 2];  // pair couple (j, j + 1): rstd x2, -rstd mean x2; by tile parity
+  float4 wb[kProjRows / 2];      // channel couple (c, c + 1): wsum x2, bias x2
   uint64_t wbar;
   uint64_t z_full[kProjStages], z_empty[kProjStages];
   uint64_t x_full, x_free, y_full, y_free;
@@ -137,6 +138,8 @@ __global__ void __launch_bounds__(kProjThreads, 1)
       s.wsum[i] = v[i];
       s.bias[i] = v[kProjRows + i];
     }
+    for (int i = threadIdx.x; i < kProjRows / 2; i += kProjThreads)
+      s.wb[i] = make_float4(v[2 * i], v[2 * i + 1], v[kProjRows + 2 * i], v[kProjRows + 2 * i + 1]);
   }
   if (warp == 0) {
     tmem_alloc(&s.tmem_base, 512);
@@ -223,7 +226,11 @@ __global__ void __launch_bounds__(kProjThreads, 1)
       if (!__all_sync(0xFFFFFFFFu, w1 && w2)) break;
       float mean, rstd;
       tile_stats(s.z[st], t, mean, rstd);
-      s.stats[sb][t] = make_float2(mean, rstd);
+      {
+        float* st4 = reinterpret_cast<float*>(&s.stats[sb][t >> 1]);
+        st4[t & 1] = rstd;
+        st4[2 + (t & 1)] = -rstd * mean;
+      }
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&s.st_full[sb]);
@@ -237,6 +244,7 @@ __global__ void __launch_bounds__(kProjThreads, 1)
       if (!__all_sync(0xFFFFFFFFu, mbar_wait(&s.x_full, it & 1, p.err, kErrTimeoutMma))) break;
       tc_fence_after();
       const int64_t row_base = (static_cast<int64_t>(b) * p.R + r) * kHeads;  // (b, r) -> head 0
+      const uint64_t rs2 = f32x2(rstd, rstd), nrm2 = f32x2(-rstd * mean, -rstd * mean);
       // Q (columns 0..127) and K (128..255): one head = 32 columns = 64 contiguous bytes
 #pragma unroll 1
       for (int cc = 0; cc < 256; cc += 32) {
@@ -244,12 +252,15 @@ __global__ void __launch_bounds__(kProjThreads, 1)
         tmem_ld32(tmem0 + lane_off + kColX + cc, v);
         tmem_ld_wait();
         if (valid) {
+          // channels (c, c + 1): rstd v - rstd mean wsum + bias
           uint32_t w[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const int c = cc + 2 * i;
-            const float a = rstd * (__uint_as_float(v[2 * i]) - mean * s.wsum[c]) + s.bias[c];
-            const float bb = rstd * (__uint_as_float(v[2 * i + 1]) - mean * s.wsum[c + 1]) + s.bias[c + 1];
+            const float4 wb = s.wb[(cc >> 1) + i];
+            float a, bb;
+            f32x2_split(fma_f32x2(rs2, f32x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])),
+                                  fma_f32x2(nrm2, f32x2(wb.x, wb.y), f32x2(wb.z, wb.w))),
+                        a, bb);
             w[i] = pack_bf16(a, bb);
           }
           const int head = (cc % 128) / 32;
@@ -282,7 +293,7 @@ __global__ void __launch_bounds__(kProjThreads, 1)
     // thread = V channel c (head c / 32, d = c % 32); TMEM columns = the tile's pairs
     const int c = (warp & 3) * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const float wsv = s.wsum[256 + c], bsv = s.bias[256 + c];
+    const uint64_t wsv2 = f32x2(s.wsum[256 + c], s.wsum[256 + c]), bsv2 = f32x2(s.bias[256 + c], s.bias[256 + c]);
     const bool issuer = warp == 6 && lane == 0;
     int it = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
@@ -303,10 +314,12 @@ __global__ void __launch_bounds__(kProjThreads, 1)
         tmem_ld_wait();
         uint32_t packed[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float2 s0 = s.stats[sb][ch + 2 * i], s1 = s.stats[sb][ch + 2 * i + 1];
-          const float a = s0.y * (__uint_as_float(v[2 * i]) - s0.x * wsv) + bsv;
-          const float bb = s1.y * (__uint_as_float(v[2 * i + 1]) - s1.x * wsv) + bsv;
+        for (int i = 0; i < 16; ++i) {  // pairs (j, j + 1): rstd v - rstd mean wsum + bias
+          const float4 st4 = s.stats[sb][(ch >> 1) + i];
+          float a, bb;
+          f32x2_split(fma_f32x2(f32x2(st4.x, st4.y), f32x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])),
+                                fma_f32x2(f32x2(st4.z, st4.w), wsv2, bsv2)),
+                      a, bb);
           packed[i] = pack_bf16(a, bb);
         }
         uint8_t* stage = s.vt[ch / 64];

@@ -12,11 +12,11 @@
 //     plain K-major GEMM per channel. The incoming direction reads COLUMN tiles of z
 //     (pairs (k, a) for fixed a), which makes its contraction the same GEMM.
 //  2. the per-channel contraction U_c = L_c R_c^T on the batched tcgen05 GEMM (gemm.cu).
-//  3. trimul_ustats (per-pair mean / rstd of u over its 128 channels, one coalesced pass)
-//     and trimul_out: per 128-pair tile, two tcgen05 GEMMs (gate from raw z, output
+//  3. trimul_out: per 128-pair tile, two tcgen05 GEMMs (gate from raw z, output
 //     projection from raw u) with both LayerNorms folded into the epilogue through the
-//     per-pair statistics (z's from step 1, u's from trimul_ustats), sigmoid gate, mask
-//     and residual, written back through the z tile and a TMA store.
+//     per-pair statistics (z's from step 1, u's taken from the staged u tile by the
+//     statistics warps), sigmoid gate, mask and residual, written back through the z tile
+//     and a TMA store.
 //
 // Kernels 1 and 3 are persistent (one CTA per SM) and warp-specialised: a TMA warp, an MMA
 // warp, statistics warps and eight epilogue warps, with the resident weights, a ring of
@@ -324,7 +324,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
 // fp32 pipe computes two channels per instruction. One thread stores the tile with TMA.
 //   warp 0      TMA: z and u tiles into a 2-stage ring
 //   warp 1      MMA: gate and out products -> 256 TMEM columns, double-buffered
-//   warps 2-3   per-pair coefficients (precomputed statistics) and the keep mask
+//   warps 2-3   per-pair coefficients (z statistics from step 1, u statistics from the
+//               staged u tile) and the keep mask
 //   warps 4-11  epilogue: lane = pair, warps 4-7 channels 0-63, warps 8-11 channels 64-127
 constexpr int kOTile = 128;
 constexpr int kOStages = 2;
@@ -351,73 +352,11 @@ struct OutParams {
   const uint8_t* packed;
   const uint8_t* mask;
   const float2* zstats;  // [B, R, N] (mean, rstd) of z (input LayerNorm)
-  const float2* ustats;  // [B, R, N] (mean, rstd) of u (centre LayerNorm)
   int B, N;
   int R, row0;           // rows held and the first one's global index
   int masked_zero;
   int* err;
 };
-
-// Per-pair mean and 1/sqrt(var + 1e-5) of u over its 128 channels (u channel-major
-// [B*h, R, Np], R rows held). Two adjacent lanes own 8 consecutive pairs of one row and walk
-// 64 channels each with 16-byte loads (coalesced across the warp, 16 loads in flight per
-// pair group); the variance is accumulated about channel 0's value (shifted data, no
-// cancellation for pairs whose mean is large) and the two halves are combined by a shuffle.
-__global__ void __launch_bounds__(256) trimul_ustats_kernel(const __nv_bfloat16* __restrict__ u,
-                                                             float2* __restrict__ ustats, int B, int R, int N,
-                                                             int Np) {
-  const int groups = (N + 7) / 8;
-  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t gid = tid >> 1;
-  const int half = static_cast<int>(tid & 1);
-  const bool live = gid < static_cast<int64_t>(B) * R * groups;
-  const int g = live ? static_cast<int>(gid % groups) : 0;
-  const int64_t bi = live ? gid / groups : 0;  // b * R + i
-  const int b = static_cast<int>(bi / R), i = static_cast<int>(bi % R);
-  const int64_t plane = static_cast<int64_t>(R) * Np;
-  const __nv_bfloat16* src = u + (static_cast<int64_t>(b) * kH * R + i) * Np + g * 8;
-  float shift[8], s1[8], s2[8];
-  {
-    const uint4 v = *reinterpret_cast<const uint4*>(src);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      shift[2 * e] = bf16_lo(w[e]);
-      shift[2 * e + 1] = bf16_hi(w[e]);
-    }
-#pragma unroll
-    for (int e = 0; e < 8; ++e) s1[e] = s2[e] = 0.f;
-  }
-  const int c0 = half * (kH / 2);
-#pragma unroll 16
-  for (int c = c0; c < c0 + kH / 2; ++c) {
-    const uint4 v = *reinterpret_cast<const uint4*>(src + c * plane);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float d0 = bf16_lo(w[e]) - shift[2 * e], d1 = bf16_hi(w[e]) - shift[2 * e + 1];
-      s1[2 * e] += d0;
-      s2[2 * e] = fmaf(d0, d0, s2[2 * e]);
-      s1[2 * e + 1] += d1;
-      s2[2 * e + 1] = fmaf(d1, d1, s2[2 * e + 1]);
-    }
-  }
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    s1[e] += __shfl_xor_sync(0xFFFFFFFFu, s1[e], 1);
-    s2[e] += __shfl_xor_sync(0xFFFFFFFFu, s2[e], 1);
-  }
-  if (!live || half) return;
-  float2* dst = ustats + bi * N + g * 8;
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    if (g * 8 + e < N) {
-      const float m = s1[e] * (1.0f / kH);
-      const float var = fmaxf(s2[e] * (1.0f / kH) - m * m, 0.f);
-      dst[e] = make_float2(shift[e] + m, rsqrtf(var + 1e-5f));
-    }
-  }
-}
 
 __global__ void __launch_bounds__(kOThreads, 1)
     trimul_out_kernel(const __grid_constant__ CUtensorMap map_z, const __grid_constant__ CUtensorMap map_u,
@@ -512,28 +451,46 @@ __global__ void __launch_bounds__(kOThreads, 1)
       }
     }
   } else if (warp < 4) {
-    // per-pair coefficients (precomputed statistics) and keep mask: thread t handles pairs
-    // t and t + 64
+    // per-pair coefficients and keep mask: z statistics precomputed by the projection, u
+    // statistics over the 128 channel rows of the staged u tile (one pass, sums about the
+    // pair's channel-0 value); thread t owns the pair couple (2t, 2t + 1), one 4-byte load
+    // per channel
     const int t = (warp - 2) * 32 + lane;
+    const int pp0 = 2 * t, pb = pp0 / 64, pcol = pp0 % 64;
     int it = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
-      const int buf = it & 1;
+      const int st = it % kOStages, buf = it & 1;
+      const bool w1 = mbar_wait(&s.full[st], (it / kOStages) & 1, p.err, kErrTimeoutLoad);
       const bool w2 = mbar_wait(&s.st_free[buf], ((it >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty);
-      if (!__all_sync(0xFFFFFFFFu, w2)) break;
+      if (!__all_sync(0xFFFFFFFFu, w1 && w2)) break;
+      const uint8_t* ut = s.u[st] + pb * (kH * 128);
+      const uint32_t w0 = *reinterpret_cast<const uint32_t*>(ut + sw128_offset(0, pcol));
+      const float sh0 = bf16_lo(w0), sh1 = bf16_hi(w0);
+      const uint64_t nsh = f32x2(-sh0, -sh1);
+      uint64_t a1 = f32x2(0.f, 0.f), a2 = f32x2(0.f, 0.f);
+#pragma unroll 16
+      for (int c = 0; c < kH; ++c) {
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(ut + sw128_offset(c, pcol));
+        const uint64_t d = add_f32x2(f32x2(bf16_lo(w), bf16_hi(w)), nsh);
+        a1 = add_f32x2(a1, d);
+        a2 = fma_f32x2(d, d, a2);
+      }
+      float s1[2], s2[2];
+      f32x2_split(a1, s1[0], s1[1]);
+      f32x2_split(a2, s2[0], s2[1]);
       const int c0 = (tile % tiles_per_row) * kOTile;
       const int rr = tile / tiles_per_row;
       const int b = rr / p.R, r = rr - b * p.R;
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
-        const int pp = t + 64 * k;
+        const int pp = pp0 + k;
         const int j = c0 + pp;
-        float2 zs = make_float2(0.f, 0.f), us = make_float2(0.f, 0.f);
-        if (j < p.N) {
-          const int64_t pair = (static_cast<int64_t>(b) * p.R + r) * p.N + j;
-          zs = p.zstats[pair];
-          us = p.ustats[pair];
-        }
-        s.pc[buf][pp] = make_float4(0.5f * zs.y, -0.5f * zs.y * zs.x, 0.5f * us.y, -0.5f * us.y * us.x);
+        const float m1 = s1[k] * (1.0f / kH);
+        const float mu = (k ? sh1 : sh0) + m1;
+        const float ru = rsqrtf(fmaxf(s2[k] * (1.0f / kH) - m1 * m1, 0.f) + 1e-5f);
+        float2 zs = make_float2(0.f, 0.f);
+        if (j < p.N) zs = p.zstats[(static_cast<int64_t>(b) * p.R + r) * p.N + j];
+        s.pc[buf][pp] = make_float4(0.5f * zs.y, -0.5f * zs.y * zs.x, 0.5f * ru, -0.5f * ru * mu);
         s.keep[buf][pp] =
             (j < p.N && (!p.masked_zero || (p.mask[b * p.N + p.row0 + r] && p.mask[b * p.N + j]))) ? 1.f : 0.f;
       }
@@ -637,7 +594,7 @@ size_t trimul_workspace_bytes(int B, int N) {
   const size_t one = static_cast<size_t>(B) * kH * N * np * 2;
   const size_t aligned = (one + 255) / 256 * 256;
   const size_t stats = (static_cast<size_t>(B) * N * N * 8 + 255) / 256 * 256;
-  return 3 * aligned + 2 * stats;  // L, R, U, z statistics, u statistics
+  return 3 * aligned + stats;  // L, R, U, z statistics
 }
 
 int trimul_prepare(const TriMulWeights& w, void* packed, cudaStream_t stream) {
@@ -733,17 +690,9 @@ int launch_contract(const void* left, const void* right, void* u, int B, int cha
   return cuda_status(launch_gemm_nt(map_l, map_r, gp, bn, info.num_sms, stream), "trimul contraction launch");
 }
 
-int launch_out(const void* z, const uint8_t* mask, const void* packed, const void* u, const float2* zstats,
-               float2* ustats, void* out, int B, int R, int N, int row0, int masked_zero, const DeviceInfo& info,
-               cudaStream_t stream) {
+int launch_out(const void* z, const uint8_t* mask, const void* packed, const void* u, const float2* zstats, void* out,
+               int B, int R, int N, int row0, int masked_zero, const DeviceInfo& info, cudaStream_t stream) {
   const int np = (N + 7) / 8 * 8;
-  {
-    const int64_t threads = 2 * static_cast<int64_t>(B) * R * ((N + 7) / 8);
-    trimul_ustats_kernel<<<static_cast<int>((threads + 255) / 256), 256, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(u), ustats, B, R, N, np);
-    int st = cuda_status(static_cast<int>(cudaGetLastError()), "trimul_ustats launch");
-    if (st) return st;
-  }
   CUtensorMap map_zo, map_out, map_u;
   int st = z_map(&map_zo, z, B, R, N, kOTile, false);
   if (st) return st;
@@ -754,7 +703,7 @@ int launch_out(const void* z, const uint8_t* mask, const void* packed, const voi
   const uint32_t ubox[3] = {64, 1, kH};  // [128 channels][64 pairs], 128-byte swizzled rows
   st = make_map(&map_u, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, u, udims, ustrides, ubox, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
-  OutParams op{static_cast<const uint8_t*>(packed), mask, zstats, ustats, B, N, R, row0, masked_zero, info.err};
+  OutParams op{static_cast<const uint8_t*>(packed), mask, zstats, B, N, R, row0, masked_zero, info.err};
   const size_t out_smem = sizeof(OutSmem) + 1024;
   const int otiles = B * R * ((N + kOTile - 1) / kOTile);
   const int ogrid = otiles < info.num_sms ? otiles : info.num_sms;
@@ -774,9 +723,7 @@ int trimul_forward(const void* z, const uint8_t* mask, const void* packed, void*
   void* left = ws;
   void* right = ws + aligned;
   void* u = ws + 2 * aligned;
-  const size_t stats_bytes = (static_cast<size_t>(B) * N * N * 8 + 255) / 256 * 256;
   float2* zstats = reinterpret_cast<float2*>(ws + 3 * aligned);
-  float2* ustats = reinterpret_cast<float2*>(ws + 3 * aligned + stats_bytes);
   // channel-major L, R, U: [B * 128][N][Np]
   const int64_t s_c = static_cast<int64_t>(N) * np, s_b = kH * s_c;
   int st = 0;
@@ -788,7 +735,7 @@ int trimul_forward(const void* z, const uint8_t* mask, const void* packed, void*
     st = launch_contract(left, right, u, B, kH, N, N, s_c, np, s_c, np, info, stream);
     if (st) return st;
   }
-  if (stages & 4) st = launch_out(z, mask, packed, u, zstats, ustats, out, B, N, N, 0, masked_zero, info, stream);
+  if (stages & 4) st = launch_out(z, mask, packed, u, zstats, out, B, N, N, 0, masked_zero, info, stream);
   return st;
 }
 
@@ -820,8 +767,8 @@ int trimul_channel_contract(const void* left, const void* right, void* u, int C,
 int trimul_shard_out(const void* z, const uint8_t* mask, const void* packed, const void* u, const void* zstats,
                      void* ustats, void* out, int R, int N, int row0, int masked_zero, const DeviceInfo& info,
                      cudaStream_t stream) {
-  return launch_out(z, mask, packed, u, static_cast<const float2*>(zstats), static_cast<float2*>(ustats), out, 1, R,
-                    N, row0, masked_zero, info, stream);
+  (void)ustats;  // the u statistics are taken inside the output kernel; the argument is kept for the ABI
+  return launch_out(z, mask, packed, u, static_cast<const float2*>(zstats), out, 1, R, N, row0, masked_zero, info, stream);
 }
 
 }  // namespace ffb

@@ -297,9 +297,8 @@ class B200ShardOps:
             right_all = self.comm.gather_rows(right)
             u = torch.empty((128, r, np_), dtype=torch.bfloat16, device=dev)
             _lib.call("ffb_trimul_shard_contract", _ptr(left), _ptr(right_all), _ptr(u), r, n, _stream())
-        ustats = torch.empty_like(zstats)
         out = torch.empty_like(z)
-        _lib.call("ffb_trimul_shard_out", _ptr(z), _ptr(mask), _ptr(packed), _ptr(u), _ptr(zstats), _ptr(ustats),
+        _lib.call("ffb_trimul_shard_out", _ptr(z), _ptr(mask), _ptr(packed), _ptr(u), _ptr(zstats), _ptr(None),
                   _ptr(out), r, n, row0, self.masked, _stream())
         return out
 

@@ -179,7 +179,8 @@ int ffb_single_transition_fwd_noalloc(const void* s, const uint8_t* mask, const 
  * between the pieces with NCCL (all-gather over rows, all-to-all transposes); no new
  * reference interface corresponds to these: FoldForge has no multi-GPU Pairformer.
  * Layouts: TriMul L, R, and the gathered right operand [rows][128][Np] bf16 (Np = N rounded
- * up to 8), U [128][R][Np] bf16, statistics [R][N] float2; TriAttn Q, K [R][4][N][32],
+ * up to 8), U [128][R][Np] bf16, statistics [R][N] float2 (ffb_trimul_shard_out's `ustats` is unused and
+ * may be null: the output kernel takes u's statistics itself); TriAttn Q, K [R][4][N][32],
  * V^T [R][4][32][Np], bias rows [R][4][Np] (gathered: [N][4][Np], rows = queries), o [R][N][128];
  * single-track pair-bias rows [R][16][N] fp32 (gathered: [N][16][N]). Weights are the
  * ffb_*_prepare images. Status codes as elsewhere. */
