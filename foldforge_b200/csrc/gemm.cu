@@ -5,9 +5,13 @@
 // shared-memory stages, warp 1 (one elected lane) issues tcgen05.mma and commits, warps
 // 2..5 drain the accumulator (TMEM -> registers) and run the epilogue. Two TMEM
 // accumulators of BN columns let the MMA of tile t+1 overlap the epilogue of tile t.
+// The plain bf16 store (the contraction's epilogue) leaves through 64-column chunks staged
+// 128-byte-swizzled in shared memory (two buffers, alternated) and written by TMA stores,
+// so the tile's rows reach memory as whole lines; the other epilogues store per thread.
 //
 // Used for the triangle-multiplication contraction (one GEMM per hidden channel, batch =
 // B * hidden) and for the single-track projections.
+#include "abi_util.h"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -25,10 +29,13 @@ struct GemmSmem {
   alignas(1024) uint8_t b[kStages][BN * kBK * 2];
   uint64_t full[kStages];
   uint64_t empty[kStages];
+  alignas(1024) uint8_t out[2][kBM * 64 * 2];  // bf16 store staging: [128 rows][64 columns], SW128
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint32_t tmem_base;
 };
+
+static_assert(sizeof(GemmSmem<256>) + 1024 <= 232448, "GEMM shared memory exceeds the per-CTA limit");
 
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& b, int& tm, int& tn) {
   const int per_batch = tiles_m * tiles_n;
@@ -171,7 +178,8 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int b, int m
 
 template <int BN>
 __global__ void __launch_bounds__(192, 1)
-    gemm_nt_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, GemmParams p) {
+    gemm_nt_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                   const __grid_constant__ CUtensorMap map_d, GemmParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   GemmSmem<BN>& s = *reinterpret_cast<GemmSmem<BN>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -200,6 +208,7 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_map(&map_a);
     tma_prefetch_map(&map_b);
+    if (p.tma_store) tma_prefetch_map(&map_d);
   }
   tc_fence_before();
   __syncthreads();
@@ -256,26 +265,62 @@ __global__ void __launch_bounds__(192, 1)
     // epilogue warps 2..5: TMEM lane quarter = warp % 4
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
-    int local = 0;
+    const bool issuer = warp == 2 && lane == 0;
+    int local = 0, chunk = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++local) {
       int b, tm, tn;
       tile_coords(tile, tiles_m, tiles_n, b, tm, tn);
       const int acc = local & 1;
       const bool ok = mbar_wait(&s.acc_full[acc], (local >> 1) & 1, p.err, kErrTimeoutMma);
-      if (!__all_sync(0xFFFFFFFFu, ok)) break;  // warp-uniform: tcgen05.ld below is .sync.aligned
+      // uniform over the four warps: the staged store below synchronises them per chunk
+      if (named_barrier_or(1, 128, !ok)) break;
       tc_fence_after();
       const uint32_t base = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
       const int m = tm * kBM + row;
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t v[32];
-        tmem_ld32(base + c, v);
-        tmem_ld_wait();
-        if (tn * BN + c < p.N) epilogue_chunk<BN>(p, b, m, tn * BN + c, v);
+      if (p.tma_store) {
+        for (int c = 0; c < BN; c += 64, ++chunk) {
+          uint8_t* stage = s.out[chunk & 1];
+          // the store issued two chunks ago has finished reading this staging buffer
+          if (issuer) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          named_barrier(1, 128);
+          uint32_t v[32], w[32];
+          tmem_ld32(base + c, v);
+          tmem_ld32(base + c + 32, w);
+          tmem_ld_wait();
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            *reinterpret_cast<uint4*>(stage + sw128_offset(row, 8 * q)) =
+                make_uint4(pack_bf16(__uint_as_float(v[8 * q]), __uint_as_float(v[8 * q + 1])),
+                           pack_bf16(__uint_as_float(v[8 * q + 2]), __uint_as_float(v[8 * q + 3])),
+                           pack_bf16(__uint_as_float(v[8 * q + 4]), __uint_as_float(v[8 * q + 5])),
+                           pack_bf16(__uint_as_float(v[8 * q + 6]), __uint_as_float(v[8 * q + 7])));
+            *reinterpret_cast<uint4*>(stage + sw128_offset(row, 32 + 8 * q)) =
+                make_uint4(pack_bf16(__uint_as_float(w[8 * q]), __uint_as_float(w[8 * q + 1])),
+                           pack_bf16(__uint_as_float(w[8 * q + 2]), __uint_as_float(w[8 * q + 3])),
+                           pack_bf16(__uint_as_float(w[8 * q + 4]), __uint_as_float(w[8 * q + 5])),
+                           pack_bf16(__uint_as_float(w[8 * q + 6]), __uint_as_float(w[8 * q + 7])));
+          }
+          fence_async_smem();
+          named_barrier(1, 128);
+          // rows past M and columns past N are clipped by the tensor map
+          if (issuer && tn * BN + c < p.N) {
+            tma_store_3d(&map_d, stage, tn * BN + c, tm * kBM, b);
+            tma_store_commit();
+          }
+        }
+      } else {
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t v[32];
+          tmem_ld32(base + c, v);
+          tmem_ld_wait();
+          if (tn * BN + c < p.N) epilogue_chunk<BN>(p, b, m, tn * BN + c, v);
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.acc_empty[acc]);
     }
+    if (issuer) tma_store_wait_all0();
   }
   tc_fence_before();
   __syncthreads();
@@ -292,18 +337,32 @@ size_t gemm_smem_bytes(int bn) {
   return (bn == 256 ? sizeof(GemmSmem<256>) : sizeof(GemmSmem<128>)) + 1024;
 }
 
-int launch_gemm_nt(const CUtensorMap& map_a, const CUtensorMap& map_b, const GemmParams& p, int bn, int num_sms,
+int launch_gemm_nt(const CUtensorMap& map_a, const CUtensorMap& map_b, const GemmParams& p_in, int bn, int num_sms,
                    cudaStream_t stream) {
+  GemmParams p = p_in;
   const int tiles = p.batch * ((p.M + kBM - 1) / kBM) * ((p.N + bn - 1) / bn);
   if (tiles <= 0) return 0;
+  // the plain bf16 store goes through a TMA store map when the output's strides allow it
+  CUtensorMap map_d;
+  memset(&map_d, 0, sizeof(map_d));
+  p.tma_store = 0;
+  if (p.epilogue == kEpiStore && !p.d_is_f32 && p.bias == nullptr && (reinterpret_cast<uintptr_t>(p.D) & 15u) == 0 &&
+      (p.ldd * 2) % 16 == 0 &&
+      (p.batch_stride_d * 2) % 16 == 0) {
+    const uint64_t dims[3] = {static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.M), static_cast<uint64_t>(p.batch)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(p.ldd) * 2, static_cast<uint64_t>(p.batch_stride_d) * 2};
+    const uint32_t box[3] = {64, kBM, 1};
+    if (make_map(&map_d, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, p.D, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B) == 0)
+      p.tma_store = 1;
+  }
   const int grid = tiles < num_sms ? tiles : num_sms;
   const size_t smem = gemm_smem_bytes(bn);
   if (bn == 256) {
     cudaFuncSetAttribute(gemm_nt_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    gemm_nt_kernel<256><<<grid, 192, smem, stream>>>(map_a, map_b, p);
+    gemm_nt_kernel<256><<<grid, 192, smem, stream>>>(map_a, map_b, map_d, p);
   } else {
     cudaFuncSetAttribute(gemm_nt_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    gemm_nt_kernel<128><<<grid, 192, smem, stream>>>(map_a, map_b, p);
+    gemm_nt_kernel<128><<<grid, 192, smem, stream>>>(map_a, map_b, map_d, p);
   }
   return static_cast<int>(cudaGetLastError());
 }

@@ -24,6 +24,7 @@ struct GemmParams {
   const void* residual;
   const uint8_t* row_mask;
   int* err;
+  int tma_store;  // set by launch_gemm_nt: the bf16 store epilogue goes through TMA stores
 };
 
 size_t gemm_smem_bytes(int bn);
