@@ -11,7 +11,7 @@
 namespace ffb {
 namespace {
 
-constexpr int kRowsInFlight = 4;  // per half-warp
+constexpr int kRowsInFlight = 8;  // per half-warp
 
 __device__ __forceinline__ float half_warp_sum(float v) {
 #pragma unroll
