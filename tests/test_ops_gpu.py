@@ -77,8 +77,11 @@ def test_trimul_masked_zero_leaves_padding_untouched(weights, outgoing):
 
 
 @pytest.mark.parametrize("starting", [True, False])
-@pytest.mark.parametrize("b,n,masked", CASES + [(1, 200, 0)])
+@pytest.mark.parametrize("b,n,masked", CASES + [(1, 200, 0), (1, 384, 20)])
 def test_triattn_matches_oracle(weights, starting, b, n, masked):
+    """N = 384: the attention's 256-query units alternate between two query groups and one
+    (the second group of the last unit holds no query), which keeps both kinds of step in
+    one launch."""
     p = sub(weights, "tri_atten_starting" if starting else "tri_atten_ending")
     z, tokens = pair_inputs(b, n, masked, seed=5)
     packed = kernels.triattn_prepare(p, torch.device("cuda"))
