@@ -74,9 +74,17 @@ class _PeerBuffer:
         return torch.tensor([a + offset for a in self.addrs], dtype=torch.int64, device=self.device)
 
     def close(self) -> None:
+        """Unmap the peers' buffers (every rank must do so before any rank frees its own)."""
         for peer in self.opened:
             _lib.call("ffb_p2p_close", peer)
         self.opened = []
+
+    def free(self) -> None:
+        """Free this rank's buffer (after every rank has closed its mapping of it)."""
+        if self.base.value:
+            self.local = None
+            _lib.call("ffb_p2p_free", self.base)
+            self.base = ctypes.c_void_p()
 
 
 class _PeerExchange:
@@ -151,10 +159,9 @@ class _PeerExchange:
         self._wait()
         return buf.local.view(torch.bfloat16).view(shape)
 
-    def close(self) -> None:
-        for buf, *_ in list(self.t_bufs.values()) + list(self.g_bufs.values()) + list(self.r_bufs.values()):
-            buf.close()
-        self.flags.close()
+    def buffers(self) -> list[_PeerBuffer]:
+        return [b for b, *_ in list(self.t_bufs.values()) + list(self.g_bufs.values()) + list(self.r_bufs.values())] + [
+            self.flags]
 
 
 class ShardComm:
@@ -197,11 +204,18 @@ class ShardComm:
         return self.trimul_mode == "channels" or self.world >= 4
 
     def close(self) -> None:
-        """Unmap the peers' exchange buffers (call on every rank, before the group is destroyed)."""
+        """Release the peer-memory exchange buffers (collective: call on every rank, before the
+        group is destroyed; tensors returned by the exchanges are invalid afterwards)."""
         if self._peer is not None:
             torch.cuda.synchronize()
             dist.barrier(group=self.group)
-            self._peer.close()
+            bufs = self._peer.buffers()
+            for buf in bufs:
+                buf.close()
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)  # every rank has unmapped every peer buffer
+            for buf in bufs:
+                buf.free()
             self._peer = None
 
     def rows(self, n: int) -> tuple[int, int]:
