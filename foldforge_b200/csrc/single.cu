@@ -55,14 +55,15 @@ int to_bf16(const float* a, const float* b, int rows_each, int cols, int interle
 // head-major ([h][b][i][j]). The LayerNorm is folded: W' = bf16(W_pb diag gamma) and
 // wsum[h] = sum_c W'[h][c], so pb = rstd * (W' z - mean * wsum) on RAW z (the LayerNorm
 // offset beta adds one constant per head to every logit of a row, which the softmax
-// cancels). Persistent, warp-specialised, 128-pair tiles:
-//   warp 0      TMA: z tiles (two 64-channel SW128 blocks) through a 4-stage ring
+// cancels). Persistent, warp-specialised, 128-pair tiles, two CTAs per SM (eight
+// statistics / epilogue warps per SM hide the staged-tile and TMEM latencies):
+//   warp 0      TMA: z tiles (two 64-channel SW128 blocks) through a 3-stage ring
 //   warp 1      MMA: acc[p][h] = z[p] . W'[h] (M = 128 pairs, N = 16 heads, K = 128),
 //               double-buffered in TMEM
 //   warps 2-5   lane = pair: LayerNorm statistics from the staged tile, then the epilogue;
 //               a warp's 32 pairs of one head are one coalesced 128-byte store
 constexpr int kPbTile = 128;
-constexpr int kPbStages = 4;
+constexpr int kPbStages = 3;  // three stages keep the CTA under half the SM's shared memory: two CTAs per SM
 constexpr int kPbThreads = 192;
 constexpr uint32_t kPbWBytes = 2 * kHs * 128;  // W' image: two 64-channel blocks of 16 rows
 
@@ -78,7 +79,7 @@ struct PbSmem {
   uint32_t tmem_base;
 };
 
-__global__ void __launch_bounds__(kPbThreads, 1)
+__global__ void __launch_bounds__(kPbThreads, 2)
     pair_bias_kernel(const __grid_constant__ CUtensorMap map_z, const uint8_t* __restrict__ w_img,
                      const float* __restrict__ wsum, float* __restrict__ pb, int64_t P, int N, int64_t pb_h,
                      int64_t pb_r, int* err) {
@@ -546,7 +547,7 @@ int launch_pair_bias(const void* z, const uint8_t* img, float* pb, int64_t rows,
   int st = make_map(&mz, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, z, zdims, zstr, zbox, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
   const int64_t tiles = static_cast<int64_t>((P + kPbTile - 1) / kPbTile);
-  const int grid = static_cast<int>(tiles < info.num_sms ? tiles : info.num_sms);
+  const int grid = static_cast<int>(tiles < 2 * info.num_sms ? tiles : 2 * info.num_sms);
   const size_t smem = sizeof(PbSmem) + 1024;
   cudaFuncSetAttribute(pair_bias_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   pair_bias_kernel<<<grid, kPbThreads, smem, stream>>>(mz, img + L.w_pb, reinterpret_cast<const float*>(img + L.pb_wsum),
