@@ -3,8 +3,9 @@
 // The pair tensor's rows are c_z = 128 bf16 = 256 bytes: 16 lanes each load one 16-byte
 // vector, so a warp covers two rows per load instruction and every load is a full
 // 128-bit access; mean and variance are two-pass in fp32 from registers with half-warp
-// shuffle reductions. Each warp keeps several rows in flight to cover HBM latency. Other
-// widths (the single track, c_s = 384) and fp32 use a one-warp-per-row kernel.
+// shuffle reductions. Each warp keeps several rows in flight to cover HBM latency. The
+// single track's bf16 rows (c_s = 384) are held in registers by one warp each; other widths
+// and fp32 use a one-warp-per-row kernel that reads the row three times.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -72,6 +73,52 @@ __global__ void __launch_bounds__(256) ln128_bf16_kernel(const uint4* __restrict
   }
 }
 
+// bf16 rows of c = 384 (the single track): one warp per row, the row held in registers (each
+// lane loads three 8-byte words: channels 4 lane + 128 k), one read and one write per element.
+__global__ void __launch_bounds__(256) ln384_bf16_kernel(const uint2* __restrict__ x, uint2* __restrict__ y,
+                                                          const float* __restrict__ gamma,
+                                                          const float* __restrict__ beta, int64_t rows, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32; r < rows; r += warps) {
+    uint2 v[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) v[k] = x[r * 96 + k * 32 + lane];
+    float f[12];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      f[4 * k] = bf16_lo(v[k].x);
+      f[4 * k + 1] = bf16_hi(v[k].x);
+      f[4 * k + 2] = bf16_lo(v[k].y);
+      f[4 * k + 3] = bf16_hi(v[k].y);
+    }
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 12; ++i) sum += f[i];
+    const float mean = warp_sum(sum) / 384.0f;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < 12; ++i) {
+      const float d = f[i] - mean;
+      q += d * d;
+    }
+    const float rstd = rsqrtf(warp_sum(q) / 384.0f + eps);
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      float o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int c = k * 128 + 4 * lane + e;
+        float t = (f[4 * k + e] - mean) * rstd;
+        if (gamma) t *= gamma[c];
+        if (beta) t += beta[c];
+        o[e] = t;
+      }
+      y[r * 96 + k * 32 + lane] = make_uint2(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]));
+    }
+  }
+}
+
 template <typename T>
 __device__ __forceinline__ float load_f(const T* p);
 template <>
@@ -125,6 +172,13 @@ int launch_layernorm(const void* x, void* y, const float* gamma, const float* be
     if (blocks > cap) blocks = cap;
     ln128_bf16_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(
         reinterpret_cast<const uint4*>(x), reinterpret_cast<uint4*>(y), gamma, beta, rows, eps);
+  } else if (!is_f32 && c == 384 && (reinterpret_cast<uintptr_t>(x) & 7u) == 0 &&
+             (reinterpret_cast<uintptr_t>(y) & 7u) == 0) {
+    int64_t blocks = (rows + 7) / 8;
+    const int64_t cap = static_cast<int64_t>(num_sms) * 16;
+    if (blocks > cap) blocks = cap;
+    ln384_bf16_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(
+        reinterpret_cast<const uint2*>(x), reinterpret_cast<uint2*>(y), gamma, beta, rows, eps);
   } else {
     int64_t blocks = (rows + 7) / 8;
     const int64_t cap = static_cast<int64_t>(num_sms) * 16;
