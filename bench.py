@@ -191,23 +191,37 @@ def cpu_block_ms(n: int, warm: bool = False) -> tuple[float, int]:
 
 
 def run_reference(args, rank: int, world: int) -> None:
+    """The reference arm: the CPU oracle (the reference block's equations, fp32, all host
+    threads) on rank 0. One step = ONE block at the workload's N (the same N as the b200 arm
+    at this GPU count); ``value`` extrapolates the median block to the 48-block trunk, and
+    ``ms_per_step`` is the measured one-block time, so ``ms_per_step x steps`` is the wall
+    time of the timed steps. Steps stop early once 150 s of CPU time have been timed."""
     if rank != 0:
         return
+    n = args.n if world == 1 else weak_n(world)
     times = []
     threads = os.cpu_count() or 1
-    for i in range(min(args.warmup, 1) + args.steps):
-        ms, threads = cpu_block_ms(args.n, warm=(i == 0))
-        if i >= min(args.warmup, 1):
-            times.append(ms)
-    value = statistics.median(times) * args.blocks
-    sample = f"one block of {args.blocks} at N={args.n} per step (fp32 CPU oracle), median of {len(times)}, x{args.blocks}"
+    budget_s, spent = 150.0, 0.0
+    for i in range(1 + args.steps):
+        ms, threads = cpu_block_ms(n, warm=(i == 0))
+        if i == 0:
+            continue  # the warm-up step
+        times.append(ms)
+        spent += ms / 1e3
+        if spent > budget_s:
+            break
+    block_ms = statistics.median(times)
+    value = block_ms * args.blocks
+    masked = round(MASKED * n / N_TOKENS)
+    sample = (f"one block of the {args.blocks}-block trunk at N={n} per step (fp32 CPU oracle, {threads} threads), "
+              f"median of {len(times)} steps; value = median x {args.blocks} blocks (extrapolated)")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "ms", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(value, 3), "higher_is_better": False,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{args.blocks}-block Pairformer trunk, N={args.n}, last {MASKED} tokens masked",
-                   "model": "AF3 Pairformer block (c_z 128, c_s 384)", "global_batch": 1, "seq_len": args.n,
-                   "parallelism": "cpu"},
+        "steps": len(times), "steps_requested": args.steps, "warmup": 1, "ms_per_step": round(block_ms, 3),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.blocks}-block Pairformer trunk, N={n}, last {masked} tokens masked",
+                   "model": "AF3 Pairformer block (c_z 128, c_s 384)", "global_batch": 1, "seq_len": n,
+                   "parallelism": "cpu", "step": "one block (value extrapolated to the trunk)"},
         "cpu_baseline": {"value": round(value, 3), "unit": "ms", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -378,6 +392,10 @@ def ladder_single_gpu(dev: torch.device) -> dict:
     del z
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
     graphed.replay()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(dev.index or 0)
+    sampler.start()
+    time.sleep(0.3)
     ts = []
     for _ in range(2):
         flush.fill_(1.0)
@@ -387,11 +405,13 @@ def ladder_single_gpu(dev: torch.device) -> dict:
         b.record()
         torch.cuda.synchronize()
         ts.append(a.elapsed_time(b))
+    clocks = sampler.stop()
     del graphed, trunk
     torch.cuda.empty_cache()
     ms = sum(ts) / len(ts)
     return {"n": n, "n_gpus": 1, "ms_per_trunk": round(ms, 1), "ms_per_block": round(ms / N_BLOCKS, 3),
-            "masked_suffix": masked, "steps": 2, "warmup": 1, "parallelism": "single GPU (CUDA-graph replay)"}
+            "masked_suffix": masked, "steps": 2, "warmup": 1, "parallelism": "single GPU (CUDA-graph replay)",
+            "clocks": clocks}
 
 
 def run_sharded(args, rank: int, world: int, local: int, dist) -> None:
@@ -480,12 +500,14 @@ def run_sharded(args, rank: int, world: int, local: int, dist) -> None:
                "d2h_bytes_per_step": out_pin.numel() * 2 + s_out_pin.numel() * 2,
                "per": "rank (its pair rows and the replicated single), max over ranks"}
 
+    parity = sharded_parity(trunk, blocks, comm, rows_h, s_h, mask, n_w, rank, dev, dist)
+
     ladder = None
     if not args.no_ladder:
-        lad_ms, _, _, _ = measure(LADDER_N, math.ceil(0.05 * LADDER_N), 2, 1)
+        lad_ms, lad_clocks, _, _ = measure(LADDER_N, math.ceil(0.05 * LADDER_N), 2, 1, True)
         ladder = {"n": LADDER_N, "n_gpus": world, "ms_per_trunk": round(lad_ms, 1),
                   "ms_per_block": round(lad_ms / nb, 3), "masked_suffix": math.ceil(0.05 * LADDER_N), "steps": 2,
-                  "warmup": 1, "parallelism": f"axial row-sharding x{world} (eager)"}
+                  "warmup": 1, "parallelism": f"axial row-sharding x{world} (eager)", "clocks": lad_clocks}
 
     # dominant kernel alone (triangle-attention core at N = 512 on this GPU)
     n = N_TOKENS
@@ -541,8 +563,48 @@ def run_sharded(args, rank: int, world: int, local: int, dist) -> None:
             line["e2e"] = e2e
         if ladder is not None:
             line["ladder"] = ladder
+        line["parity"] = parity
         print(json.dumps(line), flush=True)
     comm.close()  # every rank: unmap the peers' exchange buffers before the group goes
+
+
+def sharded_parity(trunk, blocks, comm, rows_h, s_h, mask, n: int, rank: int, dev, dist, nblocks: int = 2) -> dict:
+    """The first ``nblocks`` blocks of the row-sharded trunk (the NVLink peer-memory exchanges,
+    and the channel-sharded TriMul from four ranks) against the same blocks unsharded on rank
+    0's GPU, on the weak-scaling workload's inputs: relative L2 of pair and single on real
+    positions, and whether padded pairs / tokens kept their input exactly (masked "zero")."""
+    rows, s = rows_h.to(dev), s_h.to(dev)
+    with torch.no_grad():
+        for blk in blocks[:nblocks]:
+            rows, s = blk(rows, mask, s)
+        pair = comm.gather_rows(rows).clone()  # every rank takes part in the gather
+    torch.cuda.synchronize()
+    dist.barrier()
+    result = {"blocks": nblocks, "n": n, "reference": "the same blocks unsharded on one GPU (b200)"}
+    if rank == 0:
+        from foldforge_b200.synthetic import inputs
+
+        z_full = inputs(n, seed=0)[0].bfloat16().to(dev)  # the whole input pair the ranks' rows came from
+        key = mask[None]
+        zz, ss = z_full[None], s_h.to(dev)[None]
+        with torch.no_grad():
+            for block in trunk.blocks[:nblocks]:
+                zz, ss = block(zz, key, ss)
+        torch.cuda.synchronize()
+        tok = mask.bool()
+        pm = tok[:, None] & tok[None, :]
+
+        def rel(a, b, where):
+            a, b = a.float()[where], b.float()[where]
+            return float((a - b).norm() / b.norm().clamp_min(1e-30))
+
+        result.update({
+            "rel_l2_pair": round(rel(pair, zz[0], pm), 6),
+            "rel_l2_single": round(rel(s, ss[0], tok), 6),
+            "masked_exact": bool(torch.equal(pair[~pm], z_full[~pm]) and torch.equal(s[~tok], s_h.to(dev)[~tok])),
+        })
+    dist.barrier()
+    return result
 
 
 def kernels_once(n: int) -> None:

@@ -76,7 +76,7 @@ SIGNATURES: dict[str, list] = {
     "ffb_p2p_free": [c_void_p],
     "ffb_shard_transpose_p2p": [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p],
     "ffb_shard_gather_p2p": [c_void_p, ctypes.c_size_t, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p],
-    "ffb_shard_wait_p2p": [c_void_p, c_void_p, c_int, c_void_p],
+    "ffb_shard_wait_p2p": [c_void_p, c_void_p, c_int, c_i64, c_void_p],
     "ffb_shard_rows_p2p": [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p],
     "ffb_trimul_channel_contract": [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p],
 }

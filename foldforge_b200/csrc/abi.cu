@@ -17,7 +17,6 @@ __device__ int g_error_word;
 namespace {
 thread_local std::string t_last_error;
 std::mutex g_mutex;
-constexpr int kMaxDevices = 64;
 int g_num_sms[kMaxDevices];
 int* g_err_ptr[kMaxDevices];
 PFN_encodeTiled g_encode = nullptr;

@@ -13,6 +13,9 @@ typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_
                                     const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                     CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+// Devices a process may use with this library (per-device caches are arrays of this size).
+constexpr int kMaxDevices = 64;
+
 struct DeviceInfo {
   int device;
   int num_sms;

@@ -11,10 +11,11 @@
 // rank's `sync` words) fencing at system scope and storing a new epoch, with release
 // semantics, into slot [rank] of every peer's flag array (its own included). The epoch is
 // counted on the device (sync[1]), so a CUDA graph replaying the exchange signals new
-// epochs. ffb_shard_wait_p2p then waits, with acquire loads and a bounded spin, until
-// every slot of this rank's flags has reached the epoch: the peers' writes into this
-// rank's buffers are then visible. A wait that runs out records kErrTimeoutPeer in the
-// device error word and returns; it never traps.
+// epochs. ffb_shard_wait_p2p then waits, with acquire loads and a spin bounded by a
+// caller-given wall-clock limit (2 s by default), until every slot of this rank's flags has
+// reached the epoch: the peers' writes into this rank's buffers are then visible. A wait
+// that runs out records kErrTimeoutPeer in the device error word and returns; it never
+// traps.
 //
 // The kernels assume one rank per GPU (they wait on other ranks' kernels, which need not
 // run concurrently on a shared GPU): the host uses this path only then.
@@ -27,7 +28,7 @@ namespace {
 
 constexpr int kMaxRanks = 8;
 constexpr int kXThreads = 256;
-constexpr long long kPeerWaitCycles = 4000000000ll;  // ~2 s
+constexpr int64_t kDefaultPeerWaitNs = 2000000000ll;  // 2 s
 
 // The last CTA of the grid publishes a new epoch to every peer's flag slot [rank].
 __device__ __forceinline__ void signal_peers(const uint64_t* flag_ptrs, uint32_t* sync, int rank, int P) {
@@ -138,17 +139,22 @@ __global__ void __launch_bounds__(kXThreads) row_scatter_kernel(const uint4* __r
   signal_peers(flag_ptrs, sync, rank, P);
 }
 
-// One thread per rank q: wait until flags[q] has reached this rank's current epoch.
-__global__ void shard_wait_kernel(const uint32_t* flags, const uint32_t* sync, int P, int* err) {
+// One thread per rank q: wait until flags[q] has reached this rank's current epoch, for at
+// most `limit_ns` nanoseconds of the GPU's global timer; then record kErrTimeoutPeer and
+// return (the stream continues; the host reads the error word).
+__global__ void shard_wait_kernel(const uint32_t* flags, const uint32_t* sync, int P, int64_t limit_ns, int* err) {
   const int q = threadIdx.x;
   if (q >= P) return;
   const uint32_t e = sync[1];
-  const long long start = clock64();
+  uint64_t start;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(start));
   while (true) {
     uint32_t v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + q) : "memory");
     if (static_cast<int32_t>(v - e) >= 0) break;
-    if (clock64() - start > kPeerWaitCycles || error_raised(err)) {
+    uint64_t now;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+    if (static_cast<int64_t>(now - start) > limit_ns || error_raised(err)) {
       set_error(err, kErrTimeoutPeer);
       break;
     }
@@ -252,14 +258,16 @@ int ffb_shard_rows_p2p(const void* src, int mode, int R, int N, const void* dst_
   return cuda_status(static_cast<int>(cudaGetLastError()), "shard_rows_p2p launch");
 }
 
-int ffb_shard_wait_p2p(const void* flags, const void* sync, int P, void* stream) {
+int ffb_shard_wait_p2p(const void* flags, const void* sync, int P, int64_t limit_us, void* stream) {
   if (!flags || !sync) return fail(FFB_ERR_ARG, "shard_wait_p2p: null pointer");
   if (P < 1 || P > kMaxRanks) return fail(FFB_ERR_ARG, "shard_wait_p2p: P=%d", P);
+  if (limit_us > 3600ll * 1000000ll) return fail(FFB_ERR_ARG, "shard_wait_p2p: limit_us=%lld", static_cast<long long>(limit_us));
   DeviceInfo info;
   int st = device_info(&info);
   if (st != FFB_OK) return st;
-  shard_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const uint32_t*>(flags),
-                                                                       static_cast<const uint32_t*>(sync), P, info.err);
+  const int64_t limit_ns = limit_us > 0 ? limit_us * 1000 : kDefaultPeerWaitNs;
+  shard_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint32_t*>(flags), static_cast<const uint32_t*>(sync), P, limit_ns, info.err);
   return cuda_status(static_cast<int>(cudaGetLastError()), "shard_wait_p2p launch");
 }
 

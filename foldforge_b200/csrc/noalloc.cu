@@ -33,12 +33,13 @@ constexpr size_t kScratchBytes = static_cast<size_t>(kMaxTokens) * (kCs * 2 + 4 
 
 static __device__ __align__(256) uint8_t g_single_transition_scratch[kScratchBytes];
 
-constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mutex;
 void* g_scratch_ptr[kMaxDevices];
 
 // Device address of the scratch array on the current device (looked up once per device).
 int scratch_address(int device, void** out) {
+  if (device < 0 || device >= kMaxDevices)
+    return fail(FFB_ERR_ARG, "single_transition_fwd_noalloc: device index %d out of range", device);
   std::lock_guard<std::mutex> lock(g_scratch_mutex);
   if (g_scratch_ptr[device] == nullptr) {
     void* p = nullptr;

@@ -1,24 +1,27 @@
-"""Which backend serves which op: the table behind ``backend``, ``engine.ops`` and ``engine.unsupported``.
+"""Backend names, the op table and the per-op backend plan of the Pairformer pair stack.
 
-Mirrors FoldForge's policy module (``src/foldforge/modules/engine/backends.py:29-271``) for
-the Pairformer pair stack, with one backend name added: ``b200`` (the sm_100a kernels of
-this package). The reference engine's own names (``cuda``, ``triton``, ``anthropic``,
-``cueq``) stay VALID configuration values, so an existing FoldForge config parses, but no
-class here has them: asking for one is a refusal that runs ``pytorch`` with a reason, as the
-reference does for a class that lacks a backend (``choose_backend``, ``:137-165``).
+FoldForge chooses a backend per engine op class (``src/foldforge/modules/engine/backends.py:29-271``
+is its policy table); this package adds one name to it, ``b200`` (the sm_100a kernels). What
+is kept from FoldForge is the interface: the names below (``ENGINE_BACKENDS``, ``BACKENDS``,
+``OP_CLASSES``, ``BackendPlan.make / resolve / report`` ...), the configuration values they
+accept and the record :meth:`BackendPlan.report` writes into a load report.
 
-* ``Config.backend`` takes the backend names plus the policy alias ``miniworld`` = "the
-  engine's own kernels": here ``b200`` where the class has it and an sm_100 device exists,
-  else ``pytorch`` (not a refusal).
-* ``engine.ops`` pins single ops (the keys of ``OP_CLASSES``) to another backend.
-* ``engine.unsupported``: ``fallback`` (default) runs the ``pytorch`` backend of that module
-  for a call the chosen backend refuses, with ONE log line; ``error`` raises.
+Rules (the semantics FoldForge documents for its own names, with ``b200`` where the engine
+has ``cuda``):
+
+* ``miniworld`` means "the engine's own kernels wherever this machine runs them": ``b200`` for
+  a class that has it on an sm_100 device, else ``pytorch`` (not a refusal: nothing in
+  particular was asked for). ``cuequivariance`` is another spelling of ``cueq``.
+* A NAMED backend is a refusal when the class lacks it (``cuda`` / ``triton`` / ``anthropic``
+  / ``cueq`` are valid names that no class here has) or, for ``b200``, when there is no
+  sm_100 device; the op then runs ``pytorch`` and the reason is recorded.
+* ``engine.ops`` pins single ops to another name; ``engine.unsupported`` is ``fallback``
+  (run ``pytorch``, log once) or ``error`` (raise :class:`BackendUnsupportedError`).
 """
 
 from __future__ import annotations
 
 import logging
-from dataclasses import dataclass, field
 from typing import TYPE_CHECKING
 
 if TYPE_CHECKING:
@@ -28,15 +31,15 @@ logger = logging.getLogger("foldforge.backend")
 
 #: Backends a class of this package can have.
 ENGINE_BACKENDS = ("pytorch", "b200")
-#: The reference engine's kernel backends: valid names, served by no class here.
+#: The reference engine's kernel backends: valid configuration values that no class here has.
 FOREIGN_BACKENDS = ("cuda", "triton", "anthropic", "cueq")
-#: Policy aliases of ``Config.backend``; ``None`` = decided per class by :func:`choose_backend`.
+#: Policy aliases: ``None`` = decided per class (the engine's own kernels where they run).
 ALIASES: dict[str, str | None] = {"miniworld": None, "cuequivariance": "cueq"}
 BACKENDS = ("miniworld", "cuequivariance", *ENGINE_BACKENDS, *FOREIGN_BACKENDS)
 
-#: op -> the engine classes (by name, in :mod:`foldforge_b200.engine.modules`) that carry it.
-#: The keys are the names ``engine.ops`` takes (``backends.py:35-70``); ops outside the
-#: Pairformer pair stack have no class in this package.
+#: op (the names ``engine.ops`` takes) -> the engine classes that carry it, by class name in
+#: :mod:`foldforge_b200.engine.modules`. Ops outside the pair stack keep their key and have
+#: no class here.
 OP_CLASSES: dict[str, tuple[str, ...]] = {
     "trimul": ("TriangleMultiplication",),
     "triangle_attention": ("TriangleAttention", "TriangleAttentionAF3"),
@@ -55,165 +58,191 @@ UNSUPPORTED = ("fallback", "error")
 #: The compute capability the ``b200`` kernels are built for (sm_100a).
 B200_CAPABILITY = (10, 0)
 
+#: class name -> op, the inverse of :data:`OP_CLASSES`
+_OP_OF_CLASS = {name: op for op, names in OP_CLASSES.items() for name in names}
+
 
 class BackendUnsupportedError(RuntimeError):
     """A (backend, module) combination nothing serves, with ``engine.unsupported: error``."""
 
 
 def op_classes(op: str) -> tuple[type, ...]:
-    """The engine classes of ``op``."""
+    """The classes of this package that carry ``op`` (an op without any gives ``()``)."""
     from foldforge_b200.engine import modules
 
-    return tuple(getattr(modules, name) for name in OP_CLASSES[op] if hasattr(modules, name))
+    return tuple(cls for cls in (getattr(modules, name, None) for name in OP_CLASSES[op]) if cls is not None)
 
 
 def op_of(module: object) -> str | None:
-    """The op an engine module instance carries, or None."""
-    for op in OPS:
-        classes = op_classes(op)
-        if classes and isinstance(module, classes):
+    """The op an engine module carries: the first class on its MRO that the table names."""
+    for cls in type(module).__mro__:
+        op = _OP_OF_CLASS.get(cls.__name__)
+        if op is not None and cls.__module__ == "foldforge_b200.engine.modules":
             return op
     return None
 
 
 def serves(op: str) -> tuple[str, ...]:
-    """The backends some class of ``op`` has, in the policy's names (``miniworld`` when any has ``b200``)."""
-    have = {b for cls in op_classes(op) for b in cls.backends}
-    named = [b for b in ENGINE_BACKENDS if b in have]
-    return (*(["miniworld"] if "b200" in have else []), *named)
+    """Backends some class of ``op`` has, as policy names (``miniworld`` first when ``b200`` is among them)."""
+    have: set[str] = set()
+    for cls in op_classes(op):
+        have.update(cls.backends)
+    out = [name for name in ENGINE_BACKENDS if name in have]
+    return ("miniworld", *out) if "b200" in have else tuple(out)
 
 
 def __getattr__(name: str) -> object:
-    """``SERVES``: op -> :func:`serves`, derived from the classes on first use."""
-    if name == "SERVES":
-        return {op: serves(op) for op in OPS}
-    raise AttributeError(name)
+    """``SERVES`` (op -> :func:`serves`) is computed from the classes when first asked for."""
+    if name != "SERVES":
+        raise AttributeError(name)
+    return {op: serves(op) for op in OPS}
 
 
 def validate_ops(ops: Mapping[str, str]) -> dict[str, str]:
-    """``engine.ops``: known op names, known backends."""
-    unknown = sorted(set(ops) - set(OPS))
-    if unknown:
-        message = f"engine.ops names unknown op(s) {unknown}; known: {list(OPS)}"
-        raise ValueError(message)
-    bad = {op: b for op, b in ops.items() if b not in BACKENDS}
-    if bad:
-        message = f"engine.ops names unknown backend(s) {bad}; known: {list(BACKENDS)}"
-        raise ValueError(message)
+    """Check an ``engine.ops`` mapping: every key an op of :data:`OPS`, every value a backend name."""
+    bad_ops = sorted(k for k in ops if k not in OP_CLASSES)
+    if bad_ops:
+        raise ValueError(f"engine.ops names unknown op(s) {bad_ops}; known: {list(OPS)}")
+    bad_names = {k: v for k, v in ops.items() if v not in BACKENDS}
+    if bad_names:
+        raise ValueError(f"engine.ops names unknown backend(s) {bad_names}; known: {list(BACKENDS)}")
     return dict(ops)
 
 
 def capability(device: object | None) -> tuple[int, int] | None:
-    """The compute capability of a CUDA ``device`` (None without CUDA)."""
+    """``(major, minor)`` of a CUDA ``device`` (the current one for ``None``); ``None`` without CUDA."""
     import torch
 
-    if not torch.cuda.is_available() or getattr(device, "type", "cuda") != "cuda":
+    if getattr(device, "type", "cuda") != "cuda" or not torch.cuda.is_available():
         return None
-    index = getattr(device, "index", None)
-    return torch.cuda.get_device_capability(index)
+    return torch.cuda.get_device_capability(getattr(device, "index", None))
+
+
+def _refusal(name: str, cls: type, cc: tuple[int, int] | None) -> str | None:
+    """Why class ``cls`` cannot run the named backend ``name`` here (``None``: it can)."""
+    if name == "pytorch":
+        return None
+    if name not in cls.backends:
+        return f"{cls.__name__} has no {name!r} backend (available: {', '.join(cls.backends)})"
+    if name == "b200" and cc is None:
+        return "the b200 backend needs a CUDA device"
+    if name == "b200" and cc != B200_CAPABILITY:
+        return f"the b200 backend needs an sm_100 device (this one is sm_{cc[0]}{cc[1]})"
+    return None
 
 
 def choose_backend(requested: str, cls: type, device: object | None = None) -> tuple[str, str | None]:
-    """``(backend, reason)`` of one class: the backend it runs under ``requested`` and, when
-    that is not what was asked for, why (``backends.py:137-165`` with ``b200`` in place of
-    the engine's ``cuda``)."""
+    """``(backend, reason)``: what class ``cls`` runs when ``requested`` is asked for on ``device``,
+    and why that differs from the request (``None`` when it does not)."""
     name = ALIASES.get(requested, requested)
-    have = tuple(cls.backends)
     cc = capability(device)
     if name is None:
-        if "b200" in have and cc == B200_CAPABILITY:
-            return "b200", None
-        return "pytorch", None
-    if name == "pytorch":
-        return "pytorch", None
-    if name not in have:
-        return "pytorch", f"{cls.__name__} has no {name!r} backend (available: {', '.join(have)})"
-    if name == "b200" and cc is None:
-        return "pytorch", "the b200 backend needs a CUDA device"
-    if name == "b200" and cc != B200_CAPABILITY:
-        return "pytorch", f"the b200 backend needs an sm_100 device (this one is sm_{cc[0]}{cc[1]})"
-    return name, None
+        return ("b200" if "b200" in cls.backends and cc == B200_CAPABILITY else "pytorch"), None
+    reason = _refusal(name, cls, cc)
+    return ("pytorch", reason) if reason else (name, None)
 
 
-@dataclass(frozen=True)
 class Resolved:
-    """One op after the checks: what was asked, what runs, and why they differ."""
+    """One op after :meth:`BackendPlan.resolve`: what was asked, what runs, and why they differ."""
 
-    op: str
-    requested: str
-    backend: str
-    reason: str | None = None
+    __slots__ = ("op", "requested", "backend", "reason")
+
+    def __init__(self, op: str, requested: str, backend: str, reason: str | None = None) -> None:
+        self.op, self.requested, self.backend, self.reason = op, requested, backend, reason
+
+    def __repr__(self) -> str:
+        return f"Resolved({self.op!r}: {self.requested!r} -> {self.backend!r}, reason={self.reason!r})"
 
 
-@dataclass(frozen=True)
 class BackendPlan:
-    """The backend of every op for one loaded model (``backends.py:178-271``)."""
+    """The backend of every op of one loaded model: a default name, per-op pins and the
+    ``engine.unsupported`` policy. Build it with :meth:`make` (which validates), check it
+    against the classes and the machine with :meth:`resolve`."""
 
-    backend: str = "miniworld"
-    ops: tuple[tuple[str, str], ...] = ()
-    unsupported: str = "fallback"
-    resolved: dict[str, Resolved] = field(default_factory=dict, compare=False, hash=False)
+    def __init__(self, backend: str = "miniworld", ops: tuple[tuple[str, str], ...] = (),
+                 unsupported: str = "fallback") -> None:
+        self.backend = backend
+        self.ops = tuple(ops)
+        self.unsupported = unsupported
+        self._pins = dict(self.ops)
+        self.resolved: dict[str, Resolved] = {}
+
+    def __eq__(self, other: object) -> bool:
+        return isinstance(other, BackendPlan) and (self.backend, self.ops, self.unsupported) == (
+            other.backend, other.ops, other.unsupported)
+
+    def __hash__(self) -> int:
+        return hash((self.backend, self.ops, self.unsupported))
 
     @classmethod
     def make(cls, backend: str = "miniworld", ops: Mapping[str, str] | None = None,
              unsupported: str = "fallback") -> BackendPlan:
-        """A plan; ``backend`` and ``ops`` are validated here."""
+        """A validated plan (unknown backend, op or policy names raise ``ValueError``)."""
         if backend not in BACKENDS:
-            message = f"Unknown backend: {backend}"
-            raise ValueError(message)
+            raise ValueError(f"Unknown backend: {backend}")
         if unsupported not in UNSUPPORTED:
-            message = f"engine.unsupported must be one of {UNSUPPORTED}, got {unsupported!r}"
-            raise ValueError(message)
-        return cls(backend, tuple(sorted(validate_ops(ops or {}).items())), unsupported)
+            raise ValueError(f"engine.unsupported must be one of {UNSUPPORTED}, got {unsupported!r}")
+        pins = validate_ops(ops or {})
+        return cls(backend, tuple(sorted(pins.items())), unsupported)
 
     def requested(self, op: str) -> str:
-        """The backend asked for ``op``: its ``engine.ops`` entry, else ``backend``."""
-        return dict(self.ops).get(op, self.backend)
+        """The name asked for ``op``: its pin, else the plan's backend."""
+        return self._pins.get(op, self.backend)
 
     def of(self, op: str) -> str:
-        """The backend that runs ``op`` (after :meth:`resolve`)."""
-        resolved = self.resolved.get(op)
-        return resolved.backend if resolved is not None else self.requested(op)
+        """The backend that runs ``op``: resolved when :meth:`resolve` has run, else as requested."""
+        entry = self.resolved.get(op)
+        return self.requested(op) if entry is None else entry.backend
 
     def uses(self, *backends: str) -> bool:
-        """Whether any op is asked to run on one of ``backends``."""
-        names = {ALIASES.get(b, b) or b for b in backends} | set(backends)
-        return any(self.requested(op) in names or ALIASES.get(self.requested(op)) in names for op in OPS)
-
-    def for_class(self, cls: type, device: object | None = None) -> tuple[str, str | None]:
-        """:func:`choose_backend` for ``cls`` under this plan's request for its op."""
-        op = next(op for op in OPS if op_classes(op) and issubclass(cls, op_classes(op)))
-        return choose_backend(self.requested(op), cls, device)
-
-    def resolve(self, device: object | None = None) -> BackendPlan:
-        """Check every op against the classes and the machine; fill ``resolved``; apply ``unsupported``."""
-        self.resolved.clear()
+        """Whether some op is asked to run one of ``backends`` (policy or engine names)."""
+        wanted = set(backends) | {ALIASES.get(b) or b for b in backends}
         for op in OPS:
             asked = self.requested(op)
+            if asked in wanted or ALIASES.get(asked) in wanted:
+                return True
+        return False
+
+    def for_class(self, cls: type, device: object | None = None) -> tuple[str, str | None]:
+        """:func:`choose_backend` for ``cls`` under the request for its op."""
+        for klass in cls.__mro__:
+            op = _OP_OF_CLASS.get(klass.__name__)
+            if op is not None:
+                return choose_backend(self.requested(op), cls, device)
+        raise KeyError(f"{cls.__name__} carries no op of the table")
+
+    def resolve(self, device: object | None = None) -> BackendPlan:
+        """Decide every op against its classes on ``device``: an op runs the first backend one
+        of its classes accepts; when none accepts, ``pytorch`` with the first class's reason.
+        Ops without a class here are left out. Refused ops raise under ``error`` and are
+        named in ONE warning under ``fallback``."""
+        self.resolved = {}
+        for op in OPS:
             classes = op_classes(op)
             if not classes:
-                continue  # no class of this package carries the op
-            choices = [choose_backend(asked, cls, device) for cls in classes]
-            ok = [name for name, reason in choices if reason is None]
-            if ok:
-                self.resolved[op] = Resolved(op, asked, ok[0])
+                continue
+            asked = self.requested(op)
+            decisions = [choose_backend(asked, cls, device) for cls in classes]
+            accepted = next((name for name, reason in decisions if reason is None), None)
+            if accepted is not None:
+                self.resolved[op] = Resolved(op, asked, accepted)
             else:
-                self.resolved[op] = Resolved(op, asked, "pytorch", choices[0][1])
-        missing = [r for r in self.resolved.values() if r.reason is not None]
-        if missing and self.unsupported == "error":
-            lines = "; ".join(f"{r.op} on {r.requested}: {r.reason}" for r in missing)
-            message = f"backend ops no engine class serves (engine.unsupported: error): {lines}"
-            raise BackendUnsupportedError(message)
-        if missing:
-            lines = "; ".join(f"{r.op} ({r.requested}: {r.reason})" for r in missing)
-            logger.warning("backend %s: running the engine pytorch backend for %s", self.backend, lines)
+                self.resolved[op] = Resolved(op, asked, "pytorch", decisions[0][1])
+        refused = [r for r in self.resolved.values() if r.reason is not None]
+        if refused and self.unsupported == "error":
+            detail = "; ".join(f"{r.op} on {r.requested}: {r.reason}" for r in refused)
+            raise BackendUnsupportedError(f"backend ops no engine class serves (engine.unsupported: error): {detail}")
+        if refused:
+            detail = "; ".join(f"{r.op} ({r.requested}: {r.reason})" for r in refused)
+            logger.warning("backend %s: running the engine pytorch backend for %s", self.backend, detail)
         return self
 
     def report(self) -> dict[str, object]:
-        """The load report's record: the backend of every op and each refusal's reason."""
+        """The load report's record: ``backend``, ``ops`` (op -> backend), ``fallbacks``
+        (op -> "requested: reason") and ``unsupported``."""
         return {
             "backend": self.backend,
             "ops": {op: r.backend for op, r in self.resolved.items()},
-            "fallbacks": {op: f"{r.requested}: {r.reason}" for op, r in self.resolved.items() if r.reason is not None},
+            "fallbacks": {op: f"{r.requested}: {r.reason}" for op, r in self.resolved.items() if r.reason},
             "unsupported": self.unsupported,
         }

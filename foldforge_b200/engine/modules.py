@@ -55,10 +55,11 @@ class MasterWeights:
 
 
 class LayerNorm(nn.LayerNorm):
-    """The engine ``LayerNorm``: fp32 affine under any cast; backends ``pytorch`` / ``b200``."""
+    """The engine ``LayerNorm``: fp32 affine under any cast; backends ``pytorch`` / ``b200``.
+    Not a residual module, so it has no ``dead`` flag."""
 
     backends = ("pytorch", "b200")
-    dead = False
+    dispatches_policy = True
 
     def __init__(self, d, eps: float = 1e-5, bias: bool = True, elementwise_affine: bool = True) -> None:
         super().__init__(d, eps=eps, elementwise_affine=elementwise_affine, bias=bias)
@@ -132,14 +133,41 @@ def _library_reason() -> str | None:
 
 
 def _dispatch(module: nn.Module, *args, **kwargs):
+    """Run ``module`` on its backend. A call the backend refuses (``unsupported`` gives a
+    reason) raises :class:`BackendUnsupported` unless the module is guarded
+    (:func:`foldforge_b200.engine.policy.guard`): then its ``engine.unsupported`` policy runs
+    the ``pytorch`` backend (one log line) or raises, and the call is counted in the
+    observations."""
     backend = module.backend
-    if backend != "pytorch":
-        reason = module.unsupported(*args, **kwargs)
-        if reason is not None:
+    guarded = module.__dict__.get("_ffb_guarded", False)
+    served = backend
+    reason = None if backend == "pytorch" else module.unsupported(*args, **kwargs)
+    if reason is not None:
+        if not guarded:
             raise BackendUnsupported(f"{type(module).__name__} backend {backend!r}: {reason}")
-    if module.dead:
-        return args[0]
-    return getattr(module, f"_forward_{backend}")(*args, **kwargs)
+        from foldforge_b200.engine import policy
+
+        served = policy.fallback_backend(module, backend, *args, **kwargs)
+        policy.refuse(module, reason, served)
+    if guarded:
+        from foldforge_b200.engine.serving import observe_call
+
+        observe_call(module, backend, reason, served)
+    return getattr(module, f"_forward_{served}")(*args, **kwargs)
+
+
+def honours_dead(forward):
+    """A residual op's ``_forward_<backend>``: a module flagged ``dead`` returns its residual
+    input unchanged when it runs without grad outside training (``modules/dense/dead.py:1-11``),
+    whichever caller (this package's dispatch or FoldForge's own guard) invoked the backend."""
+
+    def run(self, x, *args, **kwargs):
+        if self.dead and not self.training and not torch.is_grad_enabled():
+            return x
+        return forward(self, x, *args, **kwargs)
+
+    run.__name__, run.__doc__, run.__wrapped__ = forward.__name__, forward.__doc__, forward
+    return run
 
 
 def _pair_mask(key_mask: Tensor | None, x: Tensor) -> Tensor:
@@ -163,6 +191,8 @@ class _PairOp(MasterWeights, nn.Module):
     """Shared plumbing of the pair ops: backend selection, refusals, the packed-weight cache."""
 
     backends = ("pytorch", "b200")
+    dispatches_policy = True
+    #: a flagged module returns its residual input unchanged (``honours_dead``)
     dead = False
     #: channels the b200 kernels are built for
     b200_channels = 128
@@ -192,10 +222,12 @@ class _PairOp(MasterWeights, nn.Module):
         return None
 
     def _cached_pack(self, pack) -> Tensor:
-        key = tuple((p.data_ptr(), p._version, p.device) for p in self.parameters())
+        """The packed device image of the weights, rebuilt only when a parameter changed
+        (its storage or version): ``pack(weights)`` gets the state dict then."""
+        key = tuple((p.data_ptr(), p._version) for p in self.parameters())
         if self._packed is None or self._packed[0] != key:
             with torch.no_grad():
-                self._packed = (key, pack())
+                self._packed = (key, pack(dict(self.state_dict())))
         return self._packed[1]
 
     def _key_mask(self, x: Tensor, key_mask: Tensor | None) -> Tensor:
@@ -248,6 +280,7 @@ class TriangleMultiplication(_PairOp):
     def forward(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
         return _dispatch(self, x, key_mask)
 
+    @honours_dead
     def _forward_pytorch(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
         z = x.float()
         v = _ln(z, self.ln_pair)
@@ -259,11 +292,11 @@ class TriangleMultiplication(_PairOp):
         delta = _linear(_ln(u, self.ln_out), self.to_out) * torch.sigmoid(_linear(v, self.to_gate))
         return self._zero_masked(x, delta, key_mask)
 
+    @honours_dead
     def _forward_b200(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
         from foldforge_b200 import kernels
 
-        weights = {k: v for k, v in self.state_dict().items()}
-        packed = self._cached_pack(lambda: kernels.trimul_prepare(weights, x.device))
+        packed = self._cached_pack(lambda w: kernels.trimul_prepare(w, x.device))
         return kernels.trimul(x, self._key_mask(x, key_mask), packed, outgoing=self.outgoing,
                               masked_zero=self._masked_zero())
 
@@ -312,6 +345,7 @@ class TriangleAttention(_PairOp):
     def forward(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
         return _dispatch(self, x, key_mask)
 
+    @honours_dead
     def _forward_pytorch(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
         z = x.float()
         b, n = z.shape[0], z.shape[1]
@@ -335,11 +369,11 @@ class TriangleAttention(_PairOp):
             delta = delta.transpose(1, 2)
         return self._zero_masked(x, delta, key_mask)
 
+    @honours_dead
     def _forward_b200(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
         from foldforge_b200 import kernels
 
-        weights = dict(self.state_dict())
-        packed = self._cached_pack(lambda: kernels.triattn_prepare(weights, x.device))
+        packed = self._cached_pack(lambda w: kernels.triattn_prepare(w, x.device))
         return kernels.triattn(x, self._key_mask(x, key_mask), packed, starting=self.starting,
                                masked_zero=self._masked_zero())
 
@@ -381,6 +415,7 @@ class Transition(_PairOp):
     def forward(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
         return _dispatch(self, x, key_mask)
 
+    @honours_dead
     def _forward_pytorch(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
         v = _ln(x.float(), self.ln_in)
         delta = _linear(F.silu(_linear(v, self.expand_a)) * _linear(v, self.expand_b), self.squeeze)
@@ -389,14 +424,14 @@ class Transition(_PairOp):
             delta = delta * m[..., None]
         return (x.float() + delta).to(x.dtype)
 
+    @honours_dead
     def _forward_b200(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
         from foldforge_b200 import kernels
 
-        weights = dict(self.state_dict())
         if self.d == 128:
-            packed = self._cached_pack(lambda: kernels.transition_prepare(weights, x.device))
+            packed = self._cached_pack(lambda w: kernels.transition_prepare(w, x.device))
             return kernels.transition(x, key_mask, packed, masked_zero=self._masked_zero())
-        packed = self._cached_pack(lambda: kernels.single_transition_prepare(weights, x.device))
+        packed = self._cached_pack(lambda w: kernels.single_transition_prepare(w, x.device))
         return kernels.single_transition(x, key_mask, packed, masked_zero=self._masked_zero())
 
 
@@ -436,6 +471,7 @@ class AttentionPairBias(_PairOp):
                 extra_pair_bias: Tensor | None = None) -> Tensor:
         return _dispatch(self, s, z, key_mask, extra_pair_bias)
 
+    @honours_dead
     def _forward_pytorch(self, s: Tensor, z: Tensor, key_mask: Tensor | None = None,
                          extra_pair_bias: Tensor | None = None) -> Tensor:
         b, n, cs = s.shape
@@ -459,14 +495,17 @@ class AttentionPairBias(_PairOp):
             delta = delta * key_mask.float()[..., None]
         return (s.float() + delta).to(s.dtype)
 
+    @honours_dead
     def _forward_b200(self, s: Tensor, z: Tensor, key_mask: Tensor | None = None,
                       extra_pair_bias: Tensor | None = None) -> Tensor:
         from foldforge_b200 import kernels
 
-        sd = dict(self.state_dict())
-        if "to_query.bias" not in sd or sd["to_query.bias"] is None:
-            sd["to_query.bias"] = torch.zeros(self.d_single, device=s.device)
-        packed = self._cached_pack(lambda: kernels.apb_prepare(sd, s.device))
+        def pack(w: dict[str, Tensor]) -> Tensor:
+            if w.get("to_query.bias") is None:
+                w["to_query.bias"] = torch.zeros(self.d_single, device=s.device)
+            return kernels.apb_prepare(w, s.device)
+
+        packed = self._cached_pack(pack)
         mask = self._key_mask(s, key_mask)
         return kernels.attention_pair_bias(s, z, mask, packed, extra_pair_bias=extra_pair_bias,
                                            gate_bias=self.gate_bias, masked_zero=self._masked_zero())
@@ -502,7 +541,6 @@ class PairformerBlock(MasterWeights, nn.Module):
     """
 
     backends = ("pytorch", "b200")
-    dead = False
 
     def __init__(self, config: PairformerConfig) -> None:
         super().__init__()
@@ -557,7 +595,6 @@ class Pairformer(MasterWeights, nn.Module):
     """A stack of :class:`PairformerBlock` (the trunk), run in order."""
 
     backends = ("pytorch", "b200")
-    dead = False
 
     def __init__(self, config: PairformerConfig, n_blocks: int) -> None:
         super().__init__()

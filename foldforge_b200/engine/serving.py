@@ -1,69 +1,62 @@
-"""Host-side observations of the op modules a model holds: which backend each runs and which calls it refused.
+"""Host-side counts of which backend served each engine op module, and which calls it refused.
 
-Same record shape as ``src/foldforge/modules/engine/serving.py:36-79`` (``report_observations``).
-The counters observe Python calls (eager execution and graph capture), not graph replays;
-they are not a kernel trace.
+The counts live in one registry keyed weakly by module (a module that is freed takes its
+counts with it) and are filled by the op classes' dispatch when a module is guarded
+(:func:`foldforge_b200.engine.policy.guard`). They count Python-level calls (eager runs and
+the call recorded while a CUDA graph is captured), never graph replays, and are not a
+kernel trace. :func:`report_observations` returns the record FoldForge's serving report
+uses (``src/foldforge/modules/engine/serving.py:36-79``: the same keys per module).
 """
 
 from __future__ import annotations
 
+import weakref
 from collections import Counter
-from dataclasses import dataclass, field
 from typing import Any
 
 import torch
 
-_STATS_ATTR = "_foldforge_observations"
-
-
-@dataclass
-class Observations:
-    """Calls of one module, aggregated by backend and by refusal reason."""
-
-    served: Counter[str] = field(default_factory=Counter)
-    refused: Counter[str] = field(default_factory=Counter)
-
-
-def observations_of(module: torch.nn.Module) -> Observations:
-    """The module's counters (created on first use)."""
-    stats = module.__dict__.get(_STATS_ATTR)
-    if stats is None:
-        stats = Observations()
-        object.__setattr__(module, _STATS_ATTR, stats)
-    return stats
+#: module -> Counter over ("served", backend) and ("refused", reason)
+_COUNTS: weakref.WeakKeyDictionary[torch.nn.Module, Counter] = weakref.WeakKeyDictionary()
 
 
 def observe_call(module: torch.nn.Module, backend: str, refusal: str | None, served_by: str = "pytorch") -> None:
-    """Record one call: ``backend`` ran it, or ``refusal`` sent it to ``served_by``."""
+    """Count one call of ``module``: served by ``backend``, or refused for ``refusal`` and served by ``served_by``."""
     if torch.compiler.is_compiling():
-        return
-    stats = observations_of(module)
+        return  # a traced region has no per-call host observation
+    counts = _COUNTS.setdefault(module, Counter())
     if refusal is None:
-        stats.served[backend] += 1
+        counts[("served", backend)] += 1
     else:
-        stats.refused[refusal] += 1
-        stats.served[served_by] += 1
+        counts[("refused", refusal)] += 1
+        counts[("served", served_by)] += 1
 
 
 def reset_observations(model: torch.nn.Module) -> None:
-    """Start observations afresh."""
+    """Forget the counts of every module of ``model``."""
     for module in model.modules():
-        module.__dict__.pop(_STATS_ATTR, None)
+        _COUNTS.pop(module, None)
+
+
+def _split(counts: Counter | None, kind: str) -> dict[str, int]:
+    if counts is None:
+        return {}
+    return {key: n for (k, key), n in counts.items() if k == kind}
 
 
 def report_observations(model: torch.nn.Module) -> dict[str, Any]:
-    """The op modules of ``model``: their selected backend and what was observed on them."""
-    modules = {}
+    """Every guarded or observed module of ``model``: its class, selected backend and counts."""
+    modules: dict[str, dict[str, Any]] = {}
     for name, module in model.named_modules():
-        stats = module.__dict__.get(_STATS_ATTR)
-        if stats is None and not getattr(module, "_foldforge_guarded", False):
+        counts = _COUNTS.get(module)
+        if counts is None and not module.__dict__.get("_ffb_guarded", False):
             continue
         modules[name or "<root>"] = {
             "class": type(module).__name__,
             "backend": getattr(module, "backend", None),
-            "host_observed": stats is not None,
-            "served_host_calls": {} if stats is None else dict(stats.served),
-            "refused_host_calls": {} if stats is None else dict(stats.refused),
+            "host_observed": counts is not None,
+            "served_host_calls": _split(counts, "served"),
+            "refused_host_calls": _split(counts, "refused"),
         }
     return {
         "coverage": "engine_modules_with_a_backend_guard",

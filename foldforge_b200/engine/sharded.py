@@ -23,6 +23,7 @@ legacy/reference/transition.py:28-59, legacy/transformer.py:88-133).
 from __future__ import annotations
 
 import ctypes
+import socket
 
 import torch
 import torch.distributed as dist
@@ -109,7 +110,8 @@ class _PeerExchange:
         assert p <= 8
 
     def _wait(self) -> None:
-        _lib.call("ffb_shard_wait_p2p", _ptr(self.flags.local), _ptr(self.sync), self.comm.world, _stream())
+        _lib.call("ffb_shard_wait_p2p", _ptr(self.flags.local), _ptr(self.sync), self.comm.world,
+                  self.comm.wait_limit_us, _stream())
 
     def transpose(self, x: Tensor) -> Tensor:
         r, n, c = x.shape
@@ -164,15 +166,35 @@ class _PeerExchange:
             self.flags]
 
 
+def device_identity(device: torch.device) -> tuple[str, str]:
+    """``(host name, device UUID)`` of this rank's GPU: what decides whether two ranks can
+    share memory over NVLink (same host) and whether their kernels may wait on one another
+    (different devices)."""
+    return socket.gethostname(), str(torch.cuda.get_device_properties(device).uuid)
+
+
+def peer_path_allowed(identities: list[tuple[str, str]]) -> bool:
+    """Whether ranks with these ``(host, device)`` identities may use the peer-memory
+    exchanges: all on one host (CUDA IPC does not cross hosts), every rank on its own device
+    (exchange kernels wait for the peers' kernels, which need not run concurrently on a
+    shared GPU), at most 8 ranks."""
+    hosts = {host for host, _ in identities}
+    devices = [dev for _, dev in identities]
+    return 1 < len(identities) <= 8 and len(hosts) == 1 and len(set(devices)) == len(devices)
+
+
 class ShardComm:
     """The two collectives of the schedule over one process group.
 
-    With NCCL and one rank per GPU (``peer="auto"``) the exchanges run over NVLink peer
-    memory (:class:`_PeerExchange`: one kernel writes each transpose / gather straight into
-    the peers' buffers); otherwise NCCL collectives on device tensors, or host copies for
-    other backends (gloo). ``world == 1`` (no group) makes both collectives local."""
+    With NCCL, one host and one GPU per rank (``peer="auto"``; checked once by gathering every
+    rank's host name and device UUID) the exchanges run over NVLink peer memory
+    (:class:`_PeerExchange`: one kernel writes each transpose / gather straight into the peers'
+    buffers, then a wait bounded by ``wait_limit_us``, 0 = the library's 2 s); otherwise NCCL
+    collectives on device tensors, or host copies for other backends (gloo). ``world == 1``
+    (no group) makes both collectives local."""
 
-    def __init__(self, group: dist.ProcessGroup | None = None, *, peer: str = "auto", trimul: str = "auto"):
+    def __init__(self, group: dist.ProcessGroup | None = None, *, peer: str = "auto", trimul: str = "auto",
+                 wait_limit_us: int = 0):
         self.group = group
         if dist.is_available() and dist.is_initialized():
             self.rank = dist.get_rank(group)
@@ -182,14 +204,26 @@ class ShardComm:
             self.rank, self.world, self.nccl = 0, 1, False
         self.peer_mode = peer
         self.trimul_mode = trimul
+        self.wait_limit_us = int(wait_limit_us)
         self._peer: _PeerExchange | None = None
+        self._peer_ok: bool | None = None
+
+    def peer_capable(self, identity: tuple[str, str] | None = None) -> bool:
+        """Collective (every rank calls it at the same point): gather each rank's
+        :func:`device_identity` (or the given one) and decide :func:`peer_path_allowed`."""
+        mine = identity if identity is not None else device_identity(torch.device("cuda", torch.cuda.current_device()))
+        everyone: list = [None] * self.world
+        dist.all_gather_object(everyone, mine, group=self.group)
+        return peer_path_allowed([tuple(x) for x in everyone])
 
     def _peer_path(self, x: Tensor) -> _PeerExchange | None:
         if self.peer_mode == "off" or self.world == 1 or not self.nccl or not x.is_cuda:
             return None
         if self._peer is None:
-            if torch.cuda.device_count() < self.world or self.world > 8:
-                return None  # ranks sharing a GPU: their kernels must not wait on one another
+            if self._peer_ok is None:
+                self._peer_ok = self.peer_capable()
+            if not self._peer_ok:
+                return None  # ranks on several hosts or sharing a GPU: NCCL collectives instead
             self._peer = _PeerExchange(self, x.device)
         return self._peer
 

@@ -214,8 +214,9 @@ int ffb_apb_shard_single(const void* s, const uint8_t* mask, const void* packed,
  * every rank's buffer dst_ptrs[q] at offset rank * bytes. Both end by publishing a new epoch
  * (counted in this rank's `sync` words, two uint32 zeroed at allocation) into slot [rank] of
  * every rank's flag array (flag_ptrs[q]: P uint32); ffb_shard_wait_p2p makes the stream wait
- * until every slot of this rank's `flags` has reached this rank's epoch (a bounded wait: a
- * peer that never signals sets the device error word, code 106, instead of hanging).
+ * until every slot of this rank's `flags` has reached this rank's epoch, for at most
+ * `limit_us` microseconds of GPU wall-clock time (<= 0: 2 s): a peer that never signals sets
+ * the device error word (code 106) and the stream goes on instead of hanging.
  * dst_ptrs and flag_ptrs are device arrays of P uint64 addresses (peers' mapped addresses,
  * this rank's own). Every rank issues the same sequence of exchanges; consecutive exchanges
  * must write different buffers. P <= 8. */
@@ -228,7 +229,7 @@ int ffb_shard_transpose_p2p(const void* x, const void* dst_ptrs, const void* fla
                             int row0, int rank, int P, void* stream);
 int ffb_shard_gather_p2p(const void* src, size_t bytes, const void* dst_ptrs, const void* flag_ptrs, void* sync,
                          int rank, int P, void* stream);
-int ffb_shard_wait_p2p(const void* flags, const void* sync, int P, void* stream);
+int ffb_shard_wait_p2p(const void* flags, const void* sync, int P, int64_t limit_us, void* stream);
 
 /* Channel-sharded TriMul contraction (P >= 4 ranks move less data this way than by gathering
  * the right operand): rank q owns channels [q C, (q + 1) C), C = 128 / P.

@@ -132,7 +132,11 @@ def triangle_attention(
     v = heads(_linear(x, _p(p, "to_value.weight", dtype)))
     pm = _pair_mask(tokens, dtype) > 0  # [rows, keys]
     keep = pm[:, None, None, :]
-    o = _masked_softmax_attention(q, k, v, bias[None], keep)  # [rows, H, n, d]
+    # rows are independent problems: take them in chunks so the [rows, H, n, n] logits of a
+    # large N never exist at once (64 rows at N = 1024: 1 GiB of fp32 logits)
+    step = max(1, (1 << 28) // max(1, n_head * n * n))
+    o = torch.cat([_masked_softmax_attention(q[r:r + step], k[r:r + step], v[r:r + step], bias[None],
+                                             keep[r:r + step]) for r in range(0, n, step)])  # [rows, H, n, d]
     o = o.permute(0, 2, 1, 3).reshape(n, n, hidden)
     o = torch.sigmoid(_linear(x, _p(p, "to_gate.weight", dtype))) * o
     delta = _linear(o, _p(p, "to_out.weight", dtype))

@@ -1,7 +1,7 @@
 """Generate the golden fixtures from the REFERENCE's own legacy Pairformer block.
 
 Run in the build container only (it imports the FoldForge source tree, which does not
-travel to GPU boxes): ``python tests/golden/make_golden.py [--reference PATH]``.
+travel to GPU boxes): ``python tests/golden/make_golden.py --reference <FoldForge checkout>/src``.
 
 For every case it
 
@@ -182,7 +182,8 @@ AF3 = BlockShape()
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference/src")
+    ap.add_argument("--reference", required=True,
+                    help="the src/ directory of a FoldForge checkout (the package foldforge is imported from it)")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     _stub_engine()

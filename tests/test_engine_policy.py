@@ -104,11 +104,13 @@ def test_unsupported_call_falls_back_once_and_logs_once(monkeypatch, caplog):
     monkeypatch.setattr(backends, "capability", lambda _d: B200)
     model = _Model()
     expected = Transition.forward(model.transition, _x())  # pytorch backend of the same weights
+    unguarded = factories.transition(128, 4, precision="fp32")
+    unguarded.set_backend("b200")
+    with pytest.raises(BackendUnsupported):  # a direct call outside the range, no policy
+        unguarded(_x())
     policy.apply_plan(model, backends.BackendPlan.make("b200"))
     assert model.transition.backend == "b200"
     assert model.transition.unsupported(_x()) is not None  # a CPU tensor is outside the b200 range
-    with pytest.raises(BackendUnsupported):
-        Transition.forward(model.transition, _x())
     with caplog.at_level(logging.WARNING, logger="foldforge.backend"):
         first = model.transition(_x())
         second = model.transition(_x())
@@ -159,3 +161,28 @@ def test_b200_refuses_widths_it_was_not_built_for(monkeypatch):
     assert "widths" in apb.unsupported(torch.randn(1, 4, 256), torch.randn(1, 4, 4, 128))
     with pytest.raises(BackendUnsupported):
         LayerNorm(8).set_backend("cuda")
+
+
+def test_dead_modules_return_their_residual_input():
+    """``modules/dense/dead.py``: a flagged residual op returns its input unchanged when it
+    runs without grad outside training; the block skips exactly that op."""
+    block = pairformer_block(d_pair=128, triangle_model="af3", d_single=384, precision="fp32").eval()
+    g = torch.Generator().manual_seed(3)
+    z, s = torch.randn(1, 6, 6, 128, generator=g), torch.randn(1, 6, 384, generator=g)
+    mask = torch.ones(1, 6, dtype=torch.bool)
+    with torch.no_grad():
+        live = block.tri_atten_starting(z, mask)
+        block.tri_atten_starting.dead = True
+        assert torch.equal(block.tri_atten_starting(z, mask), z)
+        # the block with the op skipped: every other op still runs
+        want = block.tri_multi_incoming(block.tri_multi_outgoing(z, mask), mask)
+        want = block.transition_pair(block.tri_atten_ending(want, mask), mask)
+        got_pair, _ = block(z, mask, s)
+        torch.testing.assert_close(got_pair, want)
+    assert not torch.equal(live, z)
+    with torch.enable_grad():  # with grad the flag is ignored
+        torch.testing.assert_close(block.tri_atten_starting(z, mask), live)
+    block.train()
+    with torch.no_grad():  # and in training
+        torch.testing.assert_close(block.tri_atten_starting(z, mask), live)
+    assert not hasattr(LayerNorm, "dead")  # a LayerNorm is not a residual module

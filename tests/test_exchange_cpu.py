@@ -72,8 +72,10 @@ def test_channel_scatter_rejects_bad_modes_and_rank_counts(mode, nranks):
 
 def test_wait_rank_count_and_alloc_size_are_checked():
     lib = _lib_or_skip()
-    assert _status(lib, "ffb_shard_wait_p2p", _fake(), _fake(), 9, P(0)) == ERR_ARG
-    assert _status(lib, "ffb_shard_wait_p2p", P(0), _fake(), 2, P(0)) == ERR_ARG
+    assert _status(lib, "ffb_shard_wait_p2p", _fake(), _fake(), 9, 0, P(0)) == ERR_ARG
+    assert _status(lib, "ffb_shard_wait_p2p", P(0), _fake(), 2, 0, P(0)) == ERR_ARG
+    # a wait limit above one hour is refused before anything is launched
+    assert _status(lib, "ffb_shard_wait_p2p", _fake(), _fake(), 2, 3600 * 10**6 + 1, P(0)) == ERR_ARG
     ptr = P()
     handle = (ctypes.c_uint8 * 64)()
     assert _status(lib, "ffb_p2p_alloc", ctypes.c_size_t(0), ctypes.byref(ptr), handle) == ERR_ARG

@@ -114,3 +114,84 @@ def test_rows_refuses_an_uneven_split():
     comm.world = 5
     with pytest.raises(ValueError):
         comm.rows(12)
+
+
+def test_peer_path_needs_one_host_and_a_device_per_rank():
+    from foldforge_b200.engine.sharded import peer_path_allowed
+
+    assert peer_path_allowed([("h", "gpu-0"), ("h", "gpu-1")])
+    assert not peer_path_allowed([("h", "gpu-0"), ("h", "gpu-0")])      # two ranks on one GPU
+    assert not peer_path_allowed([("h1", "gpu-0"), ("h2", "gpu-1")])    # two hosts: no CUDA IPC
+    assert not peer_path_allowed([("h", f"gpu-{i}") for i in range(9)])  # more ranks than the kernels take
+    assert not peer_path_allowed([("h", "gpu-0")])
+
+
+def _identity_rank(rank: int, world: int, port: int, fake: list, expect: bool) -> None:
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        assert ShardComm().peer_capable(identity=tuple(fake[rank])) is expect
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("fake,expect", [([("h", "gpu-0"), ("h", "gpu-1")], True),
+                                         ([("h", "gpu-3"), ("h", "gpu-3")], False),
+                                         ([("a", "gpu-0"), ("b", "gpu-1")], False)])
+def test_ranks_agree_on_the_exchange_path_from_their_identities(fake, expect):
+    """Every rank gathers the (host, device) identities and takes the same decision: a shared
+    GPU or a second host sends the exchanges to the NCCL / gloo collectives."""
+    mp.spawn(_identity_rank, args=(2, _free_port(), fake, expect), nprocs=2, join=True)
+
+
+def _leaving_rank(rank: int, world: int, port: int, queue) -> None:
+    import datetime
+    import time
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    comm = ShardComm()
+    n = 4 * world
+    z = torch.arange(n * n * 3, dtype=torch.float32).reshape(n, n, 3)
+    r, row0 = comm.rows(n)
+    rows = z[row0:row0 + r].contiguous()
+    comm.transpose(rows)  # step 1: every rank takes part
+    if rank == world - 1:
+        queue.put(("left", rank))
+        queue.close()
+        queue.join_thread()  # the message is out before the process goes
+        os._exit(0)  # leaves between steps, with nothing in flight
+    start = time.monotonic()
+    try:
+        comm.transpose(rows)  # step 2: the peer is gone
+    except Exception as exc:  # noqa: BLE001 - any error from the collective is the expected outcome
+        queue.put(("error", rank, type(exc).__name__, time.monotonic() - start))
+    else:
+        queue.put(("completed", rank))
+    queue.close()
+    queue.join_thread()
+    os._exit(0)
+
+
+def test_a_rank_that_leaves_between_steps_ends_the_next_exchange_with_an_error():
+    """A rank exits between two blocks; the other rank's next transpose must end with an error
+    within the process group's short timeout instead of waiting for good."""
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_rank, args=(r, 2, port, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank was still waiting after 120 s"
+    results = sorted((queue.get(timeout=5) for _ in range(2)), key=lambda t: t[1])
+    assert results[1] == ("left", 1)
+    outcome = results[0]
+    assert outcome[0] == "error", outcome
+    assert outcome[3] < 60.0, outcome
