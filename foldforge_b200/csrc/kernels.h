@@ -114,4 +114,34 @@ int single_transition_prepare(const TransitionWeights& w, void* packed, cudaStre
 int single_transition_forward(const void* s, const uint8_t* mask, const void* packed, void* out, void* workspace,
                               int B, int N, int masked_zero, const DeviceInfo& info, cudaStream_t stream);
 
+// ---- the fp32 / any-width path (generic.cu); weights in the engine's [out, in] layout
+struct GenericTriMulWeights {
+  const float *ln_w, *ln_b, *ln_out_w, *ln_out_b, *to_left, *to_right, *to_left_gate, *to_right_gate, *to_out,
+      *to_gate;
+};
+struct GenericTriAttnWeights {
+  const float *ln_w, *ln_b, *to_bias, *to_query, *to_key, *to_value, *to_gate, *to_out;
+};
+struct GenericTransitionWeights {
+  const float *ln_w, *ln_b, *expand_a, *expand_b, *squeeze;
+};
+struct GenericApbWeights {
+  const float *ln_single_w, *ln_single_b, *to_query, *to_query_b, *to_key, *to_value, *to_gate, *to_out, *ln_pair_w,
+      *to_bias;
+};
+size_t generic_trimul_workspace(int B, int N, int c, int h);
+int generic_trimul(const float* z, const uint8_t* mask, const GenericTriMulWeights& w, float* out, void* workspace,
+                   int B, int N, int c, int h, int outgoing, int masked_zero, cudaStream_t stream);
+size_t generic_triattn_workspace(int B, int N, int c, int H, int d);
+int generic_triattn(const float* z, const uint8_t* mask, const GenericTriAttnWeights& w, float* out, void* workspace,
+                    int B, int N, int c, int H, int d, int starting, int masked_zero, cudaStream_t stream);
+size_t generic_transition_workspace(int64_t rows, int c, int n);
+int generic_transition(const float* x, const uint8_t* mask, const GenericTransitionWeights& w, float* out,
+                       void* workspace, int64_t rows, int c, int n, int mask_kind, int mask_n, cudaStream_t stream);
+size_t generic_apb_workspace(int B, int N, int cs, int cz, int H);
+int generic_apb(const float* s, const float* z, const uint8_t* mask, const GenericApbWeights& w, const float* extra,
+                float* out, void* workspace, int B, int N, int cs, int cz, int H, float gate_bias, int masked_zero,
+                cudaStream_t stream);
+
 }  // namespace ffb
+

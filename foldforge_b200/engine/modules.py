@@ -211,15 +211,22 @@ class _PairOp(MasterWeights, nn.Module):
         reason = _cuda_reason(x, key_mask) or _library_reason()
         if reason:
             return reason
-        if x.dtype != torch.bfloat16:
-            return f"activations are {x.dtype}; the b200 pair kernels take bf16 (master precision)"
+        if x.dtype not in (torch.bfloat16, torch.float32):
+            return f"activations are {x.dtype}; the b200 kernels take bf16 (master) or fp32"
         if x.dim() != 4 or x.shape[1] != x.shape[2]:
             return f"pair tensor shape {tuple(x.shape)} is not [B, N, N, c]"
-        if x.shape[-1] != self.b200_channels:
-            return f"c_z = {x.shape[-1]} (the b200 kernels are built for {self.b200_channels})"
         if key_mask is not None and tuple(key_mask.shape) != tuple(x.shape[:2]):
             return f"key mask {tuple(key_mask.shape)} does not match pair {tuple(x.shape)}"
         return None
+
+    def _weights(self) -> dict[str, Tensor]:
+        return {k: v.detach() for k, v in self.state_dict().items()}
+
+    def _on_generic(self, fn, x: Tensor, *args, **kwargs) -> Tensor:
+        """Run ``fn`` (an fp32 SIMT op of ``csrc/generic.cu``) in fp32 and return ``x``'s dtype:
+        the fp32 precision, and widths the tcgen05 kernels are not built for."""
+        out = fn(x.float(), *args, **kwargs)
+        return out if x.dtype == torch.float32 else out.to(x.dtype)
 
     def _cached_pack(self, pack) -> Tensor:
         """The packed device image of the weights, rebuilt only when a parameter changed
@@ -273,9 +280,11 @@ class TriangleMultiplication(_PairOp):
     def unsupported(self, x: Tensor, key_mask: Tensor | None = None) -> str | None:
         if self.backend == "pytorch":
             return None
-        if self.d_hidden != 128:
-            return f"hidden width {self.d_hidden} (the b200 kernels are built for 128)"
         return self._pair_reason(x, key_mask)
+
+    def _tensor_cores(self, x: Tensor) -> bool:
+        """bf16 at the AF3 widths runs the tcgen05 kernels; anything else the fp32 SIMT path."""
+        return x.dtype == torch.bfloat16 and x.shape[-1] == 128 and self.d_hidden == 128
 
     def forward(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
         return _dispatch(self, x, key_mask)
@@ -296,6 +305,9 @@ class TriangleMultiplication(_PairOp):
     def _forward_b200(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
         from foldforge_b200 import kernels
 
+        if not self._tensor_cores(x):
+            return self._on_generic(kernels.trimul_f32, x, self._key_mask(x, key_mask), self._weights(),
+                                    outgoing=self.outgoing, masked_zero=self._masked_zero())
         packed = self._cached_pack(lambda w: kernels.trimul_prepare(w, x.device))
         return kernels.trimul(x, self._key_mask(x, key_mask), packed, outgoing=self.outgoing,
                               masked_zero=self._masked_zero())
@@ -338,9 +350,12 @@ class TriangleAttention(_PairOp):
     def unsupported(self, x: Tensor, key_mask: Tensor | None = None) -> str | None:
         if self.backend == "pytorch":
             return None
-        if (self.n_head, self.d_head) != (4, 32):
-            return f"{self.n_head} heads x {self.d_head} (the b200 kernels are built for 4 x 32)"
+        if self.d_head > 64:
+            return f"head width {self.d_head} (the b200 kernels take at most 64)"
         return self._pair_reason(x, key_mask)
+
+    def _tensor_cores(self, x: Tensor) -> bool:
+        return x.dtype == torch.bfloat16 and x.shape[-1] == 128 and (self.n_head, self.d_head) == (4, 32)
 
     def forward(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
         return _dispatch(self, x, key_mask)
@@ -373,6 +388,9 @@ class TriangleAttention(_PairOp):
     def _forward_b200(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
         from foldforge_b200 import kernels
 
+        if not self._tensor_cores(x):
+            return self._on_generic(kernels.triattn_f32, x, self._key_mask(x, key_mask), self._weights(),
+                                    starting=self.starting, n_head=self.n_head, masked_zero=self._masked_zero())
         packed = self._cached_pack(lambda w: kernels.triattn_prepare(w, x.device))
         return kernels.triattn(x, self._key_mask(x, key_mask), packed, starting=self.starting,
                                masked_zero=self._masked_zero())
@@ -385,8 +403,8 @@ class TriangleAttentionAF3(TriangleAttention):
 # --------------------------------------------------------------------------- transition
 class Transition(_PairOp):
     """``x + W_sq(silu(W_a LN(x)) * W_b LN(x))`` (``legacy/primitives.py:20-37``,
-    ``legacy/reference/transition.py:28-59``); pair (c = 128) and single (c = 384) widths
-    have b200 kernels."""
+    ``legacy/reference/transition.py:28-59``). On b200: the pair (128, 4) and single (384, 4)
+    widths in bf16 run the tcgen05 kernels, every other width and fp32 the SIMT path."""
 
     def __init__(self, d_hidden: int, n: int = 4) -> None:
         super().__init__()
@@ -399,18 +417,21 @@ class Transition(_PairOp):
     def unsupported(self, x: Tensor, key_mask: Tensor | None = None) -> str | None:
         if self.backend == "pytorch":
             return None
-        if self.n != 4 or self.d not in (128, 384):
-            return f"Transition({self.d}, {self.n}) (b200 kernels: (128, 4) pair, (384, 4) single)"
         reason = _cuda_reason(x, key_mask) or _library_reason()
         if reason:
             return reason
-        if x.dtype != torch.bfloat16:
-            return f"activations are {x.dtype}; the b200 kernels take bf16 (master precision)"
-        if self.d == 128 and (x.dim() != 4 or x.shape[1] != x.shape[2]):
-            return f"pair transition input {tuple(x.shape)} is not [B, N, N, 128]"
-        if self.d == 384 and x.dim() != 3:
-            return f"single transition input {tuple(x.shape)} is not [B, N, 384]"
+        if x.dtype not in (torch.bfloat16, torch.float32):
+            return f"activations are {x.dtype}; the b200 kernels take bf16 (master) or fp32"
+        if x.dim() == 4 and x.shape[1] != x.shape[2] or x.dim() not in (3, 4):
+            return f"transition input {tuple(x.shape)} is neither a pair [B, N, N, c] nor a single [B, N, c]"
+        if key_mask is not None and tuple(key_mask.shape) != tuple(x.shape[:2]):
+            return f"key mask {tuple(key_mask.shape)} does not match {tuple(x.shape)}"
         return None
+
+    def _tensor_cores(self, x: Tensor) -> bool:
+        if x.dtype != torch.bfloat16 or self.n != 4:
+            return False
+        return (self.d == 128 and x.dim() == 4) or (self.d == 384 and x.dim() == 3)
 
     def forward(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
         return _dispatch(self, x, key_mask)
@@ -428,6 +449,9 @@ class Transition(_PairOp):
     def _forward_b200(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
         from foldforge_b200 import kernels
 
+        if not self._tensor_cores(x):
+            return self._on_generic(kernels.transition_f32, x, key_mask, self._weights(),
+                                    masked_zero=self._masked_zero())
         if self.d == 128:
             packed = self._cached_pack(lambda w: kernels.transition_prepare(w, x.device))
             return kernels.transition(x, key_mask, packed, masked_zero=self._masked_zero())
@@ -456,16 +480,19 @@ class AttentionPairBias(_PairOp):
                     extra_pair_bias: Tensor | None = None) -> str | None:
         if self.backend == "pytorch":
             return None
-        if (self.d_single, self.d_pair, self.n_head) != (384, 128, 16):
-            return f"widths ({self.d_single}, {self.d_pair}, {self.n_head} heads) (b200: 384, 128, 16)"
+        if self.d_single % self.n_head or self.d_single // self.n_head > 64:
+            return f"widths ({self.d_single}, {self.n_head} heads): the b200 kernels take head widths up to 64"
         reason = _cuda_reason(s, z, key_mask, extra_pair_bias) or _library_reason()
         if reason:
             return reason
-        if s.dtype != torch.bfloat16 or z.dtype != torch.bfloat16:
-            return "activations must be bf16 (master precision)"
+        if s.dtype not in (torch.bfloat16, torch.float32) or z.dtype != s.dtype:
+            return f"activations s {s.dtype}, z {z.dtype} (the b200 kernels take both bf16 or both fp32)"
         if s.dim() != 3 or z.dim() != 4 or z.shape[:2] != s.shape[:2] or z.shape[1] != z.shape[2]:
             return f"shapes s {tuple(s.shape)}, z {tuple(z.shape)}"
         return None
+
+    def _tensor_cores(self, s: Tensor) -> bool:
+        return s.dtype == torch.bfloat16 and (self.d_single, self.d_pair, self.n_head) == (384, 128, 16)
 
     def forward(self, s: Tensor, z: Tensor, key_mask: Tensor | None = None,
                 extra_pair_bias: Tensor | None = None) -> Tensor:
@@ -499,6 +526,12 @@ class AttentionPairBias(_PairOp):
     def _forward_b200(self, s: Tensor, z: Tensor, key_mask: Tensor | None = None,
                       extra_pair_bias: Tensor | None = None) -> Tensor:
         from foldforge_b200 import kernels
+
+        if not self._tensor_cores(s):
+            out = kernels.attention_pair_bias_f32(s.float(), z.float(), self._key_mask(s, key_mask), self._weights(),
+                                                  n_head=self.n_head, extra_pair_bias=extra_pair_bias,
+                                                  gate_bias=self.gate_bias, masked_zero=self._masked_zero())
+            return out.to(s.dtype)
 
         def pack(w: dict[str, Tensor]) -> Tensor:
             if w.get("to_query.bias") is None:

@@ -252,3 +252,107 @@ def single_transition(s: Tensor, mask: Tensor | None, packed: Tensor, *, masked_
     _lib.call("ffb_single_transition_fwd", _ptr(s), _ptr(m), _ptr(packed), _ptr(out), _ptr(ws),
               ctypes.c_size_t(ws_bytes), b, n, int(masked_zero and m is not None), _stream())
     return out
+
+
+# --------------------------------------------------------------------------- fp32 / any-width path
+# The FP32 SIMT kernels of csrc/generic.cu: fp32 activations (the "fp32" precision), and any
+# widths (e.g. c_z = 64). Weights are the module's fp32 matrices as they are ([out, in]).
+def _weight_ptrs(weights: dict[str, Tensor], keys: tuple[str, ...], device: torch.device):
+    ts = [_f32(weights[k]).to(device) for k in keys]
+    _need_cuda(*ts)
+    table = (ctypes.c_void_p * len(ts))(*[t.data_ptr() for t in ts])  # a host array of device pointers
+    return ctypes.cast(table, ctypes.c_void_p), (ts, table)
+
+
+def _f32_input(x: Tensor, name: str) -> Tensor:
+    if x.dtype != torch.float32:
+        raise _lib.UnsupportedCall(name, 2, f"the fp32 path takes fp32 activations, got {x.dtype}")
+    return x.contiguous()
+
+
+def _workspace(nbytes: int, device: torch.device) -> Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+def trimul_f32(z: Tensor, mask: Tensor, weights: dict[str, Tensor], *, outgoing: bool,
+               masked_zero: bool = True) -> Tensor:
+    """Triangle multiplicative update with residual in fp32: ``z [B, N, N, c]``, any c / hidden."""
+    _need_cuda(z, mask)
+    z = _f32_input(z, "trimul_f32")
+    b, n, c = z.shape[0], z.shape[1], z.shape[-1]
+    h = weights["to_left.weight"].shape[0]
+    keys = ("ln_pair.weight", "ln_pair.bias", "ln_out.weight", "ln_out.bias", "to_left.weight", "to_right.weight",
+            "to_left_gate.weight", "to_right_gate.weight", "to_out.weight", "to_gate.weight")
+    ptrs, keep = _weight_ptrs(weights, keys, z.device)
+    lib = _lib.load()
+    ws = _workspace(lib.ffb_trimul_f32_workspace_bytes(b, n, c, h), z.device)
+    out = torch.empty_like(z)
+    _lib.call("ffb_trimul_fwd_f32", _ptr(z), _ptr(_mask_u8(mask)), ptrs, _ptr(out), _ptr(ws),
+              ctypes.c_size_t(ws.numel()), b, n, c, h, int(outgoing), int(masked_zero), _stream())
+    del keep
+    return out
+
+
+def triattn_f32(z: Tensor, mask: Tensor, weights: dict[str, Tensor], *, starting: bool, n_head: int,
+                masked_zero: bool = True) -> Tensor:
+    """Triangle attention with residual in fp32: ``z [B, N, N, c]``, any heads x width <= 64."""
+    _need_cuda(z, mask)
+    z = _f32_input(z, "triattn_f32")
+    b, n, c = z.shape[0], z.shape[1], z.shape[-1]
+    d = weights["to_query.weight"].shape[0] // n_head
+    keys = ("ln_pair.weight", "ln_pair.bias", "to_bias.weight", "to_query.weight", "to_key.weight",
+            "to_value.weight", "to_gate.weight", "to_out.weight")
+    ptrs, keep = _weight_ptrs(weights, keys, z.device)
+    lib = _lib.load()
+    ws = _workspace(lib.ffb_triattn_f32_workspace_bytes(b, n, c, n_head, d), z.device)
+    out = torch.empty_like(z)
+    _lib.call("ffb_triattn_fwd_f32", _ptr(z), _ptr(_mask_u8(mask)), ptrs, _ptr(out), _ptr(ws),
+              ctypes.c_size_t(ws.numel()), b, n, c, n_head, d, int(starting), int(masked_zero), _stream())
+    del keep
+    return out
+
+
+def transition_f32(x: Tensor, mask: Tensor | None, weights: dict[str, Tensor], *, masked_zero: bool = True) -> Tensor:
+    """Transition with residual in fp32: pair ``[B, N, N, c]`` or single ``[B, N, c]``, any c and factor."""
+    _need_cuda(x, mask)
+    x = _f32_input(x, "transition_f32")
+    pair = x.dim() == 4
+    b, n, c = x.shape[0], x.shape[1], x.shape[-1]
+    factor = weights["expand_a.weight"].shape[0] // c
+    if mask is None:
+        mask, masked_zero = torch.ones(b, n, dtype=torch.bool, device=x.device), False
+    keys = ("ln_in.weight", "ln_in.bias", "expand_a.weight", "expand_b.weight", "squeeze.weight")
+    ptrs, keep = _weight_ptrs(weights, keys, x.device)
+    lib = _lib.load()
+    rows = b * n * (n if pair else 1)
+    ws = _workspace(lib.ffb_transition_f32_workspace_bytes(rows, c, factor), x.device)
+    out = torch.empty_like(x)
+    _lib.call("ffb_transition_fwd_f32", _ptr(x), _ptr(_mask_u8(mask)), ptrs, _ptr(out), _ptr(ws),
+              ctypes.c_size_t(ws.numel()), b, n, c, factor, int(pair), int(masked_zero), _stream())
+    del keep
+    return out
+
+
+def attention_pair_bias_f32(s: Tensor, z: Tensor, mask: Tensor, weights: dict[str, Tensor], *, n_head: int,
+                            extra_pair_bias: Tensor | None = None, gate_bias: float = 0.0,
+                            masked_zero: bool = True) -> Tensor:
+    """Single attention with pair bias and residual in fp32: ``s [B, N, c_s]``, ``z [B, N, N, c_z]``."""
+    _need_cuda(s, z, mask, extra_pair_bias)
+    s, z = _f32_input(s, "apb_f32"), _f32_input(z, "apb_f32")
+    b, n, cs, cz = s.shape[0], s.shape[1], s.shape[-1], z.shape[-1]
+    w = dict(weights)
+    if w.get("to_query.bias") is None:
+        w["to_query.bias"] = torch.zeros(cs, device=s.device)
+    keys = ("ln_single.weight", "ln_single.bias", "to_query.weight", "to_query.bias", "to_key.weight",
+            "to_value.weight", "to_gate.weight", "to_out.weight", "ln_pair.weight", "to_bias.weight")
+    ptrs, keep = _weight_ptrs(w, keys, s.device)
+    extra = None
+    if extra_pair_bias is not None:
+        extra = extra_pair_bias.float().expand(b, n_head, n, n).contiguous()
+    lib = _lib.load()
+    ws = _workspace(lib.ffb_apb_f32_workspace_bytes(b, n, cs, cz, n_head), s.device)
+    out = torch.empty_like(s)
+    _lib.call("ffb_apb_fwd_f32", _ptr(s), _ptr(z), _ptr(_mask_u8(mask)), ptrs, _ptr(extra), ctypes.c_float(gate_bias),
+              _ptr(out), _ptr(ws), ctypes.c_size_t(ws.numel()), b, n, cs, cz, n_head, int(masked_zero), _stream())
+    del keep
+    return out

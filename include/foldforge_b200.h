@@ -241,6 +241,40 @@ int ffb_shard_rows_p2p(const void* src, int mode, int R, int N, const void* dst_
                        int rank, int P, void* stream);
 int ffb_trimul_channel_contract(const void* left, const void* right, void* u, int C, int N, void* stream);
 
+/* ---- fp32 precision, and widths the tcgen05 kernels are not built for (FP32 SIMT cores).
+ * The same ops with fp32 activations end to end (FoldForge's "fp32" precision,
+ * modules/engine/configure.py:35-70) and any widths (e.g. the template stack's c_z = 64): fp32
+ * LayerNorms, FFMA GEMMs with fp32 accumulation, softmax with expf. Weights are the engine's
+ * fp32 matrices in their natural [out, in] layout, passed as a HOST array of device pointers
+ * in the order listed; nothing is packed. Workspaces of the *_f32_workspace_bytes size,
+ * 256-byte aligned; out may not alias the input; mask [B, N] uint8 is required. Each replaces
+ * the same engine op as its bf16 counterpart above (TriangleMultiplication, TriangleAttention,
+ * Transition, AttentionPairBias; src/foldforge/modules/engine/modules.py:133-181).
+ * trimul weights: ln_w, ln_b [c], ln_out_w, ln_out_b [h], to_left, to_right, to_left_gate,
+ *   to_right_gate [h, c], to_out [c, h], to_gate [c, c].
+ * triattn weights: ln_w, ln_b [c], to_bias [H, c], to_query, to_key, to_value, to_gate [H d, c],
+ *   to_out [c, H d]; d <= 64.
+ * transition weights: ln_w, ln_b [c], expand_a, expand_b [n c, c], squeeze [c, n c]; `pair` 1:
+ *   x [B, N, N, c] with the pair mask, 0: x [B, N, c] with the token mask.
+ * apb weights: ln_single_w, ln_single_b [c_s], to_query [c_s, c_s], to_query_b [c_s], to_key,
+ *   to_value, to_gate, to_out [c_s, c_s], ln_pair_w [c_z], to_bias [H, c_z]; extra_bias
+ *   [B, H, N, N] fp32 or NULL; c_s / H <= 64. */
+size_t ffb_trimul_f32_workspace_bytes(int B, int N, int c, int h);
+int ffb_trimul_fwd_f32(const float* z, const uint8_t* mask, const float* const* weights, float* out, void* workspace,
+                       size_t workspace_bytes, int B, int N, int c, int h, int outgoing, int masked, void* stream);
+size_t ffb_triattn_f32_workspace_bytes(int B, int N, int c, int H, int d);
+int ffb_triattn_fwd_f32(const float* z, const uint8_t* mask, const float* const* weights, float* out, void* workspace,
+                        size_t workspace_bytes, int B, int N, int c, int H, int d, int starting, int masked,
+                        void* stream);
+size_t ffb_transition_f32_workspace_bytes(int64_t rows, int c, int n);
+int ffb_transition_fwd_f32(const float* x, const uint8_t* mask, const float* const* weights, float* out,
+                           void* workspace, size_t workspace_bytes, int B, int N, int c, int n, int pair, int masked,
+                           void* stream);
+size_t ffb_apb_f32_workspace_bytes(int B, int N, int cs, int cz, int H);
+int ffb_apb_fwd_f32(const float* s, const float* z, const uint8_t* mask, const float* const* weights,
+                    const float* extra_bias, float gate_bias, float* out, void* workspace, size_t workspace_bytes,
+                    int B, int N, int cs, int cz, int H, int masked, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

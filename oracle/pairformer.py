@@ -221,23 +221,35 @@ def pairformer_block(
     gate_bias: float = 0.0,
     extra_pair_bias: Tensor | None = None,
     dtype: torch.dtype = torch.float32,
+    storage: torch.dtype | None = None,
 ) -> tuple[Tensor, Tensor | None]:
     """One sequential (AF3) Pairformer block: ``legacy/pairformer.py:191-229``.
 
     ``z += TMo; z += TMi; z += TAs; z += TAe; z += Tr(z); s += APB(s, z); s += Tr(s)``.
+
+    ``storage``: the activation dtype between ops. ``None`` keeps ``dtype`` throughout;
+    ``torch.bfloat16`` rounds the pair and the single to bf16 after every op, as the
+    master-precision activation stream stores them (fp32 parameters and arithmetic, bf16
+    activations at the op boundaries, ``modules/engine/configure.py:73-99``).
     """
-    z = triangle_multiplication(z, tokens, _sub(p, "tri_multi_outgoing"), outgoing=True, dtype=dtype)
-    z = triangle_multiplication(z, tokens, _sub(p, "tri_multi_incoming"), outgoing=False, dtype=dtype)
-    z = triangle_attention(z, tokens, _sub(p, "tri_atten_starting"), starting=True, n_head=n_head_pair, dtype=dtype)
-    z = triangle_attention(z, tokens, _sub(p, "tri_atten_ending"), starting=False, n_head=n_head_pair, dtype=dtype)
-    z = transition(z, _sub(p, "transition_pair"), dtype=dtype)
+
+    def keep(x: Tensor) -> Tensor:
+        return x if storage is None else x.to(storage).to(dtype)
+
+    z = keep(triangle_multiplication(z, tokens, _sub(p, "tri_multi_outgoing"), outgoing=True, dtype=dtype))
+    z = keep(triangle_multiplication(z, tokens, _sub(p, "tri_multi_incoming"), outgoing=False, dtype=dtype))
+    z = keep(triangle_attention(z, tokens, _sub(p, "tri_atten_starting"), starting=True, n_head=n_head_pair,
+                                dtype=dtype))
+    z = keep(triangle_attention(z, tokens, _sub(p, "tri_atten_ending"), starting=False, n_head=n_head_pair,
+                                dtype=dtype))
+    z = keep(transition(z, _sub(p, "transition_pair"), dtype=dtype))
     if s is None:
         return z, None
-    s = attention_pair_bias(
+    s = keep(attention_pair_bias(
         s, z, tokens, _sub(p, "single_attention"), n_head=n_head_single, gate_bias=gate_bias,
         extra_pair_bias=extra_pair_bias, dtype=dtype,
-    )
-    s = transition(s, _sub(p, "single_transition"), dtype=dtype)
+    ))
+    s = keep(transition(s, _sub(p, "single_transition"), dtype=dtype))
     return z, s
 
 

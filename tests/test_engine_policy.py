@@ -11,7 +11,7 @@ import pytest
 import torch
 from torch import nn
 
-from foldforge_b200.engine import backends, factories, policy
+from foldforge_b200.engine import backends, factories, modules, policy
 from foldforge_b200.engine.install import install_engine
 from foldforge_b200.engine.modules import AttentionPairBias, BackendUnsupported, LayerNorm, Transition, TriangleMultiplication
 from foldforge_b200.engine.pairformer import pairformer_block
@@ -152,15 +152,30 @@ def test_install_engine_without_cuda_modules_runs_pytorch():
     assert set(report["modules"]) == {"transition", "trimul", "norm"}
 
 
-def test_b200_refuses_widths_it_was_not_built_for(monkeypatch):
+def test_b200_takes_any_width_and_refuses_what_no_kernel_serves(monkeypatch):
+    """Widths the tcgen05 kernels are not built for run the fp32 SIMT path, so b200 takes them;
+    it refuses head widths above 64 (the SIMT attention's bound) and tensors off the GPU."""
+    monkeypatch.setattr(modules, "_cuda_reason", lambda *ts: None)
+    monkeypatch.setattr(modules, "_library_reason", lambda: None)
     module = factories.transition(64, 4, precision="fp32")
     module.set_backend("b200")
-    assert "Transition(64, 4)" in module.unsupported(torch.randn(1, 4, 4, 64))
-    apb = AttentionPairBias(256, 128, 8)
+    assert module.unsupported(torch.randn(1, 4, 4, 64)) is None
+    assert not module._tensor_cores(torch.randn(1, 4, 4, 64))
+    assert module.unsupported(torch.randn(1, 4, 4, 64, dtype=torch.float16)) is not None
+    apb = AttentionPairBias(384, 128, 4)  # head width 96
     apb.set_backend("b200")
-    assert "widths" in apb.unsupported(torch.randn(1, 4, 256), torch.randn(1, 4, 4, 128))
+    assert "head widths up to 64" in apb.unsupported(torch.randn(1, 4, 384), torch.randn(1, 4, 4, 128))
+    tri = TriangleMultiplication(64, 32)
+    tri.set_backend("b200")
+    assert tri.unsupported(torch.randn(1, 4, 4, 64)) is None and not tri._tensor_cores(torch.randn(1, 4, 4, 64))
     with pytest.raises(BackendUnsupported):
         LayerNorm(8).set_backend("cuda")
+
+
+def test_b200_refuses_cpu_tensors():
+    module = factories.transition(64, 4, precision="fp32")
+    module.set_backend("b200")
+    assert module.unsupported(torch.randn(1, 4, 4, 64)) == "tensor is not on a CUDA device"
 
 
 def test_dead_modules_return_their_residual_input():
