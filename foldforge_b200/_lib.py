@@ -92,6 +92,22 @@ SIGNATURES: dict[str, list] = {
     "ffb_apb_f32_workspace_bytes": [c_int, c_int, c_int, c_int, c_int],
     "ffb_apb_fwd_f32": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p,
                         ctypes.c_size_t, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p],
+    # MSA module
+    "ffb_opm_packed_bytes": [],
+    "ffb_opm_workspace_bytes": [c_int, c_int],
+    "ffb_opm_prepare": [c_void_p] * 8,
+    "ffb_opm_fwd": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_size_t, c_int, c_int, c_int, c_float,
+                    c_void_p],
+    "ffb_pwa_packed_bytes": [],
+    "ffb_pwa_workspace_bytes": [c_int, c_int],
+    "ffb_pwa_prepare": [c_void_p] * 9,
+    "ffb_pwa_fwd": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_size_t, c_int, c_int, c_int,
+                    c_void_p],
+    "ffb_transition_gemm_packed_bytes": [c_int, c_int],
+    "ffb_transition_gemm_workspace_bytes": [c_i64, c_int, c_int],
+    "ffb_transition_gemm_prepare": [c_void_p] * 5 + [c_int, c_int, c_void_p, c_void_p],
+    "ffb_transition_gemm_fwd": [c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_size_t, c_i64, c_int, c_int,
+                                c_void_p],
 }
 
 #: entry points that return a size_t instead of a status
@@ -99,7 +115,9 @@ SIZE_RESULT = {"ffb_apb_packed_bytes", "ffb_apb_workspace_bytes", "ffb_single_tr
                "ffb_single_transition_workspace_bytes", "ffb_transition_packed_bytes", "ffb_trimul_packed_bytes",
                "ffb_trimul_workspace_bytes", "ffb_triattn_packed_bytes", "ffb_triattn_workspace_bytes",
                "ffb_apb_single_workspace_bytes", "ffb_trimul_f32_workspace_bytes", "ffb_triattn_f32_workspace_bytes",
-               "ffb_transition_f32_workspace_bytes", "ffb_apb_f32_workspace_bytes"}
+               "ffb_transition_f32_workspace_bytes", "ffb_apb_f32_workspace_bytes", "ffb_opm_packed_bytes",
+               "ffb_opm_workspace_bytes", "ffb_pwa_packed_bytes", "ffb_pwa_workspace_bytes",
+               "ffb_transition_gemm_packed_bytes", "ffb_transition_gemm_workspace_bytes"}
 
 STATUS = {0: "FFB_OK", 1: "FFB_ERR_ARG", 2: "FFB_ERR_UNSUPPORTED", 3: "FFB_ERR_CUDA", 4: "FFB_ERR_DEVICE"}
 
@@ -158,6 +176,7 @@ LAUNCHES = {
     "ffb_shard_transpose_p2p": 1, "ffb_shard_gather_p2p": 1, "ffb_shard_wait_p2p": 1, "ffb_shard_rows_p2p": 1,
     "ffb_trimul_channel_contract": 1,
     "ffb_trimul_fwd_f32": 12, "ffb_triattn_fwd_f32": 8, "ffb_transition_fwd_f32": 5, "ffb_apb_fwd_f32": 9,
+    "ffb_opm_fwd": 6, "ffb_pwa_fwd": 8, "ffb_transition_gemm_fwd": 3,
 }
 launch_count = 0
 

@@ -97,6 +97,13 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int b, int m
   }
   float rowscale = 1.0f;
   if (p.row_mask != nullptr) rowscale = p.row_mask[static_cast<int64_t>(b) * p.M + m] ? 1.0f : 0.0f;
+  if (p.row_scale != nullptr) {
+    rowscale *= p.row_scale[static_cast<int64_t>(b) * p.M + m];
+    if (p.epilogue != kEpiResidual) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc[i] *= rowscale;
+    }
+  }
   const int64_t off = static_cast<int64_t>(b) * p.batch_stride_d + static_cast<int64_t>(m) * p.ldd + n0;
   if (p.epilogue == kEpiResidual) {
     // D = R + acc * rowscale, R and D share the layout and dtype. All of the chunk's residual
@@ -346,7 +353,8 @@ int launch_gemm_nt(const CUtensorMap& map_a, const CUtensorMap& map_b, const Gem
   CUtensorMap map_d;
   memset(&map_d, 0, sizeof(map_d));
   p.tma_store = 0;
-  if (p.epilogue == kEpiStore && !p.d_is_f32 && p.bias == nullptr && (reinterpret_cast<uintptr_t>(p.D) & 15u) == 0 &&
+  if (p.epilogue == kEpiStore && !p.d_is_f32 && p.bias == nullptr && p.row_scale == nullptr &&
+      (reinterpret_cast<uintptr_t>(p.D) & 15u) == 0 &&
       (p.ldd * 2) % 16 == 0 &&
       (p.batch_stride_d * 2) % 16 == 0) {
     const uint64_t dims[3] = {static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.M), static_cast<uint64_t>(p.batch)};

@@ -25,6 +25,7 @@ struct GemmParams {
   const uint8_t* row_mask;
   int* err;
   int tma_store;  // set by launch_gemm_nt: the bf16 store epilogue goes through TMA stores
+  const float* row_scale = nullptr;  // (acc + bias) times row_scale[m] (store and residual epilogues)
 };
 
 size_t gemm_smem_bytes(int bn);

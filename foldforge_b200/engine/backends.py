@@ -43,8 +43,8 @@ BACKENDS = ("miniworld", "cuequivariance", *ENGINE_BACKENDS, *FOREIGN_BACKENDS)
 OP_CLASSES: dict[str, tuple[str, ...]] = {
     "trimul": ("TriangleMultiplication",),
     "triangle_attention": ("TriangleAttention", "TriangleAttentionAF3"),
-    "opm": (),
-    "msa_pwa": (),
+    "opm": ("OuterProductMean",),
+    "msa_pwa": ("MSAPairWeightedAveraging",),
     "single_attention": ("AttentionPairBias",),
     "transition": ("Transition",),
     "layernorm": ("LayerNorm",),

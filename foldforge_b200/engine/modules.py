@@ -422,16 +422,23 @@ class Transition(_PairOp):
             return reason
         if x.dtype not in (torch.bfloat16, torch.float32):
             return f"activations are {x.dtype}; the b200 kernels take bf16 (master) or fp32"
+        if key_mask is None:
+            return None if x.dim() >= 2 else f"transition input {tuple(x.shape)} has no rows"
         if x.dim() == 4 and x.shape[1] != x.shape[2] or x.dim() not in (3, 4):
             return f"transition input {tuple(x.shape)} is neither a pair [B, N, N, c] nor a single [B, N, c]"
-        if key_mask is not None and tuple(key_mask.shape) != tuple(x.shape[:2]):
+        if tuple(key_mask.shape) != tuple(x.shape[:2]):
             return f"key mask {tuple(key_mask.shape)} does not match {tuple(x.shape)}"
         return None
 
     def _tensor_cores(self, x: Tensor) -> bool:
+        """The fused AF3-width kernels: the pair transition (128, 4) and the single one (384, 4)."""
         if x.dtype != torch.bfloat16 or self.n != 4:
             return False
-        return (self.d == 128 and x.dim() == 4) or (self.d == 384 and x.dim() == 3)
+        return (self.d == 128 and x.dim() == 4 and x.shape[1] == x.shape[2]) or (self.d == 384 and x.dim() == 3)
+
+    def _gemm_rows(self, x: Tensor, key_mask: Tensor | None) -> bool:
+        """Unmasked bf16 rows of other widths (the MSA transition): the tensor-core GEMM transition."""
+        return (x.dtype == torch.bfloat16 and key_mask is None and self.d % 8 == 0 and (self.n * self.d) % 16 == 0)
 
     def forward(self, x: Tensor, key_mask: Tensor | None = None) -> Tensor:
         return _dispatch(self, x, key_mask)
@@ -450,6 +457,13 @@ class Transition(_PairOp):
         from foldforge_b200 import kernels
 
         if not self._tensor_cores(x):
+            if self._gemm_rows(x, key_mask):
+                packed = self._cached_pack(lambda w: kernels.transition_gemm_prepare(w, self.d, self.n, x.device))
+                return kernels.transition_gemm(x, packed, self.d, self.n)
+            if key_mask is None:  # unmasked: the rows of any leading shape
+                rows = x.reshape(1, -1, x.shape[-1])
+                return self._on_generic(kernels.transition_f32, rows, None, self._weights(),
+                                        masked_zero=False).reshape(x.shape)
             return self._on_generic(kernels.transition_f32, x, key_mask, self._weights(),
                                     masked_zero=self._masked_zero())
         if self.d == 128:
@@ -542,6 +556,131 @@ class AttentionPairBias(_PairOp):
         mask = self._key_mask(s, key_mask)
         return kernels.attention_pair_bias(s, z, mask, packed, extra_pair_bias=extra_pair_bias,
                                            gate_bias=self.gate_bias, masked_zero=self._masked_zero())
+
+
+# --------------------------------------------------------------------------- MSA module
+class OuterProductMean(_PairOp):
+    """The outer product mean's RAW update (no residual; the MSA-stack block adds it):
+    ``delta[i, j] = (W_o vec(sum_s L[s, i] (x) R[s, j]) + b_o) / d(n_ij)`` with ``L = m W_l LN(msa)``,
+    ``R = m W_r LN(msa)`` and ``n_ij = sum_s m_si m_sj`` (``legacy/primitives.py:40-136``,
+    ``legacy/reference/attention.py:57-74``; engine keys of ``legacy/released.py:227-250``).
+    ``count_offset``: ``d(n) = n + count_offset`` (AF3: 1e-3), ``None``: ``max(n, 1)``.
+    ``normalize_before_proj``: divide before adding ``b_o`` (the bias-after-norm variants) instead of
+    after (AF3). Called as ``opm(msa [B, S, N, c_m], row_mask [B, S, N])``."""
+
+    def __init__(self, d_msa: int, d_pair: int, d_hidden: int = 32, *, normalize_before_proj: bool = True,
+                 projection_bias: bool = False, groups: int = 1, product_norm_eps: float = 0.1,
+                 count_offset: float | None = None) -> None:
+        super().__init__()
+        if groups != 1:
+            raise ValueError("the grouped (Chai-1) outer product mean is not built here")
+        self.d_msa, self.d_pair, self.d_hidden = d_msa, d_pair, d_hidden
+        self.normalize_before_proj, self.projection_bias = normalize_before_proj, projection_bias
+        self.count_offset, self.product_norm_eps = count_offset, product_norm_eps
+        self.ln_msa = LayerNorm(d_msa)
+        self.to_left = nn.Linear(d_msa, d_hidden, bias=projection_bias)
+        self.to_right = nn.Linear(d_msa, d_hidden, bias=projection_bias)
+        self.to_out = nn.Linear(d_hidden * d_hidden, d_pair, bias=True)
+
+    def unsupported(self, msa: Tensor, row_mask: Tensor) -> str | None:
+        if self.backend == "pytorch":
+            return None
+        if (self.d_msa, self.d_pair, self.d_hidden) != (64, 128, 32):
+            return f"widths ({self.d_msa}, {self.d_pair}, {self.d_hidden}) (b200: 64, 128, 32)"
+        if self.projection_bias or self.normalize_before_proj:
+            return "only AF3's form (no projection bias, the output bias before the divide) has b200 kernels"
+        reason = _cuda_reason(msa, row_mask) or _library_reason()
+        if reason:
+            return reason
+        if msa.dtype != torch.bfloat16:
+            return f"activations are {msa.dtype}; the b200 MSA kernels take bf16 (master precision)"
+        if msa.dim() != 4 or tuple(row_mask.shape) != tuple(msa.shape[:3]):
+            return f"msa {tuple(msa.shape)} / row mask {tuple(row_mask.shape)} are not [B, S, N, c] / [B, S, N]"
+        return None
+
+    def forward(self, msa: Tensor, row_mask: Tensor) -> Tensor:
+        return _dispatch(self, msa, row_mask)
+
+    def _forward_pytorch(self, msa: Tensor, row_mask: Tensor) -> Tensor:
+        m = row_mask.float()[..., None]
+        x = _ln(msa.float(), self.ln_msa)
+        left, right = m * _linear(x, self.to_left), m * _linear(x, self.to_right)
+        b, _, n, k = left.shape
+        outer = torch.einsum("bsic,bsje->bijce", left, right).reshape(b, n, n, k * k)
+        count = torch.einsum("bsi,bsj->bij", m[..., 0], m[..., 0])[..., None]
+        divisor = count.clamp_min(1.0) if self.count_offset is None else count + self.count_offset
+        w = self.to_out.weight.float()
+        if self.normalize_before_proj:
+            delta = (outer @ w.t()) / divisor + self.to_out.bias.float()
+        else:
+            delta = (outer @ w.t() + self.to_out.bias.float()) / divisor
+        return delta.to(msa.dtype)
+
+    def _forward_b200(self, msa: Tensor, row_mask: Tensor) -> Tensor:
+        from foldforge_b200 import kernels
+
+        packed = self._cached_pack(lambda w: kernels.opm_prepare(w, msa.device))
+        return kernels.outer_product_mean(msa, row_mask, packed, count_offset=self.count_offset)
+
+
+class MSAPairWeightedAveraging(_PairOp):
+    """MSA pair-weighted averaging with residual: per head, the pair's logits ``W_b LN(z)[i, j]``
+    (minus 1e9 at columns no MSA row has) give softmax weights over j that average the values
+    ``W_v LN(msa)`` of each MSA row; sigmoid-gated by ``W_g LN(msa)``, projected back by ``W_o``
+    (``legacy/attention.py:174-229``; engine keys of ``legacy/released.py:253-281``). Called as
+    ``pwa(msa [B, S, N, c_m], pair [B, N, N, c_z], key_mask [B, N])``."""
+
+    def __init__(self, d_msa: int, d_pair: int, n_head: int = 8, d_hidden: int | None = None,
+                 p_drop: float = 0.0) -> None:
+        super().__init__()
+        self.d_msa, self.d_pair, self.n_head, self.p_drop = d_msa, d_pair, n_head, p_drop
+        self.d_hidden = d_hidden or d_msa // n_head
+        hidden = n_head * self.d_hidden
+        self.ln_msa = LayerNorm(d_msa)
+        self.ln_pair = LayerNorm(d_pair, bias=False)
+        self.to_bias = nn.Linear(d_pair, n_head, bias=False)
+        self.to_value = nn.Linear(d_msa, hidden, bias=False)
+        self.to_gate = nn.Linear(d_msa, hidden, bias=False)
+        self.to_out = nn.Linear(hidden, d_msa, bias=False)
+
+    def unsupported(self, msa: Tensor, pair: Tensor, key_mask: Tensor | None = None) -> str | None:
+        if self.backend == "pytorch":
+            return None
+        if (self.d_msa, self.d_pair, self.n_head, self.d_hidden) != (64, 128, 8, 8):
+            return f"widths ({self.d_msa}, {self.d_pair}, {self.n_head} x {self.d_hidden}) (b200: 64, 128, 8 x 8)"
+        reason = _cuda_reason(msa, pair, key_mask) or _library_reason()
+        if reason:
+            return reason
+        if msa.dtype != torch.bfloat16 or pair.dtype != torch.bfloat16:
+            return "activations must be bf16 (master precision)"
+        if msa.dim() != 4 or pair.dim() != 4 or pair.shape[:2] != (msa.shape[0], msa.shape[2]):
+            return f"shapes msa {tuple(msa.shape)}, pair {tuple(pair.shape)}"
+        return None
+
+    def forward(self, msa: Tensor, pair: Tensor, key_mask: Tensor | None = None) -> Tensor:
+        return _dispatch(self, msa, pair, key_mask)
+
+    @honours_dead
+    def _forward_pytorch(self, msa: Tensor, pair: Tensor, key_mask: Tensor | None = None) -> Tensor:
+        x = _ln(msa.float(), self.ln_msa)
+        logits = _linear(_ln(pair.float(), self.ln_pair), self.to_bias).permute(0, 3, 1, 2)  # [B, H, i, j]
+        if key_mask is not None:
+            logits = logits + 1e9 * (key_mask.float()[:, None, None, :] - 1.0)
+        weights = torch.softmax(logits, dim=-1)
+        b, s, n, _ = x.shape
+        v = _linear(x, self.to_value).reshape(b, s, n, self.n_head, self.d_hidden)
+        avg = torch.einsum("bhij,bsjhc->bsihc", weights, v).reshape(b, s, n, -1)
+        delta = _linear(torch.sigmoid(_linear(x, self.to_gate)) * avg, self.to_out)
+        return (msa.float() + delta).to(msa.dtype)
+
+    @honours_dead
+    def _forward_b200(self, msa: Tensor, pair: Tensor, key_mask: Tensor | None = None) -> Tensor:
+        from foldforge_b200 import kernels
+
+        packed = self._cached_pack(lambda w: kernels.pwa_prepare(w, msa.device))
+        if key_mask is None:
+            key_mask = torch.ones(pair.shape[:2], dtype=torch.bool, device=pair.device)
+        return kernels.pair_weighted_averaging(msa, pair, key_mask, packed)
 
 
 # --------------------------------------------------------------------------- the block

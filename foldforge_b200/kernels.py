@@ -356,3 +356,89 @@ def attention_pair_bias_f32(s: Tensor, z: Tensor, mask: Tensor, weights: dict[st
               _ptr(out), _ptr(ws), ctypes.c_size_t(ws.numel()), b, n, cs, cz, n_head, int(masked_zero), _stream())
     del keep
     return out
+
+
+# --------------------------------------------------------------------------- MSA module (csrc/msa.cu)
+def opm_prepare(weights: dict[str, Tensor], device: torch.device) -> Tensor:
+    """Pack an ``OuterProductMean`` (AF3 form: c_m 64, 32 channels a side, c_z 128)'s fp32 weights."""
+    lib = _lib.load()
+    packed = torch.empty(int(lib.ffb_opm_packed_bytes()), dtype=torch.uint8, device=device)
+    keys = ("ln_msa.weight", "ln_msa.bias", "to_left.weight", "to_right.weight", "to_out.weight", "to_out.bias")
+    ts = [_f32(weights[k]).to(device) for k in keys]
+    _need_cuda(*ts)
+    _lib.call("ffb_opm_prepare", *[_ptr(t) for t in ts], _ptr(packed), _stream())
+    packed._keepalive = ts
+    return packed
+
+
+def outer_product_mean(msa: Tensor, row_mask: Tensor, packed: Tensor, *, count_offset: float | None) -> Tensor:
+    """The outer product mean's raw update ``[B, N, N, 128]`` bf16 from ``msa [B, S, N, 64]`` bf16 and
+    the MSA row mask ``[B, S, N]``; divisor ``n + count_offset`` (``None``: ``max(n, 1)``)."""
+    _need_cuda(msa, row_mask, packed)
+    if msa.dtype != torch.bfloat16 or msa.dim() != 4 or msa.shape[-1] != 64:
+        raise _lib.UnsupportedCall("outer_product_mean", 2, f"needs bf16 [B, S, N, 64], got {msa.dtype} {tuple(msa.shape)}")
+    msa = msa.contiguous()
+    b, s, n = msa.shape[:3]
+    lib = _lib.load()
+    ws = _workspace(lib.ffb_opm_workspace_bytes(s, n), msa.device)
+    delta = torch.empty((b, n, n, 128), dtype=torch.bfloat16, device=msa.device)
+    offset = -1.0 if count_offset is None else float(count_offset)
+    _lib.call("ffb_opm_fwd", _ptr(msa), _ptr(_mask_u8(row_mask)), _ptr(packed), _ptr(delta), _ptr(ws),
+              ctypes.c_size_t(ws.numel()), b, s, n, ctypes.c_float(offset), _stream())
+    return delta
+
+
+def pwa_prepare(weights: dict[str, Tensor], device: torch.device) -> Tensor:
+    """Pack an ``MSAPairWeightedAveraging`` (c_m 64, c_z 128, 8 heads x 8)'s fp32 weights."""
+    lib = _lib.load()
+    packed = torch.empty(int(lib.ffb_pwa_packed_bytes()), dtype=torch.uint8, device=device)
+    keys = ("ln_msa.weight", "ln_msa.bias", "ln_pair.weight", "to_bias.weight", "to_value.weight", "to_gate.weight",
+            "to_out.weight")
+    ts = [_f32(weights[k]).to(device) for k in keys]
+    _need_cuda(*ts)
+    _lib.call("ffb_pwa_prepare", *[_ptr(t) for t in ts], _ptr(packed), _stream())
+    packed._keepalive = ts
+    return packed
+
+
+def pair_weighted_averaging(msa: Tensor, pair: Tensor, key_mask: Tensor, packed: Tensor) -> Tensor:
+    """``msa + PWA(msa, pair)``: ``msa [B, S, N, 64]``, ``pair [B, N, N, 128]`` bf16, ``key_mask [B, N]``
+    (a column is a key when some MSA row has it)."""
+    _need_cuda(msa, pair, key_mask, packed)
+    if msa.dtype != torch.bfloat16 or pair.dtype != torch.bfloat16 or msa.shape[-1] != 64 or pair.shape[-1] != 128:
+        raise _lib.UnsupportedCall("pair_weighted_averaging", 2, "needs bf16 msa [B, S, N, 64] and pair [B, N, N, 128]")
+    msa, pair = msa.contiguous(), pair.contiguous()
+    b, s, n = msa.shape[:3]
+    lib = _lib.load()
+    ws = _workspace(lib.ffb_pwa_workspace_bytes(s, n), msa.device)
+    out = torch.empty_like(msa)
+    _lib.call("ffb_pwa_fwd", _ptr(msa), _ptr(pair), _ptr(_mask_u8(key_mask)), _ptr(packed), _ptr(out), _ptr(ws),
+              ctypes.c_size_t(ws.numel()), b, s, n, _stream())
+    return out
+
+
+def transition_gemm_prepare(weights: dict[str, Tensor], c: int, n: int, device: torch.device) -> Tensor:
+    """Pack a ``Transition(c, n)`` for the tensor-core transition of any width (c a multiple of 8)."""
+    lib = _lib.load()
+    packed = torch.empty(int(lib.ffb_transition_gemm_packed_bytes(c, n)), dtype=torch.uint8, device=device)
+    keys = ("ln_in.weight", "ln_in.bias", "expand_a.weight", "expand_b.weight", "squeeze.weight")
+    ts = [_f32(weights[k]).to(device) for k in keys]
+    _need_cuda(*ts)
+    _lib.call("ffb_transition_gemm_prepare", *[_ptr(t) for t in ts], c, n, _ptr(packed), _stream())
+    packed._keepalive = ts
+    return packed
+
+
+def transition_gemm(x: Tensor, packed: Tensor, c: int, n: int) -> Tensor:
+    """Unmasked transition with residual over the rows of ``x [..., c]`` bf16 on the tensor cores."""
+    _need_cuda(x, packed)
+    if x.dtype != torch.bfloat16 or x.shape[-1] != c:
+        raise _lib.UnsupportedCall("transition_gemm", 2, f"needs bf16 [..., {c}], got {x.dtype} {tuple(x.shape)}")
+    x = x.contiguous()
+    rows = x.numel() // c
+    lib = _lib.load()
+    ws = _workspace(lib.ffb_transition_gemm_workspace_bytes(rows, c, n), x.device)
+    out = torch.empty_like(x)
+    _lib.call("ffb_transition_gemm_fwd", _ptr(x), _ptr(packed), _ptr(out), _ptr(ws), ctypes.c_size_t(ws.numel()),
+              ctypes.c_int64(rows), c, n, _stream())
+    return out

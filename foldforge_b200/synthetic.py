@@ -149,3 +149,85 @@ def inputs(
     if masked_suffix:
         tokens[n - masked_suffix :] = 0
     return z, s, tokens
+
+
+#: the Pairformer block's pair-track children under their names in the MSA-stack block
+#: (``legacy/released.py:722-749``)
+EVOFORMER_PAIR_NAMES = {
+    "tri_multi_outgoing": "triangle_multiplication_outgoing",
+    "tri_multi_incoming": "triangle_multiplication_incoming",
+    "tri_atten_starting": "pair_attention1",
+    "tri_atten_ending": "pair_attention2",
+    "transition_pair": "pair_transition",
+}
+
+
+def evoformer_schema(c_m: int = 64, shape: BlockShape = BlockShape(), opm_hidden: int = 32, pwa_heads: int = 8,
+                     n_msa: int = 4) -> list[tuple[str, tuple[int, ...]]]:
+    """``[(engine key, shape)]`` of one AF3 MSA-stack block (``evoformer_block_from_released``):
+    outer product mean, pair-weighted averaging, MSA transition, then the pair track."""
+    c, k = shape.c_z, opm_hidden
+    out: list[tuple[str, tuple[int, ...]]] = [
+        ("outer_product_mean.ln_msa.weight", (c_m,)),
+        ("outer_product_mean.ln_msa.bias", (c_m,)),
+        ("outer_product_mean.to_left.weight", (k, c_m)),
+        ("outer_product_mean.to_right.weight", (k, c_m)),
+        ("outer_product_mean.to_out.weight", (c, k * k)),
+        ("outer_product_mean.to_out.bias", (c,)),
+        ("msa_attention1.ln_msa.weight", (c_m,)),
+        ("msa_attention1.ln_msa.bias", (c_m,)),
+        ("msa_attention1.ln_pair.weight", (c,)),
+        ("msa_attention1.to_bias.weight", (pwa_heads, c)),
+        ("msa_attention1.to_value.weight", (c_m, c_m)),
+        ("msa_attention1.to_gate.weight", (c_m, c_m)),
+        ("msa_attention1.to_out.weight", (c_m, c_m)),
+        ("msa_transition.ln_in.weight", (c_m,)),
+        ("msa_transition.ln_in.bias", (c_m,)),
+        ("msa_transition.expand_a.weight", (n_msa * c_m, c_m)),
+        ("msa_transition.expand_b.weight", (n_msa * c_m, c_m)),
+        ("msa_transition.squeeze.weight", (c_m, n_msa * c_m)),
+    ]
+    for key, dims in block_schema(shape, single=False):
+        head, rest = key.split(".", 1)
+        out.append((f"{EVOFORMER_PAIR_NAMES[head]}.{rest}", dims))
+    return out
+
+
+def evoformer_state(generator: torch.Generator, c_m: int = 64, shape: BlockShape = BlockShape(),
+                    scheme: str = "baseline") -> dict[str, Tensor]:
+    """One MSA-stack block's engine-key state dict (fp32), drawn in schema order from ``generator``
+    with the same schemes as :func:`block_state`."""
+    if scheme not in ("baseline", "randomise"):
+        raise ValueError(f"unknown weight scheme {scheme!r}")
+    state: dict[str, Tensor] = {}
+    for key, dims in evoformer_schema(c_m, shape):
+        noise = torch.randn(dims, generator=generator, dtype=torch.float32)
+        if scheme == "baseline":
+            if _is_norm(key):
+                value = torch.ones(dims) if key.endswith("weight") else torch.zeros(dims)
+            else:
+                value = 0.02 * noise
+        elif len(dims) > 1:
+            value = 0.08 * noise
+        elif _is_norm(key) and key.endswith("weight"):
+            value = 1.0 + 0.1 * noise
+        else:
+            value = 0.05 * noise
+        state[key] = value
+    return state
+
+
+def msa_inputs(n_seq: int, n: int, seed: int = 0, c_m: int = 64, c_z: int = 128, masked_suffix: int = 0,
+               row_dropout: float = 0.2) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+    """``(msa [S, N, c_m], z [N, N, c_z], msa_mask [S, N], tokens [N])`` from a generator seeded
+    ``seed``: MSA then pair ~N(0, 1), each MSA position kept with probability ``1 - row_dropout``
+    (the first row, the query sequence, always), padded tokens masked in every row."""
+    g = torch.Generator().manual_seed(seed)
+    msa = torch.randn(n_seq, n, c_m, generator=g)
+    z = torch.randn(n, n, c_z, generator=g)
+    tokens = torch.ones(n)
+    if masked_suffix:
+        tokens[n - masked_suffix:] = 0
+    msa_mask = (torch.rand(n_seq, n, generator=g) > row_dropout).float() * tokens
+    msa_mask[0] = tokens
+    return msa, z, msa_mask, tokens

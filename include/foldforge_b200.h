@@ -275,6 +275,46 @@ int ffb_apb_fwd_f32(const float* s, const float* z, const uint8_t* mask, const f
                     const float* extra_bias, float gate_bias, float* out, void* workspace, size_t workspace_bytes,
                     int B, int N, int cs, int cz, int H, int masked, void* stream);
 
+/* ---- MSA module: AF3's MSA-stack block pieces (c_m = 64, c_z = 128; bf16 activations, fp32
+ * accumulation on the tensor cores). Each replaces the engine class FoldForge's
+ * graph.EvoformerBlock builds (src/foldforge/modules/engine/graph.py:237-309):
+ * ffb_opm_* the engine OuterProductMean (modules/engine/modules.py:184-210; AF3 form:
+ * legacy/reference/attention.py:57-74), ffb_pwa_* the engine MSAPairWeightedAveraging
+ * (modules.py:213-227; legacy/attention.py:174-229), ffb_transition_gemm_* the engine
+ * Transition at widths the fused pair kernel does not take (the MSA transition).
+ * ffb_opm_prepare: fp32 ln_w, ln_b [64], to_left, to_right [32, 64], to_out_w [128, 1024]
+ * (column c 32 + e), to_out_b [128] -> packed (ffb_opm_packed_bytes()).
+ * ffb_opm_fwd: msa [B, S, N, 64] bf16, row_mask [B, S, N] uint8 -> delta [B, N, N, 128] bf16, the
+ * RAW update (sum_{c,e} sum_s L[s,i,c] R[s,j,e] W[f, c 32 + e] + b[f]) / d(n_ij), n_ij = sum_s
+ * m_si m_sj, d(n) = n + count_offset (AF3: 1e-3), or max(n, 1) when count_offset < 0. Workspace
+ * ffb_opm_workspace_bytes(S, N) (per batch; batches run in turn).
+ * ffb_pwa_prepare: fp32 ln_msa_w, ln_msa_b [64], ln_pair_w [128], to_bias [8, 128], to_value,
+ * to_gate, to_out [64, 64] -> packed (ffb_pwa_packed_bytes()).
+ * ffb_pwa_fwd: out = msa + W_o (sigmoid(W_g LN(m)) * o), o[s,i,h] = sum_j softmax_j(W_b LN(z)[i,j]
+ * - 1e9 (1 - key_mask[j])) (W_v LN(m))[s,j,h]; msa, out [B, S, N, 64], pair [B, N, N, 128] bf16,
+ * key_mask [B, N] uint8 (a column is a key when some MSA row has it); out may not alias msa.
+ * ffb_transition_gemm_*: x + W_sq(silu(W_a LN(x)) * W_b LN(x)) over `rows` rows of c channels
+ * (c a multiple of 8, n c of 16), unmasked; fp32 weights ln_w, ln_b [c], expand_a, expand_b
+ * [n c, c], squeeze [c, n c]; packed 256-byte aligned. */
+size_t ffb_opm_packed_bytes(void);
+size_t ffb_opm_workspace_bytes(int S, int N);
+int ffb_opm_prepare(const float* ln_w, const float* ln_b, const float* to_left, const float* to_right,
+                    const float* to_out_w, const float* to_out_b, void* packed, void* stream);
+int ffb_opm_fwd(const void* msa, const uint8_t* row_mask, const void* packed, void* delta, void* workspace,
+                size_t workspace_bytes, int B, int S, int N, float count_offset, void* stream);
+size_t ffb_pwa_packed_bytes(void);
+size_t ffb_pwa_workspace_bytes(int S, int N);
+int ffb_pwa_prepare(const float* ln_msa_w, const float* ln_msa_b, const float* ln_pair_w, const float* to_bias,
+                    const float* to_value, const float* to_gate, const float* to_out, void* packed, void* stream);
+int ffb_pwa_fwd(const void* msa, const void* pair, const uint8_t* key_mask, const void* packed, void* out,
+                void* workspace, size_t workspace_bytes, int B, int S, int N, void* stream);
+size_t ffb_transition_gemm_packed_bytes(int c, int n);
+size_t ffb_transition_gemm_workspace_bytes(int64_t rows, int c, int n);
+int ffb_transition_gemm_prepare(const float* ln_w, const float* ln_b, const float* expand_a, const float* expand_b,
+                                const float* squeeze, int c, int n, void* packed, void* stream);
+int ffb_transition_gemm_fwd(const void* x, const void* packed, void* out, void* workspace, size_t workspace_bytes,
+                            int64_t rows, int c, int n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

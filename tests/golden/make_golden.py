@@ -31,7 +31,14 @@ import torch
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parents[1]))
 
-from foldforge_b200.synthetic import BlockShape, block_state, inputs  # noqa: E402
+from foldforge_b200.synthetic import (  # noqa: E402
+    EVOFORMER_PAIR_NAMES,
+    BlockShape,
+    block_state,
+    evoformer_state,
+    inputs,
+    msa_inputs,
+)
 
 
 def _stub_engine() -> None:
@@ -176,6 +183,76 @@ def run_case(name: str, *, shape: BlockShape, n: int, masked: list[int], scheme:
     print(f"{name}: N={n} masked={masked} -> {HERE / (name + '.npz')}")
 
 
+def released_evoformer_from_engine(state: dict[str, torch.Tensor], g: torch.Generator) -> dict[str, torch.Tensor]:
+    """Engine keys of an MSA-stack block -> the released ``EvoformerBlock`` keys (the inverse of
+    ``evoformer_block_from_released``): the pair track through :func:`released_from_engine`, then
+    the outer product mean, the pair-weighted averaging and the MSA transition."""
+    back_names = {v: k for k, v in EVOFORMER_PAIR_NAMES.items()}
+    pair_part = {}
+    for key, value in state.items():
+        head, rest = key.split(".", 1)
+        if head in back_names:
+            pair_part[f"{back_names[head]}.{rest}"] = value
+    out = released_from_engine(pair_part, g)
+    o = "outer_product_mean"
+    out[f"{o}.layer_norm_input.weight"] = state[f"{o}.ln_msa.weight"]
+    out[f"{o}.layer_norm_input.bias"] = state[f"{o}.ln_msa.bias"]
+    out[f"{o}.left_projection.weight"] = state[f"{o}.to_left.weight"]
+    out[f"{o}.right_projection.weight"] = state[f"{o}.to_right.weight"]
+    w = state[f"{o}.to_out.weight"]  # [c_z, K K] = output_w.reshape(K K, c_z).T
+    k = int(round(w.shape[1] ** 0.5))
+    out[f"{o}.output_w"] = w.t().reshape(k, k, w.shape[0]).contiguous()
+    out[f"{o}.output_b"] = state[f"{o}.to_out.bias"]
+    a = "msa_attention1"
+    out[f"{a}.act_norm.weight"] = state[f"{a}.ln_msa.weight"]
+    out[f"{a}.act_norm.bias"] = state[f"{a}.ln_msa.bias"]
+    out[f"{a}.pair_norm.weight"] = state[f"{a}.ln_pair.weight"]
+    # discarded by the converter (softmax-invariant): a NON-zero value here checks that
+    out[f"{a}.pair_norm.bias"] = 0.05 * torch.randn(state[f"{a}.ln_pair.weight"].shape, generator=g)
+    out[f"{a}.pair_logits.weight"] = state[f"{a}.to_bias.weight"]
+    out[f"{a}.v_projection.weight"] = state[f"{a}.to_value.weight"]
+    out[f"{a}.gating_query.weight"] = state[f"{a}.to_gate.weight"]
+    out[f"{a}.output_projection.weight"] = state[f"{a}.to_out.weight"]
+    t = "msa_transition"
+    out[f"{t}.input_layer_norm.weight"] = state[f"{t}.ln_in.weight"]
+    out[f"{t}.input_layer_norm.bias"] = state[f"{t}.ln_in.bias"]
+    out[f"{t}.transition1.weight"] = torch.cat([state[f"{t}.expand_a.weight"], state[f"{t}.expand_b.weight"]], 0)
+    out[f"{t}.transition2.weight"] = state[f"{t}.squeeze.weight"]
+    return out
+
+
+def run_evoformer_case(name: str, *, n_seq: int, n: int, masked: int, scheme: str, wseed: int, iseed: int) -> None:
+    """The reference's released-layout ``EvoformerBlock`` with AF3's spec on seeded engine-key
+    weights (converter round trip checked bitwise) and seeded MSA / pair inputs."""
+    from foldforge.models.checkpoints.legacy.pairformer import EvoformerBlock
+    from foldforge.models.checkpoints.legacy.released import evoformer_block_from_released
+    from foldforge.modules.dense.spec import ALPHAFOLD3
+
+    state = evoformer_state(torch.Generator().manual_seed(wseed), scheme=scheme)
+    legacy = EvoformerBlock(c_msa=64, c_pair=128, n_heads_pair=4, spec=ALPHAFOLD3).eval()
+    legacy.load_state_dict(released_evoformer_from_engine(state, torch.Generator().manual_seed(wseed + 1000)),
+                           strict=True)
+    back = evoformer_block_from_released(legacy.state_dict())
+    assert set(back) == set(state), sorted(set(back) ^ set(state))
+    for k, v in state.items():
+        assert torch.equal(back[k], v), k
+    msa, z, msa_mask, tokens = msa_inputs(n_seq, n, iseed, masked_suffix=masked)
+    pair_mask = tokens[:, None] * tokens[None, :]
+    with torch.no_grad():
+        opm = legacy.outer_product_mean(msa, msa_mask)
+        pwa = legacy.msa_attention1.residual(msa, msa_mask, z)
+        out_msa, out_pair = legacy(msa.clone(), z.clone(), msa_mask, pair_mask)
+    record = {
+        "n": np.array(n), "n_seq": np.array(n_seq), "masked": np.array(masked), "scheme": np.array(scheme),
+        "wseed": np.array(wseed), "iseed": np.array(iseed), "weights_sha256": np.array(_digest(state)),
+        "inputs_sha256": np.array(_digest({"msa": msa, "z": z, "msa_mask": msa_mask})),
+        "op.outer_product_mean": opm.numpy(), "op.msa_attention1": pwa.numpy(),
+        "out_msa": out_msa.numpy(), "out_pair": out_pair.numpy(),
+    }
+    np.savez_compressed(HERE / f"{name}.npz", **record)
+    print(f"{name}: S={n_seq} N={n} masked={masked} -> {HERE / (name + '.npz')}")
+
+
 SMALL = BlockShape(c_z=32, c_s=64, hidden_mul=32, n_head_pair=4, d_tri=8, n_head_single=4, n_pair=4, n_single=4)
 AF3 = BlockShape()
 
@@ -200,6 +277,10 @@ def main() -> None:
     run_case("small_n5_allmasked", shape=SMALL, n=5, masked=[0, 1, 2, 3, 4], scheme="randomise", wseed=4, iseed=5)
     # a single token
     run_case("small_n1", shape=SMALL, n=1, masked=[], scheme="randomise", wseed=6, iseed=7)
+    # the MSA-stack block (AF3): the reference test's shape (6 MSA rows, 20 tokens, 3 padded)
+    # and benchmark configuration 4's weight scheme at a small size
+    run_evoformer_case("evo_s6_n20_masked3", n_seq=6, n=20, masked=3, scheme="randomise", wseed=8, iseed=9)
+    run_evoformer_case("evo_s33_n40_baseline", n_seq=33, n=40, masked=2, scheme="baseline", wseed=10, iseed=11)
 
 
 if __name__ == "__main__":

@@ -43,7 +43,8 @@ def test_serves_is_derived_from_the_classes():
     assert set(table) == set(backends.OPS)
     for op in ("trimul", "triangle_attention", "single_attention", "transition", "layernorm"):
         assert table[op] == ("miniworld", "pytorch", "b200")
-    assert table["opm"] == ()
+    assert table["opm"] == ("miniworld", "pytorch", "b200")
+    assert table["dit_blocks"] == ()
 
 
 def test_choose_backend(monkeypatch):
