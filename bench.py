@@ -65,6 +65,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-ladder", action="store_true", help="skip the N=2048 length-ladder measurement")
+    ap.add_argument("--no-msa", action="store_true", help="skip the MSA-module measurement (configuration 4)")
     ap.add_argument("--kernels-once", action="store_true",
                     help="launch every pair-stack kernel once at --n (a driver for ncu captures; no timing)")
     return ap.parse_args()
@@ -370,6 +371,9 @@ def run_b200(args, rank: int, world: int, local: int, dist) -> None:
             del graphed, trunk
             torch.cuda.empty_cache()
             line["ladder"] = ladder_single_gpu(dev)
+        if world == 1 and not args.no_msa:
+            torch.cuda.empty_cache()
+            line["msa_module"] = msa_module_single_gpu(dev)
         print(json.dumps(line), flush=True)
 
 
@@ -412,6 +416,73 @@ def ladder_single_gpu(dev: torch.device) -> dict:
     return {"n": n, "n_gpus": 1, "ms_per_trunk": round(ms, 1), "ms_per_block": round(ms / N_BLOCKS, 3),
             "masked_suffix": masked, "steps": 2, "warmup": 1, "parallelism": "single GPU (CUDA-graph replay)",
             "clocks": clocks}
+
+
+def msa_inputs_config4(dev: torch.device, n_seq: int = 1024, n: int = 512, seed: int = 0):
+    """Benchmark configuration 4's MSA features: residue ids uniform in 0..31 (one-hot), has_deletion
+    Bernoulli(0.1), deletion_value uniform [0, 1], embedded to c_m = 64 by a N(0, 0.02) linear map;
+    the pair ~N(0, 1); every MSA position and token real."""
+    g = torch.Generator().manual_seed(seed)
+    ids = torch.randint(0, 32, (n_seq, n), generator=g)
+    feats = torch.cat([torch.nn.functional.one_hot(ids, 32).float(),
+                       (torch.rand(n_seq, n, 1, generator=g) < 0.1).float(),
+                       torch.rand(n_seq, n, 1, generator=g)], dim=-1)  # [S, N, 34]
+    w = 0.02 * torch.randn(64, 34, generator=g)
+    msa = (feats @ w.t()).bfloat16()
+    z = torch.randn(n, n, 128, generator=g).bfloat16()
+    return msa[None].to(dev), z[None].to(dev), torch.ones(1, n_seq, n, device=dev), torch.ones(1, n, n, device=dev)
+
+
+def msa_module_single_gpu(dev: torch.device, n_blocks: int = 4) -> dict:
+    """the MSA module's 4 AF3 MSA-stack blocks at 1024 MSA rows x N = 512
+    on one GPU (b200 backend, CUDA-graph replay, L2 flushed), 1 warm-up and 3 timed passes."""
+    from foldforge_b200.engine import backends, policy
+    from foldforge_b200.engine.capture import GraphedCall
+    from foldforge_b200.engine.evoformer import EvoformerBlock
+    from foldforge_b200.synthetic import evoformer_state
+
+    g = torch.Generator().manual_seed(0)
+    blocks = torch.nn.ModuleList()
+    for _ in range(n_blocks):
+        blk = EvoformerBlock(masked_update="zero")
+        blk.load_state_dict(evoformer_state(g, scheme="baseline"), strict=True)
+        blocks.append(blk)
+    blocks = blocks.to(dev).eval()
+    plan = backends.BackendPlan.make("b200", unsupported="error").resolve(dev)
+    policy.apply_plan(blocks, plan, dev)
+    msa, z, msa_mask, pair_mask = msa_inputs_config4(dev)
+
+    def module(m, zz):
+        for blk in blocks:
+            m, zz = blk.batched(m, zz, msa_mask, pair_mask)
+        return m, zz
+
+    graphed = GraphedCall(module, [msa, z], warmup=1)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    graphed.replay()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(3):
+        flush.fill_(1.0)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        graphed.replay()
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    del graphed, blocks
+    torch.cuda.empty_cache()
+    ms = sum(ts) / len(ts)
+    # outer product mean contraction + projection, averaging, projections; the pair track
+    n, s = 512, 1024
+    opm = 2.0 * (n * 32) ** 2 * s + 2.0 * n * n * 1024 * 128
+    pwa = 2.0 * 8 * n * n * s * 8 + 2.0 * s * n * 64 * (128 + 64)
+    tr = 2.0 * s * n * 64 * 256 * 3
+    pair = 1536.0 * n**3 + 1_121_792.0 * n**2 - 2.0 * n * n * 128 * 16  # the Pairformer pair track
+    flops = n_blocks * (opm + pwa + tr + pair)
+    return {"config": "BASELINE configuration 4: 4 MSA-stack blocks, 1024 MSA rows x N=512, c_m 64, c_z 128, bf16",
+            "ms_per_module": round(ms, 2), "ms_per_block": round(ms / n_blocks, 3), "steps": 3, "warmup": 1,
+            "tflops_approx": round(flops / (ms * 1e-3) / 1e12, 1), "parallelism": "single GPU (CUDA-graph replay)"}
 
 
 def run_sharded(args, rank: int, world: int, local: int, dist) -> None:
