@@ -286,6 +286,10 @@ __global__ void __launch_bounds__(192, 1)
       const int m = tm * kBM + row;
       if (p.tma_store) {
         for (int c = 0; c < BN; c += 64, ++chunk) {
+          // nothing of this chunk (or the later ones) lies inside the output: stop, so that
+          // every staged chunk is a committed store and the two-buffer wait below pairs each
+          // buffer with the store that last read it
+          if (tn * BN + c >= p.N) break;
           uint8_t* stage = s.out[chunk & 1];
           // the store issued two chunks ago has finished reading this staging buffer
           if (issuer) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
@@ -310,7 +314,7 @@ __global__ void __launch_bounds__(192, 1)
           fence_async_smem();
           named_barrier(1, 128);
           // rows past M and columns past N are clipped by the tensor map
-          if (issuer && tn * BN + c < p.N) {
+          if (issuer) {
             tma_store_3d(&map_d, stage, tn * BN + c, tm * kBM, b);
             tma_store_commit();
           }

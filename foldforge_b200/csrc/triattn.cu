@@ -393,7 +393,7 @@ struct AttnSmem {
   uint64_t kv_full[kKVStages], kv_empty[kKVStages];
   uint64_t s_full[kSBufs];            // both groups' S of a step
   uint64_t p_full[kGroups][kSBufs];
-  uint64_t pv_done;                   // both groups' P V of a step
+  uint64_t pv_done[kSBufs];           // both groups' P V of step i, on barrier i % kSBufs
   uint64_t o_full[kGroups], o_free[kGroups];
   uint64_t mma_done;
   uint32_t tmem_base;
@@ -452,7 +452,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
     }
     mbar_init(&s.mma_done, 1);
-    mbar_init(&s.pv_done, 1);
+    for (int i = 0; i < kSBufs; ++i) mbar_init(&s.pv_done[i], 1);
     fence_mbar_init();
   }
   // key-mask bits, per batch padded to whole 64-key blocks (zero beyond N)
@@ -567,7 +567,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           if (j == nkb - 1) mma_commit(&s.o_full[g]);
         }
         if (!ok) break;
-        mma_commit(&s.pv_done);  // both groups' P V
+        // both groups' P V of step i. One barrier per S/P buffer: when the softmax of step i + 1
+        // waits for it, S(i + 1) has landed, so every P V up to step i - 2 has too, and the
+        // barrier's previous phase (step i - 3) is complete: the parity wait is exact
+        mma_commit(&s.pv_done[buf]);
         mma_commit(&s.kv_empty[st]);
       }
       // every issued MMA completes before TMEM is released
@@ -674,7 +677,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             // P V has landed
             const float m_new = need ? bm : m;
             const float alpha = ex2(m - m_new);
-            const bool w3 = mbar_wait(&s.pv_done, (i - 1) & 1, p.err, kErrTimeoutMma);
+            const bool w3 = mbar_wait(&s.pv_done[(i - 1) % kSBufs], ((i - 1) / kSBufs) & 1, p.err, kErrTimeoutMma);
             if (!__all_sync(0xFFFFFFFFu, w3)) { ok = false; break; }
             tc_fence_after();
             uint32_t ov[32], os;

@@ -92,6 +92,53 @@ def test_triattn_matches_oracle(weights, starting, b, n, masked):
         assert oracle.rel_l2(got[i] - z[i].float(), want - z[i].float()) < DELTA_TOL
 
 
+@pytest.mark.parametrize("outgoing", [True, False])
+@pytest.mark.parametrize("n", [640, 800])
+def test_trimul_at_lengths_that_leave_a_partial_output_tile(weights, outgoing, n):
+    """N not a multiple of the contraction's 256-column tile, with two full 64-column chunks
+    before the tile's edge (the weak-scaling lengths of 2 and 4 GPUs). Every column of U must
+    be right: no output column may be worse than the bf16 floor of the whole (a staging
+    buffer overwritten before its store had read it once corrupted columns 576-583 at 640)."""
+    p = sub(weights, "tri_multi_outgoing" if outgoing else "tri_multi_incoming")
+    z, tokens = pair_inputs(1, n, 17, seed=12)
+    packed = kernels.trimul_prepare(p, torch.device("cuda"))
+    got = kernels.trimul(z.cuda(), tokens.cuda() > 0, packed, outgoing=outgoing, masked_zero=False).float().cpu()
+    want = oracle.triangle_multiplication(z[0].float(), tokens[0], p, outgoing=outgoing)
+    d, u = got[0] - want, want - z[0].float()
+    assert oracle.rel_l2(got[0] - z[0].float(), u) < DELTA_TOL
+    real = tokens[0] > 0  # padded rows / columns carry near-zero updates: their relative error is noise
+    d, u = d[real][:, real], u[real][:, real]
+    col = d.pow(2).sum((0, 2)).sqrt() / u.pow(2).sum((0, 2)).sqrt()
+    row = d.pow(2).sum((1, 2)).sqrt() / u.pow(2).sum((1, 2)).sqrt()
+    assert col.max() < 2 * DELTA_TOL and row.max() < 2 * DELTA_TOL, (col.argmax(), col.max(), row.max())
+
+
+@pytest.mark.parametrize("starting", [True, False])
+def test_triattn_rescale_for_a_late_dominant_key(starting):
+    """Weights and inputs under which some queries meet their dominant key only in a late key
+    block, so the running maximum is raised and O is rescaled in TMEM mid-row. The rescale must
+    wait for exactly the previous step's P V (a barrier phase once taken for an older one let
+    it race and corrupted query 5's row at N = 384). Every query row is held to the bf16 floor."""
+    w = block_state(torch.Generator().manual_seed(0), scheme="randomise")
+    p = sub(w, "tri_atten_starting" if starting else "tri_atten_ending")
+    n = 384
+    from foldforge_b200.synthetic import inputs
+
+    z, _, tokens = inputs(n, 0, masked_suffix=11)
+    zb = z.bfloat16()
+    packed = kernels.triattn_prepare(p, torch.device("cuda"))
+    mask = (tokens > 0)[None].cuda()
+    want = oracle.triangle_attention(zb.float(), tokens, p, starting=starting)
+    u = want - zb.float()
+    for _ in range(3):  # the race was timing-dependent
+        got = kernels.triattn(zb[None].cuda(), mask, packed, starting=starting, masked_zero=False)[0].float().cpu()
+        d2, u2 = (got - want).pow(2).sum(-1), u.pow(2).sum(-1)
+        axis = 0 if starting else 1  # the problem rows: starting (i = row, j = query), ending (i = query, j = row)
+        per_query = (d2.sum(axis) / u2.sum(axis)).sqrt()
+        assert oracle.rel_l2(got - zb.float(), u) < DELTA_TOL
+        assert per_query.max() < 2 * DELTA_TOL, (per_query.argmax(), per_query.max())
+
+
 @pytest.mark.parametrize("starting", [True, False])
 def test_triattn_fully_masked_rows_average_uniformly(weights, starting):
     """Every token padded: the reference's -1e9 replacement gives uniform weights."""
