@@ -359,11 +359,15 @@ __global__ void __launch_bounds__(kProjThreads, 1)
 // of 128) of one (batch, row, head).
 //   warp 0      TMA: Q per unit (double-buffered), K, V^T and the two groups' bias tiles
 //               per block through a 4-stage ring
-//   warp 1      MMA: S = Q K^T of step i + 2 (into the group's S/P buffer (i + 2) % 3) ahead
-//               of O += P V of step i, with P read from TMEM (A operand) and O accumulated
-//               in TMEM across the unit's blocks (one O buffer per group: the next unit's
-//               first P V waits until the previous output has been read). Three S/P
-//               buffers let the tensor pipe run two steps ahead of the softmax.
+//   warps 1, 10 MMA, one thread per group (on different SM sub-partitions): S = Q K^T of
+//               step i + 2 (into the group's S/P buffer (i + 2) % 3) ahead of O += P V of
+//               step i, with P read from TMEM (A operand) and O accumulated in TMEM across
+//               the unit's blocks (one O buffer per group: the next unit's first P V waits
+//               until the previous output has been read). Three S/P buffers let the tensor
+//               pipe run two steps ahead of the softmax. With a head width of 32 the
+//               products are small and each tcgen05 instruction costs its issuing thread
+//               tens of cycles, so one thread issuing both groups' 12 products and their
+//               commits per step would pace the kernel.
 //   warps 2-9   softmax, thread = query row (TMEM lane): logits = S + bias (+ key mask),
 //               P = 2^(x - m) written back over S as bf16. The running maximum m is raised
 //               lazily: only when a block's maximum exceeds m + kRescale does the warp
@@ -373,7 +377,8 @@ __global__ void __launch_bounds__(kProjThreads, 1)
 //               read, normalised and stored while the next unit's first block runs.
 constexpr int kKB = 64;        // keys per block
 constexpr int kKVStages = 4;
-constexpr int kAttnThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 softmax (2 groups)
+constexpr int kAttnThreads = 352;  // warp 0 TMA, warps 1 / 10 MMA (group 0 / 1), warps 2..9 softmax
+constexpr int kMmaWarp1 = 10;
 constexpr int kMaxMaskWords = 2048;  // B * ceil(N / 64) * 2 words of key-mask bits
 constexpr int kPolyEvery = 4;        // one key pair in four takes the FMA-pipe exponential
 constexpr int kVtRows = 48;          // V^T (32 rows), a row of ones, 15 zero rows
@@ -391,11 +396,11 @@ struct AttnSmem {
   uint32_t mask_words[kMaxMaskWords];
   uint64_t q_full[2], q_empty[2];
   uint64_t kv_full[kKVStages], kv_empty[kKVStages];
-  uint64_t s_full[kSBufs];            // both groups' S of a step
+  uint64_t s_full[kGroups][kSBufs];
   uint64_t p_full[kGroups][kSBufs];
-  uint64_t pv_done[kSBufs];           // both groups' P V of step i, on barrier i % kSBufs
+  uint64_t pv_done[kGroups][kSBufs];  // the group's P V of step i, on barrier i % kSBufs
   uint64_t o_full[kGroups], o_free[kGroups];
-  uint64_t mma_done;
+  uint64_t mma_done[kGroups];
   uint32_t tmem_base;
 };
 
@@ -437,22 +442,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.q_full[i], 1);
-      mbar_init(&s.q_empty[i], 1);
+      mbar_init(&s.q_empty[i], kGroups);  // one commit per MMA thread
     }
     for (int i = 0; i < kKVStages; ++i) {
       mbar_init(&s.kv_full[i], 1);
-      mbar_init(&s.kv_empty[i], 1 + 8);  // MMA commit + 8 softmax warps (bias read)
+      mbar_init(&s.kv_empty[i], kGroups + 8);  // a commit per MMA thread + 8 softmax warps (bias read)
     }
     for (int g = 0; g < kGroups; ++g) {
       mbar_init(&s.o_full[g], 1);
       mbar_init(&s.o_free[g], 4);
       for (int i = 0; i < kSBufs; ++i) {
         mbar_init(&s.p_full[g][i], 4);
-        if (g == 0) mbar_init(&s.s_full[i], 1);
+        mbar_init(&s.s_full[g][i], 1);
+        mbar_init(&s.pv_done[g][i], 1);
       }
     }
-    mbar_init(&s.mma_done, 1);
-    for (int i = 0; i < kSBufs; ++i) mbar_init(&s.pv_done[i], 1);
+    for (int g = 0; g < kGroups; ++g) mbar_init(&s.mma_done[g], 1);
     fence_mbar_init();
   }
   // key-mask bits, per batch padded to whole 64-key blocks (zero beyond N)
@@ -523,59 +528,75 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         mbar_wait(&s.q_full[i & 1], (i >> 1) & 1, p.err, kErrTimeoutLoad);
       }
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == 1 || warp == kMmaWarp1) {
+    // ------------------------------------------------------------ MMA issuers (one per group)
     if (lane == 0) {
+      const int g = warp == 1 ? 0 : 1;
       const uint32_t idesc_s = idesc_bf16_f32(128, kKB);
       const uint32_t idesc_o = idesc_bf16_f32(128, kOCols);
-      auto issue_s = [&](int i) -> bool {
-        const int ul = i / nkb, j = i % nkb;
+      // The loop is kept short (no runtime division, descriptors advanced by constant
+      // strides): this thread shares its sub-partition with softmax warps that are always
+      // ready to issue. Descriptor start addresses are in 16-byte units (14 bits; shared
+      // memory < 256 KB).
+      constexpr uint32_t kQStep = kTile * kD * 2 / 16, kKStep = kKB * kD * 2 / 16, kVStep = kVtRows * kKB * 2 / 16;
+      const uint64_t dq0 = desc_kmajor_sw64(smem_u32(s.q[0][g]));
+      const uint64_t dk0 = desc_kmajor_sw64(smem_u32(s.k[0]));
+      const uint64_t dv0 = desc_kmajor_sw128(smem_u32(s.vt[0]));
+      const uint32_t gcols = tmem0 + g * kGroupCols;
+      // S = Q K^T of step i (block j of unit ul) for this group into S/P buffer i % kSBufs
+      auto issue_s = [&](int i, int j, int ul) -> bool {
         const int st = i % kKVStages, buf = i % kSBufs, qb = ul & 1;
         if (j == 0 && !mbar_wait(&s.q_full[qb], (ul >> 1) & 1, p.err, kErrTimeoutLoad)) return false;
         if (!mbar_wait(&s.kv_full[st], (i / kKVStages) & 1, p.err, kErrTimeoutLoad)) return false;
         tc_fence_after();
-        for (int g = 0; g < kGroups; ++g) {
-          const uint32_t d = tmem0 + g * kGroupCols + buf * 64;
-          const uint64_t da = desc_kmajor_sw64(smem_u32(s.q[qb][g]));
-          const uint64_t db = desc_kmajor_sw64(smem_u32(s.k[st]));
-          mma_bf16(d, da, db, idesc_s, 0);
-          mma_bf16(d, da + 2, db + 2, idesc_s, 1);
-        }
-        mma_commit(&s.s_full[buf]);  // both groups' S
+        const uint32_t d = gcols + buf * 64;
+        const uint64_t da = dq0 + static_cast<uint64_t>(qb * kGroups * kQStep);
+        const uint64_t db = dk0 + static_cast<uint64_t>(st * kKStep);
+        mma_bf16(d, da, db, idesc_s, 0);
+        mma_bf16(d, da + 2, db + 2, idesc_s, 1);
+        mma_commit(&s.s_full[g][buf]);
         if (j == nkb - 1) mma_commit(&s.q_empty[qb]);  // the unit's Q may be refilled once these finish
         return true;
       };
       bool ok = true;
-      for (int i = 0; i < 2 && i < steps && ok; ++i) ok = issue_s(i);
+      int si = 0, sj = 0, sul = 0;  // the next S step and its (block, unit)
+      for (; si < 2 && si < steps && ok; ++si) {
+        ok = issue_s(si, sj, sul);
+        if (++sj == nkb) sj = 0, ++sul;
+      }
+      int j = 0, ul = 0;
       for (int i = 0; i < steps && ok; ++i) {
         // S two steps ahead: its buffer's last P was read by the P V issued one step ago
         // (same thread, so the tensor pipe keeps the order)
-        if (i + 2 < steps && !issue_s(i + 2)) break;
-        const int ul = i / nkb, j = i % nkb;
-        const int st = i % kKVStages, buf = i % kSBufs;
-        for (int g = 0; g < kGroups; ++g) {
-          if (!mbar_wait(&s.p_full[g][buf], (i / kSBufs) & 1, p.err, kErrTimeoutMma)) { ok = false; break; }
-          // the single O buffer: the previous unit's output has been read
-          if (j == 0 && !mbar_wait(&s.o_free[g], (ul & 1) ^ 1, p.err, kErrTimeoutEmpty)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t d = tmem0 + g * kGroupCols + kOCol;
-          const uint32_t a = tmem0 + g * kGroupCols + buf * 64;
-          const uint64_t db = desc_kmajor_sw128(smem_u32(s.vt[st]));
-#pragma unroll
-          for (int kk = 0; kk < kKB / 16; ++kk)
-            mma_bf16_tmem_a(d, a + kk * 8, db + 2 * kk, idesc_o, (j | kk) != 0);
-          if (j == nkb - 1) mma_commit(&s.o_full[g]);
+        if (si < steps) {
+          if (!issue_s(si, sj, sul)) break;
+          ++si;
+          if (++sj == nkb) sj = 0, ++sul;
         }
-        if (!ok) break;
-        // both groups' P V of step i. One barrier per S/P buffer: when the softmax of step i + 1
-        // waits for it, S(i + 1) has landed, so every P V up to step i - 2 has too, and the
-        // barrier's previous phase (step i - 3) is complete: the parity wait is exact
-        mma_commit(&s.pv_done[buf]);
+        const int st = i % kKVStages, buf = i % kSBufs;
+        if (!mbar_wait(&s.p_full[g][buf], (i / kSBufs) & 1, p.err, kErrTimeoutMma)) break;
+        // the single O buffer: the previous unit's output has been read
+        if (j == 0 && !mbar_wait(&s.o_free[g], (ul & 1) ^ 1, p.err, kErrTimeoutEmpty)) break;
+        tc_fence_after();
+        const uint32_t d = gcols + kOCol;
+        const uint32_t a = gcols + buf * 64;
+        const uint64_t db = dv0 + static_cast<uint64_t>(st * kVStep);
+        mma_bf16_tmem_a(d, a, db, idesc_o, j != 0);
+        mma_bf16_tmem_a(d, a + 8, db + 2, idesc_o, 1);
+        mma_bf16_tmem_a(d, a + 16, db + 4, idesc_o, 1);
+        mma_bf16_tmem_a(d, a + 24, db + 6, idesc_o, 1);
+        if (j == nkb - 1) mma_commit(&s.o_full[g]);
+        // this group's P V of step i. One barrier per S/P buffer: when the softmax of step
+        // i + 1 waits for it, S(i + 1) has landed, so every P V of the group up to step i - 2
+        // has too, and the barrier's previous phase (step i - 3) is complete: the parity wait
+        // is exact
+        mma_commit(&s.pv_done[g][buf]);
         mma_commit(&s.kv_empty[st]);
+        if (++j == nkb) j = 0, ++ul;
       }
       // every issued MMA completes before TMEM is released
-      mma_commit(&s.mma_done);
-      mbar_wait(&s.mma_done, 0, p.err, kErrTimeoutMma);
+      mma_commit(&s.mma_done[g]);
+      mbar_wait(&s.mma_done[g], 0, p.err, kErrTimeoutMma);
     }
   } else {
     // ------------------------------------------------------------ softmax warpgroups
@@ -626,7 +647,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int j = 0; j < nkb; ++j, ++i) {
         const int st = i % kKVStages;
         const int buf = i % kSBufs;
-        const bool w1 = mbar_wait(&s.s_full[buf], (i / kSBufs) & 1, p.err, kErrTimeoutMma);
+        const bool w1 = mbar_wait(&s.s_full[g][buf], (i / kSBufs) & 1, p.err, kErrTimeoutMma);
         const bool w2 = mbar_wait(&s.kv_full[st], (i / kKVStages) & 1, p.err, kErrTimeoutLoad);
         if (!__all_sync(0xFFFFFFFFu, w1 && w2)) { ok = false; break; }
         tc_fence_after();
@@ -677,7 +698,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             // P V has landed
             const float m_new = need ? bm : m;
             const float alpha = ex2(m - m_new);
-            const bool w3 = mbar_wait(&s.pv_done[(i - 1) % kSBufs], ((i - 1) / kSBufs) & 1, p.err, kErrTimeoutMma);
+            const bool w3 = mbar_wait(&s.pv_done[g][(i - 1) % kSBufs], ((i - 1) / kSBufs) & 1, p.err, kErrTimeoutMma);
             if (!__all_sync(0xFFFFFFFFu, w3)) { ok = false; break; }
             tc_fence_after();
             uint32_t ov[32], os;
