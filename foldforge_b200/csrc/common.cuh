@@ -192,6 +192,12 @@ __device__ __forceinline__ void tma_store_wait_read0() {
 
 __device__ __forceinline__ void tma_store_wait_all0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// Wait until every committed store group but the most recent one has finished READING
+// shared memory (two staging buffers used in turn).
+__device__ __forceinline__ void tma_store_wait_read1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+
 // Plain (untiled) bulk copy global -> shared; addresses 16-byte aligned, size % 16 == 0.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(

@@ -33,6 +33,7 @@ constexpr int kH = 128;       // hidden channels
 
 // ---------------------------------------------------------------- packed weight image
 // [0, 128K)            projection operand: rows 0..127 W_l', 128..255 W_lg', 256..383 W_r', 384..511 W_rg'
+//                      (each scaled by 1/2: the epilogue's sigmoid is 1/2 + tanh(x / 2) / 2)
 // [128K, 160K)         gate operand W_g' (rows = output channels)
 // [160K, 192K)         output operand W_o' = W_o diag(gamma_out)
 // [192K, +)            fp32: wsum_proj[512] bias_proj[512] wsum_gate[128] bias_gate[128] bias_out[128]
@@ -69,12 +70,12 @@ constexpr int kPThreads = 384;
 struct ProjSmem {
   alignas(1024) uint8_t w[kProjBytes];
   alignas(1024) uint8_t z[kPStages][kPTile * kC * 2];
-  alignas(1024) uint8_t out[2][kH * kPTile * 2];  // L / R staging: [128 channels][64 pairs], SW128
+  // L / R staging per part, two halves of 32 pairs used in turn: [128 channels][32 pairs], SW64
+  alignas(1024) uint8_t out[2][2][kH * 32 * 2];
   float wsum[512];
   float bias[512];
-  float mean[2][kPTile];
-  float rstd[2][kPTile];
-  float pm[2][kPTile];
+  float4 coef[2][kPTile / 2];  // per pair couple (2i, 2i + 1): rstd, rstd; -rstd mean, -rstd mean
+  float2 pm[2][kPTile / 2];    // per pair couple: the pair mask
   uint64_t wbar;
   uint64_t z_full[kPStages], z_empty[kPStages];
   uint64_t acc_full[2], acc_free[2];
@@ -196,44 +197,48 @@ __global__ void __launch_bounds__(kPThreads, 1)
       bool w2 = mbar_wait(&s.st_free[buf], ((it >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty);
       if (!__all_sync(0xFFFFFFFFu, w1 && w2)) break;
       const uint8_t* zt = s.z[st];
-      float sum = 0.f;
+      // one pass over the pair's 128 channels on the paired fp32 pipe: sums of x - x0 and
+      // of its square (shifted by the first channel, so the variance does not cancel)
       uint4 v[16];
 #pragma unroll
       for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
         for (int q = 0; q < 8; ++q)
           v[kb * 8 + q] = *reinterpret_cast<const uint4*>(zt + kb * (kPTile * 128) + sw128_offset(t, q * 8));
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) sum += bf16_lo(w[j]) + bf16_hi(w[j]);
-      }
-      const float mean = sum * (1.0f / kC);
-      float q2 = 0.f;
+      const float x0 = bf16_lo(v[0].x);
+      const uint64_t shift = f32x2(-x0, -x0);
+      uint64_t s1 = 0, s2 = 0;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const float a = bf16_lo(w[j]) - mean, bb = bf16_hi(w[j]) - mean;
-          q2 += a * a + bb * bb;
+          const uint64_t d = add_f32x2(f32x2(bf16_lo(w[j]), bf16_hi(w[j])), shift);
+          s1 = add_f32x2(s1, d);
+          s2 = fma_f32x2(d, d, s2);
         }
       }
+      float a1, b1, a2, b2;
+      f32x2_split(s1, a1, b1);
+      f32x2_split(s2, a2, b2);
+      const float dm = (a1 + b1) * (1.0f / kC);
+      const float mean = x0 + dm;
+      const float var = fmaxf((a2 + b2) * (1.0f / kC) - dm * dm, 0.f);
       const int c0 = (tile % tiles_per_row) * kPTile;
       const int rr = tile / tiles_per_row;
       const int b = rr / p.R, r = rr - b * p.R;
       const int k = c0 + t;
-      const float rstd = rsqrtf(q2 * (1.0f / kC) + 1e-5f);
-      s.mean[buf][t] = mean;
-      s.rstd[buf][t] = rstd;
+      const float rstd = rsqrtf(var + 1e-5f);
+      reinterpret_cast<float*>(&s.coef[buf][t >> 1])[t & 1] = rstd;
+      reinterpret_cast<float*>(&s.coef[buf][t >> 1])[2 + (t & 1)] = -rstd * mean;
       if (k < p.N) {
         // natural pair (i, j) of the rows held: outgoing row tile (r, k), incoming column
         // tile (k, r) (the incoming direction always holds all N rows)
         const int64_t pi = p.outgoing ? r : k, pj = p.outgoing ? k : r;
         p.zstats[(static_cast<int64_t>(b) * p.R + pi) * p.N + pj] = make_float2(mean, rstd);
       }
-      s.pm[buf][t] = (k < p.N && p.mask[b * p.N + p.row0 + r] && p.mask[b * p.N + k]) ? 1.0f : 0.0f;
+      reinterpret_cast<float*>(&s.pm[buf][t >> 1])[t & 1] =
+          (k < p.N && p.mask[b * p.N + p.row0 + r] && p.mask[b * p.N + k]) ? 1.0f : 0.0f;
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&s.st_full[buf]);
@@ -246,62 +251,91 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const int c = (warp & 3) * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const int rp = part * 256 + c, rg = part * 256 + 128 + c;
-    const float wsp = s.wsum[rp], bsp = s.bias[rp], wsg = s.wsum[rg], bsg = s.bias[rg];
+    // W_l / W_r and their gates carry 1/2 (packed that way), so with yp' = yp / 2 and
+    // yg' = yg / 2: yp sigmoid(yg) = yp' (1 + tanh(yg'))
+    const uint64_t wsp = f32x2(s.wsum[rp], s.wsum[rp]), bsp = f32x2(s.bias[rp], s.bias[rp]);
+    const uint64_t wsg = f32x2(s.wsum[rg], s.wsum[rg]), bsg = f32x2(s.bias[rg], s.bias[rg]);
     const CUtensorMap* map_out = part == 0 ? &map_l : &map_r;
-    const bool issuer = (warp & 3) == 0 && lane == 0;
-    uint8_t* stage = s.out[part];
-    int it = 0;
-    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
-      const int buf = it & 1;
-      bool w1 = mbar_wait(&s.acc_full[buf], (it >> 1) & 1, p.err, kErrTimeoutMma);
-      bool w2 = mbar_wait(&s.st_full[buf], (it >> 1) & 1, p.err, kErrTimeoutLoad);
-      // the previous tile's store has finished reading the staging tile before it is
-      // rewritten; the part's four warps leave together on a failed wait
-      if (issuer) tma_store_wait_read0();
-      if (named_barrier_or(1 + part, 128, !(w1 && w2))) break;
-      tc_fence_after();
+    // Software-pipelined over 32-pair chunks: a chunk's TMEM load is in flight while the
+    // previous chunk is staged and stored (the next tile's first chunk included).
+    uint32_t vp[32], vg[32], packed[16];
+    auto compute = [&](int buf, int ch) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        // pairs (j, j + 1) of this channel on the paired pipe: y = rstd acc - rstd mean wsum + b
+        const float4 cf = s.coef[buf][(ch >> 1) + i];
+        const float2 pm2 = s.pm[buf][(ch >> 1) + i];
+        const uint64_t rs = f32x2(cf.x, cf.y), nm = f32x2(cf.z, cf.w);
+        const uint64_t yp = fma_f32x2(rs, f32x2(__uint_as_float(vp[2 * i]), __uint_as_float(vp[2 * i + 1])),
+                                      fma_f32x2(nm, wsp, bsp));
+        const uint64_t yg = fma_f32x2(rs, f32x2(__uint_as_float(vg[2 * i]), __uint_as_float(vg[2 * i + 1])),
+                                      fma_f32x2(nm, wsg, bsg));
+        float g0, g1;
+        f32x2_split(yg, g0, g1);
+        const uint64_t o = mul_f32x2(fma_f32x2(yp, f32x2(tanh_fast(g0), tanh_fast(g1)), yp), f32x2(pm2.x, pm2.y));
+        float o0, o1;
+        f32x2_split(o, o0, o1);
+        packed[i] = pack_bf16(o0, o1);
+      }
+    };
+    // each warp stages and stores its own 32 channels; half h's previous store from this
+    // warp (two stores ago) has finished reading it. Pairs c0 + ch .. + 31 of row r, batch
+    // b; a half wholly past N is not stored (its group stays empty, so groups alternate halves)
+    auto stage_store = [&](int tile, int ch) {
       const int c0 = (tile % tiles_per_row) * kPTile;
       const int rr = tile / tiles_per_row;
       const int b = rr / p.R, r = rr - b * p.R;
-#pragma unroll 1
-      for (int ch = 0; ch < kPTile; ch += 32) {
-        uint32_t vp[32], vg[32];
-        tmem_ld32(tmem0 + lane_off + buf * 256 + (2 * part) * kPTile + ch, vp);
-        tmem_ld32(tmem0 + lane_off + buf * 256 + (2 * part + 1) * kPTile + ch, vg);
-        tmem_ld_wait();
-        uint32_t packed[16];
+      const int h = ch >> 5;
+      if (lane == 0) tma_store_wait_read1();
+      __syncwarp();
+      uint8_t* stage = s.out[part][h];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float o2[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int j = ch + 2 * i + e;
-            const float mu = s.mean[buf][j], rs = s.rstd[buf][j];
-            const float yp = rs * (__uint_as_float(vp[2 * i + e]) - mu * wsp) + bsp;
-            const float yg = rs * (__uint_as_float(vg[2 * i + e]) - mu * wsg) + bsg;
-            o2[e] = yp * sigmoid_fast(yg) * s.pm[buf][j];
-          }
-          packed[i] = pack_bf16(o2[0], o2[1]);
-        }
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          *reinterpret_cast<uint4*>(stage + sw128_offset(c, ch + 8 * q)) =
-              make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+      for (int q = 0; q < 4; ++q)
+        *reinterpret_cast<uint4*>(stage + sw64_offset(c, 8 * q)) =
+            make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        if (c0 + ch < p.N) tma_store_4d(map_out, stage + (warp & 3) * 32 * 64, c0 + ch, (warp & 3) * 32, r, b);
+        tma_store_commit();
       }
+    };
+    // wait for tile `it`'s accumulators and statistics, then start its first chunk's load
+    // (no barrier joins the epilogue warps, so each leaves on its own after a failed wait)
+    auto begin = [&](int it) -> bool {
+      const int buf = it & 1;
+      const bool w1 = mbar_wait(&s.acc_full[buf], (it >> 1) & 1, p.err, kErrTimeoutMma);
+      const bool w2 = mbar_wait(&s.st_full[buf], (it >> 1) & 1, p.err, kErrTimeoutLoad);
+      if (!__all_sync(0xFFFFFFFFu, w1 && w2)) return false;
+      tc_fence_after();
+      const uint32_t tb = tmem0 + lane_off + buf * 256 + (2 * part) * kPTile;
+      tmem_ld32(tb, vp);
+      tmem_ld32(tb + kPTile, vg);
+      return true;
+    };
+    int it = 0;
+    bool ok = blockIdx.x < total && begin(0);
+    for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
+      const int buf = it & 1;
+      const uint32_t tb = tmem0 + lane_off + buf * 256 + (2 * part) * kPTile;
+      tmem_ld_wait();
+      compute(buf, 0);
+      tmem_ld32(tb + 32, vp);
+      tmem_ld32(tb + kPTile + 32, vg);
+      stage_store(tile, 0);
+      tmem_ld_wait();
+      compute(buf, 32);
+      // the tile's accumulators and statistics have been read
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&s.acc_free[buf]);
         mbar_arrive(&s.st_free[buf]);
       }
-      fence_async_smem();
-      named_barrier(1 + part, 128);
-      if (issuer) {
-        tma_store_4d(map_out, stage, c0, 0, r, b);  // [pairs c0..c0+63][channels][row r][batch b]
-        tma_store_commit();
-      }
+      if (tile + static_cast<int>(gridDim.x) < total) ok = begin(it + 1);
+      stage_store(tile, 32);
     }
-    if (issuer) tma_store_wait_all0();
+    if (lane == 0) tma_store_wait_all0();
   }
   tc_fence_before();
   __syncthreads();
@@ -603,7 +637,7 @@ int trimul_prepare(const TriMulWeights& w, void* packed, cudaStream_t stream) {
   const float* mats[4] = {w.to_left, w.to_left_gate, w.to_right, w.to_right_gate};
   int rc = 0;
   for (int i = 0; i < 4 && rc == 0; ++i)
-    rc = launch_pack_weight(mats[i], kH, kC, w.ln_w, w.ln_b, img, i * kH, 512, vec + 0, vec + 512, stream);
+    rc = launch_pack_weight(mats[i], kH, kC, w.ln_w, w.ln_b, img, i * kH, 512, vec + 0, vec + 512, stream, 0.5f);
   if (rc == 0)
     rc = launch_pack_weight(w.to_gate, kC, kC, w.ln_w, w.ln_b, img + kProjBytes, 0, kC, vec + 1024, vec + 1152,
                             stream);
@@ -639,10 +673,10 @@ int launch_proj(const void* z, const uint8_t* mask, const void* packed, void* le
     const uint64_t dims[4] = {static_cast<uint64_t>(N), kH, static_cast<uint64_t>(R), static_cast<uint64_t>(B)};
     const uint64_t strides[3] = {static_cast<uint64_t>(ls_c) * 2, static_cast<uint64_t>(ls_r) * 2,
                                  static_cast<uint64_t>(ls_b) * 2};
-    const uint32_t box[4] = {kPTile, kH, 1, 1};
-    st = make_map(&map_l, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, left, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    const uint32_t box[4] = {32, 32, 1, 1};  // one warp's 32 channels of a staging half
+    st = make_map(&map_l, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, left, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
     if (st) return st;
-    st = make_map(&map_r, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, right, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    st = make_map(&map_r, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, right, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
     if (st) return st;
   }
   ProjParams pp{static_cast<const uint8_t*>(packed), mask, static_cast<__nv_bfloat16*>(left),
