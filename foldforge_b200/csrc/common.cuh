@@ -404,35 +404,38 @@ __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v 
 __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 
 // LayerNorm statistics (mean, 1/sqrt(var + 1e-5)) of row `row` of a K-major SW128 tile of
-// 128 bf16 channels stored as two 64-channel blocks `block_bytes` apart (two-pass variance
-// over the row held in registers).
+// 128 bf16 channels stored as two 64-channel blocks `block_bytes` apart: one pass on the
+// paired fp32 pipe over the row held in registers, summing x - x0 and its square (shifted by
+// the row's first channel, so the variance does not cancel when |mean| >> std).
 __device__ __forceinline__ void ln_stats_c128(const uint8_t* tile, int block_bytes, int row, float& mean,
                                               float& rstd) {
-  float s = 0.f;
   uint4 v[16];
 #pragma unroll
   for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
     for (int q = 0; q < 8; ++q)
       v[kb * 8 + q] = *reinterpret_cast<const uint4*>(tile + kb * block_bytes + sw128_offset(row, q * 8));
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) s += bf16_lo(w[j]) + bf16_hi(w[j]);
-  }
-  mean = s * (1.0f / 128.0f);
-  float q2 = 0.f;
+  const float x0 = bf16_lo(v[0].x);
+  uint64_t shift, s1 = 0, s2 = 0;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(shift) : "f"(-x0));
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const float a = bf16_lo(w[j]) - mean, b = bf16_hi(w[j]) - mean;
-      q2 += a * a + b * b;
+      uint64_t x, d;
+      asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(bf16_lo(w[j])), "f"(bf16_hi(w[j])));
+      asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(x), "l"(shift));
+      asm("add.rn.f32x2 %0, %1, %2;" : "=l"(s1) : "l"(s1), "l"(d));
+      asm("fma.rn.f32x2 %0, %1, %1, %2;" : "=l"(s2) : "l"(d), "l"(s2));
     }
   }
-  rstd = rsqrtf(q2 * (1.0f / 128.0f) + 1e-5f);
+  float a1, b1, a2, b2;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a1), "=f"(b1) : "l"(s1));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a2), "=f"(b2) : "l"(s2));
+  const float dm = (a1 + b1) * (1.0f / 128.0f);
+  mean = x0 + dm;
+  rstd = rsqrtf(fmaxf((a2 + b2) * (1.0f / 128.0f) - dm * dm, 0.f) + 1e-5f);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {

@@ -245,29 +245,36 @@ __global__ void __launch_bounds__(kProjThreads, 1)
       tc_fence_after();
       const int64_t row_base = (static_cast<int64_t>(b) * p.R + r) * kHeads;  // (b, r) -> head 0
       const uint64_t rs2 = f32x2(rstd, rstd), nrm2 = f32x2(-rstd * mean, -rstd * mean);
-      // Q (columns 0..127) and K (128..255): one head = 32 columns = 64 contiguous bytes
-#pragma unroll 1
-      for (int cc = 0; cc < 256; cc += 32) {
-        uint32_t v[32];
-        tmem_ld32(tmem0 + lane_off + kColX + cc, v);
-        tmem_ld_wait();
-        if (valid) {
-          // channels (c, c + 1): rstd v - rstd mean wsum + bias
-          uint32_t w[16];
+      // Q (columns 0..127) and K (128..255): one head = 32 columns = 64 contiguous bytes.
+      // Double-buffered TMEM loads: chunk cc + 32 is in flight while chunk cc is written.
+      auto qk_chunk = [&](int cc, const uint32_t (&v)[32]) {
+        if (!valid) return;
+        // channels (c, c + 1): rstd v - rstd mean wsum + bias
+        uint32_t w[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float4 wb = s.wb[(cc >> 1) + i];
-            float a, bb;
-            f32x2_split(fma_f32x2(rs2, f32x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])),
-                                  fma_f32x2(nrm2, f32x2(wb.x, wb.y), f32x2(wb.z, wb.w))),
-                        a, bb);
-            w[i] = pack_bf16(a, bb);
-          }
-          const int head = (cc % 128) / 32;
-          uint4* dst = reinterpret_cast<uint4*>((cc < 128 ? p.q : p.k) + ((row_base + head) * p.N + n) * kD);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        for (int i = 0; i < 16; ++i) {
+          const float4 wb = s.wb[(cc >> 1) + i];
+          float a, bb;
+          f32x2_split(fma_f32x2(rs2, f32x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])),
+                                fma_f32x2(nrm2, f32x2(wb.x, wb.y), f32x2(wb.z, wb.w))),
+                      a, bb);
+          w[i] = pack_bf16(a, bb);
         }
+        const int head = (cc % 128) / 32;
+        uint4* dst = reinterpret_cast<uint4*>((cc < 128 ? p.q : p.k) + ((row_base + head) * p.N + n) * kD);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+      };
+      uint32_t va[32], vb[32];
+      tmem_ld32(tmem0 + lane_off + kColX, va);
+#pragma unroll 1
+      for (int cc = 0; cc < 256; cc += 64) {
+        tmem_ld_wait();
+        tmem_ld32(tmem0 + lane_off + kColX + cc + 32, vb);
+        qk_chunk(cc, va);
+        tmem_ld_wait();
+        if (cc + 64 < 256) tmem_ld32(tmem0 + lane_off + kColX + cc + 64, va);
+        qk_chunk(cc + 32, vb);
       }
       {
         uint32_t v[16];
@@ -294,56 +301,69 @@ __global__ void __launch_bounds__(kProjThreads, 1)
     const int c = (warp & 3) * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint64_t wsv2 = f32x2(s.wsum[256 + c], s.wsum[256 + c]), bsv2 = f32x2(s.bias[256 + c], s.bias[256 + c]);
-    const bool issuer = warp == 6 && lane == 0;
+    // Each warp stages and stores its own 32 channels, one 64-pair half at a time (two
+    // halves used in turn); the next 32-pair chunk's TMEM load is in flight while the
+    // current one is converted.
+    auto chunk = [&](int sb, int ch, const uint32_t (&v)[32]) {
+      uint32_t packed[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {  // pairs (j, j + 1): rstd v - rstd mean wsum + bias
+        const float4 st4 = s.stats[sb][(ch >> 1) + i];
+        float a, bb;
+        f32x2_split(fma_f32x2(f32x2(st4.x, st4.y), f32x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])),
+                              fma_f32x2(f32x2(st4.z, st4.w), wsv2, bsv2)),
+                    a, bb);
+        packed[i] = pack_bf16(a, bb);
+      }
+      uint8_t* stage = s.vt[ch / 64];
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        *reinterpret_cast<uint4*>(stage + sw128_offset(c, (ch % 64) + 8 * q)) =
+            make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+    };
     int it = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
       const int sb = it & 1;
-      bool w1 = mbar_wait(&s.y_full, it & 1, p.err, kErrTimeoutMma);
-      bool w2 = mbar_wait(&s.st_full[sb], (it >> 1) & 1, p.err, kErrTimeoutLoad);
-      // the previous tile's stores have finished reading the staging tiles; the four warps
-      // leave together on a failed wait
-      if (issuer) tma_store_wait_read0();
-      if (named_barrier_or(1, 128, !(w1 && w2))) break;
+      const bool w1 = mbar_wait(&s.y_full, it & 1, p.err, kErrTimeoutMma);
+      const bool w2 = mbar_wait(&s.st_full[sb], (it >> 1) & 1, p.err, kErrTimeoutLoad);
+      // no barrier joins these warps, so each leaves on its own after a failed wait
+      if (!__all_sync(0xFFFFFFFFu, w1 && w2)) break;
       tc_fence_after();
       const int c0 = (tile % tiles_per_row) * kTile;
       const int rr = tile / tiles_per_row;
+      uint32_t va[32], vb[32];
+      tmem_ld32(tmem0 + lane_off + kColY, va);
 #pragma unroll 1
-      for (int ch = 0; ch < kTile; ch += 32) {
-        uint32_t v[32];
-        tmem_ld32(tmem0 + lane_off + kColY + ch, v);
+      for (int ch = 0; ch < kTile; ch += 64) {
+        // this warp's store of this half two stores ago has finished reading it
+        if (lane == 0) tma_store_wait_read1();
+        __syncwarp();
         tmem_ld_wait();
-        uint32_t packed[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {  // pairs (j, j + 1): rstd v - rstd mean wsum + bias
-          const float4 st4 = s.stats[sb][(ch >> 1) + i];
-          float a, bb;
-          f32x2_split(fma_f32x2(f32x2(st4.x, st4.y), f32x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])),
-                                fma_f32x2(f32x2(st4.z, st4.w), wsv2, bsv2)),
-                      a, bb);
-          packed[i] = pack_bf16(a, bb);
+        tmem_ld32(tmem0 + lane_off + kColY + ch + 32, vb);
+        chunk(sb, ch, va);
+        tmem_ld_wait();
+        if (ch + 64 < kTile) tmem_ld32(tmem0 + lane_off + kColY + ch + 64, va);
+        chunk(sb, ch + 32, vb);
+        if (ch + 64 == kTile) {
+          // the tile's accumulator and statistics have been read
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&s.y_free);
+            mbar_arrive(&s.st_free[sb]);
+          }
         }
-        uint8_t* stage = s.vt[ch / 64];
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          *reinterpret_cast<uint4*>(stage + sw128_offset(c, (ch % 64) + 8 * q)) =
-              make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&s.y_free);
-        mbar_arrive(&s.st_free[sb]);
-      }
-      fence_async_smem();
-      named_barrier(1, 128);
-      if (issuer) {
-        // V^T rows (b, r, head, d) = rr * 128 + c; pairs past N are clipped by the map
-        tma_store_2d(&map_vt, s.vt[0], c0, rr * kC);
-        if (c0 + 64 < p.N) tma_store_2d(&map_vt, s.vt[1], c0 + 64, rr * kC);
-        tma_store_commit();
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          // V^T rows (b, r, head, d) = rr * 128 + c for this warp's 32 channels; pairs past
+          // N are clipped by the map, a half wholly past N is not stored (empty group)
+          if (c0 + ch < p.N) tma_store_2d(&map_vt, s.vt[ch / 64] + (warp & 3) * 32 * 128, c0 + ch, rr * kC + (warp & 3) * 32);
+          tma_store_commit();
+        }
       }
     }
-    if (issuer) tma_store_wait_all0();
+    if (lane == 0) tma_store_wait_all0();
   }
   tc_fence_before();
   __syncthreads();
@@ -1128,7 +1148,7 @@ int launch_proj(const void* z, const void* packed, __nv_bfloat16* q, __nv_bfloat
     // V^T as rows (b, r, head, d) of N pairs (row stride Np), stored in [128 x 64] boxes
     const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(B) * R * kC};
     const uint64_t strides[1] = {static_cast<uint64_t>(np) * 2};
-    const uint32_t box[2] = {64, kC};
+    const uint32_t box[2] = {64, 32};  // one warp's 32 channels of a 64-pair half
     st = make_map(&map_vt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, vt, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
   }
