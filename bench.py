@@ -50,8 +50,8 @@ N_TOKENS = 512
 N_BLOCKS = 48
 MASKED = 26
 #: DRAM traffic of one triangle-attention core launch at N = 512 (dram__bytes_read.sum +
-#: dram__bytes_write.sum of one ncu capture of ``--kernels-once --n 512``: 203.7 + 48.6 MB).
-ATTN_TRAFFIC_BYTES: float | None = 252.3e6
+#: dram__bytes_write.sum of one ncu capture of ``--kernels-once --n 512``: 203.7 + 46.6 MB).
+ATTN_TRAFFIC_BYTES: float | None = 250.3e6
 
 
 def parse() -> argparse.Namespace:
