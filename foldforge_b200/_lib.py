@@ -68,6 +68,8 @@ SIGNATURES: dict[str, list] = {
     "ffb_apb_single_workspace_bytes": [c_int],
     "ffb_apb_shard_single": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_float, c_void_p, c_void_p,
                              ctypes.c_size_t, c_int, c_int, c_void_p],
+    "ffb_apb_shard_single_rows": [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p, ctypes.c_size_t,
+                                  c_int, c_int, c_int, c_int, c_void_p],
     # row-shard exchanges over NVLink peer memory (CUDA IPC buffers)
     "ffb_p2p_handle_bytes": [],
     "ffb_p2p_alloc": [ctypes.c_size_t, ctypes.POINTER(c_void_p), c_void_p],
@@ -171,7 +173,7 @@ LAUNCHES = {
     "ffb_transition_fwd": 1, "ffb_apb_fwd": 5, "ffb_single_transition_fwd": 3,
     "ffb_trimul_shard_proj": 1, "ffb_trimul_shard_contract": 1, "ffb_trimul_shard_out": 1,
     "ffb_triattn_shard_proj": 1, "ffb_triattn_shard_attn": 1, "ffb_triattn_shard_out": 1,
-    "ffb_transition_shard_fwd": 1, "ffb_apb_shard_pair_bias": 1, "ffb_apb_shard_single": 4,
+    "ffb_transition_shard_fwd": 1, "ffb_apb_shard_pair_bias": 1, "ffb_apb_shard_single": 4, "ffb_apb_shard_single_rows": 4,
     "ffb_single_transition_fwd_noalloc": 3,
     "ffb_shard_transpose_p2p": 1, "ffb_shard_gather_p2p": 1, "ffb_shard_wait_p2p": 1, "ffb_shard_rows_p2p": 1,
     "ffb_trimul_channel_contract": 1,

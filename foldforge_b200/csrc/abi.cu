@@ -542,4 +542,31 @@ int ffb_apb_shard_single(const void* s, const uint8_t* mask, const void* packed,
                           N, masked == FFB_MASKED_ZERO, info, static_cast<cudaStream_t>(stream));
 }
 
+// The rank's rows of the single track's attention with pair bias from its own pair-bias rows.
+int ffb_apb_shard_single_rows(const void* s, const uint8_t* mask, const void* packed, const void* pb_rows,
+                              float gate_bias, void* out_rows, void* workspace, size_t workspace_bytes, int N,
+                              int row0, int R, int masked, void* stream) {
+  if (N <= 0 || R <= 0 || row0 < 0 || row0 + R > N)
+    return fail(FFB_ERR_ARG, "apb_shard_single_rows: N=%d row0=%d R=%d", N, row0, R);
+  if (!s || !mask || !packed || !pb_rows || !out_rows || !workspace)
+    return fail(FFB_ERR_ARG, "apb_shard_single_rows: null pointer");
+  if (masked != FFB_MASKED_COMPUTE && masked != FFB_MASKED_ZERO)
+    return fail(FFB_ERR_ARG, "apb_shard_single_rows: masked=%d", masked);
+  if (workspace_bytes < apb_single_workspace_bytes(N))
+    return fail(FFB_ERR_ARG, "apb_shard_single_rows: workspace %zu < %zu bytes", workspace_bytes,
+                apb_single_workspace_bytes(N));
+  const uint8_t* s_rows = static_cast<const uint8_t*>(s) + static_cast<size_t>(row0) * 384 * 2;
+  if (!aligned16(s) || !aligned16(out_rows) || !aligned16(pb_rows) ||
+      ((reinterpret_cast<uintptr_t>(packed) | reinterpret_cast<uintptr_t>(workspace)) & 255u))
+    return fail(FFB_ERR_ARG, "apb_shard_single_rows: misaligned pointer");
+  const uint8_t* o = static_cast<const uint8_t*>(out_rows);
+  if (o < s_rows + static_cast<size_t>(R) * 384 * 2 && s_rows < o + static_cast<size_t>(R) * 384 * 2)
+    return fail(FFB_ERR_ARG, "apb_shard_single_rows: out_rows must not overlap s");
+  DeviceInfo info;
+  int st = device_info(&info);
+  if (st != FFB_OK) return st;
+  return apb_shard_single_rows(s, mask, packed, pb_rows, gate_bias, out_rows, workspace, N, row0, R,
+                               masked == FFB_MASKED_ZERO, info, static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -104,6 +104,9 @@ int apb_forward(const void* s, const void* z, const uint8_t* mask, const void* p
 int apb_shard_pair_bias(const void* z, const void* packed, void* pb_rows, int R, int N, const DeviceInfo& info,
                         cudaStream_t stream);
 size_t apb_single_workspace_bytes(int N);
+int apb_shard_single_rows(const void* s, const uint8_t* mask, const void* packed, const void* pb_rows, float gate_bias,
+                          void* out_rows, void* workspace, int N, int row0, int R, int masked_zero,
+                          const DeviceInfo& info, cudaStream_t stream);
 int apb_shard_single(const void* s, const uint8_t* mask, const void* packed, const void* pb_all, const void* extra,
                      int extra_f32, float gate_bias, void* out, void* workspace, int N, int masked_zero,
                      const DeviceInfo& info, cudaStream_t stream);

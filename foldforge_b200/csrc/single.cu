@@ -221,7 +221,7 @@ struct ChunkRegs {
 __device__ __forceinline__ void attn_load_chunk(ChunkRegs& r, const __nv_bfloat16* __restrict__ qkvg,
                                                 const float* __restrict__ pb, int64_t pb_r, const void* __restrict__ extra,
                                                 int extra_f32, const uint8_t* __restrict__ mask, int b, int h,
-                                                int qb, int N, int j0) {
+                                                int qb, int N, int j0, int q0, int nq) {
   const int t = threadIdx.x;
   const int nk = N - j0 < kKC ? N - j0 : kKC;
 #pragma unroll
@@ -241,7 +241,7 @@ __device__ __forceinline__ void attn_load_chunk(ChunkRegs& r, const __nv_bfloat1
     const int qq = e / (kKC / 4), j = (e % (kKC / 4)) * 4;
     const int ii = qb * kQ + qq;
     float v[4] = {0.f, 0.f, 0.f, 0.f};
-    if (ii < N) {
+    if (ii < nq) {
       const float* src = pb + static_cast<int64_t>(ii) * pb_r + j0 + j;
       if (j + 4 <= nk && (reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
         const float4 f = *reinterpret_cast<const float4*>(src);
@@ -255,7 +255,7 @@ __device__ __forceinline__ void attn_load_chunk(ChunkRegs& r, const __nv_bfloat1
       }
       if (extra != nullptr) {
         for (int i = 0; i < 4 && j + i < nk; ++i) {
-          const int64_t x = ((static_cast<int64_t>(b) * kHs + h) * N + ii) * N + j0 + j + i;
+          const int64_t x = ((static_cast<int64_t>(b) * kHs + h) * N + q0 + ii) * N + j0 + j + i;
           v[i] += extra_f32 ? static_cast<const float*>(extra)[x]
                             : __bfloat162float(static_cast<const __nv_bfloat16*>(extra)[x]);
         }
@@ -300,18 +300,22 @@ __device__ __forceinline__ void attn_store_chunk(const ChunkRegs& r, float* buf)
   if (t < kKC) keep[t] = r.keep;
 }
 
+// Queries [q0, q0 + nq) of each batch entry (local index i = query - q0) against all N keys:
+// the pair-bias row of local query i is pair_bias + h * pb_h + (b * nq + i) * pb_r and the
+// output row is out + (b * nq + i) * 384, so a rank passes only its own rows of both.
 __global__ void __launch_bounds__(kAttnThreads, 2) single_attention_kernel(
     const __nv_bfloat16* __restrict__ qkvg, const float* __restrict__ pair_bias, int64_t pb_h, int64_t pb_r,
     const void* __restrict__ extra,
-    int extra_f32, const uint8_t* __restrict__ mask, float gate_bias, __nv_bfloat16* __restrict__ out, int B, int N) {
+    int extra_f32, const uint8_t* __restrict__ mask, float gate_bias, __nv_bfloat16* __restrict__ out, int B, int N,
+    int q0, int nq) {
   __shared__ __align__(16) float smem[2 * kBufFloats];
-  const int qblocks = (N + kQ - 1) / kQ;
+  const int qblocks = (nq + kQ - 1) / kQ;
   const int h = blockIdx.x % kHs;
   const int qb = (blockIdx.x / kHs) % qblocks;
   const int b = blockIdx.x / (kHs * qblocks);
   const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
   const int i = qb * kQ + lane;
-  const int row = i < N ? i : N - 1;
+  const int row = q0 + (i < nq ? i : nq - 1);
   const __nv_bfloat16* row_i = qkvg + (static_cast<int64_t>(b) * N + row) * (4 * kCs);
   const float scale = rsqrtf(static_cast<float>(kDs));
   float q[kDs];
@@ -329,19 +333,19 @@ __global__ void __launch_bounds__(kAttnThreads, 2) single_attention_kernel(
   float o[kDs];
 #pragma unroll
   for (int d = 0; d < kDs; ++d) o[d] = 0.f;
-  // bias row i of head h: pair_bias + h * pb_h + (b * N + i) * pb_r
-  const float* pb = pair_bias + h * pb_h + static_cast<int64_t>(b) * N * pb_r;
+  // bias row i of head h: pair_bias + h * pb_h + (b * nq + i) * pb_r
+  const float* pb = pair_bias + h * pb_h + static_cast<int64_t>(b) * nq * pb_r;
   const int chunks = (N + kKC - 1) / kKC;
   {
     ChunkRegs r;
-    attn_load_chunk(r, qkvg, pb, pb_r, extra, extra_f32, mask, b, h, qb, N, 0);
+    attn_load_chunk(r, qkvg, pb, pb_r, extra, extra_f32, mask, b, h, qb, N, 0, q0, nq);
     attn_store_chunk(r, smem);
   }
   __syncthreads();
   for (int c = 0; c < chunks; ++c) {
     const bool next = c + 1 < chunks;
     ChunkRegs r;
-    if (next) attn_load_chunk(r, qkvg, pb, pb_r, extra, extra_f32, mask, b, h, qb, N, (c + 1) * kKC);
+    if (next) attn_load_chunk(r, qkvg, pb, pb_r, extra, extra_f32, mask, b, h, qb, N, (c + 1) * kKC, q0, nq);
     const float* buf = smem + (c & 1) * kBufFloats;
     const float* ks = buf;
     const float* vs = buf + kKC * kDs;
@@ -401,7 +405,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) single_attention_kernel(
   part[(warp * kQ + lane) * kPartPitch + kDs] = m;
   part[(warp * kQ + lane) * kPartPitch + kDs + 1] = l;
   __syncthreads();
-  if (warp != 0 || i >= N) return;
+  if (warp != 0 || i >= nq) return;
   float mm = -1.0e30f;
   for (int w = 0; w < kWarps; ++w) {
     const float* pw = part + (w * kQ + lane) * kPartPitch;
@@ -420,7 +424,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) single_attention_kernel(
     for (int d = 0; d < kDs; ++d) acc[d] = fmaf(pw[d], f, acc[d]);
   }
   const float inv = 1.0f / ll;
-  __nv_bfloat16* dst = out + (static_cast<int64_t>(b) * N + i) * kCs + h * kDs;
+  __nv_bfloat16* dst = out + (static_cast<int64_t>(b) * nq + i) * kCs + h * kDs;
 #pragma unroll
   for (int u = 0; u < 3; ++u) {
     const uint4 gv = *reinterpret_cast<const uint4*>(row_i + 3 * kCs + h * kDs + u * 8);
@@ -575,7 +579,7 @@ int launch_single_attention(const void* s, const uint8_t* mask, const uint8_t* i
   const int ctas = B * kHs * ((N + kQ - 1) / kQ);
   single_attention_kernel<<<ctas, kAttnThreads, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(qkvg), pb, pb_h, pb_r, extra, extra_f32, mask, gate_bias,
-      static_cast<__nv_bfloat16*>(gated), B, N);
+      static_cast<__nv_bfloat16*>(gated), B, N, 0, N);
   st = cuda_status(static_cast<int>(cudaGetLastError()), "single attention launch");
   if (st) return st;
   return gemm(gated, img + L.w_o, out, static_cast<int>(T), kCs, kCs, 0, nullptr, kEpiResidual, s,
@@ -618,6 +622,39 @@ int apb_shard_single(const void* s, const uint8_t* mask, const void* packed, con
   return launch_single_attention(s, mask, static_cast<const uint8_t*>(packed), static_cast<const float*>(pb_all), N,
                                  static_cast<int64_t>(kHs) * N, extra, extra_f32, gate_bias, out,
                                  static_cast<uint8_t*>(workspace), 1, N, masked_zero, info, stream);
+}
+
+// The rank's rows [row0, row0 + R) of the single track's attention with pair bias, from its
+// own pair-bias rows pb_rows [R][16][N] (fp32, as apb_shard_pair_bias writes them): LayerNorm
+// and the [q | k | v | g] projection over all N tokens (s is replicated; the keys and values
+// need every token), the attention for the R queries only, and the output projection with
+// the residual s[row0 + r] (masked rows zeroed under masked_zero). out_rows is [R][384].
+int apb_shard_single_rows(const void* s, const uint8_t* mask, const void* packed, const void* pb_rows, float gate_bias,
+                          void* out_rows, void* workspace, int N, int row0, int R, int masked_zero,
+                          const DeviceInfo& info, cudaStream_t stream) {
+  const uint8_t* img = static_cast<const uint8_t*>(packed);
+  const ApbLayout L = apb_layout();
+  const size_t T = static_cast<size_t>(N);
+  uint8_t* y = static_cast<uint8_t*>(workspace);
+  uint8_t* qkvg = y + a256(T * kCs * 2);
+  uint8_t* gated = qkvg + a256(T * 4 * kCs * 2);
+  int st = cuda_status(launch_layernorm(s, y, reinterpret_cast<const float*>(img + L.ln_s_w),
+                                        reinterpret_cast<const float*>(img + L.ln_s_b), static_cast<int64_t>(T), kCs,
+                                        1e-5f, 0, info.num_sms, stream),
+                       "apb rows layernorm");
+  if (st) return st;
+  st = gemm(y, img + L.w_qkvg, qkvg, N, 4 * kCs, kCs, 0, reinterpret_cast<const float*>(img + L.b_qkvg), kEpiStore,
+            nullptr, nullptr, info, stream);
+  if (st) return st;
+  const int ctas = kHs * ((R + kQ - 1) / kQ);
+  single_attention_kernel<<<ctas, kAttnThreads, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(qkvg), static_cast<const float*>(pb_rows), N,
+      static_cast<int64_t>(kHs) * N, nullptr, 0, mask, gate_bias, reinterpret_cast<__nv_bfloat16*>(gated), 1, N, row0, R);
+  st = cuda_status(static_cast<int>(cudaGetLastError()), "single attention (rows) launch");
+  if (st) return st;
+  return gemm(gated, img + L.w_o, out_rows, R, kCs, kCs, 0, nullptr, kEpiResidual,
+              static_cast<const __nv_bfloat16*>(s) + static_cast<int64_t>(row0) * kCs,
+              masked_zero ? mask + row0 : nullptr, info, stream);
 }
 
 size_t single_transition_packed_bytes() { return st_layout().total; }

@@ -385,18 +385,22 @@ class B200ShardOps:
 
     def single(self, s: Tensor, z: Tensor, mask: Tensor, apb_packed: Tensor, gate_bias: float,
                st_packed: Tensor) -> Tensor:
+        """Attention with pair bias for this rank's query rows (their pair-bias rows are its own
+        pair rows), an all-gather of the updated [R, 384] rows, then the single transition
+        (replicated)."""
         from foldforge_b200 import kernels
 
         r, n, _ = z.shape
+        row0 = self.comm.rows(n)[1]
         pb_rows = torch.empty((r, 16, n), dtype=torch.float32, device=z.device)
         _lib.call("ffb_apb_shard_pair_bias", _ptr(z), _ptr(apb_packed), _ptr(pb_rows), r, n, _stream())
-        pb_all = self.comm.gather_rows(pb_rows)  # [N, 16, N]
         lib = _lib.load()
         ws = torch.empty(int(lib.ffb_apb_single_workspace_bytes(n)), dtype=torch.uint8, device=z.device)
-        s2 = torch.empty_like(s)
-        _lib.call("ffb_apb_shard_single", _ptr(s), _ptr(mask), _ptr(apb_packed), _ptr(pb_all), _ptr(None), 0,
-                  ctypes.c_float(gate_bias), _ptr(s2), _ptr(ws), ctypes.c_size_t(ws.numel()), n, self.masked,
-                  _stream())
+        rows = torch.empty((r, s.shape[1]), dtype=s.dtype, device=s.device)
+        _lib.call("ffb_apb_shard_single_rows", _ptr(s), _ptr(mask), _ptr(apb_packed), _ptr(pb_rows),
+                  ctypes.c_float(gate_bias), _ptr(rows), _ptr(ws), ctypes.c_size_t(ws.numel()), n, row0, r,
+                  self.masked, _stream())
+        s2 = self.comm.gather_rows(rows)  # [N, 384]
         return kernels.single_transition(s2[None], mask[None], st_packed, masked_zero=bool(self.masked))[0]
 
 
@@ -469,22 +473,25 @@ class TorchShardOps:
 
     def single(self, s: Tensor, z: Tensor, mask: Tensor, wa: dict[str, Tensor], gate_bias: float,
                wt: dict[str, Tensor]) -> Tensor:
-        n = z.shape[1]
+        r, n = z.shape[0], z.shape[1]
+        row0 = self.comm.rows(n)[1]
         hs = wa["to_bias.weight"].shape[0]
-        pb = self.comm.gather_rows(_lin(_ln(z, wa["ln_pair.weight"], None), wa["to_bias.weight"]))  # [N, N, 16]
+        pb = _lin(_ln(z, wa["ln_pair.weight"], None), wa["to_bias.weight"])  # this rank's query rows [R, N, 16]
         y = _ln(s, wa["ln_single.weight"], wa["ln_single.bias"])
         cs = y.shape[-1]
         ds = cs // hs
-        q = _lin(y, wa["to_query.weight"]) + wa["to_query.bias"]
+        q = (_lin(y, wa["to_query.weight"]) + wa["to_query.bias"])[row0:row0 + r]
         k, v = _lin(y, wa["to_key.weight"]), _lin(y, wa["to_value.weight"])
-        q, k, v = (t.reshape(n, hs, ds).transpose(0, 1) for t in (q, k, v))
+        q = q.reshape(r, hs, ds).transpose(0, 1)
+        k, v = (t.reshape(n, hs, ds).transpose(0, 1) for t in (k, v))
         logits = q @ k.transpose(-1, -2) / ds ** 0.5 + pb.permute(2, 0, 1)
         logits = torch.where(mask[None, None, :] > 0, logits, torch.full_like(logits, -1e9))
-        o = (logits.softmax(-1) @ v).transpose(0, 1).reshape(n, cs)
-        delta = _lin(torch.sigmoid(_lin(y, wa["to_gate.weight"]) + gate_bias) * o, wa["to_out.weight"])
+        o = (logits.softmax(-1) @ v).transpose(0, 1).reshape(r, cs)
+        gate = _lin(y[row0:row0 + r], wa["to_gate.weight"])
+        delta = _lin(torch.sigmoid(gate + gate_bias) * o, wa["to_out.weight"])
         if self.masked_zero:
-            delta = delta * mask.float()[:, None]
-        s = s + delta
+            delta = delta * mask.float()[row0:row0 + r, None]
+        s = self.comm.gather_rows(s[row0:row0 + r] + delta)
         x = _ln(s, wt["ln_in.weight"], wt["ln_in.bias"])
         d2 = _lin(F.silu(_lin(x, wt["expand_a.weight"])) * _lin(x, wt["expand_b.weight"]), wt["squeeze.weight"])
         if self.masked_zero:

@@ -202,6 +202,15 @@ size_t ffb_apb_single_workspace_bytes(int N);
 int ffb_apb_shard_single(const void* s, const uint8_t* mask, const void* packed, const void* pb_all,
                          const void* extra_pair_bias, int extra_dtype, float gate_bias, void* out, void* workspace,
                          size_t workspace_bytes, int N, int masked, void* stream);
+/* The rank's rows [row0, row0 + R) of the single track's attention with pair bias, computed
+ * from its OWN pair-bias rows pb_rows [R][16][N] (fp32, ffb_apb_shard_pair_bias): the
+ * projection runs over all N tokens of the replicated s, the attention for the R queries;
+ * out_rows [R][384] bf16 = s rows + the update (the rank's rows, to be all-gathered). Replaces
+ * the all-gather of the [N][16][N] pair bias that ffb_apb_shard_single needs. Workspace:
+ * ffb_apb_single_workspace_bytes(N). */
+int ffb_apb_shard_single_rows(const void* s, const uint8_t* mask, const void* packed, const void* pb_rows,
+                              float gate_bias, void* out_rows, void* workspace, size_t workspace_bytes, int N,
+                              int row0, int R, int masked, void* stream);
 
 /* ---- Row-shard exchanges over NVLink peer memory (one rank per GPU of one box). Buffers
  * are plain device allocations shared through CUDA IPC handles (no multicast object):

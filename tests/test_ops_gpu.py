@@ -192,6 +192,38 @@ def test_attention_pair_bias_matches_oracle(weights, extra, b, n, masked):
         assert oracle.rel_l2(got[i] - s[i].float(), want - s[i].float()) < DELTA_TOL
 
 
+@pytest.mark.parametrize("n,masked,splits", [(160, 9, [(0, 80), (80, 80)]),
+                                            (200, 13, [(0, 67), (67, 67), (134, 66)])])
+@pytest.mark.parametrize("zero", [False, True])
+def test_single_track_by_query_rows_matches_the_whole(weights, n, masked, splits, zero):
+    """The row-sharded single track (each rank's queries from its own pair-bias rows,
+    ``ffb_apb_shard_single_rows``) reproduces the one-GPU op row for row."""
+    import ctypes
+
+    p = sub(weights, "single_attention")
+    s, z, tokens = single_inputs(1, n, masked)
+    dev = torch.device("cuda")
+    packed = kernels.apb_prepare(p, dev)
+    mask = (tokens[0] > 0).to(dev)
+    whole = kernels.attention_pair_bias(s.to(dev), z.to(dev), mask[None], packed, masked_zero=zero)[0]
+    lib = _lib.load()
+    ws = torch.empty(int(lib.ffb_apb_single_workspace_bytes(n)), dtype=torch.uint8, device=dev)
+    s0, z0, m8 = s[0].to(dev).contiguous(), z[0].to(dev), mask.to(torch.uint8).contiguous()
+    parts = []
+    for row0, r in splits:
+        zr = z0[row0:row0 + r].contiguous()
+        pb = torch.empty((r, 16, n), dtype=torch.float32, device=dev)
+        _lib.call("ffb_apb_shard_pair_bias", zr.data_ptr(), packed.data_ptr(), pb.data_ptr(), r, n, 0)
+        rows = torch.empty((r, 384), dtype=torch.bfloat16, device=dev)
+        _lib.call("ffb_apb_shard_single_rows", s0.data_ptr(), m8.data_ptr(), packed.data_ptr(), pb.data_ptr(),
+                  ctypes.c_float(0.0), rows.data_ptr(), ws.data_ptr(), ctypes.c_size_t(ws.numel()), n, row0, r,
+                  1 if zero else 0, 0)
+        parts.append(rows)
+    got = torch.cat(parts)
+    torch.cuda.synchronize()
+    assert torch.equal(got, whole)
+
+
 @pytest.mark.parametrize("b,n,masked", CASES)
 def test_single_transition_matches_oracle(weights, b, n, masked):
     p = sub(weights, "single_transition")
