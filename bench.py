@@ -66,6 +66,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-ladder", action="store_true", help="skip the N=2048 length-ladder measurement")
     ap.add_argument("--no-msa", action="store_true", help="skip the MSA-module measurement (configuration 4)")
+    ap.add_argument("--breakdown", action="store_true",
+                    help="with --gpus > 1: per-stage CUDA-event times of the N=2048 sharded trunk (max over ranks)")
     ap.add_argument("--kernels-once", action="store_true",
                     help="launch every pair-stack kernel once at --n (a driver for ncu captures; no timing)")
     return ap.parse_args()
@@ -485,6 +487,34 @@ def msa_module_single_gpu(dev: torch.device, n_blocks: int = 4) -> dict:
             "tflops_approx": round(flops / (ms * 1e-3) / 1e12, 1), "parallelism": "single GPU (CUDA-graph replay)"}
 
 
+def stage_breakdown(comm, run_trunk, data, nb: int, dist, dev) -> dict:
+    """Per-stage times of one pass of the sharded trunk at the ladder length: CUDA events at
+    every stage boundary of every block (``ShardComm.timer``), summed per stage name over
+    the blocks, divided by the block count, max over ranks per stage."""
+    import math
+
+    from foldforge_b200.engine.sharded import StageTimer
+
+    rows_h, s_h, mask = data(LADDER_N, math.ceil(0.05 * LADDER_N))
+    rows, s = rows_h.to(dev), s_h.to(dev)
+    run_trunk(rows, mask, s)
+    torch.cuda.synchronize()
+    dist.barrier()
+    comm.timer = StageTimer()
+    comm.mark("start")
+    run_trunk(rows, mask, s)
+    torch.cuda.synchronize()
+    per = comm.timer.durations()
+    comm.timer = None
+    names = list(per)
+    t = torch.tensor([per[k] / nb for k in names], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    stages = {k: round(float(v), 4) for k, v in zip(names, t.tolist())}
+    return {"n": LADDER_N, "n_gpus": comm.world, "ms_per_block": stages,
+            "sum_of_stage_maxima_ms": round(sum(stages.values()), 3),
+            "note": "CUDA events at stage boundaries, eager launches; each stage's max over ranks"}
+
+
 def run_sharded(args, rank: int, world: int, local: int, dist) -> None:
     """Row-sharded trunk over the ranks: weak-scaling ``value`` and the N = 2048 ladder."""
     import math
@@ -580,6 +610,10 @@ def run_sharded(args, rank: int, world: int, local: int, dist) -> None:
                   "ms_per_block": round(lad_ms / nb, 3), "masked_suffix": math.ceil(0.05 * LADDER_N), "steps": 2,
                   "warmup": 1, "parallelism": f"axial row-sharding x{world} (eager)", "clocks": lad_clocks}
 
+    breakdown = None
+    if args.breakdown:
+        breakdown = stage_breakdown(comm, run_trunk, data, nb, dist, dev)
+
     # dominant kernel alone (triangle-attention core at N = 512 on this GPU)
     n = N_TOKENS
     zz, _, tok = inputs(n, seed=0, masked_suffix=MASKED)
@@ -634,6 +668,8 @@ def run_sharded(args, rank: int, world: int, local: int, dist) -> None:
             line["e2e"] = e2e
         if ladder is not None:
             line["ladder"] = ladder
+        if breakdown is not None:
+            line["breakdown"] = breakdown
         line["parity"] = parity
         print(json.dumps(line), flush=True)
     comm.close()  # every rank: unmap the peers' exchange buffers before the group goes

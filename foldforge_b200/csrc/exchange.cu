@@ -52,6 +52,13 @@ __device__ __forceinline__ void signal_peers(const uint64_t* flag_ptrs, uint32_t
 
 // x: this rank's pair rows [R][N][128] bf16 (global rows row0 + i). Pair (i, c), c = q R + a,
 // goes to rank q's receive buffer at [a][row0 + i]: the rows of z^T that rank q holds.
+// One warp per (source column c, chunk of kTRows rows): column c of this rank's rows goes to
+// rank q = c / R, row a = c % R of its buffer, at columns row0 + i, so the chunk's pairs land
+// as ONE contiguous run there (kTRows x 256 bytes over NVLink) while the source pairs are read
+// with a stride of N pairs (each a coalesced 256-byte piece). Lanes 0-15 move one pair's 16
+// words, lanes 16-31 the next pair's; the index arithmetic is 32-bit and once per chunk.
+constexpr int kTRows = 64;
+
 __global__ void __launch_bounds__(kXThreads) pair_transpose_scatter_kernel(const uint4* __restrict__ x,
                                                                            const uint64_t* __restrict__ dst,
                                                                            const uint64_t* __restrict__ flag_ptrs,
@@ -60,27 +67,28 @@ __global__ void __launch_bounds__(kXThreads) pair_transpose_scatter_kernel(const
   __shared__ uint64_t sdst[kMaxRanks];
   if (threadIdx.x < P) sdst[threadIdx.x] = dst[threadIdx.x];
   __syncthreads();
-  const int64_t pairs = static_cast<int64_t>(R) * N;
-  const int part = threadIdx.x & 15;  // 16-byte chunk of the 256-byte pair
-  const int64_t stride = (static_cast<int64_t>(gridDim.x) * kXThreads) >> 4;
-  int64_t p0 = (static_cast<int64_t>(blockIdx.x) * kXThreads + threadIdx.x) >> 4;
-  constexpr int kUnroll = 4;
-  for (; p0 < pairs; p0 += kUnroll * stride) {
-    uint4 v[kUnroll];
+  const int lane = threadIdx.x & 31;
+  const int part = lane & 15, half = lane >> 4;
+  const int chunks = (R + kTRows - 1) / kTRows;
+  const int items = N * chunks;
+  const int warps = static_cast<int>(gridDim.x) * (kXThreads / 32);
+  for (int item = static_cast<int>(blockIdx.x) * (kXThreads / 32) + static_cast<int>(threadIdx.x >> 5); item < items;
+       item += warps) {
+    const int c = item / chunks, i0 = (item - c * chunks) * kTRows;
+    const int q = c / R, a = c - q * R;
+    const int rows = R - i0 < kTRows ? R - i0 : kTRows;
+    const uint4* src = x + (static_cast<int64_t>(i0) * N + c) * 16 + part;
+    uint4* d = reinterpret_cast<uint4*>(sdst[q]) + (static_cast<int64_t>(a) * N + row0 + i0) * 16 + part;
+    const int64_t sstep = static_cast<int64_t>(N) * 16;
+    constexpr int kUnroll = 4;  // pairs per half-warp in flight
+    for (int i = half; i < rows; i += 2 * kUnroll) {
+      uint4 v[kUnroll];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int64_t pp = p0 + u * stride;
-      if (pp < pairs) v[u] = x[pp * 16 + part];
-    }
+      for (int u = 0; u < kUnroll; ++u)
+        if (i + 2 * u < rows) v[u] = src[(i + 2 * u) * sstep];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int64_t pp = p0 + u * stride;
-      if (pp < pairs) {
-        const int i = static_cast<int>(pp / N), c = static_cast<int>(pp - static_cast<int64_t>(i) * N);
-        const int q = c / R, a = c - q * R;
-        uint4* d = reinterpret_cast<uint4*>(sdst[q]);
-        d[(static_cast<int64_t>(a) * N + row0 + i) * 16 + part] = v[u];
-      }
+      for (int u = 0; u < kUnroll; ++u)
+        if (i + 2 * u < rows) d[(i + 2 * u) * 16] = v[u];
     }
   }
   signal_peers(flag_ptrs, sync, rank, P);
@@ -117,24 +125,35 @@ __global__ void __launch_bounds__(kXThreads) row_scatter_kernel(const uint4* __r
   __shared__ uint64_t sdst[kMaxRanks];
   if (threadIdx.x < P) sdst[threadIdx.x] = dst[threadIdx.x];
   __syncthreads();
-  const int64_t rows = mode == 0 ? static_cast<int64_t>(R) * 128 : static_cast<int64_t>(cpp) * N;
-  const int64_t words = rows * row_words;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * kXThreads;
-  for (int64_t w = static_cast<int64_t>(blockIdx.x) * kXThreads + threadIdx.x; w < words; w += stride) {
-    const int64_t r = w / row_words;
-    const int k = static_cast<int>(w - r * row_words);
+  // one warp per row (its destination worked out once), lanes striding over its words
+  const int lane = threadIdx.x & 31;
+  const int rows = mode == 0 ? R * 128 : cpp * N;
+  const int warps = static_cast<int>(gridDim.x) * (kXThreads / 32);
+  for (int r = static_cast<int>(blockIdx.x) * (kXThreads / 32) + static_cast<int>(threadIdx.x >> 5); r < rows;
+       r += warps) {
     int q;
     int64_t drow;
     if (mode == 0) {
-      const int i = static_cast<int>(r / 128), c = static_cast<int>(r % 128);
+      const int i = r >> 7, c = r & 127;
       q = c / cpp;
-      drow = static_cast<int64_t>(c - q * cpp) * N + static_cast<int64_t>(rank) * R + i;
+      drow = static_cast<int64_t>(c - q * cpp) * N + rank * R + i;
     } else {
-      const int cl = static_cast<int>(r / N), g = static_cast<int>(r % N);
+      const int cl = r / N, g = r - cl * N;
       q = g / R;
       drow = static_cast<int64_t>(rank * cpp + cl) * R + (g - q * R);
     }
-    reinterpret_cast<uint4*>(sdst[q])[drow * row_words + k] = src[w];
+    const uint4* s = src + static_cast<int64_t>(r) * row_words;
+    uint4* d = reinterpret_cast<uint4*>(sdst[q]) + drow * row_words;
+    constexpr int kUnroll = 4;
+    for (int k = lane; k < row_words; k += 32 * kUnroll) {
+      uint4 v[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+        if (k + 32 * u < row_words) v[u] = s[k + 32 * u];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+        if (k + 32 * u < row_words) d[k + 32 * u] = v[u];
+    }
   }
   signal_peers(flag_ptrs, sync, rank, P);
 }

@@ -126,6 +126,7 @@ class _PeerExchange:
         x = x.contiguous()
         _lib.call("ffb_shard_transpose_p2p", _ptr(x), _ptr(p1 if b else p0), _ptr(self.flag_ptrs), _ptr(self.sync),
                   r, n, self.comm.rank * r, self.comm.rank, self.comm.world, _stream())
+        self.comm.mark("transpose_send")
         self._wait()
         return buf.local[b * one:(b + 1) * one].view(x.dtype).view(r, n, c)
 
@@ -139,6 +140,7 @@ class _PeerExchange:
         buf, ptrs = self.g_bufs[key]
         _lib.call("ffb_shard_gather_p2p", _ptr(x), ctypes.c_size_t(one), _ptr(ptrs), _ptr(self.flag_ptrs),
                   _ptr(self.sync), self.comm.rank, self.comm.world, _stream())
+        self.comm.mark("gather_send")
         self._wait()
         return buf.local.view(x.dtype).view((self.comm.world * x.shape[0],) + tuple(x.shape[1:]))
 
@@ -158,6 +160,7 @@ class _PeerExchange:
         x = x.contiguous()
         _lib.call("ffb_shard_rows_p2p", _ptr(x), mode, r, n, _ptr(ptrs), _ptr(self.flag_ptrs), _ptr(self.sync),
                   self.comm.rank, p, _stream())
+        self.comm.mark(f"scatter_{tag}_send")
         self._wait()
         return buf.local.view(torch.bfloat16).view(shape)
 
@@ -181,6 +184,25 @@ def peer_path_allowed(identities: list[tuple[str, str]]) -> bool:
     hosts = {host for host, _ in identities}
     devices = [dev for _, dev in identities]
     return 1 < len(identities) <= 8 and len(hosts) == 1 and len(set(devices)) == len(devices)
+
+
+class StageTimer:
+    """CUDA events recorded on the current stream between the stages of sharded blocks; after
+    a synchronize, :meth:`durations` sums the time between consecutive marks per stage name."""
+
+    def __init__(self) -> None:
+        self.marks: list[tuple[str, torch.cuda.Event]] = []
+
+    def mark(self, name: str) -> None:
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        self.marks.append((name, ev))
+
+    def durations(self) -> dict[str, float]:
+        out: dict[str, float] = {}
+        for (_, a), (name, b) in zip(self.marks, self.marks[1:]):
+            out[name] = out.get(name, 0.0) + a.elapsed_time(b)
+        return out
 
 
 class ShardComm:
@@ -207,6 +229,14 @@ class ShardComm:
         self.wait_limit_us = int(wait_limit_us)
         self._peer: _PeerExchange | None = None
         self._peer_ok: bool | None = None
+        #: a :class:`StageTimer` to time the stages of the blocks run over this group (None: off)
+        self.timer: StageTimer | None = None
+        self.stage = ""
+
+    def mark(self, name: str) -> None:
+        """Record the end of stage ``name`` (prefixed by :attr:`stage`) when a timer is attached."""
+        if self.timer is not None:
+            self.timer.mark(f"{self.stage}{name}")
 
     def peer_capable(self, identity: tuple[str, str] | None = None) -> bool:
         """Collective (every rank calls it at the same point): gather each rank's
@@ -333,21 +363,28 @@ class B200ShardOps:
         zstats = torch.empty((r, n, 2), dtype=torch.float32, device=dev)
         _lib.call("ffb_trimul_shard_proj", _ptr(z), _ptr(mask), _ptr(packed), _ptr(left), _ptr(right), _ptr(zstats),
                   r, n, row0, _stream())
+        self.comm.mark("proj")
         if self.comm.trimul_by_channels(z):
             peer = self.comm._peer
             cpp = 128 // self.comm.world
             lc = peer.channel_rows(left, 0, n, "L")
             rc = peer.channel_rows(right, 0, n, "R")
+            self.comm.mark("exchange_LR")
             uc = torch.empty((cpp, n, np_), dtype=torch.bfloat16, device=dev)
             _lib.call("ffb_trimul_channel_contract", _ptr(lc), _ptr(rc), _ptr(uc), cpp, n, _stream())
+            self.comm.mark("contract")
             u = peer.channel_rows(uc, 1, n, "U")
+            self.comm.mark("exchange_U")
         else:
             right_all = self.comm.gather_rows(right)
+            self.comm.mark("gather_R")
             u = torch.empty((128, r, np_), dtype=torch.bfloat16, device=dev)
             _lib.call("ffb_trimul_shard_contract", _ptr(left), _ptr(right_all), _ptr(u), r, n, _stream())
+            self.comm.mark("contract")
         out = torch.empty_like(z)
         _lib.call("ffb_trimul_shard_out", _ptr(z), _ptr(mask), _ptr(packed), _ptr(u), _ptr(zstats), _ptr(None),
                   _ptr(out), r, n, row0, self.masked, _stream())
+        self.comm.mark("out")
         return out
 
     def triattn(self, z: Tensor, mask: Tensor, packed: Tensor, *, transposed_bias: bool) -> Tensor:
@@ -361,18 +398,22 @@ class B200ShardOps:
         bias_rows = torch.empty((r, 4, np_), dtype=torch.bfloat16, device=dev)
         _lib.call("ffb_triattn_shard_proj", _ptr(z), _ptr(packed), _ptr(q), _ptr(k), _ptr(vt), _ptr(bias_rows), r, n,
                   _stream())
+        self.comm.mark("proj")
         bias_all = self.comm.gather_rows(bias_rows)  # [N (rows of the pair held), 4, Np]
         if transposed_bias:
             # bias[q][h][k] = G[k][h][q]: the ending node's bias comes from the untransposed pair
             t = torch.zeros_like(bias_all)
             t[:, :, :n] = bias_all[:, :, :n].permute(2, 1, 0)
             bias_all = t
+        self.comm.mark("gather_bias")
         o = torch.empty((r, n, 128), dtype=torch.bfloat16, device=dev)
         _lib.call("ffb_triattn_shard_attn", _ptr(q), _ptr(k), _ptr(vt), _ptr(bias_all), _ptr(mask), _ptr(o), r, n,
                   row0, _stream())
+        self.comm.mark("attn")
         out = torch.empty_like(z)
         _lib.call("ffb_triattn_shard_out", _ptr(z), _ptr(mask), _ptr(packed), _ptr(o), _ptr(out), r, n, row0,
                   self.masked, _stream())
+        self.comm.mark("out")
         return out
 
     def transition(self, z: Tensor, mask: Tensor, packed: Tensor) -> Tensor:
@@ -381,6 +422,7 @@ class B200ShardOps:
         out = torch.empty_like(z)
         _lib.call("ffb_transition_shard_fwd", _ptr(z), _ptr(mask), _ptr(packed), _ptr(out), r, n, row0, self.masked,
                   _stream())
+        self.comm.mark("transition")
         return out
 
     def single(self, s: Tensor, z: Tensor, mask: Tensor, apb_packed: Tensor, gate_bias: float,
@@ -394,14 +436,19 @@ class B200ShardOps:
         row0 = self.comm.rows(n)[1]
         pb_rows = torch.empty((r, 16, n), dtype=torch.float32, device=z.device)
         _lib.call("ffb_apb_shard_pair_bias", _ptr(z), _ptr(apb_packed), _ptr(pb_rows), r, n, _stream())
+        self.comm.mark("pair_bias")
         lib = _lib.load()
         ws = torch.empty(int(lib.ffb_apb_single_workspace_bytes(n)), dtype=torch.uint8, device=z.device)
         rows = torch.empty((r, s.shape[1]), dtype=s.dtype, device=s.device)
         _lib.call("ffb_apb_shard_single_rows", _ptr(s), _ptr(mask), _ptr(apb_packed), _ptr(pb_rows),
                   ctypes.c_float(gate_bias), _ptr(rows), _ptr(ws), ctypes.c_size_t(ws.numel()), n, row0, r,
                   self.masked, _stream())
+        self.comm.mark("attention_rows")
         s2 = self.comm.gather_rows(rows)  # [N, 384]
-        return kernels.single_transition(s2[None], mask[None], st_packed, masked_zero=bool(self.masked))[0]
+        self.comm.mark("gather_rows")
+        out = kernels.single_transition(s2[None], mask[None], st_packed, masked_zero=bool(self.masked))[0]
+        self.comm.mark("transition")
+        return out
 
 
 # --------------------------------------------------------------------------- torch shard ops
@@ -553,14 +600,33 @@ class ShardedPairformerBlock:
         if self.ops_name == "b200":
             mask = mask.to(torch.uint8).contiguous()
         a = lambda name: self._arg(name, dev)  # noqa: E731
+
+        def stage(name: str) -> None:
+            comm.stage = name
+
+        stage("TMo.")
         z = ops.trimul(z, mask, a("tri_multi_outgoing"))
         y = comm.transpose(z)
+        stage("")
+        comm.mark("transpose")
+        stage("TMi.")
         y = ops.trimul(y, mask, a("tri_multi_incoming_t"))
         z = comm.transpose(y)
+        stage("")
+        comm.mark("transpose")
+        stage("TAs.")
         z = ops.triattn(z, mask, a("tri_atten_starting"), transposed_bias=False)
         y = comm.transpose(z)
+        stage("")
+        comm.mark("transpose")
+        stage("TAe.")
         y = ops.triattn(y, mask, a("tri_atten_ending"), transposed_bias=True)
+        stage("pair.")
         y = ops.transition(y, mask, a("transition_pair"))
         z = comm.transpose(y)
+        stage("")
+        comm.mark("transpose")
+        stage("single.")
         s = ops.single(s, z, mask, a("single_attention"), self.gate_bias, a("single_transition"))
+        stage("")
         return z, s
