@@ -66,6 +66,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-ladder", action="store_true", help="skip the N=2048 length-ladder measurement")
     ap.add_argument("--no-msa", action="store_true", help="skip the MSA-module measurement (configuration 4)")
+    ap.add_argument("--eager-sharded", action="store_true",
+                    help="with --gpus > 1: time eager launches instead of a captured CUDA graph of the sharded trunk")
     ap.add_argument("--breakdown", action="store_true",
                     help="with --gpus > 1: per-stage CUDA-event times of the N=2048 sharded trunk (max over ranks)")
     ap.add_argument("--kernels-once", action="store_true",
@@ -543,11 +545,38 @@ def run_sharded(args, rank: int, world: int, local: int, dist) -> None:
         rows = z[row0:row0 + r].bfloat16().contiguous()
         return rows, s.bfloat16(), (tokens > 0).to(dev)
 
+    graph_note: dict = {}
+
+    def runner(rows, mask, s):
+        """The trunk as a CUDA graph (captured on every rank after an eager warm-up pass that
+        also creates the exchange buffers; the exchanges count their epochs on the device, so
+        replays synchronise like eager passes), or eager launches."""
+        graph_note.clear()
+        graph_note["captured"] = False
+        if args.eager_sharded:
+            return lambda: run_trunk(rows, mask, s)
+        from foldforge_b200.engine.capture import GraphedCall
+
+        _lib.launch_count = 0
+        try:
+            graphed = GraphedCall(lambda r, ss: run_trunk(r, mask, ss), [rows, s], warmup=1)
+        except RuntimeError as exc:  # noqa: PERF203 - fall back to eager launches
+            graph_note["error"] = str(exc).splitlines()[0][:160]
+            torch.cuda.synchronize()
+            return lambda: run_trunk(rows, mask, s)
+        graph_note["captured"] = True
+        # the library's launches of one pass (the warm-up call and the capture made two)
+        graph_note["launches_per_pass"] = _lib.launch_count // 2
+        return graphed.replay
+
     def measure(n: int, masked: int, steps: int, warmup: int, clocks: bool = False):
         rows_h, s_h, mask = data(n, masked)
         rows, s = rows_h.to(dev), s_h.to(dev)
         for _ in range(warmup):
             run_trunk(rows, mask, s)
+        torch.cuda.synchronize()
+        dist.barrier()
+        step = runner(rows, mask, s)
         torch.cuda.synchronize()
         dist.barrier()
         sampler = ClockSampler(local) if clocks else None
@@ -562,19 +591,22 @@ def run_sharded(args, rank: int, world: int, local: int, dist) -> None:
             dist.barrier()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
-            run_trunk(rows, mask, s)
+            step()
             b.record()
             torch.cuda.synchronize()
             ts.append(a.elapsed_time(b))
-        launches = _lib.launch_count
+        launches = _lib.launch_count if not graph_note["captured"] else graph_note["launches_per_pass"] * steps
         dist.barrier()
         clk = sampler.stop() if sampler else None
         ms = max_over_ranks(sum(ts) / len(ts), dist)
-        return ms, clk, launches, (rows_h, s_h, mask)
+        mode = "CUDA-graph replay" if graph_note["captured"] else "eager launches" + (
+            f"; capture failed: {graph_note['error']}" if "error" in graph_note else "")
+        return ms, clk, launches, (rows_h, s_h, mask), mode
 
     n_w = weak_n(world)
     masked_w = round(MASKED * n_w / N_TOKENS)
-    value_ms, clocks, launches, (rows_h, s_h, mask) = measure(n_w, masked_w, args.steps, max(args.warmup, 3), True)
+    value_ms, clocks, launches, (rows_h, s_h, mask), mode = measure(n_w, masked_w, args.steps, max(args.warmup, 3),
+                                                                     True)
     err = _lib.device_error()
     if err:
         raise RuntimeError(f"device error word {err} after the timed region")
@@ -605,10 +637,10 @@ def run_sharded(args, rank: int, world: int, local: int, dist) -> None:
 
     ladder = None
     if not args.no_ladder:
-        lad_ms, lad_clocks, _, _ = measure(LADDER_N, math.ceil(0.05 * LADDER_N), 2, 1, True)
+        lad_ms, lad_clocks, _, _, lad_mode = measure(LADDER_N, math.ceil(0.05 * LADDER_N), 2, 1, True)
         ladder = {"n": LADDER_N, "n_gpus": world, "ms_per_trunk": round(lad_ms, 1),
                   "ms_per_block": round(lad_ms / nb, 3), "masked_suffix": math.ceil(0.05 * LADDER_N), "steps": 2,
-                  "warmup": 1, "parallelism": f"axial row-sharding x{world} (eager)", "clocks": lad_clocks}
+                  "warmup": 1, "parallelism": f"axial row-sharding x{world} ({lad_mode})", "clocks": lad_clocks}
 
     breakdown = None
     if args.breakdown:
@@ -646,7 +678,7 @@ def run_sharded(args, rank: int, world: int, local: int, dist) -> None:
             "config": {
                 "workload": f"{nb}-block Pairformer trunk, N={n_w} row-sharded over {world} GPUs (per-GPU work "
                             f"{n_w ** 3 / world / N_TOKENS ** 3:.2f} x the N=512 trunk), last {masked_w} tokens "
-                            "masked, master precision, eager launches",
+                            f"masked, master precision, {mode}",
                 "model": "AF3 Pairformer block (c_z 128, c_s 384, 4x32 / 16x24 heads)",
                 "global_batch": 1, "seq_len": n_w, "parallelism": f"axial row-sharding x{world} (NVLink peer-memory "
                                                                   "transposes / row gathers)",
