@@ -231,3 +231,75 @@ def msa_inputs(n_seq: int, n: int, seed: int = 0, c_m: int = 64, c_z: int = 128,
     msa_mask = (torch.rand(n_seq, n, generator=g) > row_dropout).float() * tokens
     msa_mask[0] = tokens
     return msa, z, msa_mask, tokens
+
+
+# ------------------------------------------------------------------------- diffusion transformer
+def dit_schema(c: int = 768, c_cond: int = 384, c_pair: int = 128, n_head: int = 16,
+               factor: int = 2) -> list[tuple[str, tuple[int, ...]]]:
+    """Engine keys and shapes of one AF3 token DiT block (``TokenDiT``: the converter's
+    ``legacy/released.py:372-509`` names): AdaLN + pair-biased attention, AdaLN + SwiGLU
+    transition, each output gated by the conditioning."""
+
+    def adaln(prefix: str) -> list[tuple[str, tuple[int, ...]]]:
+        return [(f"{prefix}.ln_cond.weight", (c_cond,)), (f"{prefix}.to_scale.weight", (c, c_cond)),
+                (f"{prefix}.to_scale.bias", (c,)), (f"{prefix}.to_bias.weight", (c, c_cond))]
+
+    return [
+        *adaln("attention.ada_ln_in"),
+        ("attention.to_query.weight", (c, c)), ("attention.to_query.bias", (c,)),
+        ("attention.to_key.weight", (c, c)), ("attention.to_value.weight", (c, c)),
+        ("attention.to_gate.weight", (c, c)),
+        ("attention.to_scale.weight", (c, c_cond)), ("attention.to_scale.bias", (c,)),
+        ("attention.to_out.weight", (c, c)),
+        ("attention.ln_pair.weight", (c_pair,)), ("attention.to_bias.weight", (n_head, c_pair)),
+        *adaln("transition.ada_ln_in"),
+        ("transition.expand_a.weight", (factor * c, c)), ("transition.expand_b.weight", (factor * c, c)),
+        ("transition.squeeze.weight", (c, factor * c)),
+        ("transition.to_scale.weight", (c, c_cond)), ("transition.to_scale.bias", (c,)),
+    ]
+
+
+def dit_state(generator: torch.Generator, scheme: str = "randomise", **dims: int) -> dict[str, Tensor]:
+    """One token DiT block's engine-key state (fp32) drawn in schema order from ``generator``:
+    ``baseline`` = N(0, 0.02) matrices, unit norm weights, zero biases; ``randomise`` =
+    N(0, 0.05) matrices, norm weights 1 + N(0, 0.1), biases N(0, 0.5) (so the sigmoid gates
+    are away from one half)."""
+    if scheme not in ("baseline", "randomise"):
+        raise ValueError(f"unknown weight scheme {scheme!r}")
+    state: dict[str, Tensor] = {}
+    for key, shape in dit_schema(**dims):
+        noise = torch.randn(shape, generator=generator, dtype=torch.float32)
+        norm = ".ln_" in key
+        if scheme == "baseline":
+            value = (torch.ones(shape) if norm else torch.zeros(shape)) if len(shape) == 1 else 0.02 * noise
+        elif len(shape) > 1:
+            value = 0.05 * noise
+        else:
+            value = 1.0 + 0.1 * noise if norm else 0.5 * noise
+        state[key] = value
+    return state
+
+
+def dit_inputs(samples: int, n: int, seed: int = 0, c: int = 768, c_cond: int = 384, c_pair: int = 128,
+               masked_suffix: int = 0) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+    """``(x [S, N, c], cond [N, c_cond], pair [N, N, c_pair], mask [N])`` from a generator seeded
+    ``seed``: token activations, single and pair conditioning ~ N(0, 1), the last
+    ``masked_suffix`` tokens padding."""
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(samples, n, c, generator=g)
+    cond = torch.randn(n, c_cond, generator=g)
+    pair = torch.randn(n, n, c_pair, generator=g)
+    mask = torch.ones(n)
+    if masked_suffix:
+        mask[n - masked_suffix:] = 0
+    return x, cond, pair, mask
+
+
+def dit_stack_state(n_blocks: int, seed: int = 0, scheme: str = "randomise") -> list[dict[str, Tensor]]:
+    """``n_blocks`` token DiT block states from one generator seeded ``seed``, every block with
+    block 0's pair norm (AF3's token transformer has one shared pair norm)."""
+    g = torch.Generator().manual_seed(seed)
+    blocks = [dit_state(g, scheme) for _ in range(n_blocks)]
+    for b in blocks[1:]:
+        b["attention.ln_pair.weight"] = blocks[0]["attention.ln_pair.weight"].clone()
+    return blocks

@@ -38,6 +38,8 @@ from foldforge_b200.synthetic import (  # noqa: E402
     evoformer_state,
     inputs,
     msa_inputs,
+    dit_inputs,
+    dit_stack_state,
 )
 
 
@@ -253,6 +255,77 @@ def run_evoformer_case(name: str, *, n_seq: int, n: int, masked: int, scheme: st
     print(f"{name}: S={n_seq} N={n} masked={masked} -> {HERE / (name + '.npz')}")
 
 
+def released_dit_from_engine(blocks: list[dict[str, torch.Tensor]], super_block_size: int) -> dict[str, torch.Tensor]:
+    """Engine keys of AF3 token DiT blocks -> the released ``DiffusionTransformer`` keys (the
+    inverse of ``token_dit_blocks_from_released``): one shared pair norm (every block's
+    ``ln_pair`` must be the same tensor values), the blocks' ``to_bias`` stacked per super block
+    into ``pair_logits_projection.<j>``, each block's attention / transition renamed."""
+    out: dict[str, torch.Tensor] = {"pair_input_layer_norm.weight": blocks[0]["attention.ln_pair.weight"]}
+    for j in range(len(blocks) // super_block_size):
+        out[f"pair_logits_projection.{j}.weight"] = torch.cat(
+            [blocks[j * super_block_size + t]["attention.to_bias.weight"] for t in range(super_block_size)], 0)
+
+    def adaln(dst: str, src: str, st: dict[str, torch.Tensor]) -> None:
+        out[f"{dst}.single_cond_layer_norm.weight"] = st[f"{src}.ln_cond.weight"]
+        out[f"{dst}.single_cond_scale.weight"] = st[f"{src}.to_scale.weight"]
+        out[f"{dst}.single_cond_scale.bias"] = st[f"{src}.to_scale.bias"]
+        out[f"{dst}.single_cond_bias.weight"] = st[f"{src}.to_bias.weight"]
+
+    for i, st in enumerate(blocks):
+        a, t = f"self_attention.{i}", f"transition_block.{i}"
+        adaln(f"{a}.adaptive_layernorm", "attention.ada_ln_in", st)
+        out[f"{a}.q_projection.weight"] = st["attention.to_query.weight"]
+        out[f"{a}.q_projection.bias"] = st["attention.to_query.bias"]
+        out[f"{a}.k_projection.weight"] = st["attention.to_key.weight"]
+        out[f"{a}.v_projection.weight"] = st["attention.to_value.weight"]
+        out[f"{a}.gating_query.weight"] = st["attention.to_gate.weight"]
+        out[f"{a}.adaptive_zero_init.transition2.weight"] = st["attention.to_out.weight"]
+        out[f"{a}.adaptive_zero_init.adaptive_zero_cond.weight"] = st["attention.to_scale.weight"]
+        out[f"{a}.adaptive_zero_init.adaptive_zero_cond.bias"] = st["attention.to_scale.bias"]
+        adaln(f"{t}.adaptive_layernorm", "transition.ada_ln_in", st)
+        out[f"{t}.transition1.weight"] = torch.cat([st["transition.expand_a.weight"], st["transition.expand_b.weight"]], 0)
+        out[f"{t}.adaptive_zero_init.transition2.weight"] = st["transition.squeeze.weight"]
+        out[f"{t}.adaptive_zero_init.adaptive_zero_cond.weight"] = st["transition.to_scale.weight"]
+        out[f"{t}.adaptive_zero_init.adaptive_zero_cond.bias"] = st["transition.to_scale.bias"]
+    return out
+
+
+def run_dit_case(name: str, *, samples: int, n: int, masked: int, n_blocks: int, super_block_size: int,
+                 scheme: str, wseed: int, iseed: int) -> None:
+    """The reference's released-layout token ``DiffusionTransformer`` with AF3's spec on seeded
+    engine-key weights (converter round trip checked bitwise) and seeded inputs."""
+    from foldforge.models.checkpoints.legacy.released import token_dit_blocks_from_released
+    from foldforge.models.checkpoints.legacy.transformer import DiffusionTransformer
+    from foldforge.modules.dense.spec import ALPHAFOLD3
+
+    blocks = dit_stack_state(n_blocks, wseed, scheme)
+    legacy = DiffusionTransformer(c_act=768, c_single_cond=384, c_pair_cond=128, num_head=16, num_blocks=n_blocks,
+                                  super_block_size=super_block_size, spec=ALPHAFOLD3).eval()
+    legacy.load_state_dict(released_dit_from_engine(blocks, super_block_size), strict=True)
+    back = token_dit_blocks_from_released(legacy.state_dict(), n_head=16, super_block_size=super_block_size)
+    assert len(back) == n_blocks
+    for got, want in zip(back, blocks, strict=True):
+        assert set(got) == set(want), sorted(set(got) ^ set(want))
+        for k, v in want.items():
+            assert torch.equal(got[k], v), k
+    x, cond, pair, mask = dit_inputs(samples, n, iseed, masked_suffix=masked)
+    with torch.no_grad():
+        pl = legacy.pair_logits_projection[0](legacy.pair_input_layer_norm(pair))
+        pl0 = pl.reshape(n, n, super_block_size, 16)[:, :, 0].permute(2, 0, 1)
+        att = legacy.self_attention[0](x, mask, pl0, cond)
+        tr = legacy.transition_block[0](x + att, cond)
+        out = legacy(x.clone(), mask, cond, pair)
+    record = {
+        "samples": np.array(samples), "n": np.array(n), "masked": np.array(masked), "n_blocks": np.array(n_blocks),
+        "scheme": np.array(scheme), "wseed": np.array(wseed), "iseed": np.array(iseed),
+        "weights_sha256": np.array(_digest({f"{i}.{k}": v for i, b in enumerate(blocks) for k, v in b.items()})),
+        "inputs_sha256": np.array(_digest({"x": x, "cond": cond, "pair": pair, "mask": mask})),
+        "op.attention0": att.numpy(), "op.transition0": tr.numpy(), "out": out.numpy(),
+    }
+    np.savez_compressed(HERE / f"{name}.npz", **record)
+    print(f"{name}: S={samples} N={n} masked={masked} blocks={n_blocks} -> {HERE / (name + '.npz')}")
+
+
 SMALL = BlockShape(c_z=32, c_s=64, hidden_mul=32, n_head_pair=4, d_tri=8, n_head_single=4, n_pair=4, n_single=4)
 AF3 = BlockShape()
 
@@ -281,6 +354,13 @@ def main() -> None:
     # and benchmark configuration 4's weight scheme at a small size
     run_evoformer_case("evo_s6_n20_masked3", n_seq=6, n=20, masked=3, scheme="randomise", wseed=8, iseed=9)
     run_evoformer_case("evo_s33_n40_baseline", n_seq=33, n=40, masked=2, scheme="baseline", wseed=10, iseed=11)
+    # the token diffusion transformer (AF3 widths: 768 / 16 heads, 384 conditioning, 128 pair):
+    # two samples over 24 tokens with 3 padded, and one sample over 40 tokens through a whole
+    # super block of four
+    run_dit_case("dit_s2_n24_masked3", samples=2, n=24, masked=3, n_blocks=2, super_block_size=2,
+                 scheme="randomise", wseed=12, iseed=13)
+    run_dit_case("dit_s1_n40_sb4", samples=1, n=40, masked=0, n_blocks=4, super_block_size=4,
+                 scheme="randomise", wseed=14, iseed=15)
 
 
 if __name__ == "__main__":

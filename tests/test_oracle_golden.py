@@ -19,7 +19,7 @@ import oracle
 from foldforge_b200.synthetic import BlockShape, block_state, inputs
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
-CASES = sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith("evo_"))  # Pairformer cases
+CASES = sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith(("evo_", "dit_")))  # Pairformer cases
 #: the reference's own fp32 parity tolerance (tests/models/test_engine_graph.py:27)
 TOL = {"rtol": 1e-4, "atol": 1e-4}
 
