@@ -66,6 +66,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-ladder", action="store_true", help="skip the N=2048 length-ladder measurement")
     ap.add_argument("--no-msa", action="store_true", help="skip the MSA-module measurement (configuration 4)")
+    ap.add_argument("--no-dit", action="store_true",
+                    help="skip the diffusion-transformer measurement (configuration 5's token transformer)")
     ap.add_argument("--eager-sharded", action="store_true",
                     help="with --gpus > 1: time eager launches instead of a captured CUDA graph of the sharded trunk")
     ap.add_argument("--breakdown", action="store_true",
@@ -378,6 +380,8 @@ def run_b200(args, rank: int, world: int, local: int, dist) -> None:
         if world == 1 and not args.no_msa:
             torch.cuda.empty_cache()
             line["msa_module"] = msa_module_single_gpu(dev)
+        if world == 1 and not args.no_dit:
+            line["token_dit"] = token_dit_single_gpu(dev)
         print(json.dumps(line), flush=True)
 
 
@@ -435,6 +439,67 @@ def msa_inputs_config4(dev: torch.device, n_seq: int = 1024, n: int = 512, seed:
     msa = (feats @ w.t()).bfloat16()
     z = torch.randn(n, n, 128, generator=g).bfloat16()
     return msa[None].to(dev), z[None].to(dev), torch.ones(1, n_seq, n, device=dev), torch.ones(1, n, n, device=dev)
+
+
+def token_dit_single_gpu(dev: torch.device, n_blocks: int = 24, samples: int = 5, n: int = 512) -> dict:
+    """BASELINE configuration 5's token diffusion transformer: 24 AF3 TokenDiT blocks (c 768, 16
+    heads, conditioning 384, pair 128) over 5 samples x N = 512 tokens, conditioned on fixed random
+    trunk outputs (s, z ~ N(0, 1)), b200 backend. A sampler step (one pass of the stack) is timed
+    as a CUDA-graph replay with the L2 flushed, 1 warm-up and 3 timed steps; the once-per-fold
+    conditioning tables (AdaLN, gates, pair logits of every block) are timed separately. The
+    atom encoder / decoder and the EDM update around the transformer are not part of this."""
+    from foldforge_b200.engine import backends, policy
+    from foldforge_b200.engine.capture import GraphedCall
+    from foldforge_b200.engine.dit import TokenDiT, TokenDiTStack
+    from foldforge_b200.synthetic import dit_inputs, dit_stack_state
+
+    blocks = []
+    for st in dit_stack_state(n_blocks, 0, "baseline"):
+        blk = TokenDiT()
+        blk.load_state_dict(st, strict=True)
+        blocks.append(blk)
+    stack = TokenDiTStack(blocks).to(dev).eval()
+    plan = backends.BackendPlan.make("b200", unsupported="error").resolve(dev)
+    policy.apply_plan(stack, plan, dev)
+    x, cond, pair, mask = dit_inputs(samples, n, 0)
+    x, cond, pair = x.bfloat16().to(dev), cond.bfloat16().to(dev), pair.bfloat16().to(dev)
+    mask = mask.to(dev) > 0
+    key_mask = mask[None]
+    with torch.no_grad():
+        stack(x, mask, cond, pair, key_mask=key_mask)  # weights packed, tables built
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for blk in stack.blocks:
+        blk.release_fold()
+        blk._conditioning(cond, pair, blk._pack(dev))
+    b.record()
+    torch.cuda.synchronize()
+    cond_ms = a.elapsed_time(b)
+    graphed = GraphedCall(lambda xx: stack(xx, mask, cond, pair, key_mask=key_mask), [x], warmup=1)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    graphed.replay()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(3):
+        flush.fill_(1.0)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        graphed.replay()
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    del graphed, stack
+    torch.cuda.empty_cache()
+    ms = sum(ts) / len(ts)
+    m = samples * n
+    per_block = 2.0 * m * 768 * (4 * 768 + 768 + 2 * 1536 + 1536) + 4.0 * samples * 16 * n * n * 48
+    return {"config": "BASELINE configuration 5, token transformer: 24 TokenDiT blocks (768, 16 heads), "
+                      f"{samples} samples x N={n}, bf16, conditioned on fixed s [512, 384], z [512, 512, 128]",
+            "ms_per_sampler_step": round(ms, 3), "ms_per_block": round(ms / n_blocks, 4),
+            "ms_per_200_steps": round(200 * ms, 1), "ms_conditioning_per_fold": round(cond_ms, 3),
+            "steps": 3, "warmup": 1, "tflops_approx": round(n_blocks * per_block / (ms * 1e-3) / 1e12, 1),
+            "parallelism": "single GPU (CUDA-graph replay)"}
 
 
 def msa_module_single_gpu(dev: torch.device, n_blocks: int = 4) -> dict:

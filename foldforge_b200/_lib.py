@@ -70,6 +70,14 @@ SIGNATURES: dict[str, list] = {
                              ctypes.c_size_t, c_int, c_int, c_void_p],
     "ffb_apb_shard_single_rows": [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p, ctypes.c_size_t,
                                   c_int, c_int, c_int, c_int, c_void_p],
+    # token diffusion transformer block
+    "ffb_dit_packed_bytes": [],
+    "ffb_dit_prepare": [c_void_p, c_void_p, c_void_p],
+    "ffb_dit_tables_bytes": [c_int],
+    "ffb_dit_condition_workspace_bytes": [c_int],
+    "ffb_dit_condition": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_size_t, c_int, c_void_p],
+    "ffb_dit_workspace_bytes": [c_int, c_int],
+    "ffb_dit_fwd": [c_void_p] * 6 + [ctypes.c_size_t, c_int, c_int, c_void_p],
     # row-shard exchanges over NVLink peer memory (CUDA IPC buffers)
     "ffb_p2p_handle_bytes": [],
     "ffb_p2p_alloc": [ctypes.c_size_t, ctypes.POINTER(c_void_p), c_void_p],
@@ -116,6 +124,7 @@ SIGNATURES: dict[str, list] = {
 SIZE_RESULT = {"ffb_apb_packed_bytes", "ffb_apb_workspace_bytes", "ffb_single_transition_packed_bytes",
                "ffb_single_transition_workspace_bytes", "ffb_transition_packed_bytes", "ffb_trimul_packed_bytes",
                "ffb_trimul_workspace_bytes", "ffb_triattn_packed_bytes", "ffb_triattn_workspace_bytes",
+               "ffb_dit_packed_bytes", "ffb_dit_tables_bytes", "ffb_dit_condition_workspace_bytes", "ffb_dit_workspace_bytes",
                "ffb_apb_single_workspace_bytes", "ffb_trimul_f32_workspace_bytes", "ffb_triattn_f32_workspace_bytes",
                "ffb_transition_f32_workspace_bytes", "ffb_apb_f32_workspace_bytes", "ffb_opm_packed_bytes",
                "ffb_opm_workspace_bytes", "ffb_pwa_packed_bytes", "ffb_pwa_workspace_bytes",
@@ -173,7 +182,7 @@ LAUNCHES = {
     "ffb_transition_fwd": 1, "ffb_apb_fwd": 5, "ffb_single_transition_fwd": 3,
     "ffb_trimul_shard_proj": 1, "ffb_trimul_shard_contract": 1, "ffb_trimul_shard_out": 1,
     "ffb_triattn_shard_proj": 1, "ffb_triattn_shard_attn": 1, "ffb_triattn_shard_out": 1,
-    "ffb_transition_shard_fwd": 1, "ffb_apb_shard_pair_bias": 1, "ffb_apb_shard_single": 4, "ffb_apb_shard_single_rows": 4,
+    "ffb_transition_shard_fwd": 1, "ffb_apb_shard_pair_bias": 1, "ffb_apb_shard_single": 4, "ffb_apb_shard_single_rows": 4, "ffb_dit_prepare": 17, "ffb_dit_condition": 6, "ffb_dit_fwd": 7,
     "ffb_single_transition_fwd_noalloc": 3,
     "ffb_shard_transpose_p2p": 1, "ffb_shard_gather_p2p": 1, "ffb_shard_wait_p2p": 1, "ffb_shard_rows_p2p": 1,
     "ffb_trimul_channel_contract": 1,

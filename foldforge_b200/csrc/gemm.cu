@@ -95,6 +95,12 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int b, int m
       acc[i] = x;
     }
   }
+  if (p.col_gate != nullptr) {
+    const float* gr = p.col_gate + static_cast<int64_t>(m % p.gate_rows) * p.N + n0;
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (n0 + i < p.N) acc[i] *= 1.0f / (1.0f + __expf(-gr[i]));
+  }
   float rowscale = 1.0f;
   if (p.row_mask != nullptr) rowscale = p.row_mask[static_cast<int64_t>(b) * p.M + m] ? 1.0f : 0.0f;
   if (p.row_scale != nullptr) {

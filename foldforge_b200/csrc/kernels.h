@@ -26,6 +26,9 @@ struct GemmParams {
   int* err;
   int tma_store;  // set by launch_gemm_nt: the bf16 store epilogue goes through TMA stores
   const float* row_scale = nullptr;  // (acc + bias) times row_scale[m] (store and residual epilogues)
+  // residual epilogue only: acc times sigmoid(col_gate[(m % gate_rows) * N + n]) before the add
+  const float* col_gate = nullptr;
+  int gate_rows = 0;
 };
 
 size_t gemm_smem_bytes(int bn);
@@ -103,6 +106,11 @@ int apb_forward(const void* s, const void* z, const uint8_t* mask, const void* p
                 const DeviceInfo& info, cudaStream_t stream);
 int apb_shard_pair_bias(const void* z, const void* packed, void* pb_rows, int R, int N, const DeviceInfo& info,
                         cudaStream_t stream);
+// The 16-head pair bias pb[h * pb_h + row * pb_r + col] = W'[h] . z[pair] - folded LayerNorm,
+// for the `rows` x N pairs of z (bf16, 128 channels), from a weight image w_img (the SW128
+// image of W diag(gamma), 16 rows x 128) and its row sums wsum.
+int pair_bias16(const void* z, const uint8_t* w_img, const float* wsum, float* pb, int64_t rows, int N, int64_t pb_h,
+                int64_t pb_r, const DeviceInfo& info, cudaStream_t stream);
 size_t apb_single_workspace_bytes(int N);
 int apb_shard_single_rows(const void* s, const uint8_t* mask, const void* packed, const void* pb_rows, float gate_bias,
                           void* out_rows, void* workspace, int N, int row0, int R, int masked_zero,

@@ -541,6 +541,14 @@ namespace {
 int launch_pair_bias(const void* z, const uint8_t* img, float* pb, int64_t rows, int N, int64_t pb_h, int64_t pb_r,
                      const DeviceInfo& info, cudaStream_t stream) {
   const ApbLayout L = apb_layout();
+  return pair_bias16(z, img + L.w_pb, reinterpret_cast<const float*>(img + L.pb_wsum), pb, rows, N, pb_h, pb_r, info,
+                     stream);
+}
+
+}  // namespace
+
+int pair_bias16(const void* z, const uint8_t* w_img, const float* wsum, float* pb, int64_t rows, int N, int64_t pb_h,
+                int64_t pb_r, const DeviceInfo& info, cudaStream_t stream) {
   const size_t P = static_cast<size_t>(rows) * N;
   if (P >= (static_cast<size_t>(1) << 31))
     return fail(FFB_ERR_UNSUPPORTED, "attention_pair_bias: %zu pairs exceed the 2^31 TMA row range", P);
@@ -554,10 +562,12 @@ int launch_pair_bias(const void* z, const uint8_t* img, float* pb, int64_t rows,
   const int grid = static_cast<int>(tiles < 2 * info.num_sms ? tiles : 2 * info.num_sms);
   const size_t smem = sizeof(PbSmem) + 1024;
   cudaFuncSetAttribute(pair_bias_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  pair_bias_kernel<<<grid, kPbThreads, smem, stream>>>(mz, img + L.w_pb, reinterpret_cast<const float*>(img + L.pb_wsum),
-                                                       pb, static_cast<int64_t>(P), N, pb_h, pb_r, info.err);
+  pair_bias_kernel<<<grid, kPbThreads, smem, stream>>>(mz, w_img, wsum, pb, static_cast<int64_t>(P), N, pb_h, pb_r,
+                                                       info.err);
   return cuda_status(static_cast<int>(cudaGetLastError()), "pair bias launch");
 }
+
+namespace {
 
 // the single track of attention with pair bias, given the pair bias (strides pb_h, pb_r)
 int launch_single_attention(const void* s, const uint8_t* mask, const uint8_t* img, const float* pb, int64_t pb_h,

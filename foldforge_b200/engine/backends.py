@@ -49,7 +49,7 @@ OP_CLASSES: dict[str, tuple[str, ...]] = {
     "transition": ("Transition",),
     "layernorm": ("LayerNorm",),
     "conditioning": (),
-    "dit_blocks": (),
+    "dit_blocks": ("TokenDiT",),
     "atom_blocks": (),
     "sampler_ops": (),
 }
@@ -66,18 +66,29 @@ class BackendUnsupportedError(RuntimeError):
     """A (backend, module) combination nothing serves, with ``engine.unsupported: error``."""
 
 
+#: modules of this package that define op classes
+CLASS_MODULES = ("foldforge_b200.engine.modules", "foldforge_b200.engine.dit")
+
+
 def op_classes(op: str) -> tuple[type, ...]:
     """The classes of this package that carry ``op`` (an op without any gives ``()``)."""
-    from foldforge_b200.engine import modules
+    import importlib
 
-    return tuple(cls for cls in (getattr(modules, name, None) for name in OP_CLASSES[op]) if cls is not None)
+    found = []
+    for name in OP_CLASSES[op]:
+        for mod in CLASS_MODULES:
+            cls = getattr(importlib.import_module(mod), name, None)
+            if cls is not None:
+                found.append(cls)
+                break
+    return tuple(found)
 
 
 def op_of(module: object) -> str | None:
     """The op an engine module carries: the first class on its MRO that the table names."""
     for cls in type(module).__mro__:
         op = _OP_OF_CLASS.get(cls.__name__)
-        if op is not None and cls.__module__ == "foldforge_b200.engine.modules":
+        if op is not None and cls.__module__ in CLASS_MODULES:
             return op
     return None
 

@@ -442,3 +442,61 @@ def transition_gemm(x: Tensor, packed: Tensor, c: int, n: int) -> Tensor:
     _lib.call("ffb_transition_gemm_fwd", _ptr(x), _ptr(packed), _ptr(out), _ptr(ws), ctypes.c_size_t(ws.numel()),
               ctypes.c_int64(rows), c, n, _stream())
     return out
+
+
+# --------------------------------------------------------------------------- diffusion transformer
+#: the 23 weights of a token DiT block in the order ``ffb_dit_prepare`` takes them
+DIT_WEIGHTS = (
+    "attention.ada_ln_in.ln_cond.weight", "attention.ada_ln_in.to_scale.weight", "attention.ada_ln_in.to_scale.bias",
+    "attention.ada_ln_in.to_bias.weight", "attention.to_query.weight", "attention.to_query.bias",
+    "attention.to_key.weight", "attention.to_value.weight", "attention.to_gate.weight", "attention.to_scale.weight",
+    "attention.to_scale.bias", "attention.to_out.weight", "attention.ln_pair.weight", "attention.to_bias.weight",
+    "transition.ada_ln_in.ln_cond.weight", "transition.ada_ln_in.to_scale.weight",
+    "transition.ada_ln_in.to_scale.bias", "transition.ada_ln_in.to_bias.weight", "transition.expand_a.weight",
+    "transition.expand_b.weight", "transition.squeeze.weight", "transition.to_scale.weight",
+    "transition.to_scale.bias",
+)
+
+
+def dit_prepare(weights: dict[str, Tensor], device: torch.device) -> Tensor:
+    """The packed image of one token DiT block (AF3 widths) from its fp32 engine-key weights."""
+    lib = _lib.load()
+    ptrs, keep = _weight_ptrs(weights, DIT_WEIGHTS, device)
+    packed = torch.empty(int(lib.ffb_dit_packed_bytes()), dtype=torch.uint8, device=device)
+    _lib.call("ffb_dit_prepare", ptrs, _ptr(packed), _stream())
+    del keep
+    return packed
+
+
+def dit_condition(cond: Tensor, pair: Tensor, packed: Tensor) -> Tensor:
+    """The block's per-fold tables (AdaLN scale / shift, output gates, pair logits) from
+    ``cond [L, 384]`` and ``pair [L, L, 128]`` (bf16)."""
+    _need_cuda(cond, pair, packed)
+    if cond.dtype != torch.bfloat16 or pair.dtype != torch.bfloat16:
+        raise _lib.UnsupportedCall("ffb_dit_condition", 2, f"bf16 conditioning, got {cond.dtype} / {pair.dtype}")
+    cond, pair = cond.contiguous(), pair.contiguous()
+    n = cond.shape[0]
+    lib = _lib.load()
+    tables = torch.empty(int(lib.ffb_dit_tables_bytes(n)), dtype=torch.uint8, device=cond.device)
+    ws = _workspace(lib.ffb_dit_condition_workspace_bytes(n), cond.device)
+    _lib.call("ffb_dit_condition", _ptr(cond), _ptr(pair), _ptr(packed), _ptr(tables), _ptr(ws),
+              ctypes.c_size_t(ws.numel()), n, _stream())
+    return tables
+
+
+def dit_forward(x: Tensor, mask: Tensor, packed: Tensor, tables: Tensor, *, workspace: Tensor | None = None,
+                out: Tensor | None = None) -> Tensor:
+    """One token DiT block on ``x [S, L, 768]`` (bf16) with the fold's tables; ``mask [L]``."""
+    _need_cuda(x, mask, packed, tables)
+    if x.dtype != torch.bfloat16:
+        raise _lib.UnsupportedCall("ffb_dit_fwd", 2, f"bf16 activations, got {x.dtype}")
+    x = x.contiguous()
+    s, n = x.shape[0], x.shape[1]
+    lib = _lib.load()
+    if workspace is None:
+        workspace = _workspace(lib.ffb_dit_workspace_bytes(s, n), x.device)
+    if out is None:
+        out = torch.empty_like(x)
+    _lib.call("ffb_dit_fwd", _ptr(x), _ptr(_mask_u8(mask)), _ptr(packed), _ptr(tables), _ptr(out), _ptr(workspace),
+              ctypes.c_size_t(workspace.numel()), s, n, _stream())
+    return out

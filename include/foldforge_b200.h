@@ -324,6 +324,30 @@ int ffb_transition_gemm_prepare(const float* ln_w, const float* ln_b, const floa
 int ffb_transition_gemm_fwd(const void* x, const void* packed, void* out, void* workspace, size_t workspace_bytes,
                             int64_t rows, int c, int n, void* stream);
 
+/* ---- Token diffusion transformer block (AF3 TokenDiT: c = 768, 16 heads x 48, conditioning
+ * 384, pair 128, SwiGLU factor 2; replaces the engine TokenDiT block of
+ * src/foldforge/modules/engine/transformers.py:31-125, algorithm legacy/transformer.py:28-294).
+ * bf16 activations. Per block: ffb_dit_prepare packs the 23 fp32 weights, given as a HOST
+ * array of device pointers in the engine schema's order: attention.ada_ln_in.{ln_cond.weight,
+ * to_scale.weight, to_scale.bias, to_bias.weight}, attention.{to_query.weight, to_query.bias,
+ * to_key.weight, to_value.weight, to_gate.weight, to_scale.weight, to_scale.bias,
+ * to_out.weight, ln_pair.weight, to_bias.weight}, transition.ada_ln_in.{ln_cond.weight,
+ * to_scale.weight, to_scale.bias, to_bias.weight}, transition.{expand_a.weight,
+ * expand_b.weight, squeeze.weight, to_scale.weight, to_scale.bias}. Per fold (a fixed
+ * conditioning): ffb_dit_condition fills the block's tables (ffb_dit_tables_bytes(L)) from
+ * cond [L][384] and pair [L][L][128] (bf16): AdaLN scale / shift, output gates, pair logits.
+ * Per sampler step: ffb_dit_fwd maps x [S][L][768] to out = the block's output (out must not
+ * alias x); mask [L] (uint8, 0 = padding: keys masked with the replaced logit -1e9). */
+size_t ffb_dit_packed_bytes(void);
+int ffb_dit_prepare(const float* const* weights, void* packed, void* stream);
+size_t ffb_dit_tables_bytes(int L);
+size_t ffb_dit_condition_workspace_bytes(int L);
+int ffb_dit_condition(const void* cond, const void* pair, const void* packed, void* tables, void* workspace,
+                      size_t workspace_bytes, int L, void* stream);
+size_t ffb_dit_workspace_bytes(int S, int L);
+int ffb_dit_fwd(const void* x, const uint8_t* mask, const void* packed, const void* tables, void* out, void* workspace,
+                size_t workspace_bytes, int S, int L, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -44,7 +44,7 @@ def test_serves_is_derived_from_the_classes():
     for op in ("trimul", "triangle_attention", "single_attention", "transition", "layernorm"):
         assert table[op] == ("miniworld", "pytorch", "b200")
     assert table["opm"] == ("miniworld", "pytorch", "b200")
-    assert table["dit_blocks"] == ()
+    assert table["dit_blocks"] == ("miniworld", "pytorch", "b200")  # TokenDiT (engine/dit.py)
 
 
 def test_choose_backend(monkeypatch):
