@@ -10,12 +10,13 @@
 //
 // Everything that reads only the conditioning is the same at every sampler step of a fold,
 // so it is computed once per fold (ffb_dit_condition): the two AdaLN scale / shift tables, the
-// two output-gate tables ([L][768] each, the gates as logits) and the pair logits [16][L][L]
-// (the pair-bias kernel of the single track with this block's weights). A step
-// (ffb_dit_fwd) is then seven launches on x [S][L][768]: the AdaLN kernel, the [q|k|v|g]
-// GEMM, the attention kernel (gated output), the output GEMM whose epilogue applies the gate
-// table and the residual, the second AdaLN, the SwiGLU GEMM, and the squeeze GEMM with the
-// second gate and residual. GEMMs are the library's tcgen05 GEMM.
+// two output-gate tables ([L][768] each, the gates as logits) and the pair logits [16][L][Lp]
+// (the pair-bias kernel of the single track with this block's weights; Lp = L rounded up to
+// 8). A step (ffb_dit_fwd) on x [S][L][768] is: the AdaLN kernel, the [q|k|v|g] GEMM, the
+// attention (Q K^T batched over samples x heads, the softmax kernel with the pair logits and
+// the key mask, V transposed, P V batched likewise, the gate kernel), the output GEMM whose
+// epilogue applies the gate table and the residual, the second AdaLN, the SwiGLU GEMM, and the
+// squeeze GEMM with the second gate and residual. GEMMs are the library's tcgen05 GEMM.
 #include "../../include/foldforge_b200.h"
 #include "abi_util.h"
 #include "common.cuh"
@@ -145,185 +146,125 @@ __global__ void __launch_bounds__(kLnWarps * 32) dit_adaln_kernel(const __nv_bfl
   }
 }
 
-// ---------------------------------------------------------------- attention
-// A CTA per (sample, head, 32 queries), 8 warps; lane = query, warp w takes keys w * 8 .. +7
-// of every staged 64-key chunk (keys and values as fp32, the pair-logit tile [32 q][64 k]
-// with a padded pitch). Each warp keeps an exact online softmax per query; the eight states
-// merge at the end. Masked keys take the REPLACED logit -1e9 (a query whose keys are all
-// masked averages uniformly), keys past L do not exist. The output is sigmoid(g) * o.
-constexpr int kAQ = 32;
-constexpr int kAK = 64;
-constexpr int kAWarps = 8;
-constexpr int kAThreads = kAQ * kAWarps;
-constexpr int kAPitch = kAK + 1;
-constexpr int kAStageFloats = 2 * kAK * kD + kAQ * kAPitch + kAK;
-constexpr int kAMergeFloats = kAWarps * kAQ * (kD + 2);
-constexpr int kASmemFloats = kAStageFloats > kAMergeFloats ? kAStageFloats : kAMergeFloats;
-static_assert(kAK * 12 == 3 * kAThreads && kD == 6 * 8, "K / V staging: three 16-byte vectors per thread");
-static_assert(kAQ * kAK / 4 == 2 * kAThreads, "bias staging: two float4 per thread");
+// ---------------------------------------------------------------- attention on the tensor cores
+// For each sample: S[h] = Q_h K_h^T (a tcgen05 GEMM batched over the 16 heads, straight from the
+// [q|k|v|g] rows; K = 48 zero-filled to 64 by TMA), then one warp per row (s, h, i) takes
+// x_j = S[i][j] / sqrt(48) + P_h[i][j] (masked keys REPLACED by -1e9), the softmax in fp32,
+// and writes the normalised row as bf16 (keys past L: 0), then O_h = P_h V_h (a second
+// batched GEMM, V transposed to [48][Lp] first) lands in the [token][768] layout, and the gate
+// kernel multiplies by sigmoid(g). Rows of keys are padded to Lp (a multiple of 8) for TMA.
+// One warp per row; rows of up to kSmKeys keys are held in registers, four keys per lane per
+// step read as 16-byte vectors (S and the pair-logit rows have Lp columns, a multiple of 8, so
+// rows are 32-byte aligned); longer rows take three passes over global memory.
+constexpr int kSmKeys = 1024;
 
-__global__ void __launch_bounds__(kAThreads) dit_attention_kernel(const __nv_bfloat16* __restrict__ qkvg,
-                                                                  const float* __restrict__ logits,
-                                                                  const uint8_t* __restrict__ mask,
-                                                                  __nv_bfloat16* __restrict__ out, int L) {
-  extern __shared__ float sm[];
-  float* ks = sm;
-  float* vs = ks + kAK * kD;
-  float* bias = vs + kAK * kD;
-  float* keep = bias + kAQ * kAPitch;
-  const int qblocks = (L + kAQ - 1) / kAQ;
-  const int h = blockIdx.x % kH;
-  const int qb = (blockIdx.x / kH) % qblocks;
-  const int s = blockIdx.x / (kH * qblocks);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int i = qb * kAQ + lane;
-  const int qrow = i < L ? i : L - 1;
-  const __nv_bfloat16* base = qkvg + static_cast<int64_t>(s) * L * (4 * kC);
-  const __nv_bfloat16* row_i = base + static_cast<int64_t>(qrow) * (4 * kC);
-  float q[kD];
+__global__ void __launch_bounds__(256) dit_softmax_kernel(const float* __restrict__ S, const float* __restrict__ logits,
+                                                          const uint8_t* __restrict__ mask, __nv_bfloat16* __restrict__ P,
+                                                          int64_t rows, int L, int Lp) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int i = static_cast<int>(r % L);
+  const int h = static_cast<int>((r / L) % kH);
+  const float* srow = S + r * Lp;
+  const float* brow = logits + (static_cast<int64_t>(h) * L + i) * Lp;
+  __nv_bfloat16* prow = P + r * Lp;
   const float scale = rsqrtf(static_cast<float>(kD));
+  if (Lp <= kSmKeys) {
+    constexpr int kSteps = kSmKeys / 128;
+    float x[kSteps][4];
+    float m = -INFINITY;
 #pragma unroll
-  for (int u = 0; u < kD / 8; ++u) {
-    const uint4 w4 = *reinterpret_cast<const uint4*>(row_i + h * kD + 8 * u);
-    const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
+    for (int t = 0; t < kSteps; ++t) {
+      const int j0 = 4 * lane + 128 * t;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      q[8 * u + 2 * e] = bf16_lo(w[e]) * scale;
-      q[8 * u + 2 * e + 1] = bf16_hi(w[e]) * scale;
-    }
-  }
-  float m = -INFINITY, l = 0.f, o[kD];
-#pragma unroll
-  for (int d = 0; d < kD; ++d) o[d] = 0.f;
-  const float* lg = logits + static_cast<int64_t>(h) * L * L;
-  for (int k0 = 0; k0 < L; k0 += kAK) {
-    const int nk = L - k0 < kAK ? L - k0 : kAK;
-    __syncthreads();  // the previous chunk's reads are done
-    // keys and values: 16-byte vector e of 12 per key (0-5 key, 6-11 value), 8 channels each
-#pragma unroll
-    for (int u = 0; u < 3; ++u) {
-      const int e = threadIdx.x + u * kAThreads;  // < 64 keys x 12 vectors = 3 x 256
-      const int j = e / 12, part = e % 12;
-      float* dst = (part < 6 ? ks : vs) + j * kD + (part % 6) * 8;
-      float f[8];
-      if (j < nk) {
-        const uint4 a = *reinterpret_cast<const uint4*>(base + static_cast<int64_t>(k0 + j) * (4 * kC) +
-                                                        (part < 6 ? kC : 2 * kC) + h * kD + (part % 6) * 8);
-        const uint32_t w[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          f[2 * t] = bf16_lo(w[t]);
-          f[2 * t + 1] = bf16_hi(w[t]);
+      for (int e = 0; e < 4; ++e) x[t][e] = -INFINITY;
+      if (j0 < Lp) {
+        const float4 sv = *reinterpret_cast<const float4*>(srow + j0);
+        const float4 bv = *reinterpret_cast<const float4*>(brow + j0);
+        const float sa[4] = {sv.x, sv.y, sv.z, sv.w}, ba[4] = {bv.x, bv.y, bv.z, bv.w};
+        uint32_t mk;
+        if (j0 + 4 <= L && (reinterpret_cast<uintptr_t>(mask + j0) & 3u) == 0) {
+          mk = *reinterpret_cast<const uint32_t*>(mask + j0);
+        } else {
+          mk = 0;
+          for (int e = 0; e < 4; ++e)
+            if (j0 + e < L && mask[j0 + e]) mk |= 1u << (8 * e);
         }
-      } else {
 #pragma unroll
-        for (int t = 0; t < 8; ++t) f[t] = 0.f;
-      }
-      *reinterpret_cast<float4*>(dst) = make_float4(f[0], f[1], f[2], f[3]);
-      *reinterpret_cast<float4*>(dst + 4) = make_float4(f[4], f[5], f[6], f[7]);
-    }
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int e = threadIdx.x + u * kAThreads;
-      const int qq = e / (kAK / 4), j = (e % (kAK / 4)) * 4;
-      const int ii = qb * kAQ + qq;
-      float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (ii < L) {
-        const float* src = lg + static_cast<int64_t>(ii) * L + k0 + j;
-        float t[4];
-        for (int c = 0; c < 4; ++c) t[c] = (j + c < nk) ? src[c] : 0.f;
-        b4 = make_float4(t[0], t[1], t[2], t[3]);
-      }
-      float* dst = bias + qq * kAPitch + j;
-      dst[0] = b4.x;
-      dst[1] = b4.y;
-      dst[2] = b4.z;
-      dst[3] = b4.w;
-    }
-    if (threadIdx.x < kAK) keep[threadIdx.x] = threadIdx.x < nk ? (mask[k0 + threadIdx.x] ? 1.f : 0.f) : -1.f;
-    __syncthreads();
-    float x[kAK / kAWarps];
-    float mx = -INFINITY;
-#pragma unroll
-    for (int jj = 0; jj < kAK / kAWarps; ++jj) {
-      const int j = warp * (kAK / kAWarps) + jj;
-      const float4* kr = reinterpret_cast<const float4*>(ks + j * kD);
-      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-#pragma unroll
-      for (int u = 0; u < kD / 4; ++u) {
-        const float4 kk = kr[u];
-        a0 = fmaf(q[4 * u], kk.x, a0);
-        a1 = fmaf(q[4 * u + 1], kk.y, a1);
-        a2 = fmaf(q[4 * u + 2], kk.z, a2);
-        a3 = fmaf(q[4 * u + 3], kk.w, a3);
-      }
-      const float kp = keep[j];
-      float xv = (a0 + a1) + (a2 + a3) + bias[lane * kAPitch + j];
-      if (kp == 0.f) xv = -1.0e9f;
-      if (kp < 0.f) xv = -INFINITY;
-      x[jj] = xv;
-      mx = fmaxf(mx, xv);
-    }
-    const float m_new = fmaxf(m, mx);
-    if (m_new > -INFINITY) {
-      const float alpha = __expf(m - m_new);
-      l *= alpha;
-#pragma unroll
-      for (int d = 0; d < kD; ++d) o[d] *= alpha;
-#pragma unroll
-      for (int jj = 0; jj < kAK / kAWarps; ++jj) {
-        const int j = warp * (kAK / kAWarps) + jj;
-        const float p = __expf(x[jj] - m_new);
-        l += p;
-        const float4* vr = reinterpret_cast<const float4*>(vs + j * kD);
-#pragma unroll
-        for (int u = 0; u < kD / 4; ++u) {
-          const float4 vv = vr[u];
-          o[4 * u] = fmaf(p, vv.x, o[4 * u]);
-          o[4 * u + 1] = fmaf(p, vv.y, o[4 * u + 1]);
-          o[4 * u + 2] = fmaf(p, vv.z, o[4 * u + 2]);
-          o[4 * u + 3] = fmaf(p, vv.w, o[4 * u + 3]);
+        for (int e = 0; e < 4; ++e) {
+          if (j0 + e < L) x[t][e] = ((mk >> (8 * e)) & 0xFFu) ? fmaf(sa[e], scale, ba[e]) : -1.0e9f;
+          m = fmaxf(m, x[t][e]);
         }
       }
-      m = m_new;
     }
-  }
-  __syncthreads();  // every chunk read is done: the merge scratch aliases the staging buffer
-  float* part = sm + (warp * kAQ + lane) * (kD + 2);
 #pragma unroll
-  for (int d = 0; d < kD; ++d) part[d] = o[d];
-  part[kD] = m;
-  part[kD + 1] = l;
-  __syncthreads();
-  if (warp != 0 || i >= L) return;
-  float mm = -INFINITY;
-  for (int w = 0; w < kAWarps; ++w) mm = fmaxf(mm, sm[(w * kAQ + lane) * (kD + 2) + kD]);
-  float ll = 0.f, acc[kD];
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    float sum = 0.f;
 #pragma unroll
-  for (int d = 0; d < kD; ++d) acc[d] = 0.f;
-  for (int w = 0; w < kAWarps; ++w) {
-    const float* pw = sm + (w * kAQ + lane) * (kD + 2);
-    if (pw[kD + 1] <= 0.f) continue;
-    const float f = __expf(pw[kD] - mm);
-    ll += pw[kD + 1] * f;
+    for (int t = 0; t < kSteps; ++t)
 #pragma unroll
-    for (int d = 0; d < kD; ++d) acc[d] = fmaf(pw[d], f, acc[d]);
-  }
-  const float inv = 1.0f / ll;
-  const __nv_bfloat16* gate = row_i + 3 * kC + h * kD;
-  __nv_bfloat16* dst = out + (static_cast<int64_t>(s) * L + i) * kC + h * kD;
+      for (int e = 0; e < 4; ++e) {
+        x[t][e] = __expf(x[t][e] - m);  // keys past L: exp(-inf) = 0
+        sum += x[t][e];
+      }
 #pragma unroll
-  for (int u = 0; u < kD / 8; ++u) {
-    const uint4 g4 = reinterpret_cast<const uint4*>(gate)[u];
-    const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w};
-    uint32_t ov[4];
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+    const float inv = 1.0f / sum;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int d = 8 * u + 2 * e;
-      ov[e] = pack_bf16(acc[d] * inv / (1.0f + __expf(-bf16_lo(gw[e]))),
-                        acc[d + 1] * inv / (1.0f + __expf(-bf16_hi(gw[e]))));
+    for (int t = 0; t < kSteps; ++t) {
+      const int j0 = 4 * lane + 128 * t;
+      if (j0 < Lp)
+        *reinterpret_cast<uint2*>(prow + j0) =
+            make_uint2(pack_bf16(x[t][0] * inv, x[t][1] * inv), pack_bf16(x[t][2] * inv, x[t][3] * inv));
     }
-    reinterpret_cast<uint4*>(dst)[u] = make_uint4(ov[0], ov[1], ov[2], ov[3]);
+    return;
+  }
+  auto logit = [&](int j) { return mask[j] ? fmaf(srow[j], scale, brow[j]) : -1.0e9f; };
+  float m = -INFINITY;
+  for (int j = lane; j < L; j += 32) m = fmaxf(m, logit(j));
+#pragma unroll
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+  float sum = 0.f;
+  for (int j = lane; j < L; j += 32) sum += __expf(logit(j) - m);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+  const float inv = 1.0f / sum;
+  for (int j = lane; j < Lp; j += 32) prow[j] = __float2bfloat16_rn(j < L ? __expf(logit(j) - m) * inv : 0.f);
+}
+
+// VT[s][h][d][j] = v[s L + j][h 48 + d] (keys j >= L: 0)
+__global__ void dit_vt_kernel(const __nv_bfloat16* __restrict__ qkvg, __nv_bfloat16* __restrict__ vt, int S, int L,
+                              int Lp) {
+  const int64_t total = static_cast<int64_t>(S) * kH * kD * Lp;
+  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int j = static_cast<int>(e % Lp);
+    const int64_t rest = e / Lp;
+    const int d = static_cast<int>(rest % kD);
+    const int h = static_cast<int>((rest / kD) % kH);
+    const int s = static_cast<int>(rest / (kD * kH));
+    vt[e] = j < L ? qkvg[(static_cast<int64_t>(s) * L + j) * (4 * kC) + 2 * kC + h * kD + d] : __float2bfloat16_rn(0.f);
+  }
+}
+
+// o[r][c] *= sigmoid(g[r][c]), g = qkvg[r][3 * 768 + c]; 8 channels per thread
+__global__ void dit_gate_kernel(__nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ qkvg, int64_t rows) {
+  const int64_t total = rows * (kC / 8);
+  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = e / (kC / 8);
+    const int c8 = static_cast<int>(e % (kC / 8));
+    uint4* op = reinterpret_cast<uint4*>(o + r * kC) + c8;
+    const uint4 ov = *op;
+    const uint4 gv = *(reinterpret_cast<const uint4*>(qkvg + r * (4 * kC) + 3 * kC) + c8);
+    const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w}, gw[4] = {gv.x, gv.y, gv.z, gv.w};
+    uint32_t res[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      res[k] = pack_bf16(bf16_lo(ow[k]) / (1.0f + __expf(-bf16_lo(gw[k]))),
+                         bf16_hi(ow[k]) / (1.0f + __expf(-bf16_hi(gw[k]))));
+    *op = make_uint4(res[0], res[1], res[2], res[3]);
   }
 }
 
@@ -334,9 +275,11 @@ struct DitTables {
   float *ada1, *ada2, *gate1, *gate2, *logits;
 };
 
+int pad8(int x) { return (x + 7) / 8 * 8; }
+
 size_t tables_bytes(int L) {
   const size_t l = static_cast<size_t>(L);
-  return 2 * a256(l * 2 * kC * 4) + 2 * a256(l * kC * 4) + a256(static_cast<size_t>(kH) * l * l * 4);
+  return 2 * a256(l * 2 * kC * 4) + 2 * a256(l * kC * 4) + a256(static_cast<size_t>(kH) * l * pad8(L) * 4);
 }
 
 DitTables carve_tables(void* base, int L) {
@@ -355,7 +298,9 @@ size_t condition_workspace_bytes(int L) { return a256(static_cast<size_t>(L) * k
 
 size_t forward_workspace_bytes(int S, int L) {
   const size_t m = static_cast<size_t>(S) * L;
-  return a256(m * kC * 2) + a256(m * 4 * kC * 2);
+  const size_t sl = static_cast<size_t>(S) * kH * L * pad8(L);
+  return a256(m * kC * 2) + a256(m * 4 * kC * 2) + a256(sl * 4) + a256(sl * 2) +
+         a256(static_cast<size_t>(S) * kH * kD * pad8(L) * 2);
 }
 
 // D[m][n] = A[m][:] . W[n][:] on the tcgen05 GEMM (A, W bf16 K-major); the residual epilogue
@@ -392,6 +337,47 @@ int dgemm(const void* a, const void* w, void* d, int m, int n, int k, int d_f32,
   p.col_gate = gate;
   p.gate_rows = gate_rows;
   return cuda_status(launch_gemm_nt(ma, mb, p, bn, info.num_sms, stream), "diffusion transformer gemm");
+}
+
+// D[s][h][m][n] = A[s][h][m][:] . W[s][h][n][:] for `heads` x `samples` batches (bf16 operands
+// with element strides: rows ld, heads hs, samples ss; K zero-filled past k to the 64-wide K
+// block by TMA); D's batch offset is h * d_hs + s * d_ss
+int bgemm(const void* a, int64_t a_ld, int64_t a_hs, int64_t a_ss, const void* w, int64_t w_ld, int64_t w_hs,
+          int64_t w_ss, void* d, int64_t ldd, int64_t d_hs, int64_t d_ss, int m, int n, int k, int heads, int samples,
+          int d_f32, const DeviceInfo& info, cudaStream_t stream) {
+  const int bn = n >= 256 ? 256 : 128;
+  CUtensorMap ma, mb;
+  const uint64_t adims[4] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m), static_cast<uint64_t>(heads),
+                             static_cast<uint64_t>(samples)};
+  const uint64_t astr[3] = {static_cast<uint64_t>(a_ld) * 2, static_cast<uint64_t>(a_hs) * 2,
+                            static_cast<uint64_t>(a_ss) * 2};
+  const uint32_t abox[4] = {64, 128, 1, 1};
+  int st = make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, a, adims, astr, abox, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st) return st;
+  const uint64_t bdims[4] = {static_cast<uint64_t>(k), static_cast<uint64_t>(n), static_cast<uint64_t>(heads),
+                             static_cast<uint64_t>(samples)};
+  const uint64_t bstr[3] = {static_cast<uint64_t>(w_ld) * 2, static_cast<uint64_t>(w_hs) * 2,
+                            static_cast<uint64_t>(w_ss) * 2};
+  const uint32_t bbox[4] = {64, static_cast<uint32_t>(bn), 1, 1};
+  st = make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, w, bdims, bstr, bbox, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st) return st;
+  GemmParams p;
+  p.M = m;
+  p.N = n;
+  p.K = k;
+  p.batch = heads * samples;
+  p.D = d;
+  p.ldd = ldd;
+  p.batch_stride_d = d_hs;
+  p.d_is_f32 = d_f32;
+  p.epilogue = kEpiStore;
+  p.bias = nullptr;
+  p.residual = nullptr;
+  p.row_mask = nullptr;
+  p.err = info.err;
+  p.batch_inner = heads;
+  p.batch_stride_d2 = d_ss;
+  return cuda_status(launch_gemm_nt(ma, mb, p, bn, info.num_sms, stream), "diffusion transformer attention gemm");
 }
 
 int adaln(const void* x, const float* tab, void* y, int64_t rows, int L, cudaStream_t stream) {
@@ -459,8 +445,9 @@ int dit_condition(const void* cond, const void* pair, const void* packed, void* 
   st = dgemm(cond, img + Ly.w_z + static_cast<size_t>(kC) * kCc * 2, t.gate2, L, kC, kCc, 1,
              reinterpret_cast<const float*>(img + Ly.b_z) + kC, kEpiStore, nullptr, nullptr, 0, info, stream);
   if (st) return st;
+  // pair logits [16][L][Lp] (rows padded to Lp columns for the softmax's vector loads)
   return pair_bias16(pair, img + Ly.w_pb, reinterpret_cast<const float*>(img + Ly.pb_wsum), t.logits, L, L,
-                     static_cast<int64_t>(L) * L, L, info, stream);
+                     static_cast<int64_t>(L) * pad8(L), pad8(L), info, stream);
 }
 
 int dit_forward(const void* x, const uint8_t* mask, const void* packed, const void* tables, void* out, void* workspace,
@@ -476,11 +463,28 @@ int dit_forward(const void* x, const uint8_t* mask, const void* packed, const vo
   st = dgemm(a, img + Ly.w_qkvg, big, m, 4 * kC, kC, 0, reinterpret_cast<const float*>(img + Ly.b_qkvg), kEpiStore,
              nullptr, nullptr, 0, info, stream);
   if (st) return st;
-  const size_t smem = static_cast<size_t>(kASmemFloats) * 4;
-  cudaFuncSetAttribute(dit_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  dit_attention_kernel<<<S * kH * ((L + kAQ - 1) / kAQ), kAThreads, smem, stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(big), t.logits, mask, reinterpret_cast<__nv_bfloat16*>(a), L);
-  st = cuda_status(static_cast<int>(cudaGetLastError()), "diffusion transformer attention launch");
+  // attention: S = Q K^T and O = P V on the tensor cores, the softmax (with the pair logits and
+  // the key mask) and the gate in between
+  const int Lp = pad8(L);
+  const int64_t sl = static_cast<int64_t>(S) * kH * L * Lp;
+  float* sbuf = reinterpret_cast<float*>(big + a256(static_cast<size_t>(m) * 4 * kC * 2));
+  __nv_bfloat16* pbuf = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(sbuf) + a256(sl * 4));
+  __nv_bfloat16* vt = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(pbuf) + a256(sl * 2));
+  const __nv_bfloat16* qk = reinterpret_cast<const __nv_bfloat16*>(big);
+  st = bgemm(qk, 4 * kC, kD, static_cast<int64_t>(L) * 4 * kC, qk + kC, 4 * kC, kD, static_cast<int64_t>(L) * 4 * kC,
+             sbuf, Lp, static_cast<int64_t>(L) * Lp, static_cast<int64_t>(kH) * L * Lp, L, L, kD, kH, S, 1, info, stream);
+  if (st) return st;
+  dit_softmax_kernel<<<static_cast<int>((static_cast<int64_t>(S) * kH * L + 7) / 8), 256, 0, stream>>>(
+      sbuf, t.logits, mask, pbuf, static_cast<int64_t>(S) * kH * L, L, Lp);
+  dit_vt_kernel<<<4 * info.num_sms, 256, 0, stream>>>(qk, vt, S, L, Lp);
+  st = cuda_status(static_cast<int>(cudaGetLastError()), "diffusion transformer softmax launch");
+  if (st) return st;
+  st = bgemm(pbuf, Lp, static_cast<int64_t>(L) * Lp, static_cast<int64_t>(kH) * L * Lp, vt, Lp,
+             static_cast<int64_t>(kD) * Lp, static_cast<int64_t>(kH) * kD * Lp, a, kC, kD, static_cast<int64_t>(L) * kC,
+             L, kD, Lp, kH, S, 0, info, stream);
+  if (st) return st;
+  dit_gate_kernel<<<4 * info.num_sms, 256, 0, stream>>>(reinterpret_cast<__nv_bfloat16*>(a), qk, m);
+  st = cuda_status(static_cast<int>(cudaGetLastError()), "diffusion transformer gate launch");
   if (st) return st;
   st = dgemm(a, img + Ly.w_o, out, m, kC, kC, 0, nullptr, kEpiResidual, x, t.gate1, L, info, stream);
   if (st) return st;

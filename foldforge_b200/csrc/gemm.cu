@@ -45,6 +45,13 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
   tn = r - tm * tiles_n;
 }
 
+// element offset of batch b's output
+__device__ __forceinline__ int64_t batch_offset(const GemmParams& p, int b) {
+  if (p.batch_inner > 0)
+    return static_cast<int64_t>(b % p.batch_inner) * p.batch_stride_d + static_cast<int64_t>(b / p.batch_inner) * p.batch_stride_d2;
+  return static_cast<int64_t>(b) * p.batch_stride_d;
+}
+
 template <int BN>
 __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int b, int m, int n0, const uint32_t (&v)[32]) {
   if (m >= p.M) return;
@@ -60,7 +67,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int b, int m
       const float bb = __uint_as_float(v[16 + i]);
       out[i] = a / (1.0f + __expf(-a)) * bb;
     }
-    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + static_cast<int64_t>(b) * p.batch_stride_d +
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + batch_offset(p, b) +
                          static_cast<int64_t>(m) * p.ldd + h0;
     if (h0 + 16 <= out_cols && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
       uint4 w0 = make_uint4(pack_bf16(out[0], out[1]), pack_bf16(out[2], out[3]), pack_bf16(out[4], out[5]),
@@ -97,9 +104,19 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int b, int m
   }
   if (p.col_gate != nullptr) {
     const float* gr = p.col_gate + static_cast<int64_t>(m % p.gate_rows) * p.N + n0;
+    if (full && (reinterpret_cast<uintptr_t>(gr) & 15u) == 0) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i)
-      if (n0 + i < p.N) acc[i] *= 1.0f / (1.0f + __expf(-gr[i]));
+      for (int i = 0; i < 32; i += 4) {
+        const float4 gv = *reinterpret_cast<const float4*>(gr + i);
+        acc[i] *= 1.0f / (1.0f + __expf(-gv.x));
+        acc[i + 1] *= 1.0f / (1.0f + __expf(-gv.y));
+        acc[i + 2] *= 1.0f / (1.0f + __expf(-gv.z));
+        acc[i + 3] *= 1.0f / (1.0f + __expf(-gv.w));
+      }
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (n0 + i < p.N) acc[i] *= 1.0f / (1.0f + __expf(-gr[i]));
+    }
   }
   float rowscale = 1.0f;
   if (p.row_mask != nullptr) rowscale = p.row_mask[static_cast<int64_t>(b) * p.M + m] ? 1.0f : 0.0f;
@@ -110,7 +127,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int b, int m
       for (int i = 0; i < 32; ++i) acc[i] *= rowscale;
     }
   }
-  const int64_t off = static_cast<int64_t>(b) * p.batch_stride_d + static_cast<int64_t>(m) * p.ldd + n0;
+  const int64_t off = batch_offset(p, b) + static_cast<int64_t>(m) * p.ldd + n0;
   if (p.epilogue == kEpiResidual) {
     // D = R + acc * rowscale, R and D share the layout and dtype. All of the chunk's residual
     // values are read before the first store (R may alias D), 16 bytes at a time when the
@@ -240,8 +257,14 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t ph = (it / kStages) & 1;
           if (!mbar_wait(&s.empty[st], ph ^ 1, p.err, kErrTimeoutEmpty)) { ok = false; break; }
           mbar_arrive_expect_tx(&s.full[st], (kBM + BN) * kBK * 2);
-          tma_load_3d(s.a[st], &map_a, &s.full[st], kb * kBK, tm * kBM, b);
-          tma_load_3d(s.b[st], &map_b, &s.full[st], kb * kBK, tn * BN, b);
+          if (p.batch_inner > 0) {
+            const int bi = b % p.batch_inner, bo = b / p.batch_inner;
+            tma_load_4d(s.a[st], &map_a, &s.full[st], kb * kBK, tm * kBM, bi, bo);
+            tma_load_4d(s.b[st], &map_b, &s.full[st], kb * kBK, tn * BN, bi, bo);
+          } else {
+            tma_load_3d(s.a[st], &map_a, &s.full[st], kb * kBK, tm * kBM, b);
+            tma_load_3d(s.b[st], &map_b, &s.full[st], kb * kBK, tn * BN, b);
+          }
         }
       }
       // drain: every issued stage must land before the CTA may exit
@@ -363,7 +386,7 @@ int launch_gemm_nt(const CUtensorMap& map_a, const CUtensorMap& map_b, const Gem
   CUtensorMap map_d;
   memset(&map_d, 0, sizeof(map_d));
   p.tma_store = 0;
-  if (p.epilogue == kEpiStore && !p.d_is_f32 && p.bias == nullptr && p.row_scale == nullptr &&
+  if (p.epilogue == kEpiStore && !p.d_is_f32 && p.bias == nullptr && p.row_scale == nullptr && p.batch_inner == 0 &&
       (reinterpret_cast<uintptr_t>(p.D) & 15u) == 0 &&
       (p.ldd * 2) % 16 == 0 &&
       (p.batch_stride_d * 2) % 16 == 0) {

@@ -29,6 +29,10 @@ struct GemmParams {
   // residual epilogue only: acc times sigmoid(col_gate[(m % gate_rows) * N + n]) before the add
   const float* col_gate = nullptr;
   int gate_rows = 0;
+  // two-level batch: batch index b = outer * batch_inner + inner; the operand maps are then 4-D
+  // ({K, rows, inner, outer}) and D's offset is inner * batch_stride_d + outer * batch_stride_d2
+  int batch_inner = 0;
+  int64_t batch_stride_d2 = 0;
 };
 
 size_t gemm_smem_bytes(int bn);
