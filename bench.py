@@ -72,6 +72,8 @@ def parse() -> argparse.Namespace:
                     help="with --gpus > 1: time eager launches instead of a captured CUDA graph of the sharded trunk")
     ap.add_argument("--breakdown", action="store_true",
                     help="with --gpus > 1: per-stage CUDA-event times of the N=2048 sharded trunk (max over ranks)")
+    ap.add_argument("--dit-once", action="store_true",
+                    help="run one token DiT block three times at configuration 5's shape (a driver for ncu captures)")
     ap.add_argument("--kernels-once", action="store_true",
                     help="launch every pair-stack kernel once at --n (a driver for ncu captures; no timing)")
     return ap.parse_args()
@@ -811,6 +813,27 @@ def sharded_parity(trunk, blocks, comm, rows_h, s_h, mask, n: int, rank: int, de
     return result
 
 
+def dit_once() -> None:
+    """One AF3 TokenDiT block (b200) on 5 samples x 512 tokens, three passes (the tables are
+    built on the first): a driver for ncu launch lists and captures, no timing."""
+    from foldforge_b200 import _lib
+    from foldforge_b200.engine.dit import TokenDiT, TokenDiTStack
+    from foldforge_b200.synthetic import dit_inputs, dit_stack_state
+
+    dev = torch.device("cuda")
+    blk = TokenDiT()
+    blk.load_state_dict(dit_stack_state(1, 0, "baseline")[0], strict=True)
+    stack = TokenDiTStack([blk]).to(dev).eval()
+    blk.set_backend("b200")
+    x, cond, pair, mask = dit_inputs(5, 512, 0)
+    x, cond, pair, mask = x.bfloat16().to(dev), cond.bfloat16().to(dev), pair.bfloat16().to(dev), mask.to(dev) > 0
+    with torch.no_grad():
+        for _ in range(3):
+            stack(x, mask, cond, pair, key_mask=mask[None])
+    torch.cuda.synchronize()
+    print(f"dit-once: device error word {_lib.device_error()}")
+
+
 def kernels_once(n: int) -> None:
     """Each kernel of one block once on the bench's inputs: TriMul outgoing stages 1, 2, 4,
     TriAttn starting stages 1, 2, 4, pair transition, attention with pair bias, single
@@ -845,6 +868,9 @@ def kernels_once(n: int) -> None:
 
 def main() -> None:
     args = parse()
+    if args.dit_once:
+        dit_once()
+        return
     if args.kernels_once:
         kernels_once(args.n)
         return
