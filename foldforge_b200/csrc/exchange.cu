@@ -57,6 +57,8 @@ __device__ __forceinline__ void signal_peers(const uint64_t* flag_ptrs, uint32_t
 // as ONE contiguous run there (kTRows x 256 bytes over NVLink) while the source pairs are read
 // with a stride of N pairs (each a coalesced 256-byte piece). Lanes 0-15 move one pair's 16
 // words, lanes 16-31 the next pair's; the index arithmetic is 32-bit and once per chunk.
+// Items are (a, chunk, destination) with the destination fastest; N = P R, so each
+// (column, chunk) is one item.
 constexpr int kTRows = 64;
 
 __global__ void __launch_bounds__(kXThreads) pair_transpose_scatter_kernel(const uint4* __restrict__ x,
@@ -74,8 +76,12 @@ __global__ void __launch_bounds__(kXThreads) pair_transpose_scatter_kernel(const
   const int warps = static_cast<int>(gridDim.x) * (kXThreads / 32);
   for (int item = static_cast<int>(blockIdx.x) * (kXThreads / 32) + static_cast<int>(threadIdx.x >> 5); item < items;
        item += warps) {
-    const int c = item / chunks, i0 = (item - c * chunks) * kTRows;
-    const int q = c / R, a = c - q * R;
+    // destination rank fastest (staggered by rank): the warps in flight write to every peer
+    // at once, so no rank's incoming links take all the ranks' traffic at one time
+    const int qq = item % P, rest = item / P;
+    const int a = rest / chunks, i0 = (rest - a * chunks) * kTRows;
+    const int q = qq + rank + 1 < P ? qq + rank + 1 : qq + rank + 1 - P;
+    const int c = q * R + a;
     const int rows = R - i0 < kTRows ? R - i0 : kTRows;
     const uint4* src = x + (static_cast<int64_t>(i0) * N + c) * 16 + part;
     uint4* d = reinterpret_cast<uint4*>(sdst[q]) + (static_cast<int64_t>(a) * N + row0 + i0) * 16 + part;
