@@ -23,7 +23,8 @@
 // Warps 0..15: Z staging, SwiGLU and residual, four warps per TMEM lane quarter (warp / 4 =
 // which 16 of a chunk's hidden units, which 32 of the channels of Z and of the output; the
 // row's LayerNorm sums, taken about its channel 0, are combined over the four through shared
-// memory); warp 16: TMA; warp 17: MMA issue.
+// memory); warp 16: TMA; warp 17: first products; warp 18: second products (two issuing
+// threads, so neither product's operand waits hold up the other's issue).
 #include "../../include/foldforge_b200.h"
 #include "abi_util.h"
 #include "common.cuh"
@@ -37,7 +38,7 @@ constexpr int kHidden = 512;
 constexpr int kChunk = 64;
 constexpr int kChunks = kHidden / kChunk;
 constexpr int kRows = 128;
-constexpr int kThreads = 576;  // 16 SwiGLU / residual warps, TMA warp 16, MMA warp 17
+constexpr int kThreads = 608;  // 16 SwiGLU / residual warps, TMA warp 16, MMA warps 17 (first) and 18 (second)
 constexpr int kWStages = 3;
 constexpr size_t kW1Chunk = 128 * kC * 2;      // 32 KB: [64 a | 64 b] x 128, two SW128 K-blocks
 constexpr size_t kW2Chunk = kC * kChunk * 2;   // 16 KB: 128 out x 64 hidden, SW128
@@ -58,6 +59,7 @@ struct Smem {
   uint64_t zx_bar[2][4];    // a lane quarter's four partial sums written, by tile parity
   uint64_t zt_full, zt_free;
   uint64_t a1_full[2], h_full[2];
+  uint64_t a1_free[2], h_free[2];  // A1[i] read out by the SwiGLU warps; H[i] read by its second product
   uint64_t acc2_full, acc2_free;
   uint32_t tmem_base;
 };
@@ -90,6 +92,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.z_empty[i], 1);
       mbar_init(&s.a1_full[i], 1);
       mbar_init(&s.h_full[i], 16);
+      mbar_init(&s.a1_free[i], 16);
+      mbar_init(&s.h_free[i], 1);
     }
     for (int i = 0; i < kWStages; ++i) {
       mbar_init(&s.w1_full[i], 1);
@@ -177,37 +181,45 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == 17) {
-    // ------------------------------------------------------------ MMA issuer
+    // ------------------------------------------------------------ first products
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16_f32(128, 128);
       bool ok = true;
-      // first product of chunk j (global weight counter wc) into A1[j % 2]; A = Z from TMEM
-      auto mma1 = [&](int j, int wc) -> bool {
-        const int st = wc % kWStages;
-        if (!mbar_wait(&s.w1_full[st], (wc / kWStages) & 1, p.err, kErrTimeoutLoad)) return false;
-        tc_fence_after();
-        const uint32_t b0 = smem_u32(s.w1[st]);
-        const uint32_t d = tmem0 + kColA1 + (j & 1) * 128;
-#pragma unroll
-        for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_bf16_tmem_a(d, tmem0 + kColZ + (kb * 4 + kk) * 8, desc_kmajor_sw128(b0 + kb * 16384) + 2 * kk, idesc,
-                            (kb | kk) != 0);
-        mma_commit(&s.a1_full[j & 1]);
-        mma_commit(&s.w1_empty[st]);
-        return true;
-      };
       for (int ti = 0; ti < my_tiles && ok; ++ti) {
-        const int w0 = ti * kChunks;
         if (!mbar_wait(&s.zt_full, ti & 1, p.err, kErrTimeoutLoad)) break;
-        // prologue: chunks 0 and 1 (A1[0] / A1[1] were last read by chunks 6 / 7 of the
-        // previous tile, whose H this thread already waited for)
-        for (int j = 0; j < 2 && ok; ++j) ok = mma1(j, w0 + j);
-        for (int j = 0; j < kChunks && ok; ++j) {
-          const int wc = w0 + j;
+        for (int j = 0; j < kChunks; ++j) {
+          // chunk j into A1[j % 2] (use n of that buffer, once its use n - 1 is read out);
+          // A = Z from TMEM
+          const int wc = ti * kChunks + j;
           const int st = wc % kWStages;
-          const int u = ti * (kChunks / 2) + j / 2;  // use count of A1 / H buffer j % 2
+          const int n = ti * (kChunks / 2) + j / 2;
+          if (n > 0 && !mbar_wait(&s.a1_free[j & 1], (n - 1) & 1, p.err, kErrTimeoutEmpty)) { ok = false; break; }
+          if (!mbar_wait(&s.w1_full[st], (wc / kWStages) & 1, p.err, kErrTimeoutLoad)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t b0 = smem_u32(s.w1[st]);
+          const uint32_t d = tmem0 + kColA1 + (j & 1) * 128;
+#pragma unroll
+          for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_bf16_tmem_a(d, tmem0 + kColZ + (kb * 4 + kk) * 8, desc_kmajor_sw128(b0 + kb * 16384) + 2 * kk, idesc,
+                              (kb | kk) != 0);
+          mma_commit(&s.a1_full[j & 1]);
+          mma_commit(&s.w1_empty[st]);
+          if (j == kChunks - 1) mma_commit(&s.zt_free);  // the tile's last first product is issued
+        }
+      }
+    }
+  } else if (warp == 18) {
+    // ------------------------------------------------------------ second products
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(128, 128);
+      bool ok = true;
+      for (int ti = 0; ti < my_tiles && ok; ++ti) {
+        for (int j = 0; j < kChunks; ++j) {
+          const int wc = ti * kChunks + j;
+          const int st = wc % kWStages;
+          const int u = ti * (kChunks / 2) + j / 2;  // use count of H buffer j % 2
           if (!mbar_wait(&s.h_full[j & 1], u & 1, p.err, kErrTimeoutMma)) { ok = false; break; }
           if (j == 0 && !mbar_wait(&s.acc2_free, (ti & 1) ^ 1, p.err, kErrTimeoutEmpty)) { ok = false; break; }
           if (!mbar_wait(&s.w2_full[st], (wc / kWStages) & 1, p.err, kErrTimeoutLoad)) { ok = false; break; }
@@ -218,14 +230,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_bf16_tmem_a(tmem0 + kColAcc2, tmem0 + kColH + (j & 1) * 32 + kk * 8, desc_kmajor_sw128(b0) + 2 * kk,
                             idesc, (j | kk) != 0);
           mma_commit(&s.w2_empty[st]);
-          if (j + 2 < kChunks && !mma1(j + 2, wc + 2)) { ok = false; break; }
-          if (j == kChunks - 3) mma_commit(&s.zt_free);  // the tile's last first product is issued
+          mma_commit(&s.h_free[j & 1]);
         }
         if (!ok) break;
         mma_commit(&s.acc2_full);
       }
     }
-  } else {
+  } else if (warp < 16) {
     // ------------------------------------------------------------ SwiGLU / residual warps
     // warp w: lane quarter w % 4 (TMEM lanes = the tile's rows); part w / 4 takes 16 of a
     // chunk's 64 hidden units and 32 of the 128 channels of Z and of the output
@@ -309,6 +320,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld16(tl + kColA1 + (j & 1) * 128 + part * 16, va);
         tmem_ld16(tl + kColA1 + (j & 1) * 128 + 64 + part * 16, vb);
         tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.a1_free[j & 1]);  // the chunk after next may overwrite A1[j % 2]
         const float4* bs4 = reinterpret_cast<const float4*>(s.bias + j * 128 + part * 16);
         uint32_t hw[8];
 #pragma unroll
@@ -330,6 +344,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             hw[c / 2] = pack_bf16(o0, o1);
           }
         }
+        // H[j % 2] was read by the second product of the chunk before last
+        if (u > 0 && !__all_sync(0xFFFFFFFFu, mbar_wait(&s.h_free[j & 1], (u - 1) & 1, p.err, kErrTimeoutMma))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
         tmem_st8(tl + kColH + (j & 1) * 32 + part * 8, hw);
         tmem_st_wait();
         tc_fence_before();
