@@ -86,6 +86,7 @@ def weak_n(gpus: int) -> int:
 
 
 LADDER_N = 2048
+LADDER_WARMUP, LADDER_STEPS = 3, 3  # the ladder trunk: untimed passes, then timed ones (L2 flushed before each)
 
 
 def peaks() -> dict:
@@ -388,7 +389,7 @@ def run_b200(args, rank: int, world: int, local: int, dist) -> None:
 
 
 def ladder_single_gpu(dev: torch.device) -> dict:
-    """The N = 2048 length-ladder trunk on one GPU (CUDA-graph replay): 1 warm-up, 2 timed."""
+    """The N = 2048 length-ladder trunk on one GPU (CUDA-graph replay): 3 warm-up replays, 3 timed."""
     import math
 
     import foldforge_b200
@@ -405,13 +406,14 @@ def ladder_single_gpu(dev: torch.device) -> dict:
                           warmup=1)
     del z
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
-    graphed.replay()
+    for _ in range(LADDER_WARMUP):
+        graphed.replay()
     torch.cuda.synchronize()
     sampler = ClockSampler(dev.index or 0)
     sampler.start()
     time.sleep(0.3)
     ts = []
-    for _ in range(2):
+    for _ in range(LADDER_STEPS):
         flush.fill_(1.0)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
@@ -424,7 +426,8 @@ def ladder_single_gpu(dev: torch.device) -> dict:
     torch.cuda.empty_cache()
     ms = sum(ts) / len(ts)
     return {"n": n, "n_gpus": 1, "ms_per_trunk": round(ms, 1), "ms_per_block": round(ms / N_BLOCKS, 3),
-            "masked_suffix": masked, "steps": 2, "warmup": 1, "parallelism": "single GPU (CUDA-graph replay)",
+            "masked_suffix": masked, "steps": LADDER_STEPS, "warmup": LADDER_WARMUP,
+            "parallelism": "single GPU (CUDA-graph replay)",
             "clocks": clocks}
 
 
@@ -644,6 +647,7 @@ def run_sharded(args, rank: int, world: int, local: int, dist) -> None:
         torch.cuda.synchronize()
         dist.barrier()
         step = runner(rows, mask, s)
+        step()  # one untimed pass of what is timed (the captured graph, if capture succeeded)
         torch.cuda.synchronize()
         dist.barrier()
         sampler = ClockSampler(local) if clocks else None
@@ -704,10 +708,12 @@ def run_sharded(args, rank: int, world: int, local: int, dist) -> None:
 
     ladder = None
     if not args.no_ladder:
-        lad_ms, lad_clocks, _, _, lad_mode = measure(LADDER_N, math.ceil(0.05 * LADDER_N), 2, 1, True)
+        lad_ms, lad_clocks, _, _, lad_mode = measure(LADDER_N, math.ceil(0.05 * LADDER_N), LADDER_STEPS,
+                                                     LADDER_WARMUP, True)
         ladder = {"n": LADDER_N, "n_gpus": world, "ms_per_trunk": round(lad_ms, 1),
-                  "ms_per_block": round(lad_ms / nb, 3), "masked_suffix": math.ceil(0.05 * LADDER_N), "steps": 2,
-                  "warmup": 1, "parallelism": f"axial row-sharding x{world} ({lad_mode})", "clocks": lad_clocks}
+                  "ms_per_block": round(lad_ms / nb, 3), "masked_suffix": math.ceil(0.05 * LADDER_N),
+                  "steps": LADDER_STEPS, "warmup": LADDER_WARMUP,
+                  "parallelism": f"axial row-sharding x{world} ({lad_mode})", "clocks": lad_clocks}
 
     breakdown = None
     if args.breakdown:
