@@ -375,7 +375,7 @@ struct OutSmem {
   float4 pc[2][kOTile];  // per pair: rz / 2, -rz mz / 2, ru / 2, -ru mu / 2
   float keep[2][kOTile];
   uint64_t wbar;
-  uint64_t full[kOStages], empty[kOStages];
+  uint64_t full[kOStages], out_ready[kOStages];  // tile landed; tile's output written over its z (8 warps)
   uint64_t acc_full[2], acc_free[2], st_full[2], st_free[2];
   uint32_t tmem_base;
 };
@@ -406,7 +406,7 @@ __global__ void __launch_bounds__(kOThreads, 1)
     mbar_init(&s.wbar, 1);
     for (int i = 0; i < kOStages; ++i) {
       mbar_init(&s.full[i], 1);
-      mbar_init(&s.empty[i], 2);  // the MMA commit (u, z read) + the store's read of z
+      mbar_init(&s.out_ready[i], 8);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.acc_full[i], 1);
@@ -440,10 +440,28 @@ __global__ void __launch_bounds__(kOThreads, 1)
       mbar_arrive_expect_tx(&s.wbar, kGateBytes + kOutBytes);
       bulk_load(s.wg, p.packed + kProjBytes, kGateBytes, &s.wbar);
       bulk_load(s.wo, p.packed + kProjBytes + kGateBytes, kOutBytes, &s.wbar);
+      // the slot's previous tile: written over its z by the epilogue (which ran after the MMA
+      // and the statistics had read the slot), stored from there; the slot is free once the
+      // store has read it. This thread, not an epilogue warp, waits for that read.
+      auto store_tile = [&](int t_it, int t_tile) -> bool {
+        const int sst = t_it % kOStages;
+        if (!mbar_wait(&s.out_ready[sst], (t_it / kOStages) & 1, p.err, kErrTimeoutEmpty)) return false;
+        const int sc0 = (t_tile % tiles_per_row) * kOTile;
+        const int srr = t_tile / tiles_per_row;
+        tma_store_3d(&map_out, s.z[sst], 0, sc0, srr);
+        tma_store_3d(&map_out, s.z[sst] + kOTile * 128, 64, sc0, srr);
+        tma_store_commit();
+        tma_store_wait_read0();
+        return true;
+      };
       int it = 0;
+      bool ok = true;
       for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
         const int st = it % kOStages;
-        if (!mbar_wait(&s.empty[st], ((it / kOStages) & 1) ^ 1, p.err, kErrTimeoutEmpty)) break;
+        if (it >= kOStages && !store_tile(it - kOStages, tile - kOStages * static_cast<int>(gridDim.x))) {
+          ok = false;
+          break;
+        }
         const int c0 = (tile % tiles_per_row) * kOTile;
         const int rr = tile / tiles_per_row;
         const int b = rr / p.R, r = rr - b * p.R;
@@ -453,9 +471,13 @@ __global__ void __launch_bounds__(kOThreads, 1)
           tma_load_3d(s.u[st] + kb * (kH * 128), &map_u, &s.full[st], c0 + kb * 64, r, b * kH);
         }
       }
-      // every issued load has landed before the CTA can exit
+      // the last tiles' stores; every issued load has landed and every store has completed
+      // before the CTA can exit
+      for (int k = it - kOStages; ok && k < it; ++k)
+        if (k >= 0) ok = store_tile(k, static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x));
       mbar_wait(&s.wbar, 0, p.err, kErrTimeoutLoad);
       if (it > 0) mbar_wait(&s.full[(it - 1) % kOStages], ((it - 1) / kOStages) & 1, p.err, kErrTimeoutLoad);
+      tma_store_wait_all0();
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -481,7 +503,6 @@ __global__ void __launch_bounds__(kOThreads, 1)
           mma_bf16(dout, desc_mnmajor_sw128(ua + ks * 2048, kH * 128, 1024),
                    desc_kmajor_sw128(wo + (ks / 4) * 16384) + 2 * (ks % 4), idesc_o, ks != 0);
         mma_commit(&s.acc_full[buf]);
-        mma_commit(&s.empty[st]);
       }
     }
   } else if (warp < 4) {
@@ -494,6 +515,20 @@ __global__ void __launch_bounds__(kOThreads, 1)
     int it = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
       const int st = it % kOStages, buf = it & 1;
+      // the pairs' global inputs first (the z statistics from the projection and the masks):
+      // they do not depend on the staged tile, so their latency overlaps the waits below
+      const int c0 = (tile % tiles_per_row) * kOTile;
+      const int rr = tile / tiles_per_row;
+      const int b = rr / p.R, r = rr - b * p.R;
+      float2 zs[2];
+      bool kp[2];
+      const bool row_keep = !p.masked_zero || p.mask[b * p.N + p.row0 + r];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int j = c0 + pp0 + k;
+        zs[k] = j < p.N ? p.zstats[(static_cast<int64_t>(b) * p.R + r) * p.N + j] : make_float2(0.f, 0.f);
+        kp[k] = j < p.N && row_keep && (!p.masked_zero || p.mask[b * p.N + j]);
+      }
       const bool w1 = mbar_wait(&s.full[st], (it / kOStages) & 1, p.err, kErrTimeoutLoad);
       const bool w2 = mbar_wait(&s.st_free[buf], ((it >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty);
       if (!__all_sync(0xFFFFFFFFu, w1 && w2)) break;
@@ -512,21 +547,14 @@ __global__ void __launch_bounds__(kOThreads, 1)
       float s1[2], s2[2];
       f32x2_split(a1, s1[0], s1[1]);
       f32x2_split(a2, s2[0], s2[1]);
-      const int c0 = (tile % tiles_per_row) * kOTile;
-      const int rr = tile / tiles_per_row;
-      const int b = rr / p.R, r = rr - b * p.R;
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
         const int pp = pp0 + k;
-        const int j = c0 + pp;
         const float m1 = s1[k] * (1.0f / kH);
         const float mu = (k ? sh1 : sh0) + m1;
         const float ru = rsqrtf(fmaxf(s2[k] * (1.0f / kH) - m1 * m1, 0.f) + 1e-5f);
-        float2 zs = make_float2(0.f, 0.f);
-        if (j < p.N) zs = p.zstats[(static_cast<int64_t>(b) * p.R + r) * p.N + j];
-        s.pc[buf][pp] = make_float4(0.5f * zs.y, -0.5f * zs.y * zs.x, 0.5f * ru, -0.5f * ru * mu);
-        s.keep[buf][pp] =
-            (j < p.N && (!p.masked_zero || (p.mask[b * p.N + p.row0 + r] && p.mask[b * p.N + j]))) ? 1.f : 0.f;
+        s.pc[buf][pp] = make_float4(0.5f * zs[k].y, -0.5f * zs[k].y * zs[k].x, 0.5f * ru, -0.5f * ru * mu);
+        s.keep[buf][pp] = kp[k] ? 1.f : 0.f;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.st_full[buf]);
@@ -589,26 +617,15 @@ __global__ void __launch_bounds__(kOThreads, 1)
       tc_fence_before();
       fence_async_smem();
       __syncwarp();
+      if (!ok) break;
+      // this warp's pairs x channels are written over the staged z: the TMA thread stores the
+      // tile once all eight warps have arrived
       if (lane == 0) {
         mbar_arrive(&s.acc_free[buf]);
         mbar_arrive(&s.st_free[buf]);
+        mbar_arrive(&s.out_ready[st]);
       }
-      // all eight epilogue warps have written the tile: one thread stores it
-      ok = !named_barrier_or(1, 256, !ok);
-      if (warp == 4 && lane == 0) {
-        if (ok) {
-          const int c0 = (tile % tiles_per_row) * kOTile;
-          const int rr = tile / tiles_per_row;
-          tma_store_3d(&map_out, s.z[st], 0, c0, rr);
-          tma_store_3d(&map_out, s.z[st] + kOTile * 128, 64, c0, rr);
-          tma_store_commit();
-          tma_store_wait_read0();
-        }
-        mbar_arrive(&s.empty[st]);
-      }
-      if (!ok) break;
     }
-    if (warp == 4 && lane == 0) tma_store_wait_all0();
   }
   tc_fence_before();
   __syncthreads();
