@@ -806,7 +806,7 @@ struct OutSmem {
   float2 pc[2][kOTile];    // per pair: rstd / 2, -rstd mean / 2
   float keep[2][kOTile];
   uint64_t wbar;
-  uint64_t full[kOStages], empty[kOStages];
+  uint64_t full[kOStages], out_ready[kOStages];  // tile landed; tile's output written over its z (8 warps)
   uint64_t g_full[2], gt_ready[2], d_full[2], acc_free[2], st_full[2], st_free[2];
   uint32_t tmem_base;
 };
@@ -836,7 +836,7 @@ __global__ void __launch_bounds__(kOThreads, 1)
     mbar_init(&s.wbar, 1);
     for (int i = 0; i < kOStages; ++i) {
       mbar_init(&s.full[i], 1);
-      mbar_init(&s.empty[i], 2);  // the output MMA's commit (o / G read) + the store's read of z
+      mbar_init(&s.out_ready[i], 8);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.g_full[i], 1);
@@ -870,10 +870,28 @@ __global__ void __launch_bounds__(kOThreads, 1)
       mbar_arrive_expect_tx(&s.wbar, kGateBytes + kOutBytes);
       bulk_load(s.wg, p.packed + kProjBytes, kGateBytes, &s.wbar);
       bulk_load(s.wo, p.packed + kProjBytes + kGateBytes, kOutBytes, &s.wbar);
+      // the slot's previous tile: written over its z by the epilogue (which ran after both
+      // products had read the slot), stored from there; the slot is free once the store has
+      // read it. This thread, not an epilogue warp, waits for that read.
+      auto store_tile = [&](int t_it, int t_tile) -> bool {
+        const int sst = t_it % kOStages;
+        if (!mbar_wait(&s.out_ready[sst], (t_it / kOStages) & 1, p.err, kErrTimeoutEmpty)) return false;
+        const int sc0 = (t_tile % tiles_per_row) * kOTile;
+        const int srr = t_tile / tiles_per_row;
+        tma_store_3d(&map_out, s.z[sst], 0, sc0, srr);
+        tma_store_3d(&map_out, s.z[sst] + kOTile * 128, 64, sc0, srr);
+        tma_store_commit();
+        tma_store_wait_read0();
+        return true;
+      };
       int it = 0;
+      bool ok = true;
       for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
         const int st = it % kOStages;
-        if (!mbar_wait(&s.empty[st], ((it / kOStages) & 1) ^ 1, p.err, kErrTimeoutEmpty)) break;
+        if (it >= kOStages && !store_tile(it - kOStages, tile - kOStages * static_cast<int>(gridDim.x))) {
+          ok = false;
+          break;
+        }
         const int c0 = (tile % tiles_per_row) * kOTile;
         const int rr = tile / tiles_per_row;
         mbar_arrive_expect_tx(&s.full[st], 2 * kOTile * kC * 2);
@@ -882,9 +900,13 @@ __global__ void __launch_bounds__(kOThreads, 1)
           tma_load_3d(s.o[st] + kb * (kOTile * 128), &map_o, &s.full[st], kb * 64, c0, rr);
         }
       }
-      // every issued load has landed before the CTA can exit
+      // the last tiles' stores; every issued load has landed and every store has completed
+      // before the CTA can exit
+      for (int k = it - kOStages; ok && k < it; ++k)
+        if (k >= 0) ok = store_tile(k, static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x));
       mbar_wait(&s.wbar, 0, p.err, kErrTimeoutLoad);
       if (it > 0) mbar_wait(&s.full[(it - 1) % kOStages], ((it - 1) / kOStages) & 1, p.err, kErrTimeoutLoad);
+      tma_store_wait_all0();
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -921,7 +943,6 @@ __global__ void __launch_bounds__(kOThreads, 1)
             mma_bf16(tmem0 + buf * 256 + kC, desc_kmajor_sw128(ga + kb * (kOTile * 128)) + 2 * kk,
                      desc_kmajor_sw128(wo + kb * 16384) + 2 * kk, idesc, (kb | kk) != 0);
         mma_commit(&s.d_full[buf]);
-        mma_commit(&s.empty[st]);
       }
     }
   } else if (warp < 4) {
@@ -930,21 +951,28 @@ __global__ void __launch_bounds__(kOThreads, 1)
     int it = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
       const int st = it % kOStages, buf = it & 1;
-      const bool w1 = mbar_wait(&s.full[st], (it / kOStages) & 1, p.err, kErrTimeoutLoad);
-      const bool w2 = mbar_wait(&s.st_free[buf], ((it >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty);
-      if (!__all_sync(0xFFFFFFFFu, w1 && w2)) break;
+      // the keep mask first (global loads independent of the staged tile, so their latency
+      // overlaps the waits below)
       const int c0 = (tile % tiles_per_row) * kOTile;
       const int rr = tile / tiles_per_row;
       const int b = rr / p.R, r = rr - b * p.R;
-#pragma unroll 1
+      const bool row_keep = !p.masked_zero || p.mask[b * p.N + p.row0 + r];
+      bool kp[2];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int j = c0 + t + 64 * k;
+        kp[k] = j < p.N && row_keep && (!p.masked_zero || p.mask[b * p.N + j]);
+      }
+      const bool w1 = mbar_wait(&s.full[st], (it / kOStages) & 1, p.err, kErrTimeoutLoad);
+      const bool w2 = mbar_wait(&s.st_free[buf], ((it >> 1) & 1) ^ 1, p.err, kErrTimeoutEmpty);
+      if (!__all_sync(0xFFFFFFFFu, w1 && w2)) break;
+#pragma unroll
       for (int k = 0; k < 2; ++k) {
         const int pp = t + 64 * k;
         float mean, rstd;
         ln_stats_c128(s.z[st], kOTile * 128, pp, mean, rstd);
-        const int j = c0 + pp;
         s.pc[buf][pp] = make_float2(0.5f * rstd, -0.5f * rstd * mean);
-        s.keep[buf][pp] =
-            (j < p.N && (!p.masked_zero || (p.mask[b * p.N + p.row0 + r] && p.mask[b * p.N + j]))) ? 1.f : 0.f;
+        s.keep[buf][pp] = kp[k] ? 1.f : 0.f;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.st_full[buf]);
@@ -1037,25 +1065,15 @@ __global__ void __launch_bounds__(kOThreads, 1)
       tc_fence_before();
       fence_async_smem();
       __syncwarp();
+      if (!ok) break;
+      // this warp's pairs x channels are written over the staged z: the TMA thread stores the
+      // tile once all eight warps have arrived
       if (lane == 0) {
         mbar_arrive(&s.acc_free[buf]);
         mbar_arrive(&s.st_free[buf]);
+        mbar_arrive(&s.out_ready[st]);
       }
-      ok = !named_barrier_or(1, 256, !ok);
-      if (warp == 4 && lane == 0) {
-        if (ok) {
-          const int c0 = (tile % tiles_per_row) * kOTile;
-          const int rr = tile / tiles_per_row;
-          tma_store_3d(&map_out, s.z[st], 0, c0, rr);
-          tma_store_3d(&map_out, s.z[st] + kOTile * 128, 64, c0, rr);
-          tma_store_commit();
-          tma_store_wait_read0();
-        }
-        mbar_arrive(&s.empty[st]);
-      }
-      if (!ok) break;
     }
-    if (warp == 4 && lane == 0) tma_store_wait_all0();
   }
   tc_fence_before();
   __syncthreads();
