@@ -5,7 +5,7 @@ The drop-in claim is that FoldForge needs one added name and no other change: it
 its unmodified ``policy.py`` and ``serving.py``, applied to this package's engine classes
 (which FoldForge would import in place of the absent ``miniworld_engine`` ones). This test
 loads exactly those three reference files from a FoldForge checkout (``FOLDFORGE_SRC``, by
-default the reference tree of the build container), edits the one line in the source text,
+default a checkout named ``reference`` beside this repository), edits the one line in the source text,
 and checks what the reference's own test of the policy checks
 (``tests/kernels/test_backends.py``): the plan names, per-op pinning through ``engine.ops``,
 the per-class choice, the guard's fallback with one log line, ``engine.unsupported: error``,
@@ -31,7 +31,8 @@ from torch import nn
 from foldforge_b200.engine import modules as ours
 from foldforge_b200.engine.pairformer import pairformer_block
 
-SRC = Path(os.environ.get("FOLDFORGE_SRC", "/root/reference/src"))
+# a FoldForge checkout: FOLDFORGE_SRC, else one named `reference` beside this repository
+SRC = Path(os.environ.get("FOLDFORGE_SRC", Path(__file__).resolve().parents[2] / "reference" / "src"))
 ENGINE = SRC / "foldforge" / "modules" / "engine"
 
 pytestmark = pytest.mark.skipif(not (ENGINE / "policy.py").exists(), reason="FoldForge source tree not present")
