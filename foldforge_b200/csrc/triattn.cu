@@ -789,7 +789,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 // A thread owns one pair: its o and z rows are read and written as 16-byte swizzled
 // vectors, its LayerNorm coefficients stay in registers, and the paired fp32 pipe handles
 // two channels per instruction.
-//   warp 0      TMA: z and o tiles, 2-stage ring
+//   warp 0      TMA: z and o tiles, 2-stage ring; it also stores each finished tile from its
+//               slot (after the eight epilogue warps arrive) before reloading it
 //   warp 1      MMA: gate product (tile t + 1) ahead of the output product (tile t)
 //   warps 2-3   per-pair LayerNorm statistics of z and the keep mask
 //   warps 4-11  lane = pair; warps 4-7 channels 0-63, warps 8-11 channels 64-127

@@ -355,8 +355,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
 //   delta[p][c] = (ru_p (out - mu_p wsum_o[c]) + b_o[c]) * sigmoid(rz_p (gate - mz_p wsum_g[c]) + b_g[c])
 // A thread owns one pair and adds delta into that pair's row of the z tile in place
 // (16-byte swizzled vectors); the per-pair coefficients stay in registers and the paired
-// fp32 pipe computes two channels per instruction. One thread stores the tile with TMA.
-//   warp 0      TMA: z and u tiles into a 2-stage ring
+// fp32 pipe computes two channels per instruction.
+//   warp 0      TMA: z and u tiles into a 2-stage ring; it also stores each finished tile
+//               from its slot (after the eight epilogue warps arrive) before reloading it
 //   warp 1      MMA: gate and out products -> 256 TMEM columns, double-buffered
 //   warps 2-3   per-pair coefficients (z statistics from step 1, u statistics from the
 //               staged u tile) and the keep mask
